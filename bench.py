@@ -1,0 +1,391 @@
+#!/usr/bin/env python
+"""bench.py -- quantized decode GEMV throughput (HBM GB/s) of the B200 backend.
+
+Workload (one "step"): the int4 group-32 decode-GEMV sweep over Qwen3-1.7B projection shapes --
+q_proj 2048x2048, kv_proj 1024x2048, gate_proj and up_proj 6144x2048, down_proj 2048x6144 --
+plus the int8 per-row lm_head 151936x2048, each at batch 1 and batch 8: 12 GEMV launches that
+stream 0.68 GB of packed weights.  Weights are seeded N(0, 0.02) rounded to bf16 and quantised
+on the device by the reference's quantizer rules; x is seeded N(0, 1) f32.  The step's working
+set (~680 MB) is 5x the 126 MB L2 and every matrix is re-read only after >= 311 MB of other
+traffic, so no L2 flush is needed between steps.
+
+  value  whole-job algorithmic GB/s (weights + scales + x + y bytes per step x steps / time),
+         inputs resident in HBM, device time by CUDA events, max over ranks.
+  e2e    the same sweep through the C ABI's host-pointer matmul (pinned host x in, host y out,
+         one synchronous call per GEMV, as a Rust `matmul()` call would do it).
+  --impl reference   the oracle port of the reference's Rayon CPU path, all host threads.
+
+Multi-GPU (torchrun): every rank runs the whole sweep on its own GPU -- independent decode
+streams, data-parallel, no collective on the data path ("scaling": "weak").
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tokens/s & quantized GEMV HBM GB/s (% of peak) at 1/2/4/8 B200"
+UNIT = "GB/s"
+WORKLOAD = "int4 g32 decode GEMV sweep (q 2048x2048, kv 1024x2048, gate/up 6144x2048, down 2048x6144) + int8 per-row lm_head 151936x2048, batch 1 and 8"
+SWEEP = [  # name, qtype, N (out_features), K (in_features), block_size
+    ("q_proj", "int4", 2048, 2048, 32),
+    ("kv_proj", "int4", 1024, 2048, 32),
+    ("gate_proj", "int4", 6144, 2048, 32),
+    ("up_proj", "int4", 6144, 2048, 32),
+    ("down_proj", "int4", 2048, 6144, 32),
+    ("lm_head", "int8", 151936, 2048, 2048),
+]
+BATCHES = (1, 8)
+SEED = 0x5EED
+
+
+def gemv_bytes(qt, N, K, bs, B):
+    data = N * K if qt == "int8" else (N * K + 1) // 2
+    scales = 4 * math.ceil(N * K / bs)
+    return data + scales + 4 * B * (K + N)
+
+
+def step_bytes():
+    return sum(gemv_bytes(qt, N, K, bs, B) for B in BATCHES for (_, qt, N, K, bs) in SWEEP)
+
+
+def config_dict(n):
+    return {"workload": WORKLOAD, "batches": list(BATCHES), "weights": "seeded N(0,0.02) bf16 -> reference quantizer",
+            "x": "seeded N(0,1) f32", "l2": "working set 680 MB/step > 126 MB L2; no flush needed",
+            "parallelism": f"dp{n} (independent decode streams per GPU)"}
+
+
+# ---------------------------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str | None):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.out = None
+
+    def start(self):
+        cmd = ["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits", "-lms", "200"]
+        if self.gpu_id:
+            cmd += ["-i", self.gpu_id]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peak_hbm():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def profiled_traffic(kernel_tag: str):
+    """dram bytes per launch of the dominant kernel from its committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", f"{kernel_tag}.txt")
+    try:
+        for line in open(p):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------------------------------
+def dist_setup():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return ws, rank, local
+
+
+def max_over_ranks(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def gpu_uuid(local):
+    try:
+        import torch
+
+        u = str(torch.cuda.get_device_properties(local).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------------------------------------
+def run_cpu_sweep(nthreads: int, batches=BATCHES):
+    """One sweep step through the oracle port (the reference's Rayon CPU matmul, restated in C).
+    Returns (seconds, bytes) for the given batches."""
+    import numpy as np
+
+    import oracle
+    import pyxis_b200 as px
+
+    mats = []
+    for i, (name, qt, N, K, bs) in enumerate(SWEEP):
+        vals = oracle.bf16_to_f32(px.synth_normal_bf16(SEED + i, N * K, 0.02))
+        d, s = (oracle.quantize_int8 if qt == "int8" else oracle.quantize_int4)(vals, bs)
+        mats.append((qt, N, K, bs, d, s))
+    xs = {B: px.synth_normal_f32(SEED + 100 + B, B * 6144, 1.0) for B in batches}
+    t0 = time.perf_counter()
+    nbytes = 0
+    for B in batches:
+        for (qt, N, K, bs, d, s) in mats:
+            X = xs[B][: B * K].reshape(B, K)
+            oracle.matmul(X, oracle.INT8 if qt == "int8" else oracle.INT4, d, s, bs, N, K, nthreads=nthreads)
+            nbytes += gemv_bytes(qt, N, K, bs, B)
+    return time.perf_counter() - t0, nbytes
+
+
+def reference_arm(args, ws, rank):
+    if rank != 0:
+        return
+    import oracle
+
+    cores = oracle.num_cpus()
+    for _ in range(args.warmup):
+        run_cpu_sweep(cores, batches=(1,))
+    total_t, total_b = 0.0, 0
+    for _ in range(args.steps):
+        t, b = run_cpu_sweep(cores)
+        total_t += t
+        total_b += b
+    value = total_b / total_t / 1e9
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_t / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": config_dict(ws),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": "each step = the full sweep (12 matvec calls) through the C port of "
+                                       "src/matmul.rs (scalar x86 dot products, rows over all host threads)"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def pyxis_arm(args, ws, rank, local):
+    import numpy as np
+    import torch
+
+    import pyxis_b200 as px
+    from pyxis_b200 import _native
+
+    torch.cuda.set_device(local)
+    ctx = px.get_cuda(local)
+    if ctx is None:
+        raise SystemExit("bench: no B200 visible: " + _native.lib().pyxis_cuda_last_error().decode())
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+
+    weights = []
+    for i, (name, qt, N, K, bs) in enumerate(SWEEP):
+        bits = px.synth_normal_bf16(SEED + i, N * K, 0.02)
+        t = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).to(dev)
+        w = px.Weights.quantize_int8(t, bs, device=local) if qt == "int8" else px.Weights.quantize_int4(t, bs, device=local)
+        del t
+        weights.append((name, qt, N, K, bs, w))
+    X = {B: torch.from_numpy(px.synth_normal_f32(SEED + 100 + B, B * 6144, 1.0)).to(dev).view(B, 6144) for B in BATCHES}
+    Y = {B: torch.empty((B, 151936), dtype=torch.float32, device=dev) for B in BATCHES}
+    torch.cuda.synchronize()
+
+    lm_ev = []
+
+    def step(record=False):
+        for B in BATCHES:
+            for (name, qt, N, K, bs, w) in weights:
+                if record and name == "lm_head" and B == 1:
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    px.matmul_dev(X[B][:, :K], w, N, K, Y=Y[B][:, :N], stream=stream)
+                    e1.record(stream)
+                    lm_ev.append((e0, e1))
+                else:
+                    px.matmul_dev(X[B][:, :K], w, N, K, Y=Y[B][:, :N], stream=stream)
+
+    launches_per_step = len(BATCHES) * len(SWEEP)
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    barrier(ws)
+    clocks = ClockSampler(gpu_uuid(local))
+    clocks.start()
+    time.sleep(0.3)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(args.steps):
+        step(record=True)
+    end.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = start.elapsed_time(end)
+    ms_max = max_over_ranks(ms, ws)
+    barrier(ws)
+
+    sb = step_bytes()
+    value = ws * sb * args.steps / (ms_max / 1e3) / 1e9
+    lm_ms = statistics.mean(a.elapsed_time(b) for a, b in lm_ev)
+    lm_bytes = gemv_bytes("int8", 151936, 2048, 2048, 1)
+    peak, peak_kind = measured_peak_hbm()
+    achieved = lm_bytes / (lm_ms / 1e3) / 1e9
+
+    # e2e: the same sweep through the host-pointer C ABI (pinned host x in, host y out).
+    hx = {B: torch.empty((B, 6144), dtype=torch.float32).pin_memory() for B in BATCHES}
+    hy = {B: torch.empty((B, 151936), dtype=torch.float32).pin_memory() for B in BATCHES}
+    for B in BATCHES:
+        hx[B].copy_(X[B].cpu())
+    h2d = sum(4 * B * K for B in BATCHES for (_, _, _, K, _) in SWEEP)
+    d2h = sum(4 * B * N for B in BATCHES for (_, _, N, _, _) in SWEEP)
+    L = _native.lib()
+    import ctypes as C
+
+    # contiguous pinned copies per K so the timed loop does no host-side slicing work
+    xin_cache = {}
+    for B in BATCHES:
+        for K in {k for (_, _, _, k, _) in SWEEP}:
+            t = torch.empty((B, K), dtype=torch.float32).pin_memory()
+            t.copy_(hx[B][:, :K])
+            xin_cache[(B, K)] = t
+
+    def e2e_step_cached():
+        for B in BATCHES:
+            for (name, qt, N, K, bs, w) in weights:
+                _native.check(L.pyxis_cuda_matmul_batch(ctx.handle, C.c_void_p(xin_cache[(B, K)].data_ptr()), B,
+                                                        w.handle, N, K, C.c_void_p(hy[B].data_ptr())))
+
+    e2e_step_cached()
+    barrier(ws)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step_cached()
+    e2e_s = max_over_ranks(time.perf_counter() - t0, ws)
+    e2e_value = ws * sb * args.steps / e2e_s / 1e9
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        import oracle
+
+        cores = oracle.num_cpus()
+        t, b = run_cpu_sweep(cores)
+        cpu = {"value": b / t / 1e9, "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": "one full sweep step (12 matvec calls, 6.1 GB of int4/int8 rows incl. batch-8 re-reads) "
+                         "through the C port of the reference's Rayon matmul, all host threads"}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+                "warmup": max(args.warmup, 3), "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": config_dict(ws),
+                "roofline": {"bound": "hbm", "kernel": "gemv_team_kernel (lm_head int8 151936x2048, batch 1)",
+                             "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                             "frac": achieved / peak, "traffic": profiled_traffic("gemv_team_lm_head_int8"),
+                             "algorithmic_bytes_per_launch": lm_bytes, "avg_launch_us": lm_ms * 1e3},
+                "frac_of_peak_step": value / ws / peak,
+                "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                "cpu_baseline": cpu, "clocks": clk, "gpu_launches": launches_per_step * args.steps,
+                "per_gpu_value": value / ws}
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["pyxis", "reference"], default="pyxis")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        ws = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        from oracle import build as ob
+
+        ob.build()
+        reference_arm(args, ws, rank)
+        return
+    from pyxis_b200 import build as pb
+
+    pb.build()
+    from oracle import build as ob
+
+    ob.build()
+    ws, rank, local = dist_setup()
+    try:
+        pyxis_arm(args, ws, rank, local)
+    finally:
+        if ws > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

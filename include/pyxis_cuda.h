@@ -1,0 +1,138 @@
+/*
+ * pyxis_cuda.h -- C ABI of the B200 (sm_100a) backend for pyxis's quantized matmul hot path.
+ *
+ * This is the boundary a `--cuda` backend binds from Rust (cuda_matmul.rs + build.rs, shown in
+ * INTEGRATION.md), the way src/metal_matmul.rs binds Metal.  It replaces, one for one:
+ *
+ *   Weights::quantize_int8 / quantize_int4   src/weights.rs:94-118, :120-151  -> pyxis_cuda_quantize
+ *   dequantize_weights (bf16 -> f32 arm)     src/model.rs:535-538             -> src_dtype BF16
+ *   Weights::to_metal (persistent buffers)   src/weights.rs:65-92             -> pyxis_cuda_weights_upload
+ *   read_q8_0_weights (Int8, block 32)       src/gguf.rs:245-271              -> pyxis_cuda_weights_upload
+ *   matmul(input, &Weights, out, in)         src/matmul.rs:21-97              -> pyxis_cuda_matmul
+ *   MetalMatmul::new / OnceLock singleton    src/metal_matmul.rs:199-219,
+ *                                            src/matmul.rs:6-19               -> pyxis_cuda_init
+ *   output_head::argmax                      src/output_head.rs:30-44         -> pyxis_cuda_argmax_dev
+ *
+ * Conventions
+ *  - Every function returns PYXIS_OK (0) or a positive pyxis_status; pyxis_cuda_last_error()
+ *    returns a message for the calling thread's last failure.  The reference panics on the same
+ *    conditions (shape asserts, src/matmul.rs:27-50); a Rust wrapper maps nonzero to panic!.
+ *  - Weights live in HBM in the reference's own byte layout: int8 = num_elements i8, int4 =
+ *    ceil(num_elements/2) bytes (element i in the low nibble of byte i/2 when i is even, high
+ *    nibble when odd, stored as q+8), scales = ceil(num_elements/block_size) f32, blocks running
+ *    over the flattened row-major [out_features, in_features] index.
+ *  - A context is bound to one device and owns one CUDA stream.  Calls on one context must not
+ *    overlap from several host threads; use one context per thread or per device.
+ *  - `_dev` entry points take device pointers and a cudaStream_t (NULL = the context's stream)
+ *    and do not synchronize.  The host-pointer entry points copy in, compute and copy out, and
+ *    return after the result is in host memory (src/metal_matmul.rs:311-354 behaves the same).
+ */
+#ifndef PYXIS_CUDA_H
+#define PYXIS_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    PYXIS_OK = 0,
+    PYXIS_EINVAL = 1,   /* bad argument or shape mismatch (the reference's assert!s) */
+    PYXIS_ENODEV = 2,   /* no CUDA device / not sm_100 (MetalMatmul::new -> None) */
+    PYXIS_ECUDA = 3,    /* a CUDA runtime error */
+    PYXIS_ENOMEM = 4,   /* device or host allocation failed */
+    PYXIS_ETIMEOUT = 5, /* a bounded device-side wait gave up */
+    PYXIS_EUNSUPPORTED = 6
+} pyxis_status;
+
+/* Quantized layouts (enum Weights arms, src/weights.rs:6-21). */
+typedef enum { PYXIS_QTYPE_INT8 = 1, PYXIS_QTYPE_INT4 = 2 } pyxis_qtype;
+
+/* Source element types for quantisation: F32 (Weights::F32), BF16 (Weights::Bf16, widened by
+ * u32 << 16 before quantising, src/model.rs:535-538). */
+typedef enum { PYXIS_DTYPE_F32 = 1, PYXIS_DTYPE_BF16 = 2 } pyxis_dtype;
+
+typedef struct pyxis_cuda_ctx pyxis_cuda_ctx;
+typedef struct pyxis_cuda_weights pyxis_cuda_weights;
+
+/* Message of the calling thread's last failure ("" if none).  Never NULL. */
+const char *pyxis_cuda_last_error(void);
+
+/* ABI version (major << 16 | minor). */
+uint32_t pyxis_cuda_abi_version(void);
+
+/* Create a context on `device` (MetalMatmul::new, src/metal_matmul.rs:199-219): checks the device
+ * is sm_100, creates its stream.  PYXIS_ENODEV when there is no such device. */
+int pyxis_cuda_init(int device, pyxis_cuda_ctx **ctx);
+int pyxis_cuda_destroy(pyxis_cuda_ctx *ctx);
+/* The context's stream, as a cudaStream_t. */
+void *pyxis_cuda_stream(pyxis_cuda_ctx *ctx);
+int pyxis_cuda_synchronize(pyxis_cuda_ctx *ctx);
+
+/* Quantise and pack on the device, bit-exact with Weights::quantize_int8 (qtype INT8,
+ * src/weights.rs:94-118) or Weights::quantize_int4 (qtype INT4, :120-151) applied to the f32
+ * values of `src` (num_elements of src_dtype; host memory when src_on_device == 0, else a device
+ * pointer on the context's device).  block_size > 0, any value (the model's policy is
+ * in_features for int8 and 32 for int4, src/model.rs:20,520-530).  On success *w owns HBM. */
+int pyxis_cuda_quantize(pyxis_cuda_ctx *ctx, const void *src, int src_dtype, int src_on_device,
+                        size_t num_elements, size_t block_size, int qtype,
+                        pyxis_cuda_weights **w);
+
+/* Upload weights already quantised on the host (e.g. a GGUF Q8_0 tensor as Weights::Int8 with
+ * block 32, src/gguf.rs:245-271, or a previously downloaded pack).  data: int8 -> num_elements
+ * bytes, int4 -> ceil(num_elements/2) bytes; scales: ceil(num_elements/block_size) f32. */
+int pyxis_cuda_weights_upload(pyxis_cuda_ctx *ctx, int qtype, const void *data,
+                              const float *scales, size_t num_elements, size_t block_size,
+                              pyxis_cuda_weights **w);
+
+/* Layout of a weights handle (Weights::len, src/weights.rs:35-46 = num_elements). */
+int pyxis_cuda_weights_info(const pyxis_cuda_weights *w, int *qtype, size_t *num_elements,
+                            size_t *block_size, size_t *data_bytes, size_t *num_scales);
+
+/* Copy the packed bytes and scales back to host buffers (sizes as in _upload). */
+int pyxis_cuda_weights_download(const pyxis_cuda_weights *w, void *data, float *scales);
+
+/* Device addresses of the packed bytes and scales (valid until pyxis_cuda_weights_free). */
+int pyxis_cuda_weights_device_ptrs(const pyxis_cuda_weights *w, const void **data,
+                                   const float **scales);
+
+int pyxis_cuda_weights_free(pyxis_cuda_weights *w);
+
+/* matmul(input, &weight, out_features, in_features) -> Vec<f32> (src/matmul.rs:21-97) with host
+ * buffers: input [in_features] f32, out [out_features] f32.  Checks the reference's asserts
+ * (:27-50): weight length == out_features * in_features.  Returns when out is filled. */
+int pyxis_cuda_matmul(pyxis_cuda_ctx *ctx, const float *input, const pyxis_cuda_weights *w,
+                      size_t out_features, size_t in_features, float *out);
+
+/* Batched form with host buffers: M independent rows, input [M, in_features] -> out
+ * [M, out_features] (the reference's prefill calls matmul once per position,
+ * src/attention.rs:74-79). */
+int pyxis_cuda_matmul_batch(pyxis_cuda_ctx *ctx, const float *input, size_t M,
+                            const pyxis_cuda_weights *w, size_t out_features, size_t in_features,
+                            float *out);
+
+/* Device-pointer form, asynchronous on `stream` (NULL: the context's stream).  X [M, in] f32
+ * with row stride ldx (elements), Y [M, out] f32 with row stride ldy.  M = 1..8 run the decode
+ * GEMV kernels; larger M runs the tensor-core prefill GEMM, which needs `workspace` of
+ * pyxis_cuda_matmul_workspace_size() bytes (device memory, 256-byte aligned).  A NULL workspace
+ * makes the context allocate and keep one (not allowed while the stream is being captured). */
+int pyxis_cuda_matmul_dev(pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, const float *X,
+                          size_t M, size_t ldx, size_t out_features, size_t in_features,
+                          float *Y, size_t ldy, void *workspace, size_t workspace_bytes,
+                          void *stream);
+
+/* Workspace bytes pyxis_cuda_matmul_dev needs for M rows of in_features (0 for the GEMV). */
+size_t pyxis_cuda_matmul_workspace_size(size_t M, size_t in_features);
+
+/* Row-wise argmax (src/output_head.rs:30-44: first index of the maximum under strict >) of
+ * M rows of n f32 on the device: idx[M] int32 and val[M] f32 (val may be NULL).  `index_base`
+ * is added to every index (a vocab shard's first row).  Asynchronous on `stream`. */
+int pyxis_cuda_argmax_dev(pyxis_cuda_ctx *ctx, const float *values, size_t M, size_t n,
+                          size_t ld, int64_t index_base, int32_t *idx, float *val, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,156 @@
+"""oracle -- ctypes binding of the C restatement of the reference's CPU path (liboracle.so).
+
+TEST INFRASTRUCTURE ONLY: the parity checker and the timed CPU baseline.  Imported by tests/,
+__graft_entry__.smoke() and bench.py's CPU-baseline / --impl reference legs, never by the
+product package pyxis_b200.  See pyxis_oracle.h for the reference function each entry restates.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
+
+F32, BF16, INT8, INT4 = 0, 1, 2, 3
+_vp, _sz = C.c_void_p, C.c_size_t
+_lib = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            from . import build as _b
+            _b.build()
+        L = C.CDLL(LIB_PATH)
+        L.oracle_quantize_int8.argtypes = [_vp, _sz, _sz, _vp, _vp]
+        L.oracle_quantize_int4.argtypes = [_vp, _sz, _sz, _vp, _vp]
+        L.oracle_bf16_to_f32.argtypes = [_vp, _sz, _vp]
+        L.oracle_dequantize_int8.argtypes = [_vp, _vp, _sz, _sz, _vp]
+        L.oracle_dequantize_int4.argtypes = [_vp, _vp, _sz, _sz, _vp]
+        L.oracle_q8_0_to_int8.argtypes = [_vp, _sz, _vp, _vp]
+        L.oracle_f16_to_f32.argtypes = [C.c_uint16]
+        L.oracle_f16_to_f32.restype = C.c_float
+        for n in ("oracle_dot_int8", "oracle_dot_int4"):
+            getattr(L, n).argtypes = [_vp, _vp, _vp, _sz, _sz, _sz]
+            getattr(L, n).restype = C.c_float
+        L.oracle_dot_f32.argtypes = [_vp, _vp, _sz]
+        L.oracle_dot_f32.restype = C.c_float
+        L.oracle_matmul.argtypes = [_vp, C.c_int, _vp, _vp, _sz, _sz, _sz, _vp, C.c_int]
+        L.oracle_matmul_batch.argtypes = [_vp, _sz, C.c_int, _vp, _vp, _sz, _sz, _sz, _vp, C.c_int]
+        L.oracle_argmax.argtypes = [_vp, _sz]
+        L.oracle_argmax.restype = _sz
+        L.oracle_rmsnorm.argtypes = [_vp, _vp, _sz, C.c_float]
+        L.oracle_apply_rope.argtypes = [_vp, _sz, _sz, _sz, C.c_float]
+        L.oracle_softmax.argtypes = [_vp, _sz]
+        L.oracle_silu.argtypes = [C.c_float]
+        L.oracle_silu.restype = C.c_float
+        L.oracle_greedy_decode.argtypes = [_vp, _vp, _sz, _sz, _vp, C.c_int]
+        L.oracle_num_cpus.restype = C.c_int
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray) -> C.c_void_p:
+    return a.ctypes.data_as(C.c_void_p)
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.float32))
+
+
+def num_cpus() -> int:
+    return lib().oracle_num_cpus()
+
+
+def quantize_int8(values, block_size: int):
+    """Weights::quantize_int8 (src/weights.rs:94-118) -> (data i8 [n], scales f32)."""
+    v = _f32(values)
+    n = v.size
+    data = np.empty(n, np.int8)
+    scales = np.empty((n + block_size - 1) // block_size, np.float32)
+    lib().oracle_quantize_int8(_p(v), n, block_size, _p(data), _p(scales))
+    return data, scales
+
+
+def quantize_int4(values, block_size: int):
+    """Weights::quantize_int4 (src/weights.rs:120-151) -> (data u8 [ceil(n/2)], scales f32)."""
+    v = _f32(values)
+    n = v.size
+    data = np.empty((n + 1) // 2, np.uint8)
+    scales = np.empty((n + block_size - 1) // block_size, np.float32)
+    lib().oracle_quantize_int4(_p(v), n, block_size, _p(data), _p(scales))
+    return data, scales
+
+
+def bf16_to_f32(bits) -> np.ndarray:
+    b = np.ascontiguousarray(np.asarray(bits, dtype=np.uint16))
+    out = np.empty(b.size, np.float32)
+    lib().oracle_bf16_to_f32(_p(b), b.size, _p(out))
+    return out
+
+
+def dequantize(kind: int, data, scales, block_size: int, n: int) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    d = np.ascontiguousarray(data)
+    s = _f32(scales)
+    if kind == INT8:
+        lib().oracle_dequantize_int8(_p(d), _p(s), block_size, n, _p(out))
+    else:
+        lib().oracle_dequantize_int4(_p(d), _p(s), block_size, n, _p(out))
+    return out
+
+
+def q8_0_to_int8(blocks: bytes, n: int):
+    """read_q8_0_weights (src/gguf.rs:245-271) -> (data i8 [n], scales f32 [ceil(n/32)])."""
+    b = np.frombuffer(blocks, dtype=np.uint8).copy()
+    data = np.empty(n, np.int8)
+    scales = np.empty((n + 31) // 32, np.float32)
+    lib().oracle_q8_0_to_int8(_p(b), n, _p(data), _p(scales))
+    return data, scales
+
+
+def matmul(x, kind: int, data, scales, block_size: int, out_features: int, in_features: int,
+           nthreads: int = 0) -> np.ndarray:
+    """matmul (src/matmul.rs:21-97), rows over nthreads threads (0: all cores)."""
+    X = _f32(x)
+    d = np.ascontiguousarray(data)
+    s = _f32(scales) if scales is not None else np.zeros(1, np.float32)
+    M = X.size // in_features if in_features else 1
+    Y = np.empty((M, out_features), np.float32)
+    rc = lib().oracle_matmul_batch(_p(X), M, kind, _p(d), _p(s), block_size, out_features, in_features, _p(Y),
+                                   nthreads)
+    if rc:
+        raise ValueError("oracle_matmul: shape error")
+    return Y[0] if np.asarray(x).ndim == 1 else Y
+
+
+def argmax(values) -> int:
+    v = _f32(values)
+    return int(lib().oracle_argmax(_p(v), v.size))
+
+
+def rmsnorm(x, weight, eps: float) -> np.ndarray:
+    v = _f32(x).copy()
+    w = _f32(weight)
+    lib().oracle_rmsnorm(_p(v), _p(w), v.size, eps)
+    return v
+
+
+def apply_rope(x, head_dim: int, pos: int, theta: float) -> np.ndarray:
+    v = _f32(x).copy()
+    lib().oracle_apply_rope(_p(v), v.size, head_dim, pos, theta)
+    return v
+
+
+def softmax(x) -> np.ndarray:
+    v = _f32(x).copy()
+    lib().oracle_softmax(_p(v), v.size)
+    return v
+
+
+def silu(x: float) -> float:
+    return float(lib().oracle_silu(x))

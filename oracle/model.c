@@ -1,0 +1,230 @@
+/*
+ * model.c -- restatement of the reference's decode stack around matmul (oracle, test-only):
+ * src/rmsnorm.rs, src/attention.rs, src/ffn.rs, src/transformer.rs, src/kv_cache.rs,
+ * src/embedding.rs and the greedy arm of the output head.  Used only to produce the greedy token
+ * stream the CUDA decode loop must reproduce.  f32 transcendental functions are glibc's powf,
+ * cosf, sinf, expf and sqrtf -- the same libm rustc's f32 methods call on x86-64 Linux.
+ */
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "pyxis_oracle.h"
+
+/* src/rmsnorm.rs:11-20 */
+void oracle_rmsnorm(float *x, const float *weight, size_t n, float eps) {
+    float ss = -0.0f; /* .map(|v| v * v).sum::<f32>() */
+    for (size_t i = 0; i < n; ++i) ss += x[i] * x[i];
+    float mean_square = ss / (float)n;
+    float factor = 1.0f / sqrtf(mean_square + eps);
+    for (size_t i = 0; i < n; ++i) x[i] *= factor * weight[i];
+}
+
+/* src/attention.rs:144-162 */
+void oracle_apply_rope(float *q_or_k, size_t len, size_t head_dim, size_t pos, float theta) {
+    size_t half = head_dim / 2;
+    for (size_t h = 0; h + head_dim <= len; h += head_dim) {
+        float *head = q_or_k + h;
+        for (size_t i = 0; i < half; ++i) {
+            float freq = 1.0f / powf(theta, (float)(2 * i) / (float)head_dim);
+            float angle = (float)pos * freq;
+            float c = cosf(angle), s = sinf(angle);
+            float x0 = head[i], x1 = head[i + half];
+            head[i] = x0 * c - x1 * s;
+            head[i + half] = x1 * c + x0 * s;
+        }
+    }
+}
+
+/* src/attention.rs:164-179 */
+void oracle_softmax(float *scores, size_t n) {
+    float max = -INFINITY;
+    for (size_t i = 0; i < n; ++i) max = fmaxf(max, scores[i]);
+    float sum = 0.0f;
+    for (size_t i = 0; i < n; ++i) {
+        scores[i] = expf(scores[i] - max);
+        sum += scores[i];
+    }
+    for (size_t i = 0; i < n; ++i) scores[i] /= sum;
+}
+
+/* src/ffn.rs:52-54 */
+float oracle_silu(float x) { return x / (1.0f + expf(-x)); }
+
+struct oracle_kv {
+    size_t n_layers, kv_dim, max_len;
+    size_t *len;
+    float *keys, *values; /* [n_layers][max_len][kv_dim] */
+};
+
+oracle_kv *oracle_kv_new(const oracle_model *m, size_t max_len) {
+    oracle_kv *kv = (oracle_kv *)calloc(1, sizeof(oracle_kv));
+    if (!kv) return NULL;
+    kv->n_layers = m->n_layers;
+    kv->kv_dim = m->n_kv_heads * m->head_dim;
+    kv->max_len = max_len;
+    kv->len = (size_t *)calloc(m->n_layers, sizeof(size_t));
+    size_t sz = m->n_layers * max_len * kv->kv_dim;
+    kv->keys = (float *)malloc(sz * sizeof(float));
+    kv->values = (float *)malloc(sz * sizeof(float));
+    if (!kv->len || !kv->keys || !kv->values) {
+        oracle_kv_free(kv);
+        return NULL;
+    }
+    return kv;
+}
+
+void oracle_kv_free(oracle_kv *kv) {
+    if (!kv) return;
+    free(kv->len);
+    free(kv->keys);
+    free(kv->values);
+    free(kv);
+}
+
+size_t oracle_kv_len(const oracle_kv *kv, size_t layer) { return kv->len[layer]; }
+
+static void mm(const oracle_weights *w, const float *x, size_t out, size_t in, float *y, int nt) {
+    oracle_matmul(x, w->kind, w->data, w->scales, w->block_size, out, in, y, nt);
+}
+
+/* Attention::forward (src/attention.rs:57-141).  x: [seq_len, hidden] (already input-normed),
+ * out: [seq_len, hidden]. */
+static int attention_forward(const oracle_model *m, size_t layer, const float *x, size_t seq_len,
+                             size_t start_pos, oracle_kv *kv, float *out, int nt) {
+    size_t hd = m->head_dim, H = m->hidden;
+    size_t q_dim = m->n_q_heads * hd, kv_dim = m->n_kv_heads * hd;
+    if (kv->len[layer] != start_pos) return -1; /* assert_eq!(cache.len(), start_pos) (:68) */
+    if (start_pos + seq_len > kv->max_len) return -1;
+    float *queries = (float *)malloc(seq_len * q_dim * sizeof(float));
+    float *scores = (float *)malloc((start_pos + seq_len) * sizeof(float));
+    float *attn = (float *)malloc(q_dim * sizeof(float));
+    if (!queries || !scores || !attn) {
+        free(queries); free(scores); free(attn);
+        return -1;
+    }
+    float *kbase = kv->keys + layer * kv->max_len * kv_dim;
+    float *vbase = kv->values + layer * kv->max_len * kv_dim;
+    for (size_t pos = 0; pos < seq_len; ++pos) { /* :74-98 */
+        const float *in = x + pos * H;
+        float *q = queries + pos * q_dim;
+        float *k = kbase + (start_pos + pos) * kv_dim; /* cache.append (:100) writes here */
+        float *v = vbase + (start_pos + pos) * kv_dim;
+        mm(&m->wq[layer], in, q_dim, H, q, nt);
+        mm(&m->wk[layer], in, kv_dim, H, k, nt);
+        mm(&m->wv[layer], in, kv_dim, H, v, nt);
+        if (m->q_norm && m->q_norm[layer])
+            for (size_t h = 0; h < m->n_q_heads; ++h)
+                oracle_rmsnorm(q + h * hd, m->q_norm[layer], hd, m->rms_eps);
+        if (m->k_norm && m->k_norm[layer])
+            for (size_t h = 0; h < m->n_kv_heads; ++h)
+                oracle_rmsnorm(k + h * hd, m->k_norm[layer], hd, m->rms_eps);
+        oracle_apply_rope(q, q_dim, hd, start_pos + pos, m->rope_theta);
+        oracle_apply_rope(k, kv_dim, hd, start_pos + pos, m->rope_theta);
+    }
+    kv->len[layer] += seq_len;
+    size_t cached_len = kv->len[layer];
+    float scale = sqrtf((float)hd); /* :105 */
+    for (size_t pos = 0; pos < seq_len; ++pos) { /* :107-138 */
+        for (size_t i = 0; i < q_dim; ++i) attn[i] = 0.0f;
+        for (size_t qh = 0; qh < m->n_q_heads; ++qh) {
+            size_t kvh = qh * m->n_kv_heads / m->n_q_heads; /* :111 */
+            const float *q = queries + pos * q_dim + qh * hd;
+            size_t max_key_pos = start_pos + pos;
+            for (size_t kp = 0; kp < cached_len; ++kp) scores[kp] = -INFINITY;
+            for (size_t kp = 0; kp <= max_key_pos && kp < cached_len; ++kp) {
+                const float *k = kbase + kp * kv_dim + kvh * hd;
+                float dot = -0.0f;
+                for (size_t d = 0; d < hd; ++d) dot += q[d] * k[d];
+                scores[kp] = dot / scale;
+            }
+            oracle_softmax(scores, cached_len);
+            float *o = attn + qh * hd;
+            for (size_t kp = 0; kp < cached_len; ++kp) {
+                const float *v = vbase + kp * kv_dim + kvh * hd;
+                for (size_t d = 0; d < hd; ++d) o[d] += scores[kp] * v[d];
+            }
+        }
+        mm(&m->wo[layer], attn, H, q_dim, out + pos * H, nt); /* :136 */
+    }
+    free(queries);
+    free(scores);
+    free(attn);
+    return 0;
+}
+
+/* Ffn::forward (src/ffn.rs:33-50) for one position. */
+static void ffn_forward(const oracle_model *m, size_t layer, const float *x, float *out,
+                        float *gate, float *up, int nt) {
+    mm(&m->wgate[layer], x, m->ffn, m->hidden, gate, nt);
+    mm(&m->wup[layer], x, m->ffn, m->hidden, up, nt);
+    for (size_t i = 0; i < m->ffn; ++i) gate[i] = oracle_silu(gate[i]) * up[i];
+    mm(&m->wdown[layer], gate, m->hidden, m->ffn, out, nt);
+}
+
+/* TransformerBlock::forward (src/transformer.rs:28-62) + Transformer::forward (:80-90). */
+int oracle_transformer_forward(const oracle_model *m, float *x, size_t seq_len, size_t start_pos,
+                               oracle_kv *kv, int nt) {
+    size_t H = m->hidden;
+    float *residual = (float *)malloc(seq_len * H * sizeof(float));
+    float *attn = (float *)malloc(seq_len * H * sizeof(float));
+    float *gate = (float *)malloc(m->ffn * sizeof(float));
+    float *up = (float *)malloc(m->ffn * sizeof(float));
+    float *fo = (float *)malloc(H * sizeof(float));
+    int rc = 0;
+    if (!residual || !attn || !gate || !up || !fo) rc = -1;
+    for (size_t l = 0; l < m->n_layers && rc == 0; ++l) {
+        memcpy(residual, x, seq_len * H * sizeof(float));
+        for (size_t p = 0; p < seq_len; ++p) oracle_rmsnorm(x + p * H, m->input_norm[l], H, m->rms_eps);
+        rc = attention_forward(m, l, x, seq_len, start_pos, kv, attn, nt);
+        if (rc) break;
+        for (size_t i = 0; i < seq_len * H; ++i) x[i] = residual[i] + attn[i];
+        memcpy(residual, x, seq_len * H * sizeof(float));
+        for (size_t p = 0; p < seq_len; ++p) oracle_rmsnorm(x + p * H, m->post_norm[l], H, m->rms_eps);
+        for (size_t p = 0; p < seq_len; ++p) {
+            ffn_forward(m, l, x + p * H, fo, gate, up, nt);
+            for (size_t i = 0; i < H; ++i) x[p * H + i] = residual[p * H + i] + fo[i];
+        }
+    }
+    if (rc == 0)
+        for (size_t p = 0; p < seq_len; ++p) oracle_rmsnorm(x + p * H, m->final_norm, H, m->rms_eps);
+    free(residual);
+    free(attn);
+    free(gate);
+    free(up);
+    free(fo);
+    return rc;
+}
+
+/* Model::generate (src/model.rs:245-285) with the sampler replaced by output_head::argmax. */
+int oracle_greedy_decode(const oracle_model *m, const int32_t *prompt, size_t n_prompt,
+                         size_t n_new, int32_t *out_tokens, int nt) {
+    if (n_prompt == 0 || n_new == 0) return 0;
+    size_t H = m->hidden;
+    oracle_kv *kv = oracle_kv_new(m, n_prompt + n_new);
+    float *x = (float *)malloc(n_prompt * H * sizeof(float));
+    float *logits = (float *)malloc(m->vocab * sizeof(float));
+    int rc = (kv && x && logits) ? 0 : -1;
+    for (size_t p = 0; p < n_prompt && rc == 0; ++p) {
+        if (prompt[p] < 0 || (size_t)prompt[p] >= m->vocab) rc = -1; /* embedding.rs:19 */
+        else memcpy(x + p * H, m->embedding + (size_t)prompt[p] * H, H * sizeof(float));
+    }
+    if (rc == 0) rc = oracle_transformer_forward(m, x, n_prompt, 0, kv, nt);
+    if (rc == 0) {
+        mm(&m->lm_head, x + (n_prompt - 1) * H, m->vocab, H, logits, nt);
+        int32_t next = (int32_t)oracle_argmax(logits, m->vocab);
+        for (size_t i = 0; i < n_new; ++i) {
+            out_tokens[i] = next;
+            if (i + 1 == n_new) break;
+            memcpy(x, m->embedding + (size_t)next * H, H * sizeof(float));
+            rc = oracle_transformer_forward(m, x, 1, n_prompt + i, kv, nt);
+            if (rc) break;
+            mm(&m->lm_head, x, m->vocab, H, logits, nt);
+            next = (int32_t)oracle_argmax(logits, m->vocab);
+        }
+    }
+    oracle_kv_free(kv);
+    free(x);
+    free(logits);
+    return rc;
+}

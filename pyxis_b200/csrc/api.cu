@@ -1,0 +1,370 @@
+// api.cu -- the extern "C" boundary (include/pyxis_cuda.h): contexts, device-resident weights,
+// argument checks that mirror the reference's asserts, and kernel dispatch.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+
+#include "../../include/pyxis_cuda.h"
+#include "argmax.h"
+#include "kernels.h"
+
+using namespace pyxis;
+
+struct pyxis_cuda_ctx {
+    int device;
+    int num_sms;
+    cudaStream_t stream;
+    // staging for the host-pointer entry points (grown on demand)
+    float *dx = nullptr;
+    size_t dx_cap = 0;
+    float *dy = nullptr;
+    size_t dy_cap = 0;
+    // workspace kept for pyxis_cuda_matmul_dev calls that pass none
+    void *ws = nullptr;
+    size_t ws_cap = 0;
+    // argmax scratch (allocated and zeroed at init)
+    ArgmaxScratch amax{};
+    void *amax_mem = nullptr;
+};
+
+struct pyxis_cuda_weights {
+    int device;
+    int qtype;
+    size_t num_elements, block_size;
+    size_t data_bytes, num_scales;
+    uint8_t *data;   // one allocation: data, padded to 256 B, then scales
+    float *scales;
+};
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+    return fail(PYXIS_ECUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+#define PYXIS_CUDA_TRY(expr, what)                      \
+    do {                                                \
+        cudaError_t e_ = (expr);                        \
+        if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+    } while (0)
+
+// Makes ctx's device current for the call and restores the caller's device afterwards.
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+size_t div_ceil(size_t a, size_t b) { return (a + b - 1) / b; }
+
+size_t packed_bytes(int qtype, size_t n) { return qtype == PYXIS_QTYPE_INT8 ? n : div_ceil(n, 2); }
+
+int grow(float **buf, size_t *cap, size_t need) {
+    if (need <= *cap) return PYXIS_OK;
+    if (*buf) cudaFree(*buf);
+    *buf = nullptr;
+    *cap = 0;
+    size_t n = need < 4096 ? 4096 : need;
+    PYXIS_CUDA_TRY(cudaMalloc(buf, n * sizeof(float)), "cudaMalloc(staging)");
+    *cap = n;
+    return PYXIS_OK;
+}
+
+int alloc_weights(pyxis_cuda_ctx *ctx, int qtype, size_t n, size_t bs, pyxis_cuda_weights **out) {
+    auto *w = new (std::nothrow) pyxis_cuda_weights{};
+    if (!w) return fail(PYXIS_ENOMEM, "host allocation failed");
+    w->device = ctx->device;
+    w->qtype = qtype;
+    w->num_elements = n;
+    w->block_size = bs;
+    w->data_bytes = packed_bytes(qtype, n);
+    w->num_scales = div_ceil(n, bs);
+    size_t off = div_ceil(w->data_bytes, 256) * 256;
+    size_t total = off + w->num_scales * sizeof(float);
+    void *mem = nullptr;
+    cudaError_t e = cudaMalloc(&mem, total ? total : 256);
+    if (e != cudaSuccess) {
+        delete w;
+        if (e == cudaErrorMemoryAllocation) {
+            cudaGetLastError();
+            return fail(PYXIS_ENOMEM, "cudaMalloc(%zu bytes) for weights failed", total);
+        }
+        return cuda_fail(e, "cudaMalloc(weights)");
+    }
+    w->data = (uint8_t *)mem;
+    w->scales = (float *)((uint8_t *)mem + off);
+    *out = w;
+    return PYXIS_OK;
+}
+
+cudaStream_t pick_stream(pyxis_cuda_ctx *ctx, void *stream) {
+    return stream ? (cudaStream_t)stream : ctx->stream;
+}
+
+QMatrix qmatrix(const pyxis_cuda_weights *w, size_t N, size_t K) {
+    return QMatrix{w->qtype, w->data, w->scales, w->block_size, N, K};
+}
+
+// The reference's matmul asserts (src/matmul.rs:27-50).
+int check_matmul(const pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, size_t out_features,
+                 size_t in_features) {
+    if (!ctx || !w) return fail(PYXIS_EINVAL, "null context or weights");
+    if (w->device != ctx->device)
+        return fail(PYXIS_EINVAL, "weights live on device %d, context on device %d", w->device, ctx->device);
+    if (w->num_elements != out_features * in_features)
+        return fail(PYXIS_EINVAL, "weight.len() = %zu != out_features * in_features = %zu * %zu",
+                    w->num_elements, out_features, in_features);
+    if (w->block_size == 0) return fail(PYXIS_EINVAL, "block_size must be > 0");
+    return PYXIS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *pyxis_cuda_last_error(void) { return g_last_error.c_str(); }
+
+uint32_t pyxis_cuda_abi_version(void) { return (1u << 16) | 0u; }
+
+int pyxis_cuda_init(int device, pyxis_cuda_ctx **out) {
+    if (!out) return fail(PYXIS_EINVAL, "null output pointer");
+    *out = nullptr;
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess || count == 0) {
+        cudaGetLastError();
+        return fail(PYXIS_ENODEV, "no CUDA device (%s)", cudaGetErrorString(e));
+    }
+    if (device < 0 || device >= count) return fail(PYXIS_ENODEV, "device %d out of range (%d devices)", device, count);
+    cudaDeviceProp prop;
+    PYXIS_CUDA_TRY(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+    if (prop.major != 10 || prop.minor != 0)
+        return fail(PYXIS_ENODEV, "device %d is sm_%d%d; this library is built for sm_100a (B200)", device,
+                    prop.major, prop.minor);
+    DeviceGuard g(device);
+    auto *ctx = new (std::nothrow) pyxis_cuda_ctx{};
+    if (!ctx) return fail(PYXIS_ENOMEM, "host allocation failed");
+    ctx->device = device;
+    ctx->num_sms = prop.multiProcessorCount;
+    e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        delete ctx;
+        return cuda_fail(e, "cudaStreamCreate");
+    }
+    size_t ab = argmax_scratch_bytes(kArgmaxMaxRows);
+    e = cudaMalloc(&ctx->amax_mem, ab);
+    if (e == cudaSuccess) e = cudaMemsetAsync(ctx->amax_mem, 0, ab, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) {
+        pyxis_cuda_destroy(ctx);
+        return cuda_fail(e, "argmax scratch");
+    }
+    ctx->amax.partial = (uint64_t *)ctx->amax_mem;
+    ctx->amax.ticket = (unsigned *)((uint8_t *)ctx->amax_mem + (size_t)kArgmaxMaxRows * kArgmaxMaxCtasPerRow * sizeof(uint64_t));
+    *out = ctx;
+    return PYXIS_OK;
+}
+
+int pyxis_cuda_destroy(pyxis_cuda_ctx *ctx) {
+    if (!ctx) return PYXIS_OK;
+    DeviceGuard g(ctx->device);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    cudaFree(ctx->dx);
+    cudaFree(ctx->dy);
+    cudaFree(ctx->ws);
+    cudaFree(ctx->amax_mem);
+    if (ctx->stream) cudaStreamDestroy(ctx->stream);
+    delete ctx;
+    return PYXIS_OK;
+}
+
+void *pyxis_cuda_stream(pyxis_cuda_ctx *ctx) { return ctx ? (void *)ctx->stream : nullptr; }
+
+int pyxis_cuda_synchronize(pyxis_cuda_ctx *ctx) {
+    if (!ctx) return fail(PYXIS_EINVAL, "null context");
+    DeviceGuard g(ctx->device);
+    PYXIS_CUDA_TRY(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    return PYXIS_OK;
+}
+
+int pyxis_cuda_quantize(pyxis_cuda_ctx *ctx, const void *src, int src_dtype, int src_on_device,
+                        size_t n, size_t block_size, int qtype, pyxis_cuda_weights **out) {
+    if (!ctx || !out) return fail(PYXIS_EINVAL, "null context or output pointer");
+    *out = nullptr;
+    if (block_size == 0) return fail(PYXIS_EINVAL, "block_size must be > 0 (assert!, src/weights.rs:95)");
+    if (qtype != PYXIS_QTYPE_INT8 && qtype != PYXIS_QTYPE_INT4) return fail(PYXIS_EINVAL, "unknown qtype %d", qtype);
+    if (src_dtype != PYXIS_DTYPE_F32 && src_dtype != PYXIS_DTYPE_BF16) return fail(PYXIS_EINVAL, "unknown src dtype %d", src_dtype);
+    if (!src && n) return fail(PYXIS_EINVAL, "null source");
+    DeviceGuard g(ctx->device);
+    pyxis_cuda_weights *w = nullptr;
+    int rc = alloc_weights(ctx, qtype, n, block_size, &w);
+    if (rc) return rc;
+    const size_t esize = src_dtype == PYXIS_DTYPE_F32 ? 4 : 2;
+    const void *dsrc = src;
+    void *tmp = nullptr;
+    cudaError_t e = cudaSuccess;
+    if (!src_on_device && n) {
+        e = cudaMalloc(&tmp, n * esize);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(tmp, src, n * esize, cudaMemcpyHostToDevice, ctx->stream);
+        dsrc = tmp;
+    }
+    if (e == cudaSuccess)
+        e = launch_quantize(dsrc, src_dtype, n, block_size, qtype, w->data, w->scales, ctx->num_sms, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (tmp) cudaFree(tmp);
+    if (e != cudaSuccess) {
+        pyxis_cuda_weights_free(w);
+        return cuda_fail(e, "quantize");
+    }
+    *out = w;
+    return PYXIS_OK;
+}
+
+int pyxis_cuda_weights_upload(pyxis_cuda_ctx *ctx, int qtype, const void *data, const float *scales,
+                              size_t n, size_t block_size, pyxis_cuda_weights **out) {
+    if (!ctx || !out) return fail(PYXIS_EINVAL, "null context or output pointer");
+    *out = nullptr;
+    if (block_size == 0) return fail(PYXIS_EINVAL, "block_size must be > 0");
+    if (qtype != PYXIS_QTYPE_INT8 && qtype != PYXIS_QTYPE_INT4) return fail(PYXIS_EINVAL, "unknown qtype %d", qtype);
+    if (n && (!data || !scales)) return fail(PYXIS_EINVAL, "null data or scales");
+    DeviceGuard g(ctx->device);
+    pyxis_cuda_weights *w = nullptr;
+    int rc = alloc_weights(ctx, qtype, n, block_size, &w);
+    if (rc) return rc;
+    cudaError_t e = cudaSuccess;
+    if (w->data_bytes) e = cudaMemcpyAsync(w->data, data, w->data_bytes, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess && w->num_scales)
+        e = cudaMemcpyAsync(w->scales, scales, w->num_scales * sizeof(float), cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) {
+        pyxis_cuda_weights_free(w);
+        return cuda_fail(e, "weights upload");
+    }
+    *out = w;
+    return PYXIS_OK;
+}
+
+int pyxis_cuda_weights_info(const pyxis_cuda_weights *w, int *qtype, size_t *n, size_t *bs,
+                            size_t *data_bytes, size_t *num_scales) {
+    if (!w) return fail(PYXIS_EINVAL, "null weights");
+    if (qtype) *qtype = w->qtype;
+    if (n) *n = w->num_elements;
+    if (bs) *bs = w->block_size;
+    if (data_bytes) *data_bytes = w->data_bytes;
+    if (num_scales) *num_scales = w->num_scales;
+    return PYXIS_OK;
+}
+
+int pyxis_cuda_weights_download(const pyxis_cuda_weights *w, void *data, float *scales) {
+    if (!w) return fail(PYXIS_EINVAL, "null weights");
+    DeviceGuard g(w->device);
+    if (data && w->data_bytes) PYXIS_CUDA_TRY(cudaMemcpy(data, w->data, w->data_bytes, cudaMemcpyDeviceToHost), "download data");
+    if (scales && w->num_scales)
+        PYXIS_CUDA_TRY(cudaMemcpy(scales, w->scales, w->num_scales * sizeof(float), cudaMemcpyDeviceToHost), "download scales");
+    return PYXIS_OK;
+}
+
+int pyxis_cuda_weights_device_ptrs(const pyxis_cuda_weights *w, const void **data, const float **scales) {
+    if (!w) return fail(PYXIS_EINVAL, "null weights");
+    if (data) *data = w->data;
+    if (scales) *scales = w->scales;
+    return PYXIS_OK;
+}
+
+int pyxis_cuda_weights_free(pyxis_cuda_weights *w) {
+    if (!w) return PYXIS_OK;
+    DeviceGuard g(w->device);
+    cudaFree(w->data);
+    delete w;
+    return PYXIS_OK;
+}
+
+size_t pyxis_cuda_matmul_workspace_size(size_t M, size_t in_features) {
+    (void)M;
+    (void)in_features;
+    return 0;
+}
+
+int pyxis_cuda_matmul_dev(pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, const float *X, size_t M,
+                          size_t ldx, size_t out_features, size_t in_features, float *Y, size_t ldy,
+                          void *workspace, size_t workspace_bytes, void *stream) {
+    int rc = check_matmul(ctx, w, out_features, in_features);
+    if (rc) return rc;
+    (void)workspace;
+    (void)workspace_bytes;
+    if (M == 0 || out_features == 0) return PYXIS_OK;
+    if (!X || !Y) return fail(PYXIS_EINVAL, "null X or Y");
+    if (M > 1 && (ldx < in_features || ldy < out_features)) return fail(PYXIS_EINVAL, "row stride smaller than the row");
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = pick_stream(ctx, stream);
+    QMatrix q = qmatrix(w, out_features, in_features);
+    for (size_t m0 = 0; m0 < M; m0 += 8) {
+        size_t b = M - m0 < 8 ? M - m0 : 8;
+        cudaError_t e = launch_gemv(q, X + m0 * ldx, b, ldx, Y + m0 * ldy, ldy, ctx->num_sms, st);
+        if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
+    }
+    return PYXIS_OK;
+}
+
+int pyxis_cuda_matmul_batch(pyxis_cuda_ctx *ctx, const float *input, size_t M, const pyxis_cuda_weights *w,
+                            size_t out_features, size_t in_features, float *out) {
+    int rc = check_matmul(ctx, w, out_features, in_features);
+    if (rc) return rc;
+    if (M == 0 || out_features == 0) return PYXIS_OK;
+    if (!input || !out) return fail(PYXIS_EINVAL, "null input or output");
+    DeviceGuard g(ctx->device);
+    rc = grow(&ctx->dx, &ctx->dx_cap, M * in_features);
+    if (rc) return rc;
+    rc = grow(&ctx->dy, &ctx->dy_cap, M * out_features);
+    if (rc) return rc;
+    PYXIS_CUDA_TRY(cudaMemcpyAsync(ctx->dx, input, M * in_features * sizeof(float), cudaMemcpyHostToDevice, ctx->stream), "copy input");
+    rc = pyxis_cuda_matmul_dev(ctx, w, ctx->dx, M, in_features, out_features, in_features, ctx->dy,
+                               out_features, nullptr, 0, nullptr);
+    if (rc) return rc;
+    PYXIS_CUDA_TRY(cudaMemcpyAsync(out, ctx->dy, M * out_features * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream), "copy output");
+    PYXIS_CUDA_TRY(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    return PYXIS_OK;
+}
+
+int pyxis_cuda_matmul(pyxis_cuda_ctx *ctx, const float *input, const pyxis_cuda_weights *w,
+                      size_t out_features, size_t in_features, float *out) {
+    return pyxis_cuda_matmul_batch(ctx, input, 1, w, out_features, in_features, out);
+}
+
+int pyxis_cuda_argmax_dev(pyxis_cuda_ctx *ctx, const float *values, size_t M, size_t n, size_t ld,
+                          int64_t index_base, int32_t *idx, float *val, void *stream) {
+    if (!ctx) return fail(PYXIS_EINVAL, "null context");
+    if (M == 0) return PYXIS_OK;
+    if (n == 0) return fail(PYXIS_EINVAL, "argmax of an empty row (assert!, src/output_head.rs:31)");
+    if (n > 0xFFFFFFFFull) return fail(PYXIS_EINVAL, "row too long for argmax (%zu)", n);
+    if (M > (size_t)kArgmaxMaxRows) return fail(PYXIS_EINVAL, "argmax: %zu rows > %d per call", M, kArgmaxMaxRows);
+    if (M > 1 && ld < n) return fail(PYXIS_EINVAL, "row stride smaller than the row");
+    if (!values || !idx) return fail(PYXIS_EINVAL, "null values or idx");
+    DeviceGuard g(ctx->device);
+    cudaError_t e = launch_argmax_scratch(values, M, n, ld, index_base, idx, val, ctx->amax, ctx->num_sms,
+                                          pick_stream(ctx, stream));
+    if (e != cudaSuccess) return cuda_fail(e, "argmax launch");
+    return PYXIS_OK;
+}
+
+}  // extern "C"

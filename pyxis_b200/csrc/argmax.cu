@@ -1,0 +1,105 @@
+// argmax.cu -- row-wise argmax with the reference's tie and NaN rules (src/output_head.rs:30-44).
+//
+// The reference scans left to right and replaces the running maximum only on a strict `>`:
+//   - ties go to the lowest index;
+//   - a NaN is never `>` anything, so NaNs are skipped -- unless values[0] is NaN, in which case
+//     nothing ever beats it and the answer is 0;
+//   - +0.0 > -0.0 is false, so the two zeros tie (lowest index wins).
+// Here every element becomes a 64-bit key (order-preserving float bits << 32 | ~index), the
+// maximum key is the reference's answer, and max is associative, so CTAs reduce their segments
+// in any order.  One launch: each CTA writes its segment's key to scratch, and the last CTA to
+// finish a row (atomic ticket) reduces the row's keys and re-arms the ticket to 0 for the next
+// launch.  Scratch: ArgmaxScratch, zeroed once when it is allocated.
+#include "argmax.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace pyxis {
+
+PYXIS_DEVINL uint64_t argmax_key(float v, uint32_t idx) {
+    if (isnan(v)) return 0;  // below every number, including -inf
+    if (v == 0.0f) v = 0.0f; // -0.0 ties with +0.0
+    uint32_t u = __float_as_uint(v);
+    uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((uint64_t)ord << 32) | (uint64_t)(0xFFFFFFFFu - idx);
+}
+
+PYXIS_DEVINL uint64_t warp_max_u64(uint64_t k) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        uint64_t other = __shfl_xor_sync(0xffffffffu, k, o);
+        k = other > k ? other : k;
+    }
+    return k;
+}
+
+// Reduce a CTA's 64-bit keys; result valid in thread 0.
+PYXIS_DEVINL uint64_t cta_max_u64(uint64_t k, uint64_t *red) {
+    k = warp_max_u64(k);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) red[warp] = k;
+    __syncthreads();
+    if (warp == 0) {
+        k = lane < (int)(blockDim.x >> 5) ? red[lane] : 0;
+        k = warp_max_u64(k);
+    }
+    return k;
+}
+
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(
+    const float *__restrict__ values, size_t n, size_t ld, int64_t index_base,
+    int32_t *__restrict__ idx_out, float *__restrict__ val_out, ArgmaxScratch s) {
+    __shared__ uint64_t red[kArgmaxThreads / 32];
+    __shared__ bool last;
+    const size_t row = blockIdx.y;
+    const float *v = values + row * ld;
+    const size_t seg = (n + gridDim.x - 1) / gridDim.x;
+    const size_t beg = (size_t)blockIdx.x * seg;
+    const size_t end = beg + seg < n ? beg + seg : n;
+    uint64_t k = 0;
+    for (size_t i = beg + threadIdx.x; i < end; i += blockDim.x) {
+        uint64_t c = argmax_key(__ldg(v + i), (uint32_t)i);
+        k = c > k ? c : k;
+    }
+    k = cta_max_u64(k, red);
+    if (threadIdx.x == 0) {
+        s.partial[row * gridDim.x + blockIdx.x] = k;
+        __threadfence();
+        const unsigned ticket = atomicAdd(&s.ticket[row], 1u);
+        last = ticket == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    uint64_t m = 0;
+    for (unsigned c = threadIdx.x; c < gridDim.x; c += blockDim.x) {
+        uint64_t p = __ldcg(&s.partial[row * gridDim.x + c]);
+        m = p > m ? p : m;
+    }
+    m = cta_max_u64(m, red);
+    if (threadIdx.x == 0) {
+        uint32_t i = 0xFFFFFFFFu - (uint32_t)(m & 0xFFFFFFFFu);
+        if (isnan(v[0]) || m == 0) i = 0;  // values[0] NaN wins; all-NaN row -> 0 as well
+        idx_out[row] = (int32_t)(index_base + (int64_t)i);
+        if (val_out) val_out[row] = v[i];
+        s.ticket[row] = 0;  // re-arm for the next launch on this scratch
+    }
+}
+
+int argmax_ctas_per_row(size_t n, int num_sms) {
+    size_t c = (n + 4095) / 4096;
+    if (c > (size_t)kArgmaxMaxCtasPerRow) c = kArgmaxMaxCtasPerRow;
+    if (c > (size_t)num_sms) c = num_sms;
+    return c < 1 ? 1 : (int)c;
+}
+
+cudaError_t launch_argmax_scratch(const float *values, size_t M, size_t n, size_t ld,
+                                  int64_t index_base, int32_t *idx, float *val,
+                                  const ArgmaxScratch &s, int num_sms, cudaStream_t st) {
+    if (M == 0) return cudaSuccess;
+    dim3 grid(argmax_ctas_per_row(n, num_sms), (unsigned)M);
+    argmax_kernel<<<grid, kArgmaxThreads, 0, st>>>(values, n, ld, index_base, idx, val, s);
+    return cudaGetLastError();
+}
+
+}  // namespace pyxis

@@ -1,0 +1,33 @@
+// kernels.h -- internal launcher interface between the C ABI (api.cu) and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace pyxis {
+
+enum { kSrcF32 = 1, kSrcBF16 = 2 };  // == PYXIS_DTYPE_*
+enum { kQInt8 = 1, kQInt4 = 2 };     // == PYXIS_QTYPE_*
+
+// A quantized matrix [N, K] in the reference layout (see pyxis_cuda.h).
+struct QMatrix {
+    int qtype;
+    const uint8_t *data;
+    const float *scales;
+    size_t block_size;
+    size_t N, K;
+};
+
+cudaError_t launch_quantize(const void *src, int src_kind, size_t n, size_t bs, int qtype,
+                            void *data, float *scales, int num_sms, cudaStream_t st);
+
+// Decode GEMV: Y[b, :] = W X[b, :] for b < B (B = 1..8).  Picks the register-resident-x team
+// kernel, the shared-memory-x kernel or the generic kernel by shape (gemv.cu).
+cudaError_t launch_gemv(const QMatrix &w, const float *X, size_t B, size_t ldx, float *Y,
+                        size_t ldy, int num_sms, cudaStream_t st);
+
+// Name of the kernel launch_gemv would pick (for tests and the bench's launch accounting).
+const char *gemv_kernel_name(const QMatrix &w, size_t B);
+
+}  // namespace pyxis

@@ -1,0 +1,118 @@
+"""Decode GEMV parity: the CUDA matmul against the oracle's restatement of the reference's
+quantized CPU matmul (src/matmul.rs:21-97, :149-173, :297-317) on the same seeded inputs.
+Bar: max_i |y_i - ref_i| / max(|ref_i|, 1e-3 max|ref|) <= 1e-3 (tests/parity.py)."""
+import numpy as np
+import pytest
+
+import oracle
+import pyxis_b200 as px
+from parity import MATMUL_TOL, normwise_err, rel_err
+
+pytestmark = pytest.mark.gpu
+
+KIND = {"int8": oracle.INT8, "int4": oracle.INT4}
+
+
+def make(qt, N, K, bs, seed):
+    bits = px.synth_normal_bf16(seed, N * K, 0.02)
+    vals = oracle.bf16_to_f32(bits)
+    w = px.Weights.quantize_int8(bits, bs) if qt == "int8" else px.Weights.quantize_int4(bits, bs)
+    od, os_ = (oracle.quantize_int8 if qt == "int8" else oracle.quantize_int4)(vals, bs)
+    return w, od, os_
+
+
+def ref_matmul(qt, od, os_, bs, X, N, K):
+    return oracle.matmul(X, KIND[qt], od, os_, bs, N, K)
+
+
+# The benchmark shapes: gate_proj int8 per-row (one scale per row, the model's int8 policy), and
+# the int4 group-32 sweep (q, kv, gate/up, down).
+CONFIG_SHAPES = [
+    ("int8", 6144, 2048, 2048),
+    ("int4", 2048, 2048, 32),
+    ("int4", 1024, 2048, 32),
+    ("int4", 6144, 2048, 32),
+    ("int4", 2048, 6144, 32),
+    ("int8", 2048, 6144, 6144),
+    ("int8", 6144, 2048, 32),  # GGUF Q8_0 layout
+]
+
+
+@pytest.mark.parametrize("qt,N,K,bs", CONFIG_SHAPES)
+@pytest.mark.parametrize("B", [1, 2, 8])
+def test_gemv_matches_oracle(qt, N, K, bs, B):
+    w, od, os_ = make(qt, N, K, bs, seed=N * 7 + K + bs)
+    X = px.synth_normal_f32(1000 + B, B * K, 1.0).reshape(B, K)
+    ref = ref_matmul(qt, od, os_, bs, X, N, K)
+    Y = px.matmul_batch(X, w, N, K)
+    assert Y.shape == (B, N)
+    e = rel_err(Y, ref)
+    assert e <= MATMUL_TOL, (e, normwise_err(Y, ref))
+
+
+def test_lm_head_int8_full_size():
+    """lm_head 151936 x 2048, int8 per-row quantised copy of the tied embedding (src/model.rs:219-224)."""
+    N, K = 151936, 2048
+    w, od, os_ = make("int8", N, K, K, seed=0x11EAD)
+    x = px.synth_normal_f32(5, K, 1.0)
+    ref = ref_matmul("int8", od, os_, K, x, N, K)
+    y = px.matmul(x, w, N, K)
+    assert rel_err(y, ref) <= MATMUL_TOL
+    assert px.argmax(y) == oracle.argmax(ref)
+
+
+@pytest.mark.parametrize("qt,N,K,bs", [
+    ("int8", 2, 3, 3), ("int4", 2, 3, 4),          # the reference's own matmul tests (odd K, straddling blocks)
+    ("int8", 1, 1, 1), ("int4", 1, 1, 32), ("int4", 5, 7, 3), ("int8", 17, 100, 7),
+    ("int4", 33, 96, 32), ("int8", 100, 48, 16), ("int4", 64, 64, 64), ("int4", 300, 4096, 4096),
+    ("int8", 129, 8192, 8192), ("int4", 3, 1024 * 9, 32), ("int8", 7, 160, 32), ("int4", 31, 32 * 5, 160),
+])
+@pytest.mark.parametrize("B", [1, 3])
+def test_gemv_odd_shapes(qt, N, K, bs, B):
+    w, od, os_ = make(qt, N, K, bs, seed=N + 31 * K + bs)
+    X = px.synth_normal_f32(77 + B, B * K, 1.0).reshape(B, K)
+    ref = ref_matmul(qt, od, os_, bs, X, N, K)
+    Y = px.matmul_batch(X, w, N, K)
+    assert rel_err(Y, ref) <= MATMUL_TOL
+
+
+def test_matmul_rejects_shape_mismatch():
+    w, _, _ = make("int8", 4, 8, 8, seed=1)
+    with pytest.raises(px.PyxisError):
+        px.matmul(np.zeros(8, np.float32), w, 5, 8)  # weight.len() != out * in (src/matmul.rs:28)
+    with pytest.raises(px.PyxisError):
+        px.matmul(np.zeros(7, np.float32), w, 4, 8)  # input.len() != in_features (src/matmul.rs:27)
+
+
+def test_matmul_dev_strided_rows():
+    import torch
+    N, K = 2048, 2048
+    w, od, os_ = make("int4", N, K, 32, seed=21)
+    X = torch.from_numpy(px.synth_normal_f32(3, 4 * (K + 64), 1.0).reshape(4, K + 64)).cuda()[:, :K]
+    Y = torch.zeros((4, N + 32), device="cuda")[:, :N]
+    px.matmul_dev(X, w, N, K, Y=Y)
+    torch.cuda.synchronize()
+    ref = ref_matmul("int4", od, os_, 32, X.cpu().numpy(), N, K)
+    assert rel_err(Y.cpu().numpy(), ref) <= MATMUL_TOL
+
+
+def test_argmax_rules():
+    import torch
+    assert px.argmax([1.0, 3.0, 3.0, 2.0]) == 1
+    assert px.argmax([np.nan, 3.0, 2.0]) == 0
+    assert px.argmax([1.0, np.nan, 2.0]) == 2
+    assert px.argmax([-0.0, 0.0]) == 0
+    assert px.argmax([-np.inf, -np.inf]) == 0
+    rng = np.random.default_rng(0)
+    v = rng.standard_normal((5, 151936)).astype(np.float32)
+    v[2, 100] = v[2, 90000] = 50.0  # tie: lowest index
+    t = torch.from_numpy(v).cuda()
+    idx, val = px.argmax_dev(t, index_base=1000)
+    torch.cuda.synchronize()
+    for r in range(5):
+        assert int(idx[r]) == oracle.argmax(v[r]) + 1000
+        assert float(val[r]) == float(v[r].max())
+    for _ in range(3):  # the single-launch reduction re-arms its scratch every call
+        idx2, _ = px.argmax_dev(t)
+        torch.cuda.synchronize()
+        assert [int(i) for i in idx2] == [oracle.argmax(v[r]) for r in range(5)]

@@ -1,0 +1,111 @@
+"""On-device quantise + pack, bit-exact with the reference quantizer (src/weights.rs:94-151) as
+restated by the oracle.  Packed bytes and f32 scale bit patterns must be identical."""
+import numpy as np
+import pytest
+
+import oracle
+import pyxis_b200 as px
+from kat_check import run_kat
+from parity import load_kats
+
+pytestmark = pytest.mark.gpu
+
+
+class CudaImpl:
+    def quantize(self, qt, src, bs):
+        w = px.Weights.quantize_int8(src, bs) if qt == "int8" else px.Weights.quantize_int4(src, bs)
+        return w.download()
+
+    def quantized_matmul(self, qt, wv, bs, x, N, K):
+        w = px.Weights.quantize_int8(wv, bs) if qt == "int8" else px.Weights.quantize_int4(wv, bs)
+        return px.matmul(x, w, N, K)
+
+    def q8_0(self, blob, n):
+        data, scales = oracle.q8_0_to_int8(blob, n)  # the GGUF parser stays on the host
+        w = px.Weights.from_packed("int8", data, scales, 32, n)
+        return w.download()
+
+    def argmax(self, v):
+        return px.argmax(v)
+
+
+@pytest.mark.parametrize("kat", load_kats(), ids=lambda k: k["name"])
+def test_cuda_reference_kat(kat):
+    if not run_kat(kat, CudaImpl()):
+        pytest.skip("op not on the CUDA path (f32 weights / decode-loop op)")
+
+
+def _bits(a):
+    return np.asarray(a).view(np.uint32)
+
+
+def _oracle_pack(qt, vals, bs):
+    return oracle.quantize_int8(vals, bs) if qt == "int8" else oracle.quantize_int4(vals, bs)
+
+
+@pytest.mark.parametrize("qt", ["int8", "int4"])
+@pytest.mark.parametrize("n,bs", [(1, 1), (2, 32), (3, 2), (5, 4), (31, 32), (33, 32), (1001, 7), (4096, 64),
+                                  (2048 * 64, 2048), (6144 * 8, 6144), (100_003, 100_003), (300_000, 70_000),
+                                  (65 * 1024, 65 * 1024 + 3)])
+def test_quantize_bit_exact_f32(qt, n, bs):
+    rng = np.random.default_rng(n + bs)
+    v = (rng.standard_normal(n) * 0.02).astype(np.float32)
+    v[rng.integers(0, n, size=max(1, n // 97))] = 0.0
+    w = px.Weights.quantize_int8(v, bs) if qt == "int8" else px.Weights.quantize_int4(v, bs)
+    d, s = w.download()
+    od, os_ = _oracle_pack(qt, v, bs)
+    assert np.array_equal(d.view(np.uint8), od.view(np.uint8))
+    assert np.array_equal(_bits(s), _bits(os_))
+    assert w.len() == n and w.num_scales == -(-n // bs)
+
+
+@pytest.mark.parametrize("qt,bs", [("int8", 2048), ("int4", 32), ("int8", 32)])
+def test_quantize_bit_exact_bf16_config_shape(qt, bs):
+    """gate_proj 6144 x 2048: bf16 N(0, 0.02) weights, widened with << 16 then quantised."""
+    bits = px.synth_normal_bf16(0x6A7E, 6144 * 2048, 0.02)
+    w = px.Weights.quantize_int8(bits, bs) if qt == "int8" else px.Weights.quantize_int4(bits, bs)
+    d, s = w.download()
+    od, os_ = _oracle_pack(qt, oracle.bf16_to_f32(bits), bs)
+    assert np.array_equal(d.view(np.uint8), od.view(np.uint8))
+    assert np.array_equal(_bits(s), _bits(os_))
+
+
+def test_quantize_from_device_tensor():
+    import torch
+    bits = px.synth_normal_bf16(11, 1024 * 512, 0.02)
+    t = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).cuda()
+    w = px.Weights.quantize_int4(t, 32)
+    d, s = w.download()
+    od, os_ = oracle.quantize_int4(oracle.bf16_to_f32(bits), 32)
+    assert np.array_equal(d, od) and np.array_equal(_bits(s), _bits(os_))
+    tf = torch.from_numpy(oracle.bf16_to_f32(bits)).cuda()
+    w2 = px.Weights.quantize_int8(tf, 512)
+    d2, s2 = w2.download()
+    od2, os2 = oracle.quantize_int8(oracle.bf16_to_f32(bits), 512)
+    assert np.array_equal(d2, od2) and np.array_equal(_bits(s2), _bits(os2))
+
+
+@pytest.mark.parametrize("qt", ["int8", "int4"])
+def test_quantize_special_values(qt):
+    v = np.array([np.nan, 1.0, -np.inf, 0.5, -0.0, 3e-39, np.inf, np.nan, 0.0, 1e38, -1e38, 2.5, -2.5, 7.0],
+                 np.float32)
+    for bs in (1, 2, 3, 5, 14, 100):
+        w = px.Weights.quantize_int8(v, bs) if qt == "int8" else px.Weights.quantize_int4(v, bs)
+        d, s = w.download()
+        od, os_ = _oracle_pack(qt, v, bs)
+        assert np.array_equal(d.view(np.uint8), od.view(np.uint8)), (bs, d, od)
+        assert np.array_equal(_bits(s), _bits(os_)), (bs, s, os_)
+
+
+def test_quantize_rejects_zero_block():
+    with pytest.raises(px.PyxisError):
+        px.Weights.quantize_int8(np.ones(4, np.float32), 0)
+
+
+def test_upload_download_round_trip():
+    rng = np.random.default_rng(3)
+    data = rng.integers(0, 256, size=999, dtype=np.uint8)
+    scales = rng.standard_normal(63).astype(np.float32)
+    w = px.Weights.from_packed("int4", data, scales, 32, 1998)
+    d, s = w.download()
+    assert np.array_equal(d, data) and np.array_equal(s, scales)
