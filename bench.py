@@ -355,8 +355,32 @@ def pyxis_arm(args, ws, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def profile_case(args):
+    """A single GEMV shape, launched warmup + steps times: the target of the committed ncu
+    captures (profiles/*.txt name the exact command)."""
+    import numpy as np
+    import torch
+
+    import pyxis_b200 as px
+
+    name, B = args.profile_case.split(":") if ":" in args.profile_case else (args.profile_case, "1")
+    B = int(B)
+    (_, qt, N, K, bs) = next(m for m in SWEEP if m[0] == name)
+    bits = px.synth_normal_bf16(SEED, N * K, 0.02)
+    t = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).cuda()
+    w = px.Weights.quantize_int8(t, bs) if qt == "int8" else px.Weights.quantize_int4(t, bs)
+    X = torch.from_numpy(px.synth_normal_f32(SEED + 100 + B, B * K, 1.0)).cuda().view(B, K)
+    Y = torch.empty((B, N), dtype=torch.float32, device="cuda")
+    for _ in range(args.warmup + args.steps):
+        px.matmul_dev(X, w, N, K, Y=Y)
+    torch.cuda.synchronize()
+    print(f"profile case {name} B={B}: {qt} {N}x{K} block {bs}, {args.warmup + args.steps} launches")
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--profile-case", default=None,
+                    help="run one GEMV shape only, e.g. lm_head:1 or gate_proj:8 (for ncu)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
@@ -377,6 +401,9 @@ def main():
     from oracle import build as ob
 
     ob.build()
+    if args.profile_case:
+        profile_case(args)
+        return
     ws, rank, local = dist_setup()
     try:
         pyxis_arm(args, ws, rank, local)
