@@ -23,8 +23,8 @@
  *    over the flattened row-major [out_features, in_features] index.
  *  - A context is bound to one device and owns one CUDA stream.  Calls on one context must not
  *    overlap from several host threads; use one context per thread or per device.
- *  - `_dev` entry points take device pointers and a cudaStream_t (NULL = the context's stream)
- *    and do not synchronize.  The host-pointer entry points copy in, compute and copy out, and
+ *  - `_dev` entry points take device pointers and a cudaStream_t (NULL = the context's stream;
+ *    pass cudaStreamLegacy for the legacy default stream) and do not synchronize.  The host-pointer entry points copy in, compute and copy out, and
  *    return after the result is in host memory (src/metal_matmul.rs:311-354 behaves the same).
  */
 #ifndef PYXIS_CUDA_H
@@ -125,6 +125,11 @@ int pyxis_cuda_matmul_dev(pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, cons
 
 /* Workspace bytes pyxis_cuda_matmul_dev needs for M rows of in_features (0 for the GEMV). */
 size_t pyxis_cuda_matmul_workspace_size(size_t M, size_t in_features);
+
+/* Synchronizes the context's device and reports whether a kernel's bounded device-side wait ran
+ * out since the last check (PYXIS_ETIMEOUT; the outputs of that launch are invalid), clearing the
+ * flag.  Kernels never spin without a limit: a stuck pipeline ends the launch instead. */
+int pyxis_cuda_check_device_error(pyxis_cuda_ctx *ctx);
 
 /* Row-wise argmax (src/output_head.rs:30-44: first index of the maximum under strict >) of
  * M rows of n f32 on the device: idx[M] int32 and val[M] f32 (val may be NULL).  `index_base`

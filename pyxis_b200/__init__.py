@@ -224,6 +224,19 @@ def matmul_batch(inputs, weight: Weights, out_features: int, in_features: int) -
     return Y
 
 
+CUDA_STREAM_LEGACY = 0x1  # cudaStreamLegacy: the legacy default stream, as an explicit handle
+
+
+def _stream_handle(stream, device) -> int:
+    """cudaStream_t for a torch stream.  torch reports its default stream as 0, which the C ABI
+    reads as "the context's own stream"; pass the legacy default stream's explicit handle
+    instead so work lands on the stream the caller's events and tensors use."""
+    import torch
+
+    h = (stream or torch.cuda.current_stream(device)).cuda_stream
+    return h if h else CUDA_STREAM_LEGACY
+
+
 def matmul_dev(X, weight: Weights, out_features: int, in_features: int, Y=None, stream=None, workspace=None):
     """Device-pointer form over torch CUDA tensors: X [M, in] f32 -> Y [M, out] f32, launched
     asynchronously on ``stream`` (a torch.cuda.Stream; default: torch's current stream)."""
@@ -234,7 +247,7 @@ def matmul_dev(X, weight: Weights, out_features: int, in_features: int, Y=None, 
     M = X.shape[0]
     if Y is None:
         Y = torch.empty((M, out_features), dtype=torch.float32, device=X.device)
-    st = (stream or torch.cuda.current_stream(X.device)).cuda_stream
+    st = _stream_handle(stream, X.device)
     ws_ptr, ws_bytes = (workspace.data_ptr(), workspace.numel() * workspace.element_size()) if workspace is not None else (None, 0)
     check(_native.lib().pyxis_cuda_matmul_dev(weight.ctx.handle, weight.handle, C.c_void_p(X.data_ptr()), M,
                                               X.stride(0), out_features, in_features, C.c_void_p(Y.data_ptr()),
@@ -254,7 +267,7 @@ def argmax_dev(values, index_base: int = 0, idx=None, val=None, stream=None, dev
         idx = torch.empty(M, dtype=torch.int32, device=values.device)
     if val is None:
         val = torch.empty(M, dtype=torch.float32, device=values.device)
-    st = (stream or torch.cuda.current_stream(values.device)).cuda_stream
+    st = _stream_handle(stream, values.device)
     check(_native.lib().pyxis_cuda_argmax_dev(ctx.handle, C.c_void_p(values.data_ptr()), M, n, values.stride(0),
                                               index_base, C.c_void_p(idx.data_ptr()), C.c_void_p(val.data_ptr()),
                                               C.c_void_p(st)))

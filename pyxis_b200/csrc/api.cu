@@ -27,6 +27,8 @@ struct pyxis_cuda_ctx {
     // argmax scratch (allocated and zeroed at init)
     ArgmaxScratch amax{};
     void *amax_mem = nullptr;
+    // device error flag written by kernels whose bounded waits ran out (0 = none)
+    int *d_err = nullptr;
 };
 
 struct pyxis_cuda_weights {
@@ -76,6 +78,8 @@ struct DeviceGuard {
 };
 
 size_t div_ceil(size_t a, size_t b) { return (a + b - 1) / b; }
+
+constexpr size_t kTcMinRows = 16;  // matmul_dev rows from which the tensor-core GEMM runs
 
 size_t packed_bytes(int qtype, size_t n) { return qtype == PYXIS_QTYPE_INT8 ? n : div_ceil(n, 2); }
 
@@ -179,6 +183,12 @@ int pyxis_cuda_init(int device, pyxis_cuda_ctx **out) {
         pyxis_cuda_destroy(ctx);
         return cuda_fail(e, "argmax scratch");
     }
+    e = cudaMalloc(&ctx->d_err, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(ctx->d_err, 0, sizeof(int));
+    if (e != cudaSuccess) {
+        pyxis_cuda_destroy(ctx);
+        return cuda_fail(e, "device error flag");
+    }
     ctx->amax.partial = (uint64_t *)ctx->amax_mem;
     ctx->amax.ticket = (unsigned *)((uint8_t *)ctx->amax_mem + (size_t)kArgmaxMaxRows * kArgmaxMaxCtasPerRow * sizeof(uint64_t));
     *out = ctx;
@@ -193,6 +203,7 @@ int pyxis_cuda_destroy(pyxis_cuda_ctx *ctx) {
     cudaFree(ctx->dy);
     cudaFree(ctx->ws);
     cudaFree(ctx->amax_mem);
+    cudaFree(ctx->d_err);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
     return PYXIS_OK;
@@ -300,9 +311,19 @@ int pyxis_cuda_weights_free(pyxis_cuda_weights *w) {
 }
 
 size_t pyxis_cuda_matmul_workspace_size(size_t M, size_t in_features) {
-    (void)M;
-    (void)in_features;
-    return 0;
+    return M >= kTcMinRows ? gemm_tc_workspace_bytes(M, in_features) : 0;
+}
+
+int pyxis_cuda_check_device_error(pyxis_cuda_ctx *ctx) {
+    if (!ctx) return fail(PYXIS_EINVAL, "null context");
+    DeviceGuard g(ctx->device);
+    PYXIS_CUDA_TRY(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    PYXIS_CUDA_TRY(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+    int code = 0;
+    PYXIS_CUDA_TRY(cudaMemcpy(&code, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost), "read device error flag");
+    if (code == 0) return PYXIS_OK;
+    PYXIS_CUDA_TRY(cudaMemset(ctx->d_err, 0, sizeof(int)), "clear device error flag");
+    return fail(PYXIS_ETIMEOUT, "a kernel's bounded wait ran out (code 0x%x); its outputs are invalid", code);
 }
 
 int pyxis_cuda_matmul_dev(pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, const float *X, size_t M,
@@ -318,9 +339,29 @@ int pyxis_cuda_matmul_dev(pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, cons
     DeviceGuard g(ctx->device);
     cudaStream_t st = pick_stream(ctx, stream);
     QMatrix q = qmatrix(w, out_features, in_features);
+    if (M >= kTcMinRows && gemm_tc_supported(q) && (reinterpret_cast<uintptr_t>(X) & 15) == 0 && ldx % 4 == 0) {
+        const size_t need = gemm_tc_workspace_bytes(M, in_features);
+        if (!workspace) {
+            if (ctx->ws_cap < need) {
+                cudaFree(ctx->ws);
+                ctx->ws = nullptr;
+                ctx->ws_cap = 0;
+                PYXIS_CUDA_TRY(cudaMalloc(&ctx->ws, need), "cudaMalloc(workspace)");
+                ctx->ws_cap = need;
+            }
+            workspace = ctx->ws;
+        } else if (workspace_bytes < need) {
+            return fail(PYXIS_EINVAL, "workspace of %zu bytes < %zu needed", workspace_bytes, need);
+        } else if (reinterpret_cast<uintptr_t>(workspace) & 255) {
+            return fail(PYXIS_EINVAL, "workspace must be 256-byte aligned");
+        }
+        cudaError_t e = launch_gemm_tc(q, X, M, ldx, Y, ldy, workspace, ctx->d_err, st);
+        if (e != cudaSuccess) return cuda_fail(e, "tensor-core GEMM launch");
+        return PYXIS_OK;
+    }
     for (size_t m0 = 0; m0 < M; m0 += 8) {
         size_t b = M - m0 < 8 ? M - m0 : 8;
-        cudaError_t e = launch_gemv(q, X + m0 * ldx, b, ldx, Y + m0 * ldy, ldy, ctx->num_sms, st);
+        cudaError_t e = launch_gemv(q, X + m0 * ldx, b, ldx, Y + m0 * ldy, ldy, ctx->d_err, ctx->num_sms, st);
         if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
     }
     return PYXIS_OK;

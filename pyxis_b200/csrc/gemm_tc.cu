@@ -1,0 +1,453 @@
+// gemm_tc.cu -- prefill (many-token) quantized GEMM on the 5th-generation tensor cores.
+//
+// Y[m, n] = sum_k X[m, k] * q[n, k] * scale(n, k)   for M tokens x N weight rows, the batched form
+// of src/matmul.rs:21-97 (the reference's prefill issues one matmul per position,
+// src/attention.rs:74-79), computed as:
+//
+//   1. split_x: each token row is scaled by a power of two 2^e (max |x| -> [2^14, 2^15)) and split
+//      into fp16 hi + lo (x*2^e = hi + lo + O(2^-22 |x*2^e|)): 22 significant bits, as accurate
+//      against the reference's f32 sums as exact arithmetic (bf16 hi/lo keeps only 16).
+//   2. the tile kernel, one CTA per 128 weight rows x 128 tokens, warp-specialised:
+//        warp 0      TMA producer: raw int8/int4 codes + fp16 X hi/lo tiles into a 3-stage ring
+//        warp 1      TMEM owner and MMA issuer: tcgen05.mma kind::f16, M=128 N=128 K=16,
+//                    two MMAs (hi, lo) per K-step into an fp32 TMEM accumulator
+//        warps 2-5   converters: codes -> exact fp16 integers in the 128B-swizzled K-major layout
+//        warps 6-13  epilogue: tcgen05.ld the accumulator, apply scales, store Y
+//      Accumulation: each "period" of at most 64 K (4 K-steps, 8 MMAs) goes to one of two TMEM
+//      buffers; the epilogue folds it into fp32 registers (round-to-nearest) while the MMA warp
+//      fills the other buffer.  Long fp32 sums inside the tensor core drift (measured 1.9e-3 on
+//      the floor-relative metric for K = 2048 in one accumulator); 64-wide periods do not.
+//      Scales: one per row (block == K) is applied once at the end; a scale per group of G
+//      elements along K (int4 group 32, GGUF int8 block 32) multiplies each period of its group.
+//   Weight codes are exact in fp16 and the token power of two is exact, so the only rounding
+//   besides the fp32 accumulation is the lo term's 2^-22.
+//
+// Every mbarrier wait is bounded (globaltimer); a wait that runs out records an error code in
+// the context's device flag and the CTA winds down (drains its MMAs / copies, frees TMEM).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "kernels.h"
+#include "tc_ptx.cuh"
+
+namespace pyxis {
+namespace {
+
+constexpr int BM = 128;  // weight rows per tile: MMA M, TMEM lanes
+constexpr int BN = 128;  // tokens per tile: MMA N, TMEM columns per accumulator
+constexpr int BK = 64;   // K per stage: one 128-byte swizzle row of fp16
+constexpr int STAGES = 3;
+constexpr int kConvWarp0 = 2, kNumConvWarps = 4;
+constexpr int kEpiWarp0 = 6, kNumEpiWarps = 8;
+constexpr int kThreads = (kEpiWarp0 + kNumEpiWarps) * 32;  // 448
+constexpr uint32_t kTmemCols = 2 * BN;
+constexpr uint32_t kABytes = BM * BK * 2;
+constexpr uint32_t kBBytes = BN * BK * 2;
+constexpr uint32_t kRBytes = BM * 64;
+constexpr uint64_t kTimeoutNs = 4000000000ull;
+
+constexpr uint32_t kOffA = 0;
+constexpr uint32_t kOffBhi = kOffA + STAGES * kABytes;
+constexpr uint32_t kOffBlo = kOffBhi + STAGES * kBBytes;
+constexpr uint32_t kOffR = kOffBlo + STAGES * kBBytes;
+constexpr uint32_t kOffBar = kOffR + STAGES * kRBytes;
+constexpr uint32_t kNumBars = 3 * STAGES + 2 + 2 + 1;
+constexpr uint32_t kOffMisc = kOffBar + kNumBars * 8;
+constexpr uint32_t kSmemBytes = kOffMisc + 16 + 1024;  // + alignment slack
+
+// Device error codes (first one wins): which role's wait ran out.
+enum { kErrProducer = 0x101, kErrConverter = 0x102, kErrMma = 0x103, kErrEpilogue = 0x104, kErrDrain = 0x105 };
+
+struct TcParams {
+    int M, N, K;
+    int qtype;
+    int per_row;            // 1: one scale per row (block == K)
+    int ksteps_per_period;  // K-steps (16 each) accumulated in TMEM before the epilogue folds them
+    int periods_per_group;  // periods sharing one scale (per-group scales)
+    int groups_per_row;     // K / G (per-group scales)
+    const float *scales;
+    const float *xinv;    // [M] 2^-e per token
+    float *Y;
+    long long ldy;
+    int *err;
+};
+
+PYXIS_DEVINL uint32_t h2_bits(__half2 v) { return *reinterpret_cast<uint32_t *>(&v); }
+PYXIS_DEVINL __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
+
+// int8 codes (signed bytes) -> exact fp16 pairs: byte b -> fp16(1024 + (b ^ 0x80)) - 1152.
+PYXIS_DEVINL void i8x4_to_h(uint32_t w, uint32_t &h01, uint32_t &h23) {
+    const uint32_t u = w ^ 0x80808080u;
+    const __half2 bias = bits_h2(0x64806480u);  // (1152, 1152)
+    h01 = h2_bits(__hsub2(bits_h2(__byte_perm(u, 0x64646464u, 0x5140u)), bias));
+    h23 = h2_bits(__hsub2(bits_h2(__byte_perm(u, 0x64646464u, 0x5342u)), bias));
+}
+
+// int4 codes (q + 8 in nibbles, element 2j low / 2j+1 high nibble of byte j) -> exact fp16 pairs
+// in the order (e0,e4) (e1,e5) (e2,e6) (e3,e7); split_x applies the same order to X.
+PYXIS_DEVINL void u4x8_to_h(uint32_t w, uint32_t (&h)[4]) {
+    const __half2 bias = bits_h2(0x64086408u);  // (1032, 1032)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = h2_bits(__hsub2(bits_h2(((w >> (4 * i)) & 0x000F000Fu) | 0x64006400u), bias));
+}
+
+// Byte offset of 16-byte chunk c of row r in a 128B-swizzled K-major tile (8-row 1024 B atoms).
+PYXIS_DEVINL uint32_t sw128_off(int r, int c) { return (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4); }
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_xhi,
+                   const __grid_constant__ CUtensorMap tm_xlo, const TcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kOffBar);
+    uint64_t *full = bars, *conv = bars + STAGES, *empty = bars + 2 * STAGES;
+    uint64_t *accfull = bars + 3 * STAGES, *accempty = accfull + 2, *drain = accempty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffMisc);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + kOffMisc + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * BM, m0 = blockIdx.y * BN;
+    const int num_kb = p.K / BK;
+    const int raw_kb_bytes = p.qtype == kQInt8 ? 64 : 32;
+    const uint32_t stage_tx = 2 * kBBytes + (uint32_t)(BM * raw_kb_bytes);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&conv[s], kNumConvWarps);
+            tc::mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            tc::mbar_init(&accfull[b], 1);
+            tc::mbar_init(&accempty[b], kNumEpiWarps);
+        }
+        tc::mbar_init(drain, 1);
+        *abort_flag = 0;
+        tc::fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tc::prefetch_tmap(&tm_w);
+        tc::prefetch_tmap(&tm_xhi);
+        tc::prefetch_tmap(&tm_xlo);
+    }
+    if (warp == 1) tc::tmem_alloc(tmem_slot, kTmemCols);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            int issued = 0;
+            for (int kb = 0; kb < num_kb; ++kb) {
+                const int s = kb % STAGES;
+                if (kb >= STAGES &&
+                    !tc::mbar_wait_bounded(&empty[s], ((kb / STAGES) - 1) & 1, abort_flag, p.err, kErrProducer, kTimeoutNs))
+                    break;
+                tc::mbar_arrive_expect_tx(&full[s], stage_tx);
+                tc::tma_load_2d(smem + kOffR + s * kRBytes, &tm_w, kb * raw_kb_bytes, n0, &full[s]);
+                tc::tma_load_2d(smem + kOffBhi + s * kBBytes, &tm_xhi, kb * BK, m0, &full[s]);
+                tc::tma_load_2d(smem + kOffBlo + s * kBBytes, &tm_xlo, kb * BK, m0, &full[s]);
+                ++issued;
+            }
+            if (*abort_flag) {  // let the copies already issued land before the CTA exits
+                volatile int no_abort = 0;
+                for (int j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j)
+                    tc::mbar_wait_bounded(&full[j % STAGES], (j / STAGES) & 1, &no_abort, p.err, kErrDrain, 100000000ull);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = tc::idesc_f16_f32(BM, BN);
+            int period = 0, kin = 0, buf = 0;
+            bool ok = true;
+            for (int kb = 0; kb < num_kb && ok; ++kb) {
+                const int s = kb % STAGES;
+                const uint32_t par = (kb / STAGES) & 1;
+                ok = tc::mbar_wait_bounded(&conv[s], par, abort_flag, p.err, kErrMma, kTimeoutNs) &&
+                     tc::mbar_wait_bounded(&full[s], par, abort_flag, p.err, kErrMma, kTimeoutNs);
+                if (!ok) break;
+                tc::tc_fence_after();
+                const uint64_t a0 = tc::desc_sw128(tc::smem_u32(smem + kOffA + s * kABytes));
+                const uint64_t bh0 = tc::desc_sw128(tc::smem_u32(smem + kOffBhi + s * kBBytes));
+                const uint64_t bl0 = tc::desc_sw128(tc::smem_u32(smem + kOffBlo + s * kBBytes));
+#pragma unroll
+                for (int ks = 0; ks < BK / 16; ++ks) {
+                    if (kin == 0) {
+                        buf = period & 1;
+                        if (period >= 2) {
+                            if (!tc::mbar_wait_bounded(&accempty[buf], ((period >> 1) - 1) & 1, abort_flag, p.err,
+                                                       kErrMma, kTimeoutNs)) {
+                                ok = false;
+                                break;
+                            }
+                            tc::tc_fence_after();
+                        }
+                    }
+                    const uint32_t d = tmem_base + (uint32_t)(buf * BN);
+                    const uint64_t koff = (uint64_t)(ks * 32) >> 4;  // 16 fp16 = 32 B along the swizzled row
+                    tc::mma_f16(d, a0 + koff, bh0 + koff, idesc, kin > 0 ? 1u : 0u);
+                    tc::mma_f16(d, a0 + koff, bl0 + koff, idesc, 1u);
+                    if (++kin == p.ksteps_per_period) {
+                        tc::mma_commit(&accfull[buf]);
+                        ++period;
+                        kin = 0;
+                    }
+                }
+                tc::mma_commit(&empty[s]);
+            }
+            // wait for every MMA this thread issued before TMEM can be released
+            tc::mma_commit(drain);
+            volatile int no_abort = 0;
+            tc::mbar_wait_bounded(drain, 0, &no_abort, p.err, kErrDrain, kTimeoutNs);
+        }
+    } else if (warp < kEpiWarp0) {
+        // ------------------------------------------------------------------ converters
+        const int r = threadIdx.x - kConvWarp0 * 32;  // weight row within the tile
+        for (int kb = 0; kb < num_kb; ++kb) {
+            const int s = kb % STAGES;
+            int ok = 1;
+            if (lane == 0) ok = tc::mbar_wait_bounded(&full[s], (kb / STAGES) & 1, abort_flag, p.err, kErrConverter, kTimeoutNs);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            const uint8_t *raw = smem + kOffR + s * kRBytes;
+            uint8_t *a = smem + kOffA + s * kABytes;
+            if (p.qtype == kQInt8) {
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {  // 64-byte rows, 64-byte TMA swizzle
+                    const uint4 w = *reinterpret_cast<const uint4 *>(raw + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+                    uint4 o0, o1;
+                    i8x4_to_h(w.x, o0.x, o0.y);
+                    i8x4_to_h(w.y, o0.z, o0.w);
+                    i8x4_to_h(w.z, o1.x, o1.y);
+                    i8x4_to_h(w.w, o1.z, o1.w);
+                    *reinterpret_cast<uint4 *>(a + sw128_off(r, 2 * c)) = o0;
+                    *reinterpret_cast<uint4 *>(a + sw128_off(r, 2 * c + 1)) = o1;
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {  // 32-byte rows, 32-byte TMA swizzle
+                    const uint4 w = *reinterpret_cast<const uint4 *>(raw + r * 32 + ((c ^ ((r >> 2) & 1)) << 4));
+                    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        uint32_t h[4];
+                        u4x8_to_h(ws[j], h);
+                        *reinterpret_cast<uint4 *>(a + sw128_off(r, 4 * c + j)) = make_uint4(h[0], h[1], h[2], h[3]);
+                    }
+                }
+            }
+            tc::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&conv[s]);
+        }
+    } else {
+        // ------------------------------------------------------------------ epilogue
+        const int q = warp & 3;                 // TMEM lane quarter this warp may access
+        const int h = (warp - kEpiWarp0) >> 2;  // column half
+        const int n = n0 + 32 * q + lane;
+        const bool row_ok = n < p.N;
+        float acc[64];
+#pragma unroll
+        for (int j = 0; j < 64; ++j) acc[j] = 0.f;
+        const int num_periods = p.K / (16 * p.ksteps_per_period);
+        const int ppg = p.periods_per_group;
+        const int num_groups = p.per_row ? 0 : p.groups_per_row;
+        const float *srow = p.scales + (size_t)(row_ok ? n : 0) * p.groups_per_row;
+        float s_cur[4], s_nxt[4];  // scales of groups g0..g0+3 and g0+4..g0+7
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            s_cur[i] = (row_ok && i < num_groups) ? __ldg(srow + i) : 0.f;
+            s_nxt[i] = (row_ok && 4 + i < num_groups) ? __ldg(srow + 4 + i) : 0.f;
+        }
+        bool ok = true;
+        for (int pd = 0; pd < num_periods; ++pd) {
+            const int b = pd & 1;
+            const int g = pd / ppg;
+            int w_ok = 1;
+            if (lane == 0) w_ok = tc::mbar_wait_bounded(&accfull[b], (pd >> 1) & 1, abort_flag, p.err, kErrEpilogue, kTimeoutNs);
+            w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
+            if (!w_ok) {
+                ok = false;
+                break;
+            }
+            tc::tc_fence_after();
+            const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * BN + 64 * h);
+            const int i = g & 3;
+            const float sg = i == 0 ? s_cur[0] : i == 1 ? s_cur[1] : i == 2 ? s_cur[2] : s_cur[3];
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                float v[32];
+                tc::tmem_ld32(taddr + 32 * half, v);
+                if (p.per_row) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) acc[32 * half + j] += v[j];
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) acc[32 * half + j] = fmaf(sg, v[j], acc[32 * half + j]);
+                }
+            }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&accempty[b]);
+            if (!p.per_row && i == 3 && (pd + 1) % ppg == 0) {  // last period of group g0+3: rotate
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    s_cur[t] = s_nxt[t];
+                    const int gn = g + 5 + t;
+                    s_nxt[t] = (row_ok && gn < num_groups) ? __ldg(srow + gn) : 0.f;
+                }
+            }
+        }
+        if (ok && row_ok) {
+            const float sr = p.per_row ? __ldg(p.scales + n) : 1.0f;
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+                const int m = m0 + 64 * h + j;
+                if (m < p.M) p.Y[(size_t)m * p.ldy + n] = acc[j] * sr * __ldg(p.xinv + m);
+            }
+        }
+    }
+
+    __syncwarp();
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------------------- split_x
+// One CTA per token row: e = 15 - exponent(max|x|) so |x * 2^e| < 2^15; hi = fp16(x 2^e),
+// lo = fp16(x 2^e - hi); inv = 2^-e.  PERM writes each 8-element group in int4 converter order.
+template <bool PERM>
+__global__ void __launch_bounds__(256) split_x_kernel(const float *__restrict__ X, long long ldx, int K,
+                                                      __half *__restrict__ hi, __half *__restrict__ lo,
+                                                      float *__restrict__ inv) {
+    __shared__ float red[8];
+    const int m = blockIdx.x;
+    const float *x = X + (size_t)m * ldx;
+    float mx = 0.f;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(x[k]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w]);
+    int e = 0;
+    if (mx > 0.f && isfinite(mx)) {
+        int ex;
+        frexpf(mx, &ex);  // mx = f * 2^ex, f in [0.5, 1)
+        e = 15 - ex;
+        e = e > 120 ? 120 : (e < -120 ? -120 : e);
+    }
+    if (threadIdx.x == 0) inv[m] = ldexpf(1.0f, -e);
+    __half *hrow = hi + (size_t)m * K, *lrow = lo + (size_t)m * K;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        const float v = ldexpf(x[k], e);
+        const __half h = __float2half_rn(v);
+        const __half l = __float2half_rn(v - __half2float(h));
+        int d = k;
+        if (PERM) {
+            const int o = k & 7;  // element o of a group goes to position (o < 4 ? 2o : 2(o-4)+1)
+            d = (k & ~7) | (o < 4 ? 2 * o : 2 * (o - 4) + 1);
+        }
+        hrow[d] = h;
+        lrow[d] = l;
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return (PFN_cuTensorMapEncodeTiled_v12000) nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }();
+    return fn;
+}
+
+bool make_map_2d(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t outer,
+                 uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t es[2] = {1, 1};
+    return fn(m, dt, 2, const_cast<void *>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+}  // namespace
+
+bool gemm_tc_supported(const QMatrix &w) {
+    const size_t K = w.K, bs = w.block_size;
+    if (K == 0 || K % BK != 0 || K > (1u << 20) || w.N > (size_t)INT32_MAX) return false;
+    if ((reinterpret_cast<uintptr_t>(w.data) & 15) != 0) return false;
+    if (bs == K) return true;
+    return bs % 32 == 0 && K % bs == 0;
+}
+
+size_t gemm_tc_workspace_bytes(size_t M, size_t K) { return 2 * align256(M * K * 2) + align256(M * 4); }
+
+cudaError_t launch_gemm_tc(const QMatrix &w, const float *X, size_t M, size_t ldx, float *Y, size_t ldy, void *ws,
+                           int *err, cudaStream_t st) {
+    const int K = (int)w.K, N = (int)w.N;
+    uint8_t *wsb = reinterpret_cast<uint8_t *>(ws);
+    __half *xhi = reinterpret_cast<__half *>(wsb);
+    __half *xlo = reinterpret_cast<__half *>(wsb + align256(M * K * 2));
+    float *xinv = reinterpret_cast<float *>(wsb + 2 * align256(M * K * 2));
+    if (w.qtype == kQInt4)
+        split_x_kernel<true><<<(unsigned)M, 256, 0, st>>>(X, (long long)ldx, K, xhi, xlo, xinv);
+    else
+        split_x_kernel<false><<<(unsigned)M, 256, 0, st>>>(X, (long long)ldx, K, xhi, xlo, xinv);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+
+    CUtensorMap tw, th, tl;
+    const uint32_t raw_box = w.qtype == kQInt8 ? 64 : 32;
+    const uint64_t row_bytes = w.qtype == kQInt8 ? (uint64_t)K : (uint64_t)K / 2;
+    const bool ok = make_map_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.data, row_bytes, (uint64_t)N, row_bytes,
+                                raw_box, BM, w.qtype == kQInt8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B) &&
+                    make_map_2d(&th, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xhi, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2,
+                                BK, BN, CU_TENSOR_MAP_SWIZZLE_128B) &&
+                    make_map_2d(&tl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xlo, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2,
+                                BK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!ok) return cudaErrorInvalidValue;
+
+    TcParams p{};
+    p.M = (int)M;
+    p.N = N;
+    p.K = K;
+    p.qtype = w.qtype;
+    p.per_row = w.block_size == w.K ? 1 : 0;
+    // TMEM accumulation chains stay short (<= 64 along K); longer sums are folded in fp32
+    // registers with round-to-nearest, so the drift of long tensor-core accumulations never builds.
+    const int group_steps = p.per_row ? K / 16 : (int)(w.block_size / 16);
+    p.ksteps_per_period = group_steps < 4 ? group_steps : 4;
+    p.periods_per_group = group_steps / p.ksteps_per_period;
+    p.groups_per_row = p.per_row ? 1 : (int)(w.K / w.block_size);
+    p.scales = w.scales;
+    p.xinv = xinv;
+    p.Y = Y;
+    p.ldy = (long long)ldy;
+    p.err = err;
+    static const bool attr =
+        cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) == cudaSuccess;
+    if (!attr) return cudaErrorInvalidConfiguration;
+    dim3 grid((unsigned)((N + BM - 1) / BM), (unsigned)((M + BN - 1) / BN));
+    gemm_tc_kernel<<<grid, kThreads, kSmemBytes, st>>>(tw, th, tl, p);
+    return cudaGetLastError();
+}
+
+}  // namespace pyxis

@@ -359,7 +359,8 @@ cudaError_t dispatch_smem(size_t B, const GemvParams &p, int num_sms, cudaStream
 
 }  // namespace
 
-const char *gemv_kernel_name(const QMatrix &w, size_t B) {
+const char *gemv_kernel_name(const QMatrix &w, size_t B, int num_sms) {
+    if (B == 1 && gemv_ring_supported(w, num_sms)) return "gemv_ring_kernel";
     Plan pl = make_plan(w, B, 4);
     switch (pl.kind) {
     case Plan::kTeam: return "gemv_team_kernel";
@@ -369,8 +370,10 @@ const char *gemv_kernel_name(const QMatrix &w, size_t B) {
 }
 
 cudaError_t launch_gemv(const QMatrix &w, const float *X, size_t B, size_t ldx, float *Y,
-                        size_t ldy, int num_sms, cudaStream_t st) {
+                        size_t ldy, int *err, int num_sms, cudaStream_t st) {
     if (w.N == 0 || B == 0) return cudaSuccess;
+    if (B == 1 && (reinterpret_cast<uintptr_t>(X) & 15) == 0 && gemv_ring_supported(w, num_sms))
+        return launch_gemv_ring(w, X, Y, err, num_sms, st);
     if ((reinterpret_cast<uintptr_t>(X) & 15) != 0) ldx = 1;  // unaligned x: force generic
     Plan pl = make_plan(w, B, ldx);
     if ((reinterpret_cast<uintptr_t>(X) & 15) != 0) pl.kind = Plan::kGeneric;

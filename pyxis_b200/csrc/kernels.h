@@ -25,9 +25,20 @@ cudaError_t launch_quantize(const void *src, int src_kind, size_t n, size_t bs, 
 // Decode GEMV: Y[b, :] = W X[b, :] for b < B (B = 1..8).  Picks the register-resident-x team
 // kernel, the shared-memory-x kernel or the generic kernel by shape (gemv.cu).
 cudaError_t launch_gemv(const QMatrix &w, const float *X, size_t B, size_t ldx, float *Y,
-                        size_t ldy, int num_sms, cudaStream_t st);
+                        size_t ldy, int *err, int num_sms, cudaStream_t st);
+
+// Batch-1 GEMV streaming row tiles through a shared-memory ring (gemv_ring.cu).
+bool gemv_ring_supported(const QMatrix &w, int num_sms);
+cudaError_t launch_gemv_ring(const QMatrix &w, const float *x, float *y, int *err, int num_sms, cudaStream_t st);
 
 // Name of the kernel launch_gemv would pick (for tests and the bench's launch accounting).
-const char *gemv_kernel_name(const QMatrix &w, size_t B);
+const char *gemv_kernel_name(const QMatrix &w, size_t B, int num_sms);
+
+// Tensor-core prefill GEMM (gemm_tc.cu).  Supported when K % 64 == 0 and the scales are one per
+// row (block == K) or per group of a multiple of 32 that divides K.
+bool gemm_tc_supported(const QMatrix &w);
+size_t gemm_tc_workspace_bytes(size_t M, size_t K);
+cudaError_t launch_gemm_tc(const QMatrix &w, const float *X, size_t M, size_t ldx, float *Y, size_t ldy, void *ws,
+                           int *err, cudaStream_t st);
 
 }  // namespace pyxis

@@ -6,7 +6,7 @@ import pytest
 
 import oracle
 import pyxis_b200 as px
-from parity import MATMUL_TOL, normwise_err, rel_err
+from parity import check_matmul, exact_matmul
 
 pytestmark = pytest.mark.gpu
 
@@ -46,8 +46,7 @@ def test_gemv_matches_oracle(qt, N, K, bs, B):
     ref = ref_matmul(qt, od, os_, bs, X, N, K)
     Y = px.matmul_batch(X, w, N, K)
     assert Y.shape == (B, N)
-    e = rel_err(Y, ref)
-    assert e <= MATMUL_TOL, (e, normwise_err(Y, ref))
+    check_matmul(Y, ref, exact_matmul(qt, od, os_, bs, N, K, X))
 
 
 def test_lm_head_int8_full_size():
@@ -57,7 +56,7 @@ def test_lm_head_int8_full_size():
     x = px.synth_normal_f32(5, K, 1.0)
     ref = ref_matmul("int8", od, os_, K, x, N, K)
     y = px.matmul(x, w, N, K)
-    assert rel_err(y, ref) <= MATMUL_TOL
+    check_matmul(y, ref, exact_matmul("int8", od, os_, K, N, K, x)[0])
     assert px.argmax(y) == oracle.argmax(ref)
 
 
@@ -73,7 +72,7 @@ def test_gemv_odd_shapes(qt, N, K, bs, B):
     X = px.synth_normal_f32(77 + B, B * K, 1.0).reshape(B, K)
     ref = ref_matmul(qt, od, os_, bs, X, N, K)
     Y = px.matmul_batch(X, w, N, K)
-    assert rel_err(Y, ref) <= MATMUL_TOL
+    check_matmul(Y, ref, exact_matmul(qt, od, os_, bs, N, K, X))
 
 
 def test_matmul_rejects_shape_mismatch():
@@ -92,8 +91,9 @@ def test_matmul_dev_strided_rows():
     Y = torch.zeros((4, N + 32), device="cuda")[:, :N]
     px.matmul_dev(X, w, N, K, Y=Y)
     torch.cuda.synchronize()
-    ref = ref_matmul("int4", od, os_, 32, X.cpu().numpy(), N, K)
-    assert rel_err(Y.cpu().numpy(), ref) <= MATMUL_TOL
+    Xh = X.cpu().numpy()
+    ref = ref_matmul("int4", od, os_, 32, Xh, N, K)
+    check_matmul(Y.cpu().numpy(), ref, exact_matmul("int4", od, os_, 32, N, K, Xh))
 
 
 def test_argmax_rules():

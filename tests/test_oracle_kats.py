@@ -147,3 +147,17 @@ def test_oracle_argmax_first_max_and_nan_rules():
     assert oracle.argmax([1.0, np.nan, 2.0]) == 2
     assert oracle.argmax([-0.0, 0.0]) == 0
     assert oracle.argmax([-np.inf, -np.inf]) == 0
+
+
+def test_exact_matmul_helper_agrees_with_oracle():
+    """tests/parity.py's float64 reference sum stays within f32 rounding of the oracle."""
+    from parity import exact_matmul, rel_err
+    rng = np.random.default_rng(11)
+    N, K = 37, 96
+    w = (rng.standard_normal(N * K) * 0.02).astype(np.float32)
+    x = rng.standard_normal((3, K)).astype(np.float32)
+    for qt, q, kind in (("int8", oracle.quantize_int8, oracle.INT8), ("int4", oracle.quantize_int4, oracle.INT4)):
+        for bs in (K, 32, 7):
+            d, s = q(w, bs)
+            ref = oracle.matmul(x, kind, d, s, bs, N, K)
+            assert rel_err(exact_matmul(qt, d, s, bs, N, K, x), ref) < 1e-4
