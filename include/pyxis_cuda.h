@@ -137,6 +137,24 @@ int pyxis_cuda_check_device_error(pyxis_cuda_ctx *ctx);
 int pyxis_cuda_argmax_dev(pyxis_cuda_ctx *ctx, const float *values, size_t M, size_t n,
                           size_t ld, int64_t index_base, int32_t *idx, float *val, void *stream);
 
+/* Row-wise argmax that allocates nothing: the same result as pyxis_cuda_argmax_dev, for callers
+ * that cannot call cudaMalloc -- code running under an allocator it does not own (a framework's
+ * caching allocator, a memory-capped or pre-reserved pool), or code that may not grow its device
+ * footprint after start-up.  It has no counterpart in the reference and needs no context.
+ *  - Runs on the calling thread's current device, on `stream` (NULL: that device's default
+ *    stream); values, idx and val are device pointers, as in pyxis_cuda_argmax_dev.
+ *  - Its scratch is a fixed 33 KiB array inside the library's device image (every device that
+ *    uses it holds it until the process exits).  The first call on a device looks up that
+ *    array's device address (cudaGetSymbolAddress); make the first call on each device before
+ *    any stream capture.
+ *  - At most 64 rows per call (PYXIS_EINVAL beyond, rows of up to 2^32 - 1 values).
+ *  - Every call shares the one array: calls that can overlap on the GPU (different streams
+ *    without ordering, several host threads) race and must not be issued that way.
+ *  - Allocates no memory: no cudaMalloc/cudaFree or allocating library calls; it clears its
+ *    row counters with cudaMemsetAsync on `stream` before each launch. */
+int pyxis_cuda_argmax_noalloc(const float *values, size_t M, size_t n, size_t ld, int64_t index_base,
+                              int32_t *idx, float *val, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

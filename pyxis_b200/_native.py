@@ -48,6 +48,7 @@ SIGNATURES = {
     "pyxis_cuda_matmul_workspace_size": (_sz, [_sz, _sz]),
     "pyxis_cuda_check_device_error": (C.c_int, [_vp]),
     "pyxis_cuda_argmax_dev": (C.c_int, [_vp, _vp, _sz, _sz, _sz, C.c_int64, _vp, _vp, _vp]),
+    "pyxis_cuda_argmax_noalloc": (C.c_int, [_vp, _sz, _sz, _sz, C.c_int64, _vp, _vp, _vp]),
     "pyxis_synth_normal_f32": (None, [C.c_uint64, _sz, C.c_float, _vp]),
     "pyxis_synth_normal_bf16": (None, [C.c_uint64, _sz, C.c_float, _vp]),
     "pyxis_synth_tokens": (None, [C.c_uint64, _sz, C.c_uint32, _vp]),

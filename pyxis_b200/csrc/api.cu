@@ -144,6 +144,8 @@ int check_matmul(const pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, size_t 
 
 }  // namespace
 
+int pyxis::record_error(int code, const char *msg) { return fail(code, "%s", msg); }
+
 extern "C" {
 
 const char *pyxis_cuda_last_error(void) { return g_last_error.c_str(); }

@@ -41,4 +41,7 @@ size_t gemm_tc_workspace_bytes(size_t M, size_t K);
 cudaError_t launch_gemm_tc(const QMatrix &w, const float *X, size_t M, size_t ldx, float *Y, size_t ldy, void *ws,
                            int *err, cudaStream_t st);
 
+// Records `msg` as the calling thread's pyxis_cuda_last_error() and returns `code` (api.cu).
+int record_error(int code, const char *msg);
+
 }  // namespace pyxis
