@@ -344,9 +344,9 @@ def pyxis_arm(args, ws, rank, local):
                 "warmup": max(args.warmup, 3), "ms_per_step": ms_max / args.steps, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
                 "config": config_dict(ws),
-                "roofline": {"bound": "hbm", "kernel": "gemv_ring_kernel (lm_head int8 151936x2048, batch 1)",
+                "roofline": {"bound": "hbm", "kernel": "gemv_tc_i8_kernel (lm_head int8 151936x2048, batch 1)",
                              "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                             "frac": achieved / peak, "traffic": profiled_traffic("gemv_ring_lm_head_int8"),
+                             "frac": achieved / peak, "traffic": profiled_traffic("gemv_tc_i8_lm_head"),
                              "algorithmic_bytes_per_launch": lm_bytes, "avg_launch_us": lm_ms * 1e3},
                 "frac_of_peak_step": value / ws / peak,
                 "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},

@@ -29,6 +29,9 @@ struct pyxis_cuda_ctx {
     void *amax_mem = nullptr;
     // device error flag written by kernels whose bounded waits ran out (0 = none)
     int *d_err = nullptr;
+    // split-K scratch of the tensor-core GEMV (zeroed at init; the kernel leaves it zeroed)
+    void *tcg_scratch = nullptr;
+    size_t tcg_scratch_bytes = 0;
 };
 
 struct pyxis_cuda_weights {
@@ -79,7 +82,8 @@ struct DeviceGuard {
 
 size_t div_ceil(size_t a, size_t b) { return (a + b - 1) / b; }
 
-constexpr size_t kTcMinRows = 16;  // matmul_dev rows from which the tensor-core GEMM runs
+constexpr size_t kTcMinRows = 16;        // matmul_dev rows from which the tensor-core GEMM runs
+constexpr size_t kTcgScratchRows = 32768; // split-K runs only below 148 x 128 rows; covered
 
 size_t packed_bytes(int qtype, size_t n) { return qtype == PYXIS_QTYPE_INT8 ? n : div_ceil(n, 2); }
 
@@ -187,6 +191,9 @@ int pyxis_cuda_init(int device, pyxis_cuda_ctx **out) {
     }
     e = cudaMalloc(&ctx->d_err, sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(ctx->d_err, 0, sizeof(int));
+    ctx->tcg_scratch_bytes = gemv_tc_scratch_bytes(kTcgScratchRows);
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->tcg_scratch, ctx->tcg_scratch_bytes);
+    if (e == cudaSuccess) e = cudaMemset(ctx->tcg_scratch, 0, ctx->tcg_scratch_bytes);
     if (e != cudaSuccess) {
         pyxis_cuda_destroy(ctx);
         return cuda_fail(e, "device error flag");
@@ -206,6 +213,7 @@ int pyxis_cuda_destroy(pyxis_cuda_ctx *ctx) {
     cudaFree(ctx->ws);
     cudaFree(ctx->amax_mem);
     cudaFree(ctx->d_err);
+    cudaFree(ctx->tcg_scratch);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
     return PYXIS_OK;
@@ -363,7 +371,14 @@ int pyxis_cuda_matmul_dev(pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, cons
     }
     for (size_t m0 = 0; m0 < M; m0 += 8) {
         size_t b = M - m0 < 8 ? M - m0 : 8;
-        cudaError_t e = launch_gemv(q, X + m0 * ldx, b, ldx, Y + m0 * ldy, ldy, ctx->d_err, ctx->num_sms, st);
+        const float *xb = X + m0 * ldx;
+        cudaError_t e;
+        if (gemv_tc_supported(q, b, ctx->num_sms) && (reinterpret_cast<uintptr_t>(xb) & 15) == 0 &&
+            (b == 1 || ldx % 4 == 0))
+            e = launch_gemv_tc(q, xb, b, ldx, Y + m0 * ldy, ldy, ctx->tcg_scratch, ctx->tcg_scratch_bytes, ctx->d_err,
+                               ctx->num_sms, st);
+        else
+            e = launch_gemv(q, xb, b, ldx, Y + m0 * ldy, ldy, ctx->d_err, ctx->num_sms, st);
         if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
     }
     return PYXIS_OK;

@@ -41,6 +41,14 @@ size_t gemm_tc_workspace_bytes(size_t M, size_t K);
 cudaError_t launch_gemm_tc(const QMatrix &w, const float *X, size_t M, size_t ldx, float *Y, size_t ldy, void *ws,
                            int *err, cudaStream_t st);
 
+// int8 per-row GEMV for 1-8 input rows on tcgen05 kind::i8 (gemv_tc.cu).  `scratch` holds the
+// split-K partial sums for matrices of fewer than ~148 x 128 rows; it must be zero before the
+// first launch and the kernel leaves it zero.
+bool gemv_tc_supported(const QMatrix &w, size_t B, int num_sms);
+size_t gemv_tc_scratch_bytes(size_t N);
+cudaError_t launch_gemv_tc(const QMatrix &w, const float *X, size_t B, size_t ldx, float *Y, size_t ldy,
+                           void *scratch, size_t scratch_bytes, int *err, int num_sms, cudaStream_t st);
+
 // Records `msg` as the calling thread's pyxis_cuda_last_error() and returns `code` (api.cu).
 int record_error(int code, const char *msg);
 

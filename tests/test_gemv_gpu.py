@@ -116,3 +116,20 @@ def test_argmax_rules():
         idx2, _ = px.argmax_dev(t)
         torch.cuda.synchronize()
         assert [int(i) for i in idx2] == [oracle.argmax(v[r]) for r in range(5)]
+
+
+@pytest.mark.parametrize("N,K,B", [
+    (1, 2048, 1), (300, 128, 1), (2048, 2048, 1), (1024, 2048, 3), (6144, 2048, 5), (18000, 2048, 8),
+    (4096, 4096, 4), (129, 1024, 8), (151936, 2048, 8),
+])
+def test_int8_row_scale_tensor_core_gemv(N, K, B):
+    """int8 with one scale per row at batch 1-8 runs tcgen05 kind::i8 with x as int8 digits
+    (split-K with exact int32 atomics when there are fewer tiles than SMs)."""
+    w, od, os_ = make("int8", N, K, K, seed=N + K + B)
+    X = px.synth_normal_f32(B * 31 + 7, B * K, 1.0).reshape(B, K)
+    X[0, :5] = [0.0, -0.0, 1e-30, -3e4, 2.5]
+    for rep in range(2):  # the split-K scratch must be left clean for the next launch
+        Y = px.matmul_batch(X, w, N, K)
+        ref = ref_matmul("int8", od, os_, K, X, N, K)
+        check_matmul(Y, ref, exact_matmul("int8", od, os_, K, N, K, X))
+    px._native.check(px._native.lib().pyxis_cuda_check_device_error(w.ctx.handle))
