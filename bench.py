@@ -229,6 +229,54 @@ def reference_arm(args, ws, rank):
     print(json.dumps(line), flush=True)
 
 
+DECODE_WORKLOAD = ("Qwen3-1.7B-shape decode, random init, int8 one scale per row: hidden 2048, 28 layers, "
+                   "16/8 heads x 128, FFN 6144, vocab 151936, tied lm_head; 16 prompt ids + 128 greedy tokens, batch 1")
+DECODE_PROMPT, DECODE_NEW = 16, 128
+
+
+def decode_bytes_per_token(cfg, pos):
+    """HBM bytes one decode step reads at cache position `pos`: int8 codes + row scales of every
+    projection and the lm_head, the KV cache rows 0..pos, the embedding row."""
+    per_layer = (cfg.q_dim + 2 * cfg.kv_dim) * cfg.hidden + cfg.hidden * cfg.q_dim + 2 * cfg.ffn * cfg.hidden \
+        + cfg.hidden * cfg.ffn
+    rows = cfg.q_dim + 2 * cfg.kv_dim + cfg.hidden + 2 * cfg.ffn + cfg.hidden
+    w = cfg.n_layers * (per_layer + 4 * rows) + cfg.vocab * cfg.hidden + 4 * cfg.vocab
+    kv = cfg.n_layers * 2 * (pos + 1) * cfg.kv_dim * 4
+    return w + kv + 2 * cfg.hidden
+
+
+def run_decode(local, cpu_sample_tokens=0):
+    import time as _t
+
+    from pyxis_b200 import synth_tokens
+    from pyxis_b200.model import QWEN3_1_7B, Decoder, SyntheticModel
+
+    cfg = QWEN3_1_7B
+    m = SyntheticModel(cfg, SEED)
+    prompt = synth_tokens(0x9E0, DECODE_PROMPT, cfg.vocab)
+    t0 = _t.time()
+    dec = Decoder(m, qtype="int8", max_seq=DECODE_PROMPT + DECODE_NEW, device=local)
+    setup_s = _t.time() - t0
+    dec.generate(prompt, 8)  # warm-up: graph capture + first replays
+    toks, (p_ms, d_ms) = dec.generate(prompt, DECODE_NEW)
+    dec.close()
+    steps = DECODE_NEW - 1
+    tps = steps / (d_ms / 1e3)
+    avg_bytes = sum(decode_bytes_per_token(cfg, DECODE_PROMPT + i) for i in range(steps)) / steps
+    out = {"workload": DECODE_WORKLOAD, "tokens_per_s": tps, "ms_per_token": d_ms / steps, "prompt_ms": p_ms,
+           "bytes_per_token": avg_bytes, "achieved_gbs": avg_bytes * tps / 1e9, "model_setup_s": setup_s,
+           "first_tokens": [int(t) for t in toks[:8]]}
+    if cpu_sample_tokens:
+        import oracle
+        t0 = _t.time()
+        oracle.greedy_decode(cfg, m.bf16, "int8", prompt[:1], cpu_sample_tokens + 1)
+        cpu_s = _t.time() - t0
+        out["cpu_baseline"] = {"tokens_per_s": cpu_sample_tokens / cpu_s, "cores": oracle.num_cpus(), "kind": "port",
+                               "sample": f"1 prompt id + {cpu_sample_tokens} greedy tokens through the C port of "
+                                         "Model::generate (quantisation excluded), all host threads"}
+    return out
+
+
 def pyxis_arm(args, ws, rank, local):
     import numpy as np
     import torch
@@ -329,6 +377,18 @@ def pyxis_arm(args, ws, rank, local):
     e2e_s = max_over_ranks(time.perf_counter() - t0, ws)
     e2e_value = ws * sb * args.steps / e2e_s / 1e9
 
+    decode = None
+    if not args.no_decode:
+        del weights, X, Y
+        torch.cuda.empty_cache()
+        decode = run_decode(local, cpu_sample_tokens=0)
+        dsum = max_over_ranks(-decode["tokens_per_s"], ws)  # the slowest rank bounds the job
+        decode["tokens_per_s_min_rank"] = -dsum
+        decode["job_tokens_per_s"] = ws * (-dsum)
+        peak_d, _ = measured_peak_hbm()
+        decode["roofline_tokens_per_s"] = peak_d * 1e9 / decode["bytes_per_token"]
+        decode["frac_of_peak"] = decode["achieved_gbs"] / peak_d
+
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         import oracle
@@ -351,6 +411,7 @@ def pyxis_arm(args, ws, rank, local):
                 "frac_of_peak_step": value / ws / peak,
                 "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
                 "cpu_baseline": cpu, "clocks": clk, "gpu_launches": launches_per_step * args.steps,
+                "decode": decode,
                 "per_gpu_value": value / ws}
         print(json.dumps(line), flush=True)
 
@@ -363,6 +424,15 @@ def profile_case(args):
 
     import pyxis_b200 as px
 
+    if args.profile_case.startswith("decode"):
+        from pyxis_b200 import synth_tokens
+        from pyxis_b200.model import QWEN3_1_7B, Decoder, SyntheticModel
+        dec = Decoder(SyntheticModel(QWEN3_1_7B, SEED), qtype="int8", max_seq=64)
+        prompt = synth_tokens(0x9E0, 2, QWEN3_1_7B.vocab)
+        dec.generate(prompt, 2)
+        toks, t = dec.generate(prompt, 3)
+        print(f"profile case decode: tokens {list(toks)}, prompt {t[0]:.2f} ms, decode {t[1]:.2f} ms")
+        return
     name, B = args.profile_case.split(":") if ":" in args.profile_case else (args.profile_case, "1")
     B = int(B)
     (_, qt, N, K, bs) = next(m for m in SWEEP if m[0] == name)
@@ -386,6 +456,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["pyxis", "reference"], default="pyxis")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the Qwen3-1.7B-shape greedy decode measurement")
     args = ap.parse_args()
     if args.impl == "reference":
         ws = int(os.environ.get("WORLD_SIZE", "1"))

@@ -1,0 +1,73 @@
+/*
+ * pyxis_decode.h -- device-resident greedy decode of the transformer pyxis runs.
+ *
+ * Replaces Model::generate (src/model.rs:245-285) with temperature-0 sampling (the argmax of
+ * src/output_head.rs:25-44) for the Qwen3 layer stack of src/transformer.rs:28-90:
+ *   RmsNorm (src/rmsnorm.rs:11-20) -> Attention (src/attention.rs:57-141: q/k/v projections,
+ *   per-head QK RMSNorm, RoPE :144-162, causal GQA softmax attention over an f32 KV cache
+ *   (src/kv_cache.rs), o projection) -> residual -> RmsNorm -> Ffn (src/ffn.rs:33-54: gate/up,
+ *   SiLU, down) -> residual; final RmsNorm; lm_head; argmax.
+ * Every projection is a quantized matrix from pyxis_cuda.h, multiplied on the tensor cores or the
+ * GEMV kernels; everything between the projections runs as CUDA kernels on the context's stream,
+ * and one decode step is captured once into a CUDA graph and replayed per token.  Prompt tokens
+ * go through the same step one position at a time, as the reference's prefill does
+ * (src/attention.rs:74-98): position p attends to keys 0..p.
+ */
+#ifndef PYXIS_DECODE_H
+#define PYXIS_DECODE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "pyxis_cuda.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ModelConfig (src/model.rs:63-75) plus the KV-cache capacity in positions. */
+typedef struct {
+    int hidden, n_layers, n_q_heads, n_kv_heads, head_dim, ffn, vocab;
+    float rms_eps, rope_theta;
+    int max_seq;
+} pyxis_model_config;
+
+typedef struct pyxis_cuda_model pyxis_cuda_model;
+
+/* Allocates the KV cache, activations and the RoPE table (computed on the host in f32 with the
+ * reference's formula, src/attention.rs:151-154) on the context's device. */
+int pyxis_cuda_model_create(pyxis_cuda_ctx *ctx, const pyxis_model_config *cfg, pyxis_cuda_model **m);
+
+/* One layer's weights.  Projections are device handles kept by reference (they must outlive the
+ * model): wqkv = rows [q_proj (n_q*hd); k_proj (n_kv*hd); v_proj (n_kv*hd)] x hidden (per-row or
+ * per-group quantisation packs the stacked rows exactly as the three matrices), wo = hidden x
+ * n_q*hd, wgu = [gate_proj; up_proj] (2*ffn x hidden), wdown = hidden x ffn.  Norm weights are host
+ * f32 arrays copied to the device; q_norm / k_norm NULL means the layer has no QK-norm
+ * (src/model.rs:118-135). */
+int pyxis_cuda_model_set_layer(pyxis_cuda_model *m, int layer, const pyxis_cuda_weights *wqkv,
+                               const pyxis_cuda_weights *wo, const pyxis_cuda_weights *wgu,
+                               const pyxis_cuda_weights *wdown, const float *input_norm,
+                               const float *post_norm, const float *q_norm, const float *k_norm);
+
+/* The token embedding as host bf16 bits [vocab, hidden] (widened exactly on lookup, as
+ * tensor_f32 does), the lm_head handle (vocab x hidden; with tied embeddings a quantised copy of
+ * the same table, src/model.rs:219-224) and the final norm weight (host f32). */
+int pyxis_cuda_model_set_head(pyxis_cuda_model *m, const uint16_t *embedding_bf16,
+                              const pyxis_cuda_weights *lm_head, const float *final_norm);
+
+/* Greedy generation: feeds the n_prompt ids (>= 1), then writes the n_new next tokens to
+ * out_tokens.  n_prompt + n_new - 1 <= max_seq.  timing_ms (optional, 2 floats): device time of
+ * the prompt phase (through the first generated token) and of the remaining n_new - 1 steps. */
+int pyxis_cuda_model_generate(pyxis_cuda_model *m, const int32_t *prompt, size_t n_prompt, size_t n_new,
+                              int32_t *out_tokens, float *timing_ms);
+
+int pyxis_cuda_model_free(pyxis_cuda_model *m);
+
+/* The RoPE table the model uses: cos/sin[pos * (head_dim/2) + i] of pos * theta^(-2i/head_dim),
+ * computed on the host in f32 exactly as src/attention.rs:151-154 does. */
+int pyxis_rope_table(float theta, int head_dim, int max_pos, float *cos_out, float *sin_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

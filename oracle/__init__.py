@@ -49,6 +49,7 @@ def lib() -> C.CDLL:
         L.oracle_silu.argtypes = [C.c_float]
         L.oracle_silu.restype = C.c_float
         L.oracle_greedy_decode.argtypes = [_vp, _vp, _sz, _sz, _vp, C.c_int]
+        L.oracle_greedy_decode.restype = C.c_int
         L.oracle_num_cpus.restype = C.c_int
         _lib = L
     return _lib
@@ -154,3 +155,61 @@ def softmax(x) -> np.ndarray:
 
 def silu(x: float) -> float:
     return float(lib().oracle_silu(x))
+
+
+# ---- greedy decode (oracle_greedy_decode: Model::generate with argmax sampling) ----------------
+class OWeights(C.Structure):
+    _fields_ = [("kind", C.c_int), ("data", _vp), ("scales", _vp), ("block_size", _sz)]
+
+
+class OModel(C.Structure):
+    _fields_ = [("hidden", _sz), ("n_layers", _sz), ("n_q_heads", _sz), ("n_kv_heads", _sz), ("head_dim", _sz),
+                ("ffn", _sz), ("vocab", _sz), ("rms_eps", C.c_float), ("rope_theta", C.c_float),
+                ("embedding", _vp), ("input_norm", _vp), ("post_norm", _vp), ("q_norm", _vp), ("k_norm", _vp),
+                ("wq", _vp), ("wk", _vp), ("wv", _vp), ("wo", _vp), ("wgate", _vp), ("wup", _vp), ("wdown", _vp),
+                ("final_norm", _vp), ("lm_head", OWeights)]
+
+
+def greedy_decode(cfg, bf16, qtype: str, prompt, n_new: int, nthreads: int = 0):
+    """Greedy tokens of the model whose tensors ``bf16(name)`` returns (np.uint16 bits; names
+    ``layers.{l}.{q,k,v,o,gate,up,down}`` and ``embed``), quantised by the reference's policy
+    (src/model.rs:520-530: int8 one scale per row, int4 one per 32), tied lm_head, RMSNorm
+    weights 1, QK-norm when cfg.qk_norm."""
+    keep = []
+
+    def q(bits, in_features):
+        vals = bf16_to_f32(bits)
+        if qtype == "int8":
+            d, s = quantize_int8(vals, in_features)
+            w = OWeights(INT8, d.ctypes.data, s.ctypes.data, in_features)
+        else:
+            d, s = quantize_int4(vals, 32)
+            w = OWeights(INT4, d.ctypes.data, s.ctypes.data, 32)
+        keep.extend([d, s])
+        return w
+
+    nl = cfg.n_layers
+    ws = {k: (OWeights * nl)() for k in ("q", "k", "v", "o", "gate", "up", "down")}
+    ins = {"q": cfg.hidden, "k": cfg.hidden, "v": cfg.hidden, "o": cfg.q_dim, "gate": cfg.hidden,
+           "up": cfg.hidden, "down": cfg.ffn}
+    for l in range(nl):
+        for k in ws:
+            ws[k][l] = q(bf16(f"layers.{l}.{k}"), ins[k])
+    ones = np.ones(cfg.hidden, np.float32)
+    hones = np.ones(cfg.head_dim, np.float32)
+    norm_arr = (_vp * nl)(*([ones.ctypes.data] * nl))
+    hn_arr = (_vp * nl)(*([hones.ctypes.data if cfg.qk_norm else None] * nl))
+    emb_bits = bf16("embed")
+    emb = bf16_to_f32(emb_bits)
+    lm = q(emb_bits, cfg.hidden)
+    m = OModel(cfg.hidden, nl, cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn, cfg.vocab, cfg.rms_eps,
+               cfg.rope_theta, emb.ctypes.data, C.addressof(norm_arr), C.addressof(norm_arr), C.addressof(hn_arr),
+               C.addressof(hn_arr), C.addressof(ws["q"]), C.addressof(ws["k"]), C.addressof(ws["v"]),
+               C.addressof(ws["o"]), C.addressof(ws["gate"]), C.addressof(ws["up"]), C.addressof(ws["down"]),
+               ones.ctypes.data, lm)
+    pr = np.ascontiguousarray(np.asarray(prompt, np.int32))
+    out = np.empty(n_new, np.int32)
+    rc = lib().oracle_greedy_decode(C.addressof(m), pr.ctypes.data, pr.size, n_new, out.ctypes.data, nthreads)
+    if rc:
+        raise RuntimeError("oracle_greedy_decode failed")
+    return out

@@ -6,6 +6,7 @@
  * cosf, sinf, expf and sqrtf -- the same libm rustc's f32 methods call on x86-64 Linux.
  */
 #include <math.h>
+#include <pthread.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -84,8 +85,81 @@ void oracle_kv_free(oracle_kv *kv) {
 
 size_t oracle_kv_len(const oracle_kv *kv, size_t layer) { return kv->len[layer]; }
 
+/* The model's projections.  The value computed for each row is exactly oracle_dot_int8 /
+ * oracle_dot_int4 (same operations in the same order, so the same bits); the scale index
+ * (o+i)/block is found without a division per element, which only makes the greedy-decode
+ * oracle faster.  The timed CPU baseline keeps the reference's own per-element division. */
+typedef struct {
+    const oracle_weights *w;
+    const float *x;
+    size_t in, out;
+    float *y;
+    size_t next;
+    pthread_mutex_t mu;
+} mm_fast_job;
+
+static void mm_fast_rows(const mm_fast_job *j, size_t r0, size_t r1) {
+    const oracle_weights *w = j->w;
+    const size_t K = j->in, bs = w->block_size;
+    for (size_t r = r0; r < r1; ++r) {
+        const size_t o = r * K;
+        size_t blk = o / bs, blk_end = (blk + 1) * bs;
+        float sc = w->scales[blk];
+        if (w->kind == ORACLE_INT8) {
+            const int8_t *q = (const int8_t *)w->data;
+            float sum = -0.0f;
+            for (size_t i = 0; i < K; ++i) {
+                if (o + i == blk_end) { ++blk; blk_end += bs; sc = w->scales[blk]; }
+                float t = j->x[i] * (float)q[o + i];
+                t = t * sc;
+                sum += t;
+            }
+            j->y[r] = sum;
+        } else {
+            const uint8_t *q = (const uint8_t *)w->data;
+            float sum = 0.0f;
+            for (size_t i = 0; i < K; ++i) {
+                const size_t g = o + i;
+                if (g == blk_end) { ++blk; blk_end += bs; sc = w->scales[blk]; }
+                const uint8_t byte = q[g / 2];
+                const uint8_t nib = (g % 2 == 0) ? (byte & 0x0f) : ((byte >> 4) & 0x0f);
+                float t = j->x[i] * ((float)nib - 8.0f);
+                t = t * sc;
+                sum += t;
+            }
+            j->y[r] = sum;
+        }
+    }
+}
+
+static void *mm_fast_worker(void *arg) {
+    mm_fast_job *j = (mm_fast_job *)arg;
+    for (;;) {
+        pthread_mutex_lock(&j->mu);
+        size_t r0 = j->next;
+        j->next += 64;
+        pthread_mutex_unlock(&j->mu);
+        if (r0 >= j->out) break;
+        size_t r1 = r0 + 64 < j->out ? r0 + 64 : j->out;
+        mm_fast_rows(j, r0, r1);
+    }
+    return NULL;
+}
+
 static void mm(const oracle_weights *w, const float *x, size_t out, size_t in, float *y, int nt) {
-    oracle_matmul(x, w->kind, w->data, w->scales, w->block_size, out, in, y, nt);
+    if (w->kind != ORACLE_INT8 && w->kind != ORACLE_INT4) {
+        oracle_matmul(x, w->kind, w->data, w->scales, w->block_size, out, in, y, nt);
+        return;
+    }
+    mm_fast_job j = {w, x, in, out, y, 0, PTHREAD_MUTEX_INITIALIZER};
+    int n = nt > 0 ? nt : oracle_num_cpus();
+    if (n > 64) n = 64;
+    pthread_t th[64];
+    int started = 0;
+    for (int t = 1; t < n; ++t)
+        if (pthread_create(&th[started], NULL, mm_fast_worker, &j) == 0) ++started;
+    mm_fast_worker(&j);
+    for (int t = 0; t < started; ++t) pthread_join(th[t], NULL);
 }
 
 /* Attention::forward (src/attention.rs:57-141).  x: [seq_len, hidden] (already input-normed),

@@ -49,6 +49,12 @@ SIGNATURES = {
     "pyxis_cuda_check_device_error": (C.c_int, [_vp]),
     "pyxis_cuda_argmax_dev": (C.c_int, [_vp, _vp, _sz, _sz, _sz, C.c_int64, _vp, _vp, _vp]),
     "pyxis_cuda_argmax_noalloc": (C.c_int, [_vp, _sz, _sz, _sz, C.c_int64, _vp, _vp, _vp]),
+    "pyxis_cuda_model_create": (C.c_int, [_vp, _vp, C.POINTER(_vp)]),
+    "pyxis_cuda_model_set_layer": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "pyxis_cuda_model_set_head": (C.c_int, [_vp, _vp, _vp, _vp]),
+    "pyxis_cuda_model_generate": (C.c_int, [_vp, _vp, _sz, _sz, _vp, _vp]),
+    "pyxis_cuda_model_free": (C.c_int, [_vp]),
+    "pyxis_rope_table": (C.c_int, [C.c_float, C.c_int, C.c_int, _vp, _vp]),
     "pyxis_synth_normal_f32": (None, [C.c_uint64, _sz, C.c_float, _vp]),
     "pyxis_synth_normal_bf16": (None, [C.c_uint64, _sz, C.c_float, _vp]),
     "pyxis_synth_tokens": (None, [C.c_uint64, _sz, C.c_uint32, _vp]),

@@ -8,40 +8,11 @@
 
 #include "../../include/pyxis_cuda.h"
 #include "argmax.h"
+#include "ctx.h"
 #include "kernels.h"
 
 using namespace pyxis;
 
-struct pyxis_cuda_ctx {
-    int device;
-    int num_sms;
-    cudaStream_t stream;
-    // staging for the host-pointer entry points (grown on demand)
-    float *dx = nullptr;
-    size_t dx_cap = 0;
-    float *dy = nullptr;
-    size_t dy_cap = 0;
-    // workspace kept for pyxis_cuda_matmul_dev calls that pass none
-    void *ws = nullptr;
-    size_t ws_cap = 0;
-    // argmax scratch (allocated and zeroed at init)
-    ArgmaxScratch amax{};
-    void *amax_mem = nullptr;
-    // device error flag written by kernels whose bounded waits ran out (0 = none)
-    int *d_err = nullptr;
-    // split-K scratch of the tensor-core GEMV (zeroed at init; the kernel leaves it zeroed)
-    void *tcg_scratch = nullptr;
-    size_t tcg_scratch_bytes = 0;
-};
-
-struct pyxis_cuda_weights {
-    int device;
-    int qtype;
-    size_t num_elements, block_size;
-    size_t data_bytes, num_scales;
-    uint8_t *data;   // one allocation: data, padded to 256 B, then scales
-    float *scales;
-};
 
 namespace {
 
@@ -83,7 +54,6 @@ struct DeviceGuard {
 size_t div_ceil(size_t a, size_t b) { return (a + b - 1) / b; }
 
 constexpr size_t kTcMinRows = 16;        // matmul_dev rows from which the tensor-core GEMM runs
-constexpr size_t kTcgScratchRows = 32768; // split-K runs only below 148 x 128 rows; covered
 
 size_t packed_bytes(int qtype, size_t n) { return qtype == PYXIS_QTYPE_INT8 ? n : div_ceil(n, 2); }
 
@@ -150,6 +120,46 @@ int check_matmul(const pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, size_t 
 
 int pyxis::record_error(int code, const char *msg) { return fail(code, "%s", msg); }
 
+int pyxis::run_matmul(pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, const float *X, size_t M, size_t ldx,
+                      size_t out_features, size_t in_features, float *Y, size_t ldy, void *workspace,
+                      size_t workspace_bytes, cudaStream_t st) {
+    QMatrix q = qmatrix(w, out_features, in_features);
+    if (M >= kTcMinRows && gemm_tc_supported(q) && (reinterpret_cast<uintptr_t>(X) & 15) == 0 && ldx % 4 == 0) {
+        const size_t need = gemm_tc_workspace_bytes(M, in_features);
+        if (!workspace) {
+            if (ctx->ws_cap < need) {
+                cudaFree(ctx->ws);
+                ctx->ws = nullptr;
+                ctx->ws_cap = 0;
+                PYXIS_CUDA_TRY(cudaMalloc(&ctx->ws, need), "cudaMalloc(workspace)");
+                ctx->ws_cap = need;
+            }
+            workspace = ctx->ws;
+        } else if (workspace_bytes < need) {
+            return fail(PYXIS_EINVAL, "workspace of %zu bytes < %zu needed", workspace_bytes, need);
+        } else if (reinterpret_cast<uintptr_t>(workspace) & 255) {
+            return fail(PYXIS_EINVAL, "workspace must be 256-byte aligned");
+        }
+        cudaError_t e = launch_gemm_tc(q, X, M, ldx, Y, ldy, workspace, ctx->d_err, st);
+        if (e != cudaSuccess) return cuda_fail(e, "tensor-core GEMM launch");
+        return PYXIS_OK;
+    }
+    for (size_t m0 = 0; m0 < M; m0 += 8) {
+        size_t b = M - m0 < 8 ? M - m0 : 8;
+        const float *xb = X + m0 * ldx;
+        cudaError_t e;
+        if (gemv_tc_supported(q, b, ctx->num_sms) && (reinterpret_cast<uintptr_t>(xb) & 15) == 0 &&
+            (b == 1 || ldx % 4 == 0))
+            e = launch_gemv_tc(q, xb, b, ldx, Y + m0 * ldy, ldy, ctx->tcg_scratch, ctx->tcg_scratch_bytes, ctx->d_err,
+                               ctx->num_sms, st);
+        else
+            e = launch_gemv(q, xb, b, ldx, Y + m0 * ldy, ldy, ctx->d_err, ctx->num_sms, st);
+        if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
+    }
+    return PYXIS_OK;
+}
+
+
 extern "C" {
 
 const char *pyxis_cuda_last_error(void) { return g_last_error.c_str(); }
@@ -191,7 +201,7 @@ int pyxis_cuda_init(int device, pyxis_cuda_ctx **out) {
     }
     e = cudaMalloc(&ctx->d_err, sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(ctx->d_err, 0, sizeof(int));
-    ctx->tcg_scratch_bytes = gemv_tc_scratch_bytes(kTcgScratchRows);
+    ctx->tcg_scratch_bytes = gemv_tc_scratch_bytes(ctx->num_sms);
     if (e == cudaSuccess) e = cudaMalloc(&ctx->tcg_scratch, ctx->tcg_scratch_bytes);
     if (e == cudaSuccess) e = cudaMemset(ctx->tcg_scratch, 0, ctx->tcg_scratch_bytes);
     if (e != cudaSuccess) {
@@ -341,47 +351,12 @@ int pyxis_cuda_matmul_dev(pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, cons
                           void *workspace, size_t workspace_bytes, void *stream) {
     int rc = check_matmul(ctx, w, out_features, in_features);
     if (rc) return rc;
-    (void)workspace;
-    (void)workspace_bytes;
     if (M == 0 || out_features == 0) return PYXIS_OK;
     if (!X || !Y) return fail(PYXIS_EINVAL, "null X or Y");
     if (M > 1 && (ldx < in_features || ldy < out_features)) return fail(PYXIS_EINVAL, "row stride smaller than the row");
     DeviceGuard g(ctx->device);
-    cudaStream_t st = pick_stream(ctx, stream);
-    QMatrix q = qmatrix(w, out_features, in_features);
-    if (M >= kTcMinRows && gemm_tc_supported(q) && (reinterpret_cast<uintptr_t>(X) & 15) == 0 && ldx % 4 == 0) {
-        const size_t need = gemm_tc_workspace_bytes(M, in_features);
-        if (!workspace) {
-            if (ctx->ws_cap < need) {
-                cudaFree(ctx->ws);
-                ctx->ws = nullptr;
-                ctx->ws_cap = 0;
-                PYXIS_CUDA_TRY(cudaMalloc(&ctx->ws, need), "cudaMalloc(workspace)");
-                ctx->ws_cap = need;
-            }
-            workspace = ctx->ws;
-        } else if (workspace_bytes < need) {
-            return fail(PYXIS_EINVAL, "workspace of %zu bytes < %zu needed", workspace_bytes, need);
-        } else if (reinterpret_cast<uintptr_t>(workspace) & 255) {
-            return fail(PYXIS_EINVAL, "workspace must be 256-byte aligned");
-        }
-        cudaError_t e = launch_gemm_tc(q, X, M, ldx, Y, ldy, workspace, ctx->d_err, st);
-        if (e != cudaSuccess) return cuda_fail(e, "tensor-core GEMM launch");
-        return PYXIS_OK;
-    }
-    for (size_t m0 = 0; m0 < M; m0 += 8) {
-        size_t b = M - m0 < 8 ? M - m0 : 8;
-        const float *xb = X + m0 * ldx;
-        cudaError_t e;
-        if (gemv_tc_supported(q, b, ctx->num_sms) && (reinterpret_cast<uintptr_t>(xb) & 15) == 0 &&
-            (b == 1 || ldx % 4 == 0))
-            e = launch_gemv_tc(q, xb, b, ldx, Y + m0 * ldy, ldy, ctx->tcg_scratch, ctx->tcg_scratch_bytes, ctx->d_err,
-                               ctx->num_sms, st);
-        else
-            e = launch_gemv(q, xb, b, ldx, Y + m0 * ldy, ldy, ctx->d_err, ctx->num_sms, st);
-        if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
-    }
-    return PYXIS_OK;
+    return run_matmul(ctx, w, X, M, ldx, out_features, in_features, Y, ldy, workspace, workspace_bytes,
+                      pick_stream(ctx, stream));
 }
 
 int pyxis_cuda_matmul_batch(pyxis_cuda_ctx *ctx, const float *input, size_t M, const pyxis_cuda_weights *w,

@@ -16,11 +16,12 @@
 //
 // CTA (persistent, one per SM): warp 0 = TMA producer into an S-stage ring (16 KB stages),
 // warp 1 = TMEM owner + MMA issuer (M=128, N=16|32, K=32 per instruction, accumulator
-// double-buffered in TMEM across work items), warps 2-5 = epilogue (tcgen05.ld, one TMEM lane =
-// one weight row).  Warps 1-5 build the digit operand while the producer's first copies are in
-// flight.  Work items are (128-row tile, K split); with K splits (small N) the partial int32 sums
-// are added exactly with atomics into a scratch tile, and the CTA that finishes a tile last
-// converts it and zeroes the scratch for the next launch.  Every wait is bounded.
+// double-buffered in TMEM across tile segments), warps 2-5 = epilogue (tcgen05.ld, one TMEM
+// lane = one weight row).  Warps 1-5 build the digit operand while the producer's first copies
+// are in flight.  A tile whose stages span several CTAs has its partial int32 sums added exactly
+// with atomics into a scratch slot, and the CTA that finishes the tile last
+// converts it and zeroes the scratch for the next launch.  The schedule is stream-K: every CTA
+// gets the same number of (tile, K-block) stages.  Every wait is bounded.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -40,19 +41,24 @@ constexpr uint32_t kStageBytes = TM * TKB;
 constexpr uint32_t kSmemTotal = 222 * 1024;
 constexpr int kMaxStages = 12;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
+// The 4 MMAs of a stage (one per 32-byte K slice) write 4 separate accumulators, so they do not
+// wait on each other; the epilogue adds them (exact int32).  2 buffers x 4 x NB(<= 32) columns.
+constexpr int kAccPerBuf = TKB / 32;
+constexpr uint32_t kTmemCols = 256;
 enum { kErrProd = 0x301, kErrMma = 0x302, kErrEpi = 0x303, kErrDrain = 0x304 };
 
 struct Params {
     int N, K, B, NB;
-    int num_kb, ks, kb_per_split, num_tiles, num_items, stages;
+    int num_kb, num_tiles, stages;
+    long long total_stages;  // num_tiles * num_kb, split evenly over the grid (stream-K)
     uint32_t xd_bytes;
     const float *x;
     long long ldx;
     const float *scales;
     float *y;
     long long ldy;
-    int *accum;         // [num_tiles * 128][NB] int32, zero between launches (ks > 1)
-    unsigned *tickets;  // [num_tiles], zero between launches (ks > 1)
+    int *accum;         // [grid][128][NB] int32 partial tiles, zero between launches
+    unsigned *tickets;  // [grid], zero between launches
     int *err;
 };
 
@@ -85,6 +91,16 @@ PYXIS_DEVINL float combine(const int *D, double xs, double sr) {
     return (float)((double)s * xs * sr);
 }
 
+// Stream-K schedule: the num_tiles x num_kb stages are cut into gridDim.x equal contiguous
+// ranges; a tile whose stages span several CTAs is combined exactly (int32 atomics) in the slot
+// of the first CTA that touches it -- each CTA is the first of at most one shared tile.
+struct Sched {
+    long long T;
+    int G, nkb;
+    PYXIS_DEVINL long long begin(int c) const { return (long long)c * T / G; }
+    PYXIS_DEVINL int owner(long long s) const { return (int)(((s + 1) * G + T - 1) / T - 1); }
+};
+
 __global__ void __launch_bounds__(kThreads, 1)
     gemv_tc_i8_kernel(const __grid_constant__ CUtensorMap tm_w, const Params p) {
     extern __shared__ uint8_t smem_raw[];
@@ -115,7 +131,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort_flag = 0;
         tc::fence_mbar_init();
     }
-    if (warp == 1) tc::tmem_alloc(tmem_slot, 64);
+    if (warp == 1) tc::tmem_alloc(tmem_slot, kTmemCols);
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
@@ -126,16 +142,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             tc::prefetch_tmap(&tm_w);
             int g = 0;
-            for (int it = blockIdx.x; it < p.num_items && !*abort_flag; it += gridDim.x) {
-                const int tile = it / p.ks, kb0 = (it % p.ks) * p.kb_per_split;
-                for (int kb = kb0; kb < kb0 + p.kb_per_split; ++kb, ++g) {
-                    const int s = g % p.stages;
-                    if (g >= p.stages &&
-                        !tc::mbar_wait_bounded(&empty[s], ((g / p.stages) - 1) & 1, abort_flag, p.err, kErrProd, kTimeoutNs))
-                        break;
-                    tc::mbar_arrive_expect_tx(&full[s], kStageBytes);
-                    tc::tma_load_2d(ring + (size_t)s * kStageBytes, &tm_w, kb * TKB, tile * TM, &full[s]);
-                }
+            const Sched sc{p.total_stages, (int)gridDim.x, p.num_kb};
+            const long long se = sc.begin(blockIdx.x + 1);
+            for (long long st = sc.begin(blockIdx.x); st < se; ++st, ++g) {
+                const int s = g % p.stages;
+                if (g >= p.stages &&
+                    !tc::mbar_wait_bounded(&empty[s], ((g / p.stages) - 1) & 1, abort_flag, p.err, kErrProd, kTimeoutNs))
+                    break;
+                const int tile = (int)(st / p.num_kb), kb = (int)(st % p.num_kb);
+                tc::mbar_arrive_expect_tx(&full[s], kStageBytes);
+                tc::tma_load_2d(ring + (size_t)s * kStageBytes, &tm_w, kb * TKB, tile * TM, &full[s]);
             }
             if (*abort_flag) {  // let the copies already issued land
                 volatile int no_abort = 0;
@@ -147,6 +163,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         // -------------------------------------------------------------------- digit operand
         const int bt = threadIdx.x - 32, nbt = kThreads - 32;  // warps 1-5
         const int bwarp = warp - 1;
+        const Sched sc{p.total_stages, (int)gridDim.x, p.num_kb};
+        const long long my_sb = sc.begin(blockIdx.x), my_se = sc.begin(blockIdx.x + 1);
+        // K-blocks this CTA multiplies: a contiguous run (mod num_kb) unless it spans a whole tile
+        const int need_lo = (int)(my_sb % p.num_kb);
+        const long long need_n = my_se - my_sb;
+        auto needed = [&](int kb) { return need_n >= p.num_kb || ((kb - need_lo + p.num_kb) % p.num_kb) < need_n; };
         for (int b = 0; b < p.B; ++b) {
             const float *xb = p.x + (size_t)b * p.ldx;
             float m = 0.f;
@@ -157,7 +179,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         {
             const uint4 z = make_uint4(0, 0, 0, 0);
-            for (uint32_t i = bt; i < p.xd_bytes / 16; i += nbt) reinterpret_cast<uint4 *>(xd)[i] = z;
+            const uint32_t per_kb = (uint32_t)p.NB * TKB / 16;
+            for (uint32_t i = bt; i < p.xd_bytes / 16; i += nbt)
+                if (needed((int)(i / per_kb))) reinterpret_cast<uint4 *>(xd)[i] = z;
         }
         named_bar(1, nbt);
         if (bt < p.B) {
@@ -172,6 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kq = p.K / 4;
         for (int idx = bt; idx < p.B * kq; idx += nbt) {
             const int b = idx / kq, k = (idx - b * kq) * 4;
+            if (!needed(k / TKB)) continue;
             const int E = xexp[b];
             const float4 xv = *reinterpret_cast<const float4 *>(p.x + (size_t)b * p.ldx + k);
             const float xs4[4] = {xv.x, xv.y, xv.z, xv.w};
@@ -207,16 +232,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t idesc = idesc_i8(TM, p.NB);
                 int g = 0, li = 0;
                 bool ok = true;
-                for (int it = blockIdx.x; it < p.num_items && ok; it += gridDim.x, ++li) {
-                    const int kb0 = (it % p.ks) * p.kb_per_split;
+                for (long long st = my_sb; st < my_se && ok; ++li) {
+                    const int tile = (int)(st / p.num_kb);
+                    const long long tend = my_se < (long long)(tile + 1) * p.num_kb ? my_se : (long long)(tile + 1) * p.num_kb;
+                    const int kb0 = (int)(st % p.num_kb), nk = (int)(tend - st);
+                    st = tend;
                     const int buf = li & 1;
                     if (li >= 2) {
                         ok = tc::mbar_wait_bounded(&tempty[buf], ((li >> 1) - 1) & 1, abort_flag, p.err, kErrMma, kTimeoutNs);
                         if (!ok) break;
                     }
                     tc::tc_fence_after();
-                    const uint32_t d = tmem_base + (uint32_t)(buf * p.NB);
-                    for (int kb = kb0; kb < kb0 + p.kb_per_split; ++kb, ++g) {
+                    const uint32_t d = tmem_base + (uint32_t)(buf * kAccPerBuf * p.NB);
+                    for (int kb = kb0; kb < kb0 + nk; ++kb, ++g) {
                         const int s = g % p.stages;
                         ok = tc::mbar_wait_bounded(&full[s], (g / p.stages) & 1, abort_flag, p.err, kErrMma, kTimeoutNs);
                         if (!ok) break;
@@ -225,7 +253,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint64_t b0 = tc::desc_sw128(tc::smem_u32(xd + (size_t)kb * (p.NB * TKB)));
 #pragma unroll
                         for (int q = 0; q < TKB / 32; ++q)
-                            mma_i8(d, a0 + (uint64_t)(2 * q), b0 + (uint64_t)(2 * q), idesc, (kb > kb0 || q > 0) ? 1u : 0u);
+                            mma_i8(d + (uint32_t)(q * p.NB), a0 + (uint64_t)(2 * q), b0 + (uint64_t)(2 * q), idesc,
+                                   kb > kb0 ? 1u : 0u);
                         tc::mma_commit(&empty[s]);
                     }
                     if (ok) tc::mma_commit(&tfull[buf]);
@@ -240,8 +269,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             // whose wait ran out skips the work but keeps the barrier sequence.
             const int qd = warp & 3;  // TMEM lane quarter of this warp
             int li = 0;
-            for (int it = blockIdx.x; it < p.num_items; it += gridDim.x, ++li) {
-                const int tile = it / p.ks;
+            for (long long st = my_sb; st < my_se; ++li) {
+                const int tile = (int)(st / p.num_kb);
+                st = my_se < (long long)(tile + 1) * p.num_kb ? my_se : (long long)(tile + 1) * p.num_kb;
+                const int first = sc.owner((long long)tile * p.num_kb);
+                const int parts = sc.owner((long long)(tile + 1) * p.num_kb - 1) - first + 1;
                 const int buf = li & 1;
                 int ok = 1;
                 if (lane == 0) ok = tc::mbar_wait_bounded(&tfull[buf], (li >> 1) & 1, abort_flag, p.err, kErrEpi, kTimeoutNs);
@@ -251,27 +283,37 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < 32; ++j) D[j] = 0;
                 if (ok) {
                     tc::tc_fence_after();
-                    const uint32_t taddr = tmem_base + ((uint32_t)(32 * qd) << 16) + (uint32_t)(buf * p.NB);
-                    tmem_ld16(taddr, *reinterpret_cast<int(*)[16]>(&D[0]));
-                    if (p.NB == 32) tmem_ld16(taddr + 16, *reinterpret_cast<int(*)[16]>(&D[16]));
+                    const uint32_t taddr = tmem_base + ((uint32_t)(32 * qd) << 16) + (uint32_t)(buf * kAccPerBuf * p.NB);
+#pragma unroll
+                    for (int a = 0; a < kAccPerBuf; ++a) {
+                        int T[16];
+                        tmem_ld16(taddr + (uint32_t)(a * p.NB), T);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) D[j] += T[j];
+                        if (p.NB == 32) {
+                            tmem_ld16(taddr + (uint32_t)(a * p.NB + 16), T);
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) D[16 + j] += T[j];
+                        }
+                    }
                     tc::tc_fence_before();
                     __syncwarp();
                     if (lane == 0) tc::mbar_arrive(&tempty[buf]);
                 }
                 const int rl = 32 * qd + lane;
                 const int row = tile * TM + rl;
-                if (p.ks == 1) {
+                if (parts == 1) {
                     if (ok && row < p.N) {
                         const double sr = (double)__ldg(p.scales + row);
                         for (int b = 0; b < p.B; ++b) p.y[(size_t)b * p.ldy + row] = combine(&D[4 * b], xscale[b], sr);
                     }
                 } else {
-                    int *acc = p.accum + ((size_t)tile * TM + rl) * p.NB;
+                    int *acc = p.accum + ((size_t)first * TM + rl) * p.NB;
                     if (ok)
                         for (int j = 0; j < 4 * p.B; ++j) atomicAdd(acc + j, D[j]);
                     __threadfence();
                     named_bar(2, 128);
-                    if (warp == 2 && lane == 0) *last_flag = atomicAdd(&p.tickets[tile], 1u) == (unsigned)(p.ks - 1);
+                    if (warp == 2 && lane == 0) *last_flag = atomicAdd(&p.tickets[first], 1u) == (unsigned)(parts - 1);
                     named_bar(2, 128);
                     const bool last = *last_flag;
                     if (last) {
@@ -287,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                     named_bar(2, 128);
-                    if (last && warp == 2 && lane == 0) p.tickets[tile] = 0;
+                    if (last && warp == 2 && lane == 0) p.tickets[first] = 0;
                 }
             }
         }
@@ -297,7 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (warp == 1) {
         tc::tc_fence_after();
-        tc::tmem_dealloc(tmem_base, 64);
+        tc::tmem_dealloc(tmem_base, kTmemCols);
     }
 }
 
@@ -316,7 +358,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 struct Plan {
     bool ok = false;
-    int NB = 16, ks = 1, stages = 0;
+    int NB = 16, stages = 0;
     uint32_t xd_bytes = 0;
 };
 
@@ -331,20 +373,14 @@ Plan plan_for(const QMatrix &w, size_t B, int num_sms) {
     const uint32_t avail = kSmemTotal - 1024 - 1024 - pl.xd_bytes;  // alignment slack, barriers
     pl.stages = std::min<int>(kMaxStages, (int)(avail / kStageBytes));
     if (pl.stages < 2) return pl;
-    const int num_kb = (int)(w.K / TKB);
-    const long tiles = (long)((w.N + TM - 1) / TM);
-    int ks = 1;
-    while (tiles * ks < num_sms && num_kb % (2 * ks) == 0) ks *= 2;
-    pl.ks = ks;
     pl.ok = true;
     return pl;
 }
 
 }  // namespace
 
-size_t gemv_tc_scratch_bytes(size_t N) {
-    const size_t tiles = (N + TM - 1) / TM;
-    return tiles * TM * 32 * sizeof(int) + tiles * sizeof(unsigned) + 256;
+size_t gemv_tc_scratch_bytes(int max_grid) {
+    return (size_t)max_grid * TM * 32 * sizeof(int) + (size_t)max_grid * sizeof(unsigned) + 256;
 }
 
 bool gemv_tc_supported(const QMatrix &w, size_t B, int num_sms) { return plan_for(w, B, num_sms).ok; }
@@ -355,7 +391,9 @@ cudaError_t launch_gemv_tc(const QMatrix &w, const float *X, size_t B, size_t ld
     if (!pl.ok) return cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(X) & 15) || (B > 1 && ldx % 4)) return cudaErrorInvalidValue;
     const int num_tiles = (int)((w.N + TM - 1) / TM);
-    if (pl.ks > 1 && (!scratch || scratch_bytes < gemv_tc_scratch_bytes(w.N))) return cudaErrorInvalidValue;
+    const long long total = (long long)num_tiles * (long long)(w.K / TKB);
+    const int grid = (int)std::max<long long>(1, std::min<long long>(num_sms, total));
+    if (!scratch || scratch_bytes < gemv_tc_scratch_bytes(grid)) return cudaErrorInvalidValue;
     auto fn = encode_fn();
     if (!fn) return cudaErrorNotSupported;
     CUtensorMap tm;
@@ -373,10 +411,8 @@ cudaError_t launch_gemv_tc(const QMatrix &w, const float *X, size_t B, size_t ld
     p.B = (int)B;
     p.NB = pl.NB;
     p.num_kb = (int)(w.K / TKB);
-    p.ks = pl.ks;
-    p.kb_per_split = p.num_kb / pl.ks;
     p.num_tiles = num_tiles;
-    p.num_items = num_tiles * pl.ks;
+    p.total_stages = total;
     p.stages = pl.stages;
     p.xd_bytes = pl.xd_bytes;
     p.x = X;
@@ -384,16 +420,15 @@ cudaError_t launch_gemv_tc(const QMatrix &w, const float *X, size_t B, size_t ld
     p.scales = w.scales;
     p.y = Y;
     p.ldy = (long long)ldy;
-    if (pl.ks > 1) {
+    {
         uint8_t *sb = reinterpret_cast<uint8_t *>(scratch);
         p.accum = reinterpret_cast<int *>(sb);
-        p.tickets = reinterpret_cast<unsigned *>(sb + (size_t)num_tiles * TM * 32 * sizeof(int));
+        p.tickets = reinterpret_cast<unsigned *>(sb + (size_t)grid * TM * 32 * sizeof(int));
     }
     p.err = err;
     static const bool attr =
         cudaFuncSetAttribute(gemv_tc_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTotal) == cudaSuccess;
     if (!attr) return cudaErrorInvalidConfiguration;
-    const int grid = std::max(1, std::min(num_sms, p.num_items));
     gemv_tc_i8_kernel<<<grid, kThreads, kSmemTotal, st>>>(tm, p);
     return cudaGetLastError();
 }

@@ -42,10 +42,10 @@ cudaError_t launch_gemm_tc(const QMatrix &w, const float *X, size_t M, size_t ld
                            int *err, cudaStream_t st);
 
 // int8 per-row GEMV for 1-8 input rows on tcgen05 kind::i8 (gemv_tc.cu).  `scratch` holds the
-// split-K partial sums for matrices of fewer than ~148 x 128 rows; it must be zero before the
-// first launch and the kernel leaves it zero.
+// partial sums of tiles shared by two or more CTAs (one slot per CTA of a grid of up to
+// max_grid); it must be zero before the first launch and the kernel leaves it zero.
 bool gemv_tc_supported(const QMatrix &w, size_t B, int num_sms);
-size_t gemv_tc_scratch_bytes(size_t N);
+size_t gemv_tc_scratch_bytes(int max_grid);
 cudaError_t launch_gemv_tc(const QMatrix &w, const float *X, size_t B, size_t ldx, float *Y, size_t ldy,
                            void *scratch, size_t scratch_bytes, int *err, int num_sms, cudaStream_t st);
 

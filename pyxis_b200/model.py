@@ -1,0 +1,152 @@
+"""Device-resident greedy decode over quantized weights (include/pyxis_decode.h) and the seeded
+random-init model it is benchmarked and tested on.
+
+``SyntheticModel`` builds the Qwen3 layer stack of pyxis (src/model.rs:84-239) from seeded
+N(0, 0.02) bf16 tensors with RMSNorm weights 1 -- the checkpoint-free stand-in for a real model.
+The projections are quantised on the device by the reference's rules (src/model.rs:501-530: int8
+one scale per row, int4 one per 32 values); the lm_head is the quantised tied embedding
+(src/model.rs:219-224).  ``Decoder`` runs Model::generate with greedy sampling on the GPU.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import zlib
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import Weights, _native, _require_cuda
+from ._native import check
+
+INT4_BLOCK_SIZE = 32
+
+
+@dataclass(frozen=True)
+class ModelConfig:
+    """ModelConfig (src/model.rs:63-75)."""
+    hidden: int = 2048
+    n_layers: int = 28
+    n_q_heads: int = 16
+    n_kv_heads: int = 8
+    head_dim: int = 128
+    ffn: int = 6144
+    vocab: int = 151936
+    rms_eps: float = 1e-6
+    rope_theta: float = 1e6
+    qk_norm: bool = True
+
+    @property
+    def q_dim(self) -> int:
+        return self.n_q_heads * self.head_dim
+
+    @property
+    def kv_dim(self) -> int:
+        return self.n_kv_heads * self.head_dim
+
+
+QWEN3_1_7B = ModelConfig()
+
+
+class _CConfig(C.Structure):
+    _fields_ = [("hidden", C.c_int), ("n_layers", C.c_int), ("n_q_heads", C.c_int), ("n_kv_heads", C.c_int),
+                ("head_dim", C.c_int), ("ffn", C.c_int), ("vocab", C.c_int), ("rms_eps", C.c_float),
+                ("rope_theta", C.c_float), ("max_seq", C.c_int)]
+
+
+def tensor_seed(base: int, name: str) -> int:
+    return (base * 0x100000001B3 ^ zlib.crc32(name.encode())) & 0xFFFFFFFFFFFFFFFF
+
+
+class SyntheticModel:
+    """Seeded bf16 tensors of one model: ``bf16(name)`` -> np.uint16 bits, generated on demand
+    (include/pyxis_synth.h), so the oracle and the device see the same values."""
+
+    def __init__(self, cfg: ModelConfig, seed: int = 0x5EED):
+        self.cfg = cfg
+        self.seed = seed
+
+    def shape(self, name: str) -> tuple[int, int]:
+        c = self.cfg
+        kind = name.split(".")[-1]
+        return {"q": (c.q_dim, c.hidden), "k": (c.kv_dim, c.hidden), "v": (c.kv_dim, c.hidden),
+                "o": (c.hidden, c.q_dim), "gate": (c.ffn, c.hidden), "up": (c.ffn, c.hidden),
+                "down": (c.hidden, c.ffn), "embed": (c.vocab, c.hidden)}[kind]
+
+    def bf16(self, name: str) -> np.ndarray:
+        from . import synth_normal_bf16
+        r, k = self.shape(name)
+        return synth_normal_bf16(tensor_seed(self.seed, name), r * k, 0.02)
+
+    def norm(self) -> np.ndarray:
+        return np.ones(self.cfg.hidden, np.float32)
+
+    def head_norm(self):
+        return np.ones(self.cfg.head_dim, np.float32) if self.cfg.qk_norm else None
+
+
+def _quantize(bits: np.ndarray, qtype: str, in_features: int, device: int):
+    """quantize_weights' block policy (src/model.rs:520-530) applied on the device."""
+    import torch
+    t = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).to(f"cuda:{device}")
+    if qtype == "int8":
+        return Weights.quantize_int8(t, in_features, device=device)
+    return Weights.quantize_int4(t, INT4_BLOCK_SIZE, device=device)
+
+
+class Decoder:
+    """Model::generate (src/model.rs:245-285) with temperature-0 sampling, on one GPU."""
+
+    def __init__(self, model: SyntheticModel, qtype: str = "int8", max_seq: int = 256, device: int = 0):
+        cfg = model.cfg
+        self.cfg = cfg
+        self.ctx = _require_cuda(device)
+        L = _native.lib()
+        cc = _CConfig(cfg.hidden, cfg.n_layers, cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn, cfg.vocab,
+                      cfg.rms_eps, cfg.rope_theta, max_seq)
+        h = C.c_void_p()
+        check(L.pyxis_cuda_model_create(self.ctx.handle, C.addressof(cc), C.byref(h)))
+        self.handle = h
+        self.max_seq = max_seq
+        self._keep = []
+        ones = model.norm()
+        hn = model.head_norm()
+        fp = C.POINTER(C.c_float)
+
+        def p(a):
+            return a.ctypes.data_as(fp) if a is not None else None
+
+        for layer in range(cfg.n_layers):
+            pre = f"layers.{layer}."
+            qkv = np.concatenate([model.bf16(pre + "q"), model.bf16(pre + "k"), model.bf16(pre + "v")])
+            wqkv = _quantize(qkv, qtype, cfg.hidden, device)
+            wo = _quantize(model.bf16(pre + "o"), qtype, cfg.q_dim, device)
+            wgu = _quantize(np.concatenate([model.bf16(pre + "gate"), model.bf16(pre + "up")]), qtype, cfg.hidden,
+                            device)
+            wd = _quantize(model.bf16(pre + "down"), qtype, cfg.ffn, device)
+            self._keep += [wqkv, wo, wgu, wd]
+            check(L.pyxis_cuda_model_set_layer(self.handle, layer, wqkv.handle, wo.handle, wgu.handle, wd.handle,
+                                               p(ones), p(ones), p(hn), p(hn)))
+        emb = model.bf16("embed")
+        lm = _quantize(emb, qtype, cfg.hidden, device)
+        self._keep.append(lm)
+        check(L.pyxis_cuda_model_set_head(self.handle, emb.ctypes.data_as(C.POINTER(C.c_uint16)), lm.handle, p(ones)))
+
+    def generate(self, prompt, n_new: int):
+        """Returns (tokens [n_new], (prompt_ms, decode_ms)) -- device time of the two phases."""
+        pr = np.ascontiguousarray(np.asarray(prompt, np.int32))
+        out = np.empty(n_new, np.int32)
+        t = (C.c_float * 2)()
+        check(_native.lib().pyxis_cuda_model_generate(self.handle, pr.ctypes.data_as(C.c_void_p), pr.size, n_new,
+                                                      out.ctypes.data_as(C.c_void_p), t))
+        return out, (t[0], t[1])
+
+    def close(self):
+        if self.handle:
+            _native.lib().pyxis_cuda_model_free(self.handle)
+            self.handle = None
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
