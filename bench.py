@@ -430,8 +430,9 @@ def profile_case(args):
         dec = Decoder(SyntheticModel(QWEN3_1_7B, SEED), qtype="int8", max_seq=64)
         prompt = synth_tokens(0x9E0, 2, QWEN3_1_7B.vocab)
         dec.generate(prompt, 2)
-        toks, t = dec.generate(prompt, 3)
-        print(f"profile case decode: tokens {list(toks)}, prompt {t[0]:.2f} ms, decode {t[1]:.2f} ms")
+        n = max(2, args.steps + 1)
+        toks, t = dec.generate(prompt, n)
+        print(f"profile case decode: {n - 1} steps, prompt {t[0]:.2f} ms, decode {t[1] / (n - 1):.3f} ms/token")
         return
     name, B = args.profile_case.split(":") if ":" in args.profile_case else (args.profile_case, "1")
     B = int(B)

@@ -54,6 +54,7 @@ struct DeviceGuard {
 size_t div_ceil(size_t a, size_t b) { return (a + b - 1) / b; }
 
 constexpr size_t kTcMinRows = 16;        // matmul_dev rows from which the tensor-core GEMM runs
+constexpr size_t kTcGemvMinRows = 32768;  // out_features from which batch-1 int8 GEMVs use tensor cores
 
 size_t packed_bytes(int qtype, size_t n) { return qtype == PYXIS_QTYPE_INT8 ? n : div_ceil(n, 2); }
 
@@ -148,7 +149,12 @@ int pyxis::run_matmul(pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, const fl
         size_t b = M - m0 < 8 ? M - m0 : 8;
         const float *xb = X + m0 * ldx;
         cudaError_t e;
-        if (gemv_tc_supported(q, b, ctx->num_sms) && (reinterpret_cast<uintptr_t>(xb) & 15) == 0 &&
+        // Tensor cores for big matrices (the lm_head); below kTcGemvMinRows a GEMV is latency-bound
+        // and the CUDA-core ring kernel's shorter critical path wins (no digit build, no shared
+        // tiles).  Batches of 2-8 rows always take the tensor cores: the CUDA cores would need B
+        // FMAs per code.
+        const bool tc_ok = b > 1 || out_features >= kTcGemvMinRows || !gemv_ring_supported(q, ctx->num_sms);
+        if (tc_ok && gemv_tc_supported(q, b, ctx->num_sms) && (reinterpret_cast<uintptr_t>(xb) & 15) == 0 &&
             (b == 1 || ldx % 4 == 0))
             e = launch_gemv_tc(q, xb, b, ldx, Y + m0 * ldy, ldy, ctx->tcg_scratch, ctx->tcg_scratch_bytes, ctx->d_err,
                                ctx->num_sms, st);

@@ -86,6 +86,10 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(
     }
 }
 
+void set_argmax_carveout_max() {
+    cudaFuncSetAttribute(argmax_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+}
+
 int argmax_ctas_per_row(size_t n, int num_sms) {
     size_t c = (n + 4095) / 4096;
     if (c > (size_t)kArgmaxMaxCtasPerRow) c = kArgmaxMaxCtasPerRow;

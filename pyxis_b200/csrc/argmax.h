@@ -24,6 +24,9 @@ inline size_t argmax_scratch_bytes(size_t rows) {
 
 int argmax_ctas_per_row(size_t n, int num_sms);
 
+// Prefer the maximum shared-memory carveout (as the GEMV kernels it runs between do).
+void set_argmax_carveout_max();
+
 cudaError_t launch_argmax_scratch(const float *values, size_t M, size_t n, size_t ld,
                                   int64_t index_base, int32_t *idx, float *val,
                                   const ArgmaxScratch &s, int num_sms, cudaStream_t st);

@@ -21,7 +21,7 @@
 namespace pyxis {
 namespace {
 
-constexpr int kNormThreads = 256;
+constexpr int kNormThreads = 1024;
 
 PYXIS_DEVINL float block_sum(float v, float *red) {
     v = warp_sum(v);
@@ -57,23 +57,42 @@ __global__ void embed_kernel(const uint16_t *__restrict__ emb, const int *__rest
 }
 
 // Optional residual add (x += delta, src/transformer.rs:40-42, :54-59), then
-// h = x * (factor * w), factor = 1 / sqrt(mean(x^2) + eps) (src/rmsnorm.rs:11-20).  One CTA.
+// h = x * (factor * w), factor = 1 / sqrt(mean(x^2) + eps) (src/rmsnorm.rs:11-20).  One CTA of
+// kNormThreads; each thread keeps its kNormPer values in registers, so x, delta and w are read in
+// one pass (n <= kNormThreads * kNormPer).
+constexpr int kNormPer = 8;
 __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float *__restrict__ x, const float *__restrict__ delta,
                                                                   const float *__restrict__ w, float *__restrict__ h,
                                                                   int n, float eps) {
     __shared__ float red[kNormThreads / 32];
+    float v[kNormPer], wv[kNormPer];
     float ss = 0.f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        float v = x[i];
-        if (delta) {
-            v = __fadd_rn(v, delta[i]);
-            x[i] = v;
+#pragma unroll
+    for (int j = 0; j < kNormPer; ++j) {
+        const int i = threadIdx.x + j * kNormThreads;
+        v[j] = 0.f;
+        wv[j] = 0.f;
+        if (i < n) {
+            v[j] = x[i];
+            if (delta) v[j] = __fadd_rn(v[j], delta[i]);
+            wv[j] = w[i];
         }
-        ss = __fadd_rn(ss, __fmul_rn(v, v));
+    }
+#pragma unroll
+    for (int j = 0; j < kNormPer; ++j) {
+        const int i = threadIdx.x + j * kNormThreads;
+        if (i < n) {
+            if (delta) x[i] = v[j];
+            ss = __fadd_rn(ss, __fmul_rn(v[j], v[j]));
+        }
     }
     ss = block_sum(ss, red);
     const float factor = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
-    for (int i = threadIdx.x; i < n; i += blockDim.x) h[i] = __fmul_rn(x[i], __fmul_rn(factor, w[i]));
+#pragma unroll
+    for (int j = 0; j < kNormPer; ++j) {
+        const int i = threadIdx.x + j * kNormThreads;
+        if (i < n) h[i] = __fmul_rn(v[j], __fmul_rn(factor, wv[j]));
+    }
 }
 
 // Per head: QK RMSNorm (src/attention.rs:81-90), RoPE at `pos` from the host-made table
@@ -293,6 +312,7 @@ extern "C" int pyxis_cuda_model_create(pyxis_cuda_ctx *ctx, const pyxis_model_co
     if (c.hidden <= 0 || c.n_layers <= 0 || c.n_q_heads <= 0 || c.n_kv_heads <= 0 || c.head_dim <= 0 || c.ffn <= 0 ||
         c.vocab <= 0 || c.max_seq <= 0 || c.head_dim % 2 || c.head_dim > 1024 || c.n_q_heads % c.n_kv_heads)
         return model_fail(PYXIS_EINVAL, "pyxis_cuda_model_create: bad config");
+    if (c.hidden > 1024 * 8) return model_fail(PYXIS_EINVAL, "pyxis_cuda_model_create: hidden > 8192");
     if ((size_t)c.max_seq * 4 + 256 > 160 * 1024)
         return model_fail(PYXIS_EINVAL, "pyxis_cuda_model_create: max_seq too large for the decode attention kernel");
     Guard g(ctx->device);
@@ -415,6 +435,13 @@ extern "C" int pyxis_cuda_model_generate(pyxis_cuda_model *m, const int32_t *pro
     cudaStream_t st = m->ctx->stream;
     cudaError_t e = cudaSuccess;
     if (!m->exec) {
+        // Every kernel of the step asks for the same (maximum) shared-memory carveout as the
+        // GEMV kernels, so the SMs never re-split L1 / shared memory between graph nodes.
+        const void *small_kernels[] = {(const void *)embed_kernel, (const void *)add_rmsnorm_kernel,
+                                       (const void *)qk_rope_append_kernel, (const void *)attention_decode_kernel,
+                                       (const void *)silu_mul_kernel, (const void *)advance_kernel};
+        for (const void *k : small_kernels) cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        set_argmax_carveout_max();
         // Warm every kernel once outside capture (first-use attribute setting and occupancy
         // queries), then capture the step.
         int zero = 0;

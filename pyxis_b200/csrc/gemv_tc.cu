@@ -392,7 +392,10 @@ cudaError_t launch_gemv_tc(const QMatrix &w, const float *X, size_t B, size_t ld
     if ((reinterpret_cast<uintptr_t>(X) & 15) || (B > 1 && ldx % 4)) return cudaErrorInvalidValue;
     const int num_tiles = (int)((w.N + TM - 1) / TM);
     const long long total = (long long)num_tiles * (long long)(w.K / TKB);
-    const int grid = (int)std::max<long long>(1, std::min<long long>(num_sms, total));
+    // Every CTA pays a fixed start-up (TMEM, barriers, the digit operand) and shared tiles pay
+    // atomics: give each CTA at least kMinStagesPerCta stages unless that leaves SMs idle.
+    constexpr long long kMinStagesPerCta = 4;
+    const int grid = (int)std::max<long long>(1, std::min<long long>(num_sms, (total + kMinStagesPerCta - 1) / kMinStagesPerCta));
     if (!scratch || scratch_bytes < gemv_tc_scratch_bytes(grid)) return cudaErrorInvalidValue;
     auto fn = encode_fn();
     if (!fn) return cudaErrorNotSupported;
