@@ -51,6 +51,8 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(
     int32_t *__restrict__ idx_out, float *__restrict__ val_out, ArgmaxScratch s) {
     __shared__ uint64_t red[kArgmaxThreads / 32];
     __shared__ bool last;
+    pdl_wait();
+    pdl_trigger();
     const size_t row = blockIdx.y;
     const float *v = values + row * ld;
     const size_t seg = (n + gridDim.x - 1) / gridDim.x;
@@ -102,8 +104,8 @@ cudaError_t launch_argmax_scratch(const float *values, size_t M, size_t n, size_
                                   const ArgmaxScratch &s, int num_sms, cudaStream_t st) {
     if (M == 0) return cudaSuccess;
     dim3 grid(argmax_ctas_per_row(n, num_sms), (unsigned)M);
-    argmax_kernel<<<grid, kArgmaxThreads, 0, st>>>(values, n, ld, index_base, idx, val, s);
-    return cudaGetLastError();
+    return launch_kernel(argmax_kernel, grid, dim3(kArgmaxThreads), 0, st, values, n, ld, index_base, idx, val, s);
 }
 
 }  // namespace pyxis
+

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #define PYXIS_DEVINL __device__ __forceinline__
 
 namespace pyxis {
@@ -72,5 +74,38 @@ PYXIS_DEVINL float warp_sum(float v) {
 }
 
 PYXIS_DEVINL float bf16_bits_to_f32(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
+
+// ---- programmatic dependent launch ---------------------------------------------------------
+// A kernel launched with programmatic stream serialization may start while its predecessor is
+// still running; pdl_wait() blocks until the predecessor has completed and its writes are
+// visible.  pdl_trigger() lets this kernel's own dependents start launching.  Both are no-ops
+// for a kernel launched normally.
+PYXIS_DEVINL void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+PYXIS_DEVINL void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Host side: launches issued while a PdlScope is alive on this thread (the decode step's capture)
+// carry the programmatic-serialization attribute.
+bool pdl_enabled();
+struct PdlScope {
+    bool prev;
+    PdlScope();
+    ~PdlScope();
+};
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                          Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 }  // namespace pyxis

@@ -49,6 +49,8 @@ PYXIS_DEVINL float block_max(float v, float *red) {
 // x = widen(embedding[token]) (Embedding::lookup, src/embedding.rs:18-24 over bf16 -> f32).
 __global__ void embed_kernel(const uint16_t *__restrict__ emb, const int *__restrict__ token, int vocab, int H,
                              float *__restrict__ x) {
+    pdl_wait();
+    pdl_trigger();
     int t = *token;
     t = t < 0 ? 0 : (t >= vocab ? vocab - 1 : t);
     const uint16_t *row = emb + (size_t)t * H;
@@ -65,6 +67,8 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float *__rest
                                                                   const float *__restrict__ w, float *__restrict__ h,
                                                                   int n, float eps) {
     __shared__ float red[kNormThreads / 32];
+    pdl_wait();
+    pdl_trigger();
     float v[kNormPer], wv[kNormPer];
     float ss = 0.f;
 #pragma unroll
@@ -105,6 +109,8 @@ __global__ void qk_rope_append_kernel(const float *__restrict__ qkv, const float
                                       float *__restrict__ vcache) {
     extern __shared__ float sh[];  // [hd] head values, [32] reduction
     float *hv = sh, *red = sh + hd;
+    pdl_wait();
+    pdl_trigger();
     const int pos = *d_pos;
     const int kv_dim = n_kv * hd, q_dim = n_q * hd;
     const int b = blockIdx.x, d = threadIdx.x;
@@ -139,6 +145,8 @@ __global__ void attention_decode_kernel(const float *__restrict__ q, const float
                                         const float *__restrict__ vcache, const int *__restrict__ d_pos, int n_q,
                                         int n_kv, int hd, float *__restrict__ out) {
     extern __shared__ float sc[];  // [pos + 1] scores, then [32] reduction
+    pdl_wait();
+    pdl_trigger();
     const int pos = *d_pos;
     const int len = pos + 1;
     float *red = sc + len;
@@ -178,6 +186,8 @@ __global__ void attention_decode_kernel(const float *__restrict__ q, const float
 
 // act = silu(gate) * up, silu(x) = x / (1 + exp(-x)) (src/ffn.rs:39-41, :52-54).
 __global__ void silu_mul_kernel(const float *__restrict__ gu, int ffn, float *__restrict__ act) {
+    pdl_wait();
+    pdl_trigger();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ffn; i += gridDim.x * blockDim.x) {
         const float g = gu[i];
         act[i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), gu[ffn + i]);
@@ -186,6 +196,8 @@ __global__ void silu_mul_kernel(const float *__restrict__ gu, int ffn, float *__
 
 // Records the argmax token of this step and advances the position / step counters.
 __global__ void advance_kernel(const int *__restrict__ token, int *__restrict__ out, int *pos, int *step) {
+    pdl_wait();
+    pdl_trigger();
     const int s = *step;
     out[s] = *token;
     *step = s + 1;
@@ -248,8 +260,13 @@ struct Guard {
 int enqueue_step(pyxis_cuda_model *m, cudaStream_t st) {
     const pyxis_model_config &c = m->cfg;
     const int H = c.hidden;
-    embed_kernel<<<(H + 255) / 256, 256, 0, st>>>(m->emb, m->d_token, c.vocab, H, m->x);
-    add_rmsnorm_kernel<<<1, kNormThreads, 0, st>>>(m->x, nullptr, m->layers[0].in_norm, m->h, H, c.rms_eps);
+    PdlScope pdl;  // kernels of the step may start while their predecessor finishes
+    cudaError_t le = launch_kernel(embed_kernel, dim3((H + 255) / 256), dim3(256), 0, st, (const uint16_t *)m->emb,
+                                   (const int *)m->d_token, c.vocab, H, m->x);
+    if (le == cudaSuccess)
+        le = launch_kernel(add_rmsnorm_kernel, dim3(1), dim3(kNormThreads), 0, st, m->x, (const float *)nullptr,
+                           (const float *)m->layers[0].in_norm, m->h, H, c.rms_eps);
+    if (le != cudaSuccess) return model_fail(PYXIS_ECUDA, cudaGetErrorString(le));
     for (int l = 0; l < c.n_layers; ++l) {
         const auto &L = m->layers[l];
         float *kc = m->kcache + (size_t)l * c.max_seq * m->kv_dim;
@@ -257,29 +274,38 @@ int enqueue_step(pyxis_cuda_model *m, cudaStream_t st) {
         int rc = run_matmul(m->ctx, L.wqkv, m->h, 1, H, (size_t)m->q_dim + 2 * m->kv_dim, H, m->qkv,
                             (size_t)m->q_dim + 2 * m->kv_dim, nullptr, 0, st);
         if (rc) return rc;
-        qk_rope_append_kernel<<<c.n_q_heads + c.n_kv_heads + 1, c.head_dim, (c.head_dim + 32) * sizeof(float), st>>>(
-            m->qkv, L.q_norm, L.k_norm, m->rope_cos, m->rope_sin, m->d_pos, c.n_q_heads, c.n_kv_heads, c.head_dim,
-            c.rms_eps, m->q, kc, vc);
-        attention_decode_kernel<<<c.n_q_heads, 128, (c.max_seq + 32) * sizeof(float), st>>>(
-            m->q, kc, vc, m->d_pos, c.n_q_heads, c.n_kv_heads, c.head_dim, m->attn);
+        le = launch_kernel(qk_rope_append_kernel, dim3(c.n_q_heads + c.n_kv_heads + 1), dim3(c.head_dim),
+                           (c.head_dim + 32) * sizeof(float), st, (const float *)m->qkv, (const float *)L.q_norm,
+                           (const float *)L.k_norm, (const float *)m->rope_cos, (const float *)m->rope_sin,
+                           (const int *)m->d_pos, c.n_q_heads, c.n_kv_heads, c.head_dim, c.rms_eps, m->q, kc, vc);
+        if (le == cudaSuccess)
+            le = launch_kernel(attention_decode_kernel, dim3(c.n_q_heads), dim3(128), (c.max_seq + 32) * sizeof(float),
+                               st, (const float *)m->q, (const float *)kc, (const float *)vc, (const int *)m->d_pos,
+                               c.n_q_heads, c.n_kv_heads, c.head_dim, m->attn);
+        if (le != cudaSuccess) return model_fail(PYXIS_ECUDA, cudaGetErrorString(le));
         rc = run_matmul(m->ctx, L.wo, m->attn, 1, m->q_dim, H, m->q_dim, m->tmp, H, nullptr, 0, st);
         if (rc) return rc;
-        add_rmsnorm_kernel<<<1, kNormThreads, 0, st>>>(m->x, m->tmp, L.post_norm, m->h, H, c.rms_eps);
+        le = launch_kernel(add_rmsnorm_kernel, dim3(1), dim3(kNormThreads), 0, st, m->x, (const float *)m->tmp,
+                           (const float *)L.post_norm, m->h, H, c.rms_eps);
+        if (le != cudaSuccess) return model_fail(PYXIS_ECUDA, cudaGetErrorString(le));
         rc = run_matmul(m->ctx, L.wgu, m->h, 1, H, 2 * (size_t)c.ffn, H, m->gu, 2 * (size_t)c.ffn, nullptr, 0, st);
         if (rc) return rc;
-        silu_mul_kernel<<<(c.ffn + 255) / 256, 256, 0, st>>>(m->gu, c.ffn, m->act);
+        le = launch_kernel(silu_mul_kernel, dim3((c.ffn + 255) / 256), dim3(256), 0, st, (const float *)m->gu, c.ffn,
+                           m->act);
+        if (le != cudaSuccess) return model_fail(PYXIS_ECUDA, cudaGetErrorString(le));
         rc = run_matmul(m->ctx, L.wdown, m->act, 1, c.ffn, H, c.ffn, m->tmp, H, nullptr, 0, st);
         if (rc) return rc;
         const float *next_norm = l + 1 < c.n_layers ? m->layers[l + 1].in_norm : m->final_norm;
-        add_rmsnorm_kernel<<<1, kNormThreads, 0, st>>>(m->x, m->tmp, next_norm, m->h, H, c.rms_eps);
+        le = launch_kernel(add_rmsnorm_kernel, dim3(1), dim3(kNormThreads), 0, st, m->x, (const float *)m->tmp,
+                           next_norm, m->h, H, c.rms_eps);
+        if (le != cudaSuccess) return model_fail(PYXIS_ECUDA, cudaGetErrorString(le));
     }
     int rc = run_matmul(m->ctx, m->lm_head, m->h, 1, H, c.vocab, H, m->logits, c.vocab, nullptr, 0, st);
     if (rc) return rc;
     cudaError_t e = launch_argmax_scratch(m->logits, 1, c.vocab, c.vocab, 0, m->d_token, nullptr, m->ctx->amax,
                                           m->ctx->num_sms, st);
     if (e != cudaSuccess) return model_fail(PYXIS_ECUDA, cudaGetErrorString(e));
-    advance_kernel<<<1, 1, 0, st>>>(m->d_token, m->d_out, m->d_pos, m->d_step);
-    e = cudaGetLastError();
+    e = launch_kernel(advance_kernel, dim3(1), dim3(1), 0, st, (const int *)m->d_token, m->d_out, m->d_pos, m->d_step);
     if (e != cudaSuccess) return model_fail(PYXIS_ECUDA, cudaGetErrorString(e));
     return PYXIS_OK;
 }

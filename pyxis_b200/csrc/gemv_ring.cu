@@ -149,6 +149,8 @@ __global__ void __maxnreg__(152) gemv_ring_kernel(const RingParams p) {
         const int team = warp / Wt, wt = warp - team * Wt;
         const int t = wt * 32 + lane;
         const int cstride = 32 * Wt;
+        pdl_wait();  // x comes from the previous kernel; the producer's weight copies do not wait
+        pdl_trigger();
         float2 xr[CPL][EPC / 2];
 #pragma unroll
         for (int j = 0; j < CPL; ++j) {
@@ -283,8 +285,7 @@ static cudaError_t run_ring(const RingParams &p, int grid, cudaStream_t st) {
     static const bool attr =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kRingSmem) == cudaSuccess;
     if (!attr) return cudaErrorInvalidConfiguration;
-    kern<<<grid, kRingThreads, kRingSmem, st>>>(p);
-    return cudaGetLastError();
+    return launch_kernel(kern, dim3(grid), dim3(kRingThreads), kRingSmem, st, p);
 }
 
 template <int QT, int SMODE>

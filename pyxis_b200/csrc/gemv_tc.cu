@@ -163,6 +163,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // -------------------------------------------------------------------- digit operand
         const int bt = threadIdx.x - 32, nbt = kThreads - 32;  // warps 1-5
         const int bwarp = warp - 1;
+        pdl_wait();  // x comes from the previous kernel; the producer's weight copies do not wait
+        pdl_trigger();
         const Sched sc{p.total_stages, (int)gridDim.x, p.num_kb};
         const long long my_sb = sc.begin(blockIdx.x), my_se = sc.begin(blockIdx.x + 1);
         // K-blocks this CTA multiplies: a contiguous run (mod num_kb) unless it spans a whole tile
@@ -432,8 +434,7 @@ cudaError_t launch_gemv_tc(const QMatrix &w, const float *X, size_t B, size_t ld
     static const bool attr =
         cudaFuncSetAttribute(gemv_tc_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTotal) == cudaSuccess;
     if (!attr) return cudaErrorInvalidConfiguration;
-    gemv_tc_i8_kernel<<<grid, kThreads, kSmemTotal, st>>>(tm, p);
-    return cudaGetLastError();
+    return launch_kernel(gemv_tc_i8_kernel, dim3(grid), dim3(kThreads), kSmemTotal, st, tm, p);
 }
 
 }  // namespace pyxis
