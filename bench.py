@@ -229,6 +229,82 @@ def reference_arm(args, ws, rank):
     print(json.dumps(line), flush=True)
 
 
+PREFILL_SHAPES = [  # name, qtype, N, K, block: X [512, K] x W [N, K]^T on the tensor cores
+    ("gate_proj int8", "int8", 6144, 2048, 2048), ("gate_proj int4", "int4", 6144, 2048, 32),
+    ("down_proj int8", "int8", 2048, 6144, 6144), ("down_proj int4", "int4", 2048, 6144, 32)]
+PREFILL_M = 512
+
+
+def run_vocab_parallel_head(ws, rank, local, steps):
+    """Greedy next token through the lm_head split by vocabulary rows over the ranks: each rank's
+    int8 GEMV over V/ws rows + device argmax + NCCL all-gather of one (value, index) per rank.
+    Device time per token (max over ranks); every rank ends with the same token."""
+    import numpy as np
+    import torch
+
+    from pyxis_b200.dist import VocabParallelHead
+
+    V, H = 151936, 2048
+    bits = px_synth_bits(0x11EAD, V * H)
+    head = VocabParallelHead(bits, V, H, "int8", rank, ws, local)
+    del bits
+    h = torch.from_numpy(px_synth_f32(9, H)).cuda().view(1, H)
+    for _ in range(3):
+        head.greedy(h)
+    torch.cuda.synchronize()
+    barrier(ws)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        tok = head.greedy(h)
+    torch.cuda.synchronize()
+    us = max_over_ranks((time.perf_counter() - t0) / steps * 1e6, ws)
+    return {"n_gpus": ws, "rows_per_gpu": (V + ws - 1) // ws, "us_per_token": us, "token": int(tok[0]),
+            "note": "wall clock per greedy token incl. the all-gather and host pick (synchronous API)"}
+
+
+def px_synth_bits(seed, n):
+    import pyxis_b200 as px
+    return px.synth_normal_bf16(seed, n, 0.02)
+
+
+def px_synth_f32(seed, n):
+    import pyxis_b200 as px
+    return px.synth_normal_f32(seed, n, 1.0)
+
+
+def run_prefill(local, reps=20):
+    """Prefill GEMMs (X f32 [512, K] N(0,1) x quantised W): TFLOP/s counting 2*M*N*K only."""
+    import numpy as np
+    import torch
+
+    import pyxis_b200 as px
+
+    dev = torch.device("cuda", local)
+    out = []
+    for i, (name, qt, N, K, bs) in enumerate(PREFILL_SHAPES):
+        bits = px.synth_normal_bf16(SEED + 50 + i, N * K, 0.02)
+        t = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).to(dev)
+        w = px.Weights.quantize_int8(t, bs, device=local) if qt == "int8" else px.Weights.quantize_int4(t, bs, device=local)
+        X = torch.from_numpy(px.synth_normal_f32(SEED + 60 + i, PREFILL_M * K, 1.0)).to(dev).view(PREFILL_M, K)
+        Y = torch.empty((PREFILL_M, N), dtype=torch.float32, device=dev)
+        need = px._native.lib().pyxis_cuda_matmul_workspace_size(PREFILL_M, K)
+        ws = torch.empty(need, dtype=torch.uint8, device=dev)
+        for _ in range(3):
+            px.matmul_dev(X, w, N, K, Y=Y, workspace=ws)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            px.matmul_dev(X, w, N, K, Y=Y, workspace=ws)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        flops = 2.0 * PREFILL_M * N * K
+        out.append({"shape": f"{name}: X[{PREFILL_M},{K}] x W[{N},{K}]", "us": us, "tflops": flops / us / 1e6})
+        del w, X, Y, ws, t
+    return out
+
+
 DECODE_WORKLOAD = ("Qwen3-1.7B-shape decode, random init, int8 one scale per row: hidden 2048, 28 layers, "
                    "16/8 heads x 128, FFN 6144, vocab 151936, tied lm_head; 16 prompt ids + 128 greedy tokens, batch 1")
 DECODE_PROMPT, DECODE_NEW = 16, 128
@@ -377,6 +453,20 @@ def pyxis_arm(args, ws, rank, local):
     e2e_s = max_over_ranks(time.perf_counter() - t0, ws)
     e2e_value = ws * sb * args.steps / e2e_s / 1e9
 
+    lm_vp = None
+    if ws > 1:
+        lm_vp = run_vocab_parallel_head(ws, rank, local, args.steps)
+    prefill = run_prefill(local)
+    peak_tf = 0.0
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        peak_tf = float(pk.get("bf16_tflops", 0.0))
+    except (OSError, ValueError):
+        peak_tf = 1590.0
+    for r in prefill:
+        r["frac_of_bf16_peak"] = r["tflops"] / peak_tf if peak_tf else None
+
     decode = None
     if not args.no_decode:
         del weights, X, Y
@@ -412,6 +502,9 @@ def pyxis_arm(args, ws, rank, local):
                 "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
                 "cpu_baseline": cpu, "clocks": clk, "gpu_launches": launches_per_step * args.steps,
                 "decode": decode,
+                "lm_head_vocab_parallel": lm_vp,
+                "prefill": {"M": PREFILL_M, "kernel": "split_x_kernel + gemm_tc_kernel (tcgen05 kind::f16, fp16 hi/lo)",
+                            "peak_tflops": peak_tf, "peak_kind": "measured bf16 burst", "shapes": prefill},
                 "per_gpu_value": value / ws}
         print(json.dumps(line), flush=True)
 

@@ -133,7 +133,9 @@ int pyxis_cuda_check_device_error(pyxis_cuda_ctx *ctx);
 
 /* Row-wise argmax (src/output_head.rs:30-44: first index of the maximum under strict >) of
  * M rows of n f32 on the device: idx[M] int32 and val[M] f32 (val may be NULL).  `index_base`
- * is added to every index (a vocab shard's first row).  Asynchronous on `stream`. */
+ * is added to every index (a vocab shard's first row); with index_base > 0 the row is a shard
+ * that does not hold index 0, so a NaN at its start is skipped like any other NaN (the reference's
+ * "values[0] NaN wins" rule belongs to the shard with index_base 0).  Asynchronous on `stream`. */
 int pyxis_cuda_argmax_dev(pyxis_cuda_ctx *ctx, const float *values, size_t M, size_t n,
                           size_t ld, int64_t index_base, int32_t *idx, float *val, void *stream);
 

@@ -3,7 +3,8 @@
 // The reference scans left to right and replaces the running maximum only on a strict `>`:
 //   - ties go to the lowest index;
 //   - a NaN is never `>` anything, so NaNs are skipped -- unless values[0] is NaN, in which case
-//     nothing ever beats it and the answer is 0;
+//     nothing ever beats it and the answer is 0 (for a shard of a longer vector, index_base > 0,
+//     that rule belongs to the shard holding index 0, so the shard skips a leading NaN);
 //   - +0.0 > -0.0 is false, so the two zeros tie (lowest index wins).
 // Here every element becomes a 64-bit key (order-preserving float bits << 32 | ~index), the
 // maximum key is the reference's answer, and max is associative, so CTAs reduce their segments
@@ -81,7 +82,9 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(
     m = cta_max_u64(m, red);
     if (threadIdx.x == 0) {
         uint32_t i = 0xFFFFFFFFu - (uint32_t)(m & 0xFFFFFFFFu);
-        if (isnan(v[0]) || m == 0) i = 0;  // values[0] NaN wins; all-NaN row -> 0 as well
+        // values[0] NaN wins -- when this row starts the vector (index_base 0); a vocab shard
+        // that starts later ignores NaNs like every other position.  All-NaN -> first index.
+        if ((index_base == 0 && isnan(v[0])) || m == 0) i = 0;
         idx_out[row] = (int32_t)(index_base + (int64_t)i);
         if (val_out) val_out[row] = v[i];
         s.ticket[row] = 0;  // re-arm for the next launch on this scratch
