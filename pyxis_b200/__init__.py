@@ -121,6 +121,9 @@ class Weights:
         except ImportError:  # pragma: no cover
             is_torch = False
         if is_torch and values.is_cuda:
+            if (values.device.index or 0) != device:
+                raise PyxisError(_native.PYXIS_EINVAL,
+                                 f"source tensor on {values.device}, weights requested on cuda:{device}")
             t = values.contiguous()
             if t.dtype == torch.float32:
                 dt = DTYPE_F32
@@ -244,6 +247,8 @@ def matmul_dev(X, weight: Weights, out_features: int, in_features: int, Y=None, 
 
     if X.dim() == 1:
         X = X.unsqueeze(0)
+    if (X.device.index or 0) != weight.ctx.device or (Y is not None and (Y.device.index or 0) != weight.ctx.device):
+        raise PyxisError(_native.PYXIS_EINVAL, f"X/Y must be on cuda:{weight.ctx.device}, the weights' device")
     M = X.shape[0]
     if Y is None:
         Y = torch.empty((M, out_features), dtype=torch.float32, device=X.device)

@@ -253,6 +253,15 @@ int pyxis_cuda_quantize(pyxis_cuda_ctx *ctx, const void *src, int src_dtype, int
     if (src_dtype != PYXIS_DTYPE_F32 && src_dtype != PYXIS_DTYPE_BF16) return fail(PYXIS_EINVAL, "unknown src dtype %d", src_dtype);
     if (!src && n) return fail(PYXIS_EINVAL, "null source");
     DeviceGuard g(ctx->device);
+    if (src_on_device && n) {  // a device source must live on this context's device
+        cudaPointerAttributes pa;
+        cudaError_t pe = cudaPointerGetAttributes(&pa, src);
+        if (pe != cudaSuccess || (pa.type != cudaMemoryTypeDevice && pa.type != cudaMemoryTypeManaged) ||
+            (pa.type == cudaMemoryTypeDevice && pa.device != ctx->device)) {
+            cudaGetLastError();
+            return fail(PYXIS_EINVAL, "quantize: the device source is not memory of device %d", ctx->device);
+        }
+    }
     pyxis_cuda_weights *w = nullptr;
     int rc = alloc_weights(ctx, qtype, n, block_size, &w);
     if (rc) return rc;

@@ -24,7 +24,8 @@ def main():
         bits = px.synth_normal_bf16(N + K, N * K, 0.02)
         sh = RowShardedMatmul(bits, N, K, qt, rank, world, local)
         t = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).cuda()
-        full = px.Weights.quantize_int8(t, bs) if qt == "int8" else px.Weights.quantize_int4(t, bs)
+        full = (px.Weights.quantize_int8(t, bs, device=local) if qt == "int8"
+                else px.Weights.quantize_int4(t, bs, device=local))
         X = torch.from_numpy(px.synth_normal_f32(7, K, 1.0)).cuda().view(1, K)
         y_sh = sh.forward_gathered(X)
         y_full = px.matmul_dev(X, full, N, K)
@@ -36,7 +37,7 @@ def main():
     bits = px.synth_normal_bf16(0x11EAD, V * H, 0.02)
     head = VocabParallelHead(bits, V, H, "int8", rank, world, local)
     t = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).cuda()
-    full = px.Weights.quantize_int8(t, H)
+    full = px.Weights.quantize_int8(t, H, device=local)
     h = torch.from_numpy(px.synth_normal_f32(9, 4 * H, 1.0)).cuda().view(4, H)
     got = head.greedy(h)
     logits = px.matmul_dev(h, full, V, H)

@@ -109,3 +109,16 @@ def test_upload_download_round_trip():
     w = px.Weights.from_packed("int4", data, scales, 32, 1998)
     d, s = w.download()
     assert np.array_equal(d, data) and np.array_equal(s, scales)
+
+
+def test_device_source_must_be_this_devices_memory():
+    """A host pointer flagged as a device source is refused on the host, before any launch."""
+    import ctypes as C
+    from pyxis_b200 import _native
+    ctx = px.get_cuda(0)
+    v = np.ones(1024, np.float32)
+    h = C.c_void_p()
+    rc = _native.lib().pyxis_cuda_quantize(ctx.handle, v.ctypes.data_as(C.c_void_p), _native.DTYPE_F32, 1, v.size,
+                                           32, _native.QTYPE_INT8, C.byref(h))
+    assert rc == _native.PYXIS_EINVAL
+    assert b"device" in _native.lib().pyxis_cuda_last_error()
