@@ -416,6 +416,27 @@ def pyxis_arm(args, ws, rank, local):
 
     sb = step_bytes()
     value = ws * sb * args.steps / (ms_max / 1e3) / 1e9
+
+    # per-launch device time of every case, in sweep order (cold L2 as in the timed steps), from an
+    # untimed pass with events between the launches
+    case_ev = {}
+    for _ in range(min(args.steps, 10)):
+        for B in BATCHES:
+            for (name, qt, N, K, bs, w) in weights:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                px.matmul_dev(X[B][:, :K], w, N, K, Y=Y[B][:, :N], stream=stream)
+                e1.record(stream)
+                case_ev.setdefault((name, B), []).append((e0, e1))
+    torch.cuda.synchronize()
+    cases = []
+    for B in BATCHES:
+        for (name, qt, N, K, bs, w) in weights:
+            us = statistics.median(a.elapsed_time(b) for a, b in case_ev[(name, B)]) * 1e3
+            by = gemv_bytes(qt, N, K, bs, B)
+            cases.append({"case": f"{name} {qt} {N}x{K} B={B}", "kernel": px.matmul_kernel_name(w, B, N, K),
+                          "us": round(us, 2), "gbs": round(by / us / 1e3, 1)})
     lm_ms = statistics.mean(a.elapsed_time(b) for a, b in lm_ev)
     lm_bytes = gemv_bytes("int8", 151936, 2048, 2048, 1)
     peak, peak_kind = measured_peak_hbm()
@@ -501,6 +522,7 @@ def pyxis_arm(args, ws, rank, local):
                 "frac_of_peak_step": value / ws / peak,
                 "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
                 "cpu_baseline": cpu, "clocks": clk, "gpu_launches": launches_per_step * args.steps,
+                "cases": cases,
                 "decode": decode,
                 "lm_head_vocab_parallel": lm_vp,
                 "prefill": {"M": PREFILL_M, "kernel": "split_x_kernel + gemm_tc_kernel (tcgen05 kind::f16, fp16 hi/lo)",

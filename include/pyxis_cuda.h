@@ -131,6 +131,12 @@ size_t pyxis_cuda_matmul_workspace_size(size_t M, size_t in_features);
  * flag.  Kernels never spin without a limit: a stuck pipeline ends the launch instead. */
 int pyxis_cuda_check_device_error(pyxis_cuda_ctx *ctx);
 
+/* Diagnostics, no counterpart in the reference: the name of the kernel pyxis_cuda_matmul_dev
+ * launches for M rows of a contiguous, 16-byte aligned x (for M > 8 on the GEMV path, the kernel
+ * of each 8-row chunk).  "" for invalid arguments. */
+const char *pyxis_cuda_matmul_kernel(pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, size_t M,
+                                     size_t out_features, size_t in_features);
+
 /* Row-wise argmax (src/output_head.rs:30-44: first index of the maximum under strict >) of
  * M rows of n f32 on the device: idx[M] int32 and val[M] f32 (val may be NULL).  `index_base`
  * is added to every index (a vocab shard's first row); with index_base > 0 the row is a shard

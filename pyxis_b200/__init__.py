@@ -260,6 +260,12 @@ def matmul_dev(X, weight: Weights, out_features: int, in_features: int, Y=None, 
     return Y
 
 
+def matmul_kernel_name(weight: Weights, M: int, out_features: int, in_features: int) -> str:
+    """The kernel ``matmul_dev`` launches for M contiguous rows of x (diagnostics)."""
+    return _native.lib().pyxis_cuda_matmul_kernel(weight.ctx.handle, weight.handle, M, out_features,
+                                                   in_features).decode()
+
+
 def argmax_dev(values, index_base: int = 0, idx=None, val=None, stream=None, device: int = 0):
     """Row-wise argmax of a torch CUDA tensor [M, n] (src/output_head.rs:30-44 per row)."""
     import torch

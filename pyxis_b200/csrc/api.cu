@@ -121,11 +121,26 @@ int check_matmul(const pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, size_t 
 
 int pyxis::record_error(int code, const char *msg) { return fail(code, "%s", msg); }
 
+namespace {
+bool use_gemm_tc(const QMatrix &q, size_t M, const float *X, size_t ldx) {
+    return M >= kTcMinRows && gemm_tc_supported(q) && (reinterpret_cast<uintptr_t>(X) & 15) == 0 && ldx % 4 == 0;
+}
+
+// Tensor cores for big matrices (the lm_head); below kTcGemvMinRows a GEMV is latency-bound and
+// the CUDA-core ring kernel's shorter critical path wins (no digit build, no shared tiles).
+// Batches of 2-8 int8 rows always take the tensor cores (int4 has no tensor-core GEMV).
+bool use_gemv_tc(const pyxis_cuda_ctx *ctx, const QMatrix &q, size_t b, const float *xb, size_t ldx) {
+    const bool tc_ok = b > 1 || q.N >= kTcGemvMinRows || !gemv_ring_supported(q, ctx->num_sms);
+    return tc_ok && gemv_tc_supported(q, b, ctx->num_sms) && (reinterpret_cast<uintptr_t>(xb) & 15) == 0 &&
+           (b == 1 || ldx % 4 == 0);
+}
+}  // namespace
+
 int pyxis::run_matmul(pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, const float *X, size_t M, size_t ldx,
                       size_t out_features, size_t in_features, float *Y, size_t ldy, void *workspace,
                       size_t workspace_bytes, cudaStream_t st) {
     QMatrix q = qmatrix(w, out_features, in_features);
-    if (M >= kTcMinRows && gemm_tc_supported(q) && (reinterpret_cast<uintptr_t>(X) & 15) == 0 && ldx % 4 == 0) {
+    if (use_gemm_tc(q, M, X, ldx)) {
         const size_t need = gemm_tc_workspace_bytes(M, in_features);
         if (!workspace) {
             if (ctx->ws_cap < need) {
@@ -149,13 +164,7 @@ int pyxis::run_matmul(pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, const fl
         size_t b = M - m0 < 8 ? M - m0 : 8;
         const float *xb = X + m0 * ldx;
         cudaError_t e;
-        // Tensor cores for big matrices (the lm_head); below kTcGemvMinRows a GEMV is latency-bound
-        // and the CUDA-core ring kernel's shorter critical path wins (no digit build, no shared
-        // tiles).  Batches of 2-8 rows always take the tensor cores: the CUDA cores would need B
-        // FMAs per code.
-        const bool tc_ok = b > 1 || out_features >= kTcGemvMinRows || !gemv_ring_supported(q, ctx->num_sms);
-        if (tc_ok && gemv_tc_supported(q, b, ctx->num_sms) && (reinterpret_cast<uintptr_t>(xb) & 15) == 0 &&
-            (b == 1 || ldx % 4 == 0))
+        if (use_gemv_tc(ctx, q, b, xb, ldx))
             e = launch_gemv_tc(q, xb, b, ldx, Y + m0 * ldy, ldy, ctx->tcg_scratch, ctx->tcg_scratch_bytes, ctx->d_err,
                                ctx->num_sms, st);
         else
@@ -372,6 +381,18 @@ int pyxis_cuda_matmul_dev(pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, cons
     DeviceGuard g(ctx->device);
     return run_matmul(ctx, w, X, M, ldx, out_features, in_features, Y, ldy, workspace, workspace_bytes,
                       pick_stream(ctx, stream));
+}
+
+const char *pyxis_cuda_matmul_kernel(pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, size_t M,
+                                     size_t out_features, size_t in_features) {
+    if (!ctx || !w || check_matmul(ctx, w, out_features, in_features) || M == 0) return "";
+    QMatrix q = qmatrix(w, out_features, in_features);
+    // 256-byte aligned, contiguous x: the layout the device-pointer form's callers pass
+    const float *x = reinterpret_cast<const float *>(static_cast<uintptr_t>(256));
+    if (use_gemm_tc(q, M, x, in_features)) return "gemm_tc_kernel";
+    const size_t b = M < 8 ? M : 8;
+    if (use_gemv_tc(ctx, q, b, x, in_features)) return "gemv_tc_i8_kernel";
+    return gemv_kernel_name(q, b, ctx->num_sms);
 }
 
 int pyxis_cuda_matmul_batch(pyxis_cuda_ctx *ctx, const float *input, size_t M, const pyxis_cuda_weights *w,

@@ -29,6 +29,7 @@
 
 #include "kernels.h"
 #include "tc_ptx.cuh"
+#include "tmap.cuh"
 
 namespace pyxis {
 namespace {
@@ -361,18 +362,7 @@ __global__ void __launch_bounds__(256) split_x_kernel(const float *__restrict__ 
     }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
-        void *ptr = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) !=
-                cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            return (PFN_cuTensorMapEncodeTiled_v12000) nullptr;
-        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-    }();
-    return fn;
-}
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() { return tensor_map_encoder(); }
 
 bool make_map_2d(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t outer,
                  uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {

@@ -8,8 +8,7 @@
 //          16-byte chunks t, t+T, ... of every row it visits, so its slice of x stays in
 //          registers for the whole kernel and x costs no shared-memory or L1 traffic.  Each team
 //          loads R rows' chunks before using any (R * CPT 128-bit loads in flight per thread).
-//   smem   B = 2..8.  x [B, K] staged once per CTA in shared memory; a warp walks R rows at a
-//          time, lane l taking chunks l, l+32, ...; every x read is reused for R rows.
+//   batch  B = 2..8 (and B = 1 shapes the team kernel does not take): gemv_batch.cu.
 //   generic  any shape the two above do not take (K not a multiple of the chunk, blocks that
 //          straddle rows, odd K with int4 rows that start mid-byte): one warp per row,
 //          element-wise decode with the reference's scales[g / block_size] lookup.
@@ -158,71 +157,6 @@ __global__ void __launch_bounds__(512) gemv_team_kernel(GemvParams p) {
     }
 }
 
-// ---------------------------------------------------------------- smem kernel (B = 1..8) -----
-constexpr int kSmemCta = 256;
-
-template <int QT, int B, int R, int SMODE>
-__global__ void __launch_bounds__(kSmemCta) gemv_smem_kernel(GemvParams p) {
-    constexpr int EPC = QT_<QT>::EPC;
-    extern __shared__ float4 xs4[];  // [B][K] floats
-    float *xs = reinterpret_cast<float *>(xs4);
-    const int K = p.K;
-    for (int b = 0; b < B; ++b) {
-        const float4 *src = reinterpret_cast<const float4 *>(p.X + (size_t)b * p.ldx);
-        for (int i = threadIdx.x; i < K / 4; i += blockDim.x) xs4[(size_t)b * (K / 4) + i] = __ldg(src + i);
-    }
-    __syncthreads();
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int warps = blockDim.x >> 5;
-    for (int row0 = (blockIdx.x * warps + warp) * R; row0 < p.N; row0 += gridDim.x * warps * R) {
-        float acc[R][B];
-#pragma unroll
-        for (int r = 0; r < R; ++r)
-#pragma unroll
-            for (int b = 0; b < B; ++b) acc[r][b] = 0.f;
-        for (int c = lane; c < p.chunks; c += 32) {
-            uint4 wv[R];
-            float sv[R];
-#pragma unroll
-            for (int r = 0; r < R; ++r) {
-                const int row = min(row0 + r, p.N - 1);
-                wv[r] = ld_stream_v4(p.W + (size_t)row * p.row_bytes + (size_t)c * 16);
-                if (SMODE == kScaleChunk)
-                    sv[r] = ld_nc_f32(p.S + (size_t)row * p.blocks_per_row + c / p.chunks_per_block);
-            }
-#pragma unroll
-            for (int b = 0; b < B; ++b) {
-                float2 xv[EPC / 2];
-                const float4 *xp = reinterpret_cast<const float4 *>(xs + (size_t)b * K + (size_t)c * EPC);
-#pragma unroll
-                for (int v = 0; v < EPC / 4; ++v) {
-                    float4 f = xp[v];
-                    xv[2 * v] = f2(f.x, f.y);
-                    xv[2 * v + 1] = f2(f.z, f.w);
-                }
-#pragma unroll
-                for (int r = 0; r < R; ++r) {
-                    float d = chunk_dot<QT>(wv[r], xv);
-                    if (SMODE == kScaleChunk) acc[r][b] = fmaf(sv[r], d, acc[r][b]);
-                    else acc[r][b] += d;
-                }
-            }
-        }
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-            const int row = row0 + r;
-            float sc = 1.f;
-            if (SMODE == kScaleRow && row < p.N) sc = ld_nc_f32(p.S + row);
-#pragma unroll
-            for (int b = 0; b < B; ++b) {
-                float s = warp_sum(acc[r][b]);
-                if (lane == 0 && row < p.N) p.Y[(size_t)b * p.ldy + row] = SMODE == kScaleRow ? s * sc : s;
-            }
-        }
-    }
-}
-
 // ---------------------------------------------------------------- generic kernel --------------
 template <int QT>
 __global__ void gemv_generic_kernel(const uint8_t *W, const float *S, size_t bs, const float *X,
@@ -253,7 +187,7 @@ __global__ void gemv_generic_kernel(const uint8_t *W, const float *S, size_t bs,
 namespace {
 
 struct Plan {
-    enum Kind { kTeam, kSmem, kGeneric } kind;
+    enum Kind { kTeam, kGeneric } kind;
     int smode;
     int cpt, r;  // team kernel
     int team;
@@ -284,10 +218,6 @@ Plan make_plan(const QMatrix &w, size_t B, size_t ldx) {
             pl.r = cpt >= 3 ? 1 : (cpt == 2 ? 2 : 4);
             return pl;
         }
-    }
-    if (B * K * sizeof(float) <= 200 * 1024) {
-        pl.kind = Plan::kSmem;
-        return pl;
     }
     pl.kind = Plan::kGeneric;
     return pl;
@@ -327,44 +257,14 @@ cudaError_t dispatch_team(const Plan &pl, const GemvParams &p, int num_sms, cuda
     return run_team<QT, 1, 4, SMODE>(p, num_sms, st);
 }
 
-template <int QT, int B, int SMODE>
-cudaError_t run_smem(const GemvParams &p, int num_sms, cudaStream_t st) {
-    constexpr int R = 2;
-    const size_t smem = (size_t)B * p.K * sizeof(float);
-    auto kern = gemv_smem_kernel<QT, B, R, SMODE>;
-    static const bool attr = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                  200 * 1024) == cudaSuccess;
-    (void)attr;
-    const int occ = max_ctas_per_sm(kern, kSmemCta, smem);
-    const long rows_per_cta = (long)(kSmemCta / 32) * R;
-    long grid = (p.N + rows_per_cta - 1) / rows_per_cta;
-    grid = std::min<long>(grid, (long)occ * num_sms);
-    kern<<<(unsigned)std::max<long>(grid, 1), kSmemCta, smem, st>>>(p);
-    return cudaGetLastError();
-}
-
-template <int QT, int SMODE>
-cudaError_t dispatch_smem(size_t B, const GemvParams &p, int num_sms, cudaStream_t st) {
-    switch (B) {
-    case 1: return run_smem<QT, 1, SMODE>(p, num_sms, st);
-    case 2: return run_smem<QT, 2, SMODE>(p, num_sms, st);
-    case 3: return run_smem<QT, 3, SMODE>(p, num_sms, st);
-    case 4: return run_smem<QT, 4, SMODE>(p, num_sms, st);
-    case 5: return run_smem<QT, 5, SMODE>(p, num_sms, st);
-    case 6: return run_smem<QT, 6, SMODE>(p, num_sms, st);
-    case 7: return run_smem<QT, 7, SMODE>(p, num_sms, st);
-    default: return run_smem<QT, 8, SMODE>(p, num_sms, st);
-    }
-}
-
 }  // namespace
 
 const char *gemv_kernel_name(const QMatrix &w, size_t B, int num_sms) {
     if (B == 1 && gemv_ring_supported(w, num_sms)) return "gemv_ring_kernel";
     Plan pl = make_plan(w, B, 4);
+    if (pl.kind != Plan::kTeam && gemv_batch_supported(w, B, num_sms)) return "gemv_batch_kernel";
     switch (pl.kind) {
     case Plan::kTeam: return "gemv_team_kernel";
-    case Plan::kSmem: return "gemv_smem_kernel";
     default: return "gemv_generic_kernel";
     }
 }
@@ -377,6 +277,9 @@ cudaError_t launch_gemv(const QMatrix &w, const float *X, size_t B, size_t ldx, 
     if ((reinterpret_cast<uintptr_t>(X) & 15) != 0) ldx = 1;  // unaligned x: force generic
     Plan pl = make_plan(w, B, ldx);
     if ((reinterpret_cast<uintptr_t>(X) & 15) != 0) pl.kind = Plan::kGeneric;
+    if (pl.kind != Plan::kTeam && (reinterpret_cast<uintptr_t>(X) & 15) == 0 && (B == 1 || ldx % 4 == 0) &&
+        gemv_batch_supported(w, B, num_sms))
+        return launch_gemv_batch(w, X, B, ldx, Y, ldy, err, num_sms, st);
     if (pl.kind != Plan::kGeneric) {
         const int epc = w.qtype == kQInt8 ? 16 : 32;
         GemvParams p{};
@@ -400,11 +303,6 @@ cudaError_t launch_gemv(const QMatrix &w, const float *X, size_t B, size_t ldx, 
             return pl.smode == kScaleRow ? dispatch_team<kQInt4, kScaleRow>(pl, p, num_sms, st)
                                          : dispatch_team<kQInt4, kScaleChunk>(pl, p, num_sms, st);
         }
-        if (w.qtype == kQInt8)
-            return pl.smode == kScaleRow ? dispatch_smem<kQInt8, kScaleRow>(B, p, num_sms, st)
-                                         : dispatch_smem<kQInt8, kScaleChunk>(B, p, num_sms, st);
-        return pl.smode == kScaleRow ? dispatch_smem<kQInt4, kScaleRow>(B, p, num_sms, st)
-                                     : dispatch_smem<kQInt4, kScaleChunk>(B, p, num_sms, st);
     }
     const size_t threads = w.N * 32;
     const unsigned grid = (unsigned)((threads + 255) / 256);

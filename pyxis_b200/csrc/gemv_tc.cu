@@ -29,6 +29,7 @@
 
 #include "kernels.h"
 #include "tc_ptx.cuh"
+#include "tmap.cuh"
 
 namespace pyxis {
 namespace {
@@ -345,18 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
-        void *ptr = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) !=
-                cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            return (PFN_cuTensorMapEncodeTiled_v12000) nullptr;
-        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-    }();
-    return fn;
-}
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() { return tensor_map_encoder(); }
 
 struct Plan {
     bool ok = false;

@@ -31,6 +31,13 @@ cudaError_t launch_gemv(const QMatrix &w, const float *X, size_t B, size_t ldx, 
 bool gemv_ring_supported(const QMatrix &w, int num_sms);
 cudaError_t launch_gemv_ring(const QMatrix &w, const float *x, float *y, int *err, int num_sms, cudaStream_t st);
 
+// 1-8 input rows on the CUDA cores with x staged by TMA and split-K over warps (gemv_batch.cu):
+// K % 32 == 0, one scale per row or per block of whole 16-byte chunks, B * K * 4 bytes of x in
+// shared memory.
+bool gemv_batch_supported(const QMatrix &w, size_t B, int num_sms);
+cudaError_t launch_gemv_batch(const QMatrix &w, const float *X, size_t B, size_t ldx, float *Y, size_t ldy,
+                              int *err, int num_sms, cudaStream_t st);
+
 // Name of the kernel launch_gemv would pick (for tests and the bench's launch accounting).
 const char *gemv_kernel_name(const QMatrix &w, size_t B, int num_sms);
 

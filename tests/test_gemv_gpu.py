@@ -133,3 +133,28 @@ def test_int8_row_scale_tensor_core_gemv(N, K, B):
         ref = ref_matmul("int8", od, os_, K, X, N, K)
         check_matmul(Y, ref, exact_matmul("int8", od, os_, K, N, K, X))
     px._native.check(px._native.lib().pyxis_cuda_check_device_error(w.ctx.handle))
+
+
+@pytest.mark.parametrize("qt,N,K,bs,B", [
+    ("int4", 2048, 2048, 32, 2), ("int4", 2048, 2048, 32, 5), ("int4", 2048, 6144, 32, 7),
+    ("int4", 64, 12288, 32, 2),    # two TMA boxes per token
+    ("int4", 10, 9600, 32, 2),     # 300 rows of x: boxes of 152 rows, the last one overhangs
+    ("int4", 100, 416, 32, 3),     # 13 rows of x in a 16-row box
+    ("int4", 40000, 2048, 32, 4),  # many row-group items per CTA (double-buffered combine)
+    ("int4", 1779, 2048, 64, 6),   # N % 4 != 0, 64-value groups (2 chunks per scale)
+    ("int8", 6144, 2048, 32, 8),   # GGUF Q8_0 layout at batch 8
+    ("int8", 515, 4096, 128, 3),
+    ("int4", 300, 4096, 4096, 8),  # int4 with one scale per row
+])
+def test_batch_kernel(qt, N, K, bs, B):
+    """The CUDA-core batch kernel (x staged by TMA, split-K over warps, fixed-order combine)."""
+    w, od, os_ = make(qt, N, K, bs, seed=N + 3 * K + bs + B)
+    assert px.matmul_kernel_name(w, B, N, K) == "gemv_batch_kernel"
+    X = px.synth_normal_f32(B * 13 + 1, B * K, 1.0).reshape(B, K)
+    X[B - 1, :4] = [0.0, -0.0, 1e-30, -3e4]
+    ref = ref_matmul(qt, od, os_, bs, X, N, K)
+    Y1 = px.matmul_batch(X, w, N, K)
+    check_matmul(Y1, ref, exact_matmul(qt, od, os_, bs, N, K, X))
+    Y2 = px.matmul_batch(X, w, N, K)
+    assert np.array_equal(Y1, Y2)  # the combine order is fixed: bit-identical reruns
+    px._native.check(px._native.lib().pyxis_cuda_check_device_error(w.ctx.handle))
