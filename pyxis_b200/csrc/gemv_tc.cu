@@ -15,13 +15,17 @@
 // in int64 / double and rounds once to f32.  The only error is x's 27-bit representation.
 //
 // CTA (persistent, one per SM): warp 0 = TMA producer into an S-stage ring (16 KB stages),
-// warp 1 = TMEM owner + MMA issuer (M=128, N=16|32, K=32 per instruction, accumulator
-// double-buffered in TMEM across tile segments), warps 2-5 = epilogue (tcgen05.ld, one TMEM
-// lane = one weight row).  Warps 1-5 build the digit operand while the producer's first copies
-// are in flight.  A tile whose stages span several CTAs has its partial int32 sums added exactly
-// with atomics into a scratch slot, and the CTA that finishes the tile last
+// warp 1 = TMEM owner + MMA issuer (M=128, N=16|32, K=32 per instruction, 8 accumulators per
+// tile segment so that consecutive stages do not wait on each other, double-buffered in TMEM
+// across segments), warps 2-5 = epilogue (tcgen05.ld, one TMEM lane = one weight row).
+// x itself arrives by one bulk copy into the last ring stages, issued before the first weight
+// copy (or, under programmatic dependent launch, right after the predecessor finishes), so it
+// does not queue behind the weight stream; warps 1-5 turn it into the digit operand and hand the
+// stages back to the producer.  A tile whose stages span several CTAs has its partial int32
+// sums added exactly with atomics into a scratch slot, and the CTA that finishes the tile last
 // converts it and zeroes the scratch for the next launch.  The schedule is stream-K: every CTA
-// gets the same number of (tile, K-block) stages.  Every wait is bounded.
+// gets the same number of (tile, K-block) stages, and works on its (possibly shared) first and
+// last tiles before the whole tiles between them.  Every wait is bounded.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -42,15 +46,24 @@ constexpr uint32_t kStageBytes = TM * TKB;
 constexpr uint32_t kSmemTotal = 222 * 1024;
 constexpr int kMaxStages = 12;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
-// The 4 MMAs of a stage (one per 32-byte K slice) write 4 separate accumulators, so they do not
-// wait on each other; the epilogue adds them (exact int32).  2 buffers x 4 x NB(<= 32) columns.
-constexpr int kAccPerBuf = TKB / 32;
-constexpr uint32_t kTmemCols = 256;
+// The 4 MMAs of a stage (one per 32-byte K slice) write 4 separate accumulators, and the even and
+// odd stages of a tile use two different sets of 4: an MMA depends only on the one issued 8 MMAs
+// (two stages) earlier, so consecutive stages do not serialise on the MMA latency.  The epilogue
+// adds them (exact int32).  TMEM: 2 buffers x 8 accumulators x NB columns (256 or 512).
+constexpr int kAccPerStage = TKB / 32;
+constexpr int kAccSets = 2;
+constexpr int kAccPerBuf = kAccPerStage * kAccSets;
+// x -> digits: t + kDigitBias has the base-128 digits d_i + 64 (all in [0, 128]), so the balanced
+// digits come out of shifts and masks; kDigitBias = 64 * (2^21 + 2^14 + 2^7 + 1).
+constexpr int kDigitBias = 135274560;
 enum { kErrProd = 0x301, kErrMma = 0x302, kErrEpi = 0x303, kErrDrain = 0x304 };
 
 struct Params {
     int N, K, B, NB;
     int num_kb, num_tiles, stages;
+    uint32_t tmem_cols;
+    int x_stages;  // ring stages that hold x [B][K] f32 until the digits are built
+    int pdl;       // launched with programmatic stream serialization
     long long total_stages;  // num_tiles * num_kb, split evenly over the grid (stream-K)
     uint32_t xd_bytes;
     const float *x;
@@ -58,7 +71,7 @@ struct Params {
     const float *scales;
     float *y;
     long long ldy;
-    int *accum;         // [grid][128][NB] int32 partial tiles, zero between launches
+    int *accum;         // [grid][NB][128] int32 partial tiles, zero between launches
     unsigned *tickets;  // [grid], zero between launches
     int *err;
 };
@@ -85,6 +98,12 @@ PYXIS_DEVINL void tmem_ld16(uint32_t taddr, int (&v)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// 2^e as a float for -126 <= e <= 127 (exact)
+PYXIS_DEVINL float pow2f(int e) { return __int_as_float((e + 127) << 23); }
+
+// max that keeps a NaN once seen (fmaxf drops it): a NaN in x must reach every output
+PYXIS_DEVINL float max_nan(float m, float a) { return (a > m || a != a) ? a : m; }
+
 PYXIS_DEVINL void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
 PYXIS_DEVINL float combine(const int *D, double xs, double sr) {
@@ -95,11 +114,24 @@ PYXIS_DEVINL float combine(const int *D, double xs, double sr) {
 // Stream-K schedule: the num_tiles x num_kb stages are cut into gridDim.x equal contiguous
 // ranges; a tile whose stages span several CTAs is combined exactly (int32 atomics) in the slot
 // of the first CTA that touches it -- each CTA is the first of at most one shared tile.
+// A CTA works through its range as tile segments in this order: the first tile's, the last
+// tile's (the two that may be shared with the neighbouring CTAs, so that their fix-ups happen
+// while the stream is still running), then the whole tiles between them.
 struct Sched {
     long long T;
     int G, nkb;
     PYXIS_DEVINL long long begin(int c) const { return (long long)c * T / G; }
     PYXIS_DEVINL int owner(long long s) const { return (int)(((s + 1) * G + T - 1) / T - 1); }
+    PYXIS_DEVINL int num_segments(long long b, long long e) const {
+        return (int)((e - 1) / nkb - b / nkb) + 1;
+    }
+    // stages [s0, s1) of segment i of the range [b, e)
+    PYXIS_DEVINL void segment(long long b, long long e, int i, long long &s0, long long &s1) const {
+        const long long ft = b / nkb, lt = (e - 1) / nkb;
+        const long long tile = i == 0 ? ft : (i == 1 ? lt : ft + i - 1);
+        s0 = b > tile * nkb ? b : tile * nkb;
+        s1 = e < (tile + 1) * nkb ? e : (tile + 1) * nkb;
+    }
 };
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -111,7 +143,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *bars = reinterpret_cast<uint64_t *>(ring + (size_t)p.stages * kStageBytes);
     uint64_t *full = bars, *empty = bars + kMaxStages;
     uint64_t *tfull = bars + 2 * kMaxStages, *tempty = tfull + 2, *drain = tempty + 2;
-    double *xscale = reinterpret_cast<double *>(drain + 1);          // [kMaxTok]
+    uint64_t *xfull = drain + 1, *xfree = drain + 2;
+    double *xscale = reinterpret_cast<double *>(drain + 3);          // [kMaxTok]
     float *red = reinterpret_cast<float *>(xscale + kMaxTok);        // [kMaxTok][5]
     int *xexp = reinterpret_cast<int *>(red + kMaxTok * 5);          // [kMaxTok]
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(xexp + kMaxTok);
@@ -129,33 +162,74 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc::mbar_init(&tempty[b], 4);
         }
         tc::mbar_init(drain, 1);
+        tc::mbar_init(xfull, 1);
+        tc::mbar_init(xfree, 1);
         *abort_flag = 0;
         tc::fence_mbar_init();
     }
-    if (warp == 1) tc::tmem_alloc(tmem_slot, kTmemCols);
+    if (warp == 1) tc::tmem_alloc(tmem_slot, p.tmem_cols);
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // x [B][K] f32 borrows the last x_stages ring stages until the digit operand is built
+    const int x_gate = p.stages - p.x_stages;
+    const float *xs = reinterpret_cast<const float *>(ring + (size_t)x_gate * kStageBytes);
 
     if (warp == 0) {
         // -------------------------------------------------------------------- TMA producer
         if (lane == 0) {
             tc::prefetch_tmap(&tm_w);
+            // x first, ahead of the weight stream in the memory queues -- unless it comes from a
+            // kernel still running (PDL): then the weights go first and x after griddepcontrol.wait
+            bool x_issued = false;
+            auto issue_x = [&]() {
+                const uint32_t row = (uint32_t)p.K * 4u;
+                tc::mbar_arrive_expect_tx(xfull, row * (uint32_t)p.B);
+                uint8_t *dst = const_cast<uint8_t *>(reinterpret_cast<const uint8_t *>(xs));
+                if (p.ldx == p.K) tc::bulk_load(dst, p.x, row * (uint32_t)p.B, xfull);
+                else
+                    for (int b = 0; b < p.B; ++b) tc::bulk_load(dst + (size_t)b * row, p.x + (size_t)b * p.ldx, row, xfull);
+                x_issued = true;
+            };
+            if (!p.pdl) issue_x();
             int g = 0;
             const Sched sc{p.total_stages, (int)gridDim.x, p.num_kb};
-            const long long se = sc.begin(blockIdx.x + 1);
-            for (long long st = sc.begin(blockIdx.x); st < se; ++st, ++g) {
-                const int s = g % p.stages;
-                if (g >= p.stages &&
-                    !tc::mbar_wait_bounded(&empty[s], ((g / p.stages) - 1) & 1, abort_flag, p.err, kErrProd, kTimeoutNs))
-                    break;
-                const int tile = (int)(st / p.num_kb), kb = (int)(st % p.num_kb);
-                tc::mbar_arrive_expect_tx(&full[s], kStageBytes);
-                tc::tma_load_2d(ring + (size_t)s * kStageBytes, &tm_w, kb * TKB, tile * TM, &full[s]);
+            const long long sb = sc.begin(blockIdx.x), se = sc.begin(blockIdx.x + 1);
+            const int nseg = sc.num_segments(sb, se);
+            bool ok = true;
+            for (int i = 0; i < nseg && ok; ++i) {
+                long long s0, s1;
+                sc.segment(sb, se, i, s0, s1);
+                for (long long st = s0; st < s1; ++st, ++g) {
+                    const int s = g % p.stages;
+                    if (g == x_gate) {  // the stages x borrowed: wait until the digits are built
+                        if (!x_issued) {
+                            pdl_wait();
+                            issue_x();
+                        }
+                        if (!tc::mbar_wait_bounded(xfree, 0, abort_flag, p.err, kErrProd, kTimeoutNs)) {
+                            ok = false;
+                            break;
+                        }
+                    }
+                    if (g >= p.stages && !tc::mbar_wait_bounded(&empty[s], ((g / p.stages) - 1) & 1, abort_flag, p.err,
+                                                                kErrProd, kTimeoutNs)) {
+                        ok = false;
+                        break;
+                    }
+                    const int tile = (int)(st / p.num_kb), kb = (int)(st % p.num_kb);
+                    tc::mbar_arrive_expect_tx(&full[s], kStageBytes);
+                    tc::tma_load_2d(ring + (size_t)s * kStageBytes, &tm_w, kb * TKB, tile * TM, &full[s]);
+                }
+            }
+            if (!x_issued && ok) {  // fewer stages than the x_gate: x still has to come
+                pdl_wait();
+                issue_x();
             }
             if (*abort_flag) {  // let the copies already issued land
                 volatile int no_abort = 0;
+                if (x_issued) tc::mbar_wait_bounded(xfull, 0, &no_abort, p.err, kErrDrain, 100000000ull);
                 for (int j = g > p.stages ? g - p.stages : 0; j < g; ++j)
                     tc::mbar_wait_bounded(&full[j % p.stages], (j / p.stages) & 1, &no_abort, p.err, kErrDrain, 100000000ull);
             }
@@ -164,70 +238,112 @@ __global__ void __launch_bounds__(kThreads, 1)
         // -------------------------------------------------------------------- digit operand
         const int bt = threadIdx.x - 32, nbt = kThreads - 32;  // warps 1-5
         const int bwarp = warp - 1;
-        pdl_wait();  // x comes from the previous kernel; the producer's weight copies do not wait
-        pdl_trigger();
+        pdl_trigger();  // x reaches shared memory through the producer, after its griddepcontrol.wait
         const Sched sc{p.total_stages, (int)gridDim.x, p.num_kb};
         const long long my_sb = sc.begin(blockIdx.x), my_se = sc.begin(blockIdx.x + 1);
         // K-blocks this CTA multiplies: a contiguous run (mod num_kb) unless it spans a whole tile
         const int need_lo = (int)(my_sb % p.num_kb);
         const long long need_n = my_se - my_sb;
         auto needed = [&](int kb) { return need_n >= p.num_kb || ((kb - need_lo + p.num_kb) % p.num_kb) < need_n; };
-        for (int b = 0; b < p.B; ++b) {
-            const float *xb = p.x + (size_t)b * p.ldx;
-            float m = 0.f;
-            for (int k = bt; k < p.K; k += nbt) m = fmaxf(m, fabsf(xb[k]));
+        const int kq = p.K / 4;  // float4 quads per token
+        const float4 *xs4 = reinterpret_cast<const float4 *>(xs);
+        const bool x_ok = tc::mbar_wait_bounded(xfull, 0, abort_flag, p.err, kErrMma, kTimeoutNs);
+        // x arrived after the producer's griddepcontrol.wait, so this returns at once; it keeps the
+        // epilogue's writes (y, the shared scratch) formally ordered after the previous kernel
+        pdl_wait();
+        if (x_ok) {
+            // max |x| of every token in one pass
+            float m[kMaxTok];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            if (lane == 0) red[b * 5 + bwarp] = m;
-        }
-        {
-            const uint4 z = make_uint4(0, 0, 0, 0);
-            const uint32_t per_kb = (uint32_t)p.NB * TKB / 16;
-            for (uint32_t i = bt; i < p.xd_bytes / 16; i += nbt)
-                if (needed((int)(i / per_kb))) reinterpret_cast<uint4 *>(xd)[i] = z;
+            for (int b = 0; b < kMaxTok; ++b) m[b] = 0.f;
+#pragma unroll 2
+            for (int k4 = bt; k4 < kq; k4 += nbt) {
+                float4 v[kMaxTok];
+#pragma unroll
+                for (int b = 0; b < kMaxTok; ++b)
+                    if (b < p.B) v[b] = xs4[(size_t)b * kq + k4];
+#pragma unroll
+                for (int b = 0; b < kMaxTok; ++b)
+                    if (b < p.B)
+                        m[b] = max_nan(max_nan(max_nan(max_nan(m[b], fabsf(v[b].x)), fabsf(v[b].y)), fabsf(v[b].z)),
+                                       fabsf(v[b].w));
+            }
+#pragma unroll
+            for (int b = 0; b < kMaxTok; ++b) {
+                if (b < p.B) {  // uniform: every lane takes the same branches
+                    float mb = m[b];
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) mb = max_nan(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+                    if (lane == 0) red[b * 5 + bwarp] = mb;
+                }
+            }
         }
         named_bar(1, nbt);
         if (bt < p.B) {
             float m = red[bt * 5];
-            for (int w = 1; w < 5; ++w) m = fmaxf(m, red[bt * 5 + w]);
+            for (int w = 1; w < 5; ++w) m = max_nan(m, red[bt * 5 + w]);
             int E = 0;
             if (m > 0.f && isfinite(m)) frexpf(m, &E);  // m < 2^E
             xexp[bt] = E;
             xscale[bt] = isfinite(m) ? ldexp(1.0, E - 27) : __longlong_as_double(0x7ff8000000000000ll);
         }
-        named_bar(1, nbt);
-        const int kq = p.K / 4;
-        for (int idx = bt; idx < p.B * kq; idx += nbt) {
-            const int b = idx / kq, k = (idx - b * kq) * 4;
-            if (!needed(k / TKB)) continue;
-            const int E = xexp[b];
-            const float4 xv = *reinterpret_cast<const float4 *>(p.x + (size_t)b * p.ldx + k);
-            const float xs4[4] = {xv.x, xv.y, xv.z, xv.w};
-            uint32_t word[4] = {0, 0, 0, 0};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float v = ldexpf(xs4[e], 27 - E);
-                int t = isfinite(v) ? (int)rintf(v) : 0;
-                int dg[4];
-#pragma unroll
-                for (int i = 3; i >= 1; --i) {
-                    dg[i] = ((t + 64) & 127) - 64;
-                    t = (t - dg[i]) >> 7;
-                }
-                dg[0] = t;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) word[i] |= ((uint32_t)(dg[i] & 0xff)) << (8 * e);
-            }
-            const int kb = k / TKB, kk = k % TKB, c = kk >> 4;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int r = 4 * b + i;
+        {
+            // operand rows 4B..NB-1 (no token) are zero
+            const uint4 z = make_uint4(0, 0, 0, 0);
+            const int pad_rows = p.NB - 4 * p.B;
+            const int per_kb = pad_rows * (TKB / 16);
+            for (int i = bt; i < p.num_kb * per_kb; i += nbt) {
+                const int kb = i / per_kb, j = i - kb * per_kb, r = 4 * p.B + j / (TKB / 16);
+                if (!needed(kb)) continue;
                 uint8_t *row = xd + (size_t)kb * (p.NB * TKB) + (r >> 3) * 1024 + (r & 7) * 128;
-                *reinterpret_cast<uint32_t *>(row + ((c ^ (r & 7)) << 4) + (kk & 15)) = word[i];
+                reinterpret_cast<uint4 *>(row)[j % (TKB / 16)] = z;  // all-zero row: no swizzle needed
             }
         }
-        tc::fence_proxy_async_smem();
         named_bar(1, nbt);
+        // digits: t = rint(x 2^(27-E)) as 4 balanced base-128 digits, 8 quads per thread per round
+        const int total = x_ok ? p.B * kq : 0;
+        for (int base = bt; base < total; base += 8 * nbt) {
+            float4 xv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int idx = base + u * nbt;
+                if (idx < total) xv[u] = xs4[idx];
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int idx = base + u * nbt;
+                if (idx >= total) break;
+                const int b = idx / kq, k = (idx - b * kq) * 4;
+                if (!needed(k / TKB)) continue;
+                // x 2^(27-E) exactly, as two power-of-two products (27 - E lies in [-101, 175])
+                const int sh = 27 - xexp[b];
+                const int sa = sh < 127 ? sh : 127;
+                const float f1 = pow2f(sa), f2 = pow2f(sh - sa);
+                const float xs4[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
+                uint32_t word[4] = {0, 0, 0, 0};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float v = (xs4[e] * f1) * f2;
+                    const int t = isfinite(v) ? __float2int_rn(v) : 0;
+                    const uint32_t ub = (uint32_t)(t + kDigitBias);
+                    word[0] |= (ub >> 21) << (8 * e);
+                    word[1] |= ((ub >> 14) & 127u) << (8 * e);
+                    word[2] |= ((ub >> 7) & 127u) << (8 * e);
+                    word[3] |= (ub & 127u) << (8 * e);
+                }
+                const int kb = k / TKB, kk = k % TKB, c = kk >> 4;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int r = 4 * b + i;
+                    uint8_t *row = xd + (size_t)kb * (p.NB * TKB) + (r >> 3) * 1024 + (r & 7) * 128;
+                    *reinterpret_cast<uint32_t *>(row + ((c ^ (r & 7)) << 4) + (kk & 15)) =
+                        __vsub4(word[i], 0x40404040u);  // digit + 64 -> digit, per byte
+                }
+            }
+        }
+        tc::fence_proxy_async_smem();  // digit writes -> MMA reads; x reads -> the producer's reuse
+        named_bar(1, nbt);
+        if (bt == 0) tc::mbar_arrive(xfree);  // the stages that held x go back to the weights
 
         if (warp == 1) {
             // ---------------------------------------------------------------- MMA issuer
@@ -235,11 +351,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t idesc = idesc_i8(TM, p.NB);
                 int g = 0, li = 0;
                 bool ok = true;
-                for (long long st = my_sb; st < my_se && ok; ++li) {
-                    const int tile = (int)(st / p.num_kb);
-                    const long long tend = my_se < (long long)(tile + 1) * p.num_kb ? my_se : (long long)(tile + 1) * p.num_kb;
-                    const int kb0 = (int)(st % p.num_kb), nk = (int)(tend - st);
-                    st = tend;
+                const int nseg = sc.num_segments(my_sb, my_se);
+                for (; li < nseg && ok; ++li) {
+                    long long s0, s1;
+                    sc.segment(my_sb, my_se, li, s0, s1);
+                    const int kb0 = (int)(s0 % p.num_kb), nk = (int)(s1 - s0);
                     const int buf = li & 1;
                     if (li >= 2) {
                         ok = tc::mbar_wait_bounded(&tempty[buf], ((li >> 1) - 1) & 1, abort_flag, p.err, kErrMma, kTimeoutNs);
@@ -254,10 +370,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tc::tc_fence_after();
                         const uint64_t a0 = tc::desc_sw128(tc::smem_u32(ring + (size_t)s * kStageBytes));
                         const uint64_t b0 = tc::desc_sw128(tc::smem_u32(xd + (size_t)kb * (p.NB * TKB)));
+                        const uint32_t dset = d + (uint32_t)(((kb - kb0) & 1) * kAccPerStage * p.NB);
 #pragma unroll
-                        for (int q = 0; q < TKB / 32; ++q)
-                            mma_i8(d + (uint32_t)(q * p.NB), a0 + (uint64_t)(2 * q), b0 + (uint64_t)(2 * q), idesc,
-                                   kb > kb0 ? 1u : 0u);
+                        for (int q = 0; q < kAccPerStage; ++q)
+                            mma_i8(dset + (uint32_t)(q * p.NB), a0 + (uint64_t)(2 * q), b0 + (uint64_t)(2 * q), idesc,
+                                   kb - kb0 >= 2 ? 1u : 0u);
                         tc::mma_commit(&empty[s]);
                     }
                     if (ok) tc::mma_commit(&tfull[buf]);
@@ -271,10 +388,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             // All four warps run the same item sequence and the same named barriers; a warp
             // whose wait ran out skips the work but keeps the barrier sequence.
             const int qd = warp & 3;  // TMEM lane quarter of this warp
-            int li = 0;
-            for (long long st = my_sb; st < my_se; ++li) {
-                const int tile = (int)(st / p.num_kb);
-                st = my_se < (long long)(tile + 1) * p.num_kb ? my_se : (long long)(tile + 1) * p.num_kb;
+            const int nseg = sc.num_segments(my_sb, my_se);
+            for (int li = 0; li < nseg; ++li) {
+                long long s0, s1;
+                sc.segment(my_sb, my_se, li, s0, s1);
+                const int tile = (int)(s0 / p.num_kb);
+                const int nacc = (s1 - s0 >= 2 ? kAccSets : 1) * kAccPerStage;  // accumulators written
                 const int first = sc.owner((long long)tile * p.num_kb);
                 const int parts = sc.owner((long long)(tile + 1) * p.num_kb - 1) - first + 1;
                 const int buf = li & 1;
@@ -289,6 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t taddr = tmem_base + ((uint32_t)(32 * qd) << 16) + (uint32_t)(buf * kAccPerBuf * p.NB);
 #pragma unroll
                     for (int a = 0; a < kAccPerBuf; ++a) {
+                        if (a >= nacc) break;
                         int T[16];
                         tmem_ld16(taddr + (uint32_t)(a * p.NB), T);
 #pragma unroll
@@ -308,12 +428,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (parts == 1) {
                     if (ok && row < p.N) {
                         const double sr = (double)__ldg(p.scales + row);
-                        for (int b = 0; b < p.B; ++b) p.y[(size_t)b * p.ldy + row] = combine(&D[4 * b], xscale[b], sr);
+#pragma unroll
+                        for (int b = 0; b < kMaxTok; ++b)
+                            if (b < p.B) p.y[(size_t)b * p.ldy + row] = combine(&D[4 * b], xscale[b], sr);
                     }
                 } else {
-                    int *acc = p.accum + ((size_t)first * TM + rl) * p.NB;
-                    if (ok)
-                        for (int j = 0; j < 4 * p.B; ++j) atomicAdd(acc + j, D[j]);
+                    // column j of the slot is 128 contiguous ints: a warp's 32 rows share one line
+                    int *acc = p.accum + (size_t)first * 32 * TM + rl;
+                    if (ok) {
+#pragma unroll
+                        for (int j = 0; j < 4 * kMaxTok; ++j)
+                            if (j < 4 * p.B) atomicAdd(acc + j * TM, D[j]);
+                    }
                     __threadfence();
                     named_bar(2, 128);
                     if (warp == 2 && lane == 0) *last_flag = atomicAdd(&p.tickets[first], 1u) == (unsigned)(parts - 1);
@@ -322,13 +448,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (last) {
                         __threadfence();
                         int S[32];
-                        for (int j = 0; j < 4 * p.B; ++j) {
-                            S[j] = __ldcg(acc + j);
-                            acc[j] = 0;  // leave the scratch zeroed for the next launch
+#pragma unroll
+                        for (int j = 0; j < 4 * kMaxTok; ++j) {
+                            S[j] = 0;
+                            if (j < 4 * p.B) {
+                                S[j] = __ldcg(acc + j * TM);
+                                acc[j * TM] = 0;  // leave the scratch zeroed for the next launch
+                            }
                         }
                         if (row < p.N && !*abort_flag) {
                             const double sr = (double)__ldg(p.scales + row);
-                            for (int b = 0; b < p.B; ++b) p.y[(size_t)b * p.ldy + row] = combine(&S[4 * b], xscale[b], sr);
+#pragma unroll
+                            for (int b = 0; b < kMaxTok; ++b)
+                                if (b < p.B) p.y[(size_t)b * p.ldy + row] = combine(&S[4 * b], xscale[b], sr);
                         }
                     }
                     named_bar(2, 128);
@@ -342,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (warp == 1) {
         tc::tc_fence_after();
-        tc::tmem_dealloc(tmem_base, kTmemCols);
+        tc::tmem_dealloc(tmem_base, p.tmem_cols);
     }
 }
 
@@ -350,7 +482,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() { return tensor_map_encoder(); }
 
 struct Plan {
     bool ok = false;
-    int NB = 16, stages = 0;
+    int NB = 16, stages = 0, x_stages = 0;
     uint32_t xd_bytes = 0;
 };
 
@@ -364,7 +496,8 @@ Plan plan_for(const QMatrix &w, size_t B, int num_sms) {
     if (pl.xd_bytes > 96 * 1024) return pl;
     const uint32_t avail = kSmemTotal - 1024 - 1024 - pl.xd_bytes;  // alignment slack, barriers
     pl.stages = std::min<int>(kMaxStages, (int)(avail / kStageBytes));
-    if (pl.stages < 2) return pl;
+    pl.x_stages = (int)((B * w.K * sizeof(float) + kStageBytes - 1) / kStageBytes);
+    if (pl.stages < 2 || pl.x_stages >= pl.stages) return pl;
     pl.ok = true;
     return pl;
 }
@@ -409,6 +542,9 @@ cudaError_t launch_gemv_tc(const QMatrix &w, const float *X, size_t B, size_t ld
     p.num_tiles = num_tiles;
     p.total_stages = total;
     p.stages = pl.stages;
+    p.tmem_cols = (uint32_t)(2 * kAccPerBuf * pl.NB);  // 256 or 512
+    p.x_stages = pl.x_stages;
+    p.pdl = pdl_enabled() ? 1 : 0;
     p.xd_bytes = pl.xd_bytes;
     p.x = X;
     p.ldx = (long long)ldx;
