@@ -60,6 +60,7 @@ def step_bytes():
 def config_dict(n):
     return {"workload": WORKLOAD, "batches": list(BATCHES), "weights": "seeded N(0,0.02) bf16 -> reference quantizer",
             "x": "seeded N(0,1) f32", "l2": "working set 680 MB/step > 126 MB L2; no flush needed",
+            "timing": "CUDA events around K replays of the 12-launch step captured once as a CUDA graph",
             "parallelism": f"dp{n} (independent decode streams per GPU)"}
 
 
@@ -378,69 +379,112 @@ def pyxis_arm(args, ws, rank, local):
     Y = {B: torch.empty((B, 151936), dtype=torch.float32, device=dev) for B in BATCHES}
     torch.cuda.synchronize()
 
-    lm_ev = []
-
-    def step(record=False):
+    def step(st):
         for B in BATCHES:
             for (name, qt, N, K, bs, w) in weights:
-                if record and name == "lm_head" and B == 1:
-                    e0 = torch.cuda.Event(enable_timing=True)
-                    e1 = torch.cuda.Event(enable_timing=True)
-                    e0.record(stream)
-                    px.matmul_dev(X[B][:, :K], w, N, K, Y=Y[B][:, :N], stream=stream)
-                    e1.record(stream)
-                    lm_ev.append((e0, e1))
-                else:
-                    px.matmul_dev(X[B][:, :K], w, N, K, Y=Y[B][:, :N], stream=stream)
+                px.matmul_dev(X[B][:, :K], w, N, K, Y=Y[B][:, :N], stream=st)
+
+    def capture(fn):
+        """fn(stream) recorded once into a CUDA graph: replays run the same kernels with no
+        host launch work between them (the decode loop runs its step the same way)."""
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            fn(s)  # first-call set-up (kernel attributes, tensor maps) outside the capture
+        torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=s, capture_error_mode="thread_local"):
+            fn(s)
+        torch.cuda.synchronize()
+        return g
+
+    def replay_ms(g, n):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(n):
+            g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1)
 
     launches_per_step = len(BATCHES) * len(SWEEP)
+    # eager reference result, then the captured step must reproduce it bit for bit
+    step(stream)
+    torch.cuda.synchronize()
+    y_eager = {B: Y[B].clone() for B in BATCHES}
+    g_step = capture(step)
+    for B in BATCHES:
+        Y[B].zero_()
+    g_step.replay()
+    torch.cuda.synchronize()
+    for B in BATCHES:
+        if not torch.equal(Y[B], y_eager[B]):
+            raise SystemExit("bench: the captured sweep step does not reproduce the eager result")
     for _ in range(max(args.warmup, 3)):
-        step()
+        g_step.replay()
     torch.cuda.synchronize()
     barrier(ws)
     clocks = ClockSampler(gpu_uuid(local))
     clocks.start()
     time.sleep(0.3)
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    start.record(stream)
-    for _ in range(args.steps):
-        step(record=True)
-    end.record(stream)
-    torch.cuda.synchronize()
+    ms = replay_ms(g_step, args.steps)
     clk = clocks.stop()
-    ms = start.elapsed_time(end)
     ms_max = max_over_ranks(ms, ws)
     barrier(ws)
+    # the same steps launched one call at a time from Python (host-launch-bound at these sizes)
+    eager_ms = 0.0
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step(stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    eager_ms = e0.elapsed_time(e1)
+    eager_ms_max = max_over_ranks(eager_ms, ws)
 
     sb = step_bytes()
     value = ws * sb * args.steps / (ms_max / 1e3) / 1e9
 
-    # per-launch device time of every case, in sweep order (cold L2 as in the timed steps), from an
-    # untimed pass with events between the launches
-    case_ev = {}
-    for _ in range(min(args.steps, 10)):
-        for B in BATCHES:
-            for (name, qt, N, K, bs, w) in weights:
-                e0 = torch.cuda.Event(enable_timing=True)
-                e1 = torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-                px.matmul_dev(X[B][:, :K], w, N, K, Y=Y[B][:, :N], stream=stream)
-                e1.record(stream)
-                case_ev.setdefault((name, B), []).append((e0, e1))
-    torch.cuda.synchronize()
+    # per-case device time: a graph of R launches over enough packed copies of the matrix that
+    # each launch reads it from HBM (copies x size > 2 x L2), as in the sweep
     cases = []
+    lm_ms = None
     for B in BATCHES:
-        for (name, qt, N, K, bs, w) in weights:
-            us = statistics.median(a.elapsed_time(b) for a, b in case_ev[(name, B)]) * 1e3
+        for i, (name, qt, N, K, bs, w) in enumerate(weights):
             by = gemv_bytes(qt, N, K, bs, B)
+            wbytes = N * K if qt == "int8" else N * K // 2
+            ncopy = max(1, min(64, -(-(256 << 20) // wbytes)))
+            copies = [w]
+            if ncopy > 1:
+                bits = px.synth_normal_bf16(SEED + i, N * K, 0.02)
+                t = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).to(dev)
+                for _ in range(ncopy - 1):
+                    copies.append(px.Weights.quantize_int8(t, bs, device=local) if qt == "int8"
+                                  else px.Weights.quantize_int4(t, bs, device=local))
+                del t
+            reps = max(len(copies), 8)
+
+            def case_fn(st, copies=copies, B=B, N=N, K=K, reps=reps):
+                for r in range(reps):
+                    px.matmul_dev(X[B][:, :K], copies[r % len(copies)], N, K, Y=Y[B][:, :N], stream=st)
+
+            g = capture(case_fn)
+            g.replay()
+            us = replay_ms(g, 3) / (3 * reps) * 1e3
+            del g, copies
+            if name == "lm_head" and B == 1:
+                lm_ms = us / 1e3
             cases.append({"case": f"{name} {qt} {N}x{K} B={B}", "kernel": px.matmul_kernel_name(w, B, N, K),
                           "us": round(us, 2), "gbs": round(by / us / 1e3, 1)})
-    lm_ms = statistics.mean(a.elapsed_time(b) for a, b in lm_ev)
     lm_bytes = gemv_bytes("int8", 151936, 2048, 2048, 1)
     peak, peak_kind = measured_peak_hbm()
     achieved = lm_bytes / (lm_ms / 1e3) / 1e9
+    del g_step
 
     # e2e: the same sweep through the host-pointer C ABI (pinned host x in, host y out).
     hx = {B: torch.empty((B, 6144), dtype=torch.float32).pin_memory() for B in BATCHES}
@@ -522,6 +566,7 @@ def pyxis_arm(args, ws, rank, local):
                 "frac_of_peak_step": value / ws / peak,
                 "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
                 "cpu_baseline": cpu, "clocks": clk, "gpu_launches": launches_per_step * args.steps,
+                "eager_ms_per_step": eager_ms_max / args.steps,
                 "cases": cases,
                 "decode": decode,
                 "lm_head_vocab_parallel": lm_vp,

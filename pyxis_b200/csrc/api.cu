@@ -54,7 +54,7 @@ struct DeviceGuard {
 size_t div_ceil(size_t a, size_t b) { return (a + b - 1) / b; }
 
 constexpr size_t kTcMinRows = 16;        // matmul_dev rows from which the tensor-core GEMM runs
-constexpr size_t kTcGemvMinRows = 32768;  // out_features from which batch-1 int8 GEMVs use tensor cores
+constexpr size_t kTcGemvMinRows = 32768;  // out_features from which int8 GEMVs use tensor cores
 
 size_t packed_bytes(int qtype, size_t n) { return qtype == PYXIS_QTYPE_INT8 ? n : div_ceil(n, 2); }
 
@@ -126,11 +126,14 @@ bool use_gemm_tc(const QMatrix &q, size_t M, const float *X, size_t ldx) {
     return M >= kTcMinRows && gemm_tc_supported(q) && (reinterpret_cast<uintptr_t>(X) & 15) == 0 && ldx % 4 == 0;
 }
 
-// Tensor cores for big matrices (the lm_head); below kTcGemvMinRows a GEMV is latency-bound and
-// the CUDA-core ring kernel's shorter critical path wins (no digit build, no shared tiles).
-// Batches of 2-8 int8 rows always take the tensor cores (int4 has no tensor-core GEMV).
+// Tensor cores for big matrices (the lm_head).  Below kTcGemvMinRows a GEMV is latency-bound:
+// the CUDA-core batch kernel (all weight loads in flight at once, split-K over warps) finishes
+// first at every batch size, and the tensor-core kernel's fixed start-up (digit operand, ring
+// fill, TMEM) does not pay for itself.  Measured on B200 (graph replay, device time): int8
+// 12288 x 2048 at batch 8 takes 22.9 us on the batch kernel vs 25.0 us on the tensor cores,
+// 4096 x 2048 9.8 vs 18.1 us; the lm_head (151936 rows) is the other way round.
 bool use_gemv_tc(const pyxis_cuda_ctx *ctx, const QMatrix &q, size_t b, const float *xb, size_t ldx) {
-    const bool tc_ok = b > 1 || q.N >= kTcGemvMinRows || !gemv_ring_supported(q, ctx->num_sms);
+    const bool tc_ok = q.N >= kTcGemvMinRows || !gemv_batch_supported(q, b, ctx->num_sms);
     return tc_ok && gemv_tc_supported(q, b, ctx->num_sms) && (reinterpret_cast<uintptr_t>(xb) & 15) == 0 &&
            (b == 1 || ldx % 4 == 0);
 }
