@@ -7,8 +7,6 @@
 //   batch  B = 1..8 with K % 32 == 0, whole-chunk scale blocks and x fitting shared memory:
 //          gemv_batch.cu (x staged by TMA, every weight load in flight at once, split-K over
 //          warps).  The decode shapes and the benchmark sweep all run here.
-//   ring   B = 1 shapes the batch kernel does not take (x too large for shared memory):
-//          gemv_ring.cu.
 //   generic  any shape the others do not take (K not a multiple of the chunk, blocks that
 //          straddle rows, odd K with int4 rows that start mid-byte): one warp per row,
 //          element-wise decode with the reference's scales[g / block_size] lookup.
@@ -46,7 +44,6 @@ __global__ void gemv_generic_kernel(const uint8_t *W, const float *S, size_t bs,
 // ---------------------------------------------------------------- dispatch --------------------
 const char *gemv_kernel_name(const QMatrix &w, size_t B, int num_sms) {
     if (gemv_batch_supported(w, B, num_sms)) return "gemv_batch_kernel";
-    if (B == 1 && gemv_ring_supported(w, num_sms)) return "gemv_ring_kernel";
     return "gemv_generic_kernel";
 }
 
@@ -56,7 +53,6 @@ cudaError_t launch_gemv(const QMatrix &w, const float *X, size_t B, size_t ldx, 
     const bool x_aligned = (reinterpret_cast<uintptr_t>(X) & 15) == 0;
     if (x_aligned && (B == 1 || ldx % 4 == 0) && gemv_batch_supported(w, B, num_sms))
         return launch_gemv_batch(w, X, B, ldx, Y, ldy, err, num_sms, st);
-    if (B == 1 && x_aligned && gemv_ring_supported(w, num_sms)) return launch_gemv_ring(w, X, Y, err, num_sms, st);
     const size_t threads = w.N * 32;
     const unsigned grid = (unsigned)((threads + 255) / 256);
     if (w.qtype == kQInt8)

@@ -22,14 +22,10 @@ struct QMatrix {
 cudaError_t launch_quantize(const void *src, int src_kind, size_t n, size_t bs, int qtype,
                             void *data, float *scales, int num_sms, cudaStream_t st);
 
-// Decode GEMV: Y[b, :] = W X[b, :] for b < B (B = 1..8).  Picks the register-resident-x team
-// kernel, the shared-memory-x kernel or the generic kernel by shape (gemv.cu).
+// Decode GEMV: Y[b, :] = W X[b, :] for b < B (B = 1..8): the batch kernel where it applies, else
+// the generic kernel (gemv.cu).
 cudaError_t launch_gemv(const QMatrix &w, const float *X, size_t B, size_t ldx, float *Y,
                         size_t ldy, int *err, int num_sms, cudaStream_t st);
-
-// Batch-1 GEMV streaming row tiles through a shared-memory ring (gemv_ring.cu).
-bool gemv_ring_supported(const QMatrix &w, int num_sms);
-cudaError_t launch_gemv_ring(const QMatrix &w, const float *x, float *y, int *err, int num_sms, cudaStream_t st);
 
 // 1-8 input rows on the CUDA cores with x staged by TMA and split-K over warps (gemv_batch.cu):
 // K % 32 == 0, one scale per row or per block of whole 16-byte chunks, B * K * 4 bytes of x in
