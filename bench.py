@@ -587,12 +587,14 @@ def profile_case(args):
     if args.profile_case.startswith("decode"):
         from pyxis_b200 import synth_tokens
         from pyxis_b200.model import QWEN3_1_7B, Decoder, SyntheticModel
-        dec = Decoder(SyntheticModel(QWEN3_1_7B, SEED), qtype="int8", max_seq=64)
-        prompt = synth_tokens(0x9E0, 2, QWEN3_1_7B.vocab)
-        dec.generate(prompt, 2)
+        ctx = int(args.profile_case.split(":")[1]) if ":" in args.profile_case else 2  # prompt length
         n = max(2, args.steps + 1)
+        dec = Decoder(SyntheticModel(QWEN3_1_7B, SEED), qtype="int8", max_seq=ctx + n + 8)
+        prompt = synth_tokens(0x9E0, ctx, QWEN3_1_7B.vocab)
+        dec.generate(prompt[:2], 2)
         toks, t = dec.generate(prompt, n)
-        print(f"profile case decode: {n - 1} steps, prompt {t[0]:.2f} ms, decode {t[1] / (n - 1):.3f} ms/token")
+        print(f"profile case decode: prompt {ctx}, {n - 1} steps, prompt {t[0]:.2f} ms, "
+              f"decode {t[1] / (n - 1):.3f} ms/token")
         return
     name, B = args.profile_case.split(":") if ":" in args.profile_case else (args.profile_case, "1")
     B = int(B)

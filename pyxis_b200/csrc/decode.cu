@@ -7,9 +7,11 @@
 // src/attention.rs:107-179, src/ffn.rs:39-54) with explicit round-to-nearest multiplies and adds
 // where the reference's operation order is cheap to keep (no FMA contraction); sums of many
 // terms are reduced in parallel.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <new>
+#include <utility>
 #include <vector>
 
 #include "../../include/pyxis_decode.h"
@@ -30,18 +32,6 @@ PYXIS_DEVINL float block_sum(float v, float *red) {
     __syncthreads();
     float t = 0.f;
     for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
-    __syncthreads();
-    return t;
-}
-
-PYXIS_DEVINL float block_max(float v, float *red) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-    if (l == 0) red[w] = v;
-    __syncthreads();
-    float t = -INFINITY;
-    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t = fmaxf(t, red[i]);
     __syncthreads();
     return t;
 }
@@ -99,89 +89,213 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float *__rest
     }
 }
 
-// Per head: QK RMSNorm (src/attention.rs:81-90), RoPE at `pos` from the host-made table
-// (:92-93, :144-162), then q -> qout, k and v -> the KV cache row `pos` (cache.append, :100).
-// Grid: n_q + n_kv CTAs (one per q or k head) + 1 CTA copying v; head_dim threads.
-__global__ void qk_rope_append_kernel(const float *__restrict__ qkv, const float *__restrict__ q_norm,
-                                      const float *__restrict__ k_norm, const float *__restrict__ rcos,
-                                      const float *__restrict__ rsin, const int *__restrict__ d_pos, int n_q, int n_kv,
-                                      int hd, float eps, float *__restrict__ qout, float *__restrict__ kcache,
-                                      float *__restrict__ vcache) {
-    extern __shared__ float sh[];  // [hd] head values, [32] reduction
-    float *hv = sh, *red = sh + hd;
-    pdl_wait();
-    pdl_trigger();
-    const int pos = *d_pos;
-    const int kv_dim = n_kv * hd, q_dim = n_q * hd;
-    const int b = blockIdx.x, d = threadIdx.x;
-    if (b == n_q + n_kv) {  // v row
-        for (int i = d; i < kv_dim; i += blockDim.x) vcache[(size_t)pos * kv_dim + i] = qkv[q_dim + kv_dim + i];
-        return;
+// Attention for the newest position, fused with what precedes it (src/attention.rs:81-135):
+// per-head QK RMSNorm (:81-90), RoPE at `pos` from the host-made table (:92-93, :144-162), the
+// KV-cache append (:100), then causal GQA attention scores = (q . k_j) / sqrt(hd) for j <= pos,
+// softmax (:164-179) and out = sum_j p_j v_j.
+// Grid (splits, n_kv): CTA (s, h) handles the G = n_q / n_kv query heads of kv head h over the
+// keys [s*len/S, (s+1)*len/S).  Every CTA normalises and rotates its heads' q and the new k itself
+// (a few hundred flops), the CTA holding key `pos` writes k and v to the cache, and the newest
+// key is taken from shared memory, so no CTA reads a cache row another one is writing.  Each CTA
+// leaves (max, sum of exp, unnormalised sum_j p_j v_j) per head in `part`; the last CTA of a kv
+// head (ticket) rescales and adds the splits in order and re-arms the ticket.
+// Lane l of a warp holds head elements [l*EPL, (l+1)*EPL); RoPE pairs element i with i + hd/2,
+// which sits in lane l ^ 16.
+constexpr int kAttnThreads = 256;
+constexpr int kAttnMaxG = 4;
+
+template <int EPL>
+PYXIS_DEVINL void load_head(const float *p, float (&v)[EPL]) {
+    if constexpr (EPL == 4) {
+        const float4 t = *reinterpret_cast<const float4 *>(p);
+        v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
+    } else {
+        const float2 t = *reinterpret_cast<const float2 *>(p);
+        v[0] = t.x, v[1] = t.y;
     }
-    const bool is_q = b < n_q;
-    const float *src = is_q ? qkv + (size_t)b * hd : qkv + q_dim + (size_t)(b - n_q) * hd;
-    const float *nw = is_q ? q_norm : k_norm;
-    float v = src[d];
-    if (nw) {
-        float ss = block_sum(__fmul_rn(v, v), red);
-        const float factor = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)hd), eps)));
-        v = __fmul_rn(v, __fmul_rn(factor, nw[d]));
-    }
-    hv[d] = v;
-    __syncthreads();
-    const int half = hd / 2;
-    const int i = d < half ? d : d - half;
-    const float c = rcos[(size_t)pos * half + i], s = rsin[(size_t)pos * half + i];
-    const float x0 = hv[i], x1 = hv[i + half];
-    const float r = d < half ? __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s)) : __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s));
-    if (is_q) qout[(size_t)b * hd + d] = r;
-    else kcache[(size_t)pos * kv_dim + (size_t)(b - n_q) * hd + d] = r;
 }
 
-// Causal GQA attention for the newest position (src/attention.rs:107-135): one CTA per q head;
-// scores = (q . k_j) / sqrt(hd) for j <= pos, softmax (:164-179), out[d] = sum_j p_j v_j[d]
-// accumulated over j in order with separate multiply and add, as the reference does.
-__global__ void attention_decode_kernel(const float *__restrict__ q, const float *__restrict__ kcache,
-                                        const float *__restrict__ vcache, const int *__restrict__ d_pos, int n_q,
-                                        int n_kv, int hd, float *__restrict__ out) {
-    extern __shared__ float sc[];  // [pos + 1] scores, then [32] reduction
+// QK RMSNorm (optional) and RoPE of one head held across a warp.
+template <int EPL>
+PYXIS_DEVINL void norm_rope(float (&v)[EPL], const float *nw, const float *rcos, const float *rsin, int pos,
+                            float eps, int lane) {
+    constexpr int HD = 32 * EPL, HALF = HD / 2;
+    if (nw) {
+        float ss = 0.f;
+#pragma unroll
+        for (int t = 0; t < EPL; ++t) ss = __fadd_rn(ss, __fmul_rn(v[t], v[t]));
+        ss = warp_sum(ss);
+        const float factor = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)HD), eps)));
+#pragma unroll
+        for (int t = 0; t < EPL; ++t) v[t] = __fmul_rn(v[t], __fmul_rn(factor, nw[lane * EPL + t]));
+    }
+    const bool lo = lane < 16;
+#pragma unroll
+    for (int t = 0; t < EPL; ++t) {
+        const float other = __shfl_xor_sync(0xffffffffu, v[t], 16);
+        const int i = (lane & 15) * EPL + t;  // pair index in [0, HALF)
+        const float c = rcos[(size_t)pos * HALF + i], s = rsin[(size_t)pos * HALF + i];
+        v[t] = lo ? __fsub_rn(__fmul_rn(v[t], c), __fmul_rn(other, s)) : __fadd_rn(__fmul_rn(v[t], c), __fmul_rn(other, s));
+    }
+}
+
+template <int EPL>
+__global__ void __launch_bounds__(kAttnThreads)
+    attention_step_kernel(const float *__restrict__ qkv, const float *__restrict__ q_norm,
+                          const float *__restrict__ k_norm, const float *__restrict__ rcos,
+                          const float *__restrict__ rsin, const int *__restrict__ d_pos, int n_q, int n_kv, float eps,
+                          float *__restrict__ kcache, float *__restrict__ vcache, float *__restrict__ part,
+                          unsigned *__restrict__ tickets, float *__restrict__ out) {
+    constexpr int HD = 32 * EPL;
+    extern __shared__ float sm[];  // q [G][HD] | knew [HD] | vnew [HD] | p [G][chunk] | flag
+    const int G = n_q / n_kv;
+    const int S = gridDim.x, s = blockIdx.x, h = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const int kv_dim = n_kv * HD, q_dim = n_q * HD;
     pdl_wait();
     pdl_trigger();
     const int pos = *d_pos;
     const int len = pos + 1;
-    float *red = sc + len;
-    const int qh = blockIdx.x;
-    const int kvh = qh * n_kv / n_q;  // src/attention.rs:111
-    const int kv_dim = n_kv * hd;
-    const float *qh_p = q + (size_t)qh * hd;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    const float scale = sqrtf((float)hd);
-    for (int j = warp; j < len; j += nw) {
-        const float *k = kcache + (size_t)j * kv_dim + (size_t)kvh * hd;
-        float dot = 0.f;
-        for (int e = lane; e < hd; e += 32) dot = __fadd_rn(dot, __fmul_rn(qh_p[e], k[e]));
-        dot = warp_sum(dot);
-        if (lane == 0) sc[j] = __fdiv_rn(dot, scale);
+    const int j0 = (int)((long long)s * len / S), j1 = (int)((long long)(s + 1) * len / S);
+    const int chunk = (int)(((long long)len + S - 1) / S);
+    float *qs = sm, *knew = qs + G * HD, *vnew = knew + HD, *pr = vnew + HD;
+    volatile int *flag = reinterpret_cast<volatile int *>(pr + G * chunk);
+
+    // heads of this kv group: warps 0..G-1 take the q heads, warp G the new k, warp G+1 the new v
+    if (warp < G) {
+        float v[EPL];
+        load_head<EPL>(qkv + (size_t)(h * G + warp) * HD + lane * EPL, v);
+        norm_rope<EPL>(v, q_norm, rcos, rsin, pos, eps, lane);
+#pragma unroll
+        for (int t = 0; t < EPL; ++t) qs[warp * HD + lane * EPL + t] = v[t];
+    } else if (warp == G) {
+        float v[EPL];
+        load_head<EPL>(qkv + q_dim + (size_t)h * HD + lane * EPL, v);
+        norm_rope<EPL>(v, k_norm, rcos, rsin, pos, eps, lane);
+#pragma unroll
+        for (int t = 0; t < EPL; ++t) {
+            knew[lane * EPL + t] = v[t];
+            if (s == S - 1) kcache[(size_t)pos * kv_dim + (size_t)h * HD + lane * EPL + t] = v[t];
+        }
+    } else if (warp == G + 1) {
+        float v[EPL];
+        load_head<EPL>(qkv + q_dim + kv_dim + (size_t)h * HD + lane * EPL, v);
+#pragma unroll
+        for (int t = 0; t < EPL; ++t) {
+            vnew[lane * EPL + t] = v[t];
+            if (s == S - 1) vcache[(size_t)pos * kv_dim + (size_t)h * HD + lane * EPL + t] = v[t];
+        }
     }
     __syncthreads();
-    float m = -INFINITY;
-    for (int j = threadIdx.x; j < len; j += blockDim.x) m = fmaxf(m, sc[j]);
-    m = block_max(m, red);
-    float s = 0.f;
-    for (int j = threadIdx.x; j < len; j += blockDim.x) {
-        const float e = expf(__fsub_rn(sc[j], m));
-        sc[j] = e;
-        s = __fadd_rn(s, e);
+
+    // scores of this split's keys, one warp per key, four keys' loads in flight per warp
+    const float scale = sqrtf((float)HD);
+    float qr[kAttnMaxG][EPL];
+#pragma unroll
+    for (int g = 0; g < kAttnMaxG; ++g)
+#pragma unroll
+        for (int t = 0; t < EPL; ++t) {
+            qr[g][t] = 0.f;
+            if (g < G) qr[g][t] = qs[g * HD + lane * EPL + t];
+        }
+    for (int jb = j0 + warp; jb < j1; jb += 4 * nw) {
+        float kr[4][EPL];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int j = jb + u * nw;
+            if (j < j1) {
+                const float *k = j == pos ? knew : kcache + (size_t)j * kv_dim + (size_t)h * HD;
+                load_head<EPL>(k + lane * EPL, kr[u]);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int j = jb + u * nw;
+            if (j >= j1) break;  // uniform across the warp
+#pragma unroll
+            for (int g = 0; g < kAttnMaxG; ++g) {
+                if (g >= G) break;
+                float dot = 0.f;
+#pragma unroll
+                for (int t = 0; t < EPL; ++t) dot = __fadd_rn(dot, __fmul_rn(qr[g][t], kr[u][t]));
+                dot = warp_sum(dot);
+                if (lane == 0) pr[g * chunk + (j - j0)] = __fdiv_rn(dot, scale);
+            }
+        }
     }
-    s = block_sum(s, red);
-    for (int j = threadIdx.x; j < len; j += blockDim.x) sc[j] = __fdiv_rn(sc[j], s);
     __syncthreads();
-    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+
+    // per head: local max and exp, then sum_j p_j v_j over this split (v rows read coalesced)
+    const int n = j1 - j0;
+    float *mine = part + ((size_t)h * S + s) * G * (HD + 2);
+    for (int g = warp; g < G; g += nw) {
+        float m = -INFINITY;
+        for (int j = lane; j < n; j += 32) m = fmaxf(m, pr[g * chunk + j]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float l = 0.f;
+        for (int j = lane; j < n; j += 32) {
+            const float e = expf(__fsub_rn(pr[g * chunk + j], m));
+            pr[g * chunk + j] = e;
+            l = __fadd_rn(l, e);
+        }
+        l = warp_sum(l);
+        if (lane == 0) {
+            mine[g * (HD + 2)] = m;
+            mine[g * (HD + 2) + 1] = l;
+        }
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < G * HD; idx += blockDim.x) {
+        const int g = idx / HD, d = idx - g * HD;
+        const float *vcol = vcache + (size_t)h * HD + d;
         float acc = 0.f;
-        const float *v = vcache + (size_t)kvh * hd + d;
-        for (int j = 0; j < len; ++j) acc = __fadd_rn(acc, __fmul_rn(sc[j], v[(size_t)j * kv_dim]));
-        out[(size_t)qh * hd + d] = acc;
+        int j = 0;
+        for (; j + 8 <= n; j += 8) {
+            float vv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int jj = j0 + j + u;
+                if (jj == pos) vv[u] = vnew[d];
+                else vv[u] = vcol[(size_t)jj * kv_dim];
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, __fmul_rn(pr[g * chunk + j + u], vv[u]));
+        }
+        for (; j < n; ++j) {
+            const int jj = j0 + j;
+            float vj;
+            if (jj == pos) vj = vnew[d];
+            else vj = vcol[(size_t)jj * kv_dim];
+            acc = __fadd_rn(acc, __fmul_rn(pr[g * chunk + j], vj));
+        }
+        mine[g * (HD + 2) + 2 + d] = acc;
     }
+
+    // the last CTA of this kv head combines the splits in order
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) *flag = atomicAdd(&tickets[h], 1u) == (unsigned)(S - 1);
+    __syncthreads();
+    if (!*flag) return;
+    __threadfence();
+    const float *all = part + (size_t)h * S * G * (HD + 2);
+    for (int idx = threadIdx.x; idx < G * HD; idx += blockDim.x) {
+        const int g = idx / HD, d = idx - g * HD;
+        float M = -INFINITY;
+        for (int t = 0; t < S; ++t) M = fmaxf(M, __ldcg(all + ((size_t)t * G + g) * (HD + 2)));
+        float L = 0.f, acc = 0.f;
+        for (int t = 0; t < S; ++t) {
+            const float *pt = all + ((size_t)t * G + g) * (HD + 2);
+            const float mt = __ldcg(pt);
+            if (mt == -INFINITY) continue;  // an empty split
+            const float w = expf(__fsub_rn(mt, M));
+            L = __fadd_rn(L, __fmul_rn(__ldcg(pt + 1), w));
+            acc = __fadd_rn(acc, __fmul_rn(__ldcg(pt + 2 + d), w));
+        }
+        out[(size_t)(h * G + g) * HD + d] = __fdiv_rn(acc, L);
+    }
+    if (threadIdx.x == 0) tickets[h] = 0;
 }
 
 // act = silu(gate) * up, silu(x) = x / (1 + exp(-x)) (src/ffn.rs:39-41, :52-54).
@@ -223,6 +337,10 @@ struct pyxis_cuda_model {
     float *final_norm = nullptr;
     float *rope_cos = nullptr, *rope_sin = nullptr;
     float *kcache = nullptr, *vcache = nullptr;
+    float *x2 = nullptr;                      // the residual stream alternates between x and x2
+    float *part = nullptr;                    // attention split partials [n_kv][splits][G][hd + 2]
+    unsigned *tickets = nullptr;              // [n_kv], zero between launches
+    int attn_splits = 1;
     float *x = nullptr, *h = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *tmp = nullptr, *gu = nullptr,
           *act = nullptr, *logits = nullptr;
     int *d_pos = nullptr, *d_token = nullptr, *d_step = nullptr, *d_out = nullptr;
@@ -256,50 +374,104 @@ struct Guard {
     }
 };
 
+QMatrix qmat(const pyxis_cuda_weights *w, size_t N, size_t K) {
+    return QMatrix{w->qtype, w->data, w->scales, w->block_size, N, K};
+}
+
+// y = W x' with x' = RMSNorm(x + delta) (CTA 0 of the GEMV stores x + delta to xout), fused into
+// the GEMV's x staging when the shape allows, else the separate norm kernel and a plain GEMV.
+int norm_gemv(pyxis_cuda_model *m, const pyxis_cuda_weights *w, size_t N, float *x, const float *delta,
+              float *xout, const float *nw, float *y, cudaStream_t st) {
+    const pyxis_model_config &c = m->cfg;
+    const size_t H = c.hidden;
+    GemvPrologue pro;
+    pro.kind = kProAddNorm;
+    pro.x = x;
+    pro.delta = delta;
+    pro.w = nw;
+    pro.xout = xout;
+    pro.eps = c.rms_eps;
+    const QMatrix q = qmat(w, N, H);
+    if (gemv_batch_pro_supported(q, pro, m->ctx->num_sms)) {
+        cudaError_t e = launch_gemv_batch_pro(q, pro, y, m->ctx->d_err, m->ctx->num_sms, st);
+        return e == cudaSuccess ? PYXIS_OK : model_fail(PYXIS_ECUDA, cudaGetErrorString(e));
+    }
+    // unfused: x + delta written to xout by the norm kernel, h = norm(xout)
+    if (delta) {
+        cudaError_t e = cudaMemcpyAsync(xout, x, H * sizeof(float), cudaMemcpyDeviceToDevice, st);
+        if (e == cudaSuccess)
+            e = launch_kernel(add_rmsnorm_kernel, dim3(1), dim3(kNormThreads), 0, st, xout, delta, nw, m->h, (int)H,
+                              c.rms_eps);
+        if (e != cudaSuccess) return model_fail(PYXIS_ECUDA, cudaGetErrorString(e));
+    } else {
+        cudaError_t e = launch_kernel(add_rmsnorm_kernel, dim3(1), dim3(kNormThreads), 0, st, x, (const float *)nullptr,
+                                      nw, m->h, (int)H, c.rms_eps);
+        if (e != cudaSuccess) return model_fail(PYXIS_ECUDA, cudaGetErrorString(e));
+    }
+    return run_matmul(m->ctx, w, m->h, 1, H, N, H, y, N, nullptr, 0, st);
+}
+
+// y = Wdown (SiLU(gate) * up) from the stacked [gate; up] output gu.
+int silu_gemv(pyxis_cuda_model *m, const pyxis_cuda_weights *w, float *y, cudaStream_t st) {
+    const pyxis_model_config &c = m->cfg;
+    GemvPrologue pro;
+    pro.kind = kProSiluMul;
+    pro.x = m->gu;
+    const QMatrix q = qmat(w, c.hidden, c.ffn);
+    if (gemv_batch_pro_supported(q, pro, m->ctx->num_sms)) {
+        cudaError_t e = launch_gemv_batch_pro(q, pro, y, m->ctx->d_err, m->ctx->num_sms, st);
+        return e == cudaSuccess ? PYXIS_OK : model_fail(PYXIS_ECUDA, cudaGetErrorString(e));
+    }
+    cudaError_t e = launch_kernel(silu_mul_kernel, dim3((c.ffn + 255) / 256), dim3(256), 0, st, (const float *)m->gu,
+                                  c.ffn, m->act);
+    if (e != cudaSuccess) return model_fail(PYXIS_ECUDA, cudaGetErrorString(e));
+    return run_matmul(m->ctx, w, m->act, 1, c.ffn, c.hidden, c.ffn, y, c.hidden, nullptr, 0, st);
+}
+
+size_t attention_smem(const pyxis_cuda_model *m) {
+    const pyxis_model_config &c = m->cfg;
+    const int G = c.n_q_heads / c.n_kv_heads;
+    const int chunk = (c.max_seq + m->attn_splits - 1) / m->attn_splits;
+    return ((size_t)G * c.head_dim + 2 * (size_t)c.head_dim + (size_t)G * chunk + 4) * sizeof(float);
+}
+
 // One decode step on `st` (what the graph holds).
 int enqueue_step(pyxis_cuda_model *m, cudaStream_t st) {
     const pyxis_model_config &c = m->cfg;
     const int H = c.hidden;
+    const size_t qkv_rows = (size_t)m->q_dim + 2 * m->kv_dim;
     PdlScope pdl;  // kernels of the step may start while their predecessor finishes
     cudaError_t le = launch_kernel(embed_kernel, dim3((H + 255) / 256), dim3(256), 0, st, (const uint16_t *)m->emb,
                                    (const int *)m->d_token, c.vocab, H, m->x);
-    if (le == cudaSuccess)
-        le = launch_kernel(add_rmsnorm_kernel, dim3(1), dim3(kNormThreads), 0, st, m->x, (const float *)nullptr,
-                           (const float *)m->layers[0].in_norm, m->h, H, c.rms_eps);
     if (le != cudaSuccess) return model_fail(PYXIS_ECUDA, cudaGetErrorString(le));
+    float *xr = m->x, *xw = m->x2;  // residual stream: read xr, the fused norm writes xr + delta to xw
+    const size_t asmem = attention_smem(m);
     for (int l = 0; l < c.n_layers; ++l) {
         const auto &L = m->layers[l];
         float *kc = m->kcache + (size_t)l * c.max_seq * m->kv_dim;
         float *vc = m->vcache + (size_t)l * c.max_seq * m->kv_dim;
-        int rc = run_matmul(m->ctx, L.wqkv, m->h, 1, H, (size_t)m->q_dim + 2 * m->kv_dim, H, m->qkv,
-                            (size_t)m->q_dim + 2 * m->kv_dim, nullptr, 0, st);
+        // layer input: x (+ the previous layer's FFN output) -> RMSNorm -> q|k|v
+        int rc = norm_gemv(m, L.wqkv, qkv_rows, xr, l ? m->tmp : nullptr, xw, L.in_norm, m->qkv, st);
         if (rc) return rc;
-        le = launch_kernel(qk_rope_append_kernel, dim3(c.n_q_heads + c.n_kv_heads + 1), dim3(c.head_dim),
-                           (c.head_dim + 32) * sizeof(float), st, (const float *)m->qkv, (const float *)L.q_norm,
-                           (const float *)L.k_norm, (const float *)m->rope_cos, (const float *)m->rope_sin,
-                           (const int *)m->d_pos, c.n_q_heads, c.n_kv_heads, c.head_dim, c.rms_eps, m->q, kc, vc);
-        if (le == cudaSuccess)
-            le = launch_kernel(attention_decode_kernel, dim3(c.n_q_heads), dim3(128), (c.max_seq + 32) * sizeof(float),
-                               st, (const float *)m->q, (const float *)kc, (const float *)vc, (const int *)m->d_pos,
-                               c.n_q_heads, c.n_kv_heads, c.head_dim, m->attn);
+        if (l) std::swap(xr, xw);
+        auto kern = c.head_dim == 128 ? attention_step_kernel<4> : attention_step_kernel<2>;
+        le = launch_kernel(kern, dim3(m->attn_splits, c.n_kv_heads), dim3(kAttnThreads), asmem, st,
+                           (const float *)m->qkv, (const float *)L.q_norm, (const float *)L.k_norm,
+                           (const float *)m->rope_cos, (const float *)m->rope_sin, (const int *)m->d_pos, c.n_q_heads,
+                           c.n_kv_heads, c.rms_eps, kc, vc, m->part, m->tickets, m->attn);
         if (le != cudaSuccess) return model_fail(PYXIS_ECUDA, cudaGetErrorString(le));
         rc = run_matmul(m->ctx, L.wo, m->attn, 1, m->q_dim, H, m->q_dim, m->tmp, H, nullptr, 0, st);
         if (rc) return rc;
-        le = launch_kernel(add_rmsnorm_kernel, dim3(1), dim3(kNormThreads), 0, st, m->x, (const float *)m->tmp,
-                           (const float *)L.post_norm, m->h, H, c.rms_eps);
-        if (le != cudaSuccess) return model_fail(PYXIS_ECUDA, cudaGetErrorString(le));
-        rc = run_matmul(m->ctx, L.wgu, m->h, 1, H, 2 * (size_t)c.ffn, H, m->gu, 2 * (size_t)c.ffn, nullptr, 0, st);
+        // x + attention output -> RMSNorm -> gate|up, then SiLU(gate) * up -> down
+        rc = norm_gemv(m, L.wgu, 2 * (size_t)c.ffn, xr, m->tmp, xw, L.post_norm, m->gu, st);
         if (rc) return rc;
-        le = launch_kernel(silu_mul_kernel, dim3((c.ffn + 255) / 256), dim3(256), 0, st, (const float *)m->gu, c.ffn,
-                           m->act);
-        if (le != cudaSuccess) return model_fail(PYXIS_ECUDA, cudaGetErrorString(le));
-        rc = run_matmul(m->ctx, L.wdown, m->act, 1, c.ffn, H, c.ffn, m->tmp, H, nullptr, 0, st);
+        std::swap(xr, xw);
+        rc = silu_gemv(m, L.wdown, m->tmp, st);
         if (rc) return rc;
-        const float *next_norm = l + 1 < c.n_layers ? m->layers[l + 1].in_norm : m->final_norm;
-        le = launch_kernel(add_rmsnorm_kernel, dim3(1), dim3(kNormThreads), 0, st, m->x, (const float *)m->tmp,
-                           next_norm, m->h, H, c.rms_eps);
-        if (le != cudaSuccess) return model_fail(PYXIS_ECUDA, cudaGetErrorString(le));
     }
+    le = launch_kernel(add_rmsnorm_kernel, dim3(1), dim3(kNormThreads), 0, st, xr, (const float *)m->tmp,
+                       (const float *)m->final_norm, m->h, H, c.rms_eps);
+    if (le != cudaSuccess) return model_fail(PYXIS_ECUDA, cudaGetErrorString(le));
     int rc = run_matmul(m->ctx, m->lm_head, m->h, 1, H, c.vocab, H, m->logits, c.vocab, nullptr, 0, st);
     if (rc) return rc;
     cudaError_t e = launch_argmax_scratch(m->logits, 1, c.vocab, c.vocab, 0, m->d_token, nullptr, m->ctx->amax,
@@ -339,8 +511,10 @@ extern "C" int pyxis_cuda_model_create(pyxis_cuda_ctx *ctx, const pyxis_model_co
         c.vocab <= 0 || c.max_seq <= 0 || c.head_dim % 2 || c.head_dim > 1024 || c.n_q_heads % c.n_kv_heads)
         return model_fail(PYXIS_EINVAL, "pyxis_cuda_model_create: bad config");
     if (c.hidden > 1024 * 8) return model_fail(PYXIS_EINVAL, "pyxis_cuda_model_create: hidden > 8192");
-    if ((size_t)c.max_seq * 4 + 256 > 160 * 1024)
-        return model_fail(PYXIS_EINVAL, "pyxis_cuda_model_create: max_seq too large for the decode attention kernel");
+    if (c.head_dim != 64 && c.head_dim != 128)
+        return model_fail(PYXIS_EINVAL, "pyxis_cuda_model_create: the decode attention kernel takes head_dim 64 or 128");
+    if (c.n_q_heads / c.n_kv_heads > kAttnMaxG)
+        return model_fail(PYXIS_EINVAL, "pyxis_cuda_model_create: more than 4 query heads per kv head");
     Guard g(ctx->device);
     auto *m = new (std::nothrow) pyxis_cuda_model();
     if (!m) return model_fail(PYXIS_ENOMEM, "host allocation failed");
@@ -349,6 +523,12 @@ extern "C" int pyxis_cuda_model_create(pyxis_cuda_ctx *ctx, const pyxis_model_co
     m->q_dim = c.n_q_heads * c.head_dim;
     m->kv_dim = c.n_kv_heads * c.head_dim;
     m->layers.resize(c.n_layers);
+    // attention key splits: enough (kv head, split) CTAs to cover the SMs, >= 16 keys per split
+    m->attn_splits = std::max(1, std::min({ctx->num_sms / c.n_kv_heads, (c.max_seq + 15) / 16, 64}));
+    if (attention_smem(m) > 200 * 1024) {
+        delete m;
+        return model_fail(PYXIS_EINVAL, "pyxis_cuda_model_create: max_seq too large for the decode attention kernel");
+    }
     const size_t H = c.hidden, half = c.head_dim / 2;
     cudaError_t e = cudaSuccess;
     auto A = [&](auto **p, size_t n) {
@@ -365,6 +545,9 @@ extern "C" int pyxis_cuda_model_create(pyxis_cuda_ctx *ctx, const pyxis_model_co
     A(&m->kcache, (size_t)c.n_layers * c.max_seq * m->kv_dim);
     A(&m->vcache, (size_t)c.n_layers * c.max_seq * m->kv_dim);
     A(&m->x, H);
+    A(&m->x2, H);
+    A(&m->part, (size_t)c.n_kv_heads * m->attn_splits * (c.n_q_heads / c.n_kv_heads) * (c.head_dim + 2));
+    A(&m->tickets, (size_t)c.n_kv_heads);
     A(&m->h, H);
     A(&m->qkv, (size_t)m->q_dim + 2 * m->kv_dim);
     A(&m->q, (size_t)m->q_dim);
@@ -380,6 +563,11 @@ extern "C" int pyxis_cuda_model_create(pyxis_cuda_ctx *ctx, const pyxis_model_co
     if (e != cudaSuccess) {
         pyxis_cuda_model_free(m);
         return model_fail(PYXIS_ENOMEM, cudaGetErrorString(e));
+    }
+    e = cudaMemset(m->tickets, 0, (size_t)c.n_kv_heads * sizeof(unsigned));
+    if (e != cudaSuccess) {
+        pyxis_cuda_model_free(m);
+        return model_fail(PYXIS_ECUDA, cudaGetErrorString(e));
     }
     std::vector<float> cs((size_t)c.max_seq * half), sn((size_t)c.max_seq * half);
     pyxis_rope_table(c.rope_theta, c.head_dim, c.max_seq, cs.data(), sn.data());
@@ -464,9 +652,11 @@ extern "C" int pyxis_cuda_model_generate(pyxis_cuda_model *m, const int32_t *pro
         // Every kernel of the step asks for the same (maximum) shared-memory carveout as the
         // GEMV kernels, so the SMs never re-split L1 / shared memory between graph nodes.
         const void *small_kernels[] = {(const void *)embed_kernel, (const void *)add_rmsnorm_kernel,
-                                       (const void *)qk_rope_append_kernel, (const void *)attention_decode_kernel,
+                                       (const void *)attention_step_kernel<2>, (const void *)attention_step_kernel<4>,
                                        (const void *)silu_mul_kernel, (const void *)advance_kernel};
         for (const void *k : small_kernels) cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        for (const void *k : {(const void *)attention_step_kernel<2>, (const void *)attention_step_kernel<4>})
+            cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attention_smem(m));
         set_argmax_carveout_max();
         // Warm every kernel once outside capture (first-use attribute setting and occupancy
         // queries), then capture the step.

@@ -15,6 +15,7 @@
 // 128-byte swizzled: the 16-byte unit u of each 128-byte row r sits at u ^ (r % 8), so the eight
 // lanes of one shared-memory phase, reading eight consecutive chunks, hit eight different banks.
 #include <algorithm>
+#include <cstring>
 
 #include "kernels.h"
 #include "tc_ptx.cuh"
@@ -49,6 +50,7 @@ struct BatchParams {
     int box_rows;          // rows of 32 floats per box (multiple of 8)
     uint32_t tok_stride;   // bytes per token in shared memory (multiple of 1024)
     int *err;
+    GemvPrologue pro;      // batch 1: x computed in every CTA instead of copied (kind != kProNone)
 };
 
 template <int QT>
@@ -65,7 +67,57 @@ struct Codes<kQInt4> {
 // byte offset of logical offset `off` in a 1024-byte aligned, 128-byte swizzled region
 PYXIS_DEVINL uint32_t swz128(uint32_t off) { return off ^ (((off >> 7) & 7u) << 4); }
 
-template <int QT, int B, int SMODE>
+// x of a batch-1 product computed from the previous step's outputs, written into token 0's
+// swizzled tile: residual add + RMSNorm (src/transformer.rs:40-42,54-59, src/rmsnorm.rs:11-20:
+// x += delta; h = x * ((1 / sqrt(mean(x^2) + eps)) * w)), CTA 0 storing the new residual, or
+// SiLU(gate) * up (src/ffn.rs:39-41,52-54) from the stacked [gate; up] output.
+template <int PRO>
+PYXIS_DEVINL void run_prologue(const BatchParams &p, uint8_t *xs, float *red) {
+    const GemvPrologue &pr = p.pro;
+    const int K = p.K, nq = K / 4;
+    if constexpr (PRO == kProAddNorm) {
+        float ss = 0.f;
+        for (int k4 = threadIdx.x; k4 < nq; k4 += blockDim.x) {
+            float4 v = __ldg(reinterpret_cast<const float4 *>(pr.x) + k4);
+            if (pr.delta) {
+                const float4 d = __ldg(reinterpret_cast<const float4 *>(pr.delta) + k4);
+                v = make_float4(__fadd_rn(v.x, d.x), __fadd_rn(v.y, d.y), __fadd_rn(v.z, d.z), __fadd_rn(v.w, d.w));
+                if (blockIdx.x == 0) reinterpret_cast<float4 *>(pr.xout)[k4] = v;
+            }
+            *reinterpret_cast<float4 *>(xs + swz128((uint32_t)k4 * 16)) = v;
+            ss = __fadd_rn(ss, __fmul_rn(v.x, v.x));
+            ss = __fadd_rn(ss, __fmul_rn(v.y, v.y));
+            ss = __fadd_rn(ss, __fmul_rn(v.z, v.z));
+            ss = __fadd_rn(ss, __fmul_rn(v.w, v.w));
+        }
+        ss = warp_sum(ss);
+        const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+        if ((threadIdx.x & 31) == 0) red[warp] = ss;
+        __syncthreads();
+        float tot = 0.f;
+        for (int i = 0; i < nw; ++i) tot = __fadd_rn(tot, red[i]);
+        const float factor = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)K), pr.eps)));
+        for (int k4 = threadIdx.x; k4 < nq; k4 += blockDim.x) {
+            float4 *px = reinterpret_cast<float4 *>(xs + swz128((uint32_t)k4 * 16));
+            float4 v = *px;
+            const float4 w = __ldg(reinterpret_cast<const float4 *>(pr.w) + k4);
+            v = make_float4(__fmul_rn(v.x, __fmul_rn(factor, w.x)), __fmul_rn(v.y, __fmul_rn(factor, w.y)),
+                            __fmul_rn(v.z, __fmul_rn(factor, w.z)), __fmul_rn(v.w, __fmul_rn(factor, w.w)));
+            *px = v;
+        }
+    } else {
+        auto silu_mul = [](float g, float u) { return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u); };
+        for (int k4 = threadIdx.x; k4 < nq; k4 += blockDim.x) {
+            const float4 g = __ldg(reinterpret_cast<const float4 *>(pr.x) + k4);
+            const float4 u = __ldg(reinterpret_cast<const float4 *>(pr.x + K) + k4);
+            *reinterpret_cast<float4 *>(xs + swz128((uint32_t)k4 * 16)) =
+                make_float4(silu_mul(g.x, u.x), silu_mul(g.y, u.y), silu_mul(g.z, u.z), silu_mul(g.w, u.w));
+        }
+    }
+    __syncthreads();
+}
+
+template <int QT, int B, int SMODE, int PRO>
 __global__ void __launch_bounds__(max_warps(B) * 32, 1)
     gemv_batch_kernel(const __grid_constant__ CUtensorMap tm_x, const BatchParams p) {
     constexpr int EPC = Codes<QT>::EPC;
@@ -97,6 +149,11 @@ __global__ void __launch_bounds__(max_warps(B) * 32, 1)
     int it = blockIdx.x;
     if (it < p.items && row0_of(it) < p.N && c0 < p.chunks) load(row0_of(it), c0);
 
+    if constexpr (PRO != kProNone) {
+        pdl_wait();  // the prologue's inputs come from the previous kernels
+        pdl_trigger();
+        run_prologue<PRO>(p, xs, red);
+    } else {
     if (threadIdx.x == 0) {
         abort_flag = 0;
         tc::mbar_init(bar, 1);
@@ -122,6 +179,7 @@ __global__ void __launch_bounds__(max_warps(B) * 32, 1)
             tc::mbar_wait_bounded(bar, 0, &no_abort, p.err, kErrX, kTimeoutNs);
         }
         return;
+    }
     }
 
     int buf = 0;
@@ -249,9 +307,9 @@ Shape shape_for(const QMatrix &w, size_t B, int num_sms) {
     return sh;
 }
 
-template <int QT, int B, int SMODE>
+template <int QT, int B, int SMODE, int PRO = kProNone>
 cudaError_t run(const CUtensorMap &tm, const BatchParams &p, const Shape &sh, int num_sms, cudaStream_t st) {
-    auto kern = gemv_batch_kernel<QT, B, SMODE>;
+    auto kern = gemv_batch_kernel<QT, B, SMODE, PRO>;
     static const cudaError_t attr =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
     if (attr != cudaSuccess) return attr;
@@ -279,24 +337,9 @@ cudaError_t dispatch(size_t B, const CUtensorMap &tm, const BatchParams &p, cons
 
 bool gemv_batch_supported(const QMatrix &w, size_t B, int num_sms) { return shape_for(w, B, num_sms).ok; }
 
-cudaError_t launch_gemv_batch(const QMatrix &w, const float *X, size_t B, size_t ldx, float *Y, size_t ldy,
-                              int *err, int num_sms, cudaStream_t st) {
-    const Shape sh = shape_for(w, B, num_sms);
-    if (!sh.ok) return cudaErrorInvalidValue;
-    if ((reinterpret_cast<uintptr_t>(X) & 15) || (B > 1 && ldx % 4)) return cudaErrorInvalidValue;
-    auto fn = tensor_map_encoder();
-    if (!fn) return cudaErrorNotSupported;
-    // x as [B][K/32][32] f32: one 128-byte row per 32 values, 128-byte swizzle
-    CUtensorMap tm;
-    const cuuint64_t rows = w.K / 32;
-    cuuint64_t dims[3] = {32, rows, (cuuint64_t)B};
-    cuuint64_t strides[2] = {128, (cuuint64_t)(B > 1 ? ldx : w.K) * sizeof(float)};
-    cuuint32_t box[3] = {32, (cuuint32_t)sh.box_rows, 1};
-    cuuint32_t es[3] = {1, 1, 1};
-    if (fn(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(X), dims, strides, box, es,
-           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-        return cudaErrorInvalidValue;
+namespace {
+
+BatchParams make_params(const QMatrix &w, const Shape &sh, float *Y, size_t ldy, int *err) {
     const int epc = w.qtype == kQInt8 ? 16 : 32;
     const bool chunk_mode = w.block_size != w.K;
     BatchParams p{};
@@ -317,11 +360,71 @@ cudaError_t launch_gemv_batch(const QMatrix &w, const float *X, size_t B, size_t
     p.box_rows = sh.box_rows;
     p.tok_stride = sh.tok_stride;
     p.err = err;
+    return p;
+}
+
+}  // namespace
+
+cudaError_t launch_gemv_batch(const QMatrix &w, const float *X, size_t B, size_t ldx, float *Y, size_t ldy,
+                              int *err, int num_sms, cudaStream_t st) {
+    const Shape sh = shape_for(w, B, num_sms);
+    if (!sh.ok) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(X) & 15) || (B > 1 && ldx % 4)) return cudaErrorInvalidValue;
+    auto fn = tensor_map_encoder();
+    if (!fn) return cudaErrorNotSupported;
+    // x as [B][K/32][32] f32: one 128-byte row per 32 values, 128-byte swizzle
+    CUtensorMap tm;
+    const cuuint64_t rows = w.K / 32;
+    cuuint64_t dims[3] = {32, rows, (cuuint64_t)B};
+    cuuint64_t strides[2] = {128, (cuuint64_t)(B > 1 ? ldx : w.K) * sizeof(float)};
+    cuuint32_t box[3] = {32, (cuuint32_t)sh.box_rows, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    if (fn(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(X), dims, strides, box, es,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return cudaErrorInvalidValue;
+    const BatchParams p = make_params(w, sh, Y, ldy, err);
+    const bool chunk_mode = w.block_size != w.K;
     if (w.qtype == kQInt8)
         return chunk_mode ? dispatch<kQInt8, kScaleChunk>(B, tm, p, sh, num_sms, st)
                           : dispatch<kQInt8, kScaleRow>(B, tm, p, sh, num_sms, st);
     return chunk_mode ? dispatch<kQInt4, kScaleChunk>(B, tm, p, sh, num_sms, st)
                       : dispatch<kQInt4, kScaleRow>(B, tm, p, sh, num_sms, st);
+}
+
+bool gemv_batch_pro_supported(const QMatrix &w, const GemvPrologue &pro, int num_sms) {
+    if (pro.kind != kProAddNorm && pro.kind != kProSiluMul) return false;
+    if (!pro.x || (reinterpret_cast<uintptr_t>(pro.x) & 15)) return false;
+    if (pro.kind == kProAddNorm) {
+        if (!pro.w || (reinterpret_cast<uintptr_t>(pro.w) & 15)) return false;
+        if (pro.delta && ((reinterpret_cast<uintptr_t>(pro.delta) & 15) || !pro.xout ||
+                          (reinterpret_cast<uintptr_t>(pro.xout) & 15)))
+            return false;
+    }
+    return shape_for(w, 1, num_sms).ok;
+}
+
+cudaError_t launch_gemv_batch_pro(const QMatrix &w, const GemvPrologue &pro, float *Y, int *err, int num_sms,
+                                  cudaStream_t st) {
+    if (!gemv_batch_pro_supported(w, pro, num_sms)) return cudaErrorInvalidValue;
+    const Shape sh = shape_for(w, 1, num_sms);
+    BatchParams p = make_params(w, sh, Y, w.N, err);
+    p.pro = pro;
+    CUtensorMap tm;  // not read: the prologue writes x itself
+    memset(&tm, 0, sizeof(tm));
+    const bool chunk_mode = w.block_size != w.K;
+    if (pro.kind == kProAddNorm) {
+        if (w.qtype == kQInt8)
+            return chunk_mode ? run<kQInt8, 1, kScaleChunk, kProAddNorm>(tm, p, sh, num_sms, st)
+                              : run<kQInt8, 1, kScaleRow, kProAddNorm>(tm, p, sh, num_sms, st);
+        return chunk_mode ? run<kQInt4, 1, kScaleChunk, kProAddNorm>(tm, p, sh, num_sms, st)
+                          : run<kQInt4, 1, kScaleRow, kProAddNorm>(tm, p, sh, num_sms, st);
+    }
+    if (w.qtype == kQInt8)
+        return chunk_mode ? run<kQInt8, 1, kScaleChunk, kProSiluMul>(tm, p, sh, num_sms, st)
+                          : run<kQInt8, 1, kScaleRow, kProSiluMul>(tm, p, sh, num_sms, st);
+    return chunk_mode ? run<kQInt4, 1, kScaleChunk, kProSiluMul>(tm, p, sh, num_sms, st)
+                      : run<kQInt4, 1, kScaleRow, kProSiluMul>(tm, p, sh, num_sms, st);
 }
 
 }  // namespace pyxis

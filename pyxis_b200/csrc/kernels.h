@@ -34,6 +34,21 @@ bool gemv_batch_supported(const QMatrix &w, size_t B, int num_sms);
 cudaError_t launch_gemv_batch(const QMatrix &w, const float *X, size_t B, size_t ldx, float *Y, size_t ldy,
                               int *err, int num_sms, cudaStream_t st);
 
+// Batch-1 products whose x is computed inside the GEMV from the previous step's outputs:
+// kProAddNorm: x' = x + delta (delta may be NULL; CTA 0 stores x' to xout, which must not alias
+// x), then RMSNorm with weight w; kProSiluMul: SiLU(x[0:K]) * x[K:2K].  All pointers 16-byte
+// aligned.
+enum { kProNone = 0, kProAddNorm = 1, kProSiluMul = 2 };
+struct GemvPrologue {
+    int kind = kProNone;
+    const float *x = nullptr, *delta = nullptr, *w = nullptr;
+    float *xout = nullptr;
+    float eps = 0.f;
+};
+bool gemv_batch_pro_supported(const QMatrix &w, const GemvPrologue &pro, int num_sms);
+cudaError_t launch_gemv_batch_pro(const QMatrix &w, const GemvPrologue &pro, float *Y, int *err, int num_sms,
+                                  cudaStream_t st);
+
 // Name of the kernel launch_gemv would pick (for tests and the bench's launch accounting).
 const char *gemv_kernel_name(const QMatrix &w, size_t B, int num_sms);
 
