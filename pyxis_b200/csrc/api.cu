@@ -8,6 +8,7 @@
 
 #include "../../include/pyxis_cuda.h"
 #include "argmax.h"
+#include "common.cuh"
 #include "ctx.h"
 #include "kernels.h"
 
@@ -142,6 +143,10 @@ bool use_gemv_tc(const pyxis_cuda_ctx *ctx, const QMatrix &q, size_t b, const fl
 int pyxis::run_matmul(pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, const float *X, size_t M, size_t ldx,
                       size_t out_features, size_t in_features, float *Y, size_t ldy, void *workspace,
                       size_t workspace_bytes, cudaStream_t st) {
+    // Programmatic dependent launch: a GEMV may start while the kernel before it on the stream
+    // finishes, streaming its (immutable) weights; every kernel launched this way reads x and
+    // writes y only after griddepcontrol.wait, i.e. after its predecessor has completed.
+    PdlScope pdl;
     QMatrix q = qmatrix(w, out_features, in_features);
     if (use_gemm_tc(q, M, X, ldx)) {
         const size_t need = gemm_tc_workspace_bytes(M, in_features);

@@ -96,9 +96,11 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float *__rest
 // Grid (splits, n_kv): CTA (s, h) handles the G = n_q / n_kv query heads of kv head h over the
 // keys [s*len/S, (s+1)*len/S).  Every CTA normalises and rotates its heads' q and the new k itself
 // (a few hundred flops), the CTA holding key `pos` writes k and v to the cache, and the newest
-// key is taken from shared memory, so no CTA reads a cache row another one is writing.  Each CTA
-// leaves (max, sum of exp, unnormalised sum_j p_j v_j) per head in `part`; the last CTA of a kv
-// head (ticket) rescales and adds the splits in order and re-arms the ticket.
+// key is taken from shared memory, so no CTA reads a cache row another one is writing.  Within a
+// CTA each warp takes every 8th key, streams its K and V rows together (the first ones before
+// griddepcontrol.wait) and keeps a running (max, sum of exp, sum of p v) per query head; the
+// warps, then the splits (the last CTA of a kv head, by ticket), are rescaled to a common max and
+// added in a fixed order.  The softmax is the reference's up to the order of the f32 sums.
 // Lane l of a warp holds head elements [l*EPL, (l+1)*EPL); RoPE pairs element i with i + hd/2,
 // which sits in lane l ^ 16.
 constexpr int kAttnThreads = 256;
@@ -146,28 +148,42 @@ __global__ void __launch_bounds__(kAttnThreads)
                           const float *__restrict__ rsin, const int *__restrict__ d_pos, int n_q, int n_kv, float eps,
                           float *__restrict__ kcache, float *__restrict__ vcache, float *__restrict__ part,
                           unsigned *__restrict__ tickets, float *__restrict__ out) {
-    constexpr int HD = 32 * EPL;
-    extern __shared__ float sm[];  // q [G][HD] | knew [HD] | vnew [HD] | p [G][chunk] | flag
+    constexpr int HD = 32 * EPL, PF = 4;  // keys whose rows a warp has in flight at once
+    constexpr int NW = kAttnThreads / 32;
+    __shared__ float qs[kAttnMaxG][HD], knew[HD], vnew[HD];
+    __shared__ float wpart[NW][kAttnMaxG][HD + 2];  // per-warp (max, sum, acc[HD])
+    __shared__ int flag;
     const int G = n_q / n_kv;
     const int S = gridDim.x, s = blockIdx.x, h = blockIdx.y;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kv_dim = n_kv * HD, q_dim = n_q * HD;
-    pdl_wait();
-    pdl_trigger();
+    // The position and the cache rows below it were written by earlier steps (earlier graph
+    // launches): read them, and this warp's first keys, before waiting on the q|k|v projection.
     const int pos = *d_pos;
     const int len = pos + 1;
     const int j0 = (int)((long long)s * len / S), j1 = (int)((long long)(s + 1) * len / S);
-    const int chunk = (int)(((long long)len + S - 1) / S);
-    float *qs = sm, *knew = qs + G * HD, *vnew = knew + HD, *pr = vnew + HD;
-    volatile int *flag = reinterpret_cast<volatile int *>(pr + G * chunk);
+    float kr[PF][EPL], vr[PF][EPL];
+    auto fetch = [&](int jb) {
+#pragma unroll
+        for (int u = 0; u < PF; ++u) {
+            const int j = jb + u * NW;
+            if (j < j1 && j < pos) {
+                load_head<EPL>(kcache + (size_t)j * kv_dim + (size_t)h * HD + lane * EPL, kr[u]);
+                load_head<EPL>(vcache + (size_t)j * kv_dim + (size_t)h * HD + lane * EPL, vr[u]);
+            }
+        }
+    };
+    fetch(j0 + warp);
+    pdl_wait();
+    pdl_trigger();
 
-    // heads of this kv group: warps 0..G-1 take the q heads, warp G the new k, warp G+1 the new v
+    // heads of this kv group: warps 0..G-1 the q heads, warp G the new k, warp G+1 the new v
     if (warp < G) {
         float v[EPL];
         load_head<EPL>(qkv + (size_t)(h * G + warp) * HD + lane * EPL, v);
         norm_rope<EPL>(v, q_norm, rcos, rsin, pos, eps, lane);
 #pragma unroll
-        for (int t = 0; t < EPL; ++t) qs[warp * HD + lane * EPL + t] = v[t];
+        for (int t = 0; t < EPL; ++t) qs[warp][lane * EPL + t] = v[t];
     } else if (warp == G) {
         float v[EPL];
         load_head<EPL>(qkv + q_dim + (size_t)h * HD + lane * EPL, v);
@@ -188,112 +204,112 @@ __global__ void __launch_bounds__(kAttnThreads)
     }
     __syncthreads();
 
-    // scores of this split's keys, one warp per key, four keys' loads in flight per warp
+    // this warp's keys j0 + warp, j0 + warp + NW, ...: online softmax per query head
     const float scale = sqrtf((float)HD);
-    float qr[kAttnMaxG][EPL];
+    float qr[kAttnMaxG][EPL], acc[kAttnMaxG][EPL], m[kAttnMaxG], l[kAttnMaxG];
 #pragma unroll
-    for (int g = 0; g < kAttnMaxG; ++g)
+    for (int g = 0; g < kAttnMaxG; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.f;
 #pragma unroll
         for (int t = 0; t < EPL; ++t) {
+            acc[g][t] = 0.f;
             qr[g][t] = 0.f;
-            if (g < G) qr[g][t] = qs[g * HD + lane * EPL + t];
+            if (g < G) qr[g][t] = qs[g][lane * EPL + t];
         }
-    for (int jb = j0 + warp; jb < j1; jb += 4 * nw) {
-        float kr[4][EPL];
+    }
+    for (int jb = j0 + warp; jb < j1; jb += PF * NW) {
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int j = jb + u * nw;
-            if (j < j1) {
-                const float *k = j == pos ? knew : kcache + (size_t)j * kv_dim + (size_t)h * HD;
-                load_head<EPL>(k + lane * EPL, kr[u]);
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int j = jb + u * nw;
+        for (int u = 0; u < PF; ++u) {
+            const int j = jb + u * NW;
             if (j >= j1) break;  // uniform across the warp
+            if (j == pos) {
+#pragma unroll
+                for (int t = 0; t < EPL; ++t) {
+                    kr[u][t] = knew[lane * EPL + t];
+                    vr[u][t] = vnew[lane * EPL + t];
+                }
+            }
 #pragma unroll
             for (int g = 0; g < kAttnMaxG; ++g) {
                 if (g >= G) break;
                 float dot = 0.f;
 #pragma unroll
                 for (int t = 0; t < EPL; ++t) dot = __fadd_rn(dot, __fmul_rn(qr[g][t], kr[u][t]));
-                dot = warp_sum(dot);
-                if (lane == 0) pr[g * chunk + (j - j0)] = __fdiv_rn(dot, scale);
+                const float sc = __fdiv_rn(warp_sum(dot), scale);
+                const float mn = fmaxf(m[g], sc);
+                const float c = expf(__fsub_rn(m[g], mn));  // 0 on the first key (m = -inf)
+                const float pj = expf(__fsub_rn(sc, mn));
+                l[g] = __fadd_rn(__fmul_rn(l[g], c), pj);
+#pragma unroll
+                for (int t = 0; t < EPL; ++t) acc[g][t] = __fadd_rn(__fmul_rn(acc[g][t], c), __fmul_rn(pj, vr[u][t]));
+                m[g] = mn;
             }
         }
+        fetch(jb + PF * NW);
+    }
+#pragma unroll
+    for (int g = 0; g < kAttnMaxG; ++g) {
+        if (g >= G) break;
+        if (lane == 0) {
+            wpart[warp][g][0] = m[g];
+            wpart[warp][g][1] = l[g];
+        }
+#pragma unroll
+        for (int t = 0; t < EPL; ++t) wpart[warp][g][2 + lane * EPL + t] = acc[g][t];
     }
     __syncthreads();
 
-    // per head: local max and exp, then sum_j p_j v_j over this split (v rows read coalesced)
-    const int n = j1 - j0;
+    // this split: the warps' partials rescaled to their common max and added in warp order
     float *mine = part + ((size_t)h * S + s) * G * (HD + 2);
-    for (int g = warp; g < G; g += nw) {
-        float m = -INFINITY;
-        for (int j = lane; j < n; j += 32) m = fmaxf(m, pr[g * chunk + j]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float l = 0.f;
-        for (int j = lane; j < n; j += 32) {
-            const float e = expf(__fsub_rn(pr[g * chunk + j], m));
-            pr[g * chunk + j] = e;
-            l = __fadd_rn(l, e);
-        }
-        l = warp_sum(l);
-        if (lane == 0) {
-            mine[g * (HD + 2)] = m;
-            mine[g * (HD + 2) + 1] = l;
-        }
-    }
-    __syncthreads();
     for (int idx = threadIdx.x; idx < G * HD; idx += blockDim.x) {
         const int g = idx / HD, d = idx - g * HD;
-        const float *vcol = vcache + (size_t)h * HD + d;
-        float acc = 0.f;
-        int j = 0;
-        for (; j + 8 <= n; j += 8) {
-            float vv[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int jj = j0 + j + u;
-                if (jj == pos) vv[u] = vnew[d];
-                else vv[u] = vcol[(size_t)jj * kv_dim];
+        float M = -INFINITY;
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, wpart[w][g][0]);
+        float L = 0.f, a = 0.f;
+        if (M != -INFINITY) {
+            for (int w = 0; w < NW; ++w) {
+                const float mw = wpart[w][g][0];
+                if (mw == -INFINITY) continue;  // a warp without keys
+                const float c = expf(__fsub_rn(mw, M));
+                L = __fadd_rn(L, __fmul_rn(wpart[w][g][1], c));
+                a = __fadd_rn(a, __fmul_rn(wpart[w][g][2 + d], c));
             }
-#pragma unroll
-            for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, __fmul_rn(pr[g * chunk + j + u], vv[u]));
         }
-        for (; j < n; ++j) {
-            const int jj = j0 + j;
-            float vj;
-            if (jj == pos) vj = vnew[d];
-            else vj = vcol[(size_t)jj * kv_dim];
-            acc = __fadd_rn(acc, __fmul_rn(pr[g * chunk + j], vj));
+        if (S == 1) {
+            out[(size_t)(h * G + g) * HD + d] = __fdiv_rn(a, L);
+        } else {
+            if (d == 0) {
+                mine[g * (HD + 2)] = M;
+                mine[g * (HD + 2) + 1] = L;
+            }
+            mine[g * (HD + 2) + 2 + d] = a;
         }
-        mine[g * (HD + 2) + 2 + d] = acc;
     }
+    if (S == 1) return;
 
     // the last CTA of this kv head combines the splits in order
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) *flag = atomicAdd(&tickets[h], 1u) == (unsigned)(S - 1);
+    if (threadIdx.x == 0) flag = atomicAdd(&tickets[h], 1u) == (unsigned)(S - 1);
     __syncthreads();
-    if (!*flag) return;
+    if (!flag) return;
     __threadfence();
     const float *all = part + (size_t)h * S * G * (HD + 2);
     for (int idx = threadIdx.x; idx < G * HD; idx += blockDim.x) {
         const int g = idx / HD, d = idx - g * HD;
         float M = -INFINITY;
         for (int t = 0; t < S; ++t) M = fmaxf(M, __ldcg(all + ((size_t)t * G + g) * (HD + 2)));
-        float L = 0.f, acc = 0.f;
+        float L = 0.f, a = 0.f;
         for (int t = 0; t < S; ++t) {
             const float *pt = all + ((size_t)t * G + g) * (HD + 2);
             const float mt = __ldcg(pt);
             if (mt == -INFINITY) continue;  // an empty split
-            const float w = expf(__fsub_rn(mt, M));
-            L = __fadd_rn(L, __fmul_rn(__ldcg(pt + 1), w));
-            acc = __fadd_rn(acc, __fmul_rn(__ldcg(pt + 2 + d), w));
+            const float c = expf(__fsub_rn(mt, M));
+            L = __fadd_rn(L, __fmul_rn(__ldcg(pt + 1), c));
+            a = __fadd_rn(a, __fmul_rn(__ldcg(pt + 2 + d), c));
         }
-        out[(size_t)(h * G + g) * HD + d] = __fdiv_rn(acc, L);
+        out[(size_t)(h * G + g) * HD + d] = __fdiv_rn(a, L);
     }
     if (threadIdx.x == 0) tickets[h] = 0;
 }
@@ -428,13 +444,6 @@ int silu_gemv(pyxis_cuda_model *m, const pyxis_cuda_weights *w, float *y, cudaSt
     return run_matmul(m->ctx, w, m->act, 1, c.ffn, c.hidden, c.ffn, y, c.hidden, nullptr, 0, st);
 }
 
-size_t attention_smem(const pyxis_cuda_model *m) {
-    const pyxis_model_config &c = m->cfg;
-    const int G = c.n_q_heads / c.n_kv_heads;
-    const int chunk = (c.max_seq + m->attn_splits - 1) / m->attn_splits;
-    return ((size_t)G * c.head_dim + 2 * (size_t)c.head_dim + (size_t)G * chunk + 4) * sizeof(float);
-}
-
 // One decode step on `st` (what the graph holds).
 int enqueue_step(pyxis_cuda_model *m, cudaStream_t st) {
     const pyxis_model_config &c = m->cfg;
@@ -445,7 +454,6 @@ int enqueue_step(pyxis_cuda_model *m, cudaStream_t st) {
                                    (const int *)m->d_token, c.vocab, H, m->x);
     if (le != cudaSuccess) return model_fail(PYXIS_ECUDA, cudaGetErrorString(le));
     float *xr = m->x, *xw = m->x2;  // residual stream: read xr, the fused norm writes xr + delta to xw
-    const size_t asmem = attention_smem(m);
     for (int l = 0; l < c.n_layers; ++l) {
         const auto &L = m->layers[l];
         float *kc = m->kcache + (size_t)l * c.max_seq * m->kv_dim;
@@ -455,7 +463,7 @@ int enqueue_step(pyxis_cuda_model *m, cudaStream_t st) {
         if (rc) return rc;
         if (l) std::swap(xr, xw);
         auto kern = c.head_dim == 128 ? attention_step_kernel<4> : attention_step_kernel<2>;
-        le = launch_kernel(kern, dim3(m->attn_splits, c.n_kv_heads), dim3(kAttnThreads), asmem, st,
+        le = launch_kernel(kern, dim3(m->attn_splits, c.n_kv_heads), dim3(kAttnThreads), 0, st,
                            (const float *)m->qkv, (const float *)L.q_norm, (const float *)L.k_norm,
                            (const float *)m->rope_cos, (const float *)m->rope_sin, (const int *)m->d_pos, c.n_q_heads,
                            c.n_kv_heads, c.rms_eps, kc, vc, m->part, m->tickets, m->attn);
@@ -525,10 +533,6 @@ extern "C" int pyxis_cuda_model_create(pyxis_cuda_ctx *ctx, const pyxis_model_co
     m->layers.resize(c.n_layers);
     // attention key splits: enough (kv head, split) CTAs to cover the SMs, >= 16 keys per split
     m->attn_splits = std::max(1, std::min({ctx->num_sms / c.n_kv_heads, (c.max_seq + 15) / 16, 64}));
-    if (attention_smem(m) > 200 * 1024) {
-        delete m;
-        return model_fail(PYXIS_EINVAL, "pyxis_cuda_model_create: max_seq too large for the decode attention kernel");
-    }
     const size_t H = c.hidden, half = c.head_dim / 2;
     cudaError_t e = cudaSuccess;
     auto A = [&](auto **p, size_t n) {
@@ -655,8 +659,6 @@ extern "C" int pyxis_cuda_model_generate(pyxis_cuda_model *m, const int32_t *pro
                                        (const void *)attention_step_kernel<2>, (const void *)attention_step_kernel<4>,
                                        (const void *)silu_mul_kernel, (const void *)advance_kernel};
         for (const void *k : small_kernels) cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-        for (const void *k : {(const void *)attention_step_kernel<2>, (const void *)attention_step_kernel<4>})
-            cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attention_smem(m));
         set_argmax_carveout_max();
         // Warm every kernel once outside capture (first-use attribute setting and occupancy
         // queries), then capture the step.

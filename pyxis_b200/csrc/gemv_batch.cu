@@ -71,47 +71,93 @@ PYXIS_DEVINL uint32_t swz128(uint32_t off) { return off ^ (((off >> 7) & 7u) << 
 // swizzled tile: residual add + RMSNorm (src/transformer.rs:40-42,54-59, src/rmsnorm.rs:11-20:
 // x += delta; h = x * ((1 / sqrt(mean(x^2) + eps)) * w)), CTA 0 storing the new residual, or
 // SiLU(gate) * up (src/ffn.rs:39-41,52-54) from the stacked [gate; up] output.
+// Each thread handles quads k4 = tid + u * blockDim (u < PQ) at once, every load issued before
+// the first use; K <= 4 * PQ * blockDim is one round (the decode shapes).  The norm weight does not
+// depend on the previous kernel and is read before griddepcontrol.wait.
 template <int PRO>
 PYXIS_DEVINL void run_prologue(const BatchParams &p, uint8_t *xs, float *red) {
+    constexpr int PQ = 4;
     const GemvPrologue &pr = p.pro;
-    const int K = p.K, nq = K / 4;
+    const int K = p.K, nq = K / 4, nt = blockDim.x;
+    const float4 *x4 = reinterpret_cast<const float4 *>(pr.x);
     if constexpr (PRO == kProAddNorm) {
+        const float4 *d4 = reinterpret_cast<const float4 *>(pr.delta);
+        const float4 *w4 = reinterpret_cast<const float4 *>(pr.w);
+        float4 wv[PQ];
+#pragma unroll
+        for (int u = 0; u < PQ; ++u)
+            if (threadIdx.x + u * nt < nq) wv[u] = __ldg(w4 + threadIdx.x + u * nt);
+        pdl_wait();
+        pdl_trigger();
         float ss = 0.f;
-        for (int k4 = threadIdx.x; k4 < nq; k4 += blockDim.x) {
-            float4 v = __ldg(reinterpret_cast<const float4 *>(pr.x) + k4);
-            if (pr.delta) {
-                const float4 d = __ldg(reinterpret_cast<const float4 *>(pr.delta) + k4);
-                v = make_float4(__fadd_rn(v.x, d.x), __fadd_rn(v.y, d.y), __fadd_rn(v.z, d.z), __fadd_rn(v.w, d.w));
-                if (blockIdx.x == 0) reinterpret_cast<float4 *>(pr.xout)[k4] = v;
+        for (int base = threadIdx.x; base < nq; base += PQ * nt) {
+            float4 v[PQ], d[PQ];
+#pragma unroll
+            for (int u = 0; u < PQ; ++u) {
+                const int k4 = base + u * nt;
+                if (k4 < nq) {
+                    v[u] = __ldg(x4 + k4);
+                    if (pr.delta) d[u] = __ldg(d4 + k4);
+                }
             }
-            *reinterpret_cast<float4 *>(xs + swz128((uint32_t)k4 * 16)) = v;
-            ss = __fadd_rn(ss, __fmul_rn(v.x, v.x));
-            ss = __fadd_rn(ss, __fmul_rn(v.y, v.y));
-            ss = __fadd_rn(ss, __fmul_rn(v.z, v.z));
-            ss = __fadd_rn(ss, __fmul_rn(v.w, v.w));
+#pragma unroll
+            for (int u = 0; u < PQ; ++u) {
+                const int k4 = base + u * nt;
+                if (k4 >= nq) break;
+                if (pr.delta) {
+                    v[u] = make_float4(__fadd_rn(v[u].x, d[u].x), __fadd_rn(v[u].y, d[u].y), __fadd_rn(v[u].z, d[u].z),
+                                       __fadd_rn(v[u].w, d[u].w));
+                    if (blockIdx.x == 0) reinterpret_cast<float4 *>(pr.xout)[k4] = v[u];
+                }
+                *reinterpret_cast<float4 *>(xs + swz128((uint32_t)k4 * 16)) = v[u];
+                ss = __fadd_rn(ss, __fmul_rn(v[u].x, v[u].x));
+                ss = __fadd_rn(ss, __fmul_rn(v[u].y, v[u].y));
+                ss = __fadd_rn(ss, __fmul_rn(v[u].z, v[u].z));
+                ss = __fadd_rn(ss, __fmul_rn(v[u].w, v[u].w));
+            }
         }
         ss = warp_sum(ss);
-        const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+        const int warp = threadIdx.x >> 5, nw = nt >> 5;
         if ((threadIdx.x & 31) == 0) red[warp] = ss;
         __syncthreads();
         float tot = 0.f;
         for (int i = 0; i < nw; ++i) tot = __fadd_rn(tot, red[i]);
         const float factor = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)K), pr.eps)));
-        for (int k4 = threadIdx.x; k4 < nq; k4 += blockDim.x) {
-            float4 *px = reinterpret_cast<float4 *>(xs + swz128((uint32_t)k4 * 16));
-            float4 v = *px;
-            const float4 w = __ldg(reinterpret_cast<const float4 *>(pr.w) + k4);
-            v = make_float4(__fmul_rn(v.x, __fmul_rn(factor, w.x)), __fmul_rn(v.y, __fmul_rn(factor, w.y)),
-                            __fmul_rn(v.z, __fmul_rn(factor, w.z)), __fmul_rn(v.w, __fmul_rn(factor, w.w)));
-            *px = v;
+        for (int base = threadIdx.x; base < nq; base += PQ * nt) {
+#pragma unroll
+            for (int u = 0; u < PQ; ++u) {
+                const int k4 = base + u * nt;
+                if (k4 >= nq) break;
+                const float4 w = base == (int)threadIdx.x ? wv[u] : __ldg(w4 + k4);
+                float4 *px = reinterpret_cast<float4 *>(xs + swz128((uint32_t)k4 * 16));
+                float4 v = *px;
+                v = make_float4(__fmul_rn(v.x, __fmul_rn(factor, w.x)), __fmul_rn(v.y, __fmul_rn(factor, w.y)),
+                                __fmul_rn(v.z, __fmul_rn(factor, w.z)), __fmul_rn(v.w, __fmul_rn(factor, w.w)));
+                *px = v;
+            }
         }
     } else {
+        pdl_wait();
+        pdl_trigger();
         auto silu_mul = [](float g, float u) { return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u); };
-        for (int k4 = threadIdx.x; k4 < nq; k4 += blockDim.x) {
-            const float4 g = __ldg(reinterpret_cast<const float4 *>(pr.x) + k4);
-            const float4 u = __ldg(reinterpret_cast<const float4 *>(pr.x + K) + k4);
-            *reinterpret_cast<float4 *>(xs + swz128((uint32_t)k4 * 16)) =
-                make_float4(silu_mul(g.x, u.x), silu_mul(g.y, u.y), silu_mul(g.z, u.z), silu_mul(g.w, u.w));
+        for (int base = threadIdx.x; base < nq; base += PQ * nt) {
+            float4 g[PQ], u4[PQ];
+#pragma unroll
+            for (int u = 0; u < PQ; ++u) {
+                const int k4 = base + u * nt;
+                if (k4 < nq) {
+                    g[u] = __ldg(x4 + k4);
+                    u4[u] = __ldg(x4 + nq + k4);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < PQ; ++u) {
+                const int k4 = base + u * nt;
+                if (k4 >= nq) break;
+                *reinterpret_cast<float4 *>(xs + swz128((uint32_t)k4 * 16)) =
+                    make_float4(silu_mul(g[u].x, u4[u].x), silu_mul(g[u].y, u4[u].y), silu_mul(g[u].z, u4[u].z),
+                                silu_mul(g[u].w, u4[u].w));
+            }
         }
     }
     __syncthreads();
@@ -150,9 +196,7 @@ __global__ void __launch_bounds__(max_warps(B) * 32, 1)
     if (it < p.items && row0_of(it) < p.N && c0 < p.chunks) load(row0_of(it), c0);
 
     if constexpr (PRO != kProNone) {
-        pdl_wait();  // the prologue's inputs come from the previous kernels
-        pdl_trigger();
-        run_prologue<PRO>(p, xs, red);
+        run_prologue<PRO>(p, xs, red);  // waits on the previous kernels itself
     } else {
     if (threadIdx.x == 0) {
         abort_flag = 0;
