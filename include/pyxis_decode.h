@@ -61,6 +61,19 @@ int pyxis_cuda_model_set_head(pyxis_cuda_model *m, const uint16_t *embedding_bf1
 int pyxis_cuda_model_generate(pyxis_cuda_model *m, const int32_t *prompt, size_t n_prompt, size_t n_new,
                               int32_t *out_tokens, float *timing_ms);
 
+/* Greedy generation for n_seq independent prompts of n_prompt ids each (row-major
+ * [n_seq][n_prompt]) side by side; writes out_tokens [n_seq][n_new].  Each sequence gets exactly
+ * the tokens pyxis_cuda_model_generate would give it alone (up to the order of f32 sums: prompts
+ * go through tensor-core GEMMs and a causal prefill attention kernel, then every new token is one
+ * batched step).  n_prompt + n_new - 1 <= max_seq, n_seq <= 1024, n_prompt <= 16384.  The first call, and any later
+ * call with more sequences, a longer prompt or more new tokens, allocates on the context's device
+ * a KV cache of n_seq x n_layers x max_seq x 2 x n_kv_heads x head_dim floats and work buffers
+ * (prompts are processed up to 16384 positions at a time); they are kept until
+ * pyxis_cuda_model_free.  timing_ms (optional, 2 floats): device time of the prefill through the
+ * first generated tokens, and of the remaining n_new - 1 steps. */
+int pyxis_cuda_model_generate_batch(pyxis_cuda_model *m, const int32_t *prompts, size_t n_seq, size_t n_prompt,
+                                    size_t n_new, int32_t *out_tokens, float *timing_ms);
+
 int pyxis_cuda_model_free(pyxis_cuda_model *m);
 
 /* The RoPE table the model uses: cos/sin[pos * (head_dim/2) + i] of pos * theta^(-2i/head_dim),

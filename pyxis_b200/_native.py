@@ -54,6 +54,7 @@ SIGNATURES = {
     "pyxis_cuda_model_set_layer": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "pyxis_cuda_model_set_head": (C.c_int, [_vp, _vp, _vp, _vp]),
     "pyxis_cuda_model_generate": (C.c_int, [_vp, _vp, _sz, _sz, _vp, _vp]),
+    "pyxis_cuda_model_generate_batch": (C.c_int, [_vp, _vp, _sz, _sz, _sz, _vp, _vp]),
     "pyxis_cuda_model_free": (C.c_int, [_vp]),
     "pyxis_rope_table": (C.c_int, [C.c_float, C.c_int, C.c_int, _vp, _vp]),
     "pyxis_synth_normal_f32": (None, [C.c_uint64, _sz, C.c_float, _vp]),

@@ -18,7 +18,9 @@
 #include "argmax.h"
 #include "common.cuh"
 #include "ctx.h"
+#include "heads.cuh"
 #include "kernels.h"
+#include "model.h"
 
 namespace pyxis {
 namespace {
@@ -104,50 +106,14 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float *__rest
 // Lane l of a warp holds head elements [l*EPL, (l+1)*EPL); RoPE pairs element i with i + hd/2,
 // which sits in lane l ^ 16.
 constexpr int kAttnThreads = 256;
-constexpr int kAttnMaxG = 4;
-
-template <int EPL>
-PYXIS_DEVINL void load_head(const float *p, float (&v)[EPL]) {
-    if constexpr (EPL == 4) {
-        const float4 t = *reinterpret_cast<const float4 *>(p);
-        v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
-    } else {
-        const float2 t = *reinterpret_cast<const float2 *>(p);
-        v[0] = t.x, v[1] = t.y;
-    }
-}
-
-// QK RMSNorm (optional) and RoPE of one head held across a warp.
-template <int EPL>
-PYXIS_DEVINL void norm_rope(float (&v)[EPL], const float *nw, const float *rcos, const float *rsin, int pos,
-                            float eps, int lane) {
-    constexpr int HD = 32 * EPL, HALF = HD / 2;
-    if (nw) {
-        float ss = 0.f;
-#pragma unroll
-        for (int t = 0; t < EPL; ++t) ss = __fadd_rn(ss, __fmul_rn(v[t], v[t]));
-        ss = warp_sum(ss);
-        const float factor = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)HD), eps)));
-#pragma unroll
-        for (int t = 0; t < EPL; ++t) v[t] = __fmul_rn(v[t], __fmul_rn(factor, nw[lane * EPL + t]));
-    }
-    const bool lo = lane < 16;
-#pragma unroll
-    for (int t = 0; t < EPL; ++t) {
-        const float other = __shfl_xor_sync(0xffffffffu, v[t], 16);
-        const int i = (lane & 15) * EPL + t;  // pair index in [0, HALF)
-        const float c = rcos[(size_t)pos * HALF + i], s = rsin[(size_t)pos * HALF + i];
-        v[t] = lo ? __fsub_rn(__fmul_rn(v[t], c), __fmul_rn(other, s)) : __fadd_rn(__fmul_rn(v[t], c), __fmul_rn(other, s));
-    }
-}
-
 template <int EPL>
 __global__ void __launch_bounds__(kAttnThreads)
     attention_step_kernel(const float *__restrict__ qkv, const float *__restrict__ q_norm,
                           const float *__restrict__ k_norm, const float *__restrict__ rcos,
                           const float *__restrict__ rsin, const int *__restrict__ d_pos, int n_q, int n_kv, float eps,
                           float *__restrict__ kcache, float *__restrict__ vcache, float *__restrict__ part,
-                          unsigned *__restrict__ tickets, float *__restrict__ out) {
+                          unsigned *__restrict__ tickets, float *__restrict__ out, long long qkv_stride,
+                          long long cache_stride, long long out_stride) {
     constexpr int HD = 32 * EPL, PF = 4;  // keys whose rows a warp has in flight at once
     constexpr int NW = kAttnThreads / 32;
     __shared__ float qs[kAttnMaxG][HD], knew[HD], vnew[HD];
@@ -157,6 +123,15 @@ __global__ void __launch_bounds__(kAttnThreads)
     const int S = gridDim.x, s = blockIdx.x, h = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kv_dim = n_kv * HD, q_dim = n_q * HD;
+    {  // sequence blockIdx.z of a batch
+        const long long z = blockIdx.z;
+        qkv += z * qkv_stride;
+        kcache += z * cache_stride;
+        vcache += z * cache_stride;
+        out += z * out_stride;
+        part += z * (long long)n_kv * S * G * (HD + 2);
+        tickets += z * n_kv;
+    }
     // The position and the cache rows below it were written by earlier steps (earlier graph
     // launches): read them, and this warp's first keys, before waiting on the q|k|v projection.
     const int pos = *d_pos;
@@ -337,32 +312,19 @@ __global__ void advance_kernel(const int *__restrict__ token, int *__restrict__ 
 }  // namespace
 }  // namespace pyxis
 
+cudaError_t pyxis::launch_attention_step(const pyxis_model_config &c, int splits, int n_seq, const float *qkv,
+                                         size_t qkv_stride, const float *q_norm, const float *k_norm,
+                                         const float *rope_cos, const float *rope_sin, const int *d_pos, float *kc,
+                                         float *vc, size_t cache_stride, float *part, unsigned *tickets, float *out,
+                                         size_t out_stride, cudaStream_t st) {
+    auto kern = c.head_dim == 128 ? attention_step_kernel<4> : attention_step_kernel<2>;
+    return launch_kernel(kern, dim3(splits, c.n_kv_heads, n_seq), dim3(kAttnThreads), 0, st, qkv, q_norm, k_norm,
+                         rope_cos, rope_sin, d_pos, c.n_q_heads, c.n_kv_heads, c.rms_eps, kc, vc, part, tickets, out,
+                         (long long)qkv_stride, (long long)cache_stride, (long long)out_stride);
+}
+
 using namespace pyxis;
 
-struct pyxis_cuda_model {
-    pyxis_cuda_ctx *ctx = nullptr;
-    pyxis_model_config cfg{};
-    int q_dim = 0, kv_dim = 0;
-    struct Layer {
-        const pyxis_cuda_weights *wqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wdown = nullptr;
-        float *in_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
-    };
-    std::vector<Layer> layers;
-    uint16_t *emb = nullptr;
-    const pyxis_cuda_weights *lm_head = nullptr;
-    float *final_norm = nullptr;
-    float *rope_cos = nullptr, *rope_sin = nullptr;
-    float *kcache = nullptr, *vcache = nullptr;
-    float *x2 = nullptr;                      // the residual stream alternates between x and x2
-    float *part = nullptr;                    // attention split partials [n_kv][splits][G][hd + 2]
-    unsigned *tickets = nullptr;              // [n_kv], zero between launches
-    int attn_splits = 1;
-    float *x = nullptr, *h = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *tmp = nullptr, *gu = nullptr,
-          *act = nullptr, *logits = nullptr;
-    int *d_pos = nullptr, *d_token = nullptr, *d_step = nullptr, *d_out = nullptr;
-    cudaGraphExec_t exec = nullptr;
-    std::vector<void *> allocs;
-};
 
 namespace {
 
@@ -462,11 +424,8 @@ int enqueue_step(pyxis_cuda_model *m, cudaStream_t st) {
         int rc = norm_gemv(m, L.wqkv, qkv_rows, xr, l ? m->tmp : nullptr, xw, L.in_norm, m->qkv, st);
         if (rc) return rc;
         if (l) std::swap(xr, xw);
-        auto kern = c.head_dim == 128 ? attention_step_kernel<4> : attention_step_kernel<2>;
-        le = launch_kernel(kern, dim3(m->attn_splits, c.n_kv_heads), dim3(kAttnThreads), 0, st,
-                           (const float *)m->qkv, (const float *)L.q_norm, (const float *)L.k_norm,
-                           (const float *)m->rope_cos, (const float *)m->rope_sin, (const int *)m->d_pos, c.n_q_heads,
-                           c.n_kv_heads, c.rms_eps, kc, vc, m->part, m->tickets, m->attn);
+        le = launch_attention_step(c, m->attn_splits, 1, m->qkv, 0, L.q_norm, L.k_norm, m->rope_cos, m->rope_sin,
+                                   m->d_pos, kc, vc, 0, m->part, m->tickets, m->attn, 0, st);
         if (le != cudaSuccess) return model_fail(PYXIS_ECUDA, cudaGetErrorString(le));
         rc = run_matmul(m->ctx, L.wo, m->attn, 1, m->q_dim, H, m->q_dim, m->tmp, H, nullptr, 0, st);
         if (rc) return rc;
@@ -717,6 +676,7 @@ extern "C" int pyxis_cuda_model_free(pyxis_cuda_model *m) {
     Guard g(m->ctx->device);
     cudaStreamSynchronize(m->ctx->stream);
     if (m->exec) cudaGraphExecDestroy(m->exec);
+    free_batch_state(m->batch);
     for (void *p : m->allocs) cudaFree(p);
     delete m;
     return PYXIS_OK;

@@ -1,0 +1,627 @@
+// decode_batch.cu -- greedy generation for many independent sequences at once
+// (pyxis_cuda_model_generate_batch, include/pyxis_decode.h).
+//
+// Model::generate (src/model.rs:245-285) with temperature 0, run for n_seq prompts of the same
+// length side by side.  Prefill processes whole prompts: the projections of all their positions
+// are tensor-core GEMMs (pyxis_cuda_matmul_dev's M >= 16 path), attention is the causal
+// prefill kernel below, and the K/V rows go straight into each sequence's cache.  Every
+// generated token is then one batched step -- the projections are GEMMs over the n_seq rows,
+// attention is the fused decode kernel of decode.cu over a (split, kv head, sequence) grid --
+// captured once into a CUDA graph and replayed.  The arithmetic between the projections is the
+// single-sequence decoder's (decode.cu), row by row.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <new>
+#include <type_traits>
+#include <vector>
+
+#include "../../include/pyxis_decode.h"
+#include "argmax.h"
+#include "common.cuh"
+#include "ctx.h"
+#include "heads.cuh"
+#include "kernels.h"
+#include "model.h"
+
+namespace pyxis {
+namespace {
+
+// ------------------------------------------------------------------------------ row kernels --
+// x[r] = widen(embedding[tokens[r]]) (src/embedding.rs:18-24); grid (ceil(H / 256), rows).
+__global__ void embed_rows_kernel(const uint16_t *__restrict__ emb, const int *__restrict__ tokens, int vocab, int H,
+                                  float *__restrict__ x) {
+    pdl_wait();
+    pdl_trigger();
+    const int r = blockIdx.y;
+    int t = tokens[r];
+    t = t < 0 ? 0 : (t >= vocab ? vocab - 1 : t);
+    const uint16_t *row = emb + (size_t)t * H;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < H) x[(size_t)r * H + i] = bf16_bits_to_f32(row[i]);
+}
+
+// Output row r from residual row rx = r * row_step + row_off: x[rx] += delta[rx] (optional, in
+// place: one CTA owns the row), then h[r] = x[rx] * (factor * w), factor = 1 / sqrt(mean(x^2) + eps)
+// (src/transformer.rs:40-42,54-59, src/rmsnorm.rs:11-20).  256 threads, n % 4 == 0, n <= 8192.
+constexpr int kRowThreads = 256;
+constexpr int kRowQuads = 8;
+__global__ void __launch_bounds__(kRowThreads)
+    add_rmsnorm_rows_kernel(float *__restrict__ x, const float *__restrict__ delta, const float *__restrict__ w,
+                            float *__restrict__ h, int n, float eps, int row_step, int row_off) {
+    __shared__ float red[kRowThreads / 32];
+    pdl_wait();
+    pdl_trigger();
+    const size_t rx = (size_t)blockIdx.x * row_step + row_off;
+    float4 *xr = reinterpret_cast<float4 *>(x + rx * n);
+    const float4 *dr = delta ? reinterpret_cast<const float4 *>(delta + rx * n) : nullptr;
+    const float4 *w4 = reinterpret_cast<const float4 *>(w);
+    const int nq = n / 4;
+    float4 v[kRowQuads];
+    float ss = 0.f;
+#pragma unroll
+    for (int u = 0; u < kRowQuads; ++u) {
+        const int k = threadIdx.x + u * kRowThreads;
+        if (k < nq) {
+            v[u] = xr[k];
+            if (dr) {
+                const float4 d = dr[k];
+                v[u] = make_float4(__fadd_rn(v[u].x, d.x), __fadd_rn(v[u].y, d.y), __fadd_rn(v[u].z, d.z),
+                                   __fadd_rn(v[u].w, d.w));
+            }
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < kRowQuads; ++u) {
+        const int k = threadIdx.x + u * kRowThreads;
+        if (k < nq) {
+            if (dr) xr[k] = v[u];
+            ss = __fadd_rn(ss, __fmul_rn(v[u].x, v[u].x));
+            ss = __fadd_rn(ss, __fmul_rn(v[u].y, v[u].y));
+            ss = __fadd_rn(ss, __fmul_rn(v[u].z, v[u].z));
+            ss = __fadd_rn(ss, __fmul_rn(v[u].w, v[u].w));
+        }
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int i = 0; i < kRowThreads / 32; ++i) tot = __fadd_rn(tot, red[i]);
+    const float factor = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)n), eps)));
+    float4 *hr = reinterpret_cast<float4 *>(h + (size_t)blockIdx.x * n);
+#pragma unroll
+    for (int u = 0; u < kRowQuads; ++u) {
+        const int k = threadIdx.x + u * kRowThreads;
+        if (k < nq) {
+            const float4 ww = w4[k];
+            hr[k] = make_float4(__fmul_rn(v[u].x, __fmul_rn(factor, ww.x)), __fmul_rn(v[u].y, __fmul_rn(factor, ww.y)),
+                                __fmul_rn(v[u].z, __fmul_rn(factor, ww.z)), __fmul_rn(v[u].w, __fmul_rn(factor, ww.w)));
+        }
+    }
+}
+
+// Prefill row r = (sequence r / P, position pos0 + r % P): per-head QK RMSNorm and RoPE
+// (src/attention.rs:81-93), q to qout[r], k and v to the sequence's cache row (:100).
+// One CTA per row, one warp per head: warps [0, n_q) the q heads, [n_q, n_q + n_kv) the k heads,
+// warp n_q + n_kv copies v.
+template <int EPL>
+__global__ void qk_rope_rows_kernel(const float *__restrict__ qkv, const float *__restrict__ q_norm,
+                                    const float *__restrict__ k_norm, const float *__restrict__ rcos,
+                                    const float *__restrict__ rsin, int n_q, int n_kv, float eps, int P, int pos0,
+                                    float *__restrict__ qout, float *__restrict__ kcache, float *__restrict__ vcache,
+                                    long long cache_stride) {
+    constexpr int HD = 32 * EPL;
+    pdl_wait();
+    pdl_trigger();
+    const int r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int seq = r / P, pos = pos0 + r % P;
+    const int q_dim = n_q * HD, kv_dim = n_kv * HD;
+    const float *row = qkv + (size_t)r * (q_dim + 2 * kv_dim);
+    float *kc = kcache + seq * cache_stride + (size_t)pos * kv_dim;
+    float *vc = vcache + seq * cache_stride + (size_t)pos * kv_dim;
+    if (warp < n_q + n_kv) {
+        const bool is_q = warp < n_q;
+        const int hh = is_q ? warp : warp - n_q;
+        float v[EPL];
+        load_head<EPL>(row + (is_q ? 0 : q_dim) + (size_t)hh * HD + lane * EPL, v);
+        norm_rope<EPL>(v, is_q ? q_norm : k_norm, rcos, rsin, pos, eps, lane);
+        float *dst = is_q ? qout + (size_t)r * q_dim + (size_t)hh * HD : kc + (size_t)hh * HD;
+#pragma unroll
+        for (int t = 0; t < EPL; ++t) dst[lane * EPL + t] = v[t];
+    } else if (warp == n_q + n_kv) {
+        for (int i = lane; i < kv_dim; i += 32) vc[i] = row[q_dim + kv_dim + i];
+    }
+}
+
+// act[r] = SiLU(gu[r][0:ffn]) * gu[r][ffn:2 ffn] (src/ffn.rs:39-41,52-54); grid (ceil(ffn/256), rows).
+__global__ void silu_rows_kernel(const float *__restrict__ gu, int ffn, float *__restrict__ act) {
+    pdl_wait();
+    pdl_trigger();
+    const int r = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= ffn) return;
+    const float *row = gu + (size_t)r * 2 * ffn;
+    const float g = row[i];
+    act[(size_t)r * ffn + i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), row[ffn + i]);
+}
+
+// out[b][step] = tokens[b] for every sequence, then step += 1 and pos += 1 (one CTA).
+__global__ void advance_rows_kernel(const int *__restrict__ tokens, int n_seq, int n_new, int *__restrict__ out,
+                                    int *pos, int *step) {
+    pdl_wait();
+    pdl_trigger();
+    const int s = *step;
+    for (int b = threadIdx.x; b < n_seq; b += blockDim.x) out[(size_t)b * n_new + s] = tokens[b];
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        *step = s + 1;
+        *pos = *pos + 1;
+    }
+}
+
+// ---------------------------------------------------------------- causal prefill attention --
+// src/attention.rs:107-135 for every position of a prompt at once: query position i of head qh
+// attends the keys 0..i of kv head qh / G, scores (q . k) / sqrt(hd), softmax, sum of p v.
+// CTA = 64 queries x one head x one sequence, 256 threads as 16 x 16: thread (ty, tx) scores
+// queries ty*4..ty*4+3 against keys tx*2, tx*2+1 of each 32-key tile and accumulates output
+// dims tx*DPT.. of the same queries.  Q and K tiles sit transposed in shared memory ([d][query],
+// [d][key]), so each step over d reads one float4 of queries (shared by the 16 tx threads) and
+// one float2 of keys; softmax is online per query row (max and sum over the row's 16 threads by
+// shuffles).  fp32 throughout; the query tiles with the most keys start first.
+constexpr int kPfThreads = 256, kPfBQ = 64, kPfBK = 32;
+
+template <int HD>
+constexpr size_t prefill_smem_floats() {
+    return (size_t)HD * (kPfBQ + 4) + (size_t)HD * (kPfBK + 4) + (size_t)kPfBK * HD + (size_t)kPfBK * (kPfBQ + 4);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kPfThreads, 2)
+    attention_prefill_kernel(const float *__restrict__ q, int n_q, int n_kv, int P, const float *__restrict__ kcache,
+                             const float *__restrict__ vcache, long long cache_stride, float *__restrict__ out) {
+    constexpr int BQ = kPfBQ, BK = kPfBK, LDQ = BQ + 4, LDK = BK + 4, DPT = HD / 16, D4 = HD / 4;
+    extern __shared__ float4 pf_smem[];
+    float *Qt = reinterpret_cast<float *>(pf_smem);  // [HD][LDQ]
+    float *Kt = Qt + HD * LDQ;                        // [HD][LDK]
+    float *Vs = Kt + HD * LDK;                        // [BK][HD]
+    float *Pt = Vs + BK * HD;                         // [BK][LDQ]: p of (key, query)
+    const int qt = gridDim.x - 1 - blockIdx.x;
+    const int qh = blockIdx.y, seq = blockIdx.z;
+    const int kvh = qh / (n_q / n_kv);
+    const int q_dim = n_q * HD, kv_dim = n_kv * HD;
+    const int q0 = qt * BQ;
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    pdl_wait();
+    pdl_trigger();
+    const float *qb = q + (size_t)seq * P * q_dim + (size_t)qh * HD;
+    const float *kb = kcache + seq * cache_stride + (size_t)kvh * HD;
+    const float *vb = vcache + seq * cache_stride + (size_t)kvh * HD;
+    for (int idx = tid; idx < BQ * D4; idx += kPfThreads) {  // consecutive threads: consecutive queries
+        const int qi = idx % BQ, d4 = idx / BQ;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (q0 + qi < P) v = *reinterpret_cast<const float4 *>(qb + (size_t)(q0 + qi) * q_dim + d4 * 4);
+        Qt[(d4 * 4 + 0) * LDQ + qi] = v.x;
+        Qt[(d4 * 4 + 1) * LDQ + qi] = v.y;
+        Qt[(d4 * 4 + 2) * LDQ + qi] = v.z;
+        Qt[(d4 * 4 + 3) * LDQ + qi] = v.w;
+    }
+    float m[4], l[4], acc[4][DPT];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        m[i] = -INFINITY;
+        l[i] = 0.f;
+#pragma unroll
+        for (int c = 0; c < DPT; ++c) acc[i][c] = 0.f;
+    }
+    const float scale = sqrtf((float)HD);
+    const int kend = min(P, q0 + BQ);  // keys [0, kend) reach some query of the tile
+    for (int k0 = 0; k0 < kend; k0 += BK) {
+        __syncthreads();  // the previous tile's reads are done
+        for (int idx = tid; idx < BK * D4; idx += kPfThreads) {  // K transposed: consecutive keys
+            const int kj = idx % BK, d4 = idx / BK;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (k0 + kj < P) v = *reinterpret_cast<const float4 *>(kb + (size_t)(k0 + kj) * kv_dim + d4 * 4);
+            Kt[(d4 * 4 + 0) * LDK + kj] = v.x;
+            Kt[(d4 * 4 + 1) * LDK + kj] = v.y;
+            Kt[(d4 * 4 + 2) * LDK + kj] = v.z;
+            Kt[(d4 * 4 + 3) * LDK + kj] = v.w;
+        }
+        for (int idx = tid; idx < BK * D4; idx += kPfThreads) {  // V row-major: consecutive dims
+            const int kj = idx / D4, d4 = idx % D4;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (k0 + kj < P) v = *reinterpret_cast<const float4 *>(vb + (size_t)(k0 + kj) * kv_dim + d4 * 4);
+            *reinterpret_cast<float4 *>(Vs + kj * HD + d4 * 4) = v;
+        }
+        __syncthreads();
+        float s[4][2];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) s[i][0] = s[i][1] = 0.f;
+#pragma unroll 8
+        for (int d = 0; d < HD; ++d) {
+            const float4 qv = *reinterpret_cast<const float4 *>(Qt + d * LDQ + ty * 4);
+            const float2 kv = *reinterpret_cast<const float2 *>(Kt + d * LDK + tx * 2);
+            const float qa[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                s[i][0] = __fmaf_rn(qa[i], kv.x, s[i][0]);
+                s[i][1] = __fmaf_rn(qa[i], kv.y, s[i][1]);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int qi = q0 + ty * 4 + i;
+            float p[2];
+            float mt = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int kj = k0 + tx * 2 + j;
+                s[i][j] = (kj <= qi && kj < P) ? __fdiv_rn(s[i][j], scale) : -INFINITY;
+                mt = fmaxf(mt, s[i][j]);
+            }
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
+            const float mn = fmaxf(m[i], mt);  // finite: key 0 is in the first tile of every row
+            const float c = expf(__fsub_rn(m[i], mn));
+            p[0] = expf(__fsub_rn(s[i][0], mn));
+            p[1] = expf(__fsub_rn(s[i][1], mn));
+            float rs = __fadd_rn(p[0], p[1]);
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) rs = __fadd_rn(rs, __shfl_xor_sync(0xffffffffu, rs, o));
+            l[i] = __fadd_rn(__fmul_rn(l[i], c), rs);
+#pragma unroll
+            for (int cc = 0; cc < DPT; ++cc) acc[i][cc] = __fmul_rn(acc[i][cc], c);
+            m[i] = mn;
+            Pt[(tx * 2 + 0) * LDQ + ty * 4 + i] = p[0];
+            Pt[(tx * 2 + 1) * LDQ + ty * 4 + i] = p[1];
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int k = 0; k < BK; ++k) {
+            const float4 pv = *reinterpret_cast<const float4 *>(Pt + k * LDQ + ty * 4);
+            const float pa[4] = {pv.x, pv.y, pv.z, pv.w};
+            float vv[DPT];
+#pragma unroll
+            for (int c4 = 0; c4 < DPT / 4; ++c4) {
+                const float4 t = *reinterpret_cast<const float4 *>(Vs + k * HD + tx * DPT + c4 * 4);
+                vv[c4 * 4 + 0] = t.x, vv[c4 * 4 + 1] = t.y, vv[c4 * 4 + 2] = t.z, vv[c4 * 4 + 3] = t.w;
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int cc = 0; cc < DPT; ++cc) acc[i][cc] = __fmaf_rn(pa[i], vv[cc], acc[i][cc]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int qi = q0 + ty * 4 + i;
+        if (qi >= P) continue;
+        float *o = out + ((size_t)seq * P + qi) * q_dim + (size_t)qh * HD + tx * DPT;
+#pragma unroll
+        for (int c4 = 0; c4 < DPT / 4; ++c4)
+            *reinterpret_cast<float4 *>(o + c4 * 4) =
+                make_float4(__fdiv_rn(acc[i][c4 * 4 + 0], l[i]), __fdiv_rn(acc[i][c4 * 4 + 1], l[i]),
+                            __fdiv_rn(acc[i][c4 * 4 + 2], l[i]), __fdiv_rn(acc[i][c4 * 4 + 3], l[i]));
+    }
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------------------ host side --
+struct BatchState {
+    int n_seq = 0, n_prompt = 0, n_new = 0;  // capacity of the buffers below
+    int chunk = 0;                           // sequences per prefill pass
+    size_t cache_stride = 0;                 // floats per sequence: n_layers * max_seq * kv_dim
+    int splits = 1;                          // decode attention key splits
+    float *kc = nullptr, *vc = nullptr;      // [n_seq][n_layers][max_seq][kv_dim]
+    // prefill rows (chunk * n_prompt)
+    float *px = nullptr, *ph = nullptr, *pqkv = nullptr, *pq = nullptr, *pattn = nullptr, *ptmp = nullptr,
+          *pgu = nullptr, *pact = nullptr;
+    // decode rows (n_seq)
+    float *dx = nullptr, *dh = nullptr, *dqkv = nullptr, *dattn = nullptr, *dtmp = nullptr, *dgu = nullptr,
+          *dact = nullptr, *dlogits = nullptr;
+    float *part = nullptr;
+    unsigned *tickets = nullptr;
+    int *d_prompt = nullptr, *d_tokens = nullptr, *d_out = nullptr, *d_pos = nullptr, *d_step = nullptr;
+    void *ws = nullptr;
+    size_t ws_bytes = 0;
+    std::vector<void *> allocs;
+};
+
+namespace {
+
+int batch_fail(int code, const char *msg) { return record_error(code, msg); }
+
+int kv_dim_of(const pyxis_model_config &c) { return c.n_kv_heads * c.head_dim; }
+int q_dim_of(const pyxis_model_config &c) { return c.n_q_heads * c.head_dim; }
+
+// Buffers for n_seq prompts of n_prompt ids and n_new tokens (grown, never shrunk).
+int ensure_state(pyxis_cuda_model *m, int n_seq, int n_prompt, int n_new) {
+    BatchState *b = m->batch;
+    if (b && b->n_seq >= n_seq && b->n_prompt >= n_prompt && b->n_new >= n_new) return PYXIS_OK;
+    const pyxis_model_config &c = m->cfg;
+    if (b) {
+        n_seq = std::max(n_seq, b->n_seq);
+        n_prompt = std::max(n_prompt, b->n_prompt);
+        n_new = std::max(n_new, b->n_new);
+        free_batch_state(b);
+        m->batch = nullptr;
+    }
+    b = new (std::nothrow) BatchState();
+    if (!b) return batch_fail(PYXIS_ENOMEM, "host allocation failed");
+    const size_t H = c.hidden, qd = q_dim_of(c), kvd = kv_dim_of(c), ffn = c.ffn;
+    const size_t qkv_rows = qd + 2 * kvd;
+    b->n_seq = n_seq;
+    b->n_prompt = n_prompt;
+    b->n_new = n_new;
+    b->chunk = std::max(1, std::min(n_seq, 16384 / n_prompt));
+    b->cache_stride = (size_t)c.n_layers * c.max_seq * kvd;
+    const int G = c.n_q_heads / c.n_kv_heads;
+    const int want = (2 * m->ctx->num_sms + c.n_kv_heads * n_seq - 1) / (c.n_kv_heads * n_seq);
+    b->splits = std::max(1, std::min({want, (c.max_seq + 15) / 16, 64}));
+    const size_t rows = (size_t)b->chunk * n_prompt;
+    const size_t kmax = std::max({H, qd, ffn});
+    b->ws_bytes = gemm_tc_workspace_bytes(std::max(rows, (size_t)n_seq), kmax);
+    cudaError_t e = cudaSuccess;
+    auto A = [&](auto **p, size_t count) {
+        if (e != cudaSuccess) return;
+        void *v = nullptr;
+        e = cudaMalloc(&v, count * sizeof(**p) + 256);
+        if (e == cudaSuccess) {
+            b->allocs.push_back(v);
+            *p = reinterpret_cast<std::remove_reference_t<decltype(*p)>>(v);
+        }
+    };
+    A(&b->kc, (size_t)n_seq * b->cache_stride);
+    A(&b->vc, (size_t)n_seq * b->cache_stride);
+    A(&b->px, rows * H);
+    A(&b->ph, rows * H);
+    A(&b->pqkv, rows * qkv_rows);
+    A(&b->pq, rows * qd);
+    A(&b->pattn, rows * qd);
+    A(&b->ptmp, rows * H);
+    A(&b->pgu, rows * 2 * ffn);
+    A(&b->pact, rows * ffn);
+    A(&b->dx, (size_t)n_seq * H);
+    A(&b->dh, (size_t)n_seq * H);
+    A(&b->dqkv, (size_t)n_seq * qkv_rows);
+    A(&b->dattn, (size_t)n_seq * qd);
+    A(&b->dtmp, (size_t)n_seq * H);
+    A(&b->dgu, (size_t)n_seq * 2 * ffn);
+    A(&b->dact, (size_t)n_seq * ffn);
+    A(&b->dlogits, (size_t)n_seq * c.vocab);
+    A(&b->part, (size_t)n_seq * c.n_kv_heads * b->splits * G * (c.head_dim + 2));
+    A(&b->tickets, (size_t)n_seq * c.n_kv_heads);
+    A(&b->d_prompt, (size_t)n_seq * n_prompt);
+    A(&b->d_tokens, (size_t)n_seq);
+    A(&b->d_out, (size_t)n_seq * n_new);
+    A(&b->d_pos, 1);
+    A(&b->d_step, 1);
+    if (e == cudaSuccess) {
+        void *w = nullptr;
+        e = cudaMalloc(&w, b->ws_bytes);
+        if (e == cudaSuccess) {
+            b->allocs.push_back(w);
+            b->ws = w;
+        }
+    }
+    if (e == cudaSuccess) e = cudaMemset(b->tickets, 0, (size_t)n_seq * c.n_kv_heads * sizeof(unsigned));
+    if (e != cudaSuccess) {
+        free_batch_state(b);
+        cudaGetLastError();
+        return batch_fail(PYXIS_ENOMEM, cudaGetErrorString(e));
+    }
+    m->batch = b;
+    return PYXIS_OK;
+}
+
+#define PX_TRY(expr)                                                              \
+    do {                                                                          \
+        cudaError_t e_ = (expr);                                                  \
+        if (e_ != cudaSuccess) return batch_fail(PYXIS_ECUDA, cudaGetErrorString(e_)); \
+    } while (0)
+
+// All prompt positions of every sequence: the layers over `chunk` sequences at a time, then the
+// lm_head over each sequence's last position and the argmax -> the first generated tokens.
+int enqueue_prefill(pyxis_cuda_model *m, int n_seq, int P, cudaStream_t st) {
+    const pyxis_model_config &c = m->cfg;
+    BatchState *b = m->batch;
+    const int H = c.hidden, qd = q_dim_of(c), kvd = kv_dim_of(c), ffn = c.ffn;
+    const size_t qkv_rows = (size_t)qd + 2 * kvd;
+    const size_t layer_stride = (size_t)c.max_seq * kvd;
+    pyxis_cuda_ctx *ctx = m->ctx;
+    PdlScope pdl;
+    for (int s0 = 0; s0 < n_seq; s0 += b->chunk) {
+        const int cs = std::min(b->chunk, n_seq - s0);
+        const int M = cs * P;
+        PX_TRY(launch_kernel(embed_rows_kernel, dim3((H + 255) / 256, M), dim3(256), 0, st, (const uint16_t *)m->emb,
+                             (const int *)(b->d_prompt + (size_t)s0 * P), c.vocab, H, b->px));
+        for (int l = 0; l < c.n_layers; ++l) {
+            const auto &L = m->layers[l];
+            float *kc = b->kc + (size_t)s0 * b->cache_stride + l * layer_stride;
+            float *vc = b->vc + (size_t)s0 * b->cache_stride + l * layer_stride;
+            PX_TRY(launch_kernel(add_rmsnorm_rows_kernel, dim3(M), dim3(kRowThreads), 0, st, b->px,
+                                 (const float *)(l ? b->ptmp : nullptr), (const float *)L.in_norm, b->ph, H, c.rms_eps,
+                                 1, 0));
+            int rc = run_matmul(ctx, L.wqkv, b->ph, M, H, qkv_rows, H, b->pqkv, qkv_rows, b->ws, b->ws_bytes, st);
+            if (rc) return rc;
+            auto rope = c.head_dim == 128 ? qk_rope_rows_kernel<4> : qk_rope_rows_kernel<2>;
+            PX_TRY(launch_kernel(rope, dim3(M), dim3((c.n_q_heads + c.n_kv_heads + 1) * 32), 0, st,
+                                 (const float *)b->pqkv, (const float *)L.q_norm, (const float *)L.k_norm,
+                                 (const float *)m->rope_cos, (const float *)m->rope_sin, c.n_q_heads, c.n_kv_heads,
+                                 c.rms_eps, P, 0, b->pq, kc, vc, (long long)b->cache_stride));
+            const dim3 agrid((P + kPfBQ - 1) / kPfBQ, c.n_q_heads, cs);
+            if (c.head_dim == 128)
+                PX_TRY(launch_kernel(attention_prefill_kernel<128>, agrid, dim3(kPfThreads),
+                                     prefill_smem_floats<128>() * sizeof(float), st, (const float *)b->pq, c.n_q_heads,
+                                     c.n_kv_heads, P, (const float *)kc, (const float *)vc, (long long)b->cache_stride,
+                                     b->pattn));
+            else
+                PX_TRY(launch_kernel(attention_prefill_kernel<64>, agrid, dim3(kPfThreads),
+                                     prefill_smem_floats<64>() * sizeof(float), st, (const float *)b->pq, c.n_q_heads,
+                                     c.n_kv_heads, P, (const float *)kc, (const float *)vc, (long long)b->cache_stride,
+                                     b->pattn));
+            rc = run_matmul(ctx, L.wo, b->pattn, M, qd, H, qd, b->ptmp, H, b->ws, b->ws_bytes, st);
+            if (rc) return rc;
+            PX_TRY(launch_kernel(add_rmsnorm_rows_kernel, dim3(M), dim3(kRowThreads), 0, st, b->px,
+                                 (const float *)b->ptmp, (const float *)L.post_norm, b->ph, H, c.rms_eps, 1, 0));
+            rc = run_matmul(ctx, L.wgu, b->ph, M, H, 2 * (size_t)ffn, H, b->pgu, 2 * (size_t)ffn, b->ws, b->ws_bytes, st);
+            if (rc) return rc;
+            PX_TRY(launch_kernel(silu_rows_kernel, dim3((ffn + 255) / 256, M), dim3(256), 0, st, (const float *)b->pgu,
+                                 ffn, b->pact));
+            rc = run_matmul(ctx, L.wdown, b->pact, M, ffn, H, ffn, b->ptmp, H, b->ws, b->ws_bytes, st);
+            if (rc) return rc;
+        }
+        // final norm of each sequence's last position only
+        PX_TRY(launch_kernel(add_rmsnorm_rows_kernel, dim3(cs), dim3(kRowThreads), 0, st, b->px,
+                             (const float *)b->ptmp, (const float *)m->final_norm, b->dh + (size_t)s0 * H, H,
+                             c.rms_eps, P, P - 1));
+    }
+    int rc = run_matmul(ctx, m->lm_head, b->dh, n_seq, H, c.vocab, H, b->dlogits, c.vocab, b->ws, b->ws_bytes, st);
+    if (rc) return rc;
+    PX_TRY(launch_argmax_scratch(b->dlogits, n_seq, c.vocab, c.vocab, 0, b->d_tokens, nullptr, ctx->amax, ctx->num_sms,
+                                 st));
+    PX_TRY(launch_kernel(advance_rows_kernel, dim3(1), dim3(256), 0, st, (const int *)b->d_tokens, n_seq, b->n_new,
+                         b->d_out, b->d_pos, b->d_step));
+    return PYXIS_OK;
+}
+
+// One generated token for every sequence (what the graph holds): the step of decode.cu over
+// n_seq rows, all sequences at position *d_pos.
+int enqueue_step(pyxis_cuda_model *m, int n_seq, cudaStream_t st) {
+    const pyxis_model_config &c = m->cfg;
+    BatchState *b = m->batch;
+    const int H = c.hidden, qd = q_dim_of(c), kvd = kv_dim_of(c), ffn = c.ffn;
+    const size_t qkv_rows = (size_t)qd + 2 * kvd;
+    const size_t layer_stride = (size_t)c.max_seq * kvd;
+    pyxis_cuda_ctx *ctx = m->ctx;
+    PdlScope pdl;
+    PX_TRY(launch_kernel(embed_rows_kernel, dim3((H + 255) / 256, n_seq), dim3(256), 0, st, (const uint16_t *)m->emb,
+                         (const int *)b->d_tokens, c.vocab, H, b->dx));
+    for (int l = 0; l < c.n_layers; ++l) {
+        const auto &L = m->layers[l];
+        PX_TRY(launch_kernel(add_rmsnorm_rows_kernel, dim3(n_seq), dim3(kRowThreads), 0, st, b->dx,
+                             (const float *)(l ? b->dtmp : nullptr), (const float *)L.in_norm, b->dh, H, c.rms_eps, 1,
+                             0));
+        int rc = run_matmul(ctx, L.wqkv, b->dh, n_seq, H, qkv_rows, H, b->dqkv, qkv_rows, b->ws, b->ws_bytes, st);
+        if (rc) return rc;
+        PX_TRY(launch_attention_step(c, b->splits, n_seq, b->dqkv, qkv_rows, L.q_norm, L.k_norm, m->rope_cos,
+                                     m->rope_sin, b->d_pos, b->kc + l * layer_stride, b->vc + l * layer_stride,
+                                     b->cache_stride, b->part, b->tickets, b->dattn, qd, st));
+        rc = run_matmul(ctx, L.wo, b->dattn, n_seq, qd, H, qd, b->dtmp, H, b->ws, b->ws_bytes, st);
+        if (rc) return rc;
+        PX_TRY(launch_kernel(add_rmsnorm_rows_kernel, dim3(n_seq), dim3(kRowThreads), 0, st, b->dx,
+                             (const float *)b->dtmp, (const float *)L.post_norm, b->dh, H, c.rms_eps, 1, 0));
+        rc = run_matmul(ctx, L.wgu, b->dh, n_seq, H, 2 * (size_t)ffn, H, b->dgu, 2 * (size_t)ffn, b->ws, b->ws_bytes, st);
+        if (rc) return rc;
+        PX_TRY(launch_kernel(silu_rows_kernel, dim3((ffn + 255) / 256, n_seq), dim3(256), 0, st, (const float *)b->dgu,
+                             ffn, b->dact));
+        rc = run_matmul(ctx, L.wdown, b->dact, n_seq, ffn, H, ffn, b->dtmp, H, b->ws, b->ws_bytes, st);
+        if (rc) return rc;
+    }
+    PX_TRY(launch_kernel(add_rmsnorm_rows_kernel, dim3(n_seq), dim3(kRowThreads), 0, st, b->dx, (const float *)b->dtmp,
+                         (const float *)m->final_norm, b->dh, H, c.rms_eps, 1, 0));
+    int rc = run_matmul(ctx, m->lm_head, b->dh, n_seq, H, c.vocab, H, b->dlogits, c.vocab, b->ws, b->ws_bytes, st);
+    if (rc) return rc;
+    PX_TRY(launch_argmax_scratch(b->dlogits, n_seq, c.vocab, c.vocab, 0, b->d_tokens, nullptr, ctx->amax, ctx->num_sms,
+                                 st));
+    PX_TRY(launch_kernel(advance_rows_kernel, dim3(1), dim3(256), 0, st, (const int *)b->d_tokens, n_seq, b->n_new,
+                         b->d_out, b->d_pos, b->d_step));
+    return PYXIS_OK;
+}
+
+struct DevGuard {
+    int prev = -1;
+    explicit DevGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DevGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+}  // namespace
+
+void free_batch_state(BatchState *b) {
+    if (!b) return;
+    for (void *p : b->allocs) cudaFree(p);
+    delete b;
+}
+
+}  // namespace pyxis
+
+using namespace pyxis;
+
+extern "C" int pyxis_cuda_model_generate_batch(pyxis_cuda_model *m, const int32_t *prompts, size_t n_seq,
+                                               size_t n_prompt, size_t n_new, int32_t *out_tokens, float *timing_ms) {
+    if (!m || !prompts || !out_tokens) return batch_fail(PYXIS_EINVAL, "null argument");
+    if (n_seq == 0 || n_new == 0) return PYXIS_OK;
+    const pyxis_model_config &c = m->cfg;
+    if (n_prompt == 0) return batch_fail(PYXIS_EINVAL, "pyxis_cuda_model_generate_batch: empty prompts");
+    if (n_prompt + n_new - 1 > (size_t)c.max_seq)
+        return batch_fail(PYXIS_EINVAL, "pyxis_cuda_model_generate_batch: prompt + new tokens exceed max_seq");
+    if (n_seq > (size_t)kArgmaxMaxRows || n_prompt > 16384)
+        return batch_fail(PYXIS_EINVAL, "pyxis_cuda_model_generate_batch: more than 1024 sequences or 16384 prompt ids");
+    if (c.hidden % 4 || c.hidden > kRowThreads * kRowQuads * 4 || c.ffn % 4 || c.n_q_heads + c.n_kv_heads + 1 > 32)
+        return batch_fail(PYXIS_EINVAL, "pyxis_cuda_model_generate_batch: unsupported model shape");
+    for (size_t i = 0; i < n_seq * n_prompt; ++i)
+        if (prompts[i] < 0 || prompts[i] >= c.vocab) return batch_fail(PYXIS_EINVAL, "token id out of range");
+    for (const auto &L : m->layers)
+        if (!L.wqkv) return batch_fail(PYXIS_EINVAL, "a layer has no weights");
+    if (!m->lm_head) return batch_fail(PYXIS_EINVAL, "no lm_head");
+    DevGuard g(m->ctx->device);
+    int rc = ensure_state(m, (int)n_seq, (int)n_prompt, (int)n_new);
+    if (rc) return rc;
+    BatchState *b = m->batch;
+    cudaStream_t st = m->ctx->stream;
+    PX_TRY(cudaFuncSetAttribute(attention_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)(prefill_smem_floats<128>() * sizeof(float))));
+    PX_TRY(cudaFuncSetAttribute(attention_prefill_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)(prefill_smem_floats<64>() * sizeof(float))));
+    // prompts (row stride n_prompt capacity == n_prompt here: the prefill reads rows of n_prompt)
+    PX_TRY(cudaMemcpyAsync(b->d_prompt, prompts, n_seq * n_prompt * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    const int zero = 0, last = (int)n_prompt - 1;
+    PX_TRY(cudaMemcpyAsync(b->d_step, &zero, sizeof(int), cudaMemcpyHostToDevice, st));
+    PX_TRY(cudaMemcpyAsync(b->d_pos, &last, sizeof(int), cudaMemcpyHostToDevice, st));
+    cudaEvent_t ev[3];
+    for (auto &e : ev) PX_TRY(cudaEventCreate(&e));
+    struct EvFree {
+        cudaEvent_t *e;
+        ~EvFree() {
+            for (int i = 0; i < 3; ++i) cudaEventDestroy(e[i]);
+        }
+    } ev_free{ev};
+    PX_TRY(cudaEventRecord(ev[0], st));
+    rc = enqueue_prefill(m, (int)n_seq, (int)n_prompt, st);
+    if (rc) return rc;
+    PX_TRY(cudaEventRecord(ev[1], st));
+    if (n_new > 1) {
+        // the step as a CUDA graph (pointers and shapes are fixed for this call), replayed per token
+        cudaGraph_t graph = nullptr;
+        cudaGraphExec_t exec = nullptr;
+        PX_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed));
+        rc = enqueue_step(m, (int)n_seq, st);
+        cudaError_t ce = cudaStreamEndCapture(st, &graph);
+        if (rc) {
+            if (graph) cudaGraphDestroy(graph);
+            return rc;
+        }
+        PX_TRY(ce);
+        ce = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        PX_TRY(ce);
+        for (size_t t = 1; t < n_new && ce == cudaSuccess; ++t) ce = cudaGraphLaunch(exec, st);
+        cudaGraphExecDestroy(exec);
+        PX_TRY(ce);
+    }
+    PX_TRY(cudaEventRecord(ev[2], st));
+    PX_TRY(cudaMemcpy2DAsync(out_tokens, n_new * sizeof(int32_t), b->d_out, (size_t)b->n_new * sizeof(int32_t),
+                             n_new * sizeof(int32_t), n_seq, cudaMemcpyDeviceToHost, st));
+    PX_TRY(cudaStreamSynchronize(st));
+    rc = pyxis_cuda_check_device_error(m->ctx);
+    if (rc) return rc;
+    if (timing_ms) {
+        PX_TRY(cudaEventElapsedTime(&timing_ms[0], ev[0], ev[1]));
+        PX_TRY(cudaEventElapsedTime(&timing_ms[1], ev[1], ev[2]));
+    }
+    return PYXIS_OK;
+}

@@ -140,6 +140,20 @@ class Decoder:
                                                       out.ctypes.data_as(C.c_void_p), t))
         return out, (t[0], t[1])
 
+    def generate_batch(self, prompts, n_new: int):
+        """Greedy generation for several prompts of one length side by side
+        (pyxis_cuda_model_generate_batch): prompts [n_seq, n_prompt] ids -> (tokens [n_seq, n_new],
+        (prefill_ms, decode_ms)), the device time of the prefill through the first generated tokens
+        and of the remaining steps."""
+        pr = np.ascontiguousarray(np.asarray(prompts, np.int32))
+        if pr.ndim != 2:
+            raise ValueError("prompts must be [n_seq, n_prompt]")
+        out = np.empty((pr.shape[0], n_new), np.int32)
+        t = (C.c_float * 2)()
+        check(_native.lib().pyxis_cuda_model_generate_batch(self.handle, pr.ctypes.data_as(C.c_void_p), pr.shape[0],
+                                                            pr.shape[1], n_new, out.ctypes.data_as(C.c_void_p), t))
+        return out, (t[0], t[1])
+
     def close(self):
         if self.handle:
             _native.lib().pyxis_cuda_model_free(self.handle)

@@ -1,0 +1,66 @@
+"""Greedy generation for many sequences at once (pyxis_cuda_model_generate_batch): every
+sequence must get the tokens the oracle's restatement of Model::generate (src/model.rs:245-285,
+argmax sampling) gives it alone, and at the Qwen3-1.7B shape the tokens the single-sequence
+device decoder gives it."""
+import numpy as np
+import pytest
+
+import oracle
+from pyxis_b200 import synth_tokens
+from pyxis_b200.model import QWEN3_1_7B, Decoder, ModelConfig, SyntheticModel
+
+pytestmark = pytest.mark.gpu
+
+SMALL = ModelConfig(hidden=256, n_layers=3, n_q_heads=4, n_kv_heads=2, head_dim=64, ffn=512, vocab=2048,
+                    rope_theta=10000.0)
+
+
+@pytest.mark.parametrize("qtype", ["int8", "int4"])
+def test_small_model_batch_matches_oracle(qtype):
+    m = SyntheticModel(SMALL, seed=23)
+    dec = Decoder(m, qtype=qtype, max_seq=96)
+    # 70 prompt ids: two 64-query tiles and three 32-key tiles in the prefill attention
+    prompts = synth_tokens(0x77, 3 * 70, SMALL.vocab).reshape(3, 70)
+    toks, (t_pre, t_dec) = dec.generate_batch(prompts, 6)
+    assert toks.shape == (3, 6) and t_pre > 0 and t_dec > 0
+    for s in range(3):
+        ref = oracle.greedy_decode(SMALL, m.bf16, qtype, list(prompts[s]), 6)
+        assert np.array_equal(toks[s], ref), (s, toks[s], ref)
+    # a second, smaller call reuses the buffers; one token only (no decode step)
+    toks2, _ = dec.generate_batch(prompts[:2, :9], 1)
+    for s in range(2):
+        assert np.array_equal(toks2[s], oracle.greedy_decode(SMALL, m.bf16, qtype, list(prompts[s, :9]), 1))
+    dec.close()
+
+
+def test_small_model_batch_of_17_uses_gemm_steps():
+    """17 sequences: the decode-step projections take the tensor-core GEMM (M >= 16)."""
+    m = SyntheticModel(SMALL, seed=5)
+    dec = Decoder(m, qtype="int4", max_seq=40)
+    prompts = synth_tokens(0x99, 17 * 12, SMALL.vocab).reshape(17, 12)
+    toks, _ = dec.generate_batch(prompts, 4)
+    for s in range(17):
+        assert np.array_equal(toks[s], oracle.greedy_decode(SMALL, m.bf16, "int4", list(prompts[s]), 4)), s
+    dec.close()
+
+
+def test_qwen3_shape_batch_matches_single_sequence_decoder():
+    m = SyntheticModel(QWEN3_1_7B, seed=0x5EED)
+    dec = Decoder(m, qtype="int4", max_seq=80)
+    prompts = synth_tokens(0xB0, 3 * 40, QWEN3_1_7B.vocab).reshape(3, 40)
+    toks, _ = dec.generate_batch(prompts, 8)
+    for s in range(3):
+        one, _ = dec.generate(prompts[s], 8)
+        assert np.array_equal(toks[s], one), (s, toks[s], one)
+    dec.close()
+
+
+def test_batch_rejects_bad_arguments():
+    from pyxis_b200._native import PyxisError
+    m = SyntheticModel(SMALL, seed=1)
+    dec = Decoder(m, qtype="int8", max_seq=16)
+    with pytest.raises(PyxisError):
+        dec.generate_batch(np.zeros((2, 16), np.int32), 2)  # 16 + 2 - 1 > max_seq
+    with pytest.raises(PyxisError):
+        dec.generate_batch(np.full((2, 4), SMALL.vocab, np.int32), 2)  # id out of range
+    dec.close()
