@@ -354,6 +354,55 @@ def run_decode(local, cpu_sample_tokens=0):
     return out
 
 
+BATCH_SEQS, BATCH_PROMPT, BATCH_NEW = 64, 2048, 256
+BATCH_WORKLOAD = ("Qwen3-1.7B-shape batched decode, random init, int4 group 32 (lm_head too): 64 sequences x 2048 "
+                  "random prompt ids prefilled, then 256 greedy tokens each; sequences split data-parallel over the "
+                  "GPUs")
+
+
+def batch_step_bytes(cfg, n_seq, pos):
+    """HBM bytes of one batched int4 step at cache position `pos`: every projection's codes and
+    group-32 scales once (GEMMs over the n_seq rows) plus each sequence's KV rows 0..pos."""
+    params = cfg.n_layers * ((cfg.q_dim + 2 * cfg.kv_dim) * cfg.hidden + cfg.hidden * cfg.q_dim
+                             + 3 * cfg.ffn * cfg.hidden) + cfg.vocab * cfg.hidden
+    w = params // 2 + params // 32 * 4
+    kv = n_seq * cfg.n_layers * 2 * (pos + 1) * cfg.kv_dim * 4
+    return w + kv
+
+
+def prefill_flops(cfg, n_seq, P):
+    """Algorithmic flops of the prefill: 2 x params x tokens for the projections, the causal
+    attention's QK and PV (2 x 2 x hd per (query, key) pair and head), the lm_head of the last rows."""
+    proj = cfg.n_layers * ((cfg.q_dim + 2 * cfg.kv_dim) * cfg.hidden + cfg.hidden * cfg.q_dim
+                           + 3 * cfg.ffn * cfg.hidden)
+    attn = cfg.n_layers * cfg.n_q_heads * 4 * cfg.head_dim * (P * (P + 1) // 2)
+    return n_seq * (2 * proj * P + attn) + 2 * n_seq * cfg.vocab * cfg.hidden
+
+
+def run_batch_decode(local, ws, rank, n_seq_total=BATCH_SEQS, P=BATCH_PROMPT, n_new=BATCH_NEW):
+    """64 sequences of 2048 prompt ids then 256 greedy tokens, int4: this rank's share of the
+    sequences through pyxis_cuda_model_generate_batch."""
+    from pyxis_b200 import synth_tokens
+    from pyxis_b200.model import QWEN3_1_7B, Decoder, SyntheticModel
+
+    cfg = QWEN3_1_7B
+    n_seq = n_seq_total // ws + (1 if rank < n_seq_total % ws else 0)
+    first = rank * (n_seq_total // ws) + min(rank, n_seq_total % ws)
+    prompts = synth_tokens(0xBA7C, n_seq_total * P, cfg.vocab).reshape(n_seq_total, P)[first:first + n_seq]
+    dec = Decoder(SyntheticModel(cfg, SEED), qtype="int4", max_seq=P + n_new, device=local)
+    dec.generate_batch(prompts[:, :64], 4)  # warm-up: first-use set-up of every kernel
+    toks, (pre_ms, dec_ms) = dec.generate_batch(prompts, n_new)
+    dec.close()
+    steps = n_new - 1
+    bytes_steps = sum(batch_step_bytes(cfg, n_seq, P + i) for i in range(steps))
+    return {"workload": BATCH_WORKLOAD, "sequences_this_rank": n_seq, "prefill_ms": pre_ms, "decode_ms": dec_ms,
+            "decode_tokens_per_s": n_seq * steps / (dec_ms / 1e3),
+            "decode_achieved_gbs": bytes_steps / (dec_ms / 1e3) / 1e9,
+            "prefill_tokens_per_s": n_seq * P / (pre_ms / 1e3),
+            "prefill_tflops": prefill_flops(cfg, n_seq, P) / (pre_ms / 1e3) / 1e12,
+            "first_tokens": [int(t) for t in toks[0, :8]]}
+
+
 def pyxis_arm(args, ws, rank, local):
     import numpy as np
     import torch
@@ -544,6 +593,19 @@ def pyxis_arm(args, ws, rank, local):
         decode["roofline_tokens_per_s"] = peak_d * 1e9 / decode["bytes_per_token"]
         decode["frac_of_peak"] = decode["achieved_gbs"] / peak_d
 
+    batch = None
+    if not args.no_batch_decode:
+        torch.cuda.empty_cache()
+        batch = run_batch_decode(local, ws, rank)
+        ms = max_over_ranks(batch["prefill_ms"] + batch["decode_ms"], ws)
+        dmax = max_over_ranks(batch["decode_ms"], ws)
+        pmax = max_over_ranks(batch["prefill_ms"], ws)
+        peak_d, _ = measured_peak_hbm()
+        batch.update({"job_decode_tokens_per_s": BATCH_SEQS * (BATCH_NEW - 1) / (dmax / 1e3),
+                      "job_tokens_per_s": BATCH_SEQS * BATCH_NEW / (ms / 1e3),
+                      "job_prefill_ms": pmax, "decode_frac_of_hbm_peak": batch["decode_achieved_gbs"] / peak_d,
+                      "prefill_frac_of_bf16_peak": batch["prefill_tflops"] / (peak_tf or 1590.0)})
+
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         import oracle
@@ -569,6 +631,7 @@ def pyxis_arm(args, ws, rank, local):
                 "eager_ms_per_step": eager_ms_max / args.steps,
                 "cases": cases,
                 "decode": decode,
+                "batch_decode": batch,
                 "lm_head_vocab_parallel": lm_vp,
                 "prefill": {"M": PREFILL_M, "kernel": "split_x_kernel + gemm_tc_kernel (tcgen05 kind::f16, fp16 hi/lo)",
                             "peak_tflops": peak_tf, "peak_kind": "measured bf16 burst", "shapes": prefill},
@@ -584,6 +647,14 @@ def profile_case(args):
 
     import pyxis_b200 as px
 
+    if args.profile_case.startswith("batch"):
+        parts = [int(v) for v in args.profile_case.split(":")[1:]]
+        n_seq, P, n_new = (parts + [BATCH_SEQS, BATCH_PROMPT, BATCH_NEW][len(parts):])[:3]
+        r = run_batch_decode(0, 1, 0, n_seq_total=n_seq, P=P, n_new=n_new)
+        print(f"profile case batch: {n_seq} x {P} prompt + {n_new} new: prefill {r['prefill_ms']:.1f} ms "
+              f"({r['prefill_tflops']:.1f} TFLOP/s), decode {r['decode_ms']:.1f} ms "
+              f"({r['decode_tokens_per_s']:.0f} tok/s, {r['decode_achieved_gbs']:.0f} GB/s)")
+        return
     if args.profile_case.startswith("decode"):
         from pyxis_b200 import synth_tokens
         from pyxis_b200.model import QWEN3_1_7B, Decoder, SyntheticModel
@@ -620,6 +691,8 @@ def main():
     ap.add_argument("--impl", choices=["pyxis", "reference"], default="pyxis")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the Qwen3-1.7B-shape greedy decode measurement")
+    ap.add_argument("--no-batch-decode", action="store_true",
+                    help="skip the 64-sequence int4 batched decode measurement")
     args = ap.parse_args()
     if args.impl == "reference":
         ws = int(os.environ.get("WORLD_SIZE", "1"))

@@ -151,20 +151,24 @@ int pyxis::run_matmul(pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, const fl
     if (use_gemm_tc(q, M, X, ldx)) {
         const size_t need = gemm_tc_workspace_bytes(M, in_features);
         if (!workspace) {
-            if (ctx->ws_cap < need) {
+            // the context's own workspace also holds split-K partials when they help
+            const size_t want = gemm_tc_workspace_bytes_splitk(M, out_features, in_features, w->block_size == in_features,
+                                                               w->block_size, ctx->num_sms);
+            if (ctx->ws_cap < want) {
                 cudaFree(ctx->ws);
                 ctx->ws = nullptr;
                 ctx->ws_cap = 0;
-                PYXIS_CUDA_TRY(cudaMalloc(&ctx->ws, need), "cudaMalloc(workspace)");
-                ctx->ws_cap = need;
+                PYXIS_CUDA_TRY(cudaMalloc(&ctx->ws, want), "cudaMalloc(workspace)");
+                ctx->ws_cap = want;
             }
             workspace = ctx->ws;
+            workspace_bytes = ctx->ws_cap;
         } else if (workspace_bytes < need) {
             return fail(PYXIS_EINVAL, "workspace of %zu bytes < %zu needed", workspace_bytes, need);
         } else if (reinterpret_cast<uintptr_t>(workspace) & 255) {
             return fail(PYXIS_EINVAL, "workspace must be 256-byte aligned");
         }
-        cudaError_t e = launch_gemm_tc(q, X, M, ldx, Y, ldy, workspace, ctx->d_err, st);
+        cudaError_t e = launch_gemm_tc(q, X, M, ldx, Y, ldy, workspace, workspace_bytes, ctx->d_err, ctx->num_sms, st);
         if (e != cudaSuccess) return cuda_fail(e, "tensor-core GEMM launch");
         return PYXIS_OK;
     }

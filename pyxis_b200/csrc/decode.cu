@@ -106,7 +106,7 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float *__rest
 // Lane l of a warp holds head elements [l*EPL, (l+1)*EPL); RoPE pairs element i with i + hd/2,
 // which sits in lane l ^ 16.
 constexpr int kAttnThreads = 256;
-template <int EPL>
+template <int EPL, int G>
 __global__ void __launch_bounds__(kAttnThreads)
     attention_step_kernel(const float *__restrict__ qkv, const float *__restrict__ q_norm,
                           const float *__restrict__ k_norm, const float *__restrict__ rcos,
@@ -116,10 +116,9 @@ __global__ void __launch_bounds__(kAttnThreads)
                           long long cache_stride, long long out_stride) {
     constexpr int HD = 32 * EPL, PF = 4;  // keys whose rows a warp has in flight at once
     constexpr int NW = kAttnThreads / 32;
-    __shared__ float qs[kAttnMaxG][HD], knew[HD], vnew[HD];
-    __shared__ float wpart[NW][kAttnMaxG][HD + 2];  // per-warp (max, sum, acc[HD])
+    __shared__ float qs[G][HD], knew[HD], vnew[HD];
+    __shared__ float wpart[NW][G][HD + 2];  // per-warp (max, sum, acc[HD])
     __shared__ int flag;
-    const int G = n_q / n_kv;
     const int S = gridDim.x, s = blockIdx.x, h = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kv_dim = n_kv * HD, q_dim = n_q * HD;
@@ -181,9 +180,9 @@ __global__ void __launch_bounds__(kAttnThreads)
 
     // this warp's keys j0 + warp, j0 + warp + NW, ...: online softmax per query head
     const float scale = sqrtf((float)HD);
-    float qr[kAttnMaxG][EPL], acc[kAttnMaxG][EPL], m[kAttnMaxG], l[kAttnMaxG];
+    float qr[G][EPL], acc[G][EPL], m[G], l[G];
 #pragma unroll
-    for (int g = 0; g < kAttnMaxG; ++g) {
+    for (int g = 0; g < G; ++g) {
         m[g] = -INFINITY;
         l[g] = 0.f;
 #pragma unroll
@@ -193,12 +192,23 @@ __global__ void __launch_bounds__(kAttnThreads)
             if (g < G) qr[g][t] = qs[g][lane * EPL + t];
         }
     }
+    // Each round: the next PF keys' rows are requested first, then the current ones are scored --
+    // all PF x G dot products reduced together (interleaved shuffles) -- and folded into the
+    // running softmax with one rescale per round.
     for (int jb = j0 + warp; jb < j1; jb += PF * NW) {
+        float kn[PF][EPL], vn[PF][EPL];
 #pragma unroll
         for (int u = 0; u < PF; ++u) {
-            const int j = jb + u * NW;
-            if (j >= j1) break;  // uniform across the warp
-            if (j == pos) {
+            const int j = jb + PF * NW + u * NW;
+            if (j < j1 && j < pos) {
+                load_head<EPL>(kcache + (size_t)j * kv_dim + (size_t)h * HD + lane * EPL, kn[u]);
+                load_head<EPL>(vcache + (size_t)j * kv_dim + (size_t)h * HD + lane * EPL, vn[u]);
+            }
+        }
+        float dot[PF][G];
+#pragma unroll
+        for (int u = 0; u < PF; ++u) {
+            if (jb + u * NW == pos) {
 #pragma unroll
                 for (int t = 0; t < EPL; ++t) {
                     kr[u][t] = knew[lane * EPL + t];
@@ -206,25 +216,54 @@ __global__ void __launch_bounds__(kAttnThreads)
                 }
             }
 #pragma unroll
-            for (int g = 0; g < kAttnMaxG; ++g) {
-                if (g >= G) break;
-                float dot = 0.f;
+            for (int g = 0; g < G; ++g) {
+                dot[u][g] = 0.f;
 #pragma unroll
-                for (int t = 0; t < EPL; ++t) dot = __fadd_rn(dot, __fmul_rn(qr[g][t], kr[u][t]));
-                const float sc = __fdiv_rn(warp_sum(dot), scale);
-                const float mn = fmaxf(m[g], sc);
-                const float c = expf(__fsub_rn(m[g], mn));  // 0 on the first key (m = -inf)
-                const float pj = expf(__fsub_rn(sc, mn));
-                l[g] = __fadd_rn(__fmul_rn(l[g], c), pj);
-#pragma unroll
-                for (int t = 0; t < EPL; ++t) acc[g][t] = __fadd_rn(__fmul_rn(acc[g][t], c), __fmul_rn(pj, vr[u][t]));
-                m[g] = mn;
+                for (int t = 0; t < EPL; ++t) dot[u][g] = __fadd_rn(dot[u][g], __fmul_rn(qr[g][t], kr[u][t]));
             }
         }
-        fetch(jb + PF * NW);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int u = 0; u < PF; ++u)
+#pragma unroll
+                for (int g = 0; g < G; ++g)
+                    if (g < G) dot[u][g] = __fadd_rn(dot[u][g], __shfl_xor_sync(0xffffffffu, dot[u][g], o));
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            if (g >= G) break;
+            float sc[PF], mt = -INFINITY;
+#pragma unroll
+            for (int u = 0; u < PF; ++u) {
+                sc[u] = jb + u * NW < j1 ? __fdiv_rn(dot[u][g], scale) : -INFINITY;
+                mt = fmaxf(mt, sc[u]);
+            }
+            const float mn = fmaxf(m[g], mt);           // finite: the round has >= 1 key
+            const float c = expf(__fsub_rn(m[g], mn));  // 0 on the first round (m = -inf)
+            float ps = 0.f;
+#pragma unroll
+            for (int t = 0; t < EPL; ++t) acc[g][t] = __fmul_rn(acc[g][t], c);
+#pragma unroll
+            for (int u = 0; u < PF; ++u) {
+                if (jb + u * NW >= j1) break;  // past the split's end: those rows were never loaded
+                const float pj = expf(__fsub_rn(sc[u], mn));
+                ps = __fadd_rn(ps, pj);
+#pragma unroll
+                for (int t = 0; t < EPL; ++t) acc[g][t] = __fadd_rn(acc[g][t], __fmul_rn(pj, vr[u][t]));
+            }
+            l[g] = __fadd_rn(__fmul_rn(l[g], c), ps);
+            m[g] = mn;
+        }
+#pragma unroll
+        for (int u = 0; u < PF; ++u)
+#pragma unroll
+            for (int t = 0; t < EPL; ++t) {
+                kr[u][t] = kn[u][t];
+                vr[u][t] = vn[u][t];
+            }
     }
 #pragma unroll
-    for (int g = 0; g < kAttnMaxG; ++g) {
+    for (int g = 0; g < G; ++g) {
         if (g >= G) break;
         if (lane == 0) {
             wpart[warp][g][0] = m[g];
@@ -317,7 +356,14 @@ cudaError_t pyxis::launch_attention_step(const pyxis_model_config &c, int splits
                                          const float *rope_cos, const float *rope_sin, const int *d_pos, float *kc,
                                          float *vc, size_t cache_stride, float *part, unsigned *tickets, float *out,
                                          size_t out_stride, cudaStream_t st) {
-    auto kern = c.head_dim == 128 ? attention_step_kernel<4> : attention_step_kernel<2>;
+    using Kern = void (*)(const float *, const float *, const float *, const float *, const float *, const int *, int,
+                          int, float, float *, float *, float *, unsigned *, float *, long long, long long, long long);
+    static const Kern k128[] = {attention_step_kernel<4, 1>, attention_step_kernel<4, 2>, attention_step_kernel<4, 3>,
+                                attention_step_kernel<4, 4>};
+    static const Kern k64[] = {attention_step_kernel<2, 1>, attention_step_kernel<2, 2>, attention_step_kernel<2, 3>,
+                               attention_step_kernel<2, 4>};
+    const int G = c.n_q_heads / c.n_kv_heads;
+    const Kern kern = (c.head_dim == 128 ? k128 : k64)[G - 1];
     return launch_kernel(kern, dim3(splits, c.n_kv_heads, n_seq), dim3(kAttnThreads), 0, st, qkv, q_norm, k_norm,
                          rope_cos, rope_sin, d_pos, c.n_q_heads, c.n_kv_heads, c.rms_eps, kc, vc, part, tickets, out,
                          (long long)qkv_stride, (long long)cache_stride, (long long)out_stride);
@@ -615,7 +661,7 @@ extern "C" int pyxis_cuda_model_generate(pyxis_cuda_model *m, const int32_t *pro
         // Every kernel of the step asks for the same (maximum) shared-memory carveout as the
         // GEMV kernels, so the SMs never re-split L1 / shared memory between graph nodes.
         const void *small_kernels[] = {(const void *)embed_kernel, (const void *)add_rmsnorm_kernel,
-                                       (const void *)attention_step_kernel<2>, (const void *)attention_step_kernel<4>,
+                                       (const void *)attention_step_kernel<2, 2>, (const void *)attention_step_kernel<4, 2>,
                                        (const void *)silu_mul_kernel, (const void *)advance_kernel};
         for (const void *k : small_kernels) cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
         set_argmax_carveout_max();

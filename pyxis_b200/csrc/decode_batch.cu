@@ -13,6 +13,7 @@
 #include <cmath>
 #include <cstring>
 #include <new>
+#include <tuple>
 #include <type_traits>
 #include <vector>
 
@@ -355,11 +356,21 @@ int ensure_state(pyxis_cuda_model *m, int n_seq, int n_prompt, int n_new) {
     b->chunk = std::max(1, std::min(n_seq, 16384 / n_prompt));
     b->cache_stride = (size_t)c.n_layers * c.max_seq * kvd;
     const int G = c.n_q_heads / c.n_kv_heads;
-    const int want = (2 * m->ctx->num_sms + c.n_kv_heads * n_seq - 1) / (c.n_kv_heads * n_seq);
+    // attention key splits: at least two CTAs per SM, and at most 256 keys per CTA (a CTA's warps
+    // keep only 4 keys' rows in flight each, so long contexts need many CTAs to fill HBM)
+    const int want = std::max((2 * m->ctx->num_sms + c.n_kv_heads * n_seq - 1) / (c.n_kv_heads * n_seq),
+                              (c.max_seq + 255) / 256);
     b->splits = std::max(1, std::min({want, (c.max_seq + 15) / 16, 64}));
     const size_t rows = (size_t)b->chunk * n_prompt;
     const size_t kmax = std::max({H, qd, ffn});
-    b->ws_bytes = gemm_tc_workspace_bytes(std::max(rows, (size_t)n_seq), kmax);
+    // split_x space for the largest GEMM, plus split-K partials for the n_seq-row step GEMMs
+    size_t ws = gemm_tc_workspace_bytes(std::max(rows, (size_t)n_seq), kmax);
+    for (const auto &L : m->layers)
+        for (auto [w, N, K] : {std::tuple{L.wqkv, qkv_rows, H}, std::tuple{L.wo, H, qd}, std::tuple{L.wgu, 2 * ffn, H},
+                               std::tuple{L.wdown, H, ffn}})
+            if (w) ws = std::max(ws, gemm_tc_workspace_bytes_splitk(n_seq, N, K, w->block_size == K, w->block_size,
+                                                                    m->ctx->num_sms));
+    b->ws_bytes = ws;
     cudaError_t e = cudaSuccess;
     auto A = [&](auto **p, size_t count) {
         if (e != cudaSuccess) return;

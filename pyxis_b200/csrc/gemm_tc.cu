@@ -27,6 +27,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+
 #include "kernels.h"
 #include "tc_ptx.cuh"
 #include "tmap.cuh"
@@ -71,6 +73,8 @@ struct TcParams {
     float *Y;
     long long ldy;
     int *err;
+    int kb_per_split;     // K-blocks of one blockIdx.z slice (split-K over gridDim.z)
+    float *part;          // split-K: [gridDim.z][M][N] partial products, else nullptr
 };
 
 PYXIS_DEVINL uint32_t h2_bits(__half2 v) { return *reinterpret_cast<uint32_t *>(&v); }
@@ -108,7 +112,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * BM, m0 = blockIdx.y * BN;
-    const int num_kb = p.K / BK;
+    // this CTA's K range: K-blocks [kb0, kb0 + num_kb) (the whole of K without split-K)
+    const int kb0 = blockIdx.z * p.kb_per_split;
+    const int num_kb = min(p.K / BK - kb0, p.kb_per_split);
+    // a tile with <= 64 tokens multiplies with N = 64: the rest of the B tile is TMA zero fill
+    const int mma_n = p.M - m0 <= 64 ? 64 : BN;
     const int raw_kb_bytes = p.qtype == kQInt8 ? 64 : 32;
     const uint32_t stage_tx = 2 * kBBytes + (uint32_t)(BM * raw_kb_bytes);
 
@@ -141,10 +149,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------------------ TMA producer
         if (lane == 0) {
             int issued = 0;
-            for (int kb = 0; kb < num_kb; ++kb) {
-                const int s = kb % STAGES;
-                if (kb >= STAGES &&
-                    !tc::mbar_wait_bounded(&empty[s], ((kb / STAGES) - 1) & 1, abort_flag, p.err, kErrProducer, kTimeoutNs))
+            for (int j = 0; j < num_kb; ++j) {
+                const int s = j % STAGES, kb = kb0 + j;
+                if (j >= STAGES &&
+                    !tc::mbar_wait_bounded(&empty[s], ((j / STAGES) - 1) & 1, abort_flag, p.err, kErrProducer, kTimeoutNs))
                     break;
                 tc::mbar_arrive_expect_tx(&full[s], stage_tx);
                 tc::tma_load_2d(smem + kOffR + s * kRBytes, &tm_w, kb * raw_kb_bytes, n0, &full[s]);
@@ -161,12 +169,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ------------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            const uint32_t idesc = tc::idesc_f16_f32(BM, BN);
+            const uint32_t idesc = tc::idesc_f16_f32(BM, mma_n);
             int period = 0, kin = 0, buf = 0;
             bool ok = true;
-            for (int kb = 0; kb < num_kb && ok; ++kb) {
-                const int s = kb % STAGES;
-                const uint32_t par = (kb / STAGES) & 1;
+            for (int j = 0; j < num_kb && ok; ++j) {
+                const int s = j % STAGES;
+                const uint32_t par = (j / STAGES) & 1;
                 ok = tc::mbar_wait_bounded(&conv[s], par, abort_flag, p.err, kErrMma, kTimeoutNs) &&
                      tc::mbar_wait_bounded(&full[s], par, abort_flag, p.err, kErrMma, kTimeoutNs);
                 if (!ok) break;
@@ -207,10 +215,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp < kEpiWarp0) {
         // ------------------------------------------------------------------ converters
         const int r = threadIdx.x - kConvWarp0 * 32;  // weight row within the tile
-        for (int kb = 0; kb < num_kb; ++kb) {
-            const int s = kb % STAGES;
+        for (int j = 0; j < num_kb; ++j) {
+            const int s = j % STAGES;
             int ok = 1;
-            if (lane == 0) ok = tc::mbar_wait_bounded(&full[s], (kb / STAGES) & 1, abort_flag, p.err, kErrConverter, kTimeoutNs);
+            if (lane == 0) ok = tc::mbar_wait_bounded(&full[s], (j / STAGES) & 1, abort_flag, p.err, kErrConverter, kTimeoutNs);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             const uint8_t *raw = smem + kOffR + s * kRBytes;
@@ -253,10 +261,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         float acc[64];
 #pragma unroll
         for (int j = 0; j < 64; ++j) acc[j] = 0.f;
-        const int num_periods = p.K / (16 * p.ksteps_per_period);
+        const int num_periods = num_kb * BK / (16 * p.ksteps_per_period);
         const int ppg = p.periods_per_group;
-        const int num_groups = p.per_row ? 0 : p.groups_per_row;
-        const float *srow = p.scales + (size_t)(row_ok ? n : 0) * p.groups_per_row;
+        const int group_k = 16 * p.ksteps_per_period * ppg;  // K per scale group
+        const int num_groups = p.per_row ? 0 : num_kb * BK / group_k;
+        const float *srow = p.scales + (size_t)(row_ok ? n : 0) * p.groups_per_row + (p.per_row ? 0 : kb0 * BK / group_k);
         float s_cur[4], s_nxt[4];  // scales of groups g0..g0+3 and g0+4..g0+7
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -307,7 +316,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int j = 0; j < 64; ++j) {
                 const int m = m0 + 64 * h + j;
-                if (m < p.M) p.Y[(size_t)m * p.ldy + n] = acc[j] * sr * __ldg(p.xinv + m);
+                if (m >= p.M) continue;
+                const float y = acc[j] * sr * __ldg(p.xinv + m);
+                if (p.part) p.part[((size_t)blockIdx.z * p.M + m) * p.N + n] = y;
+                else p.Y[(size_t)m * p.ldy + n] = y;
             }
         }
     }
@@ -362,6 +374,17 @@ __global__ void __launch_bounds__(256) split_x_kernel(const float *__restrict__ 
     }
 }
 
+// Split-K: Y[m][n] = sum over the slices z, in order, of part[z][m][n].
+__global__ void splitk_reduce_kernel(const float *__restrict__ part, int ks, int M, int N, float *__restrict__ Y,
+                                     long long ldy) {
+    const size_t MN = (size_t)M * N;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < MN; i += (size_t)gridDim.x * blockDim.x) {
+        float y = part[i];
+        for (int z = 1; z < ks; ++z) y += part[(size_t)z * MN + i];
+        Y[(i / N) * ldy + i % N] = y;
+    }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() { return tensor_map_encoder(); }
 
 bool make_map_2d(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t outer,
@@ -390,8 +413,47 @@ bool gemm_tc_supported(const QMatrix &w) {
 
 size_t gemm_tc_workspace_bytes(size_t M, size_t K) { return 2 * align256(M * K * 2) + align256(M * 4); }
 
+namespace {
+// Split-K slices for a grid of `tiles` output tiles: enough to give every SM a CTA, >= 4 K-blocks
+// (256 of K) per slice, slices aligned to the scale groups.
+void plan_splitk(const QMatrix &w, size_t M, int num_sms, int &ks, int &kb_per) {
+    const int kb_all = (int)(w.K / BK);
+    const long long tiles = ((long long)w.N + BM - 1) / BM * (((long long)M + BN - 1) / BN);
+    int gran = 1;
+    if (w.block_size != w.K) {
+        const int gk = (int)w.block_size;  // a multiple of 32
+        int a = BK, b = gk;                // lcm(BK, block) / BK
+        while (b) {
+            const int t = a % b;
+            a = b;
+            b = t;
+        }
+        gran = (BK / a) * gk / BK;
+        if (gran < 1) gran = 1;
+    }
+    ks = 1;
+    kb_per = kb_all;
+    if (tiles >= num_sms) return;
+    const int max_split = kb_all / std::max(gran, 4);
+    const int want = (int)((num_sms + tiles - 1) / tiles);
+    const int k = std::min(max_split, want);
+    if (k <= 1) return;
+    kb_per = (kb_all + k - 1) / k;
+    kb_per = (kb_per + gran - 1) / gran * gran;
+    ks = (kb_all + kb_per - 1) / kb_per;
+}
+}  // namespace
+
+size_t gemm_tc_workspace_bytes_splitk(size_t M, size_t N, size_t K, int block_size_is_k, size_t block_size,
+                                      int num_sms) {
+    QMatrix q{kQInt8, nullptr, nullptr, block_size_is_k ? K : block_size, N, K};
+    int ks, kb;
+    plan_splitk(q, M, num_sms, ks, kb);
+    return gemm_tc_workspace_bytes(M, K) + (ks > 1 ? align256((size_t)ks * M * N * 4) : 0);
+}
+
 cudaError_t launch_gemm_tc(const QMatrix &w, const float *X, size_t M, size_t ldx, float *Y, size_t ldy, void *ws,
-                           int *err, cudaStream_t st) {
+                           size_t ws_bytes, int *err, int num_sms, cudaStream_t st) {
     const int K = (int)w.K, N = (int)w.N;
     uint8_t *wsb = reinterpret_cast<uint8_t *>(ws);
     __half *xhi = reinterpret_cast<__half *>(wsb);
@@ -432,11 +494,27 @@ cudaError_t launch_gemm_tc(const QMatrix &w, const float *X, size_t M, size_t ld
     p.Y = Y;
     p.ldy = (long long)ldy;
     p.err = err;
+    int ks = 1, kb_per = K / BK;
+    plan_splitk(w, M, num_sms, ks, kb_per);
+    const size_t base = gemm_tc_workspace_bytes(M, (size_t)K);
+    if (ks > 1 && ws_bytes >= base + align256((size_t)ks * M * N * 4)) {
+        p.part = reinterpret_cast<float *>(wsb + base);
+    } else {
+        ks = 1;
+        kb_per = K / BK;
+        p.part = nullptr;
+    }
+    p.kb_per_split = kb_per;
     static const bool attr =
         cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) == cudaSuccess;
     if (!attr) return cudaErrorInvalidConfiguration;
-    dim3 grid((unsigned)((N + BM - 1) / BM), (unsigned)((M + BN - 1) / BN));
+    dim3 grid((unsigned)((N + BM - 1) / BM), (unsigned)((M + BN - 1) / BN), (unsigned)ks);
     gemm_tc_kernel<<<grid, kThreads, kSmemBytes, st>>>(tw, th, tl, p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess || ks == 1) return e;
+    const size_t MN = M * (size_t)N;
+    const unsigned rgrid = (unsigned)std::min<size_t>((MN + 255) / 256, (size_t)num_sms * 8);
+    splitk_reduce_kernel<<<rgrid, 256, 0, st>>>(p.part, ks, (int)M, N, Y, (long long)ldy);
     return cudaGetLastError();
 }
 

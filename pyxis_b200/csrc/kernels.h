@@ -55,9 +55,14 @@ const char *gemv_kernel_name(const QMatrix &w, size_t B, int num_sms);
 // Tensor-core prefill GEMM (gemm_tc.cu).  Supported when K % 64 == 0 and the scales are one per
 // row (block == K) or per group of a multiple of 32 that divides K.
 bool gemm_tc_supported(const QMatrix &w);
+// Workspace: gemm_tc_workspace_bytes(M, K) is enough; with gemm_tc_workspace_bytes_splitk(...)
+// bytes a GEMM with fewer output tiles than SMs also splits K over more CTAs (partials added in a
+// fixed order by a second kernel).
 size_t gemm_tc_workspace_bytes(size_t M, size_t K);
+size_t gemm_tc_workspace_bytes_splitk(size_t M, size_t N, size_t K, int block_size_is_k, size_t block_size,
+                                      int num_sms);
 cudaError_t launch_gemm_tc(const QMatrix &w, const float *X, size_t M, size_t ldx, float *Y, size_t ldy, void *ws,
-                           int *err, cudaStream_t st);
+                           size_t ws_bytes, int *err, int num_sms, cudaStream_t st);
 
 // int8 per-row GEMV for 1-8 input rows on tcgen05 kind::i8 (gemv_tc.cu).  `scratch` holds the
 // partial sums of tiles shared by two or more CTAs (one slot per CTA of a grid of up to
