@@ -7,20 +7,30 @@
 //   1. split_x: each token row is scaled by a power of two 2^e (max |x| -> [2^14, 2^15)) and split
 //      into fp16 hi + lo (x*2^e = hi + lo + O(2^-22 |x*2^e|)): 22 significant bits, as accurate
 //      against the reference's f32 sums as exact arithmetic (bf16 hi/lo keeps only 16).
-//   2. the tile kernel, one CTA per 128 weight rows x 128 tokens, warp-specialised:
+//   2. the tile kernel, one CTA per 128 weight rows x 128 tokens (x gridDim.z K slices when
+//      there are fewer tiles than SMs), warp-specialised:
 //        warp 0      TMA producer: raw int8/int4 codes + fp16 X hi/lo tiles into a 3-stage ring
-//        warp 1      TMEM owner and MMA issuer: tcgen05.mma kind::f16, M=128 N=128 K=16,
-//                    two MMAs (hi, lo) per K-step into an fp32 TMEM accumulator
-//        warps 2-5   converters: codes -> exact fp16 integers in the 128B-swizzled K-major layout
-//        warps 6-13  epilogue: tcgen05.ld the accumulator, apply scales, store Y
-//      Accumulation: each "period" of at most 64 K (4 K-steps, 8 MMAs) goes to one of two TMEM
-//      buffers; the epilogue folds it into fp32 registers (round-to-nearest) while the MMA warp
-//      fills the other buffer.  Long fp32 sums inside the tensor core drift (measured 1.9e-3 on
-//      the floor-relative metric for K = 2048 in one accumulator); 64-wide periods do not.
-//      Scales: one per row (block == K) is applied once at the end; a scale per group of G
-//      elements along K (int4 group 32, GGUF int8 block 32) multiplies each period of its group.
+//        warp 1      TMEM owner and MMA issuer: tcgen05.mma kind::f16, M=128, K=16; the token
+//                    tiles hi and lo sit back to back, so one N=256 MMA per K-step gives W x_hi in
+//                    accumulator columns [0,128) and W x_lo in [128,256) (N=64 pairs for tiles of
+//                    <= 64 tokens)
+//        warps 2-5   converters (one per weight row): codes -> the weight operand in the
+//                    128B-swizzled K-major layout.
+//                    One scale per row: the codes themselves, exact fp16 integers.  A scale per
+//                    group along K (int4 group 32, GGUF int8 block 32): q * s * 2^e (e per row,
+//                    keeping the values normal fp16) as fp16 hi + lo, and a second MMA per K-step
+//                    adds W_lo x_hi -- so group scales never force a fold.
+//        warps 6-21  epilogue: tcgen05.ld the accumulator (4 lane quarters x 4 column quarters),
+//                    fold, apply the row scale (or 2^-e) and the token's 2^-e', store Y
+//      Accumulation: each "period" of up to 256 of K goes to one of two TMEM buffers; the
+//      epilogue folds it into fp32 registers (round-to-nearest) while the MMA warp fills the
+//      other buffer.  Long fp32 sums inside the tensor core drift (measured 1.9e-3 on the
+//      floor-relative metric for K = 2048 in one accumulator: 256 accumulations); a period is at
+//      most 16 K-steps (16 or 32 accumulations per column).
+//      The MMA rate is bounded by the issuing thread's own instruction stream (a few scalar
+//      instructions per MMA cost as much as the MMA), so that loop carries no per-MMA bookkeeping.
 //   Weight codes are exact in fp16 and the token power of two is exact, so the only rounding
-//   besides the fp32 accumulation is the lo term's 2^-22.
+//   besides the fp32 accumulation is the lo terms' 2^-22 (and, with group scales, q * s in f32).
 //
 // Every mbarrier wait is bounded (globaltimer); a wait that runs out records an error code in
 // the context's device flag and the CTA winds down (drains its MMAs / copies, frees TMEM).
@@ -37,26 +47,29 @@ namespace pyxis {
 namespace {
 
 constexpr int BM = 128;  // weight rows per tile: MMA M, TMEM lanes
-constexpr int BN = 128;  // tokens per tile: MMA N, TMEM columns per accumulator
+constexpr int BN = 128;  // tokens per tile
 constexpr int BK = 64;   // K per stage: one 128-byte swizzle row of fp16
 constexpr int STAGES = 3;
-constexpr int kConvWarp0 = 2, kNumConvWarps = 4;
-constexpr int kEpiWarp0 = 6, kNumEpiWarps = 8;
-constexpr int kThreads = (kEpiWarp0 + kNumEpiWarps) * 32;  // 448
-constexpr uint32_t kTmemCols = 2 * BN;
-constexpr uint32_t kABytes = BM * BK * 2;
-constexpr uint32_t kBBytes = BN * BK * 2;
-constexpr uint32_t kRBytes = BM * 64;
+constexpr int kConvWarp0 = 2, kNumConvWarps = 4;            // one thread per weight row
+constexpr int kConvPerRow = kNumConvWarps * 32 / 128;      // threads per weight row (1 or 2)
+constexpr int kEpiWarp0 = kConvWarp0 + kNumConvWarps, kNumEpiWarps = 16;  // 4 lane x 4 column quarters
+constexpr int kThreads = (kEpiWarp0 + kNumEpiWarps) * 32;  // 704
+constexpr uint32_t kAccCols = 2 * BN;                      // one accumulator: x_hi columns | x_lo columns
+constexpr uint32_t kTmemCols = 2 * kAccCols;               // double-buffered: 512
+constexpr uint32_t kABytes = BM * BK * 2;                  // one fp16 weight tile
+constexpr uint32_t kBBytes = BN * BK * 2;                  // one fp16 token tile (hi or lo)
+constexpr uint32_t kRBytes = BM * 64;                      // raw codes of a stage (<= 64 B per row)
 constexpr uint64_t kTimeoutNs = 4000000000ull;
 
-constexpr uint32_t kOffA = 0;
-constexpr uint32_t kOffBhi = kOffA + STAGES * kABytes;
-constexpr uint32_t kOffBlo = kOffBhi + STAGES * kBBytes;
-constexpr uint32_t kOffR = kOffBlo + STAGES * kBBytes;
+constexpr uint32_t kOffAhi = 0;
+constexpr uint32_t kOffAlo = kOffAhi + STAGES * kABytes;
+constexpr uint32_t kOffB = kOffAlo + STAGES * kABytes;     // per stage: hi rows 0..127, lo rows 128..255
+constexpr uint32_t kOffR = kOffB + STAGES * 2 * kBBytes;
 constexpr uint32_t kOffBar = kOffR + STAGES * kRBytes;
 constexpr uint32_t kNumBars = 3 * STAGES + 2 + 2 + 1;
 constexpr uint32_t kOffMisc = kOffBar + kNumBars * 8;
-constexpr uint32_t kSmemBytes = kOffMisc + 16 + 1024;  // + alignment slack
+constexpr uint32_t kOffRowInv = kOffMisc + 16;             // [BM] per-row 2^-e of grouped weights
+constexpr uint32_t kSmemBytes = kOffRowInv + BM * 4 + 1024;  // + alignment slack
 
 // Device error codes (first one wins): which role's wait ran out.
 enum { kErrProducer = 0x101, kErrConverter = 0x102, kErrMma = 0x103, kErrEpilogue = 0x104, kErrDrain = 0x105 };
@@ -64,17 +77,17 @@ enum { kErrProducer = 0x101, kErrConverter = 0x102, kErrMma = 0x103, kErrEpilogu
 struct TcParams {
     int M, N, K;
     int qtype;
-    int per_row;            // 1: one scale per row (block == K)
+    int grouped;            // 0: one scale per row (block == K), applied at the end; 1: a scale per group
+    int group_k;            // grouped: elements per scale group (a multiple of 32)
+    int groups_per_row;     // grouped: K / group_k
     int ksteps_per_period;  // K-steps (16 each) accumulated in TMEM before the epilogue folds them
-    int periods_per_group;  // periods sharing one scale (per-group scales)
-    int groups_per_row;     // K / G (per-group scales)
     const float *scales;
-    const float *xinv;    // [M] 2^-e per token
+    const float *xinv;      // [M] 2^-e per token
     float *Y;
     long long ldy;
     int *err;
-    int kb_per_split;     // K-blocks of one blockIdx.z slice (split-K over gridDim.z)
-    float *part;          // split-K: [gridDim.z][M][N] partial products, else nullptr
+    int kb_per_split;       // K-blocks of one blockIdx.z slice (split-K over gridDim.z)
+    float *part;            // split-K: [gridDim.z][M][N] partial products, else nullptr
 };
 
 PYXIS_DEVINL uint32_t h2_bits(__half2 v) { return *reinterpret_cast<uint32_t *>(&v); }
@@ -96,8 +109,25 @@ PYXIS_DEVINL void u4x8_to_h(uint32_t w, uint32_t (&h)[4]) {
     for (int i = 0; i < 4; ++i) h[i] = h2_bits(__hsub2(bits_h2(((w >> (4 * i)) & 0x000F000Fu) | 0x64006400u), bias));
 }
 
+// Codes q (exact floats) times the scale s (f32, rounded once) as fp16 hi + lo pairs: 22
+// significant bits.  hi is w rounded to 11 bits by Veltkamp's split (c = w (2^13 + 1),
+// hi = c - (c - w)), so it converts to fp16 exactly and lo = w - hi is exact in f32: one
+// f32 -> f16 conversion per value (the conversion pipe is the converters' narrowest).
+PYXIS_DEVINL void split_pair(float q0, float q1, float s, uint32_t &hi, uint32_t &lo) {
+    const float w0 = __fmul_rn(q0, s), w1 = __fmul_rn(q1, s);
+    const float c0 = __fmul_rn(w0, 8193.0f), c1 = __fmul_rn(w1, 8193.0f);
+    const float h0 = __fsub_rn(c0, __fsub_rn(c0, w0)), h1 = __fsub_rn(c1, __fsub_rn(c1, w1));
+    hi = h2_bits(__floats2half2_rn(h0, h1));
+    lo = h2_bits(__floats2half2_rn(__fsub_rn(w0, h0), __fsub_rn(w1, h1)));
+}
+
 // Byte offset of 16-byte chunk c of row r in a 128B-swizzled K-major tile (8-row 1024 B atoms).
 PYXIS_DEVINL uint32_t sw128_off(int r, int c) { return (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4); }
+
+PYXIS_DEVINL void bar_arrive(int id, int n) { asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+PYXIS_DEVINL void bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+constexpr int kBarRowInv = 1;  // converters publish rowinv, the epilogue reads it at the end
+constexpr int kRowInvThreads = (kNumConvWarps + kNumEpiWarps) * 32;
 
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_xhi,
@@ -109,14 +139,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *accfull = bars + 3 * STAGES, *accempty = accfull + 2, *drain = accempty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffMisc);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + kOffMisc + 4);
+    float *rowinv = reinterpret_cast<float *>(smem + kOffRowInv);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * BM, m0 = blockIdx.y * BN;
     // this CTA's K range: K-blocks [kb0, kb0 + num_kb) (the whole of K without split-K)
     const int kb0 = blockIdx.z * p.kb_per_split;
     const int num_kb = min(p.K / BK - kb0, p.kb_per_split);
-    // a tile with <= 64 tokens multiplies with N = 64: the rest of the B tile is TMA zero fill
-    const int mma_n = p.M - m0 <= 64 ? 64 : BN;
+    // a tile with <= 64 tokens multiplies with N = 64: the rest of the token tile is TMA zero fill
+    const bool small = p.M - m0 <= 64;
     const int raw_kb_bytes = p.qtype == kQInt8 ? 64 : 32;
     const uint32_t stage_tx = 2 * kBBytes + (uint32_t)(BM * raw_kb_bytes);
 
@@ -155,9 +186,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     !tc::mbar_wait_bounded(&empty[s], ((j / STAGES) - 1) & 1, abort_flag, p.err, kErrProducer, kTimeoutNs))
                     break;
                 tc::mbar_arrive_expect_tx(&full[s], stage_tx);
+                uint8_t *b = smem + kOffB + s * 2 * kBBytes;
                 tc::tma_load_2d(smem + kOffR + s * kRBytes, &tm_w, kb * raw_kb_bytes, n0, &full[s]);
-                tc::tma_load_2d(smem + kOffBhi + s * kBBytes, &tm_xhi, kb * BK, m0, &full[s]);
-                tc::tma_load_2d(smem + kOffBlo + s * kBBytes, &tm_xlo, kb * BK, m0, &full[s]);
+                tc::tma_load_2d(b, &tm_xhi, kb * BK, m0, &full[s]);
+                tc::tma_load_2d(b + kBBytes, &tm_xlo, kb * BK, m0, &full[s]);
                 ++issued;
             }
             if (*abort_flag) {  // let the copies already issued land before the CTA exits
@@ -169,43 +201,64 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ------------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            const uint32_t idesc = tc::idesc_f16_f32(BM, mma_n);
-            int period = 0, kin = 0, buf = 0;
+            const uint32_t id_hilo = tc::idesc_f16_f32(BM, 2 * BN);  // rows x [x_hi; x_lo]
+            const uint32_t id_hi = tc::idesc_f16_f32(BM, BN);
+            const uint32_t id_64 = tc::idesc_f16_f32(BM, 64);
+            // The issuing thread's own instructions bound the MMA rate, so the loop is lean:
+            // descriptors advance by constant offsets per stage (start address in 16-byte units),
+            // K-steps are unrolled with immediate offsets, and fold periods are whole stages.
+            const uint64_t ahi0 = tc::desc_sw128(tc::smem_u32(smem + kOffAhi));
+            const uint64_t alo0 = tc::desc_sw128(tc::smem_u32(smem + kOffAlo));
+            const uint64_t b0 = tc::desc_sw128(tc::smem_u32(smem + kOffB));
+            const int spp = p.ksteps_per_period / (BK / 16);  // stages per fold period (>= 1)
+            const bool grouped = p.grouped != 0;
+            int period = 0, sp = 0, buf = 0, s = 0;
+            uint32_t par = 0;
             bool ok = true;
-            for (int j = 0; j < num_kb && ok; ++j) {
-                const int s = j % STAGES;
-                const uint32_t par = (j / STAGES) & 1;
+            for (int j = 0; j < num_kb; ++j) {
                 ok = tc::mbar_wait_bounded(&conv[s], par, abort_flag, p.err, kErrMma, kTimeoutNs) &&
                      tc::mbar_wait_bounded(&full[s], par, abort_flag, p.err, kErrMma, kTimeoutNs);
                 if (!ok) break;
-                tc::tc_fence_after();
-                const uint64_t a0 = tc::desc_sw128(tc::smem_u32(smem + kOffA + s * kABytes));
-                const uint64_t bh0 = tc::desc_sw128(tc::smem_u32(smem + kOffBhi + s * kBBytes));
-                const uint64_t bl0 = tc::desc_sw128(tc::smem_u32(smem + kOffBlo + s * kBBytes));
-#pragma unroll
-                for (int ks = 0; ks < BK / 16; ++ks) {
-                    if (kin == 0) {
-                        buf = period & 1;
-                        if (period >= 2) {
-                            if (!tc::mbar_wait_bounded(&accempty[buf], ((period >> 1) - 1) & 1, abort_flag, p.err,
-                                                       kErrMma, kTimeoutNs)) {
-                                ok = false;
-                                break;
-                            }
-                            tc::tc_fence_after();
-                        }
+                if (sp == 0) {
+                    buf = period & 1;
+                    if (period >= 2 && !tc::mbar_wait_bounded(&accempty[buf], ((period >> 1) - 1) & 1, abort_flag,
+                                                              p.err, kErrMma, kTimeoutNs)) {
+                        ok = false;
+                        break;
                     }
-                    const uint32_t d = tmem_base + (uint32_t)(buf * BN);
-                    const uint64_t koff = (uint64_t)(ks * 32) >> 4;  // 16 fp16 = 32 B along the swizzled row
-                    tc::mma_f16(d, a0 + koff, bh0 + koff, idesc, kin > 0 ? 1u : 0u);
-                    tc::mma_f16(d, a0 + koff, bl0 + koff, idesc, 1u);
-                    if (++kin == p.ksteps_per_period) {
-                        tc::mma_commit(&accfull[buf]);
-                        ++period;
-                        kin = 0;
+                }
+                tc::tc_fence_after();
+                const uint64_t ahi = ahi0 + (uint64_t)(s * (kABytes >> 4));
+                const uint64_t alo = alo0 + (uint64_t)(s * (kABytes >> 4));
+                const uint64_t bhi = b0 + (uint64_t)(s * (2 * kBBytes >> 4));
+                const uint64_t blo = bhi + (uint64_t)(kBBytes >> 4);
+                const uint32_t d = tmem_base + (uint32_t)(buf * kAccCols);
+                const uint32_t acc0 = sp > 0 ? 1u : 0u;  // the period's first K-step starts the sums
+                if (!small) {
+                    // columns [0, 128): W x_hi, [128, 256): W x_lo -- one instruction reads A once
+#pragma unroll
+                    for (int ks = 0; ks < BK / 16; ++ks) {
+                        tc::mma_f16(d, ahi + 2 * ks, bhi + 2 * ks, id_hilo, ks ? 1u : acc0);
+                        if (grouped) tc::mma_f16(d, alo + 2 * ks, bhi + 2 * ks, id_hi, 1u);
+                    }
+                } else {
+#pragma unroll
+                    for (int ks = 0; ks < BK / 16; ++ks) {
+                        tc::mma_f16(d, ahi + 2 * ks, bhi + 2 * ks, id_64, ks ? 1u : acc0);
+                        tc::mma_f16(d + BN, ahi + 2 * ks, blo + 2 * ks, id_64, ks ? 1u : acc0);
+                        if (grouped) tc::mma_f16(d, alo + 2 * ks, bhi + 2 * ks, id_64, 1u);
                     }
                 }
                 tc::mma_commit(&empty[s]);
+                if (++sp == spp) {
+                    tc::mma_commit(&accfull[buf]);
+                    ++period;
+                    sp = 0;
+                }
+                if (++s == STAGES) {
+                    s = 0;
+                    par ^= 1u;
+                }
             }
             // wait for every MMA this thread issued before TMEM can be released
             tc::mma_commit(drain);
@@ -214,37 +267,110 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp < kEpiWarp0) {
         // ------------------------------------------------------------------ converters
-        const int r = threadIdx.x - kConvWarp0 * 32;  // weight row within the tile
+        // Thread r owns weight row r of the tile.  Per-row scales: codes become exact fp16 integers
+        // (A_hi).  Group scales: every code pair is multiplied by its group's scale times a per-row
+        // power of two 2^e (max |q s| 2^e < 2^14, so hi and lo stay normal fp16) and split into
+        // A_hi + A_lo; the epilogue multiplies by 2^-e.
+        const int ct = threadIdx.x - kConvWarp0 * 32;
+        const int r = ct % BM, half = ct / BM;  // row r, part `half` of the stage's K
+        const int n = n0 + r;
+        const bool nrow = n < p.N;
+        const float *srow = p.scales + (size_t)(nrow ? n : 0) * p.groups_per_row;
+        float se = 1.f;
+        if (p.grouped) {
+            const int g0 = kb0 * BK / p.group_k, g1 = ((kb0 + num_kb) * BK + p.group_k - 1) / p.group_k;
+            float smax = 0.f;
+            if (nrow)
+                for (int g = g0; g < g1; ++g) smax = fmaxf(smax, fabsf(__ldg(srow + g)));
+            int e = 0;
+            const float bound = (p.qtype == kQInt8 ? 127.f : 8.f) * smax;
+            if (bound > 0.f && isfinite(bound)) {
+                int ex;
+                frexpf(bound, &ex);  // bound < 2^ex
+                e = min(100, max(-100, 14 - ex));
+            }
+            se = ldexpf(1.0f, e);
+            if (half == 0) rowinv[r] = ldexpf(1.0f, -e);
+        }
+        bar_arrive(kBarRowInv, kRowInvThreads);
+        const int epc = p.qtype == kQInt8 ? 16 : 32;  // codes per 16-byte raw chunk
+        constexpr int kChunks8 = 4 / kConvPerRow, kChunks4 = 2 / kConvPerRow;  // raw chunks per thread
+        // scale x 2^e of this thread's raw chunks, read one stage ahead (the converters are the
+        // slowest role for group scales, so an L2 round trip per stage would be exposed)
+        float sc_next[kChunks8] = {};
+        auto load_scales = [&](int kb) {
+            if (!p.grouped || !nrow || kb >= kb0 + num_kb) return;
+            const int k0 = kb * BK + half * (BK / kConvPerRow);
+#pragma unroll
+            for (int cc = 0; cc < kChunks8; ++cc)
+                if (cc * epc < BK / kConvPerRow) sc_next[cc] = __ldg(srow + (k0 + cc * epc) / p.group_k) * se;
+        };
+        load_scales(kb0);
         for (int j = 0; j < num_kb; ++j) {
-            const int s = j % STAGES;
+            const int s = j % STAGES, kb = kb0 + j;
+            float sc[kChunks8];
+#pragma unroll
+            for (int cc = 0; cc < kChunks8; ++cc) sc[cc] = sc_next[cc];
+            load_scales(kb + 1);
             int ok = 1;
             if (lane == 0) ok = tc::mbar_wait_bounded(&full[s], (j / STAGES) & 1, abort_flag, p.err, kErrConverter, kTimeoutNs);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             const uint8_t *raw = smem + kOffR + s * kRBytes;
-            uint8_t *a = smem + kOffA + s * kABytes;
+            uint8_t *ahi = smem + kOffAhi + s * kABytes;
+            uint8_t *alo = smem + kOffAlo + s * kABytes;
             if (p.qtype == kQInt8) {
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {  // 64-byte rows, 64-byte TMA swizzle
+                for (int cc = 0; cc < kChunks8; ++cc) {  // 64-byte rows, 64-byte TMA swizzle
+                    const int c = kChunks8 * half + cc;
                     const uint4 w = *reinterpret_cast<const uint4 *>(raw + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
-                    uint4 o0, o1;
-                    i8x4_to_h(w.x, o0.x, o0.y);
-                    i8x4_to_h(w.y, o0.z, o0.w);
-                    i8x4_to_h(w.z, o1.x, o1.y);
-                    i8x4_to_h(w.w, o1.z, o1.w);
-                    *reinterpret_cast<uint4 *>(a + sw128_off(r, 2 * c)) = o0;
-                    *reinterpret_cast<uint4 *>(a + sw128_off(r, 2 * c + 1)) = o1;
+                    if (!p.grouped) {
+                        uint32_t h[8];
+                        i8x4_to_h(w.x, h[0], h[1]);
+                        i8x4_to_h(w.y, h[2], h[3]);
+                        i8x4_to_h(w.z, h[4], h[5]);
+                        i8x4_to_h(w.w, h[6], h[7]);
+                        *reinterpret_cast<uint4 *>(ahi + sw128_off(r, 2 * c)) = make_uint4(h[0], h[1], h[2], h[3]);
+                        *reinterpret_cast<uint4 *>(ahi + sw128_off(r, 2 * c + 1)) = make_uint4(h[4], h[5], h[6], h[7]);
+                    } else {
+                        float2 f[8];  // the 16 codes as exact floats, natural order
+                        i8x4_to_f32(w.x, f[0], f[1]);
+                        i8x4_to_f32(w.y, f[2], f[3]);
+                        i8x4_to_f32(w.z, f[4], f[5]);
+                        i8x4_to_f32(w.w, f[6], f[7]);
+                        uint32_t hi[8], lo[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) split_pair(f[i].x, f[i].y, sc[cc], hi[i], lo[i]);
+                        *reinterpret_cast<uint4 *>(ahi + sw128_off(r, 2 * c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                        *reinterpret_cast<uint4 *>(ahi + sw128_off(r, 2 * c + 1)) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+                        *reinterpret_cast<uint4 *>(alo + sw128_off(r, 2 * c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                        *reinterpret_cast<uint4 *>(alo + sw128_off(r, 2 * c + 1)) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+                    }
                 }
             } else {
 #pragma unroll
-                for (int c = 0; c < 2; ++c) {  // 32-byte rows, 32-byte TMA swizzle
+                for (int cc = 0; cc < kChunks4; ++cc) {
+                    const int c = kChunks4 * half + cc;  // 32-byte rows, 32-byte TMA swizzle
                     const uint4 w = *reinterpret_cast<const uint4 *>(raw + r * 32 + ((c ^ ((r >> 2) & 1)) << 4));
                     const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        uint32_t h[4];
-                        u4x8_to_h(ws[j], h);
-                        *reinterpret_cast<uint4 *>(a + sw128_off(r, 4 * c + j)) = make_uint4(h[0], h[1], h[2], h[3]);
+                    for (int jj = 0; jj < 4; ++jj) {
+                        if (!p.grouped) {
+                            uint32_t h[4];
+                            u4x8_to_h(ws[jj], h);
+                            *reinterpret_cast<uint4 *>(ahi + sw128_off(r, 4 * c + jj)) = make_uint4(h[0], h[1], h[2], h[3]);
+                        } else {
+                            // exact floats, paired in the converter order (e0,e4) (e1,e5) (e2,e6) (e3,e7)
+                            float2 e01, e23, e45, e67;
+                            u4x8_to_f32(ws[jj], e01, e23, e45, e67);
+                            uint32_t hi[4], lo[4];
+                            split_pair(e01.x, e45.x, sc[cc], hi[0], lo[0]);
+                            split_pair(e01.y, e45.y, sc[cc], hi[1], lo[1]);
+                            split_pair(e23.x, e67.x, sc[cc], hi[2], lo[2]);
+                            split_pair(e23.y, e67.y, sc[cc], hi[3], lo[3]);
+                            *reinterpret_cast<uint4 *>(ahi + sw128_off(r, 4 * c + jj)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                            *reinterpret_cast<uint4 *>(alo + sw128_off(r, 4 * c + jj)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                        }
                     }
                 }
             }
@@ -255,27 +381,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // ------------------------------------------------------------------ epilogue
         const int q = warp & 3;                 // TMEM lane quarter this warp may access
-        const int h = (warp - kEpiWarp0) >> 2;  // column half
-        const int n = n0 + 32 * q + lane;
+        const int h = (warp - kEpiWarp0) >> 2;  // column quarter: tokens m0 + 32 h ...
+        const int rl = 32 * q + lane;
+        const int n = n0 + rl;
         const bool row_ok = n < p.N;
-        float acc[64];
+        float acc[32];
 #pragma unroll
-        for (int j = 0; j < 64; ++j) acc[j] = 0.f;
+        for (int j = 0; j < 32; ++j) acc[j] = 0.f;
         const int num_periods = num_kb * BK / (16 * p.ksteps_per_period);
-        const int ppg = p.periods_per_group;
-        const int group_k = 16 * p.ksteps_per_period * ppg;  // K per scale group
-        const int num_groups = p.per_row ? 0 : num_kb * BK / group_k;
-        const float *srow = p.scales + (size_t)(row_ok ? n : 0) * p.groups_per_row + (p.per_row ? 0 : kb0 * BK / group_k);
-        float s_cur[4], s_nxt[4];  // scales of groups g0..g0+3 and g0+4..g0+7
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            s_cur[i] = (row_ok && i < num_groups) ? __ldg(srow + i) : 0.f;
-            s_nxt[i] = (row_ok && 4 + i < num_groups) ? __ldg(srow + 4 + i) : 0.f;
-        }
         bool ok = true;
         for (int pd = 0; pd < num_periods; ++pd) {
             const int b = pd & 1;
-            const int g = pd / ppg;
             int w_ok = 1;
             if (lane == 0) w_ok = tc::mbar_wait_bounded(&accfull[b], (pd >> 1) & 1, abort_flag, p.err, kErrEpilogue, kTimeoutNs);
             w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
@@ -284,38 +400,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             tc::tc_fence_after();
-            const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * BN + 64 * h);
-            const int i = g & 3;
-            const float sg = i == 0 ? s_cur[0] : i == 1 ? s_cur[1] : i == 2 ? s_cur[2] : s_cur[3];
+            const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * kAccCols + 32 * h);
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                float v[32];
-                tc::tmem_ld32(taddr + 32 * half, v);
-                if (p.per_row) {
+            for (int part = 0; part < 2; ++part) {  // W x_hi, then W x_lo
+                uint32_t v[32];
+                tc::tmem_ld32_async(taddr + part * BN, v);
+                tc::tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) acc[32 * half + j] += v[j];
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) acc[32 * half + j] = fmaf(sg, v[j], acc[32 * half + j]);
-                }
+                for (int j = 0; j < 32; ++j) acc[j] += __uint_as_float(v[j]);
             }
             tc::tc_fence_before();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&accempty[b]);
-            if (!p.per_row && i == 3 && (pd + 1) % ppg == 0) {  // last period of group g0+3: rotate
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    s_cur[t] = s_nxt[t];
-                    const int gn = g + 5 + t;
-                    s_nxt[t] = (row_ok && gn < num_groups) ? __ldg(srow + gn) : 0.f;
-                }
-            }
         }
+        bar_sync(kBarRowInv, kRowInvThreads);
         if (ok && row_ok) {
-            const float sr = p.per_row ? __ldg(p.scales + n) : 1.0f;
+            const float sr = p.grouped ? rowinv[rl] : __ldg(p.scales + n);
 #pragma unroll
-            for (int j = 0; j < 64; ++j) {
-                const int m = m0 + 64 * h + j;
+            for (int j = 0; j < 32; ++j) {
+                const int m = m0 + 32 * h + j;
                 if (m >= p.M) continue;
                 const float y = acc[j] * sr * __ldg(p.xinv + m);
                 if (p.part) p.part[((size_t)blockIdx.z * p.M + m) * p.N + n] = y;
@@ -414,23 +517,34 @@ bool gemm_tc_supported(const QMatrix &w) {
 size_t gemm_tc_workspace_bytes(size_t M, size_t K) { return 2 * align256(M * K * 2) + align256(M * 4); }
 
 namespace {
+// K-steps (16 of K each) accumulated in TMEM before the epilogue folds them into fp32 registers:
+// the largest power of two <= 16 dividing K / 16, i.e. chains of at most 256 of K (16 or 32 MMA
+// accumulations per column).  One accumulator over K = 2048 (256 accumulations) measured 1.9e-3 on
+// the parity metric; group scales live in the A operand, so folds need not follow the groups.
+int fold_steps(const QMatrix &w) {
+    const int steps = (int)(w.K / 16);
+    int kpp = 16;
+    while (kpp > 1 && steps % kpp) kpp >>= 1;
+    return kpp;
+}
+
+int gcd_int(int a, int b) {
+    while (b) {
+        const int t = a % b;
+        a = b;
+        b = t;
+    }
+    return a;
+}
+
 // Split-K slices for a grid of `tiles` output tiles: enough to give every SM a CTA, >= 4 K-blocks
-// (256 of K) per slice, slices aligned to the scale groups.
+// (256 of K) per slice, slices aligned to the fold periods and the scale groups.
 void plan_splitk(const QMatrix &w, size_t M, int num_sms, int &ks, int &kb_per) {
     const int kb_all = (int)(w.K / BK);
     const long long tiles = ((long long)w.N + BM - 1) / BM * (((long long)M + BN - 1) / BN);
-    int gran = 1;
-    if (w.block_size != w.K) {
-        const int gk = (int)w.block_size;  // a multiple of 32
-        int a = BK, b = gk;                // lcm(BK, block) / BK
-        while (b) {
-            const int t = a % b;
-            a = b;
-            b = t;
-        }
-        gran = (BK / a) * gk / BK;
-        if (gran < 1) gran = 1;
-    }
+    int unit = 16 * fold_steps(w);          // K of a fold period
+    unit = unit / gcd_int(unit, BK) * BK;   // lcm with the K-block
+    const int gran = unit / BK;
     ks = 1;
     kb_per = kb_all;
     if (tiles >= num_sms) return;
@@ -482,13 +596,12 @@ cudaError_t launch_gemm_tc(const QMatrix &w, const float *X, size_t M, size_t ld
     p.N = N;
     p.K = K;
     p.qtype = w.qtype;
-    p.per_row = w.block_size == w.K ? 1 : 0;
-    // TMEM accumulation chains stay short (<= 64 along K); longer sums are folded in fp32
+    p.grouped = w.block_size == w.K ? 0 : 1;
+    // TMEM accumulation chains stay short (<= 256 along K); longer sums are folded in fp32
     // registers with round-to-nearest, so the drift of long tensor-core accumulations never builds.
-    const int group_steps = p.per_row ? K / 16 : (int)(w.block_size / 16);
-    p.ksteps_per_period = group_steps < 4 ? group_steps : 4;
-    p.periods_per_group = group_steps / p.ksteps_per_period;
-    p.groups_per_row = p.per_row ? 1 : (int)(w.K / w.block_size);
+    p.ksteps_per_period = fold_steps(w);
+    p.group_k = p.grouped ? (int)w.block_size : K;
+    p.groups_per_row = p.grouped ? (int)(w.K / w.block_size) : 1;
     p.scales = w.scales;
     p.xinv = xinv;
     p.Y = Y;

@@ -40,15 +40,39 @@ PYXIS_DEVINL bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait: spins until the phase with `parity` completes, or until `abort` is raised by
-// another thread, or until deadline_ns passes (then records `code` in *err, raises abort).
-// Returns false when the caller must stop.
+// try_wait with a suspend-time hint: the warp sleeps until the phase completes (or about
+// `hint_ns` passes) instead of spinning, leaving the issue slots to the warps doing the work.
+PYXIS_DEVINL bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Non-blocking probe of the phase with `parity` (never suspends the thread).
+PYXIS_DEVINL bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: sleeps in try_wait until the phase with `parity` completes, or until `abort` is
+// raised by another thread, or until deadline_ns passes (then records `code` in *err, raises
+// abort).  Returns false when the caller must stop.  (Polling with test_wait instead measured
+// slower in every kernel here: the spinning warps take issue slots from the working ones.)
 PYXIS_DEVINL bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, volatile int *abort, int *err, int code,
                                     uint64_t timeout_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (;;) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_sleep(bar, parity, 200000u)) return true;
         if (*abort) return false;
         if (globaltimer_ns() - t0 > timeout_ns) {
             atomicCAS(err, 0, code);
@@ -112,6 +136,20 @@ PYXIS_DEVINL void mma_commit(uint64_t *bar) {
 }
 
 // 32 consecutive fp32 columns of this warp's 32 TMEM lanes (lane quarter = warp id % 4).
+// 32 lanes x 32 columns without waiting: the registers are valid after tmem_wait_ld().
+PYXIS_DEVINL void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
+          "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+          "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+PYXIS_DEVINL void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
 PYXIS_DEVINL void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     uint32_t r[32];
     asm volatile(
