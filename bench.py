@@ -146,6 +146,8 @@ def dist_setup():
         import torch
         import torch.distributed as dist
 
+        # NCCL's informational lines go to stdout; the bench's stdout is its one JSON line
+        os.environ["NCCL_DEBUG"] = "WARN"
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
