@@ -405,6 +405,66 @@ def run_batch_decode(local, ws, rank, n_seq_total=BATCH_SEQS, P=BATCH_PROMPT, n_
             "first_tokens": [int(t) for t in toks[0, :8]]}
 
 
+def run_config1(local, capture, replay_ms, with_cpu):
+    """One int8 per-row matvec, gate_proj 6144 x 2048, batch 1: device time (graph over rotating
+    packed copies, each read from HBM), the host-pointer call (x in, y out), and the oracle port of
+    the reference's Rayon matmul on the same shape."""
+    import ctypes as C
+
+    import numpy as np
+    import torch
+
+    import pyxis_b200 as px
+    from pyxis_b200 import _native
+
+    N, K = 6144, 2048
+    dev = torch.device("cuda", local)
+    bits = px.synth_normal_bf16(SEED + 7, N * K, 0.02)
+    t = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).to(dev)
+    copies = [px.Weights.quantize_int8(t, K, device=local) for _ in range(24)]  # 24 x 12.6 MB > 2 x L2
+    del t
+    x = torch.from_numpy(px.synth_normal_f32(SEED + 8, K, 1.0)).to(dev).view(1, K)
+    y = torch.empty((1, N), dtype=torch.float32, device=dev)
+
+    def fn(st):
+        for w in copies:
+            px.matmul_dev(x, w, N, K, Y=y, stream=st)
+
+    g = capture(fn)
+    g.replay()
+    us = replay_ms(g, 4) / (4 * len(copies)) * 1e3
+    del g
+    by = gemv_bytes("int8", N, K, K, 1)
+    hx = torch.from_numpy(px.synth_normal_f32(SEED + 8, K, 1.0)).pin_memory()
+    hy = torch.empty(N, dtype=torch.float32).pin_memory()
+    L = _native.lib()
+    w0 = copies[0]
+    for _ in range(3):
+        _native.check(L.pyxis_cuda_matmul(w0.ctx.handle, C.c_void_p(hx.data_ptr()), w0.handle, N, K,
+                                          C.c_void_p(hy.data_ptr())))
+    t0 = time.perf_counter()
+    for _ in range(50):
+        _native.check(L.pyxis_cuda_matmul(w0.ctx.handle, C.c_void_p(hx.data_ptr()), w0.handle, N, K,
+                                          C.c_void_p(hy.data_ptr())))
+    e2e_us = (time.perf_counter() - t0) / 50 * 1e6
+    out = {"workload": "int8 per-row matvec, gate_proj 6144 x 2048, batch 1", "kernel": px.matmul_kernel_name(w0, 1, N, K),
+           "device_us": round(us, 2), "device_gbs": round(by / us / 1e3, 1), "e2e_us": round(e2e_us, 2),
+           "e2e_gbs": round(by / e2e_us / 1e3, 1)}
+    if with_cpu:
+        import oracle
+        vals = oracle.bf16_to_f32(bits)
+        d, sc = oracle.quantize_int8(vals, K)
+        xs = px.synth_normal_f32(SEED + 8, K, 1.0).reshape(1, K)
+        cores = oracle.num_cpus()
+        oracle.matmul(xs, oracle.INT8, d, sc, K, N, K, nthreads=cores)
+        t0 = time.perf_counter()
+        for _ in range(20):
+            oracle.matmul(xs, oracle.INT8, d, sc, K, N, K, nthreads=cores)
+        cpu_us = (time.perf_counter() - t0) / 20 * 1e6
+        out["cpu_baseline"] = {"us": round(cpu_us, 1), "gbs": round(by / cpu_us / 1e3, 2), "cores": cores, "kind": "port"}
+    return out
+
+
 def pyxis_arm(args, ws, rank, local):
     import numpy as np
     import torch
@@ -569,6 +629,8 @@ def pyxis_arm(args, ws, rank, local):
     e2e_s = max_over_ranks(time.perf_counter() - t0, ws)
     e2e_value = ws * sb * args.steps / e2e_s / 1e9
 
+    config1 = run_config1(local, capture, replay_ms, rank == 0 and ws == 1 and not args.no_cpu_baseline)
+
     lm_vp = None
     if ws > 1:
         lm_vp = run_vocab_parallel_head(ws, rank, local, args.steps)
@@ -632,6 +694,7 @@ def pyxis_arm(args, ws, rank, local):
                 "cpu_baseline": cpu, "clocks": clk, "gpu_launches": launches_per_step * args.steps,
                 "eager_ms_per_step": eager_ms_max / args.steps,
                 "cases": cases,
+                "config1": config1,
                 "decode": decode,
                 "batch_decode": batch,
                 "lm_head_vocab_parallel": lm_vp,
