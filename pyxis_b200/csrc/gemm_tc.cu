@@ -129,6 +129,78 @@ PYXIS_DEVINL void bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r
 constexpr int kBarRowInv = 1;  // converters publish rowinv, the epilogue reads it at the end
 constexpr int kRowInvThreads = (kNumConvWarps + kNumEpiWarps) * 32;
 
+struct MmaRing {
+    uint64_t *full, *conv, *empty, *accfull, *accempty;
+    volatile int *abort_flag;
+    int *err;
+};
+
+// The MMA issuer for fold periods of SPP stages.  The issuing thread's own instruction stream
+// bounds the tensor pipe: a ring slot, parity or accumulator buffer computed at run time between
+// the MMAs measured up to 1.8x slower than the pipe's 128 cycles per 128x256x16 MMA.  So the loop
+// is unrolled over lcm(STAGES, 2 SPP) stages, which makes the ring slot, the phase parities, the
+// TMEM buffer and the commit points compile-time and advances the descriptors by immediates.
+// Returns false when a wait gave up (the error is recorded, the abort flag raised).
+template <int SPP, bool GROUPED, bool SMALL>
+__device__ __forceinline__ bool mma_loop(int num_kb, uint64_t ahi0, uint64_t alo0, uint64_t b0, uint32_t tmem_base,
+                                      const MmaRing r) {
+    static_assert(STAGES == 3, "lcm(STAGES, 2 SPP) = 6 SPP needs an odd ring of 3");
+    constexpr int U = STAGES * 2 * SPP;
+    constexpr uint32_t id_hilo = tc::idesc_f16_f32(BM, 2 * BN);  // rows x [x_hi; x_lo]
+    constexpr uint32_t id_hi = tc::idesc_f16_f32(BM, BN);
+    constexpr uint32_t id_64 = tc::idesc_f16_f32(BM, 64);
+    for (int j0 = 0; j0 < num_kb; j0 += U) {
+        // j0 is a multiple of U: j0 / STAGES and j0 / SPP are even, so the ring parity and the
+        // accumulator buffer of stage j0 + jj depend on jj alone
+#pragma unroll
+        for (int jj = 0; jj < U; ++jj) {
+            if (j0 + jj >= num_kb) return true;
+            const int s = jj % STAGES, sp = jj % SPP, buf = (jj / SPP) & 1;
+            const uint32_t par = (uint32_t)((jj / STAGES) & 1);
+            if (!tc::mbar_wait_bounded(&r.conv[s], par, r.abort_flag, r.err, kErrMma, kTimeoutNs) ||
+                !tc::mbar_wait_bounded(&r.full[s], par, r.abort_flag, r.err, kErrMma, kTimeoutNs))
+                return false;
+            if (sp == 0) {
+                const int period = (j0 + jj) / SPP;
+                if (period >= 2 && !tc::mbar_wait_bounded(&r.accempty[buf], (uint32_t)(((period >> 1) - 1) & 1),
+                                                          r.abort_flag, r.err, kErrMma, kTimeoutNs))
+                    return false;
+            }
+            tc::tc_fence_after();
+            const uint64_t ahi = ahi0 + (uint64_t)(s * (kABytes >> 4));
+            const uint64_t alo = alo0 + (uint64_t)(s * (kABytes >> 4));
+            const uint64_t bhi = b0 + (uint64_t)(s * (2 * kBBytes >> 4));
+            const uint64_t blo = bhi + (uint64_t)(kBBytes >> 4);
+            const uint32_t d = tmem_base + (uint32_t)(buf * kAccCols);
+#pragma unroll
+            for (int ks = 0; ks < BK / 16; ++ks) {
+                const uint32_t acc = (ks | sp) ? 1u : 0u;  // a period's first K-step starts the sums
+                if (!SMALL) {
+                    // columns [0, 128): W x_hi, [128, 256): W x_lo -- one instruction reads A once
+                    tc::mma_f16(d, ahi + 2 * ks, bhi + 2 * ks, id_hilo, acc);
+                    if (GROUPED) tc::mma_f16(d, alo + 2 * ks, bhi + 2 * ks, id_hi, 1u);
+                } else {
+                    // <= 64 tokens: the rest of the token tile is TMA zero fill
+                    tc::mma_f16(d, ahi + 2 * ks, bhi + 2 * ks, id_64, acc);
+                    tc::mma_f16(d + BN, ahi + 2 * ks, blo + 2 * ks, id_64, acc);
+                    if (GROUPED) tc::mma_f16(d, alo + 2 * ks, bhi + 2 * ks, id_64, 1u);
+                }
+            }
+            tc::mma_commit(&r.empty[s]);
+            if (sp == SPP - 1) tc::mma_commit(&r.accfull[buf]);
+        }
+    }
+    return true;
+}
+
+template <bool GROUPED, bool SMALL>
+__device__ __forceinline__ bool mma_loop_spp(int spp, int num_kb, uint64_t ahi0, uint64_t alo0, uint64_t b0,
+                                             uint32_t tmem_base, const MmaRing &r) {
+    if (spp == 4) return mma_loop<4, GROUPED, SMALL>(num_kb, ahi0, alo0, b0, tmem_base, r);
+    if (spp == 2) return mma_loop<2, GROUPED, SMALL>(num_kb, ahi0, alo0, b0, tmem_base, r);
+    return mma_loop<1, GROUPED, SMALL>(num_kb, ahi0, alo0, b0, tmem_base, r);
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_xhi,
                    const __grid_constant__ CUtensorMap tm_xlo, const TcParams p) {
@@ -201,64 +273,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ------------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            const uint32_t id_hilo = tc::idesc_f16_f32(BM, 2 * BN);  // rows x [x_hi; x_lo]
-            const uint32_t id_hi = tc::idesc_f16_f32(BM, BN);
-            const uint32_t id_64 = tc::idesc_f16_f32(BM, 64);
-            // The issuing thread's own instructions bound the MMA rate, so the loop is lean:
-            // descriptors advance by constant offsets per stage (start address in 16-byte units),
-            // K-steps are unrolled with immediate offsets, and fold periods are whole stages.
             const uint64_t ahi0 = tc::desc_sw128(tc::smem_u32(smem + kOffAhi));
             const uint64_t alo0 = tc::desc_sw128(tc::smem_u32(smem + kOffAlo));
             const uint64_t b0 = tc::desc_sw128(tc::smem_u32(smem + kOffB));
-            const int spp = p.ksteps_per_period / (BK / 16);  // stages per fold period (>= 1)
-            const bool grouped = p.grouped != 0;
-            int period = 0, sp = 0, buf = 0, s = 0;
-            uint32_t par = 0;
-            bool ok = true;
-            for (int j = 0; j < num_kb; ++j) {
-                ok = tc::mbar_wait_bounded(&conv[s], par, abort_flag, p.err, kErrMma, kTimeoutNs) &&
-                     tc::mbar_wait_bounded(&full[s], par, abort_flag, p.err, kErrMma, kTimeoutNs);
-                if (!ok) break;
-                if (sp == 0) {
-                    buf = period & 1;
-                    if (period >= 2 && !tc::mbar_wait_bounded(&accempty[buf], ((period >> 1) - 1) & 1, abort_flag,
-                                                              p.err, kErrMma, kTimeoutNs)) {
-                        ok = false;
-                        break;
-                    }
-                }
-                tc::tc_fence_after();
-                const uint64_t ahi = ahi0 + (uint64_t)(s * (kABytes >> 4));
-                const uint64_t alo = alo0 + (uint64_t)(s * (kABytes >> 4));
-                const uint64_t bhi = b0 + (uint64_t)(s * (2 * kBBytes >> 4));
-                const uint64_t blo = bhi + (uint64_t)(kBBytes >> 4);
-                const uint32_t d = tmem_base + (uint32_t)(buf * kAccCols);
-                const uint32_t acc0 = sp > 0 ? 1u : 0u;  // the period's first K-step starts the sums
-                if (!small) {
-                    // columns [0, 128): W x_hi, [128, 256): W x_lo -- one instruction reads A once
-#pragma unroll
-                    for (int ks = 0; ks < BK / 16; ++ks) {
-                        tc::mma_f16(d, ahi + 2 * ks, bhi + 2 * ks, id_hilo, ks ? 1u : acc0);
-                        if (grouped) tc::mma_f16(d, alo + 2 * ks, bhi + 2 * ks, id_hi, 1u);
-                    }
-                } else {
-#pragma unroll
-                    for (int ks = 0; ks < BK / 16; ++ks) {
-                        tc::mma_f16(d, ahi + 2 * ks, bhi + 2 * ks, id_64, ks ? 1u : acc0);
-                        tc::mma_f16(d + BN, ahi + 2 * ks, blo + 2 * ks, id_64, ks ? 1u : acc0);
-                        if (grouped) tc::mma_f16(d, alo + 2 * ks, bhi + 2 * ks, id_64, 1u);
-                    }
-                }
-                tc::mma_commit(&empty[s]);
-                if (++sp == spp) {
-                    tc::mma_commit(&accfull[buf]);
-                    ++period;
-                    sp = 0;
-                }
-                if (++s == STAGES) {
-                    s = 0;
-                    par ^= 1u;
-                }
+            const MmaRing ring{full, conv, empty, accfull, accempty, abort_flag, p.err};
+            const int spp = p.ksteps_per_period / (BK / 16);  // stages per fold period: 1, 2 or 4
+            if (p.grouped) {
+                if (small) mma_loop_spp<true, true>(spp, num_kb, ahi0, alo0, b0, tmem_base, ring);
+                else mma_loop_spp<true, false>(spp, num_kb, ahi0, alo0, b0, tmem_base, ring);
+            } else {
+                if (small) mma_loop_spp<false, true>(spp, num_kb, ahi0, alo0, b0, tmem_base, ring);
+                else mma_loop_spp<false, false>(spp, num_kb, ahi0, alo0, b0, tmem_base, ring);
             }
             // wait for every MMA this thread issued before TMEM can be released
             tc::mma_commit(drain);
@@ -280,8 +305,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.grouped) {
             const int g0 = kb0 * BK / p.group_k, g1 = ((kb0 + num_kb) * BK + p.group_k - 1) / p.group_k;
             float smax = 0.f;
-            if (nrow)
-                for (int g = g0; g < g1; ++g) smax = fmaxf(smax, fabsf(__ldg(srow + g)));
+            if (nrow) {
+                // all loads of a batch in flight before the first use: one memory latency per
+                // 32 groups instead of one per few groups (this scan precedes the first stage)
+                const float *sg = srow + g0;
+                const int ng = g1 - g0;
+                int g = 0;
+                if ((reinterpret_cast<uintptr_t>(sg) & 15) == 0) {
+                    const float4 *s4 = reinterpret_cast<const float4 *>(sg);
+                    for (; g + 32 <= ng; g += 32) {
+                        float4 v[8];
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) v[u] = __ldg(s4 + g / 4 + u);
+#pragma unroll
+                        for (int u = 0; u < 8; ++u)
+                            smax = fmaxf(smax, fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w))));
+                    }
+                }
+#pragma unroll 8
+                for (; g < ng; ++g) smax = fmaxf(smax, fabsf(__ldg(sg + g)));
+            }
             int e = 0;
             const float bound = (p.qtype == kQInt8 ? 127.f : 8.f) * smax;
             if (bound > 0.f && isfinite(bound)) {
@@ -295,23 +338,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         bar_arrive(kBarRowInv, kRowInvThreads);
         const int epc = p.qtype == kQInt8 ? 16 : 32;  // codes per 16-byte raw chunk
         constexpr int kChunks8 = 4 / kConvPerRow, kChunks4 = 2 / kConvPerRow;  // raw chunks per thread
-        // scale x 2^e of this thread's raw chunks, read one stage ahead (the converters are the
-        // slowest role for group scales, so an L2 round trip per stage would be exposed)
-        float sc_next[kChunks8] = {};
-        auto load_scales = [&](int kb) {
+        // scale x 2^e of this thread's raw chunks, read two stages ahead (the converters are the
+        // slowest role for group scales: a memory round trip per stage would be exposed)
+        // (a shift when the group size is a power of two: a division per chunk measured slower)
+        const int gshift = (p.group_k & (p.group_k - 1)) == 0 ? __ffs(p.group_k) - 1 : -1;
+        float sc_n1[kChunks8] = {}, sc_n2[kChunks8] = {};
+        auto load_scales = [&](int kb, float (&dst)[kChunks8]) {
             if (!p.grouped || !nrow || kb >= kb0 + num_kb) return;
             const int k0 = kb * BK + half * (BK / kConvPerRow);
 #pragma unroll
             for (int cc = 0; cc < kChunks8; ++cc)
-                if (cc * epc < BK / kConvPerRow) sc_next[cc] = __ldg(srow + (k0 + cc * epc) / p.group_k) * se;
+                if (cc * epc < BK / kConvPerRow) {
+                    const int k = k0 + cc * epc;
+                    dst[cc] = __ldg(srow + (gshift >= 0 ? k >> gshift : k / p.group_k)) * se;
+                }
         };
-        load_scales(kb0);
+        load_scales(kb0, sc_n1);
+        load_scales(kb0 + 1, sc_n2);
         for (int j = 0; j < num_kb; ++j) {
             const int s = j % STAGES, kb = kb0 + j;
             float sc[kChunks8];
 #pragma unroll
-            for (int cc = 0; cc < kChunks8; ++cc) sc[cc] = sc_next[cc];
-            load_scales(kb + 1);
+            for (int cc = 0; cc < kChunks8; ++cc) {
+                sc[cc] = sc_n1[cc];
+                sc_n1[cc] = sc_n2[cc];
+            }
+            load_scales(kb + 2, sc_n2);
             int ok = 1;
             if (lane == 0) ok = tc::mbar_wait_bounded(&full[s], (j / STAGES) & 1, abort_flag, p.err, kErrConverter, kTimeoutNs);
             ok = __shfl_sync(0xffffffffu, ok, 0);
