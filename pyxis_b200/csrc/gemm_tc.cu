@@ -49,7 +49,6 @@ namespace {
 constexpr int BM = 128;  // weight rows per tile: MMA M, TMEM lanes
 constexpr int BN = 128;  // tokens per tile
 constexpr int BK = 64;   // K per stage: one 128-byte swizzle row of fp16
-constexpr int STAGES = 3;
 constexpr int kConvWarp0 = 2, kNumConvWarps = 4;            // one thread per weight row
 constexpr int kConvPerRow = kNumConvWarps * 32 / 128;      // threads per weight row (1 or 2)
 constexpr int kEpiWarp0 = kConvWarp0 + kNumConvWarps, kNumEpiWarps = 16;  // 4 lane x 4 column quarters
@@ -61,15 +60,24 @@ constexpr uint32_t kBBytes = BN * BK * 2;                  // one fp16 token til
 constexpr uint32_t kRBytes = BM * 64;                      // raw codes of a stage (<= 64 B per row)
 constexpr uint64_t kTimeoutNs = 4000000000ull;
 
-constexpr uint32_t kOffAhi = 0;
-constexpr uint32_t kOffAlo = kOffAhi + STAGES * kABytes;
-constexpr uint32_t kOffB = kOffAlo + STAGES * kABytes;     // per stage: hi rows 0..127, lo rows 128..255
-constexpr uint32_t kOffR = kOffB + STAGES * 2 * kBBytes;
-constexpr uint32_t kOffBar = kOffR + STAGES * kRBytes;
-constexpr uint32_t kNumBars = 3 * STAGES + 2 + 2 + 1;
-constexpr uint32_t kOffMisc = kOffBar + kNumBars * 8;
-constexpr uint32_t kOffRowInv = kOffMisc + 16;             // [BM] per-row 2^-e of grouped weights
-constexpr uint32_t kSmemBytes = kOffRowInv + BM * 4 + 1024;  // + alignment slack
+// Shared memory of a ring of NS stages; LO adds the A_lo buffers that grouped weights need.
+// Per-row weights leave out A_lo and take a 4th stage instead (the ring's depth, not the tensor
+// pipe, bounds the per-row GEMM: a stage's slot is held from its TMA issue to its MMA's end).
+template <int NS, bool LO>
+struct Smem {
+    static constexpr uint32_t ahi = 0;
+    static constexpr uint32_t alo = ahi + NS * kABytes;
+    static constexpr uint32_t b = alo + (LO ? NS * kABytes : 0);  // per stage: hi rows 0..127, lo rows 128..255
+    static constexpr uint32_t r = b + NS * 2 * kBBytes;
+    static constexpr uint32_t bar = r + NS * kRBytes;
+    static constexpr uint32_t num_bars = 3 * NS + 2 + 2 + 1;
+    static constexpr uint32_t misc = bar + num_bars * 8;
+    static constexpr uint32_t rowinv = misc + 16;  // [BM] per-row 2^-e of grouped weights
+    static constexpr uint32_t bytes = rowinv + BM * 4 + 1024;  // + alignment slack
+};
+constexpr int kStagesGrouped = 3, kStagesRow = 4;
+static_assert(Smem<kStagesGrouped, true>::bytes <= 232448 && Smem<kStagesRow, false>::bytes <= 232448,
+              "227 KB of dynamic shared memory per CTA");
 
 // Device error codes (first one wins): which role's wait ran out.
 enum { kErrProducer = 0x101, kErrConverter = 0x102, kErrMma = 0x103, kErrEpilogue = 0x104, kErrDrain = 0x105 };
@@ -138,25 +146,34 @@ struct MmaRing {
 // The MMA issuer for fold periods of SPP stages.  The issuing thread's own instruction stream
 // bounds the tensor pipe: a ring slot, parity or accumulator buffer computed at run time between
 // the MMAs measured up to 1.8x slower than the pipe's 128 cycles per 128x256x16 MMA.  So the loop
-// is unrolled over lcm(STAGES, 2 SPP) stages, which makes the ring slot, the phase parities, the
+// is unrolled over lcm(2 NS, 2 SPP) stages, which makes the ring slot, the phase parities, the
 // TMEM buffer and the commit points compile-time and advances the descriptors by immediates.
 // Returns false when a wait gave up (the error is recorded, the abort flag raised).
-template <int SPP, bool GROUPED, bool SMALL>
+__host__ __device__ constexpr int lcm_int(int a, int b) {
+    int x = a, y = b;
+    while (y) {
+        const int t = x % y;
+        x = y;
+        y = t;
+    }
+    return a / x * b;
+}
+
+template <int NS, int SPP, bool GROUPED, bool SMALL>
 __device__ __forceinline__ bool mma_loop(int num_kb, uint64_t ahi0, uint64_t alo0, uint64_t b0, uint32_t tmem_base,
                                       const MmaRing r) {
-    static_assert(STAGES == 3, "lcm(STAGES, 2 SPP) = 6 SPP needs an odd ring of 3");
-    constexpr int U = STAGES * 2 * SPP;
+    constexpr int U = lcm_int(2 * NS, 2 * SPP);
     constexpr uint32_t id_hilo = tc::idesc_f16_f32(BM, 2 * BN);  // rows x [x_hi; x_lo]
     constexpr uint32_t id_hi = tc::idesc_f16_f32(BM, BN);
     constexpr uint32_t id_64 = tc::idesc_f16_f32(BM, 64);
     for (int j0 = 0; j0 < num_kb; j0 += U) {
-        // j0 is a multiple of U: j0 / STAGES and j0 / SPP are even, so the ring parity and the
+        // j0 is a multiple of U: j0 / NS and j0 / SPP are even, so the ring parity and the
         // accumulator buffer of stage j0 + jj depend on jj alone
 #pragma unroll
         for (int jj = 0; jj < U; ++jj) {
             if (j0 + jj >= num_kb) return true;
-            const int s = jj % STAGES, sp = jj % SPP, buf = (jj / SPP) & 1;
-            const uint32_t par = (uint32_t)((jj / STAGES) & 1);
+            const int s = jj % NS, sp = jj % SPP, buf = (jj / SPP) & 1;
+            const uint32_t par = (uint32_t)((jj / NS) & 1);
             if (!tc::mbar_wait_bounded(&r.conv[s], par, r.abort_flag, r.err, kErrMma, kTimeoutNs) ||
                 !tc::mbar_wait_bounded(&r.full[s], par, r.abort_flag, r.err, kErrMma, kTimeoutNs))
                 return false;
@@ -193,25 +210,27 @@ __device__ __forceinline__ bool mma_loop(int num_kb, uint64_t ahi0, uint64_t alo
     return true;
 }
 
-template <bool GROUPED, bool SMALL>
+template <int NS, bool GROUPED, bool SMALL>
 __device__ __forceinline__ bool mma_loop_spp(int spp, int num_kb, uint64_t ahi0, uint64_t alo0, uint64_t b0,
                                              uint32_t tmem_base, const MmaRing &r) {
-    if (spp == 4) return mma_loop<4, GROUPED, SMALL>(num_kb, ahi0, alo0, b0, tmem_base, r);
-    if (spp == 2) return mma_loop<2, GROUPED, SMALL>(num_kb, ahi0, alo0, b0, tmem_base, r);
-    return mma_loop<1, GROUPED, SMALL>(num_kb, ahi0, alo0, b0, tmem_base, r);
+    if (spp == 4) return mma_loop<NS, 4, GROUPED, SMALL>(num_kb, ahi0, alo0, b0, tmem_base, r);
+    if (spp == 2) return mma_loop<NS, 2, GROUPED, SMALL>(num_kb, ahi0, alo0, b0, tmem_base, r);
+    return mma_loop<NS, 1, GROUPED, SMALL>(num_kb, ahi0, alo0, b0, tmem_base, r);
 }
 
+template <int NS, bool LO>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_xhi,
                    const __grid_constant__ CUtensorMap tm_xlo, const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kOffBar);
-    uint64_t *full = bars, *conv = bars + STAGES, *empty = bars + 2 * STAGES;
-    uint64_t *accfull = bars + 3 * STAGES, *accempty = accfull + 2, *drain = accempty + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffMisc);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + kOffMisc + 4);
-    float *rowinv = reinterpret_cast<float *>(smem + kOffRowInv);
+    using L = Smem<NS, LO>;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::bar);
+    uint64_t *full = bars, *conv = bars + NS, *empty = bars + 2 * NS;
+    uint64_t *accfull = bars + 3 * NS, *accempty = accfull + 2, *drain = accempty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::misc);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::misc + 4);
+    float *rowinv = reinterpret_cast<float *>(smem + L::rowinv);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * BM, m0 = blockIdx.y * BN;
@@ -224,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t stage_tx = 2 * kBBytes + (uint32_t)(BM * raw_kb_bytes);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
+        for (int s = 0; s < NS; ++s) {
             tc::mbar_init(&full[s], 1);
             tc::mbar_init(&conv[s], kNumConvWarps);
             tc::mbar_init(&empty[s], 1);
@@ -253,38 +272,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             int issued = 0;
             for (int j = 0; j < num_kb; ++j) {
-                const int s = j % STAGES, kb = kb0 + j;
-                if (j >= STAGES &&
-                    !tc::mbar_wait_bounded(&empty[s], ((j / STAGES) - 1) & 1, abort_flag, p.err, kErrProducer, kTimeoutNs))
+                const int s = j % NS, kb = kb0 + j;
+                if (j >= NS &&
+                    !tc::mbar_wait_bounded(&empty[s], ((j / NS) - 1) & 1, abort_flag, p.err, kErrProducer, kTimeoutNs))
                     break;
                 tc::mbar_arrive_expect_tx(&full[s], stage_tx);
-                uint8_t *b = smem + kOffB + s * 2 * kBBytes;
-                tc::tma_load_2d(smem + kOffR + s * kRBytes, &tm_w, kb * raw_kb_bytes, n0, &full[s]);
+                uint8_t *b = smem + L::b + s * 2 * kBBytes;
+                tc::tma_load_2d(smem + L::r + s * kRBytes, &tm_w, kb * raw_kb_bytes, n0, &full[s]);
                 tc::tma_load_2d(b, &tm_xhi, kb * BK, m0, &full[s]);
                 tc::tma_load_2d(b + kBBytes, &tm_xlo, kb * BK, m0, &full[s]);
                 ++issued;
             }
             if (*abort_flag) {  // let the copies already issued land before the CTA exits
                 volatile int no_abort = 0;
-                for (int j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j)
-                    tc::mbar_wait_bounded(&full[j % STAGES], (j / STAGES) & 1, &no_abort, p.err, kErrDrain, 100000000ull);
+                for (int j = issued > NS ? issued - NS : 0; j < issued; ++j)
+                    tc::mbar_wait_bounded(&full[j % NS], (j / NS) & 1, &no_abort, p.err, kErrDrain, 100000000ull);
             }
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            const uint64_t ahi0 = tc::desc_sw128(tc::smem_u32(smem + kOffAhi));
-            const uint64_t alo0 = tc::desc_sw128(tc::smem_u32(smem + kOffAlo));
-            const uint64_t b0 = tc::desc_sw128(tc::smem_u32(smem + kOffB));
+            const uint64_t ahi0 = tc::desc_sw128(tc::smem_u32(smem + L::ahi));
+            const uint64_t alo0 = tc::desc_sw128(tc::smem_u32(smem + L::alo));
+            const uint64_t b0 = tc::desc_sw128(tc::smem_u32(smem + L::b));
             const MmaRing ring{full, conv, empty, accfull, accempty, abort_flag, p.err};
             const int spp = p.ksteps_per_period / (BK / 16);  // stages per fold period: 1, 2 or 4
-            if (p.grouped) {
-                if (small) mma_loop_spp<true, true>(spp, num_kb, ahi0, alo0, b0, tmem_base, ring);
-                else mma_loop_spp<true, false>(spp, num_kb, ahi0, alo0, b0, tmem_base, ring);
-            } else {
-                if (small) mma_loop_spp<false, true>(spp, num_kb, ahi0, alo0, b0, tmem_base, ring);
-                else mma_loop_spp<false, false>(spp, num_kb, ahi0, alo0, b0, tmem_base, ring);
-            }
+            if (small) mma_loop_spp<NS, LO, true>(spp, num_kb, ahi0, alo0, b0, tmem_base, ring);
+            else mma_loop_spp<NS, LO, false>(spp, num_kb, ahi0, alo0, b0, tmem_base, ring);
             // wait for every MMA this thread issued before TMEM can be released
             tc::mma_commit(drain);
             volatile int no_abort = 0;
@@ -302,7 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool nrow = n < p.N;
         const float *srow = p.scales + (size_t)(nrow ? n : 0) * p.groups_per_row;
         float se = 1.f;
-        if (p.grouped) {
+        if (LO) {
             const int g0 = kb0 * BK / p.group_k, g1 = ((kb0 + num_kb) * BK + p.group_k - 1) / p.group_k;
             float smax = 0.f;
             if (nrow) {
@@ -344,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int gshift = (p.group_k & (p.group_k - 1)) == 0 ? __ffs(p.group_k) - 1 : -1;
         float sc_n1[kChunks8] = {}, sc_n2[kChunks8] = {};
         auto load_scales = [&](int kb, float (&dst)[kChunks8]) {
-            if (!p.grouped || !nrow || kb >= kb0 + num_kb) return;
+            if (!LO || !nrow || kb >= kb0 + num_kb) return;
             const int k0 = kb * BK + half * (BK / kConvPerRow);
 #pragma unroll
             for (int cc = 0; cc < kChunks8; ++cc)
@@ -356,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         load_scales(kb0, sc_n1);
         load_scales(kb0 + 1, sc_n2);
         for (int j = 0; j < num_kb; ++j) {
-            const int s = j % STAGES, kb = kb0 + j;
+            const int s = j % NS, kb = kb0 + j;
             float sc[kChunks8];
 #pragma unroll
             for (int cc = 0; cc < kChunks8; ++cc) {
@@ -365,18 +379,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             load_scales(kb + 2, sc_n2);
             int ok = 1;
-            if (lane == 0) ok = tc::mbar_wait_bounded(&full[s], (j / STAGES) & 1, abort_flag, p.err, kErrConverter, kTimeoutNs);
+            if (lane == 0) ok = tc::mbar_wait_bounded(&full[s], (j / NS) & 1, abort_flag, p.err, kErrConverter, kTimeoutNs);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
-            const uint8_t *raw = smem + kOffR + s * kRBytes;
-            uint8_t *ahi = smem + kOffAhi + s * kABytes;
-            uint8_t *alo = smem + kOffAlo + s * kABytes;
+            const uint8_t *raw = smem + L::r + s * kRBytes;
+            uint8_t *ahi = smem + L::ahi + s * kABytes;
+            uint8_t *alo = smem + L::alo + s * kABytes;
             if (p.qtype == kQInt8) {
 #pragma unroll
                 for (int cc = 0; cc < kChunks8; ++cc) {  // 64-byte rows, 64-byte TMA swizzle
                     const int c = kChunks8 * half + cc;
                     const uint4 w = *reinterpret_cast<const uint4 *>(raw + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
-                    if (!p.grouped) {
+                    if (!LO) {
                         uint32_t h[8];
                         i8x4_to_h(w.x, h[0], h[1]);
                         i8x4_to_h(w.y, h[2], h[3]);
@@ -407,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
                     for (int jj = 0; jj < 4; ++jj) {
-                        if (!p.grouped) {
+                        if (!LO) {
                             uint32_t h[4];
                             u4x8_to_h(ws[jj], h);
                             *reinterpret_cast<uint4 *>(ahi + sw128_off(r, 4 * c + jj)) = make_uint4(h[0], h[1], h[2], h[3]);
@@ -467,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         bar_sync(kBarRowInv, kRowInvThreads);
         if (ok && row_ok) {
-            const float sr = p.grouped ? rowinv[rl] : __ldg(p.scales + n);
+            const float sr = LO ? rowinv[rl] : __ldg(p.scales + n);
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
                 const int m = m0 + 32 * h + j;
@@ -670,11 +684,19 @@ cudaError_t launch_gemm_tc(const QMatrix &w, const float *X, size_t M, size_t ld
         p.part = nullptr;
     }
     p.kb_per_split = kb_per;
+    using LG = Smem<kStagesGrouped, true>;
+    using LR = Smem<kStagesRow, false>;
     static const bool attr =
-        cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) == cudaSuccess;
+        cudaFuncSetAttribute(gemm_tc_kernel<kStagesGrouped, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             LG::bytes) == cudaSuccess &&
+        cudaFuncSetAttribute(gemm_tc_kernel<kStagesRow, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             LR::bytes) == cudaSuccess;
     if (!attr) return cudaErrorInvalidConfiguration;
     dim3 grid((unsigned)((N + BM - 1) / BM), (unsigned)((M + BN - 1) / BN), (unsigned)ks);
-    gemm_tc_kernel<<<grid, kThreads, kSmemBytes, st>>>(tw, th, tl, p);
+    if (p.grouped)
+        gemm_tc_kernel<kStagesGrouped, true><<<grid, kThreads, LG::bytes, st>>>(tw, th, tl, p);
+    else
+        gemm_tc_kernel<kStagesRow, false><<<grid, kThreads, LR::bytes, st>>>(tw, th, tl, p);
     e = cudaGetLastError();
     if (e != cudaSuccess || ks == 1) return e;
     const size_t MN = M * (size_t)N;
