@@ -60,23 +60,27 @@ constexpr uint32_t kBBytes = BN * BK * 2;                  // one fp16 token til
 constexpr uint32_t kRBytes = BM * 64;                      // raw codes of a stage (<= 64 B per row)
 constexpr uint64_t kTimeoutNs = 4000000000ull;
 
-// Shared memory of a ring of NS stages; LO adds the A_lo buffers that grouped weights need.
-// Per-row weights leave out A_lo and take a 4th stage instead (the ring's depth, not the tensor
-// pipe, bounds the per-row GEMM: a stage's slot is held from its TMA issue to its MMA's end).
-template <int NS, bool LO>
+// Shared memory: a ring of NA converted weight tiles (A_hi, plus A_lo for grouped weights when LO)
+// and a ring of NB TMA stages (x_hi|x_lo token tile and raw codes).  A TMA stage's slot is held
+// from its copy's issue to its MMAs' end, so NB sets how much copy latency is hidden; a converted
+// tile's slot only spans its conversion and its MMAs, so a shorter A ring suffices when converting
+// a stage takes no longer than its MMAs.  Per-row weights (no A_lo): NA = NB = 4.  Grouped weights:
+// NA = NB = 3 (their converters are the slower role: NA = 2, NB = 4 measured 7% slower).
+template <int NA, int NB, bool LO>
 struct Smem {
     static constexpr uint32_t ahi = 0;
-    static constexpr uint32_t alo = ahi + NS * kABytes;
-    static constexpr uint32_t b = alo + (LO ? NS * kABytes : 0);  // per stage: hi rows 0..127, lo rows 128..255
-    static constexpr uint32_t r = b + NS * 2 * kBBytes;
-    static constexpr uint32_t bar = r + NS * kRBytes;
-    static constexpr uint32_t num_bars = 3 * NS + 2 + 2 + 1;
+    static constexpr uint32_t alo = ahi + NA * kABytes;
+    static constexpr uint32_t b = alo + (LO ? NA * kABytes : 0);  // per stage: hi rows 0..127, lo rows 128..255
+    static constexpr uint32_t r = b + NB * 2 * kBBytes;
+    static constexpr uint32_t bar = r + NB * kRBytes;
+    static constexpr uint32_t num_bars = 2 * NB + 2 * NA + 2 + 2 + 1;
     static constexpr uint32_t misc = bar + num_bars * 8;
     static constexpr uint32_t rowinv = misc + 16;  // [BM] per-row 2^-e of grouped weights
     static constexpr uint32_t bytes = rowinv + BM * 4 + 1024;  // + alignment slack
 };
-constexpr int kStagesGrouped = 3, kStagesRow = 4;
-static_assert(Smem<kStagesGrouped, true>::bytes <= 232448 && Smem<kStagesRow, false>::bytes <= 232448,
+constexpr int kTilesGrouped = 3, kStagesGrouped = 3, kStagesRow = 4;
+static_assert(Smem<kTilesGrouped, kStagesGrouped, true>::bytes <= 232448 &&
+                  Smem<kStagesRow, kStagesRow, false>::bytes <= 232448,
               "227 KB of dynamic shared memory per CTA");
 
 // Device error codes (first one wins): which role's wait ran out.
@@ -117,16 +121,30 @@ PYXIS_DEVINL void u4x8_to_h(uint32_t w, uint32_t (&h)[4]) {
     for (int i = 0; i < 4; ++i) h[i] = h2_bits(__hsub2(bits_h2(((w >> (4 * i)) & 0x000F000Fu) | 0x64006400u), bias));
 }
 
-// Codes q (exact floats) times the scale s (f32, rounded once) as fp16 hi + lo pairs: 22
-// significant bits.  hi is w rounded to 11 bits by Veltkamp's split (c = w (2^13 + 1),
+// A pair of codes q (exact floats) times the scale s (f32, rounded once) as fp16 hi + lo pairs:
+// 22 significant bits.  hi is w rounded to 11 bits by Veltkamp's split (c = w (2^13 + 1),
 // hi = c - (c - w)), so it converts to fp16 exactly and lo = w - hi is exact in f32: one
-// f32 -> f16 conversion per value (the conversion pipe is the converters' narrowest).
-PYXIS_DEVINL void split_pair(float q0, float q1, float s, uint32_t &hi, uint32_t &lo) {
-    const float w0 = __fmul_rn(q0, s), w1 = __fmul_rn(q1, s);
-    const float c0 = __fmul_rn(w0, 8193.0f), c1 = __fmul_rn(w1, 8193.0f);
-    const float h0 = __fsub_rn(c0, __fsub_rn(c0, w0)), h1 = __fsub_rn(c1, __fsub_rn(c1, w1));
-    hi = h2_bits(__floats2half2_rn(h0, h1));
-    lo = h2_bits(__floats2half2_rn(__fsub_rn(w0, h0), __fsub_rn(w1, h1)));
+// f32 -> f16 conversion per value.  The arithmetic is paired f32x2 (five instructions per pair;
+// a - b is fma(b, -1, a), rounded once like the subtraction): the FP32 pipe bounds the converters.
+PYXIS_DEVINL void split_pair(float2 q, float2 s, uint32_t &hi, uint32_t &lo) {
+    const float2 m1 = make_float2(-1.f, -1.f);
+    const float2 w = __fmul2_rn(q, s);
+    const float2 c = __fmul2_rn(w, make_float2(8193.0f, 8193.0f));
+    const float2 h = __ffma2_rn(__ffma2_rn(w, m1, c), m1, c);  // c - (c - w)
+    const float2 l = __ffma2_rn(h, m1, w);                      // w - h
+    hi = h2_bits(__floats2half2_rn(h.x, h.y));
+    lo = h2_bits(__floats2half2_rn(l.x, l.y));
+}
+
+// Eight int4 codes (q + 8 in nibbles, element 2j low / 2j+1 high nibble of byte j) as exact float
+// pairs in the converter order (e0,e4) (e1,e5) (e2,e6) (e3,e7).
+PYXIS_DEVINL void u4x8_to_f32_pairs(uint32_t w, float2 (&e)[4]) {
+    const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;  // even / odd elements
+    const float2 m = f2(-kMagicU4, -kMagicU4);
+    e[0] = fadd2(f2(byte_to_magic(lo, 0), byte_to_magic(lo, 2)), m);
+    e[1] = fadd2(f2(byte_to_magic(hi, 0), byte_to_magic(hi, 2)), m);
+    e[2] = fadd2(f2(byte_to_magic(lo, 1), byte_to_magic(lo, 3)), m);
+    e[3] = fadd2(f2(byte_to_magic(hi, 1), byte_to_magic(hi, 3)), m);
 }
 
 // Byte offset of 16-byte chunk c of row r in a 128B-swizzled K-major tile (8-row 1024 B atoms).
@@ -138,7 +156,7 @@ constexpr int kBarRowInv = 1;  // converters publish rowinv, the epilogue reads 
 constexpr int kRowInvThreads = (kNumConvWarps + kNumEpiWarps) * 32;
 
 struct MmaRing {
-    uint64_t *full, *conv, *empty, *accfull, *accempty;
+    uint64_t *full, *conv, *empty, *aempty, *accfull, *accempty;
     volatile int *abort_flag;
     int *err;
 };
@@ -146,7 +164,7 @@ struct MmaRing {
 // The MMA issuer for fold periods of SPP stages.  The issuing thread's own instruction stream
 // bounds the tensor pipe: a ring slot, parity or accumulator buffer computed at run time between
 // the MMAs measured up to 1.8x slower than the pipe's 128 cycles per 128x256x16 MMA.  So the loop
-// is unrolled over lcm(2 NS, 2 SPP) stages, which makes the ring slot, the phase parities, the
+// is unrolled over lcm(2 NA, 2 NB, 2 SPP) stages, which makes the ring slots, the phase parities, the
 // TMEM buffer and the commit points compile-time and advances the descriptors by immediates.
 // Returns false when a wait gave up (the error is recorded, the abort flag raised).
 __host__ __device__ constexpr int lcm_int(int a, int b) {
@@ -159,23 +177,22 @@ __host__ __device__ constexpr int lcm_int(int a, int b) {
     return a / x * b;
 }
 
-template <int NS, int SPP, bool GROUPED, bool SMALL>
+template <int NA, int NB, int SPP, bool GROUPED, bool SMALL>
 __device__ __forceinline__ bool mma_loop(int num_kb, uint64_t ahi0, uint64_t alo0, uint64_t b0, uint32_t tmem_base,
                                       const MmaRing r) {
-    constexpr int U = lcm_int(2 * NS, 2 * SPP);
+    constexpr int U = lcm_int(lcm_int(2 * NA, 2 * NB), 2 * SPP);
     constexpr uint32_t id_hilo = tc::idesc_f16_f32(BM, 2 * BN);  // rows x [x_hi; x_lo]
     constexpr uint32_t id_hi = tc::idesc_f16_f32(BM, BN);
     constexpr uint32_t id_64 = tc::idesc_f16_f32(BM, 64);
     for (int j0 = 0; j0 < num_kb; j0 += U) {
-        // j0 is a multiple of U: j0 / NS and j0 / SPP are even, so the ring parity and the
+        // j0 is a multiple of U: j0 / NA, j0 / NB and j0 / SPP are even, so the ring parities and the
         // accumulator buffer of stage j0 + jj depend on jj alone
 #pragma unroll
         for (int jj = 0; jj < U; ++jj) {
             if (j0 + jj >= num_kb) return true;
-            const int s = jj % NS, sp = jj % SPP, buf = (jj / SPP) & 1;
-            const uint32_t par = (uint32_t)((jj / NS) & 1);
-            if (!tc::mbar_wait_bounded(&r.conv[s], par, r.abort_flag, r.err, kErrMma, kTimeoutNs) ||
-                !tc::mbar_wait_bounded(&r.full[s], par, r.abort_flag, r.err, kErrMma, kTimeoutNs))
+            const int a = jj % NA, s = jj % NB, sp = jj % SPP, buf = (jj / SPP) & 1;
+            if (!tc::mbar_wait_bounded(&r.conv[a], (uint32_t)((jj / NA) & 1), r.abort_flag, r.err, kErrMma, kTimeoutNs) ||
+                !tc::mbar_wait_bounded(&r.full[s], (uint32_t)((jj / NB) & 1), r.abort_flag, r.err, kErrMma, kTimeoutNs))
                 return false;
             if (sp == 0) {
                 const int period = (j0 + jj) / SPP;
@@ -184,8 +201,8 @@ __device__ __forceinline__ bool mma_loop(int num_kb, uint64_t ahi0, uint64_t alo
                     return false;
             }
             tc::tc_fence_after();
-            const uint64_t ahi = ahi0 + (uint64_t)(s * (kABytes >> 4));
-            const uint64_t alo = alo0 + (uint64_t)(s * (kABytes >> 4));
+            const uint64_t ahi = ahi0 + (uint64_t)(a * (kABytes >> 4));
+            const uint64_t alo = alo0 + (uint64_t)(a * (kABytes >> 4));
             const uint64_t bhi = b0 + (uint64_t)(s * (2 * kBBytes >> 4));
             const uint64_t blo = bhi + (uint64_t)(kBBytes >> 4);
             const uint32_t d = tmem_base + (uint32_t)(buf * kAccCols);
@@ -204,30 +221,32 @@ __device__ __forceinline__ bool mma_loop(int num_kb, uint64_t ahi0, uint64_t alo
                 }
             }
             tc::mma_commit(&r.empty[s]);
+            if (NA != NB) tc::mma_commit(&r.aempty[a]);  // with NA == NB, empty[s] frees both
             if (sp == SPP - 1) tc::mma_commit(&r.accfull[buf]);
         }
     }
     return true;
 }
 
-template <int NS, bool GROUPED, bool SMALL>
+template <int NA, int NB, bool GROUPED, bool SMALL>
 __device__ __forceinline__ bool mma_loop_spp(int spp, int num_kb, uint64_t ahi0, uint64_t alo0, uint64_t b0,
                                              uint32_t tmem_base, const MmaRing &r) {
-    if (spp == 4) return mma_loop<NS, 4, GROUPED, SMALL>(num_kb, ahi0, alo0, b0, tmem_base, r);
-    if (spp == 2) return mma_loop<NS, 2, GROUPED, SMALL>(num_kb, ahi0, alo0, b0, tmem_base, r);
-    return mma_loop<NS, 1, GROUPED, SMALL>(num_kb, ahi0, alo0, b0, tmem_base, r);
+    if (spp == 4) return mma_loop<NA, NB, 4, GROUPED, SMALL>(num_kb, ahi0, alo0, b0, tmem_base, r);
+    if (spp == 2) return mma_loop<NA, NB, 2, GROUPED, SMALL>(num_kb, ahi0, alo0, b0, tmem_base, r);
+    return mma_loop<NA, NB, 1, GROUPED, SMALL>(num_kb, ahi0, alo0, b0, tmem_base, r);
 }
 
-template <int NS, bool LO>
+template <int NA, int NB, bool LO>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_xhi,
                    const __grid_constant__ CUtensorMap tm_xlo, const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    using L = Smem<NS, LO>;
+    using L = Smem<NA, NB, LO>;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::bar);
-    uint64_t *full = bars, *conv = bars + NS, *empty = bars + 2 * NS;
-    uint64_t *accfull = bars + 3 * NS, *accempty = accfull + 2, *drain = accempty + 2;
+    uint64_t *full = bars, *empty = bars + NB;            // TMA stages
+    uint64_t *conv = bars + 2 * NB, *aempty = conv + NA;  // converted weight tiles
+    uint64_t *accfull = aempty + NA, *accempty = accfull + 2, *drain = accempty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::misc);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::misc + 4);
     float *rowinv = reinterpret_cast<float *>(smem + L::rowinv);
@@ -243,10 +262,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t stage_tx = 2 * kBBytes + (uint32_t)(BM * raw_kb_bytes);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < NS; ++s) {
+        for (int s = 0; s < NB; ++s) {
             tc::mbar_init(&full[s], 1);
-            tc::mbar_init(&conv[s], kNumConvWarps);
             tc::mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < NA; ++a) {
+            tc::mbar_init(&conv[a], kNumConvWarps);
+            tc::mbar_init(&aempty[a], 1);
         }
         for (int b = 0; b < 2; ++b) {
             tc::mbar_init(&accfull[b], 1);
@@ -272,9 +294,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             int issued = 0;
             for (int j = 0; j < num_kb; ++j) {
-                const int s = j % NS, kb = kb0 + j;
-                if (j >= NS &&
-                    !tc::mbar_wait_bounded(&empty[s], ((j / NS) - 1) & 1, abort_flag, p.err, kErrProducer, kTimeoutNs))
+                const int s = j % NB, kb = kb0 + j;
+                if (j >= NB &&
+                    !tc::mbar_wait_bounded(&empty[s], ((j / NB) - 1) & 1, abort_flag, p.err, kErrProducer, kTimeoutNs))
                     break;
                 tc::mbar_arrive_expect_tx(&full[s], stage_tx);
                 uint8_t *b = smem + L::b + s * 2 * kBBytes;
@@ -285,8 +307,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (*abort_flag) {  // let the copies already issued land before the CTA exits
                 volatile int no_abort = 0;
-                for (int j = issued > NS ? issued - NS : 0; j < issued; ++j)
-                    tc::mbar_wait_bounded(&full[j % NS], (j / NS) & 1, &no_abort, p.err, kErrDrain, 100000000ull);
+                for (int j = issued > NB ? issued - NB : 0; j < issued; ++j)
+                    tc::mbar_wait_bounded(&full[j % NB], (j / NB) & 1, &no_abort, p.err, kErrDrain, 100000000ull);
             }
         }
     } else if (warp == 1) {
@@ -295,10 +317,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t ahi0 = tc::desc_sw128(tc::smem_u32(smem + L::ahi));
             const uint64_t alo0 = tc::desc_sw128(tc::smem_u32(smem + L::alo));
             const uint64_t b0 = tc::desc_sw128(tc::smem_u32(smem + L::b));
-            const MmaRing ring{full, conv, empty, accfull, accempty, abort_flag, p.err};
+            const MmaRing ring{full, conv, empty, aempty, accfull, accempty, abort_flag, p.err};
             const int spp = p.ksteps_per_period / (BK / 16);  // stages per fold period: 1, 2 or 4
-            if (small) mma_loop_spp<NS, LO, true>(spp, num_kb, ahi0, alo0, b0, tmem_base, ring);
-            else mma_loop_spp<NS, LO, false>(spp, num_kb, ahi0, alo0, b0, tmem_base, ring);
+            if (small) mma_loop_spp<NA, NB, LO, true>(spp, num_kb, ahi0, alo0, b0, tmem_base, ring);
+            else mma_loop_spp<NA, NB, LO, false>(spp, num_kb, ahi0, alo0, b0, tmem_base, ring);
             // wait for every MMA this thread issued before TMEM can be released
             tc::mma_commit(drain);
             volatile int no_abort = 0;
@@ -356,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // slowest role for group scales: a memory round trip per stage would be exposed)
         // (a shift when the group size is a power of two: a division per chunk measured slower)
         const int gshift = (p.group_k & (p.group_k - 1)) == 0 ? __ffs(p.group_k) - 1 : -1;
-        float sc_n1[kChunks8] = {}, sc_n2[kChunks8] = {};
+        float sc_a[kChunks8] = {}, sc_b[kChunks8] = {};
         auto load_scales = [&](int kb, float (&dst)[kChunks8]) {
             if (!LO || !nrow || kb >= kb0 + num_kb) return;
             const int k0 = kb * BK + half * (BK / kConvPerRow);
@@ -367,24 +389,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                     dst[cc] = __ldg(srow + (gshift >= 0 ? k >> gshift : k / p.group_k)) * se;
                 }
         };
-        load_scales(kb0, sc_n1);
-        load_scales(kb0 + 1, sc_n2);
-        for (int j = 0; j < num_kb; ++j) {
-            const int s = j % NS, kb = kb0 + j;
-            float sc[kChunks8];
-#pragma unroll
-            for (int cc = 0; cc < kChunks8; ++cc) {
-                sc[cc] = sc_n1[cc];
-                sc_n1[cc] = sc_n2[cc];
-            }
-            load_scales(kb + 2, sc_n2);
+        // Converts stage j with the scales sc; false when a wait gave up.
+        auto convert = [&](int j, const float (&sc)[kChunks8]) -> bool {
+            const int s = j % NB, a = j % NA;
             int ok = 1;
-            if (lane == 0) ok = tc::mbar_wait_bounded(&full[s], (j / NS) & 1, abort_flag, p.err, kErrConverter, kTimeoutNs);
+            if (lane == 0) {
+                ok = tc::mbar_wait_bounded(&full[s], (j / NB) & 1, abort_flag, p.err, kErrConverter, kTimeoutNs);
+                // the tile slot's previous stage must be multiplied out (implied by full[s] when NA == NB)
+                if (ok && NA != NB && j >= NA)
+                    ok = tc::mbar_wait_bounded(&aempty[a], ((j / NA) - 1) & 1, abort_flag, p.err, kErrConverter, kTimeoutNs);
+            }
             ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok) break;
+            if (!ok) return false;
             const uint8_t *raw = smem + L::r + s * kRBytes;
-            uint8_t *ahi = smem + L::ahi + s * kABytes;
-            uint8_t *alo = smem + L::alo + s * kABytes;
+            uint8_t *ahi = smem + L::ahi + a * kABytes;
+            uint8_t *alo = smem + L::alo + a * kABytes;
             if (p.qtype == kQInt8) {
 #pragma unroll
                 for (int cc = 0; cc < kChunks8; ++cc) {  // 64-byte rows, 64-byte TMA swizzle
@@ -405,8 +424,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         i8x4_to_f32(w.z, f[4], f[5]);
                         i8x4_to_f32(w.w, f[6], f[7]);
                         uint32_t hi[8], lo[8];
+                        const float2 s2 = f2(sc[cc], sc[cc]);
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) split_pair(f[i].x, f[i].y, sc[cc], hi[i], lo[i]);
+                        for (int i = 0; i < 8; ++i) split_pair(f[i], s2, hi[i], lo[i]);
                         *reinterpret_cast<uint4 *>(ahi + sw128_off(r, 2 * c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
                         *reinterpret_cast<uint4 *>(ahi + sw128_off(r, 2 * c + 1)) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
                         *reinterpret_cast<uint4 *>(alo + sw128_off(r, 2 * c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
@@ -426,14 +446,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                             u4x8_to_h(ws[jj], h);
                             *reinterpret_cast<uint4 *>(ahi + sw128_off(r, 4 * c + jj)) = make_uint4(h[0], h[1], h[2], h[3]);
                         } else {
-                            // exact floats, paired in the converter order (e0,e4) (e1,e5) (e2,e6) (e3,e7)
-                            float2 e01, e23, e45, e67;
-                            u4x8_to_f32(ws[jj], e01, e23, e45, e67);
+                            float2 e[4];
+                            u4x8_to_f32_pairs(ws[jj], e);
+                            const float2 s2 = f2(sc[cc], sc[cc]);
                             uint32_t hi[4], lo[4];
-                            split_pair(e01.x, e45.x, sc[cc], hi[0], lo[0]);
-                            split_pair(e01.y, e45.y, sc[cc], hi[1], lo[1]);
-                            split_pair(e23.x, e67.x, sc[cc], hi[2], lo[2]);
-                            split_pair(e23.y, e67.y, sc[cc], hi[3], lo[3]);
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) split_pair(e[i], s2, hi[i], lo[i]);
                             *reinterpret_cast<uint4 *>(ahi + sw128_off(r, 4 * c + jj)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
                             *reinterpret_cast<uint4 *>(alo + sw128_off(r, 4 * c + jj)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
                         }
@@ -442,7 +460,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc::fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&conv[s]);
+            if (lane == 0) tc::mbar_arrive(&conv[a]);
+            return true;
+        };
+        // Unrolled by two with a scale buffer per parity: each buffer is read two stages after its
+        // loads were issued and is never copied while they are in flight (a loop-carried rotation
+        // of the buffers moved registers with pending loads and stalled every stage).
+        load_scales(kb0, sc_a);
+        load_scales(kb0 + 1, sc_b);
+        for (int j = 0; j < num_kb; j += 2) {
+            float sc[kChunks8];
+#pragma unroll
+            for (int cc = 0; cc < kChunks8; ++cc) sc[cc] = sc_a[cc];
+            load_scales(kb0 + j + 2, sc_a);
+            if (!convert(j, sc)) break;
+            if (j + 1 >= num_kb) break;
+#pragma unroll
+            for (int cc = 0; cc < kChunks8; ++cc) sc[cc] = sc_b[cc];
+            load_scales(kb0 + j + 3, sc_b);
+            if (!convert(j + 1, sc)) break;
         }
     } else {
         // ------------------------------------------------------------------ epilogue
@@ -684,19 +720,19 @@ cudaError_t launch_gemm_tc(const QMatrix &w, const float *X, size_t M, size_t ld
         p.part = nullptr;
     }
     p.kb_per_split = kb_per;
-    using LG = Smem<kStagesGrouped, true>;
-    using LR = Smem<kStagesRow, false>;
+    using LG = Smem<kTilesGrouped, kStagesGrouped, true>;
+    using LR = Smem<kStagesRow, kStagesRow, false>;
     static const bool attr =
-        cudaFuncSetAttribute(gemm_tc_kernel<kStagesGrouped, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             LG::bytes) == cudaSuccess &&
-        cudaFuncSetAttribute(gemm_tc_kernel<kStagesRow, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             LR::bytes) == cudaSuccess;
+        cudaFuncSetAttribute(gemm_tc_kernel<kTilesGrouped, kStagesGrouped, true>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, LG::bytes) == cudaSuccess &&
+        cudaFuncSetAttribute(gemm_tc_kernel<kStagesRow, kStagesRow, false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, LR::bytes) == cudaSuccess;
     if (!attr) return cudaErrorInvalidConfiguration;
     dim3 grid((unsigned)((N + BM - 1) / BM), (unsigned)((M + BN - 1) / BN), (unsigned)ks);
     if (p.grouped)
-        gemm_tc_kernel<kStagesGrouped, true><<<grid, kThreads, LG::bytes, st>>>(tw, th, tl, p);
+        gemm_tc_kernel<kTilesGrouped, kStagesGrouped, true><<<grid, kThreads, LG::bytes, st>>>(tw, th, tl, p);
     else
-        gemm_tc_kernel<kStagesRow, false><<<grid, kThreads, LR::bytes, st>>>(tw, th, tl, p);
+        gemm_tc_kernel<kStagesRow, kStagesRow, false><<<grid, kThreads, LR::bytes, st>>>(tw, th, tl, p);
     e = cudaGetLastError();
     if (e != cudaSuccess || ks == 1) return e;
     const size_t MN = M * (size_t)N;
