@@ -7,7 +7,10 @@
  *   Weights::quantize_int8 / quantize_int4   src/weights.rs:94-118, :120-151  -> pyxis_cuda_quantize
  *   dequantize_weights (bf16 -> f32 arm)     src/model.rs:535-538             -> src_dtype BF16
  *   Weights::to_metal (persistent buffers)   src/weights.rs:65-92             -> pyxis_cuda_weights_upload
- *   read_q8_0_weights (Int8, block 32)       src/gguf.rs:245-271              -> pyxis_cuda_weights_upload
+ *   read_q8_0_weights (Int8, block 32)       src/gguf.rs:245-271              -> pyxis_cuda_weights_upload_q8_0
+ *   Weights::F32 / Weights::Bf16 rows        src/weights.rs:6-8,
+ *   (MetalF32 / MetalBf16 buffers)           src/metal_matmul.rs:28-184       -> pyxis_cuda_weights_upload
+ *                                                                                (qtype F32 / BF16)
  *   matmul(input, &Weights, out, in)         src/matmul.rs:21-97              -> pyxis_cuda_matmul
  *   MetalMatmul::new / OnceLock singleton    src/metal_matmul.rs:199-219,
  *                                            src/matmul.rs:6-19               -> pyxis_cuda_init
@@ -47,8 +50,15 @@ typedef enum {
     PYXIS_EUNSUPPORTED = 6
 } pyxis_status;
 
-/* Quantized layouts (enum Weights arms, src/weights.rs:6-21). */
-typedef enum { PYXIS_QTYPE_INT8 = 1, PYXIS_QTYPE_INT4 = 2 } pyxis_qtype;
+/* Weight layouts (enum Weights arms, src/weights.rs:6-21): the two quantized ones and the two
+ * unquantized ones (F32: num_elements f32; BF16: num_elements u16 bf16 bit patterns, widened by
+ * u32 << 16 in the dot, src/matmul.rs:289-295).  Unquantized weights have no scales. */
+typedef enum {
+    PYXIS_QTYPE_INT8 = 1,
+    PYXIS_QTYPE_INT4 = 2,
+    PYXIS_QTYPE_F32 = 3,
+    PYXIS_QTYPE_BF16 = 4
+} pyxis_qtype;
 
 /* Source element types for quantisation: F32 (Weights::F32), BF16 (Weights::Bf16, widened by
  * u32 << 16 before quantising, src/model.rs:535-538). */
@@ -80,12 +90,21 @@ int pyxis_cuda_quantize(pyxis_cuda_ctx *ctx, const void *src, int src_dtype, int
                         size_t num_elements, size_t block_size, int qtype,
                         pyxis_cuda_weights **w);
 
-/* Upload weights already quantised on the host (e.g. a GGUF Q8_0 tensor as Weights::Int8 with
- * block 32, src/gguf.rs:245-271, or a previously downloaded pack).  data: int8 -> num_elements
- * bytes, int4 -> ceil(num_elements/2) bytes; scales: ceil(num_elements/block_size) f32. */
+/* Upload weights already in one of the layouts from host memory: a pack quantised on the host
+ * or downloaded before (int8 -> num_elements bytes, int4 -> ceil(num_elements/2) bytes;
+ * scales: ceil(num_elements/block_size) f32), or unquantized rows (qtype F32: num_elements f32,
+ * BF16: num_elements u16; `scales` and `block_size` are ignored and may be NULL / 0). */
 int pyxis_cuda_weights_upload(pyxis_cuda_ctx *ctx, int qtype, const void *data,
                               const float *scales, size_t num_elements, size_t block_size,
                               pyxis_cuda_weights **w);
+
+/* read_q8_0_weights (src/gguf.rs:245-271) on the device: `blocks` is a GGUF Q8_0 tensor,
+ * ceil(num_elements/32) blocks of 34 bytes (f16 scale, little-endian, then 32 int8), in host
+ * memory (blocks_on_device == 0) or device memory of the context's device.  The result is INT8
+ * weights with block_size 32: the codes truncated to num_elements and each scale widened to f32
+ * exactly as half 2.7.1's f16::to_f32 does (a NaN keeps its payload and gets the quiet bit). */
+int pyxis_cuda_weights_upload_q8_0(pyxis_cuda_ctx *ctx, const void *blocks, int blocks_on_device,
+                                   size_t num_elements, pyxis_cuda_weights **w);
 
 /* Layout of a weights handle (Weights::len, src/weights.rs:35-46 = num_elements). */
 int pyxis_cuda_weights_info(const pyxis_cuda_weights *w, int *qtype, size_t *num_elements,

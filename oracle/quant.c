@@ -90,7 +90,8 @@ void oracle_dequantize_int4(const uint8_t *data, const float *scales, size_t blo
     }
 }
 
-/* half::f16::to_f32 (half 2.7.1), exact widening of IEEE binary16. */
+/* half::f16::to_f32 (half 2.7.1; x86 F16C widens the same way): exact for finite values and
+ * infinities; a NaN keeps its sign and payload and gets the quiet bit (0x00400000). */
 float oracle_f16_to_f32(uint16_t h) {
     uint32_t sign = (uint32_t)(h >> 15) << 31;
     uint32_t exp = (h >> 10) & 0x1f;
@@ -105,7 +106,7 @@ float oracle_f16_to_f32(uint16_t h) {
             bits = sign | ((uint32_t)(127 - 15 - e) << 23) | ((man & 0x3ff) << 13);
         }
     } else if (exp == 0x1f) {
-        bits = sign | 0x7f800000u | (man << 13);
+        bits = sign | 0x7f800000u | (man ? 0x00400000u | (man << 13) : 0u);
     } else {
         bits = sign | ((exp + 127 - 15) << 23) | (man << 13);
     }

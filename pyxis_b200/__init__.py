@@ -22,7 +22,7 @@ from typing import Optional
 import numpy as np
 
 from . import _native
-from ._native import PyxisError, QTYPE_INT4, QTYPE_INT8, DTYPE_BF16, DTYPE_F32, check
+from ._native import PyxisError, QTYPE_BF16, QTYPE_F32, QTYPE_INT4, QTYPE_INT8, DTYPE_BF16, DTYPE_F32, check
 
 __all__ = ["Weights", "CudaMatmul", "get_cuda", "matmul", "matmul_batch", "matmul_dev", "argmax",
            "argmax_dev", "PyxisError", "synth_normal_f32", "synth_normal_bf16", "synth_tokens"]
@@ -91,11 +91,15 @@ def _f32(a) -> np.ndarray:
     return np.ascontiguousarray(np.asarray(a, dtype=np.float32))
 
 
-class Weights:
-    """HBM-resident quantized weights in the reference layout (enum Weights, src/weights.rs:6-21).
+_QTYPE_NAMES = {QTYPE_INT8: "int8", QTYPE_INT4: "int4", QTYPE_F32: "f32", QTYPE_BF16: "bf16"}
 
-    ``qtype`` is "int8" or "int4"; the packed bytes and scales are bit-identical to the
-    reference quantizer's (``download()`` returns them)."""
+
+class Weights:
+    """HBM-resident weights in the reference layout (enum Weights, src/weights.rs:6-21).
+
+    ``qtype`` is "int8" or "int4" (packed bytes and scales bit-identical to the reference
+    quantizer's; ``download()`` returns them), or "f32" / "bf16" for unquantized rows
+    (Weights::F32 / Weights::Bf16, no scales)."""
 
     def __init__(self, handle: C.c_void_p, ctx: CudaMatmul):
         self.handle = handle
@@ -103,7 +107,7 @@ class Weights:
         L = _native.lib()
         qt, n, bs, nb, ns = C.c_int(), C.c_size_t(), C.c_size_t(), C.c_size_t(), C.c_size_t()
         check(L.pyxis_cuda_weights_info(handle, C.byref(qt), C.byref(n), C.byref(bs), C.byref(nb), C.byref(ns)))
-        self.qtype = "int8" if qt.value == QTYPE_INT8 else "int4"
+        self.qtype = _QTYPE_NAMES[qt.value]
         self.num_elements = n.value
         self.block_size = bs.value
         self.data_bytes = nb.value
@@ -171,6 +175,56 @@ class Weights:
                                                       C.byref(h)))
         return Weights(h, ctx)
 
+    @staticmethod
+    def from_q8_0(blocks, num_elements: int, device: int = 0) -> "Weights":
+        """read_q8_0_weights (src/gguf.rs:245-271) on the device: ``blocks`` holds the GGUF Q8_0
+        tensor bytes (ceil(n/32) blocks of 34 bytes: f16 scale, 32 int8) on the host, or is a
+        CUDA torch uint8 tensor on the weights' device.  Returns int8 weights with block 32."""
+        ctx = _require_cuda(device)
+        h = C.c_void_p()
+        try:
+            import torch
+            is_dev = isinstance(blocks, torch.Tensor) and blocks.is_cuda
+        except ImportError:  # pragma: no cover
+            is_dev = False
+        nb = (num_elements + 31) // 32
+        if is_dev:
+            if blocks.numel() * blocks.element_size() < nb * 34:
+                raise PyxisError(_native.PYXIS_EINVAL, "q8_0 tensor shorter than ceil(n/32) * 34 bytes")
+            check(_native.lib().pyxis_cuda_weights_upload_q8_0(ctx.handle, C.c_void_p(blocks.data_ptr()), 1,
+                                                               num_elements, C.byref(h)))
+            return Weights(h, ctx)
+        b = np.frombuffer(bytes(blocks), dtype=np.uint8) if isinstance(blocks, (bytes, bytearray, memoryview)) \
+            else np.ascontiguousarray(np.asarray(blocks).view(np.uint8).reshape(-1))
+        if b.size < nb * 34:  # tensor_bytes: the data must cover every block (src/gguf.rs:273-287)
+            raise PyxisError(_native.PYXIS_EINVAL, "q8_0 tensor shorter than ceil(n/32) * 34 bytes")
+        check(_native.lib().pyxis_cuda_weights_upload_q8_0(ctx.handle, b.ctypes.data_as(C.c_void_p), 0,
+                                                           num_elements, C.byref(h)))
+        return Weights(h, ctx)
+
+    @staticmethod
+    def from_dense(values, device: int = 0) -> "Weights":
+        """Unquantized rows on the device: Weights::F32 from float values, Weights::Bf16 from raw
+        bf16 bit patterns (a np.uint16 array or a torch.bfloat16 tensor)."""
+        ctx = _require_cuda(device)
+        try:
+            import torch
+            if isinstance(values, torch.Tensor):
+                values = values.detach().cpu()
+                values = values.view(torch.int16).numpy().view(np.uint16) if values.dtype == torch.bfloat16 \
+                    else values.numpy()
+        except ImportError:  # pragma: no cover
+            pass
+        arr = np.asarray(values)
+        if arr.dtype == np.uint16:
+            arr, qt = np.ascontiguousarray(arr.reshape(-1)), QTYPE_BF16
+        else:
+            arr, qt = _f32(arr).reshape(-1), QTYPE_F32
+        h = C.c_void_p()
+        check(_native.lib().pyxis_cuda_weights_upload(ctx.handle, qt, arr.ctypes.data_as(C.c_void_p), None,
+                                                      arr.size, 0, C.byref(h)))
+        return Weights(h, ctx)
+
     # -- accessors ---------------------------------------------------------------------------
     def len(self) -> int:
         return self.num_elements
@@ -182,8 +236,10 @@ class Weights:
         return self.num_elements == 0
 
     def download(self) -> tuple[np.ndarray, np.ndarray]:
-        """(data, scales) on the host: int8 -> np.int8 [n]; int4 -> np.uint8 [ceil(n/2)]."""
-        data = np.empty(self.data_bytes, dtype=np.int8 if self.qtype == "int8" else np.uint8)
+        """(data, scales) on the host: int8 -> np.int8 [n]; int4 -> np.uint8 [ceil(n/2)];
+        f32 -> np.float32 [n]; bf16 -> np.uint16 [n] (no scales: an empty array)."""
+        dt = {"int8": np.int8, "int4": np.uint8, "f32": np.float32, "bf16": np.uint16}[self.qtype]
+        data = np.empty(self.data_bytes // np.dtype(dt).itemsize, dtype=dt)
         scales = np.empty(self.num_scales, dtype=np.float32)
         check(_native.lib().pyxis_cuda_weights_download(self.handle, data.ctypes.data_as(C.c_void_p),
                                                         scales.ctypes.data_as(C.c_void_p)))

@@ -21,6 +21,8 @@ PYXIS_EUNSUPPORTED = 6
 
 QTYPE_INT8 = 1
 QTYPE_INT4 = 2
+QTYPE_F32 = 3
+QTYPE_BF16 = 4
 DTYPE_F32 = 1
 DTYPE_BF16 = 2
 
@@ -37,6 +39,7 @@ SIGNATURES = {
     "pyxis_cuda_synchronize": (C.c_int, [_vp]),
     "pyxis_cuda_quantize": (C.c_int, [_vp, _vp, C.c_int, C.c_int, _sz, _sz, C.c_int, C.POINTER(_vp)]),
     "pyxis_cuda_weights_upload": (C.c_int, [_vp, C.c_int, _vp, _vp, _sz, _sz, C.POINTER(_vp)]),
+    "pyxis_cuda_weights_upload_q8_0": (C.c_int, [_vp, _vp, C.c_int, _sz, C.POINTER(_vp)]),
     "pyxis_cuda_weights_info": (C.c_int, [_vp, C.POINTER(C.c_int), C.POINTER(_sz), C.POINTER(_sz),
                                           C.POINTER(_sz), C.POINTER(_sz)]),
     "pyxis_cuda_weights_download": (C.c_int, [_vp, _vp, _vp]),

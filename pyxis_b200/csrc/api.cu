@@ -57,7 +57,17 @@ size_t div_ceil(size_t a, size_t b) { return (a + b - 1) / b; }
 constexpr size_t kTcMinRows = 16;        // matmul_dev rows from which the tensor-core GEMM runs
 constexpr size_t kTcGemvMinRows = 32768;  // out_features from which int8 GEMVs use tensor cores
 
-size_t packed_bytes(int qtype, size_t n) { return qtype == PYXIS_QTYPE_INT8 ? n : div_ceil(n, 2); }
+bool is_dense(int qtype) { return qtype == PYXIS_QTYPE_F32 || qtype == PYXIS_QTYPE_BF16; }
+bool is_qtype(int qtype) { return qtype >= PYXIS_QTYPE_INT8 && qtype <= PYXIS_QTYPE_BF16; }
+
+size_t packed_bytes(int qtype, size_t n) {
+    switch (qtype) {
+    case PYXIS_QTYPE_INT8: return n;
+    case PYXIS_QTYPE_INT4: return div_ceil(n, 2);
+    case PYXIS_QTYPE_F32: return n * 4;
+    default: return n * 2;  // BF16
+    }
+}
 
 int grow(float **buf, size_t *cap, size_t need) {
     if (need <= *cap) return PYXIS_OK;
@@ -76,9 +86,9 @@ int alloc_weights(pyxis_cuda_ctx *ctx, int qtype, size_t n, size_t bs, pyxis_cud
     w->device = ctx->device;
     w->qtype = qtype;
     w->num_elements = n;
-    w->block_size = bs;
+    w->block_size = is_dense(qtype) ? 0 : bs;
     w->data_bytes = packed_bytes(qtype, n);
-    w->num_scales = div_ceil(n, bs);
+    w->num_scales = is_dense(qtype) ? 0 : div_ceil(n, bs);
     size_t off = div_ceil(w->data_bytes, 256) * 256;
     size_t total = off + w->num_scales * sizeof(float);
     void *mem = nullptr;
@@ -114,7 +124,7 @@ int check_matmul(const pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, size_t 
     if (w->num_elements != out_features * in_features)
         return fail(PYXIS_EINVAL, "weight.len() = %zu != out_features * in_features = %zu * %zu",
                     w->num_elements, out_features, in_features);
-    if (w->block_size == 0) return fail(PYXIS_EINVAL, "block_size must be > 0");
+    if (!is_dense(w->qtype) && w->block_size == 0) return fail(PYXIS_EINVAL, "block_size must be > 0");
     return PYXIS_OK;
 }
 
@@ -311,9 +321,9 @@ int pyxis_cuda_weights_upload(pyxis_cuda_ctx *ctx, int qtype, const void *data, 
                               size_t n, size_t block_size, pyxis_cuda_weights **out) {
     if (!ctx || !out) return fail(PYXIS_EINVAL, "null context or output pointer");
     *out = nullptr;
-    if (block_size == 0) return fail(PYXIS_EINVAL, "block_size must be > 0");
-    if (qtype != PYXIS_QTYPE_INT8 && qtype != PYXIS_QTYPE_INT4) return fail(PYXIS_EINVAL, "unknown qtype %d", qtype);
-    if (n && (!data || !scales)) return fail(PYXIS_EINVAL, "null data or scales");
+    if (!is_qtype(qtype)) return fail(PYXIS_EINVAL, "unknown qtype %d", qtype);
+    if (!is_dense(qtype) && block_size == 0) return fail(PYXIS_EINVAL, "block_size must be > 0");
+    if (n && (!data || (!is_dense(qtype) && !scales))) return fail(PYXIS_EINVAL, "null data or scales");
     DeviceGuard g(ctx->device);
     pyxis_cuda_weights *w = nullptr;
     int rc = alloc_weights(ctx, qtype, n, block_size, &w);
@@ -326,6 +336,48 @@ int pyxis_cuda_weights_upload(pyxis_cuda_ctx *ctx, int qtype, const void *data, 
     if (e != cudaSuccess) {
         pyxis_cuda_weights_free(w);
         return cuda_fail(e, "weights upload");
+    }
+    *out = w;
+    return PYXIS_OK;
+}
+
+int pyxis_cuda_weights_upload_q8_0(pyxis_cuda_ctx *ctx, const void *blocks, int blocks_on_device, size_t n,
+                                   pyxis_cuda_weights **out) {
+    if (!ctx || !out) return fail(PYXIS_EINVAL, "null context or output pointer");
+    *out = nullptr;
+    if (n && !blocks) return fail(PYXIS_EINVAL, "null blocks");
+    constexpr size_t kQ8Block = 32, kQ8Bytes = 34;  // src/gguf.rs:246-247
+    const size_t nb = div_ceil(n, kQ8Block);
+    if (nb > SIZE_MAX / kQ8Bytes) return fail(PYXIS_EINVAL, "tensor too large");  // checked_byte_len
+    DeviceGuard g(ctx->device);
+    if (blocks_on_device && n) {
+        cudaPointerAttributes pa;
+        cudaError_t pe = cudaPointerGetAttributes(&pa, blocks);
+        if (pe != cudaSuccess || (pa.type != cudaMemoryTypeDevice && pa.type != cudaMemoryTypeManaged) ||
+            (pa.type == cudaMemoryTypeDevice && pa.device != ctx->device)) {
+            cudaGetLastError();
+            return fail(PYXIS_EINVAL, "upload_q8_0: the blocks are not memory of device %d", ctx->device);
+        }
+    }
+    pyxis_cuda_weights *w = nullptr;
+    int rc = alloc_weights(ctx, PYXIS_QTYPE_INT8, n, kQ8Block, &w);
+    if (rc) return rc;
+    const void *dblocks = blocks;
+    void *tmp = nullptr;
+    cudaError_t e = cudaSuccess;
+    if (!blocks_on_device && n) {
+        e = cudaMalloc(&tmp, nb * kQ8Bytes);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(tmp, blocks, nb * kQ8Bytes, cudaMemcpyHostToDevice, ctx->stream);
+        dblocks = tmp;
+    }
+    if (e == cudaSuccess && n)
+        e = launch_q8_0_unpack(reinterpret_cast<const uint8_t *>(dblocks), n, reinterpret_cast<int8_t *>(w->data),
+                               w->scales, ctx->num_sms, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (tmp) cudaFree(tmp);
+    if (e != cudaSuccess) {
+        pyxis_cuda_weights_free(w);
+        return cuda_fail(e, "upload_q8_0");
     }
     *out = w;
     return PYXIS_OK;

@@ -495,8 +495,11 @@ int enqueue_step(pyxis_cuda_model *m, cudaStream_t st) {
     return PYXIS_OK;
 }
 
+// The decode model takes the quantized layouts (its fused GEMV prologues and the prefill GEMM
+// are int8 / int4 kernels); unquantized rows go through pyxis_cuda_matmul*.
 bool weights_ok(const pyxis_cuda_weights *w, size_t n, int device) {
-    return w && w->num_elements == n && w->device == device;
+    return w && w->num_elements == n && w->device == device &&
+           (w->qtype == PYXIS_QTYPE_INT8 || w->qtype == PYXIS_QTYPE_INT4);
 }
 
 }  // namespace

@@ -609,6 +609,7 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 }  // namespace
 
 bool gemm_tc_supported(const QMatrix &w) {
+    if (w.qtype != kQInt8 && w.qtype != kQInt4) return false;  // unquantized rows take the GEMV
     const size_t K = w.K, bs = w.block_size;
     if (K == 0 || K % BK != 0 || K > (1u << 20) || w.N > (size_t)INT32_MAX) return false;
     if ((reinterpret_cast<uintptr_t>(w.data) & 15) != 0) return false;

@@ -1,4 +1,5 @@
-// gemv.cu -- decode GEMV over int8 / int4 weights in the reference layout, fp32 accumulation.
+// gemv.cu -- decode GEMV over int8 / int4 / f32 / bf16 weights in the reference layout, fp32
+// accumulation.
 //
 // Computes what src/matmul.rs:67-96 computes row by row -- y[n] = sum_i x[i] * q[n,i] *
 // scale(n,i) -- for B = 1..8 input rows at once, streaming the packed weights from HBM once.
@@ -28,7 +29,14 @@ __global__ void gemv_generic_kernel(const uint8_t *W, const float *S, size_t bs,
         for (size_t i = lane; i < K; i += 32) {
             const size_t g = row * K + i;  // flattened index: blocks run over it (src/matmul.rs:70)
             float q;
-            if (QT == kQInt8) {
+            if (QT == kQF32) {
+                acc += x[i] * reinterpret_cast<const float *>(W)[g];  // dot_product_scalar, :284-287
+                continue;
+            } else if (QT == kQBF16) {
+                const uint32_t bits = reinterpret_cast<const uint16_t *>(W)[g];
+                acc += x[i] * __uint_as_float(bits << 16);  // dot_product_bf16_scalar, :289-295
+                continue;
+            } else if (QT == kQInt8) {
                 q = (float)(int8_t)W[g];
             } else {
                 const uint8_t byte = W[g / 2];
@@ -55,10 +63,21 @@ cudaError_t launch_gemv(const QMatrix &w, const float *X, size_t B, size_t ldx, 
         return launch_gemv_batch(w, X, B, ldx, Y, ldy, err, num_sms, st);
     const size_t threads = w.N * 32;
     const unsigned grid = (unsigned)((threads + 255) / 256);
-    if (w.qtype == kQInt8)
+    switch (w.qtype) {
+    case kQInt8:
         gemv_generic_kernel<kQInt8><<<grid, 256, 0, st>>>(w.data, w.scales, w.block_size, X, ldx, Y, ldy, w.N, w.K, (int)B);
-    else
+        break;
+    case kQInt4:
         gemv_generic_kernel<kQInt4><<<grid, 256, 0, st>>>(w.data, w.scales, w.block_size, X, ldx, Y, ldy, w.N, w.K, (int)B);
+        break;
+    case kQF32:
+        gemv_generic_kernel<kQF32><<<grid, 256, 0, st>>>(w.data, w.scales, 1, X, ldx, Y, ldy, w.N, w.K, (int)B);
+        break;
+    case kQBF16:
+        gemv_generic_kernel<kQBF16><<<grid, 256, 0, st>>>(w.data, w.scales, 1, X, ldx, Y, ldy, w.N, w.K, (int)B);
+        break;
+    default: return cudaErrorInvalidValue;
+    }
     return cudaGetLastError();
 }
 

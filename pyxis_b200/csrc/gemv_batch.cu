@@ -1,6 +1,6 @@
-// gemv_batch.cu -- quantized matmul for 1-8 input rows on the CUDA cores (int4 groups and int8),
-// the decode shapes the tensor-core GEMV does not take: y[b, n] = sum_k x[b, k] * dequant(W)[n, k]
-// (src/matmul.rs:21-97 for each of the B input rows).
+// gemv_batch.cu -- matmul for 1-8 input rows on the CUDA cores (int4 groups, int8, and the
+// unquantized f32 / bf16 rows), the decode shapes the tensor-core GEMV does not take:
+// y[b, n] = sum_k x[b, k] * dequant(W)[n, k] (src/matmul.rs:21-97 for each of the B input rows).
 //
 // Layout of the work.  A row group is 4 weight rows.  A CTA takes `groups_cta` row groups at a
 // time and splits each group's K range over `slices` warps: warp (g, s) streams the 16-byte
@@ -32,7 +32,7 @@ constexpr int max_warps(int B) { return B >= 7 ? 8 : kMaxWarps; }
 constexpr int kXBoxRows = 256;  // TMA box limit per dimension (rows of 32 floats)
 constexpr int kErrX = 0x401;    // x never arrived
 constexpr uint64_t kTimeoutNs = 2000000000ull;
-enum { kScaleRow = 0, kScaleChunk = 1 };  // one scale per row / per block of whole chunks
+enum { kScaleRow = 0, kScaleChunk = 1, kScaleNone = 2 };  // per row / per block of whole chunks / none
 
 struct BatchParams {
     const uint8_t *W;
@@ -63,6 +63,19 @@ template <>
 struct Codes<kQInt4> {
     static constexpr int EPC = 32;
 };
+template <>
+struct Codes<kQF32> {
+    static constexpr int EPC = 4;
+};
+template <>
+struct Codes<kQBF16> {
+    static constexpr int EPC = 8;
+};
+
+constexpr int elems_per_chunk(int qtype) {
+    return qtype == kQInt8 ? 16 : qtype == kQInt4 ? 32 : qtype == kQF32 ? 4 : 8;
+}
+constexpr bool dense_qtype(int qtype) { return qtype == kQF32 || qtype == kQBF16; }
 
 // byte offset of logical offset `off` in a 1024-byte aligned, 128-byte swizzled region
 PYXIS_DEVINL uint32_t swz128(uint32_t off) { return off ^ (((off >> 7) & 7u) << 4); }
@@ -252,6 +265,35 @@ __global__ void __launch_bounds__(max_warps(B) * 32, 1)
                     if (nit < p.items && row0_of(nit) < p.N) load(row0_of(nit), c0);
                 }
                 const uint32_t xoff = (uint32_t)c * (EPC * 4);
+                if constexpr (dense_qtype(QT)) {
+                    // unquantized rows: an f32 chunk is one quad of weights, a bf16 chunk two
+                    // (bf16 -> f32 by u32 << 16, src/matmul.rs:289-295)
+#pragma unroll
+                    for (int qd = 0; qd < EPC / 4; ++qd) {
+                        float4 xq[B];
+#pragma unroll
+                        for (int t = 0; t < B; ++t)
+                            xq[t] = *reinterpret_cast<const float4 *>(xs + (size_t)t * p.tok_stride +
+                                                                      swz128(xoff + (uint32_t)qd * 16));
+#pragma unroll
+                        for (int r = 0; r < kRows; ++r) {
+                            float2 q0, q1;
+                            if constexpr (QT == kQF32) {
+                                q0 = f2(__uint_as_float(wc[r].x), __uint_as_float(wc[r].y));
+                                q1 = f2(__uint_as_float(wc[r].z), __uint_as_float(wc[r].w));
+                            } else {
+                                const uint32_t a = qd == 0 ? wc[r].x : wc[r].z, b = qd == 0 ? wc[r].y : wc[r].w;
+                                q0 = f2(__uint_as_float(a << 16), __uint_as_float(a & 0xffff0000u));
+                                q1 = f2(__uint_as_float(b << 16), __uint_as_float(b & 0xffff0000u));
+                            }
+#pragma unroll
+                            for (int t = 0; t < B; ++t) {
+                                acc[r][t] = ffma2(q0, f2(xq[t].x, xq[t].y), acc[r][t]);
+                                acc[r][t] = ffma2(q1, f2(xq[t].z, xq[t].w), acc[r][t]);
+                            }
+                        }
+                    }
+                } else {
 #pragma unroll
                 for (int wi = 0; wi < 4; ++wi) {
                     // one 32-bit word of codes per row: int8 4 elements (1 x quad), int4 8 (2 quads)
@@ -281,6 +323,7 @@ __global__ void __launch_bounds__(max_warps(B) * 32, 1)
                                 acc[r][t] = ffma2(q[2 * qd + 1], f2(xq[qd][t].z, xq[qd][t].w), acc[r][t]);
                             }
                     }
+                }
                 }
             }
         }
@@ -328,12 +371,13 @@ constexpr size_t kMaxSmem = 226 * 1024;
 
 Shape shape_for(const QMatrix &w, size_t B, int num_sms) {
     Shape sh;
-    const int epc = w.qtype == kQInt8 ? 16 : 32;
+    if (w.qtype < kQInt8 || w.qtype > kQBF16) return sh;
+    const int epc = elems_per_chunk(w.qtype);
     const size_t K = w.K, bs = w.block_size;
     if (B < 1 || B > 8 || K == 0 || K % 32 != 0 || K > (1u << 20) || w.N == 0 || w.N > (size_t)INT32_MAX / 2)
         return sh;
     if (reinterpret_cast<uintptr_t>(w.data) & 15) return sh;
-    if (!(bs == K || (bs % epc == 0 && K % bs == 0))) return sh;
+    if (!dense_qtype(w.qtype) && !(bs == K || (bs % epc == 0 && K % bs == 0))) return sh;
     const int chunks = (int)(K / epc);
     const int rows = (int)(K / 32);
     sh.x_boxes = (rows + kXBoxRows - 1) / kXBoxRows;
@@ -384,8 +428,8 @@ bool gemv_batch_supported(const QMatrix &w, size_t B, int num_sms) { return shap
 namespace {
 
 BatchParams make_params(const QMatrix &w, const Shape &sh, float *Y, size_t ldy, int *err) {
-    const int epc = w.qtype == kQInt8 ? 16 : 32;
-    const bool chunk_mode = w.block_size != w.K;
+    const int epc = elems_per_chunk(w.qtype);
+    const bool chunk_mode = !dense_qtype(w.qtype) && w.block_size != w.K;
     BatchParams p{};
     p.W = w.data;
     p.S = w.scales;
@@ -393,7 +437,7 @@ BatchParams make_params(const QMatrix &w, const Shape &sh, float *Y, size_t ldy,
     p.N = (int)w.N;
     p.K = (int)w.K;
     p.ldy = (int)ldy;
-    p.row_bytes = w.qtype == kQInt8 ? (int)w.K : (int)(w.K / 2);
+    p.row_bytes = (int)(w.K / epc * 16);
     p.chunks = (int)(w.K / epc);
     p.blocks_per_row = chunk_mode ? (int)(w.K / w.block_size) : 1;
     p.chunks_per_block = chunk_mode ? (int)(w.block_size / epc) : 1;
@@ -428,6 +472,8 @@ cudaError_t launch_gemv_batch(const QMatrix &w, const float *X, size_t B, size_t
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return cudaErrorInvalidValue;
     const BatchParams p = make_params(w, sh, Y, ldy, err);
+    if (w.qtype == kQF32) return dispatch<kQF32, kScaleNone>(B, tm, p, sh, num_sms, st);
+    if (w.qtype == kQBF16) return dispatch<kQBF16, kScaleNone>(B, tm, p, sh, num_sms, st);
     const bool chunk_mode = w.block_size != w.K;
     if (w.qtype == kQInt8)
         return chunk_mode ? dispatch<kQInt8, kScaleChunk>(B, tm, p, sh, num_sms, st)
@@ -438,6 +484,7 @@ cudaError_t launch_gemv_batch(const QMatrix &w, const float *X, size_t B, size_t
 
 bool gemv_batch_pro_supported(const QMatrix &w, const GemvPrologue &pro, int num_sms) {
     if (pro.kind != kProAddNorm && pro.kind != kProSiluMul) return false;
+    if (w.qtype != kQInt8 && w.qtype != kQInt4) return false;  // the decode model's layouts
     if (!pro.x || (reinterpret_cast<uintptr_t>(pro.x) & 15)) return false;
     if (pro.kind == kProAddNorm) {
         if (!pro.w || (reinterpret_cast<uintptr_t>(pro.w) & 15)) return false;

@@ -8,9 +8,10 @@
 namespace pyxis {
 
 enum { kSrcF32 = 1, kSrcBF16 = 2 };  // == PYXIS_DTYPE_*
-enum { kQInt8 = 1, kQInt4 = 2 };     // == PYXIS_QTYPE_*
+enum { kQInt8 = 1, kQInt4 = 2, kQF32 = 3, kQBF16 = 4 };  // == PYXIS_QTYPE_*
 
-// A quantized matrix [N, K] in the reference layout (see pyxis_cuda.h).
+// A weight matrix [N, K] in the reference layout (see pyxis_cuda.h); unquantized (kQF32, kQBF16)
+// matrices have no scales.
 struct QMatrix {
     int qtype;
     const uint8_t *data;
@@ -22,8 +23,12 @@ struct QMatrix {
 cudaError_t launch_quantize(const void *src, int src_kind, size_t n, size_t bs, int qtype,
                             void *data, float *scales, int num_sms, cudaStream_t st);
 
+// GGUF Q8_0 blocks (34 bytes: f16 scale, 32 int8) -> int8 codes [n] and f32 scales [ceil(n/32)].
+cudaError_t launch_q8_0_unpack(const uint8_t *blocks, size_t n, int8_t *data, float *scales, int num_sms,
+                               cudaStream_t st);
+
 // Decode GEMV: Y[b, :] = W X[b, :] for b < B (B = 1..8): the batch kernel where it applies, else
-// the generic kernel (gemv.cu).
+// the generic kernel (gemv.cu).  Every weight layout.
 cudaError_t launch_gemv(const QMatrix &w, const float *X, size_t B, size_t ldx, float *Y,
                         size_t ldy, int *err, int num_sms, cudaStream_t st);
 

@@ -135,6 +135,50 @@ static cudaError_t launch_quantize_t(const void *src, size_t n, size_t bs, int q
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------- GGUF Q8_0 ---------------------
+// f16 bits -> f32 as half 2.7.1's f16::to_f32 widens (the same as x86 F16C): exact for every
+// finite value and for infinities; a NaN keeps its sign and payload and gets the quiet bit.
+__device__ __forceinline__ float f16_bits_to_f32(uint32_t h) {
+    const uint32_t sign = (h & 0x8000u) << 16, exp = (h >> 10) & 0x1fu, man = h & 0x3ffu;
+    if (exp == 0x1fu) return __uint_as_float(sign | 0x7f800000u | (man ? 0x400000u | (man << 13) : 0u));
+    if (exp != 0) return __uint_as_float(sign | ((exp + 112u) << 23) | (man << 13));
+    // zero or subnormal: man * 2^-24, exact in f32 (man < 2^10, a normal f32 result)
+    return __uint_as_float(sign | __float_as_uint(__fmul_rn((float)man, __uint_as_float(0x33800000u))));
+}
+
+// One thread per 34-byte block (src/gguf.rs:246-271): scale, then the 32 codes, the codes past
+// n (the last block's tail) dropped.  Byte loads: a block starts at any 2-byte boundary, and a
+// warp's 32 blocks are 1088 contiguous bytes, so the loads still coalesce.
+__global__ void q8_0_unpack_kernel(const uint8_t *__restrict__ blocks, size_t n, size_t nb, int8_t *__restrict__ data,
+                                   float *__restrict__ scales) {
+    for (size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x; b < nb; b += (size_t)gridDim.x * blockDim.x) {
+        const uint8_t *blk = blocks + b * 34;
+        scales[b] = f16_bits_to_f32((uint32_t)__ldg(blk) | ((uint32_t)__ldg(blk + 1) << 8));
+        uint32_t w[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            w[i] = (uint32_t)__ldg(blk + 2 + 4 * i) | ((uint32_t)__ldg(blk + 3 + 4 * i) << 8) |
+                   ((uint32_t)__ldg(blk + 4 + 4 * i) << 16) | ((uint32_t)__ldg(blk + 5 + 4 * i) << 24);
+        const size_t g0 = b * 32;
+        if (g0 + 32 <= n) {  // data is 256-byte aligned and g0 a multiple of 32
+            uint4 *d = reinterpret_cast<uint4 *>(data + g0);
+            d[0] = make_uint4(w[0], w[1], w[2], w[3]);
+            d[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        } else {
+            for (size_t i = 0; g0 + i < n; ++i) data[g0 + i] = (int8_t)((w[i / 4] >> (8 * (i % 4))) & 0xffu);
+        }
+    }
+}
+
+cudaError_t launch_q8_0_unpack(const uint8_t *blocks, size_t n, int8_t *data, float *scales, int num_sms,
+                               cudaStream_t st) {
+    if (n == 0) return cudaSuccess;
+    const size_t nb = (n + 31) / 32;
+    const size_t g = (nb + 255) / 256, gmax = (size_t)num_sms * 16;
+    q8_0_unpack_kernel<<<(unsigned)(g < gmax ? g : gmax), 256, 0, st>>>(blocks, n, nb, data, scales);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_quantize(const void *src, int src_kind, size_t n, size_t bs, int qtype,
                             void *data, float *scales, int num_sms, cudaStream_t st) {
     if (n == 0) return cudaSuccess;

@@ -161,3 +161,16 @@ def test_exact_matmul_helper_agrees_with_oracle():
             d, s = q(w, bs)
             ref = oracle.matmul(x, kind, d, s, bs, N, K)
             assert rel_err(exact_matmul(qt, d, s, bs, N, K, x), ref) < 1e-4
+
+
+def test_oracle_f16_widening_over_every_bit_pattern():
+    """Q8_0 scales: half 2.7.1's f16::to_f32 (the x86 F16C instruction widens the same way).
+    Finite values and infinities are exact (numpy's widening agrees); a NaN keeps its sign and
+    payload and gets the quiet bit."""
+    L = oracle.lib()
+    h = np.arange(65536, dtype=np.uint32)
+    got = np.array([L.oracle_f16_to_f32(int(v)) for v in h], np.float32).view(np.uint32)
+    is_nan = ((h >> 10) & 0x1F == 0x1F) & (h & 0x3FF != 0)
+    want = h.astype(np.uint16).view(np.float16).astype(np.float32).view(np.uint32).copy()
+    want[is_nan] = ((h[is_nan] & 0x8000) << 16) | 0x7FC00000 | ((h[is_nan] & 0x3FF) << 13)
+    assert np.array_equal(got, want)
