@@ -290,21 +290,23 @@ def run_prefill(local, reps=20):
         w = px.Weights.quantize_int8(t, bs, device=local) if qt == "int8" else px.Weights.quantize_int4(t, bs, device=local)
         X = torch.from_numpy(px.synth_normal_f32(SEED + 60 + i, PREFILL_M * K, 1.0)).to(dev).view(PREFILL_M, K)
         Y = torch.empty((PREFILL_M, N), dtype=torch.float32, device=dev)
-        need = px._native.lib().pyxis_cuda_matmul_workspace_size(PREFILL_M, K)
-        ws = torch.empty(need, dtype=torch.uint8, device=dev)
+        # the context's own workspace (allocated by the first call, outside the timing): it also
+        # holds split-K partials, which a caller workspace of pyxis_cuda_matmul_workspace_size
+        # bytes has no room for (down_proj's 64 output tiles would leave most SMs idle)
         for _ in range(3):
-            px.matmul_dev(X, w, N, K, Y=Y, workspace=ws)
+            px.matmul_dev(X, w, N, K, Y=Y)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(reps):
-            px.matmul_dev(X, w, N, K, Y=Y, workspace=ws)
+            px.matmul_dev(X, w, N, K, Y=Y)
         e1.record()
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1e3 / reps
         flops = 2.0 * PREFILL_M * N * K
-        out.append({"shape": f"{name}: X[{PREFILL_M},{K}] x W[{N},{K}]", "us": us, "tflops": flops / us / 1e6})
-        del w, X, Y, ws, t
+        out.append({"shape": f"{name}: X[{PREFILL_M},{K}] x W[{N},{K}]", "us": us, "tflops": flops / us / 1e6,
+                    "kernel": px.matmul_kernel_name(w, PREFILL_M, N, K), "l2": "warm (back-to-back launches)"})
+        del w, X, Y, t
     return out
 
 
@@ -732,6 +734,39 @@ def profile_case(args):
         print(f"profile case decode: prompt {ctx}, {n - 1} steps, prompt {t[0]:.2f} ms, "
               f"decode {t[1] / (n - 1):.3f} ms/token")
         return
+    if args.profile_case == "sweep":
+        # the timed step's 12 GEMV launches (every SWEEP matrix at batch 1 and 8), eagerly
+        ws_ = {}
+        for i, (name, qt, N, K, bs) in enumerate(SWEEP):
+            bits = px.synth_normal_bf16(SEED + i, N * K, 0.02)
+            t = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).cuda()
+            ws_[name] = px.Weights.quantize_int8(t, bs) if qt == "int8" else px.Weights.quantize_int4(t, bs)
+            del t
+        X = {B: torch.from_numpy(px.synth_normal_f32(SEED + 100 + B, B * 6144, 1.0)).cuda().view(B, 6144)
+             for B in BATCHES}
+        Y = {B: torch.empty((B, 151936), dtype=torch.float32, device="cuda") for B in BATCHES}
+        for _ in range(args.warmup + args.steps):
+            for B in BATCHES:
+                for (name, qt, N, K, bs) in SWEEP:
+                    px.matmul_dev(X[B][:, :K], ws_[name], N, K, Y=Y[B][:, :N])
+        torch.cuda.synchronize()
+        print(f"profile case sweep: {args.warmup + args.steps} steps of {len(SWEEP) * len(BATCHES)} launches")
+        return
+    if args.profile_case.startswith("prefill"):
+        # one prefill GEMM: prefill:<int8|int4>:<gate|down>:<M>
+        _, qt, which, M = args.profile_case.split(":")
+        M = int(M)
+        (name, _, N, K, bs) = next(s for s in PREFILL_SHAPES if s[0] == f"{which}_proj {qt}")
+        bits = px.synth_normal_bf16(SEED + 50, N * K, 0.02)
+        t = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).cuda()
+        w = px.Weights.quantize_int8(t, bs) if qt == "int8" else px.Weights.quantize_int4(t, bs)
+        X = torch.from_numpy(px.synth_normal_f32(SEED + 60, M * K, 1.0)).cuda().view(M, K)
+        Y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        for _ in range(args.warmup + args.steps):
+            px.matmul_dev(X, w, N, K, Y=Y)
+        torch.cuda.synchronize()
+        print(f"profile case {name} M={M}: {px.matmul_kernel_name(w, M, N, K)}, {args.warmup + args.steps} launches")
+        return
     name, B = args.profile_case.split(":") if ":" in args.profile_case else (args.profile_case, "1")
     B = int(B)
     (_, qt, N, K, bs) = next(m for m in SWEEP if m[0] == name)
@@ -749,7 +784,8 @@ def profile_case(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--profile-case", default=None,
-                    help="run one GEMV shape only, e.g. lm_head:1 or gate_proj:8 (for ncu)")
+                    help="run one shape only, for ncu: lm_head:1, gate_proj:8, sweep (the timed step's "
+                         "12 GEMVs), prefill:int4:gate:512, decode:CTX, batch:SEQS:PROMPT:NEW")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
