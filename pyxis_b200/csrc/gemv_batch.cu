@@ -88,10 +88,9 @@ PYXIS_DEVINL uint32_t swz128(uint32_t off) { return off ^ (((off >> 7) & 7u) << 
 // the first use; K <= 4 * PQ * blockDim is one round (the decode shapes).  The norm weight does not
 // depend on the previous kernel and is read before griddepcontrol.wait.
 template <int PRO>
-PYXIS_DEVINL void run_prologue(const BatchParams &p, uint8_t *xs, float *red) {
+PYXIS_DEVINL void run_prologue(const GemvPrologue &pr, int K, uint8_t *xs, float *red) {
     constexpr int PQ = 4;
-    const GemvPrologue &pr = p.pro;
-    const int K = p.K, nq = K / 4, nt = blockDim.x;
+    const int nq = K / 4, nt = blockDim.x;
     const float4 *x4 = reinterpret_cast<const float4 *>(pr.x);
     if constexpr (PRO == kProAddNorm) {
         const float4 *d4 = reinterpret_cast<const float4 *>(pr.delta);
@@ -176,6 +175,115 @@ PYXIS_DEVINL void run_prologue(const BatchParams &p, uint8_t *xs, float *red) {
     __syncthreads();
 }
 
+// acc[r][t] += W[row r, the 16-byte chunk's values] * x[t, the same k] for one chunk: codes
+// decoded to exact float pairs (int8 / int4) or unquantized f32 / bf16 (bf16 -> f32 by u32 << 16,
+// src/matmul.rs:289-295), x read from its 128-byte swizzled shared-memory tile at byte offset xoff
+// (4 * the chunk's first k).  Group scales (chunk mode; a chunk lies inside one group): up to 4
+// input rows sum q x over the chunk and multiply by the scale once (one paired FMA per row and
+// token instead of a paired multiply per code pair); 5-8 rows, which would need more than 255
+// registers for the chunk sums, scale the code pairs (one multiply per pair serves every token).
+template <int QT, int B, int SMODE>
+PYXIS_DEVINL void fma_chunk(const uint4 (&wc)[kRows], const float2 (&sc)[kRows], const uint8_t *xs,
+                            uint32_t tok_stride, uint32_t xoff, float2 (&acc)[kRows][B]) {
+    constexpr int EPC = Codes<QT>::EPC;
+    if constexpr (SMODE == kScaleChunk && B <= (QT == kQInt4 ? 4 : 3)) {
+        float2 part[kRows][B];
+#pragma unroll
+        for (int r = 0; r < kRows; ++r)
+#pragma unroll
+            for (int t = 0; t < B; ++t) part[r][t] = f2(0.f, 0.f);
+        float2 one[kRows];
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) one[r] = f2(1.f, 1.f);
+        fma_chunk<QT, B, kScaleRow>(wc, one, xs, tok_stride, xoff, part);
+#pragma unroll
+        for (int r = 0; r < kRows; ++r)
+#pragma unroll
+            for (int t = 0; t < B; ++t) acc[r][t] = ffma2(part[r][t], sc[r], acc[r][t]);
+        return;
+    }
+    if constexpr (dense_qtype(QT)) {
+        // an f32 chunk is one quad of weights, a bf16 chunk two
+#pragma unroll
+        for (int qd = 0; qd < EPC / 4; ++qd) {
+            float4 xq[B];
+#pragma unroll
+            for (int t = 0; t < B; ++t)
+                xq[t] = *reinterpret_cast<const float4 *>(xs + (size_t)t * tok_stride + swz128(xoff + (uint32_t)qd * 16));
+#pragma unroll
+            for (int r = 0; r < kRows; ++r) {
+                float2 q0, q1;
+                if constexpr (QT == kQF32) {
+                    q0 = f2(__uint_as_float(wc[r].x), __uint_as_float(wc[r].y));
+                    q1 = f2(__uint_as_float(wc[r].z), __uint_as_float(wc[r].w));
+                } else {
+                    const uint32_t a = qd == 0 ? wc[r].x : wc[r].z, b = qd == 0 ? wc[r].y : wc[r].w;
+                    q0 = f2(__uint_as_float(a << 16), __uint_as_float(a & 0xffff0000u));
+                    q1 = f2(__uint_as_float(b << 16), __uint_as_float(b & 0xffff0000u));
+                }
+#pragma unroll
+                for (int t = 0; t < B; ++t) {
+                    acc[r][t] = ffma2(q0, f2(xq[t].x, xq[t].y), acc[r][t]);
+                    acc[r][t] = ffma2(q1, f2(xq[t].z, xq[t].w), acc[r][t]);
+                }
+            }
+        }
+    } else {
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) {
+            // one 32-bit word of codes per row: int8 4 elements (1 x quad), int4 8 (2 quads)
+            constexpr int QPW = EPC / 16;
+            float4 xq[QPW][B];
+#pragma unroll
+            for (int qd = 0; qd < QPW; ++qd)
+#pragma unroll
+                for (int t = 0; t < B; ++t)
+                    xq[qd][t] = *reinterpret_cast<const float4 *>(xs + (size_t)t * tok_stride +
+                                                                  swz128(xoff + (uint32_t)(wi * QPW + qd) * 16));
+#pragma unroll
+            for (int r = 0; r < kRows; ++r) {
+                const uint32_t word = wi == 0 ? wc[r].x : wi == 1 ? wc[r].y : wi == 2 ? wc[r].z : wc[r].w;
+                float2 q[2 * QPW];
+                if constexpr (QT == kQInt8) i8x4_to_f32(word, q[0], q[1]);
+                else u4x8_to_f32(word, q[0], q[1], q[2], q[3]);
+                if constexpr (SMODE == kScaleChunk) {
+#pragma unroll
+                    for (int j = 0; j < 2 * QPW; ++j) q[j] = __fmul2_rn(q[j], sc[r]);
+                }
+#pragma unroll
+                for (int qd = 0; qd < QPW; ++qd)
+#pragma unroll
+                    for (int t = 0; t < B; ++t) {
+                        acc[r][t] = ffma2(q[2 * qd], f2(xq[qd][t].x, xq[qd][t].y), acc[r][t]);
+                        acc[r][t] = ffma2(q[2 * qd + 1], f2(xq[qd][t].z, xq[qd][t].w), acc[r][t]);
+                    }
+            }
+        }
+    }
+}
+
+// The warp's 32 (row, token) sums: even + odd partials, then halving exchanges over
+// v[r*8 + t] (31 shuffles); lane l ends with row l/8, token l%8.
+template <int B>
+PYXIS_DEVINL float reduce_rows_tokens(const float2 (&acc)[kRows][B], int lane) {
+    float v[32];
+#pragma unroll
+    for (int r = 0; r < kRows; ++r)
+#pragma unroll
+        for (int t = 0; t < 8; ++t) v[r * 8 + t] = t < B ? acc[r][t].x + acc[r][t].y : 0.f;
+#pragma unroll
+    for (int o = 16, n = 32; o >= 1; o >>= 1, n >>= 1) {
+        const bool upper = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < n / 2; ++i) {
+            const float send = upper ? v[i] : v[i + n / 2];
+            const float keep = upper ? v[i + n / 2] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+    }
+    return v[0];
+}
+
 template <int QT, int B, int SMODE, int PRO>
 __global__ void __launch_bounds__(max_warps(B) * 32, 1)
     gemv_batch_kernel(const __grid_constant__ CUtensorMap tm_x, const BatchParams p) {
@@ -209,7 +317,7 @@ __global__ void __launch_bounds__(max_warps(B) * 32, 1)
     if (it < p.items && row0_of(it) < p.N && c0 < p.chunks) load(row0_of(it), c0);
 
     if constexpr (PRO != kProNone) {
-        run_prologue<PRO>(p, xs, red);  // waits on the previous kernels itself
+        run_prologue<PRO>(p.pro, p.K, xs, red);  // waits on the previous kernels itself
     } else {
     if (threadIdx.x == 0) {
         abort_flag = 0;
@@ -264,87 +372,12 @@ __global__ void __launch_bounds__(max_warps(B) * 32, 1)
                     const int nit = it + gridDim.x;
                     if (nit < p.items && row0_of(nit) < p.N) load(row0_of(nit), c0);
                 }
-                const uint32_t xoff = (uint32_t)c * (EPC * 4);
-                if constexpr (dense_qtype(QT)) {
-                    // unquantized rows: an f32 chunk is one quad of weights, a bf16 chunk two
-                    // (bf16 -> f32 by u32 << 16, src/matmul.rs:289-295)
-#pragma unroll
-                    for (int qd = 0; qd < EPC / 4; ++qd) {
-                        float4 xq[B];
-#pragma unroll
-                        for (int t = 0; t < B; ++t)
-                            xq[t] = *reinterpret_cast<const float4 *>(xs + (size_t)t * p.tok_stride +
-                                                                      swz128(xoff + (uint32_t)qd * 16));
-#pragma unroll
-                        for (int r = 0; r < kRows; ++r) {
-                            float2 q0, q1;
-                            if constexpr (QT == kQF32) {
-                                q0 = f2(__uint_as_float(wc[r].x), __uint_as_float(wc[r].y));
-                                q1 = f2(__uint_as_float(wc[r].z), __uint_as_float(wc[r].w));
-                            } else {
-                                const uint32_t a = qd == 0 ? wc[r].x : wc[r].z, b = qd == 0 ? wc[r].y : wc[r].w;
-                                q0 = f2(__uint_as_float(a << 16), __uint_as_float(a & 0xffff0000u));
-                                q1 = f2(__uint_as_float(b << 16), __uint_as_float(b & 0xffff0000u));
-                            }
-#pragma unroll
-                            for (int t = 0; t < B; ++t) {
-                                acc[r][t] = ffma2(q0, f2(xq[t].x, xq[t].y), acc[r][t]);
-                                acc[r][t] = ffma2(q1, f2(xq[t].z, xq[t].w), acc[r][t]);
-                            }
-                        }
-                    }
-                } else {
-#pragma unroll
-                for (int wi = 0; wi < 4; ++wi) {
-                    // one 32-bit word of codes per row: int8 4 elements (1 x quad), int4 8 (2 quads)
-                    constexpr int QPW = EPC / 16;
-                    float4 xq[QPW][B];
-#pragma unroll
-                    for (int qd = 0; qd < QPW; ++qd)
-#pragma unroll
-                        for (int t = 0; t < B; ++t)
-                            xq[qd][t] = *reinterpret_cast<const float4 *>(
-                                xs + (size_t)t * p.tok_stride + swz128(xoff + (uint32_t)(wi * QPW + qd) * 16));
-#pragma unroll
-                    for (int r = 0; r < kRows; ++r) {
-                        const uint32_t word = wi == 0 ? wc[r].x : wi == 1 ? wc[r].y : wi == 2 ? wc[r].z : wc[r].w;
-                        float2 q[2 * QPW];
-                        if constexpr (QT == kQInt8) i8x4_to_f32(word, q[0], q[1]);
-                        else u4x8_to_f32(word, q[0], q[1], q[2], q[3]);
-                        if constexpr (SMODE == kScaleChunk) {
-#pragma unroll
-                            for (int j = 0; j < 2 * QPW; ++j) q[j] = __fmul2_rn(q[j], sc[r]);
-                        }
-#pragma unroll
-                        for (int qd = 0; qd < QPW; ++qd)
-#pragma unroll
-                            for (int t = 0; t < B; ++t) {
-                                acc[r][t] = ffma2(q[2 * qd], f2(xq[qd][t].x, xq[qd][t].y), acc[r][t]);
-                                acc[r][t] = ffma2(q[2 * qd + 1], f2(xq[qd][t].z, xq[qd][t].w), acc[r][t]);
-                            }
-                    }
-                }
-                }
+                fma_chunk<QT, B, SMODE>(wc, sc, xs, p.tok_stride, (uint32_t)c * (EPC * 4), acc);
             }
         }
-        // even + odd partials, then halving exchanges over v[r*8 + t]: lane l keeps index l
-        float v[32];
-#pragma unroll
-        for (int r = 0; r < kRows; ++r)
-#pragma unroll
-            for (int t = 0; t < 8; ++t) v[r * 8 + t] = t < B ? acc[r][t].x + acc[r][t].y : 0.f;
-#pragma unroll
-        for (int o = 16, n = 32; o >= 1; o >>= 1, n >>= 1) {
-            const bool upper = (lane & o) != 0;
-#pragma unroll
-            for (int i = 0; i < n / 2; ++i) {
-                const float send = upper ? v[i] : v[i + n / 2];
-                const float keep = upper ? v[i + n / 2] : v[i];
-                v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-            }
-        }
+        const float v0 = reduce_rows_tokens<B>(acc, lane);
         float *rb = red + buf * (kMaxWarps * 32);
-        rb[warp * 32 + lane] = v[0];
+        rb[warp * 32 + lane] = v0;
         __syncthreads();
         if (s == 0 && active) {
             float y = 0.f;
@@ -498,12 +531,12 @@ bool gemv_batch_pro_supported(const QMatrix &w, const GemvPrologue &pro, int num
 cudaError_t launch_gemv_batch_pro(const QMatrix &w, const GemvPrologue &pro, float *Y, int *err, int num_sms,
                                   cudaStream_t st) {
     if (!gemv_batch_pro_supported(w, pro, num_sms)) return cudaErrorInvalidValue;
+    const bool chunk_mode = w.block_size != w.K;
+    CUtensorMap tm;  // not read: the prologue writes x itself
+    memset(&tm, 0, sizeof(tm));
     const Shape sh = shape_for(w, 1, num_sms);
     BatchParams p = make_params(w, sh, Y, w.N, err);
     p.pro = pro;
-    CUtensorMap tm;  // not read: the prologue writes x itself
-    memset(&tm, 0, sizeof(tm));
-    const bool chunk_mode = w.block_size != w.K;
     if (pro.kind == kProAddNorm) {
         if (w.qtype == kQInt8)
             return chunk_mode ? run<kQInt8, 1, kScaleChunk, kProAddNorm>(tm, p, sh, num_sms, st)
