@@ -99,13 +99,18 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float *__rest
 // keys [s*len/S, (s+1)*len/S).  Every CTA normalises and rotates its heads' q and the new k itself
 // (a few hundred flops), the CTA holding key `pos` writes k and v to the cache, and the newest
 // key is taken from shared memory, so no CTA reads a cache row another one is writing.  Within a
-// CTA each warp takes every 8th key, streams its K and V rows together (the first ones before
-// griddepcontrol.wait) and keeps a running (max, sum of exp, sum of p v) per query head; the
+// CTA each warp takes every 8th key and streams its K and V rows through its own ring of
+// kAttnRing keys in shared memory with cp.async (the first ones before griddepcontrol.wait; data
+// in flight holds no registers, so three CTAs of 8 warps keep ~96 KB per SM in flight), and keeps
+// a running (max, sum of exp, sum of p v) per query head; the
 // warps, then the splits (the last CTA of a kv head, by ticket), are rescaled to a common max and
 // added in a fixed order.  The softmax is the reference's up to the order of the f32 sums.
 // Lane l of a warp holds head elements [l*EPL, (l+1)*EPL); RoPE pairs element i with i + hd/2,
 // which sits in lane l ^ 16.
 constexpr int kAttnThreads = 256;
+constexpr int kAttnRing = 8;  // keys per warp in its cp.async ring: PF being scored, the rest in flight
+template <int EPL>
+constexpr size_t attn_ring_bytes() { return (size_t)(kAttnThreads / 32) * kAttnRing * 2 * (32 * EPL) * sizeof(float); }
 template <int EPL, int G>
 __global__ void __launch_bounds__(kAttnThreads)
     attention_step_kernel(const float *__restrict__ qkv, const float *__restrict__ q_norm,
@@ -114,11 +119,13 @@ __global__ void __launch_bounds__(kAttnThreads)
                           float *__restrict__ kcache, float *__restrict__ vcache, float *__restrict__ part,
                           unsigned *__restrict__ tickets, float *__restrict__ out, long long qkv_stride,
                           long long cache_stride, long long out_stride) {
-    constexpr int HD = 32 * EPL, PF = 4;  // keys whose rows a warp has in flight at once
-    constexpr int NW = kAttnThreads / 32;
+    constexpr int HD = 32 * EPL, PF = 4;  // keys scored per round
+    constexpr int NW = kAttnThreads / 32, R = kAttnRing;
+    static_assert(R > PF, "the ring must hold the round being scored and keys in flight");
     __shared__ float qs[G][HD], knew[HD], vnew[HD];
     __shared__ float wpart[NW][G][HD + 2];  // per-warp (max, sum, acc[HD])
     __shared__ int flag;
+    extern __shared__ float4 attn_ring_raw[];  // [NW][R][K row | V row]
     const int S = gridDim.x, s = blockIdx.x, h = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kv_dim = n_kv * HD, q_dim = n_q * HD;
@@ -136,18 +143,20 @@ __global__ void __launch_bounds__(kAttnThreads)
     const int pos = *d_pos;
     const int len = pos + 1;
     const int j0 = (int)((long long)s * len / S), j1 = (int)((long long)(s + 1) * len / S);
-    float kr[PF][EPL], vr[PF][EPL];
-    auto fetch = [&](int jb) {
-#pragma unroll
-        for (int u = 0; u < PF; ++u) {
-            const int j = jb + u * NW;
-            if (j < j1 && j < pos) {
-                load_head<EPL>(kcache + (size_t)j * kv_dim + (size_t)h * HD + lane * EPL, kr[u]);
-                load_head<EPL>(vcache + (size_t)j * kv_dim + (size_t)h * HD + lane * EPL, vr[u]);
-            }
+    // this warp's keys j0 + warp + i * NW, i < nk; key i sits in ring slot i % R
+    const int nk = j0 + warp < j1 ? (j1 - 1 - (j0 + warp)) / NW + 1 : 0;
+    float *ring = reinterpret_cast<float *>(attn_ring_raw) + (size_t)warp * R * 2 * HD + lane * EPL;
+    auto issue = [&](int i) {  // one commit group per key (empty past the warp's keys)
+        const int j = j0 + warp + i * NW;
+        if (i < nk && j < pos) {  // key pos is the new one: taken from shared memory below
+            float *slot = ring + (size_t)(i % R) * 2 * HD;
+            cp_async_head<EPL>(slot, kcache + (size_t)j * kv_dim + (size_t)h * HD + lane * EPL);
+            cp_async_head<EPL>(slot + HD, vcache + (size_t)j * kv_dim + (size_t)h * HD + lane * EPL);
         }
+        cp_async_commit();
     };
-    fetch(j0 + warp);
+#pragma unroll
+    for (int i = 0; i < R - PF; ++i) issue(i);
     pdl_wait();
     pdl_trigger();
 
@@ -192,19 +201,16 @@ __global__ void __launch_bounds__(kAttnThreads)
             if (g < G) qr[g][t] = qs[g][lane * EPL + t];
         }
     }
-    // Each round: the next PF keys' rows are requested first, then the current ones are scored --
-    // all PF x G dot products reduced together (interleaved shuffles) -- and folded into the
-    // running softmax with one rescale per round.
-    for (int jb = j0 + warp; jb < j1; jb += PF * NW) {
-        float kn[PF][EPL], vn[PF][EPL];
+    // Each round: the copies of the keys R - PF ahead are issued, the round's PF keys are read
+    // back from the ring (each lane its own elements, so no warp barrier), scored -- all PF x G
+    // dot products reduced together (interleaved shuffles) -- and folded into the running softmax
+    // with one rescale per round.
+    for (int i0 = 0; i0 < nk; i0 += PF) {
+        const int jb = j0 + warp + i0 * NW;
 #pragma unroll
-        for (int u = 0; u < PF; ++u) {
-            const int j = jb + PF * NW + u * NW;
-            if (j < j1 && j < pos) {
-                load_head<EPL>(kcache + (size_t)j * kv_dim + (size_t)h * HD + lane * EPL, kn[u]);
-                load_head<EPL>(vcache + (size_t)j * kv_dim + (size_t)h * HD + lane * EPL, vn[u]);
-            }
-        }
+        for (int u = 0; u < PF; ++u) issue(i0 + R - PF + u);
+        cp_async_wait<R - PF>();  // keys up to i0 + PF - 1 have landed
+        float kr[PF][EPL], vr[PF][EPL];
         float dot[PF][G];
 #pragma unroll
         for (int u = 0; u < PF; ++u) {
@@ -214,6 +220,13 @@ __global__ void __launch_bounds__(kAttnThreads)
                     kr[u][t] = knew[lane * EPL + t];
                     vr[u][t] = vnew[lane * EPL + t];
                 }
+            } else if (i0 + u < nk) {
+                const float *slot = ring + (size_t)((i0 + u) % R) * 2 * HD;
+                load_head<EPL>(slot, kr[u]);
+                load_head<EPL>(slot + HD, vr[u]);
+            } else {
+#pragma unroll
+                for (int t = 0; t < EPL; ++t) kr[u][t] = vr[u][t] = 0.f;  // past the split: scored -inf
             }
 #pragma unroll
             for (int g = 0; g < G; ++g) {
@@ -254,14 +267,8 @@ __global__ void __launch_bounds__(kAttnThreads)
             l[g] = __fadd_rn(__fmul_rn(l[g], c), ps);
             m[g] = mn;
         }
-#pragma unroll
-        for (int u = 0; u < PF; ++u)
-#pragma unroll
-            for (int t = 0; t < EPL; ++t) {
-                kr[u][t] = kn[u][t];
-                vr[u][t] = vn[u][t];
-            }
     }
+    cp_async_wait<0>();  // only empty groups can be left: nothing in flight past this point
 #pragma unroll
     for (int g = 0; g < G; ++g) {
         if (g >= G) break;
@@ -364,7 +371,19 @@ cudaError_t pyxis::launch_attention_step(const pyxis_model_config &c, int splits
                                attention_step_kernel<2, 4>};
     const int G = c.n_q_heads / c.n_kv_heads;
     const Kern kern = (c.head_dim == 128 ? k128 : k64)[G - 1];
-    return launch_kernel(kern, dim3(splits, c.n_kv_heads, n_seq), dim3(kAttnThreads), 0, st, qkv, q_norm, k_norm,
+    const size_t ring = c.head_dim == 128 ? attn_ring_bytes<4>() : attn_ring_bytes<2>();
+    static const bool attr = [&] {
+        bool ok = true;
+        for (int g = 0; g < 4; ++g) {
+            ok &= cudaFuncSetAttribute(k128[g], cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)attn_ring_bytes<4>()) == cudaSuccess;
+            ok &= cudaFuncSetAttribute(k64[g], cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)attn_ring_bytes<2>()) == cudaSuccess;
+        }
+        return ok;
+    }();
+    if (!attr) return cudaErrorInvalidConfiguration;
+    return launch_kernel(kern, dim3(splits, c.n_kv_heads, n_seq), dim3(kAttnThreads), ring, st, qkv, q_norm, k_norm,
                          rope_cos, rope_sin, d_pos, c.n_q_heads, c.n_kv_heads, c.rms_eps, kc, vc, part, tickets, out,
                          (long long)qkv_stride, (long long)cache_stride, (long long)out_stride);
 }

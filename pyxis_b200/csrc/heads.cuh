@@ -18,6 +18,20 @@ PYXIS_DEVINL void load_head(const float *p, float (&v)[EPL]) {
     }
 }
 
+// This lane's EPL floats of a head row, global -> shared without registers (cp.async: 16 bytes
+// bypassing L1, or 8 bytes through it for EPL = 2); complete after cp_async_wait<n>().
+template <int EPL>
+PYXIS_DEVINL void cp_async_head(float *dst_smem, const float *src) {
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst_smem);
+    if constexpr (EPL == 4)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+    else
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(d), "l"(src) : "memory");
+}
+PYXIS_DEVINL void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+PYXIS_DEVINL void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 // QK RMSNorm (optional) and RoPE of one head held across a warp.
 template <int EPL>
 PYXIS_DEVINL void norm_rope(float (&v)[EPL], const float *nw, const float *rcos, const float *rsin, int pos,
