@@ -379,6 +379,9 @@ cudaError_t pyxis::launch_attention_step(const pyxis_model_config &c, int splits
                                        (int)attn_ring_bytes<4>()) == cudaSuccess;
             ok &= cudaFuncSetAttribute(k64[g], cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)attn_ring_bytes<2>()) == cudaSuccess;
+            // all of the SM's L1 as shared memory: three CTAs' rings (~76 KB each) fit only then
+            ok &= cudaFuncSetAttribute(k128[g], cudaFuncAttributePreferredSharedMemoryCarveout, 100) == cudaSuccess;
+            ok &= cudaFuncSetAttribute(k64[g], cudaFuncAttributePreferredSharedMemoryCarveout, 100) == cudaSuccess;
         }
         return ok;
     }();

@@ -329,6 +329,11 @@ struct BatchState {
 
 namespace {
 
+// Keys per decode-attention CTA of a batched step: fewer, longer splits amortise each CTA's fixed
+// work (q/k norm + RoPE, the fence and ticket of the split combine) now that its warps stream
+// keys through cp.async rings.
+constexpr int kKeysPerSplit = 768;
+
 int batch_fail(int code, const char *msg) { return record_error(code, msg); }
 
 int kv_dim_of(const pyxis_model_config &c) { return c.n_kv_heads * c.head_dim; }
@@ -356,10 +361,9 @@ int ensure_state(pyxis_cuda_model *m, int n_seq, int n_prompt, int n_new) {
     b->chunk = std::max(1, std::min(n_seq, 16384 / n_prompt));
     b->cache_stride = (size_t)c.n_layers * c.max_seq * kvd;
     const int G = c.n_q_heads / c.n_kv_heads;
-    // attention key splits: at least two CTAs per SM, and at most 256 keys per CTA (a CTA's warps
-    // keep only 4 keys' rows in flight each, so long contexts need many CTAs to fill HBM)
+    // attention key splits: at least two CTAs per SM, and at most kKeysPerSplit keys per CTA
     const int want = std::max((2 * m->ctx->num_sms + c.n_kv_heads * n_seq - 1) / (c.n_kv_heads * n_seq),
-                              (c.max_seq + 255) / 256);
+                              (c.max_seq + kKeysPerSplit - 1) / kKeysPerSplit);
     b->splits = std::max(1, std::min({want, (c.max_seq + 15) / 16, 64}));
     const size_t rows = (size_t)b->chunk * n_prompt;
     const size_t kmax = std::max({H, qd, ffn});
