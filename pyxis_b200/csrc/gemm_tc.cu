@@ -640,9 +640,14 @@ int gcd_int(int a, int b) {
     return a;
 }
 
-// Split-K slices for a grid of `tiles` output tiles: enough to give every SM a CTA, >= 4 K-blocks
-// (256 of K) per slice, slices aligned to the fold periods and the scale groups.
+// Split-K slices when the output tiles do not fill the SMs: the split that minimises
+// waves x (a CTA's fixed cost + its K-blocks), in K-block units -- a CTA's start (ring fill, scale
+// scan) and epilogue tail cost about kFixedKb K-blocks, the fixed-order reduction of the partials
+// about kReduceKb.  Slices are aligned to the fold periods and the scale groups, >= 4 K-blocks
+// (256 of K).  Splitting until every SM has a CTA can double the waves (gate|up at 64 tokens:
+// 96 tiles x 2 = 192 CTAs on 148 SMs), which this avoids.
 void plan_splitk(const QMatrix &w, size_t M, int num_sms, int &ks, int &kb_per) {
+    constexpr int kFixedKb = 10, kReduceKb = 5;
     const int kb_all = (int)(w.K / BK);
     const long long tiles = ((long long)w.N + BM - 1) / BM * (((long long)M + BN - 1) / BN);
     int unit = 16 * fold_steps(w);          // K of a fold period
@@ -652,12 +657,20 @@ void plan_splitk(const QMatrix &w, size_t M, int num_sms, int &ks, int &kb_per) 
     kb_per = kb_all;
     if (tiles >= num_sms) return;
     const int max_split = kb_all / std::max(gran, 4);
-    const int want = (int)((num_sms + tiles - 1) / tiles);
-    const int k = std::min(max_split, want);
-    if (k <= 1) return;
-    kb_per = (kb_all + k - 1) / k;
-    kb_per = (kb_per + gran - 1) / gran * gran;
-    ks = (kb_all + kb_per - 1) / kb_per;
+    long long best = (long long)((tiles + num_sms - 1) / num_sms) * (kFixedKb + kb_all);
+    for (int k = 2; k <= max_split; ++k) {
+        int per = (kb_all + k - 1) / k;
+        per = (per + gran - 1) / gran * gran;
+        const int n = (kb_all + per - 1) / per;
+        if (n < 2) continue;
+        const long long waves = (tiles * n + num_sms - 1) / num_sms;
+        const long long cost = waves * (kFixedKb + per) + kReduceKb;
+        if (cost < best) {
+            best = cost;
+            ks = n;
+            kb_per = per;
+        }
+    }
 }
 }  // namespace
 
