@@ -198,11 +198,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             const long long sb = sc.begin(blockIdx.x), se = sc.begin(blockIdx.x + 1);
             const int nseg = sc.num_segments(sb, se);
             bool ok = true;
+            // ring slot s of stage g and its round ph = g / stages, tile and K-block of the stage:
+            // all advanced by increments (a division per stage was most of this thread's work)
+            int s = 0, ph = 0;
             for (int i = 0; i < nseg && ok; ++i) {
                 long long s0, s1;
                 sc.segment(sb, se, i, s0, s1);
+                int tile = (int)(s0 / p.num_kb), kb = (int)(s0 - (long long)tile * p.num_kb);
                 for (long long st = s0; st < s1; ++st, ++g) {
-                    const int s = g % p.stages;
                     if (g == x_gate) {  // the stages x borrowed: wait until the digits are built
                         if (!x_issued) {
                             pdl_wait();
@@ -213,14 +216,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                             break;
                         }
                     }
-                    if (g >= p.stages && !tc::mbar_wait_bounded(&empty[s], ((g / p.stages) - 1) & 1, abort_flag, p.err,
+                    if (g >= p.stages && !tc::mbar_wait_bounded(&empty[s], (uint32_t)((ph - 1) & 1), abort_flag, p.err,
                                                                 kErrProd, kTimeoutNs)) {
                         ok = false;
                         break;
                     }
-                    const int tile = (int)(st / p.num_kb), kb = (int)(st % p.num_kb);
                     tc::mbar_arrive_expect_tx(&full[s], kStageBytes);
                     tc::tma_load_2d(ring + (size_t)s * kStageBytes, &tm_w, kb * TKB, tile * TM, &full[s]);
+                    if (++kb == p.num_kb) {
+                        kb = 0;
+                        ++tile;
+                    }
+                    if (++s == p.stages) {
+                        s = 0;
+                        ++ph;
+                    }
                 }
             }
             if (!x_issued && ok) {  // fewer stages than the x_gate: x still has to come
@@ -349,7 +359,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             // ---------------------------------------------------------------- MMA issuer
             if (lane == 0) {
                 const uint32_t idesc = idesc_i8(TM, p.NB);
-                int g = 0, li = 0;
+                // descriptors advance by constant offsets (start address in 16-byte units), the ring
+                // slot and its phase by increments: no per-stage division or descriptor rebuild
+                const uint64_t ring_d = tc::desc_sw128(tc::smem_u32(ring)), xd_d = tc::desc_sw128(tc::smem_u32(xd));
+                const uint32_t stage_step = kStageBytes >> 4, kb_step = (uint32_t)(p.NB * TKB) >> 4;
+                int li = 0, s = 0, ph = 0;
                 bool ok = true;
                 const int nseg = sc.num_segments(my_sb, my_se);
                 for (; li < nseg && ok; ++li) {
@@ -363,19 +377,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     tc::tc_fence_after();
                     const uint32_t d = tmem_base + (uint32_t)(buf * kAccPerBuf * p.NB);
-                    for (int kb = kb0; kb < kb0 + nk; ++kb, ++g) {
-                        const int s = g % p.stages;
-                        ok = tc::mbar_wait_bounded(&full[s], (g / p.stages) & 1, abort_flag, p.err, kErrMma, kTimeoutNs);
+                    for (int kb = kb0; kb < kb0 + nk; ++kb) {
+                        ok = tc::mbar_wait_bounded(&full[s], (uint32_t)(ph & 1), abort_flag, p.err, kErrMma, kTimeoutNs);
                         if (!ok) break;
                         tc::tc_fence_after();
-                        const uint64_t a0 = tc::desc_sw128(tc::smem_u32(ring + (size_t)s * kStageBytes));
-                        const uint64_t b0 = tc::desc_sw128(tc::smem_u32(xd + (size_t)kb * (p.NB * TKB)));
+                        const uint64_t a0 = ring_d + (uint64_t)(s * stage_step);
+                        const uint64_t b0 = xd_d + (uint64_t)(kb * kb_step);
                         const uint32_t dset = d + (uint32_t)(((kb - kb0) & 1) * kAccPerStage * p.NB);
 #pragma unroll
                         for (int q = 0; q < kAccPerStage; ++q)
                             mma_i8(dset + (uint32_t)(q * p.NB), a0 + (uint64_t)(2 * q), b0 + (uint64_t)(2 * q), idesc,
                                    kb - kb0 >= 2 ? 1u : 0u);
                         tc::mma_commit(&empty[s]);
+                        if (++s == p.stages) {
+                            s = 0;
+                            ++ph;
+                        }
                     }
                     if (ok) tc::mma_commit(&tfull[buf]);
                 }
