@@ -43,6 +43,7 @@ struct BatchParams {
     int chunks;            // 16-byte chunks per row
     int blocks_per_row;    // scale blocks per row (chunk mode)
     int chunks_per_block;  // chunks per scale block (chunk mode)
+    int cpb_shift;         // log2(chunks_per_block) when it is a power of two, else -1
     int slices;            // warps per row group
     int groups_cta;        // row groups per CTA item
     int items;             // ceil(row groups / groups_cta)
@@ -302,12 +303,14 @@ __global__ void __launch_bounds__(max_warps(B) * 32, 1)
     uint4 wn[kRows];
     float sn[kRows];
     auto load = [&](int row0, int c) {
+        // the chunk's scale block (a shift for the usual power-of-two groups: a division per chunk
+        // was a visible share of the lanes' instructions)
+        const int blk = SMODE == kScaleChunk ? (p.cpb_shift >= 0 ? c >> p.cpb_shift : c / p.chunks_per_block) : 0;
 #pragma unroll
         for (int r = 0; r < kRows; ++r) {
             const int row = min(row0 + r, p.N - 1);
             wn[r] = ld_stream_v4(p.W + (size_t)row * p.row_bytes + (size_t)c * 16);
-            sn[r] = SMODE == kScaleChunk ? ld_nc_f32(p.S + (size_t)row * p.blocks_per_row + c / p.chunks_per_block)
-                                         : 1.f;
+            sn[r] = SMODE == kScaleChunk ? ld_nc_f32(p.S + (size_t)row * p.blocks_per_row + blk) : 1.f;
         }
     };
     auto row0_of = [&](int item) { return (item * p.groups_cta + gi) * kRows; };
@@ -474,6 +477,7 @@ BatchParams make_params(const QMatrix &w, const Shape &sh, float *Y, size_t ldy,
     p.chunks = (int)(w.K / epc);
     p.blocks_per_row = chunk_mode ? (int)(w.K / w.block_size) : 1;
     p.chunks_per_block = chunk_mode ? (int)(w.block_size / epc) : 1;
+    p.cpb_shift = (p.chunks_per_block & (p.chunks_per_block - 1)) == 0 ? __builtin_ctz((unsigned)p.chunks_per_block) : -1;
     p.slices = sh.slices;
     p.groups_cta = sh.groups_cta;
     p.items = sh.items;
