@@ -8,8 +8,9 @@
 //      into fp16 hi + lo (x*2^e = hi + lo + O(2^-22 |x*2^e|)): 22 significant bits, as accurate
 //      against the reference's f32 sums as exact arithmetic (bf16 hi/lo keeps only 16).
 //   2. the tile kernel, one CTA per 128 weight rows x 128 tokens (x gridDim.z K slices when
-//      there are fewer tiles than SMs), warp-specialised:
-//        warp 0      TMA producer: raw int8/int4 codes + fp16 X hi/lo tiles into a 3-stage ring
+//      there are fewer tiles than SMs and splitting saves waves), warp-specialised:
+//        warp 0      TMA producer: raw int8/int4 codes + fp16 X hi/lo tiles into a ring of 4
+//                    stages (one scale per row) or 3 (group scales, whose A_lo tiles take room)
 //        warp 1      TMEM owner and MMA issuer: tcgen05.mma kind::f16, M=128, K=16; the token
 //                    tiles hi and lo sit back to back, so one N=256 MMA per K-step gives W x_hi in
 //                    accumulator columns [0,128) and W x_lo in [128,256) (N=64 pairs for tiles of
@@ -28,7 +29,8 @@
 //      floor-relative metric for K = 2048 in one accumulator: 256 accumulations); a period is at
 //      most 16 K-steps (16 or 32 accumulations per column).
 //      The MMA rate is bounded by the issuing thread's own instruction stream (a few scalar
-//      instructions per MMA cost as much as the MMA), so that loop carries no per-MMA bookkeeping.
+//      instructions per MMA cost as much as the MMA), so that loop is unrolled over the ring and
+//      the fold period: slots, phases, buffers and commit points are compile-time.
 //   Weight codes are exact in fp16 and the token power of two is exact, so the only rounding
 //   besides the fp32 accumulation is the lo terms' 2^-22 (and, with group scales, q * s in f32).
 //
