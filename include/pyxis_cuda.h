@@ -133,10 +133,13 @@ int pyxis_cuda_matmul_batch(pyxis_cuda_ctx *ctx, const float *input, size_t M,
                             float *out);
 
 /* Device-pointer form, asynchronous on `stream` (NULL: the context's stream).  X [M, in] f32
- * with row stride ldx (elements), Y [M, out] f32 with row stride ldy.  M = 1..8 run the decode
- * GEMV kernels; larger M runs the tensor-core prefill GEMM, which needs `workspace` of
- * pyxis_cuda_matmul_workspace_size() bytes (device memory, 256-byte aligned).  A NULL workspace
- * makes the context allocate and keep one (not allowed while the stream is being captured). */
+ * with row stride ldx (elements), Y [M, out] f32 with row stride ldy.  M < 16 runs the decode
+ * GEMV kernels, 8 rows per launch; M >= 16 with int8/int4 weights runs the tensor-core prefill
+ * GEMM, which needs `workspace` of pyxis_cuda_matmul_workspace_size() bytes (device memory,
+ * 256-byte aligned).  A NULL workspace makes the context allocate and keep one (not allowed while
+ * the stream is being captured); the context's workspace also holds split-K partial sums, which
+ * a caller workspace of that size has no room for, so GEMMs with fewer output tiles than SMs
+ * (e.g. 2048 output rows at M = 512) run faster on it. */
 int pyxis_cuda_matmul_dev(pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, const float *X,
                           size_t M, size_t ldx, size_t out_features, size_t in_features,
                           float *Y, size_t ldy, void *workspace, size_t workspace_bytes,
