@@ -1,0 +1,66 @@
+"""The bench's JSON line is a contract with whoever runs it: one line, fixed keys, the metric
+named the way the benchmark names it.  These checks run on the CPU: the reference arm (the
+oracle port of the reference's Rayon matmul) needs no GPU, and the byte counts behind every
+GB/s and roofline figure are plain arithmetic."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+import bench  # noqa: E402
+
+
+def _run_reference(env_extra):
+    env = dict(os.environ, **env_extra)
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
+                          "--warmup", "0"], capture_output=True, text=True, env=env, timeout=600, cwd=ROOT)
+    assert out.returncode == 0, out.stderr[-2000:]
+    return [l for l in out.stdout.splitlines() if l.strip()]
+
+
+def test_reference_arm_prints_one_contract_line():
+    lines = _run_reference({"WORLD_SIZE": "1", "RANK": "0"})
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling",
+                "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert key in d, key
+    assert d["impl"] == "reference" and d["metric"] == bench.METRIC and d["unit"] == "GB/s"
+    assert d["n_gpus"] == 1 and d["steps"] == 1 and d["warmup"] == 0 and d["higher_is_better"] is True
+    assert d["value"] > 0 and d["ms_per_step"] > 0 and d["vs_baseline"] is None
+    assert d["config"]["workload"] == bench.WORKLOAD
+    cb = d["cpu_baseline"]
+    assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
+    e = d["e2e"]
+    assert e["value"] == d["value"] and e["unit"] == "GB/s" and e["h2d_bytes_per_step"] == 0 and e["d2h_bytes_per_step"] == 0
+
+
+def test_reference_arm_other_ranks_print_nothing():
+    """Under torchrun only rank 0 runs the CPU sweep and prints; the other ranks exit 0 quietly."""
+    assert _run_reference({"WORLD_SIZE": "2", "RANK": "1"}) == []
+
+
+def test_metric_matches_the_benchmark_definition():
+    path = os.path.join(ROOT, "BASELINE.json")
+    if not os.path.exists(path):
+        pytest.skip("no benchmark definition file in this checkout")
+    with open(path) as f:
+        assert json.load(f)["metric"] == bench.METRIC
+
+
+def test_algorithmic_bytes():
+    """codes + scales + x + y per GEMV: the numbers the GB/s values and the roofline divide by."""
+    # int8 per-row gate_proj 6144 x 2048 at batch 1: N K + 4 N + 4 K + 4 N
+    assert bench.gemv_bytes("int8", 6144, 2048, 2048, 1) == 12_640_256
+    # the lm_head launch the roofline reports: 151936 x 2048 int8 per row, batch 1
+    assert bench.gemv_bytes("int8", 151936, 2048, 2048, 1) == 312_388_608
+    # int4 group 32: N K / 2 + 4 N K / 32 + 4 B (K + N)
+    assert bench.gemv_bytes("int4", 2048, 2048, 32, 8) == 2048 * 2048 // 2 + 4 * 2048 * 2048 // 32 + 4 * 8 * 4096
+    assert bench.step_bytes() == sum(bench.gemv_bytes(qt, N, K, bs, B) for B in bench.BATCHES
+                                     for (_, qt, N, K, bs) in bench.SWEEP)
+    assert 0.6e9 < bench.step_bytes() < 0.8e9  # "0.68 GB of packed weights" per step
