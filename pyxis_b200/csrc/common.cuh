@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include <utility>
 
 #define PYXIS_DEVINL __device__ __forceinline__
@@ -43,6 +45,23 @@ PYXIS_DEVINL float byte_to_magic(uint32_t word, int sel) {
 }
 
 PYXIS_DEVINL float2 f2(float a, float b) { return make_float2(a, b); }
+
+// Runs `setup` (cudaFuncSetAttribute calls) once per device and returns its status.  A kernel's
+// attributes belong to each device's copy of the module, so a process that drives several GPUs
+// (one context per device) must set them on every device it launches on.  `done` is the call
+// site's mask of devices already set up; a failed setup is retried on the next call.
+template <typename F>
+inline cudaError_t once_per_device(std::atomic<uint64_t> &done, F &&setup) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return setup();
+    const uint64_t bit = 1ull << dev;
+    if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    e = setup();
+    if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
+    return e;
+}
 
 PYXIS_DEVINL float2 fadd2(float2 a, float2 b) { return __fadd2_rn(a, b); }
 PYXIS_DEVINL float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }

@@ -372,7 +372,8 @@ cudaError_t pyxis::launch_attention_step(const pyxis_model_config &c, int splits
     const int G = c.n_q_heads / c.n_kv_heads;
     const Kern kern = (c.head_dim == 128 ? k128 : k64)[G - 1];
     const size_t ring = c.head_dim == 128 ? attn_ring_bytes<4>() : attn_ring_bytes<2>();
-    static const bool attr = [&] {
+    static std::atomic<uint64_t> attr_done{0};
+    const cudaError_t attr = once_per_device(attr_done, [&] {
         bool ok = true;
         for (int g = 0; g < 4; ++g) {
             ok &= cudaFuncSetAttribute(k128[g], cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -383,9 +384,9 @@ cudaError_t pyxis::launch_attention_step(const pyxis_model_config &c, int splits
             ok &= cudaFuncSetAttribute(k128[g], cudaFuncAttributePreferredSharedMemoryCarveout, 100) == cudaSuccess;
             ok &= cudaFuncSetAttribute(k64[g], cudaFuncAttributePreferredSharedMemoryCarveout, 100) == cudaSuccess;
         }
-        return ok;
-    }();
-    if (!attr) return cudaErrorInvalidConfiguration;
+        return ok ? cudaSuccess : cudaErrorInvalidConfiguration;
+    });
+    if (attr != cudaSuccess) return attr;
     return launch_kernel(kern, dim3(splits, c.n_kv_heads, n_seq), dim3(kAttnThreads), ring, st, qkv, q_norm, k_norm,
                          rope_cos, rope_sin, d_pos, c.n_q_heads, c.n_kv_heads, c.rms_eps, kc, vc, part, tickets, out,
                          (long long)qkv_stride, (long long)cache_stride, (long long)out_stride);

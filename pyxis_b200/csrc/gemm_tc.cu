@@ -738,12 +738,16 @@ cudaError_t launch_gemm_tc(const QMatrix &w, const float *X, size_t M, size_t ld
     p.kb_per_split = kb_per;
     using LG = Smem<kTilesGrouped, kStagesGrouped, true>;
     using LR = Smem<kStagesRow, kStagesRow, false>;
-    static const bool attr =
-        cudaFuncSetAttribute(gemm_tc_kernel<kTilesGrouped, kStagesGrouped, true>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, LG::bytes) == cudaSuccess &&
-        cudaFuncSetAttribute(gemm_tc_kernel<kStagesRow, kStagesRow, false>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, LR::bytes) == cudaSuccess;
-    if (!attr) return cudaErrorInvalidConfiguration;
+    static std::atomic<uint64_t> attr_done{0};
+    const cudaError_t attr = once_per_device(attr_done, [] {
+        cudaError_t a = cudaFuncSetAttribute(gemm_tc_kernel<kTilesGrouped, kStagesGrouped, true>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, LG::bytes);
+        if (a == cudaSuccess)
+            a = cudaFuncSetAttribute(gemm_tc_kernel<kStagesRow, kStagesRow, false>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, LR::bytes);
+        return a;
+    });
+    if (attr != cudaSuccess) return attr;
     dim3 grid((unsigned)((N + BM - 1) / BM), (unsigned)((M + BN - 1) / BN), (unsigned)ks);
     if (p.grouped)
         gemm_tc_kernel<kTilesGrouped, kStagesGrouped, true><<<grid, kThreads, LG::bytes, st>>>(tw, th, tl, p);

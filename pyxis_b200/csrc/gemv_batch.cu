@@ -434,8 +434,9 @@ Shape shape_for(const QMatrix &w, size_t B, int num_sms) {
 template <int QT, int B, int SMODE, int PRO = kProNone>
 cudaError_t run(const CUtensorMap &tm, const BatchParams &p, const Shape &sh, int num_sms, cudaStream_t st) {
     auto kern = gemv_batch_kernel<QT, B, SMODE, PRO>;
-    static const cudaError_t attr =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
+    static std::atomic<uint64_t> attr_done{0};
+    const cudaError_t attr = once_per_device(
+        attr_done, [&] { return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem); });
     if (attr != cudaSuccess) return attr;
     const int threads = sh.slices * sh.groups_cta * 32;
     const int grid = std::max(1, std::min(sh.items, num_sms));

@@ -574,9 +574,11 @@ cudaError_t launch_gemv_tc(const QMatrix &w, const float *X, size_t B, size_t ld
         p.tickets = reinterpret_cast<unsigned *>(sb + (size_t)grid * TM * 32 * sizeof(int));
     }
     p.err = err;
-    static const bool attr =
-        cudaFuncSetAttribute(gemv_tc_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTotal) == cudaSuccess;
-    if (!attr) return cudaErrorInvalidConfiguration;
+    static std::atomic<uint64_t> attr_done{0};
+    const cudaError_t attr = once_per_device(attr_done, [] {
+        return cudaFuncSetAttribute(gemv_tc_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTotal);
+    });
+    if (attr != cudaSuccess) return attr;
     return launch_kernel(gemv_tc_i8_kernel, dim3(grid), dim3(kThreads), kSmemTotal, st, tm, p);
 }
 
