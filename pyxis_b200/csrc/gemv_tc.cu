@@ -254,8 +254,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         // K-blocks this CTA multiplies: a contiguous run (mod num_kb) unless it spans a whole tile
         const int need_lo = (int)(my_sb % p.num_kb);
         const long long need_n = my_se - my_sb;
-        auto needed = [&](int kb) { return need_n >= p.num_kb || ((kb - need_lo + p.num_kb) % p.num_kb) < need_n; };
+        auto needed = [&](int kb) {  // kb, need_lo in [0, num_kb): a wrap-around offset without a modulo
+            int d = kb - need_lo;
+            if (d < 0) d += p.num_kb;
+            return need_n >= p.num_kb || d < need_n;
+        };
         const int kq = p.K / 4;  // float4 quads per token
+        const int kq_shift = (kq & (kq - 1)) == 0 ? __ffs(kq) - 1 : -1;  // token of a quad index by shift
         const float4 *xs4 = reinterpret_cast<const float4 *>(xs);
         const bool x_ok = tc::mbar_wait_bounded(xfull, 0, abort_flag, p.err, kErrMma, kTimeoutNs);
         // x arrived after the producer's griddepcontrol.wait, so this returns at once; it keeps the
@@ -323,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int u = 0; u < 8; ++u) {
                 const int idx = base + u * nbt;
                 if (idx >= total) break;
-                const int b = idx / kq, k = (idx - b * kq) * 4;
+                const int b = kq_shift >= 0 ? idx >> kq_shift : idx / kq, k = (idx - b * kq) * 4;
                 if (!needed(k / TKB)) continue;
                 // x 2^(27-E) exactly, as two power-of-two products (27 - E lies in [-101, 175])
                 const int sh = 27 - xexp[b];
