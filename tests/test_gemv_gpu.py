@@ -123,9 +123,11 @@ def test_argmax_rules():
     (4096, 4096, 4), (129, 1024, 8), (151936, 2048, 8),
 ])
 def test_int8_row_scale_tensor_core_gemv(N, K, B):
-    """int8 with one scale per row at batch 1-8 runs tcgen05 kind::i8 with x as int8 digits
-    (split-K with exact int32 atomics when there are fewer tiles than SMs)."""
+    """int8 with one scale per row at batch 1-8.  From 32768 output rows (the lm_head) it runs
+    tcgen05 kind::i8 with x as int8 digits and stream-K (tiles shared by two CTAs added with exact
+    int32 atomics); below that the CUDA-core batch kernel, which finishes first at those sizes."""
     w, od, os_ = make("int8", N, K, K, seed=N + K + B)
+    assert px.matmul_kernel_name(w, B, N, K) == ("gemv_tc_i8_kernel" if N >= 32768 else "gemv_batch_kernel")
     X = px.synth_normal_f32(B * 31 + 7, B * K, 1.0).reshape(B, K)
     X[0, :5] = [0.0, -0.0, 1e-30, -3e4, 2.5]
     for rep in range(2):  # the split-K scratch must be left clean for the next launch
