@@ -85,7 +85,9 @@ int pyxis_cuda_synchronize(pyxis_cuda_ctx *ctx);
  * src/weights.rs:94-118) or Weights::quantize_int4 (qtype INT4, :120-151) applied to the f32
  * values of `src` (num_elements of src_dtype; host memory when src_on_device == 0, else a device
  * pointer on the context's device).  block_size > 0, any value (the model's policy is
- * in_features for int8 and 32 for int4, src/model.rs:20,520-530).  On success *w owns HBM. */
+ * in_features for int8 and 32 for int4, src/model.rs:20,520-530).  On success *w owns HBM.
+ * The call runs on the context's stream, which does not wait for other streams: a device
+ * source must be complete when the call is made.  It returns after the packing has finished. */
 int pyxis_cuda_quantize(pyxis_cuda_ctx *ctx, const void *src, int src_dtype, int src_on_device,
                         size_t num_elements, size_t block_size, int qtype,
                         pyxis_cuda_weights **w);
@@ -102,7 +104,8 @@ int pyxis_cuda_weights_upload(pyxis_cuda_ctx *ctx, int qtype, const void *data,
  * ceil(num_elements/32) blocks of 34 bytes (f16 scale, little-endian, then 32 int8), in host
  * memory (blocks_on_device == 0) or device memory of the context's device.  The result is INT8
  * weights with block_size 32: the codes truncated to num_elements and each scale widened to f32
- * exactly as half 2.7.1's f16::to_f32 does (a NaN keeps its payload and gets the quiet bit). */
+ * exactly as half 2.7.1's f16::to_f32 does (a NaN keeps its payload and gets the quiet bit).
+ * As for pyxis_cuda_quantize, device blocks must be complete when the call is made. */
 int pyxis_cuda_weights_upload_q8_0(pyxis_cuda_ctx *ctx, const void *blocks, int blocks_on_device,
                                    size_t num_elements, pyxis_cuda_weights **w);
 

@@ -129,6 +129,9 @@ class Weights:
                 raise PyxisError(_native.PYXIS_EINVAL,
                                  f"source tensor on {values.device}, weights requested on cuda:{device}")
             t = values.contiguous()
+            # The library reads the source on its own non-blocking stream: torch's writes of the
+            # tensor (and of the contiguous copy) must be complete first.
+            torch.cuda.synchronize(device)
             if t.dtype == torch.float32:
                 dt = DTYPE_F32
             elif t.dtype == torch.bfloat16:
@@ -189,8 +192,12 @@ class Weights:
             is_dev = False
         nb = (num_elements + 31) // 32
         if is_dev:
+            if (blocks.device.index or 0) != device:
+                raise PyxisError(_native.PYXIS_EINVAL,
+                                 f"q8_0 tensor on {blocks.device}, weights requested on cuda:{device}")
             if blocks.numel() * blocks.element_size() < nb * 34:
                 raise PyxisError(_native.PYXIS_EINVAL, "q8_0 tensor shorter than ceil(n/32) * 34 bytes")
+            torch.cuda.synchronize(device)  # the upload reads it on the library's own stream
             check(_native.lib().pyxis_cuda_weights_upload_q8_0(ctx.handle, C.c_void_p(blocks.data_ptr()), 1,
                                                                num_elements, C.byref(h)))
             return Weights(h, ctx)

@@ -152,3 +152,23 @@ def test_dense_shape_assert():
     w = px.Weights.from_dense(np.zeros(64, np.float32))
     with pytest.raises(px.PyxisError):
         px.matmul(np.zeros(8, np.float32), w, 9, 8)
+
+
+def test_q8_0_device_blocks_written_just_before_the_call():
+    """Device blocks that torch's stream is still copying when the upload is called (the copy is
+    queued behind other work) are unpacked from their final bytes."""
+    rng = np.random.default_rng(9)
+    n = 2048 * 2048
+    blob = _q8_0_blob(rng, n)
+    staged = torch.from_numpy(np.frombuffer(blob, np.uint8).copy()).cuda()
+    dev = torch.zeros_like(staged)
+    torch.cuda.synchronize()
+    a = torch.full((4096, 4096), 1e-3, device="cuda")
+    for _ in range(8):  # tens of milliseconds of f32 GEMMs ahead of the copy
+        a = a @ a
+    dev.copy_(staged)
+    w = px.Weights.from_q8_0(dev, n)
+    d, s = w.download()
+    od, os_ = oracle.q8_0_to_int8(blob, n)
+    assert np.array_equal(d.view(np.uint8), od.view(np.uint8))
+    assert np.array_equal(s.view(np.uint32), os_.view(np.uint32))

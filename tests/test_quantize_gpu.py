@@ -123,3 +123,30 @@ def test_device_source_must_be_this_devices_memory():
                                            32, _native.QTYPE_INT8, C.byref(h))
     assert rc == _native.PYXIS_EINVAL
     assert b"device" in _native.lib().pyxis_cuda_last_error()
+
+
+def _queue_torch_work(torch):
+    """Tens of milliseconds of f32 GEMMs queued on torch's current stream."""
+    a = torch.full((4096, 4096), 1e-3, device="cuda")
+    for _ in range(8):
+        a = a @ a
+    return a
+
+
+def test_device_source_written_just_before_the_call():
+    """The library packs on its own non-blocking stream.  A source that torch's stream is still
+    writing when the call is made (a copy queued behind other work, read through a strided view
+    whose contiguous copy is queued too) must be packed from its final values."""
+    import torch
+    N, K = 1024, 2048
+    bits = px.synth_normal_bf16(13, 2 * N * K, 0.02)
+    vals = oracle.bf16_to_f32(bits).reshape(2 * N, K)
+    staged = torch.from_numpy(vals).cuda()
+    src = torch.zeros_like(staged)
+    torch.cuda.synchronize()
+    _queue_torch_work(torch)
+    src.copy_(staged)
+    w = px.Weights.quantize_int4(src[::2], 32)
+    d, s = w.download()
+    od, os_ = oracle.quantize_int4(np.ascontiguousarray(vals[::2]).reshape(-1), 32)
+    assert np.array_equal(d, od) and np.array_equal(_bits(s), _bits(os_))
