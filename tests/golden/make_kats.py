@@ -68,6 +68,49 @@ KATS = [
     dict(name="matmul_large_output", src="src/matmul.rs:358",
          literal="let weight = Weights::F32(vec![1.0; 1000 * 100]);",
          op="matmul_f32_ones", out_features=1000, in_features=100, expect_all=100.0),
+    dict(name="matmul_identity_matrix", src="src/matmul.rs:338",
+         literal="let weight = Weights::F32(vec![1.0, 0.0, 0.0, 0.0, 1.0, 0.0, 0.0, 0.0, 1.0]);",
+         also=[["src/matmul.rs:337", "let input = vec![1.0, 2.0, 3.0];"]],
+         op="matmul_f32", input=[1.0, 2.0, 3.0], weight=[1.0, 0.0, 0.0, 0.0, 1.0, 0.0, 0.0, 0.0, 1.0],
+         out_features=3, in_features=3, expect=[1.0, 2.0, 3.0], tol=1e-5),
+    dict(name="matmul_known_values", src="src/matmul.rs:348",
+         literal="let weight = Weights::F32(vec![1.0, 0.0, 0.0, 0.0, 1.0, 0.0]);",
+         also=[["src/matmul.rs:347", "let input = vec![1.0, 2.0, 3.0];"]],
+         op="matmul_f32", input=[1.0, 2.0, 3.0], weight=[1.0, 0.0, 0.0, 0.0, 1.0, 0.0],
+         out_features=2, in_features=3, expect=[1.0, 2.0], tol=1e-5),
+    # dot_product (src/matmul.rs:127-147) is one output row of an F32 matmul
+    dict(name="dot_product_matches_scalar", src="src/matmul.rs:369", literal="let weight = vec![2.0, 3.0, 4.0, 5.0, 6.0];",
+         also=[["src/matmul.rs:368", "let input = vec![1.0, 2.0, 3.0, 4.0, 5.0];"]],
+         op="matmul_f32", input=[1.0, 2.0, 3.0, 4.0, 5.0], weight=[2.0, 3.0, 4.0, 5.0, 6.0],
+         out_features=1, in_features=5, expect=[70.0], tol=0.0),
+    dict(name="dot_product_large_aligned", src="src/matmul.rs:378", literal="let input = vec![1.0; 1024];",
+         op="matmul_f32", input=[1.0] * 1024, weight=[1.0] * 1024, out_features=1, in_features=1024,
+         expect=[1024.0], tol=0.0),
+    dict(name="dot_product_with_remainder", src="src/matmul.rs:389",
+         literal="let weight = vec![7.0, 6.0, 5.0, 4.0, 3.0, 2.0, 1.0];",
+         also=[["src/matmul.rs:388", "let input = vec![1.0, 2.0, 3.0, 4.0, 5.0, 6.0, 7.0];"]],
+         op="matmul_f32", input=[1.0, 2.0, 3.0, 4.0, 5.0, 6.0, 7.0], weight=[7.0, 6.0, 5.0, 4.0, 3.0, 2.0, 1.0],
+         out_features=1, in_features=7, expect=[84.0], tol=0.0),
+    # bf16 rows are the top 16 bits of the f32 values (`value.to_bits() >> 16`)
+    dict(name="dot_product_bf16_matches_f32", src="src/matmul.rs:399",
+         literal="let weight = vec![1.5, -0.25, 2.0, 0.125, -1.0];",
+         also=[["src/matmul.rs:398", "let input = vec![1.0, -2.0, 0.5, 4.0, 3.0];"]],
+         op="bf16_vs_f32", input=[1.0, -2.0, 0.5, 4.0, 3.0], weight=[1.5, -0.25, 2.0, 0.125, -1.0],
+         out_features=1, in_features=5, against="widened", tol=1e-5),
+    dict(name="matmul_with_bf16_weights", src="src/matmul.rs:449",
+         literal="let output = matmul(&input, &Weights::Bf16(weight_bf16), 2, 3);",
+         also=[["src/matmul.rs:443", "let weight_f32 = vec![1.5, -0.5, 2.0, 0.25, 3.0, -1.0];"]],
+         op="bf16_vs_f32", input=[1.0, 2.0, -1.0], weight=[1.5, -0.5, 2.0, 0.25, 3.0, -1.0],
+         out_features=2, in_features=3, against="f32", tol=1e-5),
+    # ---- src/weights.rs: Weights::len (:35-46) ---------------------------------------------------
+    dict(name="weights_len_f32", src="src/weights.rs:166", literal="let weights = Weights::F32(vec![0.0; 10]);",
+         op="weights_len", kind="f32", data_len=10, expect=10),
+    dict(name="weights_len_bf16", src="src/weights.rs:173", literal="let weights = Weights::Bf16(vec![0; 10]);",
+         op="weights_len", kind="bf16", data_len=10, expect=10),
+    dict(name="weights_len_int8", src="src/weights.rs:183", literal="block_size: 5,",
+         op="weights_len", kind="int8", data_len=10, n_scales=2, block_size=5, num_elements=10, expect=10),
+    dict(name="weights_len_int4", src="src/weights.rs:193", literal="data: vec![0; 5],",
+         op="weights_len", kind="int4", data_len=5, n_scales=1, block_size=32, num_elements=10, expect=10),
     # ---- src/model.rs (quantize_weights block policy) -----------------------------------------
     dict(name="quantize_weights_quantizes_f32_weights", src="src/model.rs:630",
          literal="Weights::F32(vec![1.0, -2.0, 0.0, 4.0]),",
@@ -102,6 +145,63 @@ KATS = [
          literal="OutputHead::new(vec![1.0, 0.0, 3.0, 0.0, 2.0, 0.0].into(), 3, 2);",
          op="greedy_f32", weight=[1.0, 0.0, 3.0, 0.0, 2.0, 0.0], vocab=3, hidden=2, hidden_state=[1.0, 1.0],
          expect=1),
+    dict(name="logits_with_identity_weight", src="src/output_head.rs:53",
+         literal="vec![1.0, 0.0, 0.0, 0.0, 1.0, 0.0, 0.0, 0.0, 1.0].into(),",
+         also=[["src/output_head.rs:58", "let logits = output_head.logits(&[1.0, 2.0, 3.0]);"]],
+         op="matmul_f32", input=[1.0, 2.0, 3.0], weight=[1.0, 0.0, 0.0, 0.0, 1.0, 0.0, 0.0, 0.0, 1.0],
+         out_features=3, in_features=3, expect=[1.0, 2.0, 3.0], tol=0.0),
+    dict(name="logits_returns_correct_length", src="src/output_head.rs:65",
+         literal="OutputHead::new(vec![0.0; 12].into(), 4, 3);",
+         op="matmul_f32", input=[1.0, 2.0, 3.0], weight=[0.0] * 12, out_features=4, in_features=3,
+         expect=[0.0] * 4, tol=0.0),
+    # ---- tests/metal_matmul.rs: the GPU backend's own parity tests ------------------------------
+    # Inputs are index formulas: x_i = f32(i) % xm / xd - xs and w_i = f32((i*wa + wb) % wm) / wd - ws,
+    # every operation in f32.  "expect" is the reference's CPU matmul ("matmul") or the test's
+    # sequential sum (cpu_matmul_f32, "sequential"), each within the test's tolerance.
+    dict(name="metal_matmul_identity", src="tests/metal_matmul.rs:61",
+         literal="let weight = vec![1.0, 0.0, 0.0, 0.0, 1.0, 0.0, 0.0, 0.0, 1.0];",
+         op="matmul_f32", input=[1.0, 2.0, 3.0], weight=[1.0, 0.0, 0.0, 0.0, 1.0, 0.0, 0.0, 0.0, 1.0],
+         out_features=3, in_features=3, expect=[1.0, 2.0, 3.0], tol=1e-4),
+    dict(name="metal_matmul_known_values", src="tests/metal_matmul.rs:74",
+         literal="let weight = vec![1.0, 0.0, 0.0, 0.0, 1.0, 0.0];",
+         op="matmul_f32", input=[1.0, 2.0, 3.0], weight=[1.0, 0.0, 0.0, 0.0, 1.0, 0.0],
+         out_features=2, in_features=3, expect=[1.0, 2.0], tol=1e-4),
+    dict(name="metal_matmul_large", src="tests/metal_matmul.rs:87", literal="let weight = vec![1.0; 1000 * 100];",
+         op="matmul_f32_ones", out_features=1000, in_features=100, expect_all=100.0),
+    dict(name="metal_matmul_matches_cpu", src="tests/metal_matmul.rs:106",
+         literal=".map(|index| ((index * 17 + 11) % 23) as f32 / 7.0 - 1.5)",
+         also=[["tests/metal_matmul.rs:103", ".map(|index| (index as f32 % 7.0) - 3.0)"]],
+         op="formula_matmul", dtype="f32", out_features=16, in_features=17, x=[7.0, 1.0, 3.0],
+         w=[17, 11, 23, 7.0, 1.5], expect="matmul", tol=1e-4, via=["host"]),
+    dict(name="metal_matmul_bf16_matches_cpu", src="tests/metal_matmul.rs:126",
+         literal=".map(|index| ((index * 17 + 11) % 23) as f32 / 7.0 - 1.5)",
+         also=[["tests/metal_matmul.rs:123", ".map(|index| (index as f32 % 7.0) - 3.0)"]],
+         op="formula_matmul", dtype="bf16", out_features=16, in_features=17, x=[7.0, 1.0, 3.0],
+         w=[17, 11, 23, 7.0, 1.5], expect="matmul", tol=1e-4, via=["host"]),
+    dict(name="metal_matmul_matches_cpu_transformer_dimensions", src="tests/metal_matmul.rs:156",
+         literal=".map(|index| ((index * 29 + 7) % 37) as f32 / 19.0 - 0.95)",
+         also=[["tests/metal_matmul.rs:153", ".map(|index| (index as f32 % 31.0) / 17.0 - 0.9)"]],
+         op="formula_matmul", dtype="f32", out_features=2048, in_features=2048, x=[31.0, 17.0, 0.9],
+         w=[29, 7, 37, 19.0, 0.95], expect="sequential", tol=1e-2, via=["host"]),
+    dict(name="metal_matmul_multi_tile", src="tests/metal_matmul.rs:176",
+         literal=".map(|index| ((index * 31 + 13) % 47) as f32 / 29.0 - 0.8)",
+         also=[["tests/metal_matmul.rs:173", ".map(|index| (index as f32 % 43.0) / 23.0 - 0.85)"]],
+         op="formula_matmul", dtype="f32", out_features=64, in_features=5504, x=[43.0, 23.0, 0.85],
+         w=[31, 13, 47, 29.0, 0.8], expect="sequential", tol=1e-2, via=["host"]),
+    dict(name="metal_buffer_matmul_matches_cpu", src="tests/metal_matmul.rs:196",
+         literal=".map(|index| ((index * 17 + 11) % 23) as f32 / 7.0 - 1.5)",
+         also=[["tests/metal_matmul.rs:193", ".map(|index| (index as f32 % 7.0) - 3.0)"]],
+         op="formula_matmul", dtype="f32", out_features=16, in_features=17, x=[7.0, 1.0, 3.0],
+         w=[17, 11, 23, 7.0, 1.5], expect="matmul", tol=1e-4, via=["host", "device"]),
+    dict(name="weights_to_metal_f32", src="tests/metal_matmul.rs:218",
+         literal="let weights = Weights::F32(vec![1.0, 2.0, 3.0, 4.0]);",
+         op="dense_upload", dtype="f32", values=[1.0, 2.0, 3.0, 4.0], expect_len=4, expect_bytes=16),
+    dict(name="weights_to_metal_bf16", src="tests/metal_matmul.rs:234",
+         literal="let weights = Weights::Bf16(vec![f32_to_bf16(1.5), f32_to_bf16(-2.0)]);",
+         op="dense_upload", dtype="bf16", values=[1.5, -2.0], expect_len=2, expect_bytes=4),
+    dict(name="weights_to_metal_bf16_creates_metal_bf16", src="tests/metal_matmul.rs:251",
+         literal="let weights = Weights::Bf16(vec![f32_to_bf16(0.5), f32_to_bf16(4.0), f32_to_bf16(-8.0)]);",
+         op="dense_upload", dtype="bf16", values=[0.5, 4.0, -8.0], expect_len=3, expect_bytes=6),
     # ---- src/rmsnorm.rs, src/attention.rs, src/ffn.rs (decode-loop support ops) ----------------
     dict(name="rmsnorm_forward_normalizes_with_weights", src="src/rmsnorm.rs:48",
          literal="let rmsnorm = RmsNorm::new(vec![0.5, 1.0], 1e-6);", op="rmsnorm", x=[2.0, 4.0],
@@ -125,12 +225,13 @@ def reference_root() -> str:
 
 def verify(root: str) -> None:
     for k in KATS:
-        path, line = k["src"].rsplit(":", 1)
-        with open(os.path.join(root, path)) as f:
-            lines = f.read().splitlines()
-        text = lines[int(line) - 1]
-        if k["literal"] not in text:
-            raise SystemExit(f"{k['name']}: {k['src']} does not contain {k['literal']!r}: {text!r}")
+        for src, literal in [[k["src"], k["literal"]]] + k.get("also", []):
+            path, line = src.rsplit(":", 1)
+            with open(os.path.join(root, path)) as f:
+                lines = f.read().splitlines()
+            text = lines[int(line) - 1]
+            if literal not in text:
+                raise SystemExit(f"{k['name']}: {src} does not contain {literal!r}: {text!r}")
 
 
 def main() -> None:
@@ -138,9 +239,10 @@ def main() -> None:
     if not os.path.isdir(root):
         raise SystemExit(f"reference tree {root} not found; the committed JSON stays as it is")
     verify(root)
-    with open(OUT, "w") as f:
-        json.dump({"source": "mizzy/pyxis test suite (Rust); transcribed by tests/golden/make_kats.py",
-                   "kats": KATS}, f, indent=1)
+    with open(OUT, "w") as f:  # one test per line
+        f.write('{"source": "mizzy/pyxis test suite (Rust); transcribed by tests/golden/make_kats.py",\n "kats": [\n')
+        f.write(",\n".join("  " + json.dumps(k) for k in KATS))
+        f.write("\n ]\n}\n")
     print(f"wrote {OUT}: {len(KATS)} known-answer tests, all citations verified", file=sys.stderr)
 
 

@@ -131,4 +131,79 @@ def run_kat(kat, impl) -> bool:
             return False
         assert abs(impl.silu(kat["x"]) - kat["expect"]) < kat["tol"]
         return True
+    if op == "matmul_f32":
+        y = impl.matmul_f32(np.asarray(kat["input"], np.float32), np.asarray(kat["weight"], np.float32),
+                            kat["out_features"], kat["in_features"])
+        assert len(y) == len(kat["expect"]), (kat["name"], len(y))
+        for a, b in zip(y, kat["expect"]):
+            if kat["tol"] == 0.0:
+                assert float(a) == b, (kat["name"], float(a), b)
+            else:
+                assert abs(float(a) - b) < kat["tol"], (kat["name"], float(a), b)
+        return True
+    if op == "bf16_vs_f32":
+        if not hasattr(impl, "matmul_bf16"):
+            return False
+        N, K = kat["out_features"], kat["in_features"]
+        x = np.asarray(kat["input"], np.float32)
+        wf = np.asarray(kat["weight"], np.float32)
+        bits = bf16_truncate(wf)
+        y = impl.matmul_bf16(x, bits, N, K)
+        ref = sequential_matmul(x, widen_bf16(bits) if kat["against"] == "widened" else wf, N, K)
+        for a, b in zip(y, ref):
+            assert abs(float(a) - float(b)) < kat["tol"], (kat["name"], float(a), float(b))
+        return True
+    if op == "formula_matmul":
+        if not hasattr(impl, "dense_matmul"):
+            return False
+        N, K = kat["out_features"], kat["in_features"]
+        x, wf = formula_inputs(kat)
+        w = bf16_truncate(wf) if kat["dtype"] == "bf16" else wf
+        ref = sequential_matmul(x, widen_bf16(w) if kat["dtype"] == "bf16" else w, N, K)
+        for via in kat["via"]:
+            y = np.asarray(impl.dense_matmul(kat["dtype"], x, w, N, K, via), np.float32).reshape(-1)
+            assert y.size == N, (kat["name"], via, y.size)
+            err = float(np.abs(y.astype(np.float64) - ref.astype(np.float64)).max())
+            assert err < kat["tol"], (kat["name"], via, err)
+        return True
+    if op == "weights_len":
+        if not hasattr(impl, "weights_len"):
+            return False
+        assert impl.weights_len(kat["kind"], kat["data_len"], kat.get("n_scales", 0), kat.get("block_size", 0),
+                                kat.get("num_elements", kat["data_len"])) == kat["expect"]
+        return True
+    if op == "dense_upload":
+        if not hasattr(impl, "dense_upload"):
+            return False
+        vals = np.asarray(kat["values"], np.float32)
+        n, nbytes = impl.dense_upload(kat["dtype"], bf16_truncate(vals) if kat["dtype"] == "bf16" else vals)
+        assert n == kat["expect_len"] and nbytes == kat["expect_bytes"], (kat["name"], n, nbytes)
+        return True
     raise AssertionError(f"unknown KAT op {op}")
+
+
+def bf16_truncate(v) -> np.ndarray:
+    """`(value.to_bits() >> 16) as u16`, the reference tests' f32 -> bf16."""
+    return (np.asarray(v, np.float32).view(np.uint32) >> 16).astype(np.uint16)
+
+
+def widen_bf16(bits) -> np.ndarray:
+    return (np.asarray(bits, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def sequential_matmul(x, w, N: int, K: int) -> np.ndarray:
+    """Each row's f32 products summed one after another in f32 (cpu_matmul_f32's iterator sum)."""
+    prod = (np.asarray(w, np.float32).reshape(N, K) * np.asarray(x, np.float32)[None, :]).astype(np.float32)
+    return np.cumsum(prod, axis=1, dtype=np.float32)[:, -1]
+
+
+def formula_inputs(kat):
+    """x_i = f32(i) % xm / xd - xs, w_i = f32((i*wa + wb) % wm) / wd - ws, each step in f32."""
+    N, K = kat["out_features"], kat["in_features"]
+    xm, xd, xs = kat["x"]
+    wa, wb, wm, wd, ws = kat["w"]
+    i = np.arange(K, dtype=np.int64)
+    x = np.fmod(i.astype(np.float32), np.float32(xm)) / np.float32(xd) - np.float32(xs)
+    j = np.arange(N * K, dtype=np.int64)
+    w = ((j * wa + wb) % wm).astype(np.float32) / np.float32(wd) - np.float32(ws)
+    return x.astype(np.float32), w.astype(np.float32)

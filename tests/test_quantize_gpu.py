@@ -26,6 +26,31 @@ class CudaImpl:
     def matmul_f32(self, x, w, N, K):
         return px.matmul(x, px.Weights.from_dense(w), N, K)
 
+    def matmul_bf16(self, x, bits, N, K):
+        return px.matmul(x, px.Weights.from_dense(bits), N, K)
+
+    def dense_matmul(self, dtype, x, w, N, K, via):
+        wd = px.Weights.from_dense(w)  # np.uint16 bits -> Bf16 rows, np.float32 -> F32 rows
+        assert wd.qtype == dtype
+        if via == "host":
+            return px.matmul(x, wd, N, K)
+        import torch
+        y = px.matmul_dev(torch.from_numpy(np.ascontiguousarray(x)).cuda().view(1, K), wd, N, K)
+        return y.cpu().numpy()
+
+    def weights_len(self, kind, data_len, n_scales, block_size, num_elements):
+        if kind in ("f32", "bf16"):
+            w = px.Weights.from_dense(np.zeros(data_len, np.float32 if kind == "f32" else np.uint16))
+        else:
+            w = px.Weights.from_packed(kind, np.zeros(data_len, np.uint8), np.ones(n_scales, np.float32),
+                                       block_size, num_elements)
+        return w.len()
+
+    def dense_upload(self, dtype, values):
+        w = px.Weights.from_dense(values)
+        assert w.qtype == dtype
+        return w.len(), w.data_bytes
+
     def argmax(self, v):
         return px.argmax(v)
 
