@@ -24,8 +24,13 @@
  *    ceil(num_elements/2) bytes (element i in the low nibble of byte i/2 when i is even, high
  *    nibble when odd, stored as q+8), scales = ceil(num_elements/block_size) f32, blocks running
  *    over the flattened row-major [out_features, in_features] index.
- *  - A context is bound to one device and owns one CUDA stream.  Calls on one context must not
- *    overlap from several host threads; use one context per thread or per device.
+ *  - A context is bound to one device and owns one CUDA stream.  Its kernels share the
+ *    context's scratch (the tensor-core GEMV's split-K slots, the GEMM workspace, the argmax
+ *    scratch), so its launches must not overlap on the GPU: issue `_dev` calls on one stream or
+ *    on streams ordered by events, from one host thread at a time.  The host-pointer entry
+ *    points run on the context's stream and return after it drains; pyxis_cuda_matmul and
+ *    pyxis_cuda_matmul_batch hold a per-context lock for their staging buffers, so several host
+ *    threads may call them at once (the calls run one after another).
  *  - `_dev` entry points take device pointers and a cudaStream_t (NULL = the context's stream;
  *    pass cudaStreamLegacy for the legacy default stream) and do not synchronize.  The host-pointer entry points copy in, compute and copy out, and
  *    return after the result is in host memory (src/metal_matmul.rs:311-354 behaves the same).

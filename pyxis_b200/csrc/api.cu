@@ -466,6 +466,7 @@ int pyxis_cuda_matmul_batch(pyxis_cuda_ctx *ctx, const float *input, size_t M, c
     if (M == 0 || out_features == 0) return PYXIS_OK;
     if (!input || !out) return fail(PYXIS_EINVAL, "null input or output");
     DeviceGuard g(ctx->device);
+    std::lock_guard<std::mutex> lock(ctx->host_mu);
     rc = grow(&ctx->dx, &ctx->dx_cap, M * in_features);
     if (rc) return rc;
     rc = grow(&ctx->dy, &ctx->dy_cap, M * out_features);

@@ -5,13 +5,17 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "argmax.h"
 
 struct pyxis_cuda_ctx {
     int device;
     int num_sms;
     cudaStream_t stream;
-    // staging for the host-pointer entry points (grown on demand)
+    // staging for the host-pointer entry points (grown on demand), guarded by host_mu: host
+    // threads that call pyxis_cuda_matmul(_batch) on one context at once run one after another
+    std::mutex host_mu;
     float *dx = nullptr;
     size_t dx_cap = 0;
     float *dy = nullptr;

@@ -160,3 +160,34 @@ def test_batch_kernel(qt, N, K, bs, B):
     Y2 = px.matmul_batch(X, w, N, K)
     assert np.array_equal(Y1, Y2)  # the combine order is fixed: bit-identical reruns
     px._native.check(px._native.lib().pyxis_cuda_check_device_error(w.ctx.handle))
+
+
+def test_host_calls_from_several_threads():
+    """pyxis_cuda_matmul from four host threads on one context: the calls share its staging
+    buffers and serialise on its lock, so every thread gets its own product, bit for bit the
+    single-threaded result (the kernels reduce in a fixed order)."""
+    import threading
+    jobs = []
+    for t in range(4):
+        N, K = 1024 + 512 * t, 2048
+        w, od, os_ = make("int4", N, K, 32, seed=300 + t)
+        x = px.synth_normal_f32(400 + t, K, 1.0)
+        y0 = px.matmul(x, w, N, K)
+        check_matmul(y0[None], ref_matmul("int4", od, os_, 32, x[None], N, K), exact_matmul("int4", od, os_, 32, N, K, x[None]))
+        jobs.append((w, x, y0, N, K))
+    bad = []
+
+    def run(i):
+        w, x, y0, N, K = jobs[i]
+        for _ in range(200):
+            y = px.matmul(x, w, N, K)
+            if y.shape != y0.shape or not np.array_equal(y.view(np.uint32), y0.view(np.uint32)):
+                bad.append(i)
+                return
+
+    threads = [threading.Thread(target=run, args=(i,)) for i in range(len(jobs))]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join()
+    assert not bad, bad
