@@ -12,6 +12,11 @@
  * and one decode step is captured once into a CUDA graph and replayed per token.  Prompt tokens
  * go through the same step one position at a time, as the reference's prefill does
  * (src/attention.rs:74-98): position p attends to keys 0..p.
+ *
+ * A model runs on its context's stream and uses the context's scratch, so its calls follow the
+ * context's rule: they must not overlap with other work of the same context (another model's
+ * generate, a `_dev` call, a host-pointer matmul from another thread).  Use one context per
+ * concurrently generating model.
  */
 #ifndef PYXIS_DECODE_H
 #define PYXIS_DECODE_H
