@@ -62,6 +62,33 @@ def test_init_without_device_reports_enodev():
         pyxis_b200.Weights.quantize_int8(np.ones(4, np.float32), 4)
 
 
+def _construct(px, what):
+    from pyxis_b200.model import Decoder, ModelConfig, SyntheticModel
+    if what == "quantize_int4":
+        return px.Weights.quantize_int4(np.ones(64, np.float32), 32)
+    if what == "quantize_int8_bf16":
+        return px.Weights.quantize_int8(np.ones(4, np.uint16), 4)
+    if what == "from_packed":
+        return px.Weights.from_packed("int8", np.zeros(4, np.int8), np.ones(1, np.float32), 4, 4)
+    if what == "from_q8_0":
+        return px.Weights.from_q8_0(bytes(34), 32)
+    if what == "from_dense":
+        return px.Weights.from_dense(np.ones(8, np.float32))
+    cfg = ModelConfig(hidden=64, n_layers=1, n_q_heads=1, n_kv_heads=1, head_dim=64, ffn=64, vocab=64)
+    return Decoder(SyntheticModel(cfg))
+
+
+@pytest.mark.skipif(_has_gpu(), reason="checks the no-device path")
+@pytest.mark.parametrize("what", ["quantize_int4", "quantize_int8_bf16", "from_packed", "from_q8_0", "from_dense",
+                                  "decoder"])
+def test_every_entry_point_raises_without_a_device(what):
+    """No CPU fallback anywhere: without a B200 each constructor raises the library's ENODEV."""
+    import pyxis_b200 as px
+    with pytest.raises(px.PyxisError) as e:
+        _construct(px, what)
+    assert e.value.code == _native.PYXIS_ENODEV
+
+
 def test_null_arguments_are_rejected_on_the_host():
     L = _native.lib()
     assert L.pyxis_cuda_init(0, None) == _native.PYXIS_EINVAL
