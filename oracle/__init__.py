@@ -8,6 +8,7 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+import time
 
 import numpy as np
 
@@ -170,11 +171,12 @@ class OModel(C.Structure):
                 ("final_norm", _vp), ("lm_head", OWeights)]
 
 
-def greedy_decode(cfg, bf16, qtype: str, prompt, n_new: int, nthreads: int = 0):
+def greedy_decode(cfg, bf16, qtype: str, prompt, n_new: int, nthreads: int = 0, timing=None):
     """Greedy tokens of the model whose tensors ``bf16(name)`` returns (np.uint16 bits; names
     ``layers.{l}.{q,k,v,o,gate,up,down}`` and ``embed``), quantised by the reference's policy
     (src/model.rs:520-530: int8 one scale per row, int4 one per 32), tied lm_head, RMSNorm
-    weights 1, QK-norm when cfg.qk_norm."""
+    weights 1, QK-norm when cfg.qk_norm.  A list passed as ``timing`` receives the seconds of
+    the generation alone (the len(prompt) + n_new - 1 forward passes, without the packing)."""
     keep = []
 
     def q(bits, in_features):
@@ -209,7 +211,10 @@ def greedy_decode(cfg, bf16, qtype: str, prompt, n_new: int, nthreads: int = 0):
                ones.ctypes.data, lm)
     pr = np.ascontiguousarray(np.asarray(prompt, np.int32))
     out = np.empty(n_new, np.int32)
+    t0 = time.perf_counter()
     rc = lib().oracle_greedy_decode(C.addressof(m), pr.ctypes.data, pr.size, n_new, out.ctypes.data, nthreads)
+    if timing is not None:
+        timing.append(time.perf_counter() - t0)
     if rc:
         raise RuntimeError("oracle_greedy_decode failed")
     return out
