@@ -10,7 +10,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 import oracle
-from pyxis_b200.dist import gather_pick, pick_global_argmax, shard_range
+from pyxis_b200.dist import bits_rows, gather_pick, pick_global_argmax, shard_range
 
 
 def shard_argmax(v, lo):
@@ -53,6 +53,27 @@ def test_global_pick_matches_reference_argmax(world):
         pairs = [shard_argmax(v[lo:hi], lo) for lo, hi in (shard_range(n, r, world) for r in range(world)) if hi > lo]
         got = pick_global_argmax([p[0] for p in pairs], [p[1] for p in pairs])
         assert got == oracle.argmax(v), (v, pairs, got)
+
+
+@pytest.mark.parametrize("qt,N,K,bs", [("int8", 37, 96, 96), ("int4", 37, 96, 32), ("int4", 10, 2048, 32),
+                                        ("int8", 300, 64, 64)])
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_row_shard_packs_are_slices_of_the_full_pack(qt, N, K, bs, world):
+    """A rank quantises only its rows (RowShardedMatmul): with one scale per row, or groups that
+    divide the row (K % 32 == 0, K even for int4's two codes per byte), the shard's bytes and
+    scales are exactly the rows' slice of the full matrix's pack, so the shards' outputs
+    concatenate to the single-GPU result."""
+    from pyxis_b200 import synth_normal_bf16
+    bits = synth_normal_bf16(N * 31 + K, N * K, 0.02)
+    quant = oracle.quantize_int8 if qt == "int8" else oracle.quantize_int4
+    full_d, full_s = quant(oracle.bf16_to_f32(bits), bs)
+    row_bytes = K if qt == "int8" else K // 2
+    for r in range(world):
+        lo, hi = shard_range(N, r, world)
+        d, s = quant(oracle.bf16_to_f32(bits_rows(bits, K, lo, hi)), bs)
+        assert np.array_equal(d.view(np.uint8), full_d.view(np.uint8)[lo * row_bytes:hi * row_bytes])
+        spr = K // bs
+        assert np.array_equal(s.view(np.uint32), full_s.view(np.uint32)[lo * spr:hi * spr])
 
 
 def _worker(rank, world, port, q):
