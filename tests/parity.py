@@ -81,3 +81,24 @@ def q8_0_bytes(blocks) -> bytes:
         out += int(scale_bits).to_bytes(2, "little")
         out += bytes((v & 0xFF) for v in vals)
     return bytes(out)
+
+
+def tie_blocks(amax: float, bs: int = 16) -> np.ndarray:
+    """Blocks of bs values whose last element is amax (127 for int8, 7 for int4), so the block's
+    scale is exactly 1 and each other value is its own quotient: the rounding ties k + 0.5 of
+    f32::round and their f32 neighbours for |k + 0.5| < amax, plus +-0.49999997."""
+    lim = int(amax) - 1
+    ties = []
+    for k in range(-lim - 1, lim + 1):
+        c = np.float32(k + 0.5)
+        ties += [np.nextafter(c, np.float32(-np.inf)), c, np.nextafter(c, np.float32(np.inf))]
+    ties += [np.float32(0.49999997), np.float32(-0.49999997)]
+    ties = np.array([t for t in ties if abs(float(t)) < amax], np.float32)
+    blocks = []
+    for i in range(0, ties.size, bs - 1):
+        blk = np.zeros(bs, np.float32)
+        part = ties[i:i + bs - 1]
+        blk[:part.size] = part
+        blk[-1] = np.float32(amax)
+        blocks.append(blk)
+    return np.concatenate(blocks)

@@ -5,7 +5,7 @@ import pytest
 
 import oracle
 from kat_check import run_kat
-from parity import load_kats
+from parity import load_kats, tie_blocks
 
 
 class OracleImpl:
@@ -50,6 +50,16 @@ def test_oracle_reference_kat(kat):
 
 
 # ---- an independent numpy restatement of src/weights.rs:94-151 ----------------------------------
+def round_half_away(t):
+    """f32::round: nearest integer, ties away from zero.  t - trunc(t) is exact in f32, so the tie
+    test is exact (floor(|t| + 0.5) is not: 0.49999997 + 0.5 rounds up to 1.0)."""
+    t = np.asarray(t, np.float32)
+    tr = np.trunc(t)
+    with np.errstate(invalid="ignore"):
+        frac = np.abs(t - tr)
+        return (tr + np.sign(t) * (frac >= np.float32(0.5))).astype(np.float32)
+
+
 def np_quantize_int8(v, bs):
     v = np.asarray(v, np.float32)
     n = v.size
@@ -58,9 +68,9 @@ def np_quantize_int8(v, bs):
     pad[:n] = np.abs(v)
     absmax = np.nanmax(np.where(np.isnan(pad), 0, pad).reshape(nb, bs), axis=1).astype(np.float32)
     scales = np.where(absmax == 0, np.float32(1.0), absmax / np.float32(127.0)).astype(np.float32)
-    t = (v / np.repeat(scales, bs)[:n]).astype(np.float32)
-    r = np.sign(t) * np.floor(np.abs(t) + np.float32(0.5))  # half away from zero
-    r = np.clip(r, -127, 127)
+    with np.errstate(invalid="ignore", divide="ignore"):
+        t = (v / np.repeat(scales, bs)[:n]).astype(np.float32)
+    r = np.clip(round_half_away(t), -127, 127)
     r = np.where(np.isnan(r), 0, r)
     return r.astype(np.int8), scales
 
@@ -73,9 +83,9 @@ def np_quantize_int4(v, bs):
     pad[:n] = np.abs(v)
     absmax = np.max(np.where(np.isnan(pad), 0, pad).reshape(nb, bs), axis=1).astype(np.float32)
     scales = np.where(absmax == 0, np.float32(1.0), absmax / np.float32(7.0)).astype(np.float32)
-    t = (v / np.repeat(scales, bs)[:n]).astype(np.float32)
-    r = np.sign(t) * np.floor(np.abs(t) + np.float32(0.5))
-    r = np.clip(r, -8, 7)
+    with np.errstate(invalid="ignore", divide="ignore"):
+        t = (v / np.repeat(scales, bs)[:n]).astype(np.float32)
+    r = np.clip(round_half_away(t), -8, 7)
     r = np.where(np.isnan(r), 0, r).astype(np.int64) + 8
     codes = np.full(2 * (-(-n // 2)), 8, np.int64)
     codes[:n] = r
@@ -182,3 +192,40 @@ def test_oracle_f16_widening_over_every_bit_pattern():
     want = h.astype(np.uint16).view(np.float16).astype(np.float32).view(np.uint32).copy()
     want[is_nan] = ((h[is_nan] & 0x8000) << 16) | 0x7FC00000 | ((h[is_nan] & 0x3FF) << 13)
     assert np.array_equal(got, want)
+
+
+def test_oracle_quantizers_round_ties_away_from_zero():
+    """Blocks whose scale is exactly 1, so every value is its own quotient: the codes must be
+    f32::round of the value, ties away from zero."""
+    for qt, amax, quant, ref in (("int8", 127.0, oracle.quantize_int8, np_quantize_int8),
+                                 ("int4", 7.0, oracle.quantize_int4, np_quantize_int4)):
+        v = tie_blocks(amax, 16)
+        d, s = quant(v, 16)
+        e, f = ref(v, 16)
+        assert np.all(s == 1.0) and np.array_equal(s.view(np.uint32), f.view(np.uint32))
+        assert np.array_equal(np.asarray(d).view(np.uint8), np.asarray(e).view(np.uint8)), qt
+        if qt == "int8":
+            want = [int(np.sign(x) * np.floor(abs(float(x)) + 0.5)) for x in v]  # float64: exact here
+            assert list(np.asarray(d, np.int64)) == want
+
+
+def test_oracle_quantizers_property():
+    """Random lengths, block sizes and values including NaN, infinities, subnormals and signed
+    zeros: the oracle and the numpy restatement agree bit for bit."""
+    hyp = pytest.importorskip("hypothesis")
+    from hypothesis import given, settings, strategies as st
+
+    floats = st.floats(width=32, allow_nan=True, allow_infinity=True, allow_subnormal=True)
+
+    @settings(max_examples=300, deadline=None, derandomize=True, database=None)
+    @given(st.lists(floats, min_size=1, max_size=200), st.integers(min_value=1, max_value=70))
+    def check(values, bs):
+        v = np.asarray(values, np.float32)
+        for quant, ref in ((oracle.quantize_int8, np_quantize_int8), (oracle.quantize_int4, np_quantize_int4)):
+            with np.errstate(all="ignore"):
+                d, s = quant(v, bs)
+                e, f = ref(v, bs)
+            assert np.array_equal(np.asarray(d).view(np.uint8), np.asarray(e).view(np.uint8))
+            assert np.array_equal(s.view(np.uint32), f.view(np.uint32))
+
+    check()

@@ -6,7 +6,7 @@ import pytest
 import oracle
 import pyxis_b200 as px
 from kat_check import run_kat
-from parity import load_kats
+from parity import load_kats, tie_blocks
 
 pytestmark = pytest.mark.gpu
 
@@ -175,3 +175,16 @@ def test_device_source_written_just_before_the_call():
     d, s = w.download()
     od, os_ = oracle.quantize_int4(np.ascontiguousarray(vals[::2]).reshape(-1), 32)
     assert np.array_equal(d, od) and np.array_equal(_bits(s), _bits(os_))
+
+
+@pytest.mark.parametrize("qt", ["int8", "int4"])
+def test_quantize_rounds_ties_away_from_zero(qt):
+    """Blocks whose scale is exactly 1: every code is f32::round of its value (ties away from
+    zero, 0.49999997 -> 0), as the oracle's roundf gives."""
+    amax = 127.0 if qt == "int8" else 7.0
+    v = tie_blocks(amax, 16)
+    w = px.Weights.quantize_int8(v, 16) if qt == "int8" else px.Weights.quantize_int4(v, 16)
+    d, s = w.download()
+    od, os_ = (oracle.quantize_int8 if qt == "int8" else oracle.quantize_int4)(v, 16)
+    assert np.array_equal(_bits(s), _bits(os_)) and np.all(s == 1.0)
+    assert np.array_equal(np.asarray(d).view(np.uint8), np.asarray(od).view(np.uint8))
