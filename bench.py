@@ -186,6 +186,19 @@ def gpu_uuid(local):
 _CPU_SWEEP_INPUTS = None
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (the CPU baselines run on it)."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
 def cpu_sweep_inputs():
     """The sweep's matrices packed by the oracle quantizer and the x rows of every batch size,
     built once per process (the packing takes ~10x longer than one timed sweep)."""
@@ -239,7 +252,7 @@ def reference_arm(args, ws, rank):
             "warmup": args.warmup, "ms_per_step": total_t / args.steps * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": config_dict(ws),
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "cpu": cpu_model(), "kind": "port",
                              "sample": "each step = the full sweep (12 matvec calls) through the C port of "
                                        "src/matmul.rs (scalar x86 dot products, rows over all host threads)"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -366,7 +379,8 @@ def run_decode(local, cpu_sample_tokens=0):
         import oracle
         tm = []
         oracle.greedy_decode(cfg, m.bf16, "int8", prompt[:1], cpu_sample_tokens, timing=tm)
-        out["cpu_baseline"] = {"tokens_per_s": cpu_sample_tokens / tm[0], "cores": oracle.num_cpus(), "kind": "port",
+        out["cpu_baseline"] = {"tokens_per_s": cpu_sample_tokens / tm[0], "cores": oracle.num_cpus(), "cpu": cpu_model(),
+                               "kind": "port",
                                "sample": f"1 prompt id + {cpu_sample_tokens} greedy tokens ({cpu_sample_tokens} forward "
                                          "passes) through the C port of Model::generate on all host threads; the "
                                          "host-side packing of the weights is outside the timed region"}
@@ -474,11 +488,14 @@ def run_config1(local, capture, replay_ms, with_cpu):
         xs = px.synth_normal_f32(SEED + 8, K, 1.0).reshape(1, K)
         cores = oracle.num_cpus()
         oracle.matmul(xs, oracle.INT8, d, sc, K, N, K, nthreads=cores)
-        t0 = time.perf_counter()
-        for _ in range(20):
+        times = []
+        for _ in range(21):
+            t0 = time.perf_counter()
             oracle.matmul(xs, oracle.INT8, d, sc, K, N, K, nthreads=cores)
-        cpu_us = (time.perf_counter() - t0) / 20 * 1e6
-        out["cpu_baseline"] = {"us": round(cpu_us, 1), "gbs": round(by / cpu_us / 1e3, 2), "cores": cores, "kind": "port"}
+            times.append(time.perf_counter() - t0)
+        cpu_us = sorted(times)[len(times) // 2] * 1e6
+        out["cpu_baseline"] = {"us": round(cpu_us, 1), "gbs": round(by / cpu_us / 1e3, 2), "cores": cores, "cpu": cpu_model(),
+                               "kind": "port", "sample": "median of 21 calls through the C port on all host threads"}
     return out
 
 
@@ -694,7 +711,7 @@ def pyxis_arm(args, ws, rank, local):
 
         cores = oracle.num_cpus()
         t, b = run_cpu_sweep(cores)
-        cpu = {"value": b / t / 1e9, "unit": UNIT, "cores": cores, "kind": "port",
+        cpu = {"value": b / t / 1e9, "unit": UNIT, "cores": cores, "cpu": cpu_model(), "kind": "port",
                "sample": "one full sweep step (12 matvec calls, 6.1 GB of int4/int8 rows incl. batch-8 re-reads) "
                          "through the C port of the reference's Rayon matmul, all host threads"}
 
