@@ -340,7 +340,7 @@ def run_prefill(local, reps=20):
 DECODE_WORKLOAD = ("Qwen3-1.7B-shape decode, random init, int8 one scale per row: hidden 2048, 28 layers, "
                    "16/8 heads x 128, FFN 6144, vocab 151936, tied lm_head; 16 prompt ids + 128 greedy tokens, batch 1")
 DECODE_PROMPT, DECODE_NEW = 16, 128
-DECODE_CPU_TOKENS = 4  # the CPU baseline's bounded sample of config 4: weight-bound passes of ~1.7 GB each
+DECODE_CPU_TOKENS = 16  # the CPU baseline's bounded sample of config 4: weight-bound passes of ~1.7 GB each
 
 
 def decode_bytes_per_token(cfg, pos):
