@@ -51,6 +51,21 @@ def lib() -> C.CDLL:
         L.oracle_silu.restype = C.c_float
         L.oracle_greedy_decode.argtypes = [_vp, _vp, _sz, _sz, _vp, C.c_int]
         L.oracle_greedy_decode.restype = C.c_int
+        L.oracle_kv_new.argtypes = [_vp, _sz]
+        L.oracle_kv_new.restype = _vp
+        L.oracle_kv_free.argtypes = [_vp]
+        L.oracle_kv_len.argtypes = [_vp, _sz]
+        L.oracle_kv_len.restype = _sz
+        L.oracle_kv_keys.argtypes = [_vp, _sz]
+        L.oracle_kv_keys.restype = C.POINTER(C.c_float)
+        L.oracle_attention_forward.argtypes = [_vp, _sz, _vp, _sz, _sz, _vp, _vp, C.c_int]
+        L.oracle_attention_forward.restype = C.c_int
+        L.oracle_ffn_forward.argtypes = [_vp, _sz, _vp, _vp, C.c_int]
+        L.oracle_ffn_forward.restype = C.c_int
+        L.oracle_block_forward.argtypes = [_vp, _sz, _vp, _sz, _sz, _vp, C.c_int]
+        L.oracle_block_forward.restype = C.c_int
+        L.oracle_transformer_forward.argtypes = [_vp, _vp, _sz, _sz, _vp, C.c_int]
+        L.oracle_transformer_forward.restype = C.c_int
         L.oracle_num_cpus.restype = C.c_int
         _lib = L
     return _lib
@@ -218,3 +233,96 @@ def greedy_decode(cfg, bf16, qtype: str, prompt, n_new: int, nthreads: int = 0, 
     if rc:
         raise RuntimeError("oracle_greedy_decode failed")
     return out
+
+
+# ---- layers with f32 weights, as the reference's unit tests build them -------------------------
+class Layers:
+    """n_layers identical transformer layers with f32 weights (Weights::F32): wq [q_dim, hidden],
+    wk / wv [kv_dim, hidden], wo [hidden, q_dim], QK-norm weights [head_dim] or None, FFN
+    wgate / wup [ffn, hidden] and wdown [hidden, ffn], RMSNorm weights [hidden] (1 when omitted),
+    every norm with eps.  Drives oracle_attention_forward / _ffn_ / _block_ / _transformer_."""
+
+    def __init__(self, hidden, n_q_heads, n_kv_heads, head_dim, wq, wk, wv, wo, q_norm=None, k_norm=None,
+                 theta=10.0, eps=1e-6, ffn=0, wgate=None, wup=None, wdown=None, n_layers=1):
+        self._keep = []
+        self.hidden = hidden
+
+        def arr(a):
+            a = np.ascontiguousarray(np.asarray(a, np.float32).ravel())
+            self._keep.append(a)
+            return a
+
+        def weights(a):
+            if a is None:
+                return OWeights(F32, None, None, 1)
+            return OWeights(F32, arr(a).ctypes.data, None, 1)
+
+        def per_layer(w):
+            return (OWeights * n_layers)(*([weights(w)] * n_layers))
+
+        def norm_ptrs(v):
+            p = None if v is None else arr(v).ctypes.data
+            return (_vp * n_layers)(*([p] * n_layers))
+
+        ones = arr(np.ones(hidden, np.float32))
+        self._tabs = [per_layer(w) for w in (wq, wk, wv, wo, wgate, wup, wdown)]
+        self._norms = [norm_ptrs(np.ones(hidden, np.float32)), norm_ptrs(np.ones(hidden, np.float32)),
+                       norm_ptrs(q_norm), norm_ptrs(k_norm)]
+        self.m = OModel(hidden, n_layers, n_q_heads, n_kv_heads, head_dim, ffn, 0, eps, theta, None,
+                        C.addressof(self._norms[0]), C.addressof(self._norms[1]), C.addressof(self._norms[2]),
+                        C.addressof(self._norms[3]), *[C.addressof(t) for t in self._tabs], ones.ctypes.data,
+                        OWeights(F32, None, None, 1))
+        self.kv_dim = n_kv_heads * head_dim
+
+    def cache(self, max_len=64):
+        return _KV(self, max_len)
+
+    def attention(self, x, seq_len, start_pos, kv, layer=0):
+        x = _f32(x).copy()
+        out = np.empty(seq_len * self.hidden, np.float32)
+        if lib().oracle_attention_forward(C.byref(self.m), layer, _p(x), seq_len, start_pos, kv.h, _p(out), 1):
+            raise RuntimeError("oracle_attention_forward failed")
+        return out
+
+    def ffn(self, x, layer=0):
+        x = _f32(x).copy()
+        out = np.empty(self.hidden, np.float32)
+        if lib().oracle_ffn_forward(C.byref(self.m), layer, _p(x), _p(out), 1):
+            raise RuntimeError("oracle_ffn_forward failed")
+        return out
+
+    def block(self, x, seq_len, start_pos, kv, layer=0):
+        x = _f32(x).copy()
+        if lib().oracle_block_forward(C.byref(self.m), layer, _p(x), seq_len, start_pos, kv.h, 1):
+            raise RuntimeError("oracle_block_forward failed")
+        return x
+
+    def transformer(self, x, seq_len, start_pos, kv):
+        x = _f32(x).copy()
+        if lib().oracle_transformer_forward(C.byref(self.m), _p(x), seq_len, start_pos, kv.h, 1):
+            raise RuntimeError("oracle_transformer_forward failed")
+        return x
+
+
+class _KV:
+    """KvCache for a Layers model (oracle_kv)."""
+
+    def __init__(self, layers: Layers, max_len: int):
+        self.layers = layers
+        self.max_len = max_len
+        self.h = lib().oracle_kv_new(C.byref(layers.m), max_len)
+        if not self.h:
+            raise MemoryError("oracle_kv_new")
+
+    def __len__(self):
+        return int(lib().oracle_kv_len(self.h, 0))
+
+    def keys(self, layer=0) -> np.ndarray:
+        """The cached keys so far, [len * kv_dim] (LayerCache::keys)."""
+        n = int(lib().oracle_kv_len(self.h, layer)) * self.layers.kv_dim
+        return np.ctypeslib.as_array(lib().oracle_kv_keys(self.h, layer), shape=(max(n, 1),))[:n].copy()
+
+    def __del__(self):  # pragma: no cover
+        if getattr(self, "h", None):
+            lib().oracle_kv_free(self.h)
+            self.h = None

@@ -162,9 +162,13 @@ static void mm(const oracle_weights *w, const float *x, size_t out, size_t in, f
     for (int t = 0; t < started; ++t) pthread_join(th[t], NULL);
 }
 
+const float *oracle_kv_keys(const oracle_kv *kv, size_t layer) {
+    return kv->keys + layer * kv->max_len * kv->kv_dim;
+}
+
 /* Attention::forward (src/attention.rs:57-141).  x: [seq_len, hidden] (already input-normed),
  * out: [seq_len, hidden]. */
-static int attention_forward(const oracle_model *m, size_t layer, const float *x, size_t seq_len,
+int oracle_attention_forward(const oracle_model *m, size_t layer, const float *x, size_t seq_len,
                              size_t start_pos, oracle_kv *kv, float *out, int nt) {
     size_t hd = m->head_dim, H = m->hidden;
     size_t q_dim = m->n_q_heads * hd, kv_dim = m->n_kv_heads * hd;
@@ -236,37 +240,59 @@ static void ffn_forward(const oracle_model *m, size_t layer, const float *x, flo
     mm(&m->wdown[layer], gate, m->hidden, m->ffn, out, nt);
 }
 
-/* TransformerBlock::forward (src/transformer.rs:28-62) + Transformer::forward (:80-90). */
+int oracle_ffn_forward(const oracle_model *m, size_t layer, const float *x, float *out, int nt) {
+    float *gate = (float *)malloc(m->ffn * sizeof(float));
+    float *up = (float *)malloc(m->ffn * sizeof(float));
+    int rc = (gate && up) ? 0 : -1;
+    if (rc == 0) ffn_forward(m, layer, x, out, gate, up, nt);
+    free(gate);
+    free(up);
+    return rc;
+}
+
+/* TransformerBlock::forward (src/transformer.rs:28-62) for layer l; scratch holds 2 seq_len H +
+ * 2 ffn + H floats. */
+static int block_forward(const oracle_model *m, size_t l, float *x, size_t seq_len, size_t start_pos,
+                         oracle_kv *kv, float *scratch, int nt) {
+    size_t H = m->hidden;
+    float *residual = scratch, *attn = residual + seq_len * H, *gate = attn + seq_len * H;
+    float *up = gate + m->ffn, *fo = up + m->ffn;
+    memcpy(residual, x, seq_len * H * sizeof(float));
+    for (size_t p = 0; p < seq_len; ++p) oracle_rmsnorm(x + p * H, m->input_norm[l], H, m->rms_eps);
+    int rc = oracle_attention_forward(m, l, x, seq_len, start_pos, kv, attn, nt);
+    if (rc) return rc;
+    for (size_t i = 0; i < seq_len * H; ++i) x[i] = residual[i] + attn[i];
+    memcpy(residual, x, seq_len * H * sizeof(float));
+    for (size_t p = 0; p < seq_len; ++p) oracle_rmsnorm(x + p * H, m->post_norm[l], H, m->rms_eps);
+    for (size_t p = 0; p < seq_len; ++p) {
+        ffn_forward(m, l, x + p * H, fo, gate, up, nt);
+        for (size_t i = 0; i < H; ++i) x[p * H + i] = residual[p * H + i] + fo[i];
+    }
+    return 0;
+}
+
+static float *block_scratch(const oracle_model *m, size_t seq_len) {
+    return (float *)malloc((2 * seq_len * m->hidden + 2 * m->ffn + m->hidden) * sizeof(float));
+}
+
+int oracle_block_forward(const oracle_model *m, size_t layer, float *x, size_t seq_len, size_t start_pos,
+                         oracle_kv *kv, int nt) {
+    float *scratch = block_scratch(m, seq_len);
+    int rc = scratch ? block_forward(m, layer, x, seq_len, start_pos, kv, scratch, nt) : -1;
+    free(scratch);
+    return rc;
+}
+
+/* Transformer::forward (src/transformer.rs:80-90): the blocks, then the final norm. */
 int oracle_transformer_forward(const oracle_model *m, float *x, size_t seq_len, size_t start_pos,
                                oracle_kv *kv, int nt) {
     size_t H = m->hidden;
-    float *residual = (float *)malloc(seq_len * H * sizeof(float));
-    float *attn = (float *)malloc(seq_len * H * sizeof(float));
-    float *gate = (float *)malloc(m->ffn * sizeof(float));
-    float *up = (float *)malloc(m->ffn * sizeof(float));
-    float *fo = (float *)malloc(H * sizeof(float));
-    int rc = 0;
-    if (!residual || !attn || !gate || !up || !fo) rc = -1;
-    for (size_t l = 0; l < m->n_layers && rc == 0; ++l) {
-        memcpy(residual, x, seq_len * H * sizeof(float));
-        for (size_t p = 0; p < seq_len; ++p) oracle_rmsnorm(x + p * H, m->input_norm[l], H, m->rms_eps);
-        rc = attention_forward(m, l, x, seq_len, start_pos, kv, attn, nt);
-        if (rc) break;
-        for (size_t i = 0; i < seq_len * H; ++i) x[i] = residual[i] + attn[i];
-        memcpy(residual, x, seq_len * H * sizeof(float));
-        for (size_t p = 0; p < seq_len; ++p) oracle_rmsnorm(x + p * H, m->post_norm[l], H, m->rms_eps);
-        for (size_t p = 0; p < seq_len; ++p) {
-            ffn_forward(m, l, x + p * H, fo, gate, up, nt);
-            for (size_t i = 0; i < H; ++i) x[p * H + i] = residual[p * H + i] + fo[i];
-        }
-    }
+    float *scratch = block_scratch(m, seq_len);
+    int rc = scratch ? 0 : -1;
+    for (size_t l = 0; l < m->n_layers && rc == 0; ++l) rc = block_forward(m, l, x, seq_len, start_pos, kv, scratch, nt);
     if (rc == 0)
         for (size_t p = 0; p < seq_len; ++p) oracle_rmsnorm(x + p * H, m->final_norm, H, m->rms_eps);
-    free(residual);
-    free(attn);
-    free(gate);
-    free(up);
-    free(fo);
+    free(scratch);
     return rc;
 }
 

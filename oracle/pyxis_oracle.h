@@ -130,6 +130,24 @@ oracle_kv *oracle_kv_new(const oracle_model *m, size_t max_len);
 void oracle_kv_free(oracle_kv *kv);
 size_t oracle_kv_len(const oracle_kv *kv, size_t layer);
 
+/* The cached keys of one layer, [max_len][n_kv_heads * head_dim] (LayerCache::keys,
+ * src/kv_cache.rs:43-45): normalised and rotated as Attention::forward stores them. */
+const float *oracle_kv_keys(const oracle_kv *kv, size_t layer);
+
+/* Attention::forward (src/attention.rs:57-141) of one layer over seq_len positions of x
+ * [seq_len, hidden] starting at start_pos (== the layer's cache length, :68), appending to kv;
+ * out [seq_len, hidden].  Returns 0 or -1. */
+int oracle_attention_forward(const oracle_model *m, size_t layer, const float *x, size_t seq_len,
+                             size_t start_pos, oracle_kv *kv, float *out, int nthreads);
+
+/* Ffn::forward (src/ffn.rs:33-50) of one layer for one position: out [hidden].  Returns 0 or -1. */
+int oracle_ffn_forward(const oracle_model *m, size_t layer, const float *x, float *out, int nthreads);
+
+/* TransformerBlock::forward (src/transformer.rs:28-62) of one layer, in place on x
+ * [seq_len, hidden].  Returns 0 or -1. */
+int oracle_block_forward(const oracle_model *m, size_t layer, float *x, size_t seq_len, size_t start_pos,
+                         oracle_kv *kv, int nthreads);
+
 /* Transformer::forward (src/transformer.rs:80-90) over seq_len positions of x [seq_len, hidden],
  * in place, appending to kv.  Returns 0 or -1 (capacity / shape). */
 int oracle_transformer_forward(const oracle_model *m, float *x, size_t seq_len, size_t start_pos,
