@@ -43,3 +43,19 @@ def test_qwen3_1p7b_shape_int8_greedy_matches_golden():
     toks, (t_prompt, t_decode) = dec.generate(g["prompt"], len(g["tokens"]))
     assert [int(t) for t in toks] == g["tokens"]
     dec.close()
+
+
+def test_generate_rejects_bad_arguments():
+    """Checked on the host before any launch: token ids outside the vocabulary (the embedding
+    lookup's bounds assert, src/embedding.rs:18-24) and runs longer than the KV cache."""
+    from pyxis_b200._native import PyxisError
+    dec = Decoder(SyntheticModel(SMALL, seed=1), qtype="int8", max_seq=16)
+    with pytest.raises(PyxisError):
+        dec.generate([1, SMALL.vocab], 2)
+    with pytest.raises(PyxisError):
+        dec.generate([-1], 2)
+    with pytest.raises(PyxisError):
+        dec.generate(np.zeros(16, np.int32), 2)  # 16 + 2 - 1 > max_seq
+    toks, _ = dec.generate([1, 2], 2)  # the model still works after the rejections
+    assert toks.shape == (2,)
+    dec.close()
