@@ -54,3 +54,35 @@ def test_algorithmic_bytes():
     assert bench.step_bytes() == sum(bench.gemv_bytes(qt, N, K, bs, B) for B in bench.BATCHES
                                      for (_, qt, N, K, bs) in bench.SWEEP)
     assert 0.6e9 < bench.step_bytes() < 0.8e9  # "0.68 GB of packed weights" per step
+
+
+def _fake_smi(tmp_path, lines):
+    script = tmp_path / "nvidia-smi"
+    body = "\n".join(f"echo '{l}'" for l in lines)
+    script.write_text(f"#!/bin/bash\nwhile true; do\n{body}\nsleep 0.05\ndone\n")
+    script.chmod(0o755)
+    return str(tmp_path)
+
+
+def test_clock_sampler_reads_clocks_and_throttle_reasons(tmp_path, monkeypatch):
+    """The clocks record beside every number: median SM clock under load, the maximum, and any
+    throttle reason nvidia-smi reports Active (from a stand-in nvidia-smi on PATH)."""
+    lines = ["0, 1965, 1965, 700.5, 0x0, Not Active, Not Active, Not Active, Not Active",
+             "0, 1800, 1965, 990.1, 0x4, Not Active, Not Active, Not Active, Active",
+             "0, 1700, 1965, 1001.0, 0x8, Active, Not Active, Not Active, Active"]
+    monkeypatch.setenv("PATH", _fake_smi(tmp_path, lines) + os.pathsep + os.environ["PATH"])
+    s = bench.ClockSampler("0")
+    s.start()
+    import time
+    time.sleep(0.5)
+    r = s.stop()
+    assert r["samples"] >= 3 and r["sm_max_mhz"] == 1965.0
+    assert 1700.0 <= r["sm_mhz"] <= 1965.0
+    assert r["reasons"] == ["hw_slowdown", "sw_power_cap"]
+
+
+def test_clock_sampler_without_nvidia_smi(tmp_path, monkeypatch):
+    monkeypatch.setenv("PATH", str(tmp_path))
+    s = bench.ClockSampler(None)
+    s.start()
+    assert s.stop()["reasons"] == ["nvidia-smi unavailable"]
