@@ -160,7 +160,8 @@ def max_over_ranks(x: float, ws: int) -> float:
     import torch
     import torch.distributed as dist
 
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    # NCCL reduces device tensors; the gloo groups of the CPU tests reduce host tensors
+    t = torch.tensor([x], dtype=torch.float64, device="cuda" if dist.get_backend() == "nccl" else "cpu")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 

@@ -86,3 +86,33 @@ def test_clock_sampler_without_nvidia_smi(tmp_path, monkeypatch):
     s = bench.ClockSampler(None)
     s.start()
     assert s.stop()["reasons"] == ["nvidia-smi unavailable"]
+
+
+def _max_worker(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        q.put((rank, bench.max_over_ranks(1.5 + rank * 2.25, world)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_max_over_ranks_world2():
+    """Every rank reports the slowest rank's time: the job's time under torchrun."""
+    import socket
+
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_max_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert got == {0: 3.75, 1: 3.75}
