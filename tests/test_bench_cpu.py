@@ -56,6 +56,20 @@ def test_algorithmic_bytes():
     assert 0.6e9 < bench.step_bytes() < 0.8e9  # "0.68 GB of packed weights" per step
 
 
+def test_decode_and_batch_step_bytes():
+    """The bytes behind the decode GB/s figures, Qwen3-1.7B shape."""
+    from pyxis_b200.model import QWEN3_1_7B as c
+    layer_int8 = 50_331_648 + 81_920          # 7 projections' codes + one f32 scale per row
+    lm_head_int8 = 151936 * 2048 + 151936 * 4
+    kv_per_pos = 28 * 2 * 1024 * 4            # f32 K and V rows of every layer: 229,376 B
+    for pos in (0, 15, 143):
+        # int8 single-sequence step: all weights once, the KV rows 0..pos, one bf16 embedding row
+        assert bench.decode_bytes_per_token(c, pos) == 28 * layer_int8 + lm_head_int8 + kv_per_pos * (pos + 1) + 2 * 2048
+    weights_int4 = 28 * 31_457_280 + 151936 * 2048 * 5 // 8   # codes + group-32 f32 scales, lm_head int4
+    for n_seq, pos in ((1, 0), (64, 2047), (8, 2302)):
+        assert bench.batch_step_bytes(c, n_seq, pos) == weights_int4 + n_seq * kv_per_pos * (pos + 1)
+
+
 def _fake_smi(tmp_path, lines):
     script = tmp_path / "nvidia-smi"
     body = "\n".join(f"echo '{l}'" for l in lines)
