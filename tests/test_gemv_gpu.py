@@ -96,6 +96,24 @@ def test_matmul_dev_strided_rows():
     check_matmul(Y.cpu().numpy(), ref, exact_matmul("int4", od, os_, 32, N, K, Xh))
 
 
+@pytest.mark.parametrize("qt,bs", [("int4", 32), ("int8", 2048)])
+def test_matmul_dev_rows_off_16_byte_boundaries(qt, bs):
+    """x rows that start one float into a buffer cannot be fetched by TMA or 16-byte loads: the
+    calls take the element-wise kernel (also for M >= 16, 8 rows per launch) with the same
+    results."""
+    import torch
+    N, K = 1024, 2048
+    w, od, os_ = make(qt, N, K, bs, seed=23)
+    for M in (1, 3, 20):
+        base = torch.from_numpy(px.synth_normal_f32(40 + M, M * K + 1, 1.0)).cuda()
+        X = base[1:].view(M, K)
+        assert X.data_ptr() % 16 != 0
+        Y = px.matmul_dev(X, w, N, K)
+        torch.cuda.synchronize()
+        Xh = X.cpu().numpy()
+        check_matmul(Y.cpu().numpy(), ref_matmul(qt, od, os_, bs, Xh, N, K), exact_matmul(qt, od, os_, bs, N, K, Xh))
+
+
 def test_argmax_rules():
     import torch
     assert px.argmax([1.0, 3.0, 3.0, 2.0]) == 1
