@@ -52,7 +52,8 @@ typedef enum {
     PYXIS_ECUDA = 3,    /* a CUDA runtime error */
     PYXIS_ENOMEM = 4,   /* device or host allocation failed */
     PYXIS_ETIMEOUT = 5, /* a bounded device-side wait gave up */
-    PYXIS_EUNSUPPORTED = 6
+    PYXIS_EUNSUPPORTED = 6,
+    PYXIS_ENCCL = 7     /* a collective of a multi-GPU communicator failed (pyxis_comm.h) */
 } pyxis_status;
 
 /* Weight layouts (enum Weights arms, src/weights.rs:6-21): the two quantized ones and the two
@@ -171,7 +172,9 @@ const char *pyxis_cuda_matmul_kernel(pyxis_cuda_ctx *ctx, const pyxis_cuda_weigh
  * M rows of n f32 on the device: idx[M] int32 and val[M] f32 (val may be NULL).  `index_base`
  * is added to every index (a vocab shard's first row); with index_base > 0 the row is a shard
  * that does not hold index 0, so a NaN at its start is skipped like any other NaN (the reference's
- * "values[0] NaN wins" rule belongs to the shard with index_base 0).  Asynchronous on `stream`. */
+ * "values[0] NaN wins" rule belongs to the shard with index_base 0).  index_base >= 0 and
+ * index_base + n - 1 <= 2^31 - 1 (the indices are int32), else PYXIS_EINVAL.  Asynchronous on
+ * `stream`. */
 int pyxis_cuda_argmax_dev(pyxis_cuda_ctx *ctx, const float *values, size_t M, size_t n,
                           size_t ld, int64_t index_base, int32_t *idx, float *val, void *stream);
 
@@ -182,9 +185,11 @@ int pyxis_cuda_argmax_dev(pyxis_cuda_ctx *ctx, const float *values, size_t M, si
  *  - Runs on the calling thread's current device, on `stream` (NULL: that device's default
  *    stream); values, idx and val are device pointers, as in pyxis_cuda_argmax_dev.
  *  - Its scratch is a fixed 33 KiB array inside the library's device image (every device that
- *    uses it holds it until the process exits).  The first call on a device looks up that
- *    array's device address (cudaGetSymbolAddress); make the first call on each device before
- *    any stream capture.
+ *    uses it holds it until the process exits).  Every call looks up that array's device
+ *    address on the current device (cudaGetSymbolAddress, which allocates nothing), so a
+ *    device reset by the application does not leave a stale address behind; make the first call
+ *    on each device before any stream capture (it loads the library's module there).
+ *  - index_base >= 0 and index_base + n - 1 <= 2^31 - 1, as for pyxis_cuda_argmax_dev.
  *  - At most 64 rows per call (PYXIS_EINVAL beyond, rows of up to 2^32 - 1 values).
  *  - Every call shares the one array: calls that can overlap on the GPU (different streams
  *    without ordering, several host threads) race and must not be issued that way.

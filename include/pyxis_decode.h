@@ -60,8 +60,9 @@ int pyxis_cuda_model_set_layer(pyxis_cuda_model *m, int layer, const pyxis_cuda_
 int pyxis_cuda_model_set_head(pyxis_cuda_model *m, const uint16_t *embedding_bf16,
                               const pyxis_cuda_weights *lm_head, const float *final_norm);
 
-/* Greedy generation: feeds the n_prompt ids (>= 1), then writes the n_new next tokens to
- * out_tokens.  n_prompt + n_new - 1 <= max_seq.  timing_ms (optional, 2 floats): device time of
+/* Greedy generation: feeds the n_prompt ids, then writes the n_new next tokens to out_tokens.
+ * An empty prompt (n_prompt == 0) is PYXIS_EINVAL, as in pyxis_cuda_model_generate_batch; n_new
+ * == 0 returns PYXIS_OK with nothing written.  n_prompt + n_new - 1 <= max_seq.  timing_ms (optional, 2 floats): device time of
  * the prompt phase (through the first generated token) and of the remaining n_new - 1 steps. */
 int pyxis_cuda_model_generate(pyxis_cuda_model *m, const int32_t *prompt, size_t n_prompt, size_t n_new,
                               int32_t *out_tokens, float *timing_ms);
@@ -79,7 +80,26 @@ int pyxis_cuda_model_generate(pyxis_cuda_model *m, const int32_t *prompt, size_t
 int pyxis_cuda_model_generate_batch(pyxis_cuda_model *m, const int32_t *prompts, size_t n_seq, size_t n_prompt,
                                     size_t n_new, int32_t *out_tokens, float *timing_ms);
 
+/* Diagnostics, no counterpart in the reference: runs the prefill of pyxis_cuda_model_generate_batch
+ * for n_seq prompts of n_prompt ids and writes each sequence's final-norm hidden state of its last
+ * prompt position (the row the lm_head multiplies for the first generated token) to hidden_out
+ * [n_seq][hidden] (host memory).  Not with a vocab-parallel head. */
+int pyxis_cuda_model_prefill_hidden(pyxis_cuda_model *m, const int32_t *prompts, size_t n_seq, size_t n_prompt,
+                                    float *hidden_out);
+
 int pyxis_cuda_model_free(pyxis_cuda_model *m);
+
+/* The decode step's row operations, for known-answer checks of the device arithmetic: the same
+ * device functions the decode kernels apply, run by one CTA on n host values (n <= 65536),
+ * synchronously on the context's stream.
+ *   PYXIS_ROW_RMSNORM  out = RmsNorm::forward(x) with weight w and eps (src/rmsnorm.rs:11-20)
+ *   PYXIS_ROW_ROPE     out = apply_rope on every head_dim-wide head of x at `pos` with `theta`
+ *                      (src/attention.rs:144-162; the table from pyxis_rope_table)
+ *   PYXIS_ROW_SILU     out[i] = silu(x[i]) (src/ffn.rs:52-54)
+ * Unused arguments are ignored. */
+enum { PYXIS_ROW_RMSNORM = 1, PYXIS_ROW_ROPE = 2, PYXIS_ROW_SILU = 3 };
+int pyxis_cuda_row_op(pyxis_cuda_ctx *ctx, int op, const float *x, size_t n, const float *w, float eps,
+                      int head_dim, int pos, float theta, float *out);
 
 /* The RoPE table the model uses: cos/sin[pos * (head_dim/2) + i] of pos * theta^(-2i/head_dim),
  * computed on the host in f32 exactly as src/attention.rs:151-154 does. */

@@ -1,4 +1,5 @@
-"""ctypes binding of libpyxis_cuda.so (include/pyxis_cuda.h, include/pyxis_synth.h).
+"""ctypes binding of libpyxis_cuda.so (include/pyxis_cuda.h, pyxis_decode.h, pyxis_comm.h,
+include/pyxis_synth.h).
 
 The library is built in-tree by ``pyxis_b200.build``.  There is no fallback: if the shared
 library is missing or cannot be loaded, importing the CUDA path raises.
@@ -18,6 +19,7 @@ PYXIS_ECUDA = 3
 PYXIS_ENOMEM = 4
 PYXIS_ETIMEOUT = 5
 PYXIS_EUNSUPPORTED = 6
+PYXIS_ENCCL = 7
 
 QTYPE_INT8 = 1
 QTYPE_INT4 = 2
@@ -60,6 +62,15 @@ SIGNATURES = {
     "pyxis_cuda_model_generate_batch": (C.c_int, [_vp, _vp, _sz, _sz, _sz, _vp, _vp]),
     "pyxis_cuda_model_free": (C.c_int, [_vp]),
     "pyxis_rope_table": (C.c_int, [C.c_float, C.c_int, C.c_int, _vp, _vp]),
+    "pyxis_cuda_row_op": (C.c_int, [_vp, C.c_int, _vp, _sz, _vp, C.c_float, C.c_int, C.c_int, C.c_float, _vp]),
+    "pyxis_cuda_model_prefill_hidden": (C.c_int, [_vp, _vp, _sz, _sz, _vp]),
+    "pyxis_cuda_comm_unique_id": (C.c_int, [_vp]),
+    "pyxis_cuda_comm_init": (C.c_int, [_vp, _vp, C.c_int, C.c_int, C.POINTER(_vp)]),
+    "pyxis_cuda_comm_info": (C.c_int, [_vp, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+    "pyxis_cuda_comm_free": (C.c_int, [_vp]),
+    "pyxis_cuda_head_greedy_dev": (C.c_int, [_vp, _vp, _sz, _sz, _sz, _sz, _vp, _sz, _sz, _vp, _vp]),
+    "pyxis_cuda_head_reserve": (C.c_int, [_vp, _sz, _sz]),
+    "pyxis_cuda_model_set_vocab_parallel": (C.c_int, [_vp, _vp, _vp, _sz, _sz]),
     "pyxis_synth_normal_f32": (None, [C.c_uint64, _sz, C.c_float, _vp]),
     "pyxis_synth_normal_bf16": (None, [C.c_uint64, _sz, C.c_float, _vp]),
     "pyxis_synth_tokens": (None, [C.c_uint64, _sz, C.c_uint32, _vp]),

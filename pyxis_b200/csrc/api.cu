@@ -55,7 +55,7 @@ struct DeviceGuard {
 size_t div_ceil(size_t a, size_t b) { return (a + b - 1) / b; }
 
 constexpr size_t kTcMinRows = 16;        // matmul_dev rows from which the tensor-core GEMM runs
-constexpr size_t kTcGemvMinRows = 32768;  // out_features from which int8 GEMVs use tensor cores
+constexpr size_t kTcGemvMinRows = 16384;  // out_features from which int8 GEMVs use tensor cores
 
 bool is_dense(int qtype) { return qtype == PYXIS_QTYPE_F32 || qtype == PYXIS_QTYPE_BF16; }
 bool is_qtype(int qtype) { return qtype >= PYXIS_QTYPE_INT8 && qtype <= PYXIS_QTYPE_BF16; }
@@ -494,6 +494,8 @@ int pyxis_cuda_argmax_dev(pyxis_cuda_ctx *ctx, const float *values, size_t M, si
     if (M > (size_t)kArgmaxMaxRows) return fail(PYXIS_EINVAL, "argmax: %zu rows > %d per call", M, kArgmaxMaxRows);
     if (M > 1 && ld < n) return fail(PYXIS_EINVAL, "row stride smaller than the row");
     if (!values || !idx) return fail(PYXIS_EINVAL, "null values or idx");
+    if (index_base < 0 || index_base + (int64_t)n - 1 > (int64_t)INT32_MAX)
+        return fail(PYXIS_EINVAL, "argmax: index_base + n - 1 outside [0, 2^31 - 1] (the int32 index)");
     DeviceGuard g(ctx->device);
     cudaError_t e = launch_argmax_scratch(values, M, n, ld, index_base, idx, val, ctx->amax, ctx->num_sms,
                                           pick_stream(ctx, stream));

@@ -11,6 +11,9 @@
 // in any order.  One launch: each CTA writes its segment's key to scratch, and the last CTA to
 // finish a row (atomic ticket) reduces the row's keys and re-arms the ticket to 0 for the next
 // launch.  Scratch: ArgmaxScratch, zeroed once when it is allocated.
+// For a vocab shard of a multi-GPU head the kernel can instead write each row's key with the
+// global index in its low word (key_out): the maximum of the shards' keys is then the global
+// answer, a NaN at global index 0 being the all-ones key.
 #include "argmax.h"
 #include "common.cuh"
 #include "kernels.h"
@@ -49,7 +52,7 @@ PYXIS_DEVINL uint64_t cta_max_u64(uint64_t k, uint64_t *red) {
 
 __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(
     const float *__restrict__ values, size_t n, size_t ld, int64_t index_base,
-    int32_t *__restrict__ idx_out, float *__restrict__ val_out, ArgmaxScratch s) {
+    int32_t *__restrict__ idx_out, float *__restrict__ val_out, uint64_t *__restrict__ key_out, ArgmaxScratch s) {
     __shared__ uint64_t red[kArgmaxThreads / 32];
     __shared__ bool last;
     pdl_wait();
@@ -84,9 +87,15 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(
         uint32_t i = 0xFFFFFFFFu - (uint32_t)(m & 0xFFFFFFFFu);
         // values[0] NaN wins -- when this row starts the vector (index_base 0); a vocab shard
         // that starts later ignores NaNs like every other position.  All-NaN -> first index.
-        if ((index_base == 0 && isnan(v[0])) || m == 0) i = 0;
-        idx_out[row] = (int32_t)(index_base + (int64_t)i);
-        if (val_out) val_out[row] = v[i];
+        const bool nan0 = index_base == 0 && isnan(v[0]);
+        if (nan0 || m == 0) i = 0;
+        if (key_out) {
+            const uint32_t g = (uint32_t)(index_base + (int64_t)i);
+            key_out[row] = nan0 ? ~0ull : m == 0 ? 0ull : ((m & 0xFFFFFFFF00000000ull) | (uint64_t)(0xFFFFFFFFu - g));
+        } else {
+            idx_out[row] = (int32_t)(index_base + (int64_t)i);
+            if (val_out) val_out[row] = v[i];
+        }
         s.ticket[row] = 0;  // re-arm for the next launch on this scratch
     }
 }
@@ -107,7 +116,38 @@ cudaError_t launch_argmax_scratch(const float *values, size_t M, size_t n, size_
                                   const ArgmaxScratch &s, int num_sms, cudaStream_t st) {
     if (M == 0) return cudaSuccess;
     dim3 grid(argmax_ctas_per_row(n, num_sms), (unsigned)M);
-    return launch_kernel(argmax_kernel, grid, dim3(kArgmaxThreads), 0, st, values, n, ld, index_base, idx, val, s);
+    return launch_kernel(argmax_kernel, grid, dim3(kArgmaxThreads), 0, st, values, n, ld, index_base, idx, val,
+                         (uint64_t *)nullptr, s);
+}
+
+cudaError_t launch_argmax_keys(const float *values, size_t M, size_t n, size_t ld, int64_t index_base,
+                               uint64_t *keys, const ArgmaxScratch &s, int num_sms, cudaStream_t st) {
+    if (M == 0) return cudaSuccess;
+    dim3 grid(argmax_ctas_per_row(n, num_sms), (unsigned)M);
+    return launch_kernel(argmax_kernel, grid, dim3(kArgmaxThreads), 0, st, values, n, ld, index_base,
+                         (int32_t *)nullptr, (float *)nullptr, keys, s);
+}
+
+// tokens[r] = the index in the largest of the nranks keys of row row0 + r (keys_all [nranks][rows]).
+__global__ void pick_keys_kernel(const uint64_t *__restrict__ keys_all, int nranks, int rows, int row0, int nrows,
+                                 int32_t *__restrict__ tokens) {
+    pdl_wait();
+    pdl_trigger();
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= nrows) return;
+    uint64_t m = 0;
+    for (int w = 0; w < nranks; ++w) {
+        const uint64_t k = keys_all[(size_t)w * rows + row0 + r];
+        m = k > m ? k : m;
+    }
+    tokens[r] = m == 0 ? 0 : (int32_t)(0xFFFFFFFFu - (uint32_t)(m & 0xFFFFFFFFu));
+}
+
+cudaError_t launch_pick_keys(const uint64_t *keys_all, int nranks, int rows, int row0, int nrows, int32_t *tokens,
+                             cudaStream_t st) {
+    if (nrows <= 0) return cudaSuccess;
+    return launch_kernel(pick_keys_kernel, dim3((nrows + 127) / 128), dim3(128), 0, st, keys_all, nranks, rows, row0,
+                         nrows, tokens);
 }
 
 }  // namespace pyxis

@@ -31,4 +31,16 @@ cudaError_t launch_argmax_scratch(const float *values, size_t M, size_t n, size_
                                   int64_t index_base, int32_t *idx, float *val,
                                   const ArgmaxScratch &s, int num_sms, cudaStream_t st);
 
+// The same scan writing one 64-bit key per row instead of (idx, val): order-preserving value
+// bits << 32 | (0xFFFFFFFF - (index_base + first index of the maximum)); 0 for a row of NaNs
+// only; all ones for a NaN at global index 0 (index_base 0).  The maximum of several shards' keys
+// of one row is the key of the whole row's first maximum.
+cudaError_t launch_argmax_keys(const float *values, size_t M, size_t n, size_t ld, int64_t index_base,
+                               uint64_t *keys, const ArgmaxScratch &s, int num_sms, cudaStream_t st);
+
+// tokens[r] for r < nrows: the index in the largest key of row row0 + r over keys_all
+// [nranks][rows] (0 when every key is 0).
+cudaError_t launch_pick_keys(const uint64_t *keys_all, int nranks, int rows, int row0, int nrows, int32_t *tokens,
+                             cudaStream_t st);
+
 }  // namespace pyxis

@@ -1,8 +1,6 @@
 // argmax_noalloc.cu -- the row-wise argmax of argmax.cu for callers that cannot allocate device
 // memory: its scratch lives in a fixed array in the library's own device image instead of in a
 // context (see pyxis_cuda_argmax_noalloc in include/pyxis_cuda.h).
-#include <mutex>
-
 #include "../../include/pyxis_cuda.h"
 #include "argmax.h"
 #include "kernels.h"
@@ -20,24 +18,14 @@ constexpr size_t kScratchBytes = kPartialBytes + kNoAllocMaxRows * sizeof(unsign
 // cudaGetSymbolAddress below.
 static __device__ __align__(256) unsigned char g_argmax_scratch[kScratchBytes];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_setup_mu;
-void *g_scratch_addr[kMaxDevices] = {};
-
-// Device address of g_argmax_scratch on the current device, looked up once per device.
+// Device address of g_argmax_scratch on the current device.  Looked up on every call
+// (cudaGetSymbolAddress allocates nothing): an address kept from an earlier call would be stale
+// after the application resets the device (cudaDeviceReset) and its context is re-created.
 cudaError_t scratch_for_current_device(void **out) {
-    int dev = -1;
-    cudaError_t e = cudaGetDevice(&dev);
+    void *ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_argmax_scratch);
     if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-    std::lock_guard<std::mutex> lk(g_setup_mu);
-    if (!g_scratch_addr[dev]) {
-        void *ptr = nullptr;
-        e = cudaGetSymbolAddress(&ptr, g_argmax_scratch);
-        if (e != cudaSuccess) return e;
-        g_scratch_addr[dev] = ptr;
-    }
-    *out = g_scratch_addr[dev];
+    *out = ptr;
     return cudaSuccess;
 }
 
@@ -54,6 +42,8 @@ extern "C" int pyxis_cuda_argmax_noalloc(const float *values, size_t M, size_t n
     if (n > 0xFFFFFFFFull) return record_error(PYXIS_EINVAL, "pyxis_cuda_argmax_noalloc: row longer than 2^32 - 1");
     if (M > 1 && ld < n) return record_error(PYXIS_EINVAL, "pyxis_cuda_argmax_noalloc: row stride smaller than the row");
     if (!values || !idx) return record_error(PYXIS_EINVAL, "pyxis_cuda_argmax_noalloc: null values or idx");
+    if (index_base < 0 || index_base + (int64_t)n - 1 > (int64_t)INT32_MAX)
+        return record_error(PYXIS_EINVAL, "pyxis_cuda_argmax_noalloc: index_base + n - 1 outside [0, 2^31 - 1]");
     void *base = nullptr;
     cudaError_t e = scratch_for_current_device(&base);
     if (e != cudaSuccess) return record_error(PYXIS_ECUDA, cudaGetErrorString(e));

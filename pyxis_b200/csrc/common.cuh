@@ -94,6 +94,20 @@ PYXIS_DEVINL float warp_sum(float v) {
 
 PYXIS_DEVINL float bf16_bits_to_f32(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
 
+// ---- the decode step's row arithmetic, one definition for every kernel that applies it --------
+// RMSNorm (src/rmsnorm.rs:11-20): factor = 1 / sqrt(sum(x^2) / n + eps), then x * (factor * w).
+PYXIS_DEVINL float rms_factor(float sumsq, int n, float eps) {
+    return __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(sumsq, (float)n), eps)));
+}
+PYXIS_DEVINL float rms_scale(float v, float factor, float w) { return __fmul_rn(v, __fmul_rn(factor, w)); }
+// SiLU (src/ffn.rs:52-54): x / (1 + exp(-x)).
+PYXIS_DEVINL float silu_f(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))); }
+// RoPE (src/attention.rs:144-162) of element i of a head and its partner i +- head_dim / 2 at
+// angle pos * theta^(-2i / head_dim): x c - y s for the first half, x c + y s for the second.
+PYXIS_DEVINL float rope_rot(float v, float other, float c, float s, bool first_half) {
+    return first_half ? __fsub_rn(__fmul_rn(v, c), __fmul_rn(other, s)) : __fadd_rn(__fmul_rn(v, c), __fmul_rn(other, s));
+}
+
 // ---- programmatic dependent launch ---------------------------------------------------------
 // A kernel launched with programmatic stream serialization may start while its predecessor is
 // still running; pdl_wait() blocks until the predecessor has completed and its writes are

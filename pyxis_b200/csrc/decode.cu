@@ -83,11 +83,11 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float *__rest
         }
     }
     ss = block_sum(ss, red);
-    const float factor = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
+    const float factor = rms_factor(ss, n, eps);
 #pragma unroll
     for (int j = 0; j < kNormPer; ++j) {
         const int i = threadIdx.x + j * kNormThreads;
-        if (i < n) h[i] = __fmul_rn(v[j], __fmul_rn(factor, wv[j]));
+        if (i < n) h[i] = rms_scale(v[j], factor, wv[j]);
     }
 }
 
@@ -341,7 +341,7 @@ __global__ void silu_mul_kernel(const float *__restrict__ gu, int ffn, float *__
     pdl_trigger();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ffn; i += gridDim.x * blockDim.x) {
         const float g = gu[i];
-        act[i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), gu[ffn + i]);
+        act[i] = __fmul_rn(silu_f(g), gu[ffn + i]);
     }
 }
 
@@ -542,6 +542,76 @@ extern "C" int pyxis_rope_table(float theta, int head_dim, int max_pos, float *c
     return PYXIS_OK;
 }
 
+namespace pyxis {
+
+// One CTA applies one of the decode step's row operations to n values with the device helpers
+// the decode kernels use (rms_factor / rms_scale, rope_rot, silu_f): the known-answer checks of
+// the device arithmetic.  RMSNorm sums x^2 over a CTA reduction like the row kernels do.
+__global__ void row_op_kernel(int op, const float *__restrict__ x, int n, const float *__restrict__ w, float eps,
+                              const float *__restrict__ rcos, const float *__restrict__ rsin, int head_dim, int pos,
+                              float *__restrict__ out) {
+    __shared__ float red[32];
+    if (op == PYXIS_ROW_RMSNORM) {
+        float ss = 0.f;
+        for (int i = threadIdx.x; i < n; i += blockDim.x) ss = __fadd_rn(ss, __fmul_rn(x[i], x[i]));
+        ss = warp_sum(ss);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+        __syncthreads();
+        float tot = 0.f;
+        for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot = __fadd_rn(tot, red[i]);
+        const float factor = rms_factor(tot, n, eps);
+        for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = rms_scale(x[i], factor, w[i]);
+    } else if (op == PYXIS_ROW_ROPE) {
+        const int half = head_dim / 2;
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            const int j = i % head_dim, base = i - j;
+            const bool first = j < half;
+            const int pair = first ? j : j - half;
+            const float other = x[base + (first ? j + half : j - half)];
+            out[i] = rope_rot(x[i], other, rcos[(size_t)pos * half + pair], rsin[(size_t)pos * half + pair], first);
+        }
+    } else {
+        for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = silu_f(x[i]);
+    }
+}
+
+}  // namespace pyxis
+
+extern "C" int pyxis_cuda_row_op(pyxis_cuda_ctx *ctx, int op, const float *x, size_t n, const float *w, float eps,
+                                 int head_dim, int pos, float theta, float *out) {
+    if (!ctx || !x || !out) return model_fail(PYXIS_EINVAL, "null argument");
+    if (op != PYXIS_ROW_RMSNORM && op != PYXIS_ROW_ROPE && op != PYXIS_ROW_SILU)
+        return model_fail(PYXIS_EINVAL, "pyxis_cuda_row_op: unknown op");
+    if (n == 0) return PYXIS_OK;
+    if (n > 65536) return model_fail(PYXIS_EINVAL, "pyxis_cuda_row_op: more than 65536 values");
+    if (op == PYXIS_ROW_RMSNORM && !w) return model_fail(PYXIS_EINVAL, "pyxis_cuda_row_op: RMSNorm needs a weight");
+    if (op == PYXIS_ROW_ROPE && (head_dim <= 0 || head_dim % 2 || n % (size_t)head_dim || pos < 0 || pos > 1 << 20))
+        return model_fail(PYXIS_EINVAL, "pyxis_cuda_row_op: RoPE needs whole heads of even head_dim and pos >= 0");
+    Guard g(ctx->device);
+    const size_t half = op == PYXIS_ROW_ROPE ? (size_t)head_dim / 2 : 0;
+    const size_t ntab = (size_t)(pos + 1) * half;
+    std::vector<float> cs(ntab), sn(ntab);
+    if (op == PYXIS_ROW_ROPE) pyxis_rope_table(theta, head_dim, pos + 1, cs.data(), sn.data());
+    float *d = nullptr;
+    const size_t total = 3 * n + 2 * ntab;
+    cudaError_t e = cudaMalloc(&d, total * sizeof(float));
+    if (e != cudaSuccess) return model_fail(PYXIS_ENOMEM, cudaGetErrorString(e));
+    float *dx = d, *dw = d + n, *dout = d + 2 * n, *dc = d + 3 * n, *ds = dc + ntab;
+    e = cudaMemcpy(dx, x, n * sizeof(float), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && op == PYXIS_ROW_RMSNORM) e = cudaMemcpy(dw, w, n * sizeof(float), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && ntab) e = cudaMemcpy(dc, cs.data(), ntab * sizeof(float), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && ntab) e = cudaMemcpy(ds, sn.data(), ntab * sizeof(float), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) {
+        pyxis::row_op_kernel<<<1, 256, 0, ctx->stream>>>(op, dx, (int)n, dw, eps, dc, ds, head_dim, pos, dout);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e == cudaSuccess) e = cudaMemcpy(out, dout, n * sizeof(float), cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    if (e != cudaSuccess) return model_fail(PYXIS_ECUDA, cudaGetErrorString(e));
+    return PYXIS_OK;
+}
+
 extern "C" int pyxis_cuda_model_create(pyxis_cuda_ctx *ctx, const pyxis_model_config *cfg, pyxis_cuda_model **out) {
     if (!ctx || !cfg || !out) return model_fail(PYXIS_EINVAL, "null argument");
     *out = nullptr;
@@ -655,7 +725,8 @@ extern "C" int pyxis_cuda_model_set_head(pyxis_cuda_model *m, const uint16_t *em
                                          const pyxis_cuda_weights *lm_head, const float *final_norm) {
     if (!m || !embedding_bf16 || !final_norm) return model_fail(PYXIS_EINVAL, "null argument");
     const pyxis_model_config &c = m->cfg;
-    if (!weights_ok(lm_head, (size_t)c.vocab * c.hidden, m->ctx->device))
+    // NULL lm_head: a vocab-parallel model that holds only its shard (pyxis_comm.h)
+    if (lm_head && !weights_ok(lm_head, (size_t)c.vocab * c.hidden, m->ctx->device))
         return model_fail(PYXIS_EINVAL, "pyxis_cuda_model_set_head: lm_head has the wrong length or device");
     Guard g(m->ctx->device);
     m->lm_head = lm_head;
@@ -672,7 +743,8 @@ extern "C" int pyxis_cuda_model_set_head(pyxis_cuda_model *m, const uint16_t *em
 extern "C" int pyxis_cuda_model_generate(pyxis_cuda_model *m, const int32_t *prompt, size_t n_prompt, size_t n_new,
                                          int32_t *out_tokens, float *timing_ms) {
     if (!m || !prompt || !out_tokens) return model_fail(PYXIS_EINVAL, "null argument");
-    if (n_prompt == 0 || n_new == 0) return PYXIS_OK;
+    if (n_prompt == 0) return model_fail(PYXIS_EINVAL, "pyxis_cuda_model_generate: empty prompt");
+    if (n_new == 0) return PYXIS_OK;
     const pyxis_model_config &c = m->cfg;
     if (n_prompt + n_new - 1 > (size_t)c.max_seq) return model_fail(PYXIS_EINVAL, "prompt + new tokens exceed max_seq");
     for (size_t i = 0; i < n_prompt; ++i)

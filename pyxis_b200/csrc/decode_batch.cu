@@ -19,6 +19,7 @@
 
 #include "../../include/pyxis_decode.h"
 #include "argmax.h"
+#include "comm.h"
 #include "common.cuh"
 #include "ctx.h"
 #include "heads.cuh"
@@ -88,15 +89,15 @@ __global__ void __launch_bounds__(kRowThreads)
     __syncthreads();
     float tot = 0.f;
     for (int i = 0; i < kRowThreads / 32; ++i) tot = __fadd_rn(tot, red[i]);
-    const float factor = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)n), eps)));
+    const float factor = rms_factor(tot, n, eps);
     float4 *hr = reinterpret_cast<float4 *>(h + (size_t)blockIdx.x * n);
 #pragma unroll
     for (int u = 0; u < kRowQuads; ++u) {
         const int k = threadIdx.x + u * kRowThreads;
         if (k < nq) {
             const float4 ww = w4[k];
-            hr[k] = make_float4(__fmul_rn(v[u].x, __fmul_rn(factor, ww.x)), __fmul_rn(v[u].y, __fmul_rn(factor, ww.y)),
-                                __fmul_rn(v[u].z, __fmul_rn(factor, ww.z)), __fmul_rn(v[u].w, __fmul_rn(factor, ww.w)));
+            hr[k] = make_float4(rms_scale(v[u].x, factor, ww.x), rms_scale(v[u].y, factor, ww.y),
+                                rms_scale(v[u].z, factor, ww.z), rms_scale(v[u].w, factor, ww.w));
         }
     }
 }
@@ -142,7 +143,7 @@ __global__ void silu_rows_kernel(const float *__restrict__ gu, int ffn, float *_
     if (i >= ffn) return;
     const float *row = gu + (size_t)r * 2 * ffn;
     const float g = row[i];
-    act[(size_t)r * ffn + i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), row[ffn + i]);
+    act[(size_t)r * ffn + i] = __fmul_rn(silu_f(g), row[ffn + i]);
 }
 
 // out[b][step] = tokens[b] for every sequence, then step += 1 and pos += 1 (one CTA).
@@ -319,6 +320,9 @@ struct BatchState {
     // decode rows (n_seq)
     float *dx = nullptr, *dh = nullptr, *dqkv = nullptr, *dattn = nullptr, *dtmp = nullptr, *dgu = nullptr,
           *dact = nullptr, *dlogits = nullptr;
+    // vocab-parallel head: every rank's final hidden rows [nranks][n_seq][hidden]
+    float *xall = nullptr;
+    int vp_ranks = 0;
     float *part = nullptr;
     unsigned *tickets = nullptr;
     int *d_prompt = nullptr, *d_tokens = nullptr, *d_out = nullptr, *d_pos = nullptr, *d_step = nullptr;
@@ -374,6 +378,16 @@ int ensure_state(pyxis_cuda_model *m, int n_seq, int n_prompt, int n_new) {
                                std::tuple{L.wdown, H, ffn}})
             if (w) ws = std::max(ws, gemm_tc_workspace_bytes_splitk(n_seq, N, K, w->block_size == K, w->block_size,
                                                                     m->ctx->num_sms));
+    pyxis_cuda_comm *vp = m->vp_comm;
+    const size_t head_rows = vp ? (size_t)vp->nranks * n_seq : (size_t)n_seq;
+    if (vp) {
+        ws = std::max(ws, gemm_tc_workspace_bytes(head_rows, H));
+        ws = std::max(ws, gemm_tc_workspace_bytes_splitk(head_rows, m->vp_rows, H, m->vp_shard->block_size == H,
+                                                         m->vp_shard->block_size, m->ctx->num_sms));
+    } else if (m->lm_head) {
+        ws = std::max(ws, gemm_tc_workspace_bytes_splitk(n_seq, c.vocab, H, m->lm_head->block_size == H,
+                                                         m->lm_head->block_size, m->ctx->num_sms));
+    }
     b->ws_bytes = ws;
     cudaError_t e = cudaSuccess;
     auto A = [&](auto **p, size_t count) {
@@ -402,7 +416,12 @@ int ensure_state(pyxis_cuda_model *m, int n_seq, int n_prompt, int n_new) {
     A(&b->dtmp, (size_t)n_seq * H);
     A(&b->dgu, (size_t)n_seq * 2 * ffn);
     A(&b->dact, (size_t)n_seq * ffn);
-    A(&b->dlogits, (size_t)n_seq * c.vocab);
+    if (vp) {
+        A(&b->xall, head_rows * H);
+        b->vp_ranks = vp->nranks;
+    } else {
+        A(&b->dlogits, (size_t)n_seq * c.vocab);
+    }
     A(&b->part, (size_t)n_seq * c.n_kv_heads * b->splits * G * (c.head_dim + 2));
     A(&b->tickets, (size_t)n_seq * c.n_kv_heads);
     A(&b->d_prompt, (size_t)n_seq * n_prompt);
@@ -424,6 +443,13 @@ int ensure_state(pyxis_cuda_model *m, int n_seq, int n_prompt, int n_new) {
         cudaGetLastError();
         return batch_fail(PYXIS_ENOMEM, cudaGetErrorString(e));
     }
+    if (vp) {
+        const int rc = head_reserve(vp, head_rows, m->vp_rows);
+        if (rc) {
+            free_batch_state(b);
+            return rc;
+        }
+    }
     m->batch = b;
     return PYXIS_OK;
 }
@@ -433,6 +459,27 @@ int ensure_state(pyxis_cuda_model *m, int n_seq, int n_prompt, int n_new) {
         cudaError_t e_ = (expr);                                                  \
         if (e_ != cudaSuccess) return batch_fail(PYXIS_ECUDA, cudaGetErrorString(e_)); \
     } while (0)
+
+// Next tokens of the n_seq rows of b->dh: the lm_head and argmax on this GPU, or (vocab-parallel)
+// every rank's rows all-gathered, this rank's vocab shard, the keys' all-gather and the pick of
+// this rank's rows.
+int enqueue_head(pyxis_cuda_model *m, int n_seq, cudaStream_t st) {
+    const pyxis_model_config &c = m->cfg;
+    BatchState *b = m->batch;
+    const int H = c.hidden;
+    pyxis_cuda_ctx *ctx = m->ctx;
+    if (pyxis_cuda_comm *vp = m->vp_comm) {
+        int rc = comm_allgather(vp, b->dh, b->xall, (size_t)n_seq * H, false, st);
+        if (rc) return rc;
+        return head_greedy_enqueue(vp, m->vp_shard, m->vp_lo, m->vp_rows, H, b->xall, (size_t)vp->nranks * n_seq, H,
+                                   vp->rank * n_seq, n_seq, b->d_tokens, b->ws, b->ws_bytes, st);
+    }
+    int rc = run_matmul(ctx, m->lm_head, b->dh, n_seq, H, c.vocab, H, b->dlogits, c.vocab, b->ws, b->ws_bytes, st);
+    if (rc) return rc;
+    PX_TRY(launch_argmax_scratch(b->dlogits, n_seq, c.vocab, c.vocab, 0, b->d_tokens, nullptr, ctx->amax, ctx->num_sms,
+                                 st));
+    return PYXIS_OK;
+}
 
 // All prompt positions of every sequence: the layers over `chunk` sequences at a time, then the
 // lm_head over each sequence's last position and the argmax -> the first generated tokens.
@@ -490,10 +537,8 @@ int enqueue_prefill(pyxis_cuda_model *m, int n_seq, int P, cudaStream_t st) {
                              (const float *)b->ptmp, (const float *)m->final_norm, b->dh + (size_t)s0 * H, H,
                              c.rms_eps, P, P - 1));
     }
-    int rc = run_matmul(ctx, m->lm_head, b->dh, n_seq, H, c.vocab, H, b->dlogits, c.vocab, b->ws, b->ws_bytes, st);
+    int rc = enqueue_head(m, n_seq, st);
     if (rc) return rc;
-    PX_TRY(launch_argmax_scratch(b->dlogits, n_seq, c.vocab, c.vocab, 0, b->d_tokens, nullptr, ctx->amax, ctx->num_sms,
-                                 st));
     PX_TRY(launch_kernel(advance_rows_kernel, dim3(1), dim3(256), 0, st, (const int *)b->d_tokens, n_seq, b->n_new,
                          b->d_out, b->d_pos, b->d_step));
     return PYXIS_OK;
@@ -534,10 +579,8 @@ int enqueue_step(pyxis_cuda_model *m, int n_seq, cudaStream_t st) {
     }
     PX_TRY(launch_kernel(add_rmsnorm_rows_kernel, dim3(n_seq), dim3(kRowThreads), 0, st, b->dx, (const float *)b->dtmp,
                          (const float *)m->final_norm, b->dh, H, c.rms_eps, 1, 0));
-    int rc = run_matmul(ctx, m->lm_head, b->dh, n_seq, H, c.vocab, H, b->dlogits, c.vocab, b->ws, b->ws_bytes, st);
+    int rc = enqueue_head(m, n_seq, st);
     if (rc) return rc;
-    PX_TRY(launch_argmax_scratch(b->dlogits, n_seq, c.vocab, c.vocab, 0, b->d_tokens, nullptr, ctx->amax, ctx->num_sms,
-                                 st));
     PX_TRY(launch_kernel(advance_rows_kernel, dim3(1), dim3(256), 0, st, (const int *)b->d_tokens, n_seq, b->n_new,
                          b->d_out, b->d_pos, b->d_step));
     return PYXIS_OK;
@@ -566,10 +609,10 @@ void free_batch_state(BatchState *b) {
 
 using namespace pyxis;
 
-extern "C" int pyxis_cuda_model_generate_batch(pyxis_cuda_model *m, const int32_t *prompts, size_t n_seq,
-                                               size_t n_prompt, size_t n_new, int32_t *out_tokens, float *timing_ms) {
-    if (!m || !prompts || !out_tokens) return batch_fail(PYXIS_EINVAL, "null argument");
-    if (n_seq == 0 || n_new == 0) return PYXIS_OK;
+namespace {
+
+// The host-side checks of pyxis_cuda_model_generate_batch (PYXIS_OK or a recorded error).
+int check_batch_args(const pyxis_cuda_model *m, const int32_t *prompts, size_t n_seq, size_t n_prompt, size_t n_new) {
     const pyxis_model_config &c = m->cfg;
     if (n_prompt == 0) return batch_fail(PYXIS_EINVAL, "pyxis_cuda_model_generate_batch: empty prompts");
     if (n_prompt + n_new - 1 > (size_t)c.max_seq)
@@ -582,9 +625,55 @@ extern "C" int pyxis_cuda_model_generate_batch(pyxis_cuda_model *m, const int32_
         if (prompts[i] < 0 || prompts[i] >= c.vocab) return batch_fail(PYXIS_EINVAL, "token id out of range");
     for (const auto &L : m->layers)
         if (!L.wqkv) return batch_fail(PYXIS_EINVAL, "a layer has no weights");
-    if (!m->lm_head) return batch_fail(PYXIS_EINVAL, "no lm_head");
+    if (!m->lm_head && !m->vp_comm) return batch_fail(PYXIS_EINVAL, "no lm_head");
+    if (m->vp_comm && (size_t)m->vp_comm->nranks * n_seq > (size_t)kArgmaxMaxRows)
+        return batch_fail(PYXIS_EINVAL, "vocab-parallel generate_batch: more than 1024 sequences over all ranks");
+    return PYXIS_OK;
+}
+
+// Vocab-parallel mode: the ranks exchange (n_seq, n_prompt, n_new, local verdict) before any other
+// collective, so that all of them go on, or all of them return PYXIS_EINVAL, together.
+int agree_batch_args(pyxis_cuda_model *m, size_t n_seq, size_t n_prompt, size_t n_new, int local_rc) {
+    pyxis_cuda_comm *vp = m->vp_comm;
+    const int W = vp->nranks;
+    uint64_t *d = nullptr;
+    std::vector<uint64_t> all((size_t)W * 4);
+    const uint64_t mine[4] = {n_seq, n_prompt, n_new, (uint64_t)local_rc};
+    cudaError_t ce = cudaMalloc(&d, (size_t)(W + 1) * 4 * sizeof(uint64_t));
+    if (ce != cudaSuccess) return batch_fail(PYXIS_ECUDA, cudaGetErrorString(ce));
+    ce = cudaMemcpyAsync(d, mine, sizeof mine, cudaMemcpyHostToDevice, m->ctx->stream);
+    int rc = ce == cudaSuccess ? comm_allgather(vp, d, d + 4, 4, true, m->ctx->stream) : PYXIS_ECUDA;
+    if (rc == PYXIS_OK) {
+        ce = cudaMemcpyAsync(all.data(), d + 4, all.size() * sizeof(uint64_t), cudaMemcpyDeviceToHost, m->ctx->stream);
+        if (ce == cudaSuccess) ce = cudaStreamSynchronize(m->ctx->stream);
+        if (ce != cudaSuccess) rc = PYXIS_ECUDA;
+    }
+    cudaFree(d);
+    if (rc == PYXIS_ECUDA) return batch_fail(PYXIS_ECUDA, cudaGetErrorString(ce));
+    if (rc) return rc;
+    if (local_rc) return local_rc;  // this rank's own message stays the recorded one
+    for (int r = 0; r < W; ++r) {
+        const uint64_t *a = &all[(size_t)r * 4];
+        if (a[3] != 0)
+            return batch_fail(PYXIS_EINVAL, "vocab-parallel generate_batch: another rank's arguments failed its checks");
+        if (a[0] != n_seq || a[1] != n_prompt || a[2] != n_new)
+            return batch_fail(PYXIS_EINVAL,
+                              "vocab-parallel generate_batch: the ranks passed different n_seq, n_prompt or n_new");
+    }
+    return PYXIS_OK;
+}
+
+}  // namespace
+
+extern "C" int pyxis_cuda_model_generate_batch(pyxis_cuda_model *m, const int32_t *prompts, size_t n_seq,
+                                               size_t n_prompt, size_t n_new, int32_t *out_tokens, float *timing_ms) {
+    if (!m || !prompts || !out_tokens) return batch_fail(PYXIS_EINVAL, "null argument");
+    if (n_seq == 0 || n_new == 0) return PYXIS_OK;
+    int rc = check_batch_args(m, prompts, n_seq, n_prompt, n_new);
     DevGuard g(m->ctx->device);
-    int rc = ensure_state(m, (int)n_seq, (int)n_prompt, (int)n_new);
+    if (m->vp_comm) rc = agree_batch_args(m, n_seq, n_prompt, n_new, rc);
+    if (rc) return rc;
+    rc = ensure_state(m, (int)n_seq, (int)n_prompt, (int)n_new);
     if (rc) return rc;
     BatchState *b = m->batch;
     cudaStream_t st = m->ctx->stream;
@@ -638,5 +727,60 @@ extern "C" int pyxis_cuda_model_generate_batch(pyxis_cuda_model *m, const int32_
         PX_TRY(cudaEventElapsedTime(&timing_ms[0], ev[0], ev[1]));
         PX_TRY(cudaEventElapsedTime(&timing_ms[1], ev[1], ev[2]));
     }
+    return PYXIS_OK;
+}
+
+extern "C" int pyxis_cuda_model_prefill_hidden(pyxis_cuda_model *m, const int32_t *prompts, size_t n_seq,
+                                               size_t n_prompt, float *hidden_out) {
+    if (!m || !prompts || !hidden_out) return batch_fail(PYXIS_EINVAL, "null argument");
+    if (n_seq == 0) return PYXIS_OK;
+    if (m->vp_comm) return batch_fail(PYXIS_EINVAL, "prefill_hidden: not with a vocab-parallel head");
+    int rc = check_batch_args(m, prompts, n_seq, n_prompt, 1);
+    if (rc) return rc;
+    DevGuard g(m->ctx->device);
+    rc = ensure_state(m, (int)n_seq, (int)n_prompt, 1);
+    if (rc) return rc;
+    BatchState *b = m->batch;
+    cudaStream_t st = m->ctx->stream;
+    PX_TRY(cudaFuncSetAttribute(attention_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)(prefill_smem_floats<128>() * sizeof(float))));
+    PX_TRY(cudaFuncSetAttribute(attention_prefill_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)(prefill_smem_floats<64>() * sizeof(float))));
+    PX_TRY(cudaMemcpyAsync(b->d_prompt, prompts, n_seq * n_prompt * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    const int zero = 0, last = (int)n_prompt - 1;
+    PX_TRY(cudaMemcpyAsync(b->d_step, &zero, sizeof(int), cudaMemcpyHostToDevice, st));
+    PX_TRY(cudaMemcpyAsync(b->d_pos, &last, sizeof(int), cudaMemcpyHostToDevice, st));
+    rc = enqueue_prefill(m, (int)n_seq, (int)n_prompt, st);
+    if (rc) return rc;
+    PX_TRY(cudaMemcpyAsync(hidden_out, b->dh, n_seq * (size_t)m->cfg.hidden * sizeof(float), cudaMemcpyDeviceToHost,
+                           st));
+    PX_TRY(cudaStreamSynchronize(st));
+    return pyxis_cuda_check_device_error(m->ctx);
+}
+
+extern "C" int pyxis_cuda_model_set_vocab_parallel(pyxis_cuda_model *m, pyxis_cuda_comm *comm,
+                                                   const pyxis_cuda_weights *lm_head_shard, size_t vocab_lo,
+                                                   size_t shard_rows) {
+    if (!m) return batch_fail(PYXIS_EINVAL, "null model");
+    const pyxis_model_config &c = m->cfg;
+    if (comm) {
+        if (comm->ctx->device != m->ctx->device)
+            return batch_fail(PYXIS_EINVAL, "set_vocab_parallel: communicator and model on different devices");
+        if (!lm_head_shard || lm_head_shard->device != m->ctx->device ||
+            lm_head_shard->num_elements != shard_rows * (size_t)c.hidden)
+            return batch_fail(PYXIS_EINVAL, "set_vocab_parallel: shard length != shard_rows * hidden, or wrong device");
+        if (lm_head_shard->qtype != PYXIS_QTYPE_INT8 && lm_head_shard->qtype != PYXIS_QTYPE_INT4)
+            return batch_fail(PYXIS_EINVAL, "set_vocab_parallel: the shard must be int8 or int4");
+        if (shard_rows == 0 || vocab_lo + shard_rows > (size_t)c.vocab)
+            return batch_fail(PYXIS_EINVAL, "set_vocab_parallel: the shard's rows are not inside [0, vocab)");
+    }
+    DevGuard g(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+    free_batch_state(m->batch);  // the head buffers depend on the mode
+    m->batch = nullptr;
+    m->vp_comm = comm;
+    m->vp_shard = comm ? lm_head_shard : nullptr;
+    m->vp_lo = comm ? vocab_lo : 0;
+    m->vp_rows = comm ? shard_rows : 0;
     return PYXIS_OK;
 }

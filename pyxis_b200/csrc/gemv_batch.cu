@@ -135,7 +135,7 @@ PYXIS_DEVINL void run_prologue(const GemvPrologue &pr, int K, uint8_t *xs, float
         __syncthreads();
         float tot = 0.f;
         for (int i = 0; i < nw; ++i) tot = __fadd_rn(tot, red[i]);
-        const float factor = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)K), pr.eps)));
+        const float factor = rms_factor(tot, K, pr.eps);
         for (int base = threadIdx.x; base < nq; base += PQ * nt) {
 #pragma unroll
             for (int u = 0; u < PQ; ++u) {
@@ -144,15 +144,15 @@ PYXIS_DEVINL void run_prologue(const GemvPrologue &pr, int K, uint8_t *xs, float
                 const float4 w = base == (int)threadIdx.x ? wv[u] : __ldg(w4 + k4);
                 float4 *px = reinterpret_cast<float4 *>(xs + swz128((uint32_t)k4 * 16));
                 float4 v = *px;
-                v = make_float4(__fmul_rn(v.x, __fmul_rn(factor, w.x)), __fmul_rn(v.y, __fmul_rn(factor, w.y)),
-                                __fmul_rn(v.z, __fmul_rn(factor, w.z)), __fmul_rn(v.w, __fmul_rn(factor, w.w)));
+                v = make_float4(rms_scale(v.x, factor, w.x), rms_scale(v.y, factor, w.y), rms_scale(v.z, factor, w.z),
+                                rms_scale(v.w, factor, w.w));
                 *px = v;
             }
         }
     } else {
         pdl_wait();
         pdl_trigger();
-        auto silu_mul = [](float g, float u) { return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u); };
+        auto silu_mul = [](float g, float u) { return __fmul_rn(silu_f(g), u); };
         for (int base = threadIdx.x; base < nq; base += PQ * nt) {
             float4 g[PQ], u4[PQ];
 #pragma unroll

@@ -42,9 +42,9 @@ PYXIS_DEVINL void norm_rope(float (&v)[EPL], const float *nw, const float *rcos,
 #pragma unroll
         for (int t = 0; t < EPL; ++t) ss = __fadd_rn(ss, __fmul_rn(v[t], v[t]));
         ss = warp_sum(ss);
-        const float factor = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)HD), eps)));
+        const float factor = rms_factor(ss, HD, eps);
 #pragma unroll
-        for (int t = 0; t < EPL; ++t) v[t] = __fmul_rn(v[t], __fmul_rn(factor, nw[lane * EPL + t]));
+        for (int t = 0; t < EPL; ++t) v[t] = rms_scale(v[t], factor, nw[lane * EPL + t]);
     }
     const bool lo = lane < 16;
 #pragma unroll
@@ -52,7 +52,7 @@ PYXIS_DEVINL void norm_rope(float (&v)[EPL], const float *nw, const float *rcos,
         const float other = __shfl_xor_sync(0xffffffffu, v[t], 16);
         const int i = (lane & 15) * EPL + t;  // pair index in [0, HALF)
         const float c = rcos[(size_t)pos * HALF + i], s = rsin[(size_t)pos * HALF + i];
-        v[t] = lo ? __fsub_rn(__fmul_rn(v[t], c), __fmul_rn(other, s)) : __fadd_rn(__fmul_rn(v[t], c), __fmul_rn(other, s));
+        v[t] = rope_rot(v[t], other, c, s, lo);
     }
 }
 

@@ -4,6 +4,7 @@
 
 #include <vector>
 
+#include "../../include/pyxis_comm.h"
 #include "../../include/pyxis_decode.h"
 #include "ctx.h"
 #include "kernels.h"
@@ -46,4 +47,8 @@ struct pyxis_cuda_model {
     cudaGraphExec_t exec = nullptr;
     std::vector<void *> allocs;
     pyxis::BatchState *batch = nullptr;  // buffers of pyxis_cuda_model_generate_batch (decode_batch.cu)
+    // vocab-parallel head of pyxis_cuda_model_generate_batch (pyxis_cuda_model_set_vocab_parallel)
+    pyxis_cuda_comm *vp_comm = nullptr;
+    const pyxis_cuda_weights *vp_shard = nullptr;
+    size_t vp_lo = 0, vp_rows = 0;
 };

@@ -56,6 +56,8 @@ def test_generate_rejects_bad_arguments():
         dec.generate([-1], 2)
     with pytest.raises(PyxisError):
         dec.generate(np.zeros(16, np.int32), 2)  # 16 + 2 - 1 > max_seq
+    with pytest.raises(PyxisError):
+        dec.generate(np.zeros(0, np.int32), 2)  # an empty prompt, as generate_batch rejects it
     toks, _ = dec.generate([1, 2], 2)  # the model still works after the rejections
     assert toks.shape == (2,)
     dec.close()

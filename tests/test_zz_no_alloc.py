@@ -40,20 +40,63 @@ def _call_both(values, index_base):
     return idx_ref.cpu().numpy(), val_ref.cpu().numpy(), out
 
 
-@pytest.mark.parametrize("M,n", [(1, 151936), (5, 151936), (64, 4096), (3, 7)])
-def test_noalloc_argmax_matches_context_argmax(M, n):
+@pytest.mark.parametrize("index_base", [0, 123])
+@pytest.mark.parametrize("M,n,ld", [(1, 151936, 151936), (5, 151936, 151936), (64, 4096, 4096), (3, 7, 7),
+                                    (4, 1000, 1536)])
+def test_noalloc_argmax_matches_context_argmax(M, n, ld, index_base):
+    """Contiguous rows and rows that are a slice of a wider tensor (ld > n); index_base 0, where
+    a NaN at a row's index 0 wins (the reference never moves off values[0]), and 123 (a vocab
+    shard that does not hold index 0, where that NaN is skipped)."""
     import torch
 
-    rng = np.random.default_rng(M * 1000 + n)
-    v = rng.standard_normal((M, n)).astype(np.float32)
+    rng = np.random.default_rng(M * 1000 + n + index_base)
+    v = rng.standard_normal((M, ld)).astype(np.float32)
     if n > 100:
         v[0, 17] = v[0, n - 3] = 99.0   # a tie: the lowest index wins
-        v[-1, 0] = np.nan               # values[0] NaN: the reference answers 0
-    t = torch.from_numpy(v).cuda()
-    idx_ref, val_ref, calls = _call_both(t, index_base=123)
+        v[-1, 0] = np.nan               # values[0] NaN
+        if M > 2:
+            v[1, 5] = np.nan            # a NaN elsewhere is skipped
+            v[1, n:] = 1e30             # past the row's end (ld > n): never read
+    t = torch.from_numpy(v).cuda()[:, :n]
+    assert t.stride(0) == ld
+    idx_ref, val_ref, calls = _call_both(t, index_base=index_base)
+    if n > 100 and index_base == 0:
+        assert idx_ref[-1] == 0
     for idx, val in calls:
         assert np.array_equal(idx, idx_ref)
         assert np.array_equal(val.view(np.uint32), val_ref.view(np.uint32))
+
+
+def test_noalloc_argmax_allocates_nothing():
+    """Device memory in use is the same before and after repeated calls (after one warm-up call,
+    which loads the kernel)."""
+    import torch
+
+    t = torch.from_numpy(np.random.default_rng(1).standard_normal((8, 151936)).astype(np.float32)).cuda()
+    _call_both(t, index_base=0)
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        _call_both(t, index_base=0)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    # the helper's own small torch outputs come from torch's cache, not new device memory
+    assert free1 == free0, (free0, free1)
+
+
+def test_noalloc_argmax_rejects_out_of_range_index_base():
+    import torch
+
+    import pyxis_b200 as px  # noqa: F401
+    from pyxis_b200 import _native
+
+    L = _native.lib()
+    t = torch.zeros((2, 16), dtype=torch.float32, device="cuda")
+    idx = torch.empty(2, dtype=torch.int32, device="cuda")
+    for base in (-1, 2**31 - 15):  # the last index, base + n - 1, must fit an int32
+        rc = L.pyxis_cuda_argmax_noalloc(C.c_void_p(t.data_ptr()), 2, 16, 16, base, C.c_void_p(idx.data_ptr()),
+                                         None, None)
+        assert rc == _native.PYXIS_EINVAL, base
 
 
 def test_noalloc_argmax_rejects_more_rows_than_its_scratch():
