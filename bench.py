@@ -16,7 +16,13 @@ traffic, so no L2 flush is needed between steps.
   --impl reference   the oracle port of the reference's Rayon CPU path, all host threads.
 
 Multi-GPU (torchrun): every rank runs the whole sweep on its own GPU -- independent decode
-streams, data-parallel, no collective on the data path ("scaling": "weak").
+streams, data-parallel, no collective on the data path ("scaling": "weak").  With N > 1 the line
+also carries the sharded legs, each checked against the single-GPU result on the same rank:
+  row_split       gate/up/down (int4) and the lm_head (int8) split by output rows: per-rank and
+                  aggregate device GB/s, with and without the NCCL all-gather of the outputs
+  lm_head_vocab_parallel   the greedy head split by vocabulary rows (device argmax keys + one
+                  NCCL all-gather of 8 bytes per row and rank), device time per token
+  batch_decode    config 5 with its sequences data-parallel and the lm_head vocab-parallel
 """
 from __future__ import annotations
 
@@ -146,8 +152,10 @@ def dist_setup():
         import torch
         import torch.distributed as dist
 
-        # NCCL's informational lines go to stdout; the bench's stdout is its one JSON line
-        os.environ["NCCL_DEBUG"] = "WARN"
+        # NCCL's communicator set-up lines (rank counts) go to stdout before the JSON line,
+        # which is printed last, after the communicators are destroyed
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
@@ -206,15 +214,14 @@ def cpu_sweep_inputs():
     global _CPU_SWEEP_INPUTS
     if _CPU_SWEEP_INPUTS is None:
         import oracle
-        import pyxis_b200 as px
 
         mats = []
         for i, (name, qt, N, K, bs) in enumerate(SWEEP):
-            vals = oracle.bf16_to_f32(px.synth_normal_bf16(SEED + i, N * K, 0.02))
+            vals = oracle.bf16_to_f32(oracle.synth_normal_bf16(SEED + i, N * K, 0.02))
             d, s = (oracle.quantize_int8 if qt == "int8" else oracle.quantize_int4)(vals, bs)
             del vals
             mats.append((qt, N, K, bs, d, s))
-        xs = {B: px.synth_normal_f32(SEED + 100 + B, B * 6144, 1.0) for B in BATCHES}
+        xs = {B: oracle.synth_normal_f32(SEED + 100 + B, B * 6144, 1.0) for B in BATCHES}
         _CPU_SWEEP_INPUTS = (mats, xs)
     return _CPU_SWEEP_INPUTS
 
@@ -266,31 +273,128 @@ PREFILL_SHAPES = [  # name, qtype, N, K, block: X [512, K] x W [N, K]^T on the t
 PREFILL_M = 512
 
 
-def run_vocab_parallel_head(ws, rank, local, steps):
-    """Greedy next token through the lm_head split by vocabulary rows over the ranks: each rank's
-    int8 GEMV over V/ws rows + device argmax + NCCL all-gather of one (value, index) per rank.
-    Device time per token (max over ranks); every rank ends with the same token."""
-    import numpy as np
+def run_vocab_parallel_head(comm, ws, rank, local, steps, lm_full):
+    """Greedy next token through the int8 lm_head split by vocabulary rows over the ranks: each
+    rank's GEMV over V/ws rows, device argmax keys, one NCCL all-gather of 8 bytes per row and
+    rank, the pick on the device (pyxis_cuda_head_greedy_dev).  Device time per token (CUDA
+    events around back-to-back calls, max over ranks), at batch 1 and 8; every rank's tokens are
+    checked against the single-GPU matmul + argmax of the full head on the same rank."""
     import torch
 
+    import pyxis_b200 as px
     from pyxis_b200.dist import VocabParallelHead
 
     V, H = 151936, 2048
-    bits = px_synth_bits(0x11EAD, V * H)
-    head = VocabParallelHead(bits, V, H, "int8", rank, ws, local)
+    bits = px.synth_normal_bf16(SEED + 5, V * H, 0.02)  # the sweep's lm_head
+    head = VocabParallelHead(bits, V, H, "int8", comm)
     del bits
-    h = torch.from_numpy(px_synth_f32(9, H)).cuda().view(1, H)
+    out = {"n_gpus": ws, "rows_per_gpu": head.mm.hi - head.mm.lo,
+           "kernel": px.matmul_kernel_name(head.mm.w, 1, head.mm.hi - head.mm.lo, H), "batches": []}
+    parity = True
+    peak, _ = measured_peak_hbm()
+    for B in BATCHES:
+        h = torch.from_numpy(px.synth_normal_f32(9 + B, B * H, 1.0)).cuda().view(B, H)
+        tok = head.greedy(h)
+        want = px.argmax_dev(px.matmul_dev(h, lm_full, V, H))[0]
+        same = bool(torch.equal(tok, want))
+        parity = parity and same
+        for _ in range(3):
+            head.greedy(h, tokens=tok)
+        torch.cuda.synchronize()
+        barrier(ws)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            head.greedy(h, tokens=tok)
+        e1.record()
+        torch.cuda.synchronize()
+        us = max_over_ranks(e0.elapsed_time(e1) * 1e3 / steps, ws)
+        shard_bytes = gemv_bytes("int8", head.mm.hi - head.mm.lo, H, H, B)
+        out["batches"].append({"B": B, "us_per_token": us, "tokens_match_single_gpu": same,
+                               "shard_gbs": shard_bytes / us / 1e3, "shard_frac_of_peak": shard_bytes / us / 1e3 / peak,
+                               "first_tokens": [int(t) for t in tok[:4].cpu()]})
+    out["parity"] = bool(max_over_ranks(0.0 if parity else 1.0, ws) == 0.0)
+    out["note"] = ("device time per call: shard GEMV + argmax keys + NCCL all-gather + device pick; "
+                   "shard_frac_of_peak = the shard's algorithmic bytes / time / one GPU's HBM peak")
+    return out
+
+
+def run_row_split(ws, rank, local, steps, capture, replay_ms, full):
+    """gate/up/down (int4 g32) and the lm_head (int8 per row) split by output rows: rank r
+    quantises and streams only its rows [r*N/ws, (r+1)*N/ws) of each (pyxis_b200.dist
+    RowShardedMatmul), at batch 1 and 8.  Device GB/s per rank (CUDA graph of the shard GEMVs),
+    aggregate GB/s over the job, and the same with the NCCL all-gather of every output into the
+    full vector; the all-gathered output is checked bit for bit against the full matrix on the
+    same rank."""
+    import torch
+
+    import pyxis_b200 as px
+    from pyxis_b200.dist import RowShardedMatmul, shard_range
+
+    dev = torch.device("cuda", local)
+    shards = []
+    for i, (name, qt, N, K, bs) in enumerate(SWEEP):
+        if name not in ("gate_proj", "up_proj", "down_proj", "lm_head"):
+            continue
+        bits = px.synth_normal_bf16(SEED + i, N * K, 0.02)
+        shards.append((name, qt, N, K, bs, RowShardedMatmul(bits, N, K, qt, rank, ws, local, block_size=bs)))
+        del bits
+    X = {B: torch.from_numpy(px.synth_normal_f32(SEED + 100 + B, B * 6144, 1.0)).to(dev).view(B, 6144) for B in BATCHES}
+    Y = {B: torch.empty((B, 151936), dtype=torch.float32, device=dev) for B in BATCHES}
+
+    def step(st):
+        for B in BATCHES:
+            for (name, qt, N, K, bs, sh) in shards:
+                sh.forward(X[B][:, :K], Y=Y[B][:, :sh.hi - sh.lo], stream=st)
+
+    g = capture(step)
     for _ in range(3):
-        head.greedy(h)
+        g.replay()
+    barrier(ws)
+    ms = max_over_ranks(replay_ms(g, steps), ws)
+    del g
+    rank_bytes = sum(gemv_bytes(qt, sh.hi - sh.lo, K, bs, B) for B in BATCHES for (_, qt, N, K, bs, sh) in shards)
+    # every rank's algorithmic bytes (its rows' codes and scales, x, its outputs), summed
+    job_bytes = sum(gemv_bytes(qt, hi - lo, K, bs, B) for B in BATCHES for (_, qt, N, K, bs, _) in shards
+                    for (lo, hi) in (shard_range(N, r, ws) for r in range(ws)))
+    peak, peak_kind = measured_peak_hbm()
+    # parity: all-gathered shards == the full matrix on this rank, bit for bit
+    parity = True
+    mismatch = []
+    for B in BATCHES:
+        for (name, qt, N, K, bs, sh) in shards:
+            yg = sh.forward_gathered(X[B][:, :K])
+            yf = px.matmul_dev(X[B][:, :K], full[name], N, K)
+            if not torch.equal(yg, yf):
+                parity = False
+                mismatch.append(f"{name} B={B}")
+    # with the all-gather: eager, one NCCL all-gather per output (device time on torch's stream)
+    for _ in range(2):
+        for B in BATCHES:
+            for (name, qt, N, K, bs, sh) in shards:
+                sh.forward_gathered(X[B][:, :K])
     torch.cuda.synchronize()
     barrier(ws)
-    t0 = time.perf_counter()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
     for _ in range(steps):
-        tok = head.greedy(h)
+        for B in BATCHES:
+            for (name, qt, N, K, bs, sh) in shards:
+                sh.forward_gathered(X[B][:, :K])
+    e1.record()
     torch.cuda.synchronize()
-    us = max_over_ranks((time.perf_counter() - t0) / steps * 1e6, ws)
-    return {"n_gpus": ws, "rows_per_gpu": (V + ws - 1) // ws, "us_per_token": us, "token": int(tok[0]),
-            "note": "wall clock per greedy token incl. the all-gather and host pick (synchronous API)"}
+    ms_ag = max_over_ranks(e0.elapsed_time(e1), ws)
+    cases = [{"matrix": f"{name} {qt} {N}x{K}", "rows_per_gpu": sh.hi - sh.lo,
+              "kernel": px.matmul_kernel_name(sh.w, 1, sh.hi - sh.lo, K)} for (name, qt, N, K, bs, sh) in shards]
+    agg = job_bytes * steps / (ms / 1e3) / 1e9
+    return {"matrices": cases, "batches": list(BATCHES), "ms_per_step": ms / steps,
+            "rank_gbs": rank_bytes * steps / (ms / 1e3) / 1e9, "aggregate_gbs": agg,
+            "aggregate_frac_of_job_peak": agg / (ws * peak), "peak_per_gpu": peak, "peak_kind": peak_kind,
+            "ms_per_step_with_allgather": ms_ag / steps,
+            "aggregate_gbs_with_allgather": job_bytes * steps / (ms_ag / 1e3) / 1e9,
+            "parity": bool(max_over_ranks(0.0 if parity else 1.0, ws) == 0.0), "mismatch": mismatch,
+            "note": "without the all-gather: CUDA graph of the shard GEMVs; with it: eager calls, "
+                    "torch NCCL all_gather_into_tensor after every GEMV (latency-bound at these sizes)"}
 
 
 def px_synth_bits(seed, n):
@@ -394,12 +498,14 @@ BATCH_WORKLOAD = ("Qwen3-1.7B-shape batched decode, random init, int4 group 32 (
                   "GPUs")
 
 
-def batch_step_bytes(cfg, n_seq, pos):
+def batch_step_bytes(cfg, n_seq, pos, head_ranks=1):
     """HBM bytes of one batched int4 step at cache position `pos`: every projection's codes and
-    group-32 scales once (GEMMs over the n_seq rows) plus each sequence's KV rows 0..pos."""
-    params = cfg.n_layers * ((cfg.q_dim + 2 * cfg.kv_dim) * cfg.hidden + cfg.hidden * cfg.q_dim
-                             + 3 * cfg.ffn * cfg.hidden) + cfg.vocab * cfg.hidden
-    w = params // 2 + params // 32 * 4
+    group-32 scales once (GEMMs over the n_seq rows) plus each sequence's KV rows 0..pos; with a
+    vocab-parallel head over head_ranks GPUs, this rank's 1/head_ranks of the lm_head."""
+    layers = cfg.n_layers * ((cfg.q_dim + 2 * cfg.kv_dim) * cfg.hidden + cfg.hidden * cfg.q_dim
+                             + 3 * cfg.ffn * cfg.hidden)
+    head = cfg.vocab * cfg.hidden // head_ranks
+    w = (layers + head) // 2 + (layers + head) // 32 * 4
     kv = n_seq * cfg.n_layers * 2 * (pos + 1) * cfg.kv_dim * 4
     return w + kv
 
@@ -413,9 +519,16 @@ def prefill_flops(cfg, n_seq, P):
     return n_seq * (2 * proj * P + attn) + 2 * n_seq * cfg.vocab * cfg.hidden
 
 
-def run_batch_decode(local, ws, rank, n_seq_total=BATCH_SEQS, P=BATCH_PROMPT, n_new=BATCH_NEW):
+def run_batch_decode(local, ws, rank, n_seq_total=BATCH_SEQS, P=BATCH_PROMPT, n_new=BATCH_NEW, comm=None):
     """64 sequences of 2048 prompt ids then 256 greedy tokens, int4: this rank's share of the
-    sequences through pyxis_cuda_model_generate_batch."""
+    sequences through pyxis_cuda_model_generate_batch.  With a communicator (N > 1) the lm_head is
+    vocab-parallel over the ranks (every rank's final hidden rows all-gathered, its V/N rows of
+    the head, the argmax keys all-gathered); its tokens are then checked against the same model's
+    full head on this rank for the first two sequences."""
+    import zlib
+
+    import numpy as np
+
     from pyxis_b200 import synth_tokens
     from pyxis_b200.model import QWEN3_1_7B, Decoder, SyntheticModel
 
@@ -423,18 +536,36 @@ def run_batch_decode(local, ws, rank, n_seq_total=BATCH_SEQS, P=BATCH_PROMPT, n_
     n_seq = n_seq_total // ws + (1 if rank < n_seq_total % ws else 0)
     first = rank * (n_seq_total // ws) + min(rank, n_seq_total % ws)
     prompts = synth_tokens(0xBA7C, n_seq_total * P, cfg.vocab).reshape(n_seq_total, P)[first:first + n_seq]
-    dec = Decoder(SyntheticModel(cfg, SEED), qtype="int4", max_seq=P + n_new, device=local)
+    vp = comm if (comm is not None and n_seq_total % ws == 0) else None
+    dec = Decoder(SyntheticModel(cfg, SEED), qtype="int4", max_seq=P + n_new, device=local, vocab_parallel=vp)
     dec.generate_batch(prompts[:, :64], 4)  # warm-up: first-use set-up of every kernel
     toks, (pre_ms, dec_ms) = dec.generate_batch(prompts, n_new)
+    out = {"workload": BATCH_WORKLOAD, "sequences_this_rank": n_seq, "prefill_ms": pre_ms, "decode_ms": dec_ms,
+           "lm_head": f"vocab-parallel over {ws} GPUs (NCCL all-gather of hidden rows and argmax keys)" if vp
+           else "full int4 lm_head on each GPU"}
+    if vp is not None:
+        n_chk = 16
+        dec.set_vocab_parallel(False)
+        ref, _ = dec.generate_batch(prompts[:2], n_chk)
+        out["vocab_parallel_parity"] = bool(np.array_equal(ref, toks[:2, :n_chk]))
+        import torch
+        import torch.distributed as dist
+        t = torch.from_numpy(np.ascontiguousarray(toks)).cuda()
+        allt = torch.empty((ws,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+        dist.all_gather_into_tensor(allt, t)
+        toks_all = allt.cpu().numpy().reshape(n_seq_total, n_new)
+    else:
+        toks_all = toks
+    out["tokens_crc32"] = zlib.crc32(np.ascontiguousarray(toks_all, np.int32).tobytes())
     dec.close()
     steps = n_new - 1
-    bytes_steps = sum(batch_step_bytes(cfg, n_seq, P + i) for i in range(steps))
-    return {"workload": BATCH_WORKLOAD, "sequences_this_rank": n_seq, "prefill_ms": pre_ms, "decode_ms": dec_ms,
-            "decode_tokens_per_s": n_seq * steps / (dec_ms / 1e3),
-            "decode_achieved_gbs": bytes_steps / (dec_ms / 1e3) / 1e9,
-            "prefill_tokens_per_s": n_seq * P / (pre_ms / 1e3),
-            "prefill_tflops": prefill_flops(cfg, n_seq, P) / (pre_ms / 1e3) / 1e12,
-            "first_tokens": [int(t) for t in toks[0, :8]]}
+    bytes_steps = sum(batch_step_bytes(cfg, n_seq, P + i, ws if vp is not None else 1) for i in range(steps))
+    out.update({"decode_tokens_per_s": n_seq * steps / (dec_ms / 1e3),
+                "decode_achieved_gbs": bytes_steps / (dec_ms / 1e3) / 1e9,
+                "prefill_tokens_per_s": n_seq * P / (pre_ms / 1e3),
+                "prefill_tflops": prefill_flops(cfg, n_seq, P) / (pre_ms / 1e3) / 1e12,
+                "first_tokens": [int(t) for t in toks[0, :8]]})
+    return out
 
 
 def run_config1(local, capture, replay_ms, with_cpu):
@@ -666,9 +797,14 @@ def pyxis_arm(args, ws, rank, local):
 
     config1 = run_config1(local, capture, replay_ms, rank == 0 and ws == 1 and not args.no_cpu_baseline)
 
-    lm_vp = None
+    lm_vp = row_split = comm = None
     if ws > 1:
-        lm_vp = run_vocab_parallel_head(ws, rank, local, args.steps)
+        from pyxis_b200.dist import Comm
+        comm = Comm(rank, ws, local)
+        full = {name: w for (name, qt, N, K, bs, w) in weights}
+        row_split = run_row_split(ws, rank, local, args.steps, capture, replay_ms, full)
+        lm_vp = run_vocab_parallel_head(comm, ws, rank, local, args.steps, full["lm_head"])
+        del full
     prefill = run_prefill(local)
     peak_tf = 0.0
     try:
@@ -696,7 +832,9 @@ def pyxis_arm(args, ws, rank, local):
     batch = None
     if not args.no_batch_decode:
         torch.cuda.empty_cache()
-        batch = run_batch_decode(local, ws, rank)
+        batch = run_batch_decode(local, ws, rank, comm=comm)
+        if "vocab_parallel_parity" in batch:
+            batch["vocab_parallel_parity"] = max_over_ranks(0.0 if batch["vocab_parallel_parity"] else 1.0, ws) == 0.0
         ms = max_over_ranks(batch["prefill_ms"] + batch["decode_ms"], ws)
         dmax = max_over_ranks(batch["decode_ms"], ws)
         pmax = max_over_ranks(batch["prefill_ms"], ws)
@@ -706,6 +844,8 @@ def pyxis_arm(args, ws, rank, local):
                       "job_prefill_ms": pmax, "decode_frac_of_hbm_peak": batch["decode_achieved_gbs"] / peak_d,
                       "prefill_frac_of_bf16_peak": batch["prefill_tflops"] / (peak_tf or 1590.0)})
 
+    if comm is not None:
+        comm.close()
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         import oracle
@@ -734,10 +874,15 @@ def pyxis_arm(args, ws, rank, local):
                 "decode": decode,
                 "batch_decode": batch,
                 "lm_head_vocab_parallel": lm_vp,
+                "row_split": row_split,
+                "parity": None if ws == 1 else {
+                    "row_split": row_split["parity"], "vocab_parallel": lm_vp["parity"],
+                    "batch_decode_vocab_parallel": None if batch is None else batch.get("vocab_parallel_parity")},
                 "prefill": {"M": PREFILL_M, "kernel": "split_x_kernel + gemm_tc_kernel (tcgen05 kind::f16, fp16 hi/lo)",
                             "peak_tflops": peak_tf, "peak_kind": "measured bf16 burst", "shapes": prefill},
                 "per_gpu_value": value / ws}
-        print(json.dumps(line), flush=True)
+        return line
+    return None
 
 
 def profile_case(args):
@@ -847,13 +992,17 @@ def main():
         profile_case(args)
         return
     ws, rank, local = dist_setup()
+    line = None
     try:
-        pyxis_arm(args, ws, rank, local)
+        line = pyxis_arm(args, ws, rank, local)
     finally:
         if ws > 1:
             import torch.distributed as dist
 
             dist.destroy_process_group()
+    if line is not None:  # last on stdout, after NCCL's own lines
+        sys.stdout.flush()
+        print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":

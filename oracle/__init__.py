@@ -51,6 +51,8 @@ def lib() -> C.CDLL:
         L.oracle_silu.restype = C.c_float
         L.oracle_greedy_decode.argtypes = [_vp, _vp, _sz, _sz, _vp, C.c_int]
         L.oracle_greedy_decode.restype = C.c_int
+        L.oracle_prefill_hidden.argtypes = [_vp, _vp, _sz, _vp, C.c_int]
+        L.oracle_prefill_hidden.restype = C.c_int
         L.oracle_kv_new.argtypes = [_vp, _sz]
         L.oracle_kv_new.restype = _vp
         L.oracle_kv_free.argtypes = [_vp]
@@ -67,12 +69,37 @@ def lib() -> C.CDLL:
         L.oracle_transformer_forward.argtypes = [_vp, _vp, _sz, _sz, _vp, C.c_int]
         L.oracle_transformer_forward.restype = C.c_int
         L.oracle_num_cpus.restype = C.c_int
+        L.pyxis_synth_normal_f32.argtypes = [C.c_uint64, _sz, C.c_float, _vp]
+        L.pyxis_synth_normal_bf16.argtypes = [C.c_uint64, _sz, C.c_float, _vp]
+        L.pyxis_synth_tokens.argtypes = [C.c_uint64, _sz, C.c_uint32, _vp]
+        for n in ("pyxis_synth_normal_f32", "pyxis_synth_normal_bf16", "pyxis_synth_tokens"):
+            getattr(L, n).restype = None
         _lib = L
     return _lib
 
 
 def _p(a: np.ndarray) -> C.c_void_p:
     return a.ctypes.data_as(C.c_void_p)
+
+
+# The seeded generator of include/pyxis_synth.h (the same source as the CUDA library's copy), for
+# the CPU baseline, which must not load the CUDA library.
+def synth_normal_f32(seed: int, n: int, sigma: float = 1.0) -> np.ndarray:
+    out = np.empty(n, dtype=np.float32)
+    lib().pyxis_synth_normal_f32(seed, n, sigma, _p(out))
+    return out
+
+
+def synth_normal_bf16(seed: int, n: int, sigma: float = 0.02) -> np.ndarray:
+    out = np.empty(n, dtype=np.uint16)
+    lib().pyxis_synth_normal_bf16(seed, n, sigma, _p(out))
+    return out
+
+
+def synth_tokens(seed: int, n: int, vocab: int) -> np.ndarray:
+    out = np.empty(n, dtype=np.int32)
+    lib().pyxis_synth_tokens(seed, n, vocab, _p(out))
+    return out
 
 
 def _f32(a) -> np.ndarray:
@@ -186,12 +213,11 @@ class OModel(C.Structure):
                 ("final_norm", _vp), ("lm_head", OWeights)]
 
 
-def greedy_decode(cfg, bf16, qtype: str, prompt, n_new: int, nthreads: int = 0, timing=None):
-    """Greedy tokens of the model whose tensors ``bf16(name)`` returns (np.uint16 bits; names
+def _model(cfg, bf16, qtype: str):
+    """The oracle_model of a config whose tensors ``bf16(name)`` returns (np.uint16 bits; names
     ``layers.{l}.{q,k,v,o,gate,up,down}`` and ``embed``), quantised by the reference's policy
     (src/model.rs:520-530: int8 one scale per row, int4 one per 32), tied lm_head, RMSNorm
-    weights 1, QK-norm when cfg.qk_norm.  A list passed as ``timing`` receives the seconds of
-    the generation alone (the len(prompt) + n_new - 1 forward passes, without the packing)."""
+    weights 1, QK-norm when cfg.qk_norm.  Returns (model, arrays to keep alive)."""
     keep = []
 
     def q(bits, in_features):
@@ -224,6 +250,15 @@ def greedy_decode(cfg, bf16, qtype: str, prompt, n_new: int, nthreads: int = 0, 
                C.addressof(hn_arr), C.addressof(ws["q"]), C.addressof(ws["k"]), C.addressof(ws["v"]),
                C.addressof(ws["o"]), C.addressof(ws["gate"]), C.addressof(ws["up"]), C.addressof(ws["down"]),
                ones.ctypes.data, lm)
+    keep += [ws, ones, hones, norm_arr, hn_arr, emb]
+    return m, keep
+
+
+def greedy_decode(cfg, bf16, qtype: str, prompt, n_new: int, nthreads: int = 0, timing=None):
+    """Greedy tokens (Model::generate with argmax sampling, src/model.rs:245-285) of the model
+    ``_model`` builds.  A list passed as ``timing`` receives the seconds of the generation alone
+    (the len(prompt) + n_new - 1 forward passes, without the packing)."""
+    m, keep = _model(cfg, bf16, qtype)
     pr = np.ascontiguousarray(np.asarray(prompt, np.int32))
     out = np.empty(n_new, np.int32)
     t0 = time.perf_counter()
@@ -232,6 +267,17 @@ def greedy_decode(cfg, bf16, qtype: str, prompt, n_new: int, nthreads: int = 0, 
         timing.append(time.perf_counter() - t0)
     if rc:
         raise RuntimeError("oracle_greedy_decode failed")
+    return out
+
+
+def prefill_hidden(cfg, bf16, qtype: str, prompt, nthreads: int = 0) -> np.ndarray:
+    """The final-norm hidden state [hidden] of the prompt's last position: what the first greedy
+    token's lm_head product reads."""
+    m, keep = _model(cfg, bf16, qtype)
+    pr = np.ascontiguousarray(np.asarray(prompt, np.int32))
+    out = np.empty(cfg.hidden, np.float32)
+    if lib().oracle_prefill_hidden(C.addressof(m), pr.ctypes.data, pr.size, out.ctypes.data, nthreads):
+        raise RuntimeError("oracle_prefill_hidden failed")
     return out
 
 

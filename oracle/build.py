@@ -18,15 +18,26 @@ CFLAGS = ["-O2", "-ffp-contract=off", "-fno-fast-math", "-std=c11", "-fPIC", "-p
           "-Wall", "-Wextra", "-Wno-unused-parameter"]
 
 
+# The seeded input generator (pyxis_synth.h) is linked in as well, so that the CPU baseline can
+# make the benchmark's inputs without loading the CUDA library.
+ROOT = os.path.dirname(HERE)
+SYNTH = os.path.join(ROOT, "pyxis_b200", "csrc", "synth.cpp")
+SYNTH_H = os.path.join(ROOT, "include", "pyxis_synth.h")
+
+
 def build(verbose: bool = False, force: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     srcs = sorted(glob.glob(os.path.join(HERE, "*.c")))
-    deps = srcs + glob.glob(os.path.join(HERE, "*.h"))
+    deps = srcs + glob.glob(os.path.join(HERE, "*.h")) + [SYNTH, SYNTH_H, os.path.abspath(__file__)]
     if force or not os.path.exists(LIB) or any(os.path.getmtime(d) > os.path.getmtime(LIB) for d in deps):
-        cmd = ["gcc"] + CFLAGS + ["-shared", "-o", LIB] + srcs + ["-lm"]
-        if verbose:
-            print(" ".join(cmd), file=sys.stderr)
-        subprocess.run(cmd, check=True)
+        synth_o = os.path.join(BUILD, "synth.o")
+        cmds = [["g++", "-O2", "-std=c++17", "-fPIC", "-pthread", "-I" + os.path.join(ROOT, "include"), "-c", SYNTH,
+                 "-o", synth_o],
+                ["gcc"] + CFLAGS + ["-shared", "-o", LIB] + srcs + [synth_o, "-lm", "-lstdc++"]]
+        for cmd in cmds:
+            if verbose:
+                print(" ".join(cmd), file=sys.stderr)
+            subprocess.run(cmd, check=True)
     return LIB
 
 

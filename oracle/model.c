@@ -328,3 +328,23 @@ int oracle_greedy_decode(const oracle_model *m, const int32_t *prompt, size_t n_
     free(logits);
     return rc;
 }
+
+/* The hidden state greedy decoding reads the first token from: the whole prompt through the
+ * transformer (src/model.rs:245-262, src/transformer.rs:28-90), then the final RMSNorm of its last
+ * position (the row that src/output_head.rs:21-28 multiplies with the lm_head). */
+int oracle_prefill_hidden(const oracle_model *m, const int32_t *prompt, size_t n_prompt, float *out_hidden, int nt) {
+    if (n_prompt == 0) return -1;
+    size_t H = m->hidden;
+    oracle_kv *kv = oracle_kv_new(m, n_prompt);
+    float *x = (float *)malloc(n_prompt * H * sizeof(float));
+    int rc = (kv && x) ? 0 : -1;
+    for (size_t p = 0; p < n_prompt && rc == 0; ++p) {
+        if (prompt[p] < 0 || (size_t)prompt[p] >= m->vocab) rc = -1;
+        else memcpy(x + p * H, m->embedding + (size_t)prompt[p] * H, H * sizeof(float));
+    }
+    if (rc == 0) rc = oracle_transformer_forward(m, x, n_prompt, 0, kv, nt);
+    if (rc == 0) memcpy(out_hidden, x + (n_prompt - 1) * H, H * sizeof(float));
+    oracle_kv_free(kv);
+    free(x);
+    return rc;
+}

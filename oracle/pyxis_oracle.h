@@ -156,6 +156,8 @@ int oracle_transformer_forward(const oracle_model *m, float *x, size_t seq_len, 
 /* Greedy decode: prefill `prompt` (n_prompt ids), then n_new tokens, each the argmax of the
  * lm_head logits (output_head.rs:25-27) -- Model::generate (src/model.rs:245-285) with temperature
  * 0 and no repetition penalty.  Writes n_new ids to out_tokens.  Returns 0 or -1. */
+/* The final-norm hidden state of the prompt's last position (the first token's lm_head input). */
+int oracle_prefill_hidden(const oracle_model *m, const int32_t *prompt, size_t n_prompt, float *out_hidden, int nt);
 int oracle_greedy_decode(const oracle_model *m, const int32_t *prompt, size_t n_prompt,
                          size_t n_new, int32_t *out_tokens, int nthreads);
 

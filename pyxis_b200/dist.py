@@ -1,4 +1,5 @@
-"""Multi-GPU sharding of the quantized matmul path (one process per GPU, torch.distributed).
+"""Multi-GPU sharding of the quantized matmul path (one process per GPU, torch.distributed for the
+rendezvous, NCCL over NVLink for the data; include/pyxis_comm.h).
 
 Only the parts that shard naturally are split; nothing here reduces partial sums:
   * row-sharded matmul: rank r owns output rows [r*N/n, (r+1)*N/n) of a matrix.  With one scale
@@ -6,14 +7,21 @@ Only the parts that shard naturally are split; nothing here reduces partial sums
     and scales are exactly that slice of the full pack, so each rank quantises only its rows and
     the outputs concatenate to the single-GPU result (optionally all-gathered, NCCL over NVLink).
   * vocab-parallel lm_head + greedy argmax (src/output_head.rs:21-44): each rank computes the
-    logits of its vocab shard, takes their argmax on the device (index offset by the shard start),
-    and the ranks all-gather one (value, index) pair each; the winner is the largest value, the
-    lowest index on ties -- the first maximum, as the reference's strict `>` scan picks it.
-  * independent decode sequences: data-parallel replicas (bench.py), no collective.
+    logits of its vocab shard and reduces every row to one 64-bit key on the device
+    (order-preserving value bits, then the inverted global index); the ranks all-gather the keys
+    and the largest key of a row is the reference's first maximum, so every rank ends with the
+    same token, on the device, with no host round trip.
+  * independent decode sequences: data-parallel, the lm_head of the batched decode vocab-parallel
+    (``Decoder(..., vocab_parallel=comm)``, pyxis_cuda_model_set_vocab_parallel).
 """
 from __future__ import annotations
 
+import ctypes as C
+
 import numpy as np
+
+from . import _native
+from ._native import check
 
 
 def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
@@ -23,25 +31,53 @@ def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
     return lo, hi
 
 
-def pick_global_argmax(vals, idxs) -> int:
-    """The first maximum over the per-shard (value, index) pairs: largest value, lowest index on
-    ties.  A NaN value never wins (the reference's `value > max_value` is false for NaN) unless the
-    global first element is NaN, which the shard holding index 0 reports as its own answer."""
-    vals = np.asarray(vals, np.float64)
-    idxs = np.asarray(idxs, np.int64)
-    if idxs.size == 0:
-        raise ValueError("no shards")
-    # index 0 holds NaN: the reference never moves off it
-    first = np.argmin(idxs)
-    if idxs[first] == 0 and np.isnan(vals[first]):
-        return 0
-    best = None
-    for v, i in zip(vals, idxs):
-        if np.isnan(v):
-            continue
-        if best is None or v > best[0] or (v == best[0] and i < best[1]):
-            best = (v, i)
-    return int(best[1]) if best is not None else 0
+def bits_rows(bits: np.ndarray, in_features: int, lo: int, hi: int) -> np.ndarray:
+    return np.ascontiguousarray(bits.reshape(-1, in_features)[lo:hi]).ravel()
+
+
+def exchange_comm_id(rank: int, make_id=None, group=None) -> bytes:
+    """The 128-byte communicator id made on rank 0 (pyxis_cuda_comm_unique_id) and broadcast to
+    every rank over the torch.distributed group (gloo or NCCL)."""
+    import torch.distributed as dist
+
+    if make_id is None:
+        def make_id():
+            buf = (C.c_uint8 * 128)()
+            check(_native.lib().pyxis_cuda_comm_unique_id(buf))
+            return bytes(buf)
+    obj = [make_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0, group=group)
+    uid = obj[0]
+    if not isinstance(uid, (bytes, bytearray)) or len(uid) != 128:
+        raise ValueError("communicator id must be 128 bytes")
+    return bytes(uid)
+
+
+class Comm:
+    """A communicator of the library (pyxis_cuda_comm_init) on this rank's context: the ranks of
+    the current torch.distributed group, one per GPU."""
+
+    def __init__(self, rank: int, world: int, device: int, group=None):
+        from . import _require_cuda
+
+        self.ctx = _require_cuda(device)
+        self.rank, self.world, self.device = rank, world, device
+        uid = exchange_comm_id(rank, group=group)
+        buf = (C.c_uint8 * 128).from_buffer_copy(uid)
+        h = C.c_void_p()
+        check(_native.lib().pyxis_cuda_comm_init(self.ctx.handle, buf, world, rank, C.byref(h)))
+        self.handle = h
+
+    def close(self) -> None:
+        if self.handle:
+            _native.lib().pyxis_cuda_comm_free(self.handle)
+            self.handle = None
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class RowShardedMatmul:
@@ -49,7 +85,7 @@ class RowShardedMatmul:
     ``forward_gathered`` all-gathers them into the full output on every rank."""
 
     def __init__(self, bf16_bits: np.ndarray, out_features: int, in_features: int, qtype: str, rank: int,
-                 world: int, device: int):
+                 world: int, device: int, block_size: int | None = None):
         import torch
 
         from . import Weights
@@ -58,15 +94,14 @@ class RowShardedMatmul:
         self.lo, self.hi = shard_range(out_features, rank, world)
         rows = bits_rows(bf16_bits, in_features, self.lo, self.hi)
         t = torch.from_numpy(rows.view(np.int16)).view(torch.bfloat16).to(f"cuda:{device}")
-        if qtype == "int8":
-            self.w = Weights.quantize_int8(t, in_features, device=device)
-        else:
-            self.w = Weights.quantize_int4(t, 32, device=device)
+        bs = block_size or (in_features if qtype == "int8" else 32)
+        self.w = Weights.quantize_int8(t, bs, device=device) if qtype == "int8" else \
+            Weights.quantize_int4(t, bs, device=device)
         self.device = device
 
-    def forward(self, X):
+    def forward(self, X, Y=None, stream=None):
         from . import matmul_dev
-        return matmul_dev(X, self.w, self.hi - self.lo, self.K)
+        return matmul_dev(X, self.w, self.hi - self.lo, self.K, Y=Y, stream=stream)
 
     def forward_gathered(self, X, group=None):
         import torch
@@ -77,41 +112,36 @@ class RowShardedMatmul:
         width = max(hi - lo for lo, hi in sizes)
         pad = torch.zeros((local.shape[0], width), dtype=local.dtype, device=local.device)
         pad[:, : local.shape[1]] = local
-        parts = [torch.empty_like(pad) for _ in range(self.world)]
-        dist.all_gather(parts, pad, group=group)
-        return torch.cat([p[:, : hi - lo] for p, (lo, hi) in zip(parts, sizes)], dim=1)
-
-
-def bits_rows(bits: np.ndarray, in_features: int, lo: int, hi: int) -> np.ndarray:
-    return np.ascontiguousarray(bits.reshape(-1, in_features)[lo:hi]).ravel()
+        parts = torch.empty((self.world,) + tuple(pad.shape), dtype=pad.dtype, device=pad.device)
+        dist.all_gather_into_tensor(parts, pad, group=group)
+        return torch.cat([parts[r, :, : hi - lo] for r, (lo, hi) in enumerate(sizes)], dim=1)
 
 
 class VocabParallelHead:
-    """The lm_head split by vocabulary rows across the ranks, with the distributed greedy argmax."""
+    """The lm_head split by vocabulary rows across the ranks, with the distributed greedy argmax
+    (pyxis_cuda_head_greedy_dev)."""
 
-    def __init__(self, bf16_bits: np.ndarray, vocab: int, hidden: int, qtype: str, rank: int, world: int,
-                 device: int):
-        self.mm = RowShardedMatmul(bf16_bits, vocab, hidden, qtype, rank, world, device)
-        self.vocab = vocab
+    def __init__(self, bf16_bits: np.ndarray, vocab: int, hidden: int, qtype: str, comm: Comm,
+                 block_size: int | None = None):
+        self.comm = comm
+        self.mm = RowShardedMatmul(bf16_bits, vocab, hidden, qtype, comm.rank, comm.world, comm.device,
+                                   block_size=block_size)
+        self.vocab, self.hidden = vocab, hidden
 
-    def greedy(self, h, group=None):
-        """Next-token ids [M] on every rank for hidden states h [M, hidden] (device tensor)."""
-        from . import argmax_dev
+    def greedy(self, h, tokens=None, stream=None):
+        """Next-token ids (int32 CUDA tensor [M], the same on every rank) for hidden states h
+        [M, hidden] (CUDA f32, the same rows on every rank).  Asynchronous on ``stream``."""
+        import torch
 
-        logits = self.mm.forward(h)
-        idx, val = argmax_dev(logits, index_base=self.mm.lo)
-        return gather_pick(val, idx, self.mm.world, group)
+        from . import _stream_handle
 
-
-def gather_pick(val, idx, world: int, group=None) -> np.ndarray:
-    """All-gather each rank's per-row (value, index) shard argmax and pick the global first
-    maximum on every rank (works for CUDA tensors over NCCL and CPU tensors over gloo)."""
-    import torch
-    import torch.distributed as dist
-
-    pair = torch.stack([val.to(torch.float64), idx.to(torch.float64)], dim=1)  # [M, 2]
-    parts = [torch.empty_like(pair) for _ in range(world)]
-    dist.all_gather(parts, pair, group=group)
-    allp = torch.stack(parts, dim=0).cpu().numpy()  # [world, M, 2]
-    return np.array([pick_global_argmax(allp[:, m, 0], allp[:, m, 1]) for m in range(allp.shape[1])],
-                    dtype=np.int64)
+        if h.dim() == 1:
+            h = h.unsqueeze(0)
+        M = h.shape[0]
+        if tokens is None:
+            tokens = torch.empty(M, dtype=torch.int32, device=h.device)
+        st = _stream_handle(stream, h.device)
+        check(_native.lib().pyxis_cuda_head_greedy_dev(self.comm.handle, self.mm.w.handle, self.vocab, self.mm.lo,
+                                                       self.mm.hi - self.mm.lo, self.hidden, C.c_void_p(h.data_ptr()),
+                                                       M, h.stride(0), C.c_void_p(tokens.data_ptr()), C.c_void_p(st)))
+        return tokens

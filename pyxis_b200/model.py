@@ -96,7 +96,12 @@ def _quantize(bits: np.ndarray, qtype: str, in_features: int, device: int):
 class Decoder:
     """Model::generate (src/model.rs:245-285) with temperature-0 sampling, on one GPU."""
 
-    def __init__(self, model: SyntheticModel, qtype: str = "int8", max_seq: int = 256, device: int = 0):
+    def __init__(self, model: SyntheticModel, qtype: str = "int8", max_seq: int = 256, device: int = 0,
+                 vocab_parallel=None, full_head: bool = True):
+        """``vocab_parallel``: a ``pyxis_b200.dist.Comm`` -- generate_batch then runs this rank's
+        sequences with the lm_head split by vocabulary rows over the communicator's ranks (this
+        rank quantises only its rows).  ``full_head`` False leaves the full lm_head out (generate
+        then fails; generate_batch needs the vocab-parallel head)."""
         cfg = model.cfg
         self.cfg = cfg
         self.ctx = _require_cuda(device)
@@ -127,9 +132,39 @@ class Decoder:
             check(L.pyxis_cuda_model_set_layer(self.handle, layer, wqkv.handle, wo.handle, wgu.handle, wd.handle,
                                                p(ones), p(ones), p(hn), p(hn)))
         emb = model.bf16("embed")
-        lm = _quantize(emb, qtype, cfg.hidden, device)
-        self._keep.append(lm)
-        check(L.pyxis_cuda_model_set_head(self.handle, emb.ctypes.data_as(C.POINTER(C.c_uint16)), lm.handle, p(ones)))
+        lm = _quantize(emb, qtype, cfg.hidden, device) if full_head else None
+        if lm is not None:
+            self._keep.append(lm)
+        check(L.pyxis_cuda_model_set_head(self.handle, emb.ctypes.data_as(C.POINTER(C.c_uint16)),
+                                          lm.handle if lm is not None else None, p(ones)))
+        self.vocab_parallel = None
+        if vocab_parallel is not None:
+            from .dist import bits_rows, shard_range
+            lo, hi = shard_range(cfg.vocab, vocab_parallel.rank, vocab_parallel.world)
+            shard = _quantize(bits_rows(emb, cfg.hidden, lo, hi), qtype, cfg.hidden, device)
+            self._keep.append(shard)
+            check(L.pyxis_cuda_model_set_vocab_parallel(self.handle, vocab_parallel.handle, shard.handle, lo, hi - lo))
+            self.vocab_parallel = vocab_parallel
+            self._shard = (shard, lo, hi)
+
+    def set_vocab_parallel(self, on: bool) -> None:
+        """Switch generate_batch between the vocab-parallel head and this rank's full head."""
+        L = _native.lib()
+        if on:
+            shard, lo, hi = self._shard
+            check(L.pyxis_cuda_model_set_vocab_parallel(self.handle, self.vocab_parallel.handle, shard.handle, lo,
+                                                        hi - lo))
+        else:
+            check(L.pyxis_cuda_model_set_vocab_parallel(self.handle, None, None, 0, 0))
+
+    def prefill_hidden(self, prompts) -> np.ndarray:
+        """The batched prefill's final-norm hidden state of every prompt's last position
+        (pyxis_cuda_model_prefill_hidden): prompts [n_seq, n_prompt] -> [n_seq, hidden] f32."""
+        pr = np.ascontiguousarray(np.asarray(prompts, np.int32))
+        out = np.empty((pr.shape[0], self.cfg.hidden), np.float32)
+        check(_native.lib().pyxis_cuda_model_prefill_hidden(self.handle, pr.ctypes.data_as(C.c_void_p), pr.shape[0],
+                                                            pr.shape[1], out.ctypes.data_as(C.c_void_p)))
+        return out
 
     def generate(self, prompt, n_new: int):
         """Returns (tokens [n_new], (prompt_ms, decode_ms)) -- device time of the two phases."""

@@ -130,3 +130,15 @@ def test_max_over_ranks_world2():
     for p in procs:
         p.join(timeout=60)
     assert got == {0: 3.75, 1: 3.75}
+
+
+def test_reference_arm_loads_no_cuda_library():
+    """The CPU arm makes its seeded inputs with the oracle's copy of the generator: the CUDA
+    library is never mapped into the reference process."""
+    code = ("import sys, types; sys.path.insert(0, %r); import bench; "
+            "bench.reference_arm(types.SimpleNamespace(steps=1, warmup=0), 1, 0); "
+            "maps = open('/proc/self/maps').read(); "
+            "print('CUDA_LIB_MAPPED' if 'libpyxis_cuda' in maps else 'CUDA_LIB_ABSENT')") % ROOT
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert "CUDA_LIB_ABSENT" in out.stdout, out.stdout[-500:]

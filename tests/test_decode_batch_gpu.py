@@ -55,6 +55,32 @@ def test_qwen3_shape_batch_matches_single_sequence_decoder():
     dec.close()
 
 
+# GQA 16 / 8 x 128 like Qwen3-1.7B, narrow elsewhere so that the oracle's prefill of 2048
+# positions takes seconds
+GQA_2048 = ModelConfig(hidden=256, n_layers=1, n_q_heads=16, n_kv_heads=8, head_dim=128, ffn=512, vocab=2048,
+                       rope_theta=1e6)
+
+
+def test_prefill_of_2048_positions_matches_oracle():
+    """The batched prefill at the config-5 prompt length: 2048 positions, i.e. 32 query tiles of
+    64 and 64 key tiles of 32 in the causal prefill attention, with the GQA 16 / 8 x 128 heads.
+    Sequence 0's final-norm hidden state (the first token's lm_head input) is held to the matmul
+    bar against the oracle's prefill -- rel(y, r) = max_i |y_i - r_i| / max(|r_i|, 1e-3 max|r|)
+    <= 1e-3 -- and sequence 1's greedy tokens must equal the oracle's."""
+    m = SyntheticModel(GQA_2048, seed=41)
+    dec = Decoder(m, qtype="int4", max_seq=2048 + 4)
+    prompts = synth_tokens(0x2048, 2 * 2048, GQA_2048.vocab).reshape(2, 2048)
+    hid = dec.prefill_hidden(prompts)
+    toks, _ = dec.generate_batch(prompts, 4)
+    dec.close()
+    ref = oracle.prefill_hidden(GQA_2048, m.bf16, "int4", list(prompts[0]))
+    r = ref.astype(np.float64)
+    err = float((np.abs(hid[0].astype(np.float64) - r) / np.maximum(np.abs(r), 1e-3 * np.abs(r).max())).max())
+    assert err <= 1e-3, err
+    want = oracle.greedy_decode(GQA_2048, m.bf16, "int4", list(prompts[1]), 4)
+    assert np.array_equal(toks[1], want), (toks[1], want)
+
+
 def test_batch_rejects_bad_arguments():
     from pyxis_b200._native import PyxisError
     m = SyntheticModel(SMALL, seed=1)

@@ -1,6 +1,7 @@
-"""Host logic of the multi-GPU sharding (pyxis_b200/dist.py), on CPU: shard ranges, the global
-first-maximum pick across vocab shards (against the oracle's argmax, src/output_head.rs:30-44),
-and the all-gather + pick over a world-size-2 gloo group."""
+"""Host logic of the multi-GPU sharding (pyxis_b200/dist.py), on CPU: shard ranges, the
+vocab-parallel key scheme (a numpy restatement of the device keys, tests/keys.py) against the
+oracle's argmax (src/output_head.rs:30-44), and over a world-size-2 gloo group the communicator-id
+exchange and the all-gather + pick of the keys."""
 import os
 
 import numpy as np
@@ -10,23 +11,8 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 import oracle
-from pyxis_b200.dist import bits_rows, gather_pick, pick_global_argmax, shard_range
-
-
-def shard_argmax(v, lo):
-    """What argmax_kernel returns for one shard: first max, NaNs skipped except a NaN at global
-    index 0 (only the shard with lo == 0 applies that rule)."""
-    if lo == 0 and np.isnan(v[0]):
-        return np.nan, 0
-    best = None
-    for i, x in enumerate(v):
-        if np.isnan(x):
-            continue
-        if best is None or x > best[0]:
-            best = (x, i)
-    if best is None:
-        return np.nan, lo
-    return best[0], lo + best[1]
+from keys import pick, shard_key
+from pyxis_b200.dist import bits_rows, exchange_comm_id, shard_range
 
 
 @pytest.mark.parametrize("n,world", [(10, 3), (151936, 8), (7, 7), (1, 1), (100, 2)])
@@ -39,20 +25,23 @@ def test_shard_range_partitions(n, world):
 
 
 @pytest.mark.parametrize("world", [1, 2, 3, 8])
-def test_global_pick_matches_reference_argmax(world):
+def test_key_pick_matches_reference_argmax(world):
     rng = np.random.default_rng(world)
     for trial in range(200):
         n = int(rng.integers(1, 60))
         v = rng.integers(-3, 4, size=n).astype(np.float32)  # many ties
+        if trial % 3 == 0:
+            v[rng.integers(0, n)] = -0.0 if trial % 2 else 0.0
         if trial % 5 == 0:
             v[rng.integers(0, n)] = np.nan
+        if trial % 11 == 0:
+            v[rng.integers(0, n)] = np.inf if trial % 2 else -np.inf
         if trial % 17 == 0:
             v[0] = np.nan
         if trial % 23 == 0:
             v[:] = np.nan
-        pairs = [shard_argmax(v[lo:hi], lo) for lo, hi in (shard_range(n, r, world) for r in range(world)) if hi > lo]
-        got = pick_global_argmax([p[0] for p in pairs], [p[1] for p in pairs])
-        assert got == oracle.argmax(v), (v, pairs, got)
+        keys = [shard_key(v[lo:hi], lo) for lo, hi in (shard_range(n, r, world) for r in range(world)) if hi > lo]
+        assert pick(keys) == oracle.argmax(v), (v, keys)
 
 
 @pytest.mark.parametrize("qt,N,K,bs", [("int8", 37, 96, 96), ("int4", 37, 96, 32), ("int4", 10, 2048, 32),
@@ -80,19 +69,25 @@ def _worker(rank, world, port, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
+    # the communicator id made on rank 0 reaches every rank unchanged
+    uid = exchange_comm_id(rank, make_id=lambda: bytes(range(128)))
     rng = np.random.default_rng(0)
     M, V = 3, 1001
     logits = rng.standard_normal((M, V)).astype(np.float32)
     logits[1, 5] = logits[1, 900] = 50.0  # a tie across the shard boundary: index 5 wins
+    logits[2, 0] = np.nan  # NaN at index 0: index 0 wins
     lo, hi = shard_range(V, rank, world)
-    vals, idxs = zip(*[shard_argmax(logits[m, lo:hi], lo) for m in range(M)])
-    got = gather_pick(torch.tensor(vals, dtype=torch.float32), torch.tensor(idxs, dtype=torch.int32), world)
+    # 64-bit keys travel as int64 bit patterns, as the device keys do through NCCL
+    mine = torch.from_numpy(np.array([shard_key(logits[m, lo:hi], lo) for m in range(M)], np.uint64).view(np.int64))
+    parts = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(parts, mine)
+    got = [pick([int(p.numpy().view(np.uint64)[m]) for p in parts]) for m in range(M)]
     want = [oracle.argmax(logits[m]) for m in range(M)]
-    q.put((rank, list(got), want))
+    q.put((rank, uid == bytes(range(128)), got, want))
     dist.destroy_process_group()
 
 
-def test_gather_pick_over_gloo_world2():
+def test_key_gather_pick_over_gloo_world2():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = 29500 + os.getpid() % 1000
@@ -103,5 +98,6 @@ def test_gather_pick_over_gloo_world2():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    for rank, got, want in res:
+    for rank, id_ok, got, want in res:
+        assert id_ok, rank
         assert got == want, (rank, got, want)

@@ -14,7 +14,7 @@ def test_row_sharded_and_vocab_parallel_on_two_gpus():
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+    cmd = ["timeout", "-k", "30", "900", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", str(29600 + os.getpid() % 500),
            os.path.join(HERE, "dist_worker.py")]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")

@@ -54,11 +54,34 @@ class CudaImpl:
     def argmax(self, v):
         return px.argmax(v)
 
+    # the decode step's row operations, through the device helpers the decode kernels use
+    # (pyxis_cuda_row_op)
+    def _row_op(self, op, x, w=None, eps=0.0, head_dim=0, pos=0, theta=0.0):
+        import ctypes as C
+        x = np.ascontiguousarray(np.asarray(x, np.float32))
+        wv = None if w is None else np.ascontiguousarray(np.asarray(w, np.float32))
+        out = np.empty_like(x)
+        ctx = px.get_cuda(0)
+        px._native.check(px._native.lib().pyxis_cuda_row_op(
+            ctx.handle, op, x.ctypes.data_as(C.c_void_p), x.size,
+            None if wv is None else wv.ctypes.data_as(C.c_void_p), eps, head_dim, pos, theta,
+            out.ctypes.data_as(C.c_void_p)))
+        return out
+
+    def rmsnorm(self, x, w, eps):
+        return self._row_op(1, x, w=w, eps=eps)
+
+    def rope(self, x, head_dim, pos, theta):
+        return self._row_op(2, x, head_dim=head_dim, pos=pos, theta=theta)
+
+    def silu(self, x):
+        return float(self._row_op(3, [x])[0])
+
 
 @pytest.mark.parametrize("kat", load_kats(), ids=lambda k: k["name"])
 def test_cuda_reference_kat(kat):
     if not run_kat(kat, CudaImpl()):
-        pytest.skip("op not on the CUDA path (a decode-loop op)")
+        pytest.skip("op not on the CUDA path")
 
 
 def _bits(a):
