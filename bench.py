@@ -358,16 +358,25 @@ def run_row_split(ws, rank, local, steps, capture, replay_ms, full):
     job_bytes = sum(gemv_bytes(qt, hi - lo, K, bs, B) for B in BATCHES for (_, qt, N, K, bs, _) in shards
                     for (lo, hi) in (shard_range(N, r, ws) for r in range(ws)))
     peak, peak_kind = measured_peak_hbm()
-    # parity: all-gathered shards == the full matrix on this rank, bit for bit
+    # parity: all-gathered shards == the full matrix on this rank: bit for bit, or (where the
+    # weight-streaming matmul splits K by the row count) within the matmul bar
+    # max_i |y_i - r_i| / max(|r_i|, 1e-3 max|r|) <= 1e-3
     parity = True
-    mismatch = []
+    mismatch, bitwise, max_rel = [], [], 0.0
     for B in BATCHES:
         for (name, qt, N, K, bs, sh) in shards:
             yg = sh.forward_gathered(X[B][:, :K])
             yf = px.matmul_dev(X[B][:, :K], full[name], N, K)
-            if not torch.equal(yg, yf):
+            if torch.equal(yg, yf):
+                bitwise.append(f"{name} B={B}")
+                continue
+            d = (yg.double() - yf.double()).abs()
+            den = torch.maximum(yf.double().abs(), 1e-3 * yf.double().abs().max())
+            rel = float((d / den).max())
+            max_rel = max(max_rel, rel)
+            if rel > 1e-3:
                 parity = False
-                mismatch.append(f"{name} B={B}")
+                mismatch.append(f"{name} B={B}: {rel:.3g}")
     # with the all-gather: eager, one NCCL all-gather per output (device time on torch's stream)
     for _ in range(2):
         for B in BATCHES:
@@ -393,6 +402,7 @@ def run_row_split(ws, rank, local, steps, capture, replay_ms, full):
             "ms_per_step_with_allgather": ms_ag / steps,
             "aggregate_gbs_with_allgather": job_bytes * steps / (ms_ag / 1e3) / 1e9,
             "parity": bool(max_over_ranks(0.0 if parity else 1.0, ws) == 0.0), "mismatch": mismatch,
+            "bitwise_equal": bitwise, "max_rel_err_vs_full": max_over_ranks(max_rel, ws),
             "note": "without the all-gather: CUDA graph of the shard GEMVs; with it: eager calls, "
                     "torch NCCL all_gather_into_tensor after every GEMV (latency-bound at these sizes)"}
 

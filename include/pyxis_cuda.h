@@ -142,13 +142,19 @@ int pyxis_cuda_matmul_batch(pyxis_cuda_ctx *ctx, const float *input, size_t M,
                             float *out);
 
 /* Device-pointer form, asynchronous on `stream` (NULL: the context's stream).  X [M, in] f32
- * with row stride ldx (elements), Y [M, out] f32 with row stride ldy.  M < 16 runs the decode
- * GEMV kernels, 8 rows per launch; M >= 16 with int8/int4 weights runs the tensor-core prefill
- * GEMM, which needs `workspace` of pyxis_cuda_matmul_workspace_size() bytes (device memory,
- * 256-byte aligned).  A NULL workspace makes the context allocate and keep one (not allowed while
- * the stream is being captured); the context's workspace also holds split-K partial sums, which
- * a caller workspace of that size has no room for, so GEMMs with fewer output tiles than SMs
- * (e.g. 2048 output rows at M = 512) run faster on it. */
+ * with row stride ldx (elements), Y [M, out] f32 with row stride ldy.  Kernels by shape:
+ *  - M = 1: the decode GEMVs (CUDA cores; int8 one-scale-per-row matrices of >= 16384 rows on
+ *    the tensor cores, kind::i8);
+ *  - 2..64 rows of int4 / int8 with a scale per 32 values, or 9..64 rows of int8 with one scale per
+ *    row, in_features % 128 == 0: the weight-streaming tensor-core matmul;
+ *  - other M <= 15: the GEMVs, 8 rows per launch; M >= 16 with int8/int4 weights: the tensor-core
+ *    prefill GEMM.
+ * The tensor-core products need `workspace` of pyxis_cuda_matmul_workspace_size() bytes (device
+ * memory, 256-byte aligned).  A NULL workspace uses the context's, allocated at init and grown
+ * when a product needs more (not allowed while the stream is being captured:
+ * pyxis_cuda_reserve_workspace grows it beforehand); it also has room for split-K partial sums,
+ * which a caller workspace of the minimum size lacks, so matrices with fewer 128-row tiles than
+ * SMs run faster on it. */
 int pyxis_cuda_matmul_dev(pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, const float *X,
                           size_t M, size_t ldx, size_t out_features, size_t in_features,
                           float *Y, size_t ldy, void *workspace, size_t workspace_bytes,
@@ -156,6 +162,11 @@ int pyxis_cuda_matmul_dev(pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, cons
 
 /* Workspace bytes pyxis_cuda_matmul_dev needs for M rows of in_features (0 for the GEMV). */
 size_t pyxis_cuda_matmul_workspace_size(size_t M, size_t in_features);
+
+/* Grows the context's own workspace to at least `bytes` (synchronizes the context's stream), so
+ * that later pyxis_cuda_matmul_dev calls with a NULL workspace allocate nothing -- e.g. before
+ * they are captured into a CUDA graph. */
+int pyxis_cuda_reserve_workspace(pyxis_cuda_ctx *ctx, size_t bytes);
 
 /* Synchronizes the context's device and reports whether a kernel's bounded device-side wait ran
  * out since the last check (PYXIS_ETIMEOUT; the outputs of that launch are invalid), clearing the

@@ -51,6 +51,7 @@ SIGNATURES = {
     "pyxis_cuda_matmul_batch": (C.c_int, [_vp, _vp, _sz, _vp, _sz, _sz, _vp]),
     "pyxis_cuda_matmul_dev": (C.c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _sz, _vp, _sz, _vp, _sz, _vp]),
     "pyxis_cuda_matmul_workspace_size": (_sz, [_sz, _sz]),
+    "pyxis_cuda_reserve_workspace": (C.c_int, [_vp, _sz]),
     "pyxis_cuda_check_device_error": (C.c_int, [_vp]),
     "pyxis_cuda_matmul_kernel": (C.c_char_p, [_vp, _vp, C.c_size_t, C.c_size_t, C.c_size_t]),
     "pyxis_cuda_argmax_dev": (C.c_int, [_vp, _vp, _sz, _sz, _sz, C.c_int64, _vp, _vp, _vp]),

@@ -1,5 +1,6 @@
 // api.cu -- the extern "C" boundary (include/pyxis_cuda.h): contexts, device-resident weights,
 // argument checks that mirror the reference's asserts, and kernel dispatch.
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -128,11 +129,50 @@ int check_matmul(const pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, size_t 
     return PYXIS_OK;
 }
 
+// The context's default workspace, allocated at init: it covers the weight-streaming matmul's x
+// copies for 64 tokens of K <= 16384 plus kWsPartialCap of split-K partial sums, and the
+// tensor-core GEMM's needs up to a few hundred tokens.  Larger needs grow it outside stream
+// capture (pyxis_cuda_reserve_workspace, or the first call that needs it).
+constexpr size_t kWsPartialCap = 12u << 20;
+constexpr size_t kDefaultWorkspace = 20u << 20;
+constexpr size_t kWsTickets = 16384;  // 128-row tiles: matrices of up to 2M rows
+
+int grow_workspace(pyxis_cuda_ctx *ctx, size_t want) {
+    if (ctx->ws_cap >= want) return PYXIS_OK;
+    cudaFree(ctx->ws);
+    ctx->ws = nullptr;
+    ctx->ws_cap = 0;
+    PYXIS_CUDA_TRY(cudaMalloc(&ctx->ws, want), "cudaMalloc(workspace)");
+    ctx->ws_cap = want;
+    return PYXIS_OK;
+}
+
+// Grows the context workspace, refusing while `st` is being captured (an allocation there would
+// be an error, and a graph would keep the old pointer).
+int ensure_ctx_workspace(pyxis_cuda_ctx *ctx, size_t want, cudaStream_t st) {
+    if (ctx->ws_cap >= want) return PYXIS_OK;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
+        return fail(PYXIS_EINVAL,
+                    "the context workspace must grow to %zu bytes, which cannot happen during stream capture: "
+                    "call pyxis_cuda_reserve_workspace first",
+                    want);
+    return grow_workspace(ctx, want);
+}
+
 }  // namespace
 
 int pyxis::record_error(int code, const char *msg) { return fail(code, "%s", msg); }
 
 namespace {
+// Weight-streaming tensor-core matmul for decode-shaped batches: int4 / int8 group-32 weights from 2
+// tokens (one token stays on the CUDA-core GEMV), int8 one-scale-per-row weights from 9 (up to 8
+// the exact kind::i8 GEMV or the batch GEMV), up to 64 tokens.
+bool use_gemm_ws(const QMatrix &q, size_t M) {
+    if (!gemm_ws_supported(q, M)) return false;
+    return q.block_size == q.K ? M >= 9 : M >= 2;
+}
+
 bool use_gemm_tc(const QMatrix &q, size_t M, const float *X, size_t ldx) {
     return M >= kTcMinRows && gemm_tc_supported(q) && (reinterpret_cast<uintptr_t>(X) & 15) == 0 && ldx % 4 == 0;
 }
@@ -158,19 +198,33 @@ int pyxis::run_matmul(pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, const fl
     // writes y only after griddepcontrol.wait, i.e. after its predecessor has completed.
     PdlScope pdl;
     QMatrix q = qmatrix(w, out_features, in_features);
+    if (use_gemm_ws(q, M)) {
+        const size_t need = gemm_ws_workspace_bytes(M, out_features, in_features, ctx->num_sms, 0);
+        if (!workspace) {
+            // the context's workspace: x's fp16 copies, the rest for split-K partial sums
+            const size_t want = gemm_ws_workspace_bytes(M, out_features, in_features, ctx->num_sms, kWsPartialCap);
+            int rc = ensure_ctx_workspace(ctx, want, st);
+            if (rc) return rc;
+            workspace = ctx->ws;
+            workspace_bytes = ctx->ws_cap;
+        } else if (workspace_bytes < need) {
+            return fail(PYXIS_EINVAL, "workspace of %zu bytes < %zu needed", workspace_bytes, need);
+        } else if (reinterpret_cast<uintptr_t>(workspace) & 255) {
+            return fail(PYXIS_EINVAL, "workspace must be 256-byte aligned");
+        }
+        cudaError_t e = launch_gemm_ws(q, X, M, ldx, Y, ldy, workspace, workspace_bytes, ctx->ws_tickets,
+                                       ctx->ws_tickets_n, ctx->d_err, ctx->num_sms, st);
+        if (e != cudaSuccess) return cuda_fail(e, "weight-streaming matmul launch");
+        return PYXIS_OK;
+    }
     if (use_gemm_tc(q, M, X, ldx)) {
         const size_t need = gemm_tc_workspace_bytes(M, in_features);
         if (!workspace) {
             // the context's own workspace also holds split-K partials when they help
             const size_t want = gemm_tc_workspace_bytes_splitk(M, out_features, in_features, w->block_size == in_features,
                                                                w->block_size, ctx->num_sms);
-            if (ctx->ws_cap < want) {
-                cudaFree(ctx->ws);
-                ctx->ws = nullptr;
-                ctx->ws_cap = 0;
-                PYXIS_CUDA_TRY(cudaMalloc(&ctx->ws, want), "cudaMalloc(workspace)");
-                ctx->ws_cap = want;
-            }
+            int rc = ensure_ctx_workspace(ctx, want, st);
+            if (rc) return rc;
             workspace = ctx->ws;
             workspace_bytes = ctx->ws_cap;
         } else if (workspace_bytes < need) {
@@ -245,6 +299,20 @@ int pyxis_cuda_init(int device, pyxis_cuda_ctx **out) {
         pyxis_cuda_destroy(ctx);
         return cuda_fail(e, "device error flag");
     }
+    ctx->ws_tickets_n = kWsTickets;
+    e = cudaMalloc(&ctx->ws_tickets, kWsTickets * sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(ctx->ws_tickets, 0, kWsTickets * sizeof(unsigned));
+    if (e == cudaSuccess) {
+        const int rc = grow_workspace(ctx, kDefaultWorkspace);
+        if (rc) {
+            pyxis_cuda_destroy(ctx);
+            return rc;
+        }
+    }
+    if (e != cudaSuccess) {
+        pyxis_cuda_destroy(ctx);
+        return cuda_fail(e, "workspace tickets");
+    }
     ctx->amax.partial = (uint64_t *)ctx->amax_mem;
     ctx->amax.ticket = (unsigned *)((uint8_t *)ctx->amax_mem + (size_t)kArgmaxMaxRows * kArgmaxMaxCtasPerRow * sizeof(uint64_t));
     *out = ctx;
@@ -261,6 +329,7 @@ int pyxis_cuda_destroy(pyxis_cuda_ctx *ctx) {
     cudaFree(ctx->amax_mem);
     cudaFree(ctx->d_err);
     cudaFree(ctx->tcg_scratch);
+    cudaFree(ctx->ws_tickets);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
     return PYXIS_OK;
@@ -419,7 +488,19 @@ int pyxis_cuda_weights_free(pyxis_cuda_weights *w) {
 }
 
 size_t pyxis_cuda_matmul_workspace_size(size_t M, size_t in_features) {
-    return M >= kTcMinRows ? gemm_tc_workspace_bytes(M, in_features) : 0;
+    size_t need = M >= kTcMinRows ? gemm_tc_workspace_bytes(M, in_features) : 0;
+    if (M >= 2 && M <= 64 && in_features % 128 == 0) {  // the weight-streaming matmul's x copies
+        QMatrix probe{PYXIS_QTYPE_INT4, nullptr, nullptr, 32, 1, in_features};
+        if (gemm_ws_supported(probe, M)) need = std::max(need, gemm_ws_workspace_bytes(M, 1, in_features, 1, 0));
+    }
+    return need;
+}
+
+int pyxis_cuda_reserve_workspace(pyxis_cuda_ctx *ctx, size_t bytes) {
+    if (!ctx) return fail(PYXIS_EINVAL, "null context");
+    DeviceGuard g(ctx->device);
+    PYXIS_CUDA_TRY(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    return grow_workspace(ctx, bytes);
 }
 
 int pyxis_cuda_check_device_error(pyxis_cuda_ctx *ctx) {
@@ -453,6 +534,7 @@ const char *pyxis_cuda_matmul_kernel(pyxis_cuda_ctx *ctx, const pyxis_cuda_weigh
     QMatrix q = qmatrix(w, out_features, in_features);
     // 256-byte aligned, contiguous x: the layout the device-pointer form's callers pass
     const float *x = reinterpret_cast<const float *>(static_cast<uintptr_t>(256));
+    if (use_gemm_ws(q, M)) return "gemm_ws_kernel";
     if (use_gemm_tc(q, M, x, in_features)) return "gemm_tc_kernel";
     const size_t b = M < 8 ? M : 8;
     if (use_gemv_tc(ctx, q, b, x, in_features)) return "gemv_tc_i8_kernel";

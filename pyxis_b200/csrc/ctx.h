@@ -31,6 +31,9 @@ struct pyxis_cuda_ctx {
     // split-K scratch of the tensor-core GEMV (zeroed at init; the kernel leaves it zeroed)
     void *tcg_scratch = nullptr;
     size_t tcg_scratch_bytes = 0;
+    // per-tile tickets of the weight-streaming matmul (zeroed at init; the kernel leaves them zero)
+    unsigned *ws_tickets = nullptr;
+    size_t ws_tickets_n = 0;
 };
 
 struct pyxis_cuda_weights {

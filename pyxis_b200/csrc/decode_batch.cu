@@ -380,6 +380,15 @@ int ensure_state(pyxis_cuda_model *m, int n_seq, int n_prompt, int n_new) {
                                                                     m->ctx->num_sms));
     pyxis_cuda_comm *vp = m->vp_comm;
     const size_t head_rows = vp ? (size_t)vp->nranks * n_seq : (size_t)n_seq;
+    // the decode step's products of n_seq rows on the weight-streaming matmul: x copies plus room
+    // for split-K partial sums
+    constexpr size_t kStepPartialCap = 12u << 20;
+    for (const auto &L : m->layers)
+        for (auto [w, N, K] : {std::tuple{L.wqkv, qkv_rows, H}, std::tuple{L.wo, H, qd}, std::tuple{L.wgu, 2 * ffn, H},
+                               std::tuple{L.wdown, H, ffn}})
+            if (w) ws = std::max(ws, gemm_ws_workspace_bytes(n_seq, N, K, m->ctx->num_sms, kStepPartialCap));
+    ws = std::max(ws, gemm_ws_workspace_bytes(head_rows, vp ? m->vp_rows : (size_t)c.vocab, H, m->ctx->num_sms,
+                                              kStepPartialCap));
     if (vp) {
         ws = std::max(ws, gemm_tc_workspace_bytes(head_rows, H));
         ws = std::max(ws, gemm_tc_workspace_bytes_splitk(head_rows, m->vp_rows, H, m->vp_shard->block_size == H,

@@ -1,0 +1,658 @@
+// gemm_ws.cu -- weight-streaming matmul for a few tokens (M = 1..64) on the tcgen05 tensor cores:
+// the decode-shaped products of src/matmul.rs:21-97 (the batched decode step's projections and
+// lm_head, src/attention.rs:77-79,136, src/ffn.rs:36-48, src/output_head.rs:22, with several
+// sequences' rows at once) for weights with a scale per group of 32 (int4 q + 8 nibbles, or int8
+// codes) or one scale per row (int8).
+//
+//   y[t, n] = sum_g s[n, g] * sum_{k in g} q[n, k] x[t, k]            (group scales)
+//   y[t, n] = s[n] * sum_k q[n, k] x[t, k]                           (row scales)
+//
+// With few tokens the weights' bytes set the time, so the kernel is built around streaming them
+// once with every SM busy:
+//   - x is split once per launch (split_x_ws_kernel) into fp16 hi + lo (x 2^e = hi + lo to 22
+//     bits, one power of two 2^e per token) and stacked along K: each MMA K-step multiplies the
+//     codes with x_hi and then, into the same accumulator, with x_lo, so one fp32 accumulator per
+//     (row, token) carries the 22-bit x.
+//   - the codes become exact fp16 integers on the CUDA cores (a mask and a paired subtraction per
+//     two codes) and go to the tensor core as operand A; no scale is folded into them.
+//   - each group of 32 has its own TMEM accumulator (128 rows x the token columns, fp32); the
+//     epilogue warps read it back and add s[n, g] * D into fp32 registers, in group order.  With
+//     row scales a stage's 128 of K share one accumulator and the scale is applied at the end.
+//   - persistent CTAs, one per SM.  Work unit = (128-row tile, K part); the number of K parts per
+//     tile is chosen so that the SMs get equal numbers of stages.  A tile split into several parts
+//     is finished by the CTA that completes its last part: it adds the parts' partial sums in part
+//     order (reruns are bit-identical) and writes y.
+//
+// Warp roles (320 threads): 0 TMA producer (codes + x_hi / x_lo tiles into a ring), 1 TMEM owner
+// and MMA issuer, 2-5 converters (one weight row per thread), 6-9 epilogue (one row per thread,
+// the warp's TMEM lane quarter).  Every mbarrier wait is bounded; a wait that runs out records a
+// code in the context's device flag and the CTA winds down (drains its copies and MMAs, frees TMEM).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <atomic>
+
+#include "kernels.h"
+#include "tc_ptx.cuh"
+#include "tmap.cuh"
+
+namespace pyxis {
+namespace {
+
+constexpr int WM = 128;       // weight rows per tile: MMA M, TMEM lanes
+constexpr int WSK = 128;      // K per stage
+constexpr int WG = 32;        // K per scale group (group-scale mode)
+constexpr int kGroupsPerStage = WSK / WG;
+constexpr int kProdWarp = 0, kMmaWarp = 1, kConvWarp0 = 2, kNumConv = 4, kEpiWarp0 = 6, kNumEpi = 4;
+constexpr int kThreads = (kEpiWarp0 + kNumEpi) * 32;  // 320
+constexpr int kSlots = 8;                              // group accumulators in flight (TMEM)
+constexpr int kMaxTokens = 64;
+constexpr uint64_t kTimeoutNs = 2000000000ull;
+constexpr uint32_t kABlock = WM * 128;      // one column block (64 of K) of the fp16 weight tile
+constexpr uint32_t kABytes = 2 * kABlock;   // one fp16 weight stage
+enum { kErrProd = 0x501, kErrConv = 0x502, kErrMma = 0x503, kErrEpi = 0x504, kErrDrain = 0x505 };
+
+struct WsParams {
+    int M, N, K;
+    int tiles, parts;    // tiles of 128 rows, K parts per tile
+    int stages_k;        // stages per row (K / 128)
+    int units;           // tiles * parts
+    const float *scales;
+    const float *xinv;   // [M] 2^-e per token
+    float *Y;
+    long long ldy;
+    float *partial;      // [units][NBT][128] partial sums of split tiles (parts > 1)
+    unsigned *tickets;   // [tiles], zero between launches
+    int *err;
+};
+
+PYXIS_DEVINL uint32_t h2_bits(__half2 v) { return *reinterpret_cast<uint32_t *>(&v); }
+PYXIS_DEVINL __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
+
+// Eight int4 codes (q + 8 in nibbles; element 2j low, 2j+1 high nibble of byte j) -> exact fp16
+// pairs (e0,e4) (e1,e5) (e2,e6) (e3,e7): nibbles i and i+4 of the word land in the two halves of
+// (w >> 4i) & 0x000F000F; OR-ing in 1024's exponent makes them 1024 + (q + 8), then - 1032.  x is
+// split in the same element order (split_x_ws_kernel<true>).
+PYXIS_DEVINL void u4x8_to_h(uint32_t w, uint32_t (&h)[4]) {
+    const __half2 bias = bits_h2(0x64086408u);  // (1032, 1032)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = h2_bits(__hsub2(bits_h2(((w >> (4 * i)) & 0x000F000Fu) | 0x64006400u), bias));
+}
+
+// Four int8 codes -> exact fp16 pairs (e0,e1) (e2,e3): byte b -> fp16(1024 + (b ^ 0x80)) - 1152.
+PYXIS_DEVINL void i8x4_to_h(uint32_t w, uint32_t &h01, uint32_t &h23) {
+    const uint32_t u = w ^ 0x80808080u;
+    const __half2 bias = bits_h2(0x64806480u);  // (1152, 1152)
+    h01 = h2_bits(__hsub2(bits_h2(__byte_perm(u, 0x64646464u, 0x5140u)), bias));
+    h23 = h2_bits(__hsub2(bits_h2(__byte_perm(u, 0x64646464u, 0x5342u)), bias));
+}
+
+// Byte offset of 16-byte chunk c of row r in a 128-byte-swizzled K-major block (8-row 1024 B atoms).
+PYXIS_DEVINL uint32_t sw128_off(int r, int c) { return (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4); }
+
+PYXIS_DEVINL void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+
+// 16 consecutive fp32 columns of this warp's 32 TMEM lanes, waited for.
+PYXIS_DEVINL void tmem_ld16f(uint32_t taddr, float *v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Unit u = (tile u / parts, part u % parts); part p covers stages [p S / parts, (p + 1) S / parts)
+// of the row (S = stages_k).  A CTA takes units blockIdx.x, blockIdx.x + gridDim.x, ...
+PYXIS_DEVINL void unit_range(const WsParams &p, int u, int &tile, int &part, int &s0, int &s1) {
+    tile = u / p.parts;
+    part = u - tile * p.parts;
+    s0 = part * p.stages_k / p.parts;
+    s1 = (part + 1) * p.stages_k / p.parts;
+}
+
+template <int NBT>
+struct WsSmem {
+    static constexpr int NR = NBT <= 32 ? 4 : 3;  // stages of codes + x tiles
+    static constexpr int NA = NBT <= 32 ? 3 : 2;  // converted weight tiles
+    static constexpr uint32_t kBBlock = NBT * 128;             // one column block of an x tile
+    static constexpr uint32_t kRawMax = WM * 128;              // codes of a stage (int8: 16 KB)
+    static constexpr uint32_t kStage = kRawMax + 4 * kBBlock;  // codes, x_hi (2 blocks), x_lo (2 blocks)
+    static constexpr uint32_t a = 0;
+    static constexpr uint32_t r = a + NA * kABytes;
+    static constexpr uint32_t bar = r + NR * kStage;
+    static constexpr uint32_t num_bars = 2 * NR + 2 * NA + 2 * kSlots + 1;
+    static constexpr uint32_t misc = bar + num_bars * 8;
+    static constexpr uint32_t bytes = misc + 64 + 1024;  // + alignment slack
+};
+static_assert(WsSmem<16>::bytes <= 232448 && WsSmem<32>::bytes <= 232448 && WsSmem<48>::bytes <= 232448 &&
+                  WsSmem<64>::bytes <= 232448,
+              "227 KB of shared memory per CTA");
+
+template <int NBT, bool INT4, bool GROUPED>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_ws_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_xhi,
+                   const __grid_constant__ CUtensorMap tm_xlo, const WsParams p) {
+    using L = WsSmem<NBT>;
+    constexpr int NR = L::NR, NA = L::NA;
+    constexpr uint32_t kRaw = INT4 ? WM * 64 : WM * 128;
+    constexpr uint32_t kStageTx = kRaw + 4 * L::kBBlock;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::bar);
+    uint64_t *full = bars, *rawfree = bars + NR;           // code / x stages
+    uint64_t *conv = bars + 2 * NR, *aempty = conv + NA;   // converted weight tiles
+    uint64_t *accfull = aempty + NA, *accempty = accfull + kSlots, *drain = accempty + kSlots;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::misc);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::misc + 4);
+    volatile int *last_flag = reinterpret_cast<volatile int *>(smem + L::misc + 8);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NR; ++s) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&rawfree[s], kNumConv + 1);  // the converters' reads of the codes + the MMAs' reads of x
+        }
+        for (int a = 0; a < NA; ++a) {
+            tc::mbar_init(&conv[a], kNumConv);
+            tc::mbar_init(&aempty[a], 1);
+        }
+        for (int k = 0; k < kSlots; ++k) {
+            tc::mbar_init(&accfull[k], 1);
+            tc::mbar_init(&accempty[k], kNumEpi);
+        }
+        tc::mbar_init(drain, 1);
+        *abort_flag = 0;
+        tc::fence_mbar_init();
+    }
+    // accumulator slots at a power-of-two column pitch (48 tokens take 64 columns)
+    constexpr int SP = NBT == 48 ? 64 : NBT;
+    constexpr uint32_t kTmemCols = kSlots * SP <= 128 ? 128 : (kSlots * SP <= 256 ? 256 : 512);
+    if (warp == kMmaWarp) tc::tmem_alloc(tmem_slot, kTmemCols);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == kProdWarp) {
+        // ------------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            tc::prefetch_tmap(&tm_w);
+            tc::prefetch_tmap(&tm_xhi);
+            tc::prefetch_tmap(&tm_xlo);
+            // the codes do not depend on the previous kernel: the first NR stages' codes go out
+            // before griddepcontrol.wait, their x tiles after it
+            auto issue_x = [&](int slot, int k) {
+                uint8_t *bhi = smem + L::r + slot * L::kStage + L::kRawMax, *blo = bhi + 2 * L::kBBlock;
+                tc::tma_load_2d(bhi, &tm_xhi, k, 0, &full[slot]);
+                tc::tma_load_2d(bhi + L::kBBlock, &tm_xhi, k + 64, 0, &full[slot]);
+                tc::tma_load_2d(blo, &tm_xlo, k, 0, &full[slot]);
+                tc::tma_load_2d(blo + L::kBBlock, &tm_xlo, k + 64, 0, &full[slot]);
+            };
+            int g = 0, s = 0, ph = 0, pend_n = 0;
+            int pend_k[NR];
+            bool ok = true, waited = false;
+            for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+                int tile, part, s0, s1;
+                unit_range(p, u, tile, part, s0, s1);
+                for (int sk = s0; sk < s1; ++sk, ++g) {
+                    if (g >= NR && !tc::mbar_wait_bounded(&rawfree[s], (uint32_t)((ph - 1) & 1), abort_flag, p.err,
+                                                          kErrProd, kTimeoutNs)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::mbar_arrive_expect_tx(&full[s], kStageTx);
+                    tc::tma_load_2d(smem + L::r + s * L::kStage, &tm_w, sk * (INT4 ? 64 : 128), tile * WM, &full[s]);
+                    if (!waited) {
+                        pend_k[pend_n++] = sk * WSK;  // stage g == slot g here (g < NR)
+                        if (pend_n == NR) {
+                            pdl_wait();
+                            waited = true;
+                            for (int i = 0; i < pend_n; ++i) issue_x(i, pend_k[i]);
+                        }
+                    } else {
+                        issue_x(s, sk * WSK);
+                    }
+                    if (++s == NR) {
+                        s = 0;
+                        ++ph;
+                    }
+                }
+            }
+            if (!waited) {
+                pdl_wait();
+                if (ok)
+                    for (int i = 0; i < pend_n; ++i) issue_x(i, pend_k[i]);
+            }
+            pdl_trigger();
+            if (*abort_flag) {  // let the copies already issued land before the CTA exits
+                volatile int no_abort = 0;
+                for (int j = g > NR ? g - NR : 0; j < g; ++j)
+                    tc::mbar_wait_bounded(&full[j % NR], (j / NR) & 1, &no_abort, p.err, kErrDrain, 100000000ull);
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        // ------------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc::idesc_f16_f32(WM, NBT);
+            const uint64_t a_d = tc::desc_sw128(tc::smem_u32(smem + L::a));
+            const uint64_t b_d = tc::desc_sw128(tc::smem_u32(smem + L::r + L::kRawMax));
+            int s = 0, sph = 0, a = 0, aph = 0, gs = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+                int tile, part, s0, s1;
+                unit_range(p, u, tile, part, s0, s1);
+                for (int sk = s0; sk < s1; ++sk) {
+                    ok = tc::mbar_wait_bounded(&conv[a], (uint32_t)(aph & 1), abort_flag, p.err, kErrMma, kTimeoutNs) &&
+                         tc::mbar_wait_bounded(&full[s], (uint32_t)(sph & 1), abort_flag, p.err, kErrMma, kTimeoutNs);
+                    if (!ok) break;
+                    tc::tc_fence_after();
+                    const uint64_t abase = a_d + (uint64_t)(a * (kABytes >> 4));
+                    const uint64_t hbase = b_d + (uint64_t)(s * (L::kStage >> 4));
+                    const uint64_t lbase = hbase + (uint64_t)((2 * L::kBBlock) >> 4);
+                    // group-scale mode: one accumulator per 32 of K; row-scale mode: one per stage
+                    constexpr int kAccPerStage = GROUPED ? kGroupsPerStage : 1;
+                    constexpr int kStepsPerAcc = (WSK / 16) / kAccPerStage;
+#pragma unroll
+                    for (int gi = 0; gi < kAccPerStage; ++gi) {
+                        const int slot = gs % kSlots, use = gs / kSlots;
+                        if (use >= 1 && !tc::mbar_wait_bounded(&accempty[slot], (uint32_t)((use - 1) & 1), abort_flag,
+                                                               p.err, kErrMma, kTimeoutNs)) {
+                            ok = false;
+                            break;
+                        }
+                        tc::tc_fence_after();
+                        const uint32_t d = tmem_base + (uint32_t)(slot * SP);
+#pragma unroll
+                        for (int ks = 0; ks < kStepsPerAcc; ++ks) {
+                            const int k = (gi * kStepsPerAcc + ks) * 16;           // K offset in the stage
+                            const uint64_t off = (uint64_t)((k & 63) >> 3);  // 16-byte units in the 128-byte row
+                            const uint64_t ad = abase + (uint64_t)((k >> 6) * (kABlock >> 4)) + off;
+                            const uint64_t bh = hbase + (uint64_t)((k >> 6) * (L::kBBlock >> 4)) + off;
+                            const uint64_t bl = lbase + (uint64_t)((k >> 6) * (L::kBBlock >> 4)) + off;
+                            tc::mma_f16(d, ad, bh, idesc, ks > 0 ? 1u : 0u);  // the accumulator's first K-step starts it
+                            tc::mma_f16(d, ad, bl, idesc, 1u);
+                        }
+                        tc::mma_commit(&accfull[slot]);
+                        ++gs;
+                    }
+                    if (!ok) break;
+                    tc::mma_commit(&rawfree[s]);
+                    tc::mma_commit(&aempty[a]);
+                    if (++s == NR) {
+                        s = 0;
+                        ++sph;
+                    }
+                    if (++a == NA) {
+                        a = 0;
+                        ++aph;
+                    }
+                }
+            }
+            // every MMA this thread issued must complete before TMEM is released
+            tc::mma_commit(drain);
+            volatile int no_abort = 0;
+            tc::mbar_wait_bounded(drain, 0, &no_abort, p.err, kErrDrain, kTimeoutNs);
+        }
+    } else if (warp < kEpiWarp0) {
+        // ------------------------------------------------------------------ converters
+        const int r = threadIdx.x - kConvWarp0 * 32;  // weight row of the tile
+        int s = 0, sph = 0, a = 0, aph = 0, g = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+            int tile, part, s0, s1;
+            unit_range(p, u, tile, part, s0, s1);
+            for (int sk = s0; sk < s1; ++sk, ++g) {
+                int w_ok = 1;
+                if (lane == 0) {
+                    w_ok = tc::mbar_wait_bounded(&full[s], (uint32_t)(sph & 1), abort_flag, p.err, kErrConv, kTimeoutNs);
+                    if (w_ok && g >= NA)
+                        w_ok = tc::mbar_wait_bounded(&aempty[a], (uint32_t)((aph - 1) & 1), abort_flag, p.err, kErrConv,
+                                                     kTimeoutNs);
+                }
+                w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
+                if (!w_ok) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t *raw = smem + L::r + s * L::kStage;
+                uint8_t *ab = smem + L::a + a * kABytes;
+                if constexpr (INT4) {
+                    // 64-byte rows, 64-byte TMA swizzle: chunk c at ((c ^ ((r >> 1) & 3)) << 4); chunk c
+                    // holds K [32c, 32c + 32): one scale group
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const uint4 w = *reinterpret_cast<const uint4 *>(raw + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+                        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {  // word i: K [32c + 8i, 32c + 8i + 8)
+                            uint32_t h[4];
+                            u4x8_to_h(ws[i], h);
+                            const int k = 32 * c + 8 * i;
+                            *reinterpret_cast<uint4 *>(ab + (k >> 6) * kABlock + sw128_off(r, (k & 63) >> 3)) =
+                                make_uint4(h[0], h[1], h[2], h[3]);
+                        }
+                    }
+                } else {
+                    // 128-byte rows, 128-byte TMA swizzle: chunk c (16 of K) at ((c ^ (r & 7)) << 4)
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const uint4 w = *reinterpret_cast<const uint4 *>(raw + r * 128 + ((c ^ (r & 7)) << 4));
+                        uint32_t h[8];
+                        i8x4_to_h(w.x, h[0], h[1]);
+                        i8x4_to_h(w.y, h[2], h[3]);
+                        i8x4_to_h(w.z, h[4], h[5]);
+                        i8x4_to_h(w.w, h[6], h[7]);
+                        const int k = 16 * c;
+                        uint8_t *blk = ab + (k >> 6) * kABlock;
+                        *reinterpret_cast<uint4 *>(blk + sw128_off(r, (k & 63) >> 3)) = make_uint4(h[0], h[1], h[2], h[3]);
+                        *reinterpret_cast<uint4 *>(blk + sw128_off(r, ((k & 63) >> 3) + 1)) =
+                            make_uint4(h[4], h[5], h[6], h[7]);
+                    }
+                }
+                tc::fence_proxy_async_smem();  // the fp16 tile -> the tensor core's reads
+                __syncwarp();
+                if (lane == 0) {
+                    tc::mbar_arrive(&conv[a]);
+                    tc::mbar_arrive(&rawfree[s]);
+                }
+                if (++s == NR) {
+                    s = 0;
+                    ++sph;
+                }
+                if (++a == NA) {
+                    a = 0;
+                    ++aph;
+                }
+            }
+        }
+    } else {
+        // ------------------------------------------------------------------ epilogue
+        // All four warps run the same unit / stage sequence and the same named barriers; a warp
+        // whose wait ran out skips the work but keeps the barrier sequence.
+        const int q = warp & 3;  // TMEM lane quarter
+        const int rl = 32 * q + lane;
+        const int gpr = p.K / WG;  // scale groups per row
+        pdl_wait();                // y and the partial sums are written after the previous kernel
+        int gs = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+            int tile, part, s0, s1;
+            unit_range(p, u, tile, part, s0, s1);
+            const int row = tile * WM + rl;
+            const bool rowok = row < p.N;
+            float acc[NBT];
+#pragma unroll
+            for (int t = 0; t < NBT; ++t) acc[t] = 0.f;
+            for (int sk = s0; sk < s1; ++sk) {
+                float4 sc4 = make_float4(1.f, 1.f, 1.f, 1.f);
+                if (GROUPED && rowok) sc4 = __ldg(reinterpret_cast<const float4 *>(p.scales + (size_t)row * gpr + sk * 4));
+                const float scs[4] = {sc4.x, sc4.y, sc4.z, sc4.w};
+                constexpr int kAccPerStage = GROUPED ? kGroupsPerStage : 1;
+#pragma unroll
+                for (int gi = 0; gi < kAccPerStage; ++gi) {
+                    const int slot = gs % kSlots, use = gs / kSlots;
+                    ++gs;
+                    if (ok) ok = tc::mbar_wait_bounded(&accfull[slot], (uint32_t)(use & 1), abort_flag, p.err, kErrEpi,
+                                                       kTimeoutNs);
+                    ok = __all_sync(0xffffffffu, ok);
+                    if (!ok) continue;
+                    tc::tc_fence_after();
+                    float D[NBT];
+                    const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(slot * SP);
+#pragma unroll
+                    for (int c = 0; c < NBT / 16; ++c) tmem_ld16f(taddr + 16 * c, D + 16 * c);
+                    tc::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(&accempty[slot]);
+                    if constexpr (GROUPED) {
+                        const float sg = scs[gi];
+#pragma unroll
+                        for (int t = 0; t < NBT; ++t) acc[t] = fmaf(sg, D[t], acc[t]);
+                    } else {
+#pragma unroll
+                        for (int t = 0; t < NBT; ++t) acc[t] = __fadd_rn(acc[t], D[t]);
+                    }
+                }
+            }
+            const float rs = (!GROUPED && rowok) ? __ldg(p.scales + row) : 1.f;
+            if (p.parts == 1) {
+                if (ok && rowok) {
+#pragma unroll
+                    for (int t = 0; t < NBT; ++t)
+                        if (t < p.M) p.Y[(size_t)t * p.ldy + row] = (acc[t] * rs) * __ldg(p.xinv + t);
+                }
+            } else {
+                float *mine = p.partial + (size_t)u * NBT * WM + rl;
+#pragma unroll
+                for (int t = 0; t < NBT; ++t)
+                    if (t < p.M) mine[(size_t)t * WM] = acc[t];
+                __threadfence();
+                named_bar(1, kNumEpi * 32);
+                if (threadIdx.x == kEpiWarp0 * 32) {
+                    const unsigned old = atomicAdd(&p.tickets[tile], 1u);
+                    *last_flag = old == (unsigned)(p.parts - 1);
+                }
+                named_bar(1, kNumEpi * 32);
+                if (*last_flag) {
+                    __threadfence();
+                    if (ok && rowok) {
+                        const float *base = p.partial + (size_t)tile * p.parts * NBT * WM + rl;
+#pragma unroll 4
+                        for (int t = 0; t < NBT; ++t) {
+                            if (t >= p.M) break;
+                            float y = __ldcg(base + (size_t)t * WM);
+                            for (int pp = 1; pp < p.parts; ++pp) y += __ldcg(base + ((size_t)pp * NBT + t) * WM);
+                            p.Y[(size_t)t * p.ldy + row] = (y * rs) * __ldg(p.xinv + t);
+                        }
+                    }
+                    if (threadIdx.x == kEpiWarp0 * 32) p.tickets[tile] = 0;  // re-armed for the next launch
+                }
+                named_bar(1, kNumEpi * 32);  // last_flag is reused by the next unit
+            }
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// One CTA per token row: e = 15 - exponent(max|x|) so |x 2^e| < 2^15; hi = fp16(x 2^e),
+// lo = fp16(x 2^e - hi); inv = 2^-e.  PERM writes each 8-element group in the int4 converter's
+// order (e0, e4, e1, e5, e2, e6, e3, e7).
+template <bool PERM>
+__global__ void __launch_bounds__(256) split_x_ws_kernel(const float *__restrict__ X, long long ldx, int K,
+                                                         __half *__restrict__ hi, __half *__restrict__ lo,
+                                                         float *__restrict__ inv) {
+    __shared__ float red[8];
+    pdl_wait();
+    pdl_trigger();
+    const int m = blockIdx.x;
+    const float *x = X + (size_t)m * ldx;
+    float mx = 0.f;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(x[k]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w]);
+    int e = 0;
+    if (mx > 0.f && isfinite(mx)) {
+        int ex;
+        frexpf(mx, &ex);  // mx = f 2^ex, f in [0.5, 1)
+        e = 15 - ex;
+        e = e > 120 ? 120 : (e < -120 ? -120 : e);
+    }
+    if (threadIdx.x == 0) inv[m] = ldexpf(1.0f, -e);
+    __half *hrow = hi + (size_t)m * K, *lrow = lo + (size_t)m * K;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        const float v = ldexpf(x[k], e);
+        const __half h = __float2half_rn(v);
+        const __half l = __float2half_rn(v - __half2float(h));
+        int d = k;
+        if (PERM) {
+            const int o = k & 7;
+            d = (k & ~7) | (o < 4 ? 2 * o : 2 * (o - 4) + 1);
+        }
+        hrow[d] = h;
+        lrow[d] = l;
+    }
+}
+
+// ------------------------------------------------------------------------------ host side --
+int nbt_for(size_t M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 48 ? 48 : 64; }
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// K parts per tile: minimises the stages of the busiest CTA, ceil(units / grid) * ceil(S / parts),
+// with partial sums no larger than `partial_cap` bytes when a tile is split.
+int choose_parts(size_t N, size_t K, int nbt, int num_sms, size_t partial_cap) {
+    const long T = (long)((N + WM - 1) / WM), S = (long)(K / WSK);
+    long best_cost = -1;
+    int best = 1;
+    for (long P = 1; P <= S && P <= 64; ++P) {
+        const long units = T * P;
+        if (P > 1 && (size_t)units * nbt * WM * 4 > partial_cap) break;
+        const long grid = std::min<long>(num_sms, units);
+        const long cost = (units + grid - 1) / grid * ((S + P - 1) / P);
+        if (best_cost < 0 || cost < best_cost) {
+            best_cost = cost;
+            best = (int)P;
+        }
+    }
+    return best;
+}
+
+struct WsLayout {
+    size_t xhi, xlo, xinv, partial, total;
+};
+WsLayout ws_layout(size_t M, size_t K, size_t partial_bytes) {
+    WsLayout l;
+    const size_t xb = align_up(M * K * 2, 1024);
+    l.xhi = 0;
+    l.xlo = xb;
+    l.xinv = 2 * xb;
+    l.partial = align_up(l.xinv + M * 4, 1024);
+    l.total = l.partial + partial_bytes;
+    return l;
+}
+
+bool make_map(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t outer,
+              uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+    auto fn = tensor_map_encoder();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t es[2] = {1, 1};
+    return fn(m, dt, 2, const_cast<void *>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int NBT, bool INT4, bool GROUPED>
+cudaError_t run_ws(const CUtensorMap &tw, const CUtensorMap &th, const CUtensorMap &tl, const WsParams &p, int grid,
+                   cudaStream_t st) {
+    auto kern = gemm_ws_kernel<NBT, INT4, GROUPED>;
+    static std::atomic<uint64_t> attr_done{0};
+    const cudaError_t e = once_per_device(attr_done, [&] {
+        return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)WsSmem<NBT>::bytes);
+    });
+    if (e != cudaSuccess) return e;
+    return launch_kernel(kern, dim3(grid), dim3(kThreads), WsSmem<NBT>::bytes, st, tw, th, tl, p);
+}
+
+template <bool INT4, bool GROUPED>
+cudaError_t dispatch_nbt(int nbt, const CUtensorMap &tw, const CUtensorMap &th, const CUtensorMap &tl,
+                         const WsParams &p, int grid, cudaStream_t st) {
+    switch (nbt) {
+    case 16: return run_ws<16, INT4, GROUPED>(tw, th, tl, p, grid, st);
+    case 32: return run_ws<32, INT4, GROUPED>(tw, th, tl, p, grid, st);
+    case 48: return run_ws<48, INT4, GROUPED>(tw, th, tl, p, grid, st);
+    default: return run_ws<64, INT4, GROUPED>(tw, th, tl, p, grid, st);
+    }
+}
+
+}  // namespace
+
+bool gemm_ws_supported(const QMatrix &w, size_t M) {
+    if (M < 1 || M > (size_t)kMaxTokens || w.N == 0 || w.N > (size_t)INT32_MAX / 2) return false;
+    if (w.K == 0 || w.K % WSK != 0 || w.K > (1u << 20)) return false;
+    if (reinterpret_cast<uintptr_t>(w.data) & 15 || reinterpret_cast<uintptr_t>(w.scales) & 15) return false;
+    if (w.qtype == kQInt4) return w.block_size == (size_t)WG;
+    if (w.qtype == kQInt8) return w.block_size == (size_t)WG || w.block_size == w.K;
+    return false;
+}
+
+size_t gemm_ws_workspace_bytes(size_t M, size_t N, size_t K, int num_sms, size_t partial_cap) {
+    const int nbt = nbt_for(M);
+    const int parts = choose_parts(N, K, nbt, num_sms, partial_cap);
+    const size_t tiles = (N + WM - 1) / WM;
+    const size_t partial = parts > 1 ? tiles * parts * nbt * WM * 4 : 0;
+    return ws_layout(M, K, partial).total;
+}
+
+cudaError_t launch_gemm_ws(const QMatrix &w, const float *X, size_t M, size_t ldx, float *Y, size_t ldy, void *ws,
+                           size_t ws_bytes, unsigned *tickets, size_t num_tickets, int *err, int num_sms,
+                           cudaStream_t st) {
+    if (!gemm_ws_supported(w, M)) return cudaErrorInvalidValue;
+    const int nbt = nbt_for(M);
+    const size_t tiles = (w.N + WM - 1) / WM;
+    if (tiles > num_tickets) return cudaErrorInvalidValue;
+    // the partial sums may use whatever the workspace holds beyond x's fp16 copies
+    const WsLayout base = ws_layout(M, w.K, 0);
+    if (ws_bytes < base.total || (reinterpret_cast<uintptr_t>(ws) & 255)) return cudaErrorInvalidValue;
+    const int parts = choose_parts(w.N, w.K, nbt, num_sms, ws_bytes - base.partial);
+    uint8_t *wsb = static_cast<uint8_t *>(ws);
+    __half *xhi = reinterpret_cast<__half *>(wsb + base.xhi), *xlo = reinterpret_cast<__half *>(wsb + base.xlo);
+    float *xinv = reinterpret_cast<float *>(wsb + base.xinv);
+    const bool int4 = w.qtype == kQInt4, grouped = w.block_size == (size_t)WG;
+
+    CUtensorMap tw, th, tl;
+    const uint64_t row_bytes = int4 ? w.K / 2 : w.K;
+    if (!make_map(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.data, row_bytes, w.N, row_bytes, int4 ? 64 : 128, WM,
+                  int4 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map(&th, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xhi, w.K, M, w.K * 2, 64, (uint32_t)nbt,
+                  CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map(&tl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xlo, w.K, M, w.K * 2, 64, (uint32_t)nbt,
+                  CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+
+    cudaError_t e = int4 ? launch_kernel(split_x_ws_kernel<true>, dim3((unsigned)M), dim3(256), 0, st, X,
+                                         (long long)ldx, (int)w.K, xhi, xlo, xinv)
+                         : launch_kernel(split_x_ws_kernel<false>, dim3((unsigned)M), dim3(256), 0, st, X,
+                                         (long long)ldx, (int)w.K, xhi, xlo, xinv);
+    if (e != cudaSuccess) return e;
+
+    WsParams p{};
+    p.M = (int)M;
+    p.N = (int)w.N;
+    p.K = (int)w.K;
+    p.tiles = (int)tiles;
+    p.parts = parts;
+    p.stages_k = (int)(w.K / WSK);
+    p.units = (int)tiles * parts;
+    p.scales = w.scales;
+    p.xinv = xinv;
+    p.Y = Y;
+    p.ldy = (long long)ldy;
+    p.partial = reinterpret_cast<float *>(wsb + base.partial);
+    p.tickets = tickets;
+    p.err = err;
+    const int grid = std::min(num_sms, p.units);
+    if (int4) return dispatch_nbt<true, true>(nbt, tw, th, tl, p, grid, st);
+    return grouped ? dispatch_nbt<false, true>(nbt, tw, th, tl, p, grid, st)
+                   : dispatch_nbt<false, false>(nbt, tw, th, tl, p, grid, st);
+}
+
+const char *gemm_ws_kernel_name() { return "gemm_ws_kernel"; }
+
+}  // namespace pyxis

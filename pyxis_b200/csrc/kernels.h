@@ -77,6 +77,17 @@ size_t gemv_tc_scratch_bytes(int max_grid);
 cudaError_t launch_gemv_tc(const QMatrix &w, const float *X, size_t B, size_t ldx, float *Y, size_t ldy,
                            void *scratch, size_t scratch_bytes, int *err, int num_sms, cudaStream_t st);
 
+// Weight-streaming matmul for 1..64 tokens on tcgen05 (gemm_ws.cu): int4 or int8 codes with a scale
+// per group of 32, or int8 with one scale per row; K % 128 == 0.  The workspace holds x's fp16
+// hi / lo copies (gemm_ws_workspace_bytes(M, N, K, sms, 0) bytes, 256-byte aligned) and, in what
+// is left, the partial sums of tiles split along K; `tickets` (one per 128-row tile) must be zero
+// before the first launch and are left zero.
+bool gemm_ws_supported(const QMatrix &w, size_t M);
+size_t gemm_ws_workspace_bytes(size_t M, size_t N, size_t K, int num_sms, size_t partial_cap);
+cudaError_t launch_gemm_ws(const QMatrix &w, const float *X, size_t M, size_t ldx, float *Y, size_t ldy, void *ws,
+                           size_t ws_bytes, unsigned *tickets, size_t num_tickets, int *err, int num_sms,
+                           cudaStream_t st);
+
 // Records `msg` as the calling thread's pyxis_cuda_last_error() and returns `code` (api.cu).
 int record_error(int code, const char *msg);
 

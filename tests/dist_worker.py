@@ -1,6 +1,9 @@
 """One rank of the multi-GPU check (launched by tests/test_dist_gpu.py through torchrun, one
 process per GPU, NCCL):
-  * row-sharded GEMVs all-gathered equal the single-GPU product bit for bit;
+  * row-sharded products all-gathered equal the single-GPU product: bit for bit where the kernel's
+    per-row arithmetic does not depend on the row count (the GEMVs), within the matmul bar
+    (max_i |y_i - r_i| / max(|r_i|, 1e-3 max|r|) <= 1e-3) where the weight-streaming matmul splits K
+    by the number of tiles;
   * the vocab-parallel lm_head's device-side greedy argmax (pyxis_cuda_head_greedy_dev) equals
     the single-GPU argmax, int8 per-row and int4 group-32 heads, 1 to 64 rows, including a NaN at
     index 0, -0.0 against +0.0 and ties across the shard boundary;
@@ -21,6 +24,7 @@ sys.path.insert(0, os.path.dirname(HERE))
 sys.path.insert(0, HERE)
 
 import oracle  # noqa: E402
+from parity import rel_err  # noqa: E402
 import pyxis_b200 as px  # noqa: E402
 from pyxis_b200 import _native  # noqa: E402
 from pyxis_b200.dist import Comm, RowShardedMatmul, VocabParallelHead, shard_range  # noqa: E402
@@ -46,7 +50,11 @@ def main():
             y_sh = sh.forward_gathered(X)
             y_full = px.matmul_dev(X, full, N, K)
             torch.cuda.synchronize()
-            if not torch.equal(y_sh, y_full):
+            if px.matmul_kernel_name(full, B, N, K) == "gemm_ws_kernel":
+                err = rel_err(y_sh.cpu().numpy(), y_full.cpu().numpy())
+                if err > 1e-3:
+                    fails.append(f"row-sharded {qt} {N}x{K} B={B}: rel err {err}")
+            elif not torch.equal(y_sh, y_full):
                 fails.append(f"row-sharded {qt} {N}x{K} B={B} differs: {(y_sh - y_full).abs().max().item()}")
 
     comm = Comm(rank, world, local)

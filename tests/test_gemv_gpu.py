@@ -141,11 +141,12 @@ def test_argmax_rules():
     (4096, 4096, 4), (129, 1024, 8), (151936, 2048, 8),
 ])
 def test_int8_row_scale_tensor_core_gemv(N, K, B):
-    """int8 with one scale per row at batch 1-8.  From 32768 output rows (the lm_head) it runs
+    """int8 with one scale per row at batch 1-8.  From 16384 output rows (the lm_head and its
+    vocab shards on up to 8 GPUs) it runs
     tcgen05 kind::i8 with x as int8 digits and stream-K (tiles shared by two CTAs added with exact
     int32 atomics); below that the CUDA-core batch kernel, which finishes first at those sizes."""
     w, od, os_ = make("int8", N, K, K, seed=N + K + B)
-    assert px.matmul_kernel_name(w, B, N, K) == ("gemv_tc_i8_kernel" if N >= 32768 else "gemv_batch_kernel")
+    assert px.matmul_kernel_name(w, B, N, K) == ("gemv_tc_i8_kernel" if N >= 16384 else "gemv_batch_kernel")
     X = px.synth_normal_f32(B * 31 + 7, B * K, 1.0).reshape(B, K)
     X[0, :5] = [0.0, -0.0, 1e-30, -3e4, 2.5]
     for rep in range(2):  # the split-K scratch must be left clean for the next launch
@@ -156,18 +157,20 @@ def test_int8_row_scale_tensor_core_gemv(N, K, B):
 
 
 @pytest.mark.parametrize("qt,N,K,bs,B", [
-    ("int4", 2048, 2048, 32, 2), ("int4", 2048, 2048, 32, 5), ("int4", 2048, 6144, 32, 7),
-    ("int4", 64, 12288, 32, 2),    # two TMA boxes per token
-    ("int4", 10, 9600, 32, 2),     # 300 rows of x: boxes of 152 rows, the last one overhangs
+    # K % 128 != 0 keeps group-32 batches of 2-8 rows off the weight-streaming matmul
+    ("int4", 2048, 2016, 32, 2), ("int4", 2048, 2016, 32, 5), ("int4", 2048, 6112, 32, 7),
+    ("int4", 64, 12256, 32, 2),    # two TMA boxes per token
+    ("int4", 10, 9632, 32, 2),     # 301 rows of x: boxes of 152 rows, the last one overhangs
     ("int4", 100, 416, 32, 3),     # 13 rows of x in a 16-row box
-    ("int4", 40000, 2048, 32, 4),  # many row-group items per CTA (double-buffered combine)
+    ("int4", 40000, 2016, 32, 4),  # many row-group items per CTA (double-buffered combine)
     ("int4", 1779, 2048, 64, 6),   # N % 4 != 0, 64-value groups (2 chunks per scale)
-    ("int8", 6144, 2048, 32, 8),   # GGUF Q8_0 layout at batch 8
+    ("int8", 6144, 2016, 32, 8),   # GGUF Q8_0 layout at batch 8
     ("int8", 515, 4096, 128, 3),
     ("int4", 300, 4096, 4096, 8),  # int4 with one scale per row
 ])
 def test_batch_kernel(qt, N, K, bs, B):
-    """The CUDA-core batch kernel (x staged by TMA, split-K over warps, fixed-order combine)."""
+    """The CUDA-core batch kernel (x staged by TMA, split-K over warps, fixed-order combine): every
+    batch-1 product, and the batches of 2-8 rows the weight-streaming matmul does not take."""
     w, od, os_ = make(qt, N, K, bs, seed=N + 3 * K + bs + B)
     assert px.matmul_kernel_name(w, B, N, K) == "gemv_batch_kernel"
     X = px.synth_normal_f32(B * 13 + 1, B * K, 1.0).reshape(B, K)
