@@ -145,8 +145,8 @@ int pyxis_cuda_matmul_batch(pyxis_cuda_ctx *ctx, const float *input, size_t M,
  * with row stride ldx (elements), Y [M, out] f32 with row stride ldy.  Kernels by shape:
  *  - M = 1: the decode GEMVs (CUDA cores; int8 one-scale-per-row matrices of >= 16384 rows on
  *    the tensor cores, kind::i8);
- *  - 2..64 rows of int4 / int8 with a scale per 32 values, or 9..64 rows of int8 with one scale per
- *    row, in_features % 128 == 0: the weight-streaming tensor-core matmul;
+ *  - 9..64 rows of int4 / int8 with a scale per 32 values or int8 with one scale per row,
+ *    in_features % 128 == 0: the weight-streaming tensor-core matmul;
  *  - other M <= 15: the GEMVs, 8 rows per launch; M >= 16 with int8/int4 weights: the tensor-core
  *    prefill GEMM.
  * The tensor-core products need `workspace` of pyxis_cuda_matmul_workspace_size() bytes (device

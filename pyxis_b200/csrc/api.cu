@@ -165,13 +165,14 @@ int ensure_ctx_workspace(pyxis_cuda_ctx *ctx, size_t want, cudaStream_t st) {
 int pyxis::record_error(int code, const char *msg) { return fail(code, "%s", msg); }
 
 namespace {
-// Weight-streaming tensor-core matmul for decode-shaped batches: int4 / int8 group-32 weights from 2
-// tokens (one token stays on the CUDA-core GEMV), int8 one-scale-per-row weights from 9 (up to 8
-// the exact kind::i8 GEMV or the batch GEMV), up to 64 tokens.
-bool use_gemm_ws(const QMatrix &q, size_t M) {
-    if (!gemm_ws_supported(q, M)) return false;
-    return q.block_size == q.K ? M >= 9 : M >= 2;
-}
+// Weight-streaming tensor-core matmul for decode-shaped batches of 9-64 tokens (int4 / int8 with
+// group-32 scales, int8 with one scale per row).  Its MMAs are K = 16 fp16 instructions with x as hi
+// and lo halves, 16 per 128 of K and 128 rows, and a tcgen05.mma costs about 128 cycles at any N up
+// to 256 (measured per stage: 1.05 us at 16 token columns, 1.2 us at 64), so the instruction count,
+// not the token count, sets its pace: it wins where the CUDA cores' FMAs per weight grow with the
+// tokens (int4 gate|up 12288 x 2048 at 64 tokens: 22 us against 67 us on the prefill GEMM), while
+// up to 8 tokens the batch GEMV streams faster.
+bool use_gemm_ws(const QMatrix &q, size_t M) { return M >= 9 && gemm_ws_supported(q, M); }
 
 bool use_gemm_tc(const QMatrix &q, size_t M, const float *X, size_t ldx) {
     return M >= kTcMinRows && gemm_tc_supported(q) && (reinterpret_cast<uintptr_t>(X) & 15) == 0 && ldx % 4 == 0;

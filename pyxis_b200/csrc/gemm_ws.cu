@@ -45,9 +45,7 @@ constexpr int WM = 128;       // weight rows per tile: MMA M, TMEM lanes
 constexpr int WSK = 128;      // K per stage
 constexpr int WG = 32;        // K per scale group (group-scale mode)
 constexpr int kGroupsPerStage = WSK / WG;
-constexpr int kProdWarp = 0, kMmaWarp = 1, kConvWarp0 = 2, kNumConv = 4, kEpiWarp0 = 6, kNumEpi = 4;
-constexpr int kThreads = (kEpiWarp0 + kNumEpi) * 32;  // 320
-constexpr int kSlots = 8;                              // group accumulators in flight (TMEM)
+constexpr int kProdWarp = 0, kMmaWarp = 1, kConvWarp0 = 2, kNumConv = 4, kEpiWarp0 = 6;
 constexpr int kMaxTokens = 64;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 constexpr uint32_t kABlock = WM * 128;      // one column block (64 of K) of the fp16 weight tile
@@ -94,19 +92,6 @@ PYXIS_DEVINL uint32_t sw128_off(int r, int c) { return (r >> 3) * 1024 + (r & 7)
 
 PYXIS_DEVINL void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
-// 16 consecutive fp32 columns of this warp's 32 TMEM lanes, waited for.
-PYXIS_DEVINL void tmem_ld16f(uint32_t taddr, float *v) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
 // Unit u = (tile u / parts, part u % parts); part p covers stages [p S / parts, (p + 1) S / parts)
 // of the row (S = stages_k).  A CTA takes units blockIdx.x, blockIdx.x + gridDim.x, ...
 PYXIS_DEVINL void unit_range(const WsParams &p, int u, int &tile, int &part, int &s0, int &s1) {
@@ -115,6 +100,25 @@ PYXIS_DEVINL void unit_range(const WsParams &p, int u, int &tile, int &part, int
     s0 = part * p.stages_k / p.parts;
     s1 = (part + 1) * p.stages_k / p.parts;
 }
+
+// Epilogue warps: 4 lane quarters x EW column slices of CW = 16 token columns (a warp's
+// accumulators and two readback buffers stay within the register budget of up to 704 threads).
+template <int NBT>
+struct WsRoles {
+    static constexpr int CW = 16;
+    static constexpr int EW = NBT / CW;
+    static constexpr int kEpiWarps = 4 * EW;
+    static constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;  // 320, 448 or 704
+    // TMEM accumulators: a group's two K-steps go to two accumulators (KS = 2) when they fit, so a
+    // stage issues 8 independent chains of 2 MMAs (x_hi, x_lo) instead of 4 chains of 4: the MMA
+    // pipe runs in order and a dependent MMA waits for its predecessor's result.  Two stages'
+    // accumulators (sets) are in flight: the MMAs of one while the epilogue reads the other.
+    static constexpr int KS = NBT <= 32 ? 2 : 1;
+    static constexpr int kAccPerStage = kGroupsPerStage * KS;
+    static constexpr int kSetCols = kAccPerStage * NBT;
+    static constexpr uint32_t kTmemCols = 2 * kSetCols <= 128 ? 128 : (2 * kSetCols <= 256 ? 256 : 512);
+    static_assert(2 * kSetCols <= 512, "two sets of accumulators fit in TMEM");
+};
 
 template <int NBT>
 struct WsSmem {
@@ -126,19 +130,53 @@ struct WsSmem {
     static constexpr uint32_t a = 0;
     static constexpr uint32_t r = a + NA * kABytes;
     static constexpr uint32_t bar = r + NR * kStage;
-    static constexpr uint32_t num_bars = 2 * NR + 2 * NA + 2 * kSlots + 1;
+    static constexpr uint32_t num_bars = 2 * NR + 2 * NA + 4 + 1;
     static constexpr uint32_t misc = bar + num_bars * 8;
     static constexpr uint32_t bytes = misc + 64 + 1024;  // + alignment slack
 };
-static_assert(WsSmem<16>::bytes <= 232448 && WsSmem<32>::bytes <= 232448 && WsSmem<48>::bytes <= 232448 &&
-                  WsSmem<64>::bytes <= 232448,
+static_assert(WsSmem<16>::bytes <= 232448 && WsSmem<32>::bytes <= 232448 && WsSmem<64>::bytes <= 232448,
               "227 KB of shared memory per CTA");
 
+// CW token columns of this warp's 32 TMEM lanes, without waiting (valid after tmem_wait_regs).
+template <int CW>
+PYXIS_DEVINL void tmem_ld_cols(uint32_t taddr, float (&v)[CW]) {
+    uint32_t *r = reinterpret_cast<uint32_t *>(v);
+    if constexpr (CW == 16) {
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+            : "r"(taddr));
+    } else {
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+              "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
+              "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+              "=r"(r[30]), "=r"(r[31])
+            : "r"(taddr));
+    }
+}
+
+// tcgen05.wait::ld, then the registers of v are passed through empty asm statements so that no
+// use of them is scheduled before the wait.
+template <int CW>
+PYXIS_DEVINL void tmem_wait_regs(float (&v)[CW]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < CW; i += 8)
+        asm volatile("" : "+f"(v[i]), "+f"(v[i + 1]), "+f"(v[i + 2]), "+f"(v[i + 3]), "+f"(v[i + 4]), "+f"(v[i + 5]),
+                     "+f"(v[i + 6]), "+f"(v[i + 7]));
+}
+
 template <int NBT, bool INT4, bool GROUPED>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
     gemm_ws_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_xhi,
                    const __grid_constant__ CUtensorMap tm_xlo, const WsParams p) {
     using L = WsSmem<NBT>;
+    using R = WsRoles<NBT>;
     constexpr int NR = L::NR, NA = L::NA;
     constexpr uint32_t kRaw = INT4 ? WM * 64 : WM * 128;
     constexpr uint32_t kStageTx = kRaw + 4 * L::kBBlock;
@@ -147,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::bar);
     uint64_t *full = bars, *rawfree = bars + NR;           // code / x stages
     uint64_t *conv = bars + 2 * NR, *aempty = conv + NA;   // converted weight tiles
-    uint64_t *accfull = aempty + NA, *accempty = accfull + kSlots, *drain = accempty + kSlots;
+    uint64_t *accfull = aempty + NA, *accempty = accfull + 2, *drain = accempty + 2;  // per accumulator set
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::misc);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::misc + 4);
     volatile int *last_flag = reinterpret_cast<volatile int *>(smem + L::misc + 8);
@@ -162,17 +200,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc::mbar_init(&conv[a], kNumConv);
             tc::mbar_init(&aempty[a], 1);
         }
-        for (int k = 0; k < kSlots; ++k) {
+        for (int k = 0; k < 2; ++k) {
             tc::mbar_init(&accfull[k], 1);
-            tc::mbar_init(&accempty[k], kNumEpi);
+            tc::mbar_init(&accempty[k], R::kEpiWarps);
         }
         tc::mbar_init(drain, 1);
         *abort_flag = 0;
         tc::fence_mbar_init();
     }
-    // accumulator slots at a power-of-two column pitch (48 tokens take 64 columns)
-    constexpr int SP = NBT == 48 ? 64 : NBT;
-    constexpr uint32_t kTmemCols = kSlots * SP <= 128 ? 128 : (kSlots * SP <= 256 ? 256 : 512);
+    constexpr uint32_t kTmemCols = R::kTmemCols;
     if (warp == kMmaWarp) tc::tmem_alloc(tmem_slot, kTmemCols);
     tc::tc_fence_before();
     __syncthreads();
@@ -242,46 +278,41 @@ __global__ void __launch_bounds__(kThreads, 1)
             constexpr uint32_t idesc = tc::idesc_f16_f32(WM, NBT);
             const uint64_t a_d = tc::desc_sw128(tc::smem_u32(smem + L::a));
             const uint64_t b_d = tc::desc_sw128(tc::smem_u32(smem + L::r + L::kRawMax));
-            int s = 0, sph = 0, a = 0, aph = 0, gs = 0;
+            int s = 0, sph = 0, a = 0, aph = 0, st = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
                 int tile, part, s0, s1;
                 unit_range(p, u, tile, part, s0, s1);
-                for (int sk = s0; sk < s1; ++sk) {
+                for (int sk = s0; sk < s1; ++sk, ++st) {
+                    const int set = st & 1, use = st >> 1;
                     ok = tc::mbar_wait_bounded(&conv[a], (uint32_t)(aph & 1), abort_flag, p.err, kErrMma, kTimeoutNs) &&
-                         tc::mbar_wait_bounded(&full[s], (uint32_t)(sph & 1), abort_flag, p.err, kErrMma, kTimeoutNs);
+                         tc::mbar_wait_bounded(&full[s], (uint32_t)(sph & 1), abort_flag, p.err, kErrMma, kTimeoutNs) &&
+                         (use == 0 || tc::mbar_wait_bounded(&accempty[set], (uint32_t)((use - 1) & 1), abort_flag,
+                                                            p.err, kErrMma, kTimeoutNs));
                     if (!ok) break;
                     tc::tc_fence_after();
                     const uint64_t abase = a_d + (uint64_t)(a * (kABytes >> 4));
                     const uint64_t hbase = b_d + (uint64_t)(s * (L::kStage >> 4));
                     const uint64_t lbase = hbase + (uint64_t)((2 * L::kBBlock) >> 4);
-                    // group-scale mode: one accumulator per 32 of K; row-scale mode: one per stage
-                    constexpr int kAccPerStage = GROUPED ? kGroupsPerStage : 1;
-                    constexpr int kStepsPerAcc = (WSK / 16) / kAccPerStage;
+                    const uint32_t dset = tmem_base + (uint32_t)(set * R::kSetCols);
+                    // K-step ks of group gi covers K [32 gi + 16 ks, +16) of the stage; the issue order
+                    // runs over the groups innermost, so consecutive MMAs use different accumulators
 #pragma unroll
-                    for (int gi = 0; gi < kAccPerStage; ++gi) {
-                        const int slot = gs % kSlots, use = gs / kSlots;
-                        if (use >= 1 && !tc::mbar_wait_bounded(&accempty[slot], (uint32_t)((use - 1) & 1), abort_flag,
-                                                               p.err, kErrMma, kTimeoutNs)) {
-                            ok = false;
-                            break;
-                        }
-                        tc::tc_fence_after();
-                        const uint32_t d = tmem_base + (uint32_t)(slot * SP);
+                    for (int ks = 0; ks < 2; ++ks)
 #pragma unroll
-                        for (int ks = 0; ks < kStepsPerAcc; ++ks) {
-                            const int k = (gi * kStepsPerAcc + ks) * 16;           // K offset in the stage
-                            const uint64_t off = (uint64_t)((k & 63) >> 3);  // 16-byte units in the 128-byte row
-                            const uint64_t ad = abase + (uint64_t)((k >> 6) * (kABlock >> 4)) + off;
-                            const uint64_t bh = hbase + (uint64_t)((k >> 6) * (L::kBBlock >> 4)) + off;
-                            const uint64_t bl = lbase + (uint64_t)((k >> 6) * (L::kBBlock >> 4)) + off;
-                            tc::mma_f16(d, ad, bh, idesc, ks > 0 ? 1u : 0u);  // the accumulator's first K-step starts it
-                            tc::mma_f16(d, ad, bl, idesc, 1u);
-                        }
-                        tc::mma_commit(&accfull[slot]);
-                        ++gs;
-                    }
-                    if (!ok) break;
+                        for (int hl = 0; hl < 2; ++hl)
+#pragma unroll
+                            for (int gi = 0; gi < kGroupsPerStage; ++gi) {
+                                const int k = gi * 32 + ks * 16;
+                                const uint64_t off = (uint64_t)((k >> 6) * (kABlock >> 4)) + (uint64_t)((k & 63) >> 3);
+                                const uint64_t boff = (uint64_t)((k >> 6) * (L::kBBlock >> 4)) + (uint64_t)((k & 63) >> 3);
+                                const int acc_i = gi * R::KS + (R::KS == 2 ? ks : 0);
+                                // an accumulator's first MMA starts it: (ks 0, x_hi), or with KS = 2 its x_hi
+                                const uint32_t accum = R::KS == 2 ? (uint32_t)hl : (uint32_t)(ks | hl);
+                                tc::mma_f16(dset + (uint32_t)(acc_i * NBT), abase + off, (hl ? lbase : hbase) + boff,
+                                            idesc, accum);
+                            }
+                    tc::mma_commit(&accfull[set]);
                     tc::mma_commit(&rawfree[s]);
                     tc::mma_commit(&aempty[a]);
                     if (++s == NR) {
@@ -373,87 +404,119 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ------------------------------------------------------------------ epilogue
-        // All four warps run the same unit / stage sequence and the same named barriers; a warp
-        // whose wait ran out skips the work but keeps the barrier sequence.
-        const int q = warp & 3;  // TMEM lane quarter
-        const int rl = 32 * q + lane;
+        // Warp (q, h): TMEM lane quarter q = warp % 4 (rows 32q..32q+31 of the tile, one per
+        // lane), token columns [h CW, h CW + CW).  Every group's readback is one tcgen05.ld issued
+        // before the previous group's FMAs, so the TMEM latency overlaps them.  All epilogue warps
+        // run the same unit / stage sequence and named barriers; a warp whose wait ran out skips
+        // the work but keeps the barrier sequence.
+        constexpr int CW = R::CW;
+        constexpr int kEpiThreads = R::kEpiWarps * 32;
+        const int q = warp & 3, h = (warp - kEpiWarp0) >> 2;
+        const int rl = 32 * q + lane, c0 = h * CW;
         const int gpr = p.K / WG;  // scale groups per row
         pdl_wait();                // y and the partial sums are written after the previous kernel
-        int gs = 0;
+        int st = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
             int tile, part, s0, s1;
             unit_range(p, u, tile, part, s0, s1);
             const int row = tile * WM + rl;
             const bool rowok = row < p.N;
-            float acc[NBT];
+            float acc[CW];
 #pragma unroll
-            for (int t = 0; t < NBT; ++t) acc[t] = 0.f;
-            for (int sk = s0; sk < s1; ++sk) {
+            for (int c = 0; c < CW; ++c) acc[c] = 0.f;
+            // A stage's 4 groups are read back in turn into two alternating buffers (4 is even, so
+            // group gi of every stage uses buffer gi % 2): the readback of group gi is issued before
+            // the FMAs of group gi - 1, so the TMEM latency overlaps them.  With row scales the 4
+            // groups' sums are added with scale 1 (exact).
+            float DA[R::KS * CW], DB[R::KS * CW];
+            float s_pend = 0.f;
+            bool pend = false;
+            auto fma_group = [&](float sg, const float (&D)[R::KS * CW]) {
+#pragma unroll
+                for (int c = 0; c < CW; ++c) {
+                    const float d = R::KS == 2 ? __fadd_rn(D[c], D[CW + c]) : D[c];
+                    acc[c] = fmaf(sg, d, acc[c]);
+                }
+            };
+            for (int sk = s0; sk < s1; ++sk, ++st) {
+                const int set = st & 1, use = st >> 1;
                 float4 sc4 = make_float4(1.f, 1.f, 1.f, 1.f);
                 if (GROUPED && rowok) sc4 = __ldg(reinterpret_cast<const float4 *>(p.scales + (size_t)row * gpr + sk * 4));
                 const float scs[4] = {sc4.x, sc4.y, sc4.z, sc4.w};
-                constexpr int kAccPerStage = GROUPED ? kGroupsPerStage : 1;
+                if (ok) ok = tc::mbar_wait_bounded(&accfull[set], (uint32_t)(use & 1), abort_flag, p.err, kErrEpi,
+                                                   kTimeoutNs);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) continue;
+                tc::tc_fence_after();
+                const uint32_t tset = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(set * R::kSetCols + c0);
 #pragma unroll
-                for (int gi = 0; gi < kAccPerStage; ++gi) {
-                    const int slot = gs % kSlots, use = gs / kSlots;
-                    ++gs;
-                    if (ok) ok = tc::mbar_wait_bounded(&accfull[slot], (uint32_t)(use & 1), abort_flag, p.err, kErrEpi,
-                                                       kTimeoutNs);
-                    ok = __all_sync(0xffffffffu, ok);
-                    if (!ok) continue;
-                    tc::tc_fence_after();
-                    float D[NBT];
-                    const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(slot * SP);
+                for (int gi = 0; gi < kGroupsPerStage; ++gi) {
+                    float(&Dn)[R::KS * CW] = (gi & 1) ? DB : DA;
+                    float(&Dp)[R::KS * CW] = (gi & 1) ? DA : DB;
 #pragma unroll
-                    for (int c = 0; c < NBT / 16; ++c) tmem_ld16f(taddr + 16 * c, D + 16 * c);
-                    tc::tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) tc::mbar_arrive(&accempty[slot]);
-                    if constexpr (GROUPED) {
-                        const float sg = scs[gi];
-#pragma unroll
-                        for (int t = 0; t < NBT; ++t) acc[t] = fmaf(sg, D[t], acc[t]);
-                    } else {
-#pragma unroll
-                        for (int t = 0; t < NBT; ++t) acc[t] = __fadd_rn(acc[t], D[t]);
-                    }
+                    for (int j = 0; j < R::KS; ++j)
+                        tmem_ld_cols<CW>(tset + (uint32_t)((gi * R::KS + j) * NBT),
+                                         *reinterpret_cast<float(*)[CW]>(Dn + j * CW));
+                    if (pend) fma_group(s_pend, Dp);
+                    tmem_wait_regs<R::KS * CW>(Dn);
+                    s_pend = scs[gi];
+                    pend = true;
                 }
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&accempty[set]);
             }
+            if (pend) fma_group(s_pend, DB);
             const float rs = (!GROUPED && rowok) ? __ldg(p.scales + row) : 1.f;
+            float *__restrict__ Y = p.Y;
             if (p.parts == 1) {
                 if (ok && rowok) {
 #pragma unroll
-                    for (int t = 0; t < NBT; ++t)
-                        if (t < p.M) p.Y[(size_t)t * p.ldy + row] = (acc[t] * rs) * __ldg(p.xinv + t);
+                    for (int c = 0; c < CW; ++c)
+                        if (c0 + c < p.M) Y[(size_t)(c0 + c) * p.ldy + row] = (acc[c] * rs) * __ldg(p.xinv + c0 + c);
                 }
             } else {
-                float *mine = p.partial + (size_t)u * NBT * WM + rl;
+                float *__restrict__ mine = p.partial + ((size_t)u * NBT + c0) * WM + rl;
 #pragma unroll
-                for (int t = 0; t < NBT; ++t)
-                    if (t < p.M) mine[(size_t)t * WM] = acc[t];
+                for (int c = 0; c < CW; ++c) mine[(size_t)c * WM] = acc[c];
                 __threadfence();
-                named_bar(1, kNumEpi * 32);
+                named_bar(1, kEpiThreads);
                 if (threadIdx.x == kEpiWarp0 * 32) {
                     const unsigned old = atomicAdd(&p.tickets[tile], 1u);
                     *last_flag = old == (unsigned)(p.parts - 1);
                 }
-                named_bar(1, kNumEpi * 32);
+                named_bar(1, kEpiThreads);
                 if (*last_flag) {
                     __threadfence();
                     if (ok && rowok) {
-                        const float *base = p.partial + (size_t)tile * p.parts * NBT * WM + rl;
-#pragma unroll 4
-                        for (int t = 0; t < NBT; ++t) {
-                            if (t >= p.M) break;
-                            float y = __ldcg(base + (size_t)t * WM);
-                            for (int pp = 1; pp < p.parts; ++pp) y += __ldcg(base + ((size_t)pp * NBT + t) * WM);
-                            p.Y[(size_t)t * p.ldy + row] = (y * rs) * __ldg(p.xinv + t);
+                        // the parts' partial sums in part order; two parts' loads in flight at a time
+                        const float *__restrict__ base = p.partial + ((size_t)tile * p.parts * NBT + c0) * WM + rl;
+                        float y[CW];
+#pragma unroll
+                        for (int c = 0; c < CW; ++c) y[c] = __ldcg(base + (size_t)c * WM);
+                        int pp = 1;
+                        for (; pp + 1 < p.parts; pp += 2) {
+                            float a[CW], b[CW];
+#pragma unroll
+                            for (int c = 0; c < CW; ++c) {
+                                a[c] = __ldcg(base + ((size_t)pp * NBT + c) * WM);
+                                b[c] = __ldcg(base + ((size_t)(pp + 1) * NBT + c) * WM);
+                            }
+#pragma unroll
+                            for (int c = 0; c < CW; ++c) y[c] = (y[c] + a[c]) + b[c];
                         }
+                        if (pp < p.parts) {
+#pragma unroll
+                            for (int c = 0; c < CW; ++c) y[c] += __ldcg(base + ((size_t)pp * NBT + c) * WM);
+                        }
+#pragma unroll
+                        for (int c = 0; c < CW; ++c)
+                            if (c0 + c < p.M) Y[(size_t)(c0 + c) * p.ldy + row] = (y[c] * rs) * __ldg(p.xinv + c0 + c);
                     }
                     if (threadIdx.x == kEpiWarp0 * 32) p.tickets[tile] = 0;  // re-armed for the next launch
                 }
-                named_bar(1, kNumEpi * 32);  // last_flag is reused by the next unit
+                named_bar(1, kEpiThreads);  // last_flag is reused by the next unit
             }
         }
     }
@@ -509,12 +572,14 @@ __global__ void __launch_bounds__(256) split_x_ws_kernel(const float *__restrict
 }
 
 // ------------------------------------------------------------------------------ host side --
-int nbt_for(size_t M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 48 ? 48 : 64; }
+int nbt_for(size_t M) { return M <= 16 ? 16 : M <= 32 ? 32 : 64; }
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// K parts per tile: minimises the stages of the busiest CTA, ceil(units / grid) * ceil(S / parts),
-// with partial sums no larger than `partial_cap` bytes when a tile is split.
+// K parts per tile: minimises the busiest CTA's stages, ceil(units / grid) * ceil(S / parts), plus,
+// for split tiles, the finishing CTA's reduce (its partial-sum reads: about 2 stages' time per
+// pair of parts, more with more token columns), with partial sums no larger than `partial_cap`
+// bytes.
 int choose_parts(size_t N, size_t K, int nbt, int num_sms, size_t partial_cap) {
     const long T = (long)((N + WM - 1) / WM), S = (long)(K / WSK);
     long best_cost = -1;
@@ -523,7 +588,8 @@ int choose_parts(size_t N, size_t K, int nbt, int num_sms, size_t partial_cap) {
         const long units = T * P;
         if (P > 1 && (size_t)units * nbt * WM * 4 > partial_cap) break;
         const long grid = std::min<long>(num_sms, units);
-        const long cost = (units + grid - 1) / grid * ((S + P - 1) / P);
+        const long reduce = P > 1 ? 2 + (2 + nbt / 32) * ((P + 1) / 2) : 0;
+        const long cost = (units + grid - 1) / grid * ((S + P - 1) / P) + reduce;
         if (best_cost < 0 || cost < best_cost) {
             best_cost = cost;
             best = (int)P;
@@ -567,7 +633,7 @@ cudaError_t run_ws(const CUtensorMap &tw, const CUtensorMap &th, const CUtensorM
         return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)WsSmem<NBT>::bytes);
     });
     if (e != cudaSuccess) return e;
-    return launch_kernel(kern, dim3(grid), dim3(kThreads), WsSmem<NBT>::bytes, st, tw, th, tl, p);
+    return launch_kernel(kern, dim3(grid), dim3(WsRoles<NBT>::kThreads), WsSmem<NBT>::bytes, st, tw, th, tl, p);
 }
 
 template <bool INT4, bool GROUPED>
@@ -576,7 +642,6 @@ cudaError_t dispatch_nbt(int nbt, const CUtensorMap &tw, const CUtensorMap &th, 
     switch (nbt) {
     case 16: return run_ws<16, INT4, GROUPED>(tw, th, tl, p, grid, st);
     case 32: return run_ws<32, INT4, GROUPED>(tw, th, tl, p, grid, st);
-    case 48: return run_ws<48, INT4, GROUPED>(tw, th, tl, p, grid, st);
     default: return run_ws<64, INT4, GROUPED>(tw, th, tl, p, grid, st);
     }
 }

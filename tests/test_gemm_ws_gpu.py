@@ -1,4 +1,4 @@
-"""The weight-streaming tensor-core matmul (gemm_ws.cu) that takes decode-shaped batches of 2-64
+"""The weight-streaming tensor-core matmul (gemm_ws.cu) that takes decode-shaped batches of 9-64
 token rows: int4 and int8 weights with a scale per 32 values, int8 with one scale per row.
 Parity as for every matmul (tests/parity.py): against the oracle's restatement of the
 reference's quantized CPU matmul (src/matmul.rs:21-97, :149-173, :297-317) and the float64 sum of
@@ -33,14 +33,14 @@ def inputs(M, K, seed):
 
 
 @pytest.mark.parametrize("qt,N,K,bs,M", [
-    ("int4", 2048, 2048, 32, 2), ("int4", 2048, 2048, 32, 8), ("int4", 2048, 2048, 32, 16),
-    ("int4", 2048, 2048, 32, 33), ("int4", 2048, 2048, 32, 64),       # 16 / 32 / 48 / 64 token columns
-    ("int4", 1024, 2048, 32, 4), ("int4", 6144, 2048, 32, 8), ("int4", 12288, 2048, 32, 64),
-    ("int4", 2048, 6144, 32, 8), ("int4", 2048, 6144, 32, 64),        # down_proj: 48 stages per row
-    ("int4", 1779, 2048, 32, 5),                                      # a partial last tile
-    ("int4", 100, 128, 32, 7),                                        # one stage per row
-    ("int4", 37, 9600, 32, 3),                                        # 75 stages, a lone tile
-    ("int8", 6144, 2048, 32, 8), ("int8", 515, 4096, 32, 3),          # GGUF Q8_0 layout
+    ("int4", 2048, 2048, 32, 9), ("int4", 2048, 2048, 32, 16), ("int4", 2048, 2048, 32, 17),
+    ("int4", 2048, 2048, 32, 33), ("int4", 2048, 2048, 32, 64),       # 16 / 32 / 64 token columns
+    ("int4", 1024, 2048, 32, 12), ("int4", 6144, 2048, 32, 16), ("int4", 12288, 2048, 32, 64),
+    ("int4", 2048, 6144, 32, 10), ("int4", 2048, 6144, 32, 64),       # down_proj: 48 stages per row
+    ("int4", 1779, 2048, 32, 13),                                     # a partial last tile
+    ("int4", 100, 128, 32, 11),                                       # one stage per row
+    ("int4", 37, 9600, 32, 9),                                        # 75 stages, a lone tile
+    ("int8", 6144, 2048, 32, 16), ("int8", 515, 4096, 32, 9),         # GGUF Q8_0 layout
     ("int8", 6144, 2048, 2048, 12), ("int8", 2048, 6144, 6144, 64),   # one scale per row
     ("int8", 4096, 2048, 2048, 40),
 ])
@@ -57,11 +57,11 @@ def test_gemm_ws_matches_oracle(qt, N, K, bs, M):
 
 
 def test_gemm_ws_lm_head_int4_batch():
-    """The config-5 head: int4 group-32 lm_head 151936 x 2048 for 8 and 64 sequences' rows
+    """The config-5 head: int4 group-32 lm_head 151936 x 2048 for 16 and 64 sequences' rows
     (1187 tiles: several tiles per CTA, K not split), with the argmax of every row."""
     N, K = 151936, 2048
     w, od, os_ = make("int4", N, K, 32, seed=0x11EAD)
-    for M in (8, 64):
+    for M in (16, 64):
         X = px.synth_normal_f32(M + 3, M * K, 1.0).reshape(M, K)
         ref = oracle.matmul(X, oracle.INT4, od, os_, 32, N, K).reshape(M, N)
         Y = px.matmul_batch(X, w, N, K)
@@ -73,7 +73,7 @@ def test_gemm_ws_lm_head_int4_batch():
 def test_gemm_ws_nan_stays_in_its_token():
     """A NaN in one token row makes that token's outputs NaN (as the reference's sums do) and
     leaves the other tokens' outputs as they are."""
-    N, K, M = 2048, 2048, 6
+    N, K, M = 2048, 2048, 10
     w, od, os_ = make("int4", N, K, 32, seed=77)
     X = px.synth_normal_f32(9, M * K, 1.0).reshape(M, K)
     Y0 = px.matmul_batch(X, w, N, K)
@@ -128,7 +128,7 @@ def test_reserve_workspace():
     product allocates nothing)."""
     ctx = px.get_cuda(0)
     px._native.check(px._native.lib().pyxis_cuda_reserve_workspace(ctx.handle, 64 << 20))
-    N, K, M = 2048, 2048, 8
+    N, K, M = 2048, 2048, 12
     w, od, os_ = make("int4", N, K, 32, seed=12)
     X = inputs(M, K, seed=13)
     check_matmul(px.matmul_batch(X, w, N, K), oracle.matmul(X, oracle.INT4, od, os_, 32, N, K),
