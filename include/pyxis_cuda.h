@@ -1,8 +1,9 @@
 /*
  * pyxis_cuda.h -- C ABI of the B200 (sm_100a) backend for pyxis's quantized matmul hot path.
  *
- * This is the boundary a `--cuda` backend binds from Rust (cuda_matmul.rs + build.rs, shown in
- * INTEGRATION.md), the way src/metal_matmul.rs binds Metal.  It replaces, one for one:
+ * This is the boundary a `--cuda` backend binds from Rust (a cuda_matmul.rs binding module and a
+ * build.rs that runs the nvcc build), the way src/metal_matmul.rs binds Metal.  It replaces, one
+ * for one:
  *
  *   Weights::quantize_int8 / quantize_int4   src/weights.rs:94-118, :120-151  -> pyxis_cuda_quantize
  *   dequantize_weights (bf16 -> f32 arm)     src/model.rs:535-538             -> src_dtype BF16

@@ -109,11 +109,15 @@ struct WsRoles {
     static constexpr int EW = NBT / CW;
     static constexpr int kEpiWarps = 4 * EW;
     static constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;  // 320, 448 or 704
-    // TMEM accumulators: a group's two K-steps go to two accumulators (KS = 2) when they fit, so a
-    // stage issues 8 independent chains of 2 MMAs (x_hi, x_lo) instead of 4 chains of 4: the MMA
-    // pipe runs in order and a dependent MMA waits for its predecessor's result.  Two stages'
-    // accumulators (sets) are in flight: the MMAs of one while the epilogue reads the other.
-    static constexpr int KS = NBT <= 32 ? 2 : 1;
+    // A tcgen05.mma costs about the same at any N up to 256, so the MMA count per stage sets the
+    // pace.  Up to 32 token columns x_hi and x_lo sit side by side in N (NSTACK): one N = 2 NBT MMA
+    // per K-step of 16 multiplies the codes with both, into columns [0, NBT) and [NBT, 2 NBT) of the
+    // group's accumulator -- 8 MMAs per stage, 4 independent chains of 2.  With 64 token columns
+    // (N would exceed the TMEM budget) x_lo is stacked along K instead: 16 MMAs per stage.  KS = the
+    // NBT-column parts a group's readback adds (hi and lo, or one).  Two stages' accumulators (sets)
+    // are in flight: the MMAs of one while the epilogue reads the other.
+    static constexpr bool NSTACK = NBT <= 32;
+    static constexpr int KS = NSTACK ? 2 : 1;
     static constexpr int kAccPerStage = kGroupsPerStage * KS;
     static constexpr int kSetCols = kAccPerStage * NBT;
     static constexpr uint32_t kTmemCols = 2 * kSetCols <= 128 ? 128 : (2 * kSetCols <= 256 ? 256 : 512);
@@ -126,11 +130,12 @@ struct WsSmem {
     static constexpr int NA = NBT <= 32 ? 3 : 2;  // converted weight tiles
     static constexpr uint32_t kBBlock = NBT * 128;             // one column block of an x tile
     static constexpr uint32_t kRawMax = WM * 128;              // codes of a stage (int8: 16 KB)
-    static constexpr uint32_t kStage = kRawMax + 4 * kBBlock;  // codes, x_hi (2 blocks), x_lo (2 blocks)
+    // codes, then per 64-K column block c: x_hi rows, x_lo rows (one 2 NBT-row operand for NSTACK)
+    static constexpr uint32_t kStage = kRawMax + 4 * kBBlock;
     static constexpr uint32_t a = 0;
     static constexpr uint32_t r = a + NA * kABytes;
     static constexpr uint32_t bar = r + NR * kStage;
-    static constexpr uint32_t num_bars = 2 * NR + 2 * NA + 4 + 1;
+    static constexpr uint32_t num_bars = 3 * NR + 2 * NA + 4 + 1;
     static constexpr uint32_t misc = bar + num_bars * 8;
     static constexpr uint32_t bytes = misc + 64 + 1024;  // + alignment slack
 };
@@ -179,12 +184,13 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
     using R = WsRoles<NBT>;
     constexpr int NR = L::NR, NA = L::NA;
     constexpr uint32_t kRaw = INT4 ? WM * 64 : WM * 128;
-    constexpr uint32_t kStageTx = kRaw + 4 * L::kBBlock;
+    constexpr uint32_t kXTx = 4 * L::kBBlock;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::bar);
-    uint64_t *full = bars, *rawfree = bars + NR;           // code / x stages
-    uint64_t *conv = bars + 2 * NR, *aempty = conv + NA;   // converted weight tiles
+    // code / x stages: fullw (the codes landed), fullx (the x tiles landed), rawfree (both consumed)
+    uint64_t *full = bars, *rawfree = bars + NR, *fullx = bars + 2 * NR;
+    uint64_t *conv = bars + 3 * NR, *aempty = conv + NA;   // converted weight tiles
     uint64_t *accfull = aempty + NA, *accempty = accfull + 2, *drain = accempty + 2;  // per accumulator set
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::misc);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::misc + 4);
@@ -194,6 +200,7 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < NR; ++s) {
             tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&fullx[s], 1);
             tc::mbar_init(&rawfree[s], kNumConv + 1);  // the converters' reads of the codes + the MMAs' reads of x
         }
         for (int a = 0; a < NA; ++a) {
@@ -221,14 +228,17 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
             tc::prefetch_tmap(&tm_w);
             tc::prefetch_tmap(&tm_xhi);
             tc::prefetch_tmap(&tm_xlo);
-            // the codes do not depend on the previous kernel: the first NR stages' codes go out
-            // before griddepcontrol.wait, their x tiles after it
+            // the codes do not depend on the previous kernel: the first NR stages' codes go out (and
+            // are converted) before griddepcontrol.wait, their x tiles after it
+            int xg = 0;  // stages whose x tiles are issued
             auto issue_x = [&](int slot, int k) {
-                uint8_t *bhi = smem + L::r + slot * L::kStage + L::kRawMax, *blo = bhi + 2 * L::kBBlock;
-                tc::tma_load_2d(bhi, &tm_xhi, k, 0, &full[slot]);
-                tc::tma_load_2d(bhi + L::kBBlock, &tm_xhi, k + 64, 0, &full[slot]);
-                tc::tma_load_2d(blo, &tm_xlo, k, 0, &full[slot]);
-                tc::tma_load_2d(blo + L::kBBlock, &tm_xlo, k + 64, 0, &full[slot]);
+                uint8_t *b0 = smem + L::r + slot * L::kStage + L::kRawMax;  // [hi 0 | lo 0 | hi 1 | lo 1]
+                tc::mbar_arrive_expect_tx(&fullx[slot], kXTx);
+                tc::tma_load_2d(b0, &tm_xhi, k, 0, &fullx[slot]);
+                tc::tma_load_2d(b0 + L::kBBlock, &tm_xlo, k, 0, &fullx[slot]);
+                tc::tma_load_2d(b0 + 2 * L::kBBlock, &tm_xhi, k + 64, 0, &fullx[slot]);
+                tc::tma_load_2d(b0 + 3 * L::kBBlock, &tm_xlo, k + 64, 0, &fullx[slot]);
+                ++xg;
             };
             int g = 0, s = 0, ph = 0, pend_n = 0;
             int pend_k[NR];
@@ -242,7 +252,7 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
                         ok = false;
                         break;
                     }
-                    tc::mbar_arrive_expect_tx(&full[s], kStageTx);
+                    tc::mbar_arrive_expect_tx(&full[s], kRaw);
                     tc::tma_load_2d(smem + L::r + s * L::kStage, &tm_w, sk * (INT4 ? 64 : 128), tile * WM, &full[s]);
                     if (!waited) {
                         pend_k[pend_n++] = sk * WSK;  // stage g == slot g here (g < NR)
@@ -270,12 +280,14 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
                 volatile int no_abort = 0;
                 for (int j = g > NR ? g - NR : 0; j < g; ++j)
                     tc::mbar_wait_bounded(&full[j % NR], (j / NR) & 1, &no_abort, p.err, kErrDrain, 100000000ull);
+                for (int j = xg > NR ? xg - NR : 0; j < xg; ++j)
+                    tc::mbar_wait_bounded(&fullx[j % NR], (j / NR) & 1, &no_abort, p.err, kErrDrain, 100000000ull);
             }
         }
     } else if (warp == kMmaWarp) {
         // ------------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = tc::idesc_f16_f32(WM, NBT);
+            constexpr uint32_t idesc = tc::idesc_f16_f32(WM, R::NSTACK ? 2 * NBT : NBT);
             const uint64_t a_d = tc::desc_sw128(tc::smem_u32(smem + L::a));
             const uint64_t b_d = tc::desc_sw128(tc::smem_u32(smem + L::r + L::kRawMax));
             int s = 0, sph = 0, a = 0, aph = 0, st = 0;
@@ -286,31 +298,30 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
                 for (int sk = s0; sk < s1; ++sk, ++st) {
                     const int set = st & 1, use = st >> 1;
                     ok = tc::mbar_wait_bounded(&conv[a], (uint32_t)(aph & 1), abort_flag, p.err, kErrMma, kTimeoutNs) &&
-                         tc::mbar_wait_bounded(&full[s], (uint32_t)(sph & 1), abort_flag, p.err, kErrMma, kTimeoutNs) &&
+                         tc::mbar_wait_bounded(&fullx[s], (uint32_t)(sph & 1), abort_flag, p.err, kErrMma, kTimeoutNs) &&
                          (use == 0 || tc::mbar_wait_bounded(&accempty[set], (uint32_t)((use - 1) & 1), abort_flag,
                                                             p.err, kErrMma, kTimeoutNs));
                     if (!ok) break;
                     tc::tc_fence_after();
                     const uint64_t abase = a_d + (uint64_t)(a * (kABytes >> 4));
-                    const uint64_t hbase = b_d + (uint64_t)(s * (L::kStage >> 4));
-                    const uint64_t lbase = hbase + (uint64_t)((2 * L::kBBlock) >> 4);
+                    const uint64_t bbase = b_d + (uint64_t)(s * (L::kStage >> 4));
                     const uint32_t dset = tmem_base + (uint32_t)(set * R::kSetCols);
                     // K-step ks of group gi covers K [32 gi + 16 ks, +16) of the stage; the issue order
                     // runs over the groups innermost, so consecutive MMAs use different accumulators
 #pragma unroll
                     for (int ks = 0; ks < 2; ++ks)
 #pragma unroll
-                        for (int hl = 0; hl < 2; ++hl)
+                        for (int hl = 0; hl < (R::NSTACK ? 1 : 2); ++hl)
 #pragma unroll
                             for (int gi = 0; gi < kGroupsPerStage; ++gi) {
                                 const int k = gi * 32 + ks * 16;
-                                const uint64_t off = (uint64_t)((k >> 6) * (kABlock >> 4)) + (uint64_t)((k & 63) >> 3);
-                                const uint64_t boff = (uint64_t)((k >> 6) * (L::kBBlock >> 4)) + (uint64_t)((k & 63) >> 3);
-                                const int acc_i = gi * R::KS + (R::KS == 2 ? ks : 0);
-                                // an accumulator's first MMA starts it: (ks 0, x_hi), or with KS = 2 its x_hi
-                                const uint32_t accum = R::KS == 2 ? (uint32_t)hl : (uint32_t)(ks | hl);
-                                tc::mma_f16(dset + (uint32_t)(acc_i * NBT), abase + off, (hl ? lbase : hbase) + boff,
-                                            idesc, accum);
+                                const uint64_t koff = (uint64_t)((k & 63) >> 3);  // 16-byte units in the row
+                                const uint64_t ad = abase + (uint64_t)((k >> 6) * (kABlock >> 4)) + koff;
+                                // block c = k / 64 of x: hi rows at 2c blocks, lo rows right after them
+                                const uint64_t bd = bbase + (uint64_t)((2 * (k >> 6) + hl) * (L::kBBlock >> 4)) + koff;
+                                const uint32_t d = dset + (uint32_t)(gi * R::KS * NBT);
+                                // a group's first K-step (x_hi) starts its accumulator
+                                tc::mma_f16(d, ad, bd, idesc, (uint32_t)(ks | hl));
                             }
                     tc::mma_commit(&accfull[set]);
                     tc::mma_commit(&rawfree[s]);
@@ -536,8 +547,10 @@ __global__ void __launch_bounds__(256) split_x_ws_kernel(const float *__restrict
                                                          __half *__restrict__ hi, __half *__restrict__ lo,
                                                          float *__restrict__ inv) {
     __shared__ float red[8];
-    pdl_wait();
+    // the matmul that reads this kernel's output may launch at once: it streams and converts its
+    // weights before its own griddepcontrol.wait, which still waits for this kernel to finish
     pdl_trigger();
+    pdl_wait();
     const int m = blockIdx.x;
     const float *x = X + (size_t)m * ldx;
     float mx = 0.f;

@@ -2,9 +2,8 @@
 suite for the quantized-matmul path, transcribed from its Rust sources.
 
 Each entry records its source (file:line in the reference) and a `literal` that must appear on
-that line.  Run with the reference tree available (REFERENCE_ROOT, default ../reference next to
-the repository root's parent) and the script verifies every citation against the source before
-writing; without it the script refuses.  The GPU box never needs the reference: the JSON is the
+that line.  Run it with the reference tree's path (first argument, or REFERENCE_ROOT) and it
+verifies every citation against the source before writing; without one it refuses.  The GPU box never needs the reference: the JSON is the
 committed fixture.
 """
 from __future__ import annotations
@@ -220,7 +219,12 @@ KATS = [
 
 
 def reference_root() -> str:
-    return os.environ.get("REFERENCE_ROOT", "/root/reference")
+    """The reference source tree whose lines the citations are checked against: the first
+    command-line argument, else the REFERENCE_ROOT environment variable."""
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("REFERENCE_ROOT", "")
+    if not root:
+        raise SystemExit("usage: make_kats.py <reference source tree> (or set REFERENCE_ROOT)")
+    return root
 
 
 def verify(root: str) -> None:
