@@ -45,7 +45,10 @@ constexpr int WM = 128;       // weight rows per tile: MMA M, TMEM lanes
 constexpr int WSK = 128;      // K per stage
 constexpr int WG = 32;        // K per scale group (group-scale mode)
 constexpr int kGroupsPerStage = WSK / WG;
-constexpr int kProdWarp = 0, kMmaWarp = 1, kConvWarp0 = 2, kNumConv = 4, kEpiWarp0 = 6;
+// Warp roles: 0 TMA producer; 1 and 2 MMA issuers (even and odd stages: a tcgen05.mma costs its
+// issuing thread about 70 cycles at any N <= 128, and two issuers overlap that, measured 39-48
+// cycles per MMA); 3-6 converters; then the epilogue warps.  Warp 1 also owns TMEM.
+constexpr int kProdWarp = 0, kMmaWarp = 1, kNumIssuers = 2, kConvWarp0 = 3, kNumConv = 4, kEpiWarp0 = 7;
 constexpr int kMaxTokens = 64;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 constexpr uint32_t kABlock = WM * 128;      // one column block (64 of K) of the fp16 weight tile
@@ -108,7 +111,7 @@ struct WsRoles {
     static constexpr int CW = 16;
     static constexpr int EW = NBT / CW;
     static constexpr int kEpiWarps = 4 * EW;
-    static constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;  // 320, 448 or 704
+    static constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;  // 352, 480 or 736
     // A tcgen05.mma costs about the same at any N up to 256, so the MMA count per stage sets the
     // pace.  Up to 32 token columns x_hi and x_lo sit side by side in N (NSTACK): one N = 2 NBT MMA
     // per K-step of 16 multiplies the codes with both, into columns [0, NBT) and [NBT, 2 NBT) of the
@@ -135,7 +138,7 @@ struct WsSmem {
     static constexpr uint32_t a = 0;
     static constexpr uint32_t r = a + NA * kABytes;
     static constexpr uint32_t bar = r + NR * kStage;
-    static constexpr uint32_t num_bars = 3 * NR + 2 * NA + 4 + 1;
+    static constexpr uint32_t num_bars = 3 * NR + 2 * NA + 4 + 2;
     static constexpr uint32_t misc = bar + num_bars * 8;
     static constexpr uint32_t bytes = misc + 64 + 1024;  // + alignment slack
 };
@@ -211,7 +214,8 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
             tc::mbar_init(&accfull[k], 1);
             tc::mbar_init(&accempty[k], R::kEpiWarps);
         }
-        tc::mbar_init(drain, 1);
+        tc::mbar_init(&drain[0], 1);
+        tc::mbar_init(&drain[1], 1);
         *abort_flag = 0;
         tc::fence_mbar_init();
     }
@@ -284,19 +288,24 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
                     tc::mbar_wait_bounded(&fullx[j % NR], (j / NR) & 1, &no_abort, p.err, kErrDrain, 100000000ull);
             }
         }
-    } else if (warp == kMmaWarp) {
-        // ------------------------------------------------------------------ MMA issuer
+    } else if (warp < kMmaWarp + kNumIssuers) {
+        // ------------------------------------------------------------------ MMA issuers
+        // Issuer i takes the stages st with st % 2 == i, into accumulator set i: the two sets, and
+        // the ring slots of consecutive stages, never meet.
+        const int issuer = warp - kMmaWarp;
         if (lane == 0) {
             constexpr uint32_t idesc = tc::idesc_f16_f32(WM, R::NSTACK ? 2 * NBT : NBT);
             const uint64_t a_d = tc::desc_sw128(tc::smem_u32(smem + L::a));
             const uint64_t b_d = tc::desc_sw128(tc::smem_u32(smem + L::r + L::kRawMax));
-            int s = 0, sph = 0, a = 0, aph = 0, st = 0;
+            int st = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
                 int tile, part, s0, s1;
                 unit_range(p, u, tile, part, s0, s1);
                 for (int sk = s0; sk < s1; ++sk, ++st) {
-                    const int set = st & 1, use = st >> 1;
+                    if ((st & 1) != issuer) continue;
+                    const int set = issuer, use = st >> 1;
+                    const int s = st % NR, sph = st / NR, a = st % NA, aph = st / NA;
                     ok = tc::mbar_wait_bounded(&conv[a], (uint32_t)(aph & 1), abort_flag, p.err, kErrMma, kTimeoutNs) &&
                          tc::mbar_wait_bounded(&fullx[s], (uint32_t)(sph & 1), abort_flag, p.err, kErrMma, kTimeoutNs) &&
                          (use == 0 || tc::mbar_wait_bounded(&accempty[set], (uint32_t)((use - 1) & 1), abort_flag,
@@ -326,20 +335,12 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
                     tc::mma_commit(&accfull[set]);
                     tc::mma_commit(&rawfree[s]);
                     tc::mma_commit(&aempty[a]);
-                    if (++s == NR) {
-                        s = 0;
-                        ++sph;
-                    }
-                    if (++a == NA) {
-                        a = 0;
-                        ++aph;
-                    }
                 }
             }
             // every MMA this thread issued must complete before TMEM is released
-            tc::mma_commit(drain);
+            tc::mma_commit(&drain[issuer]);
             volatile int no_abort = 0;
-            tc::mbar_wait_bounded(drain, 0, &no_abort, p.err, kErrDrain, kTimeoutNs);
+            tc::mbar_wait_bounded(&drain[issuer], 0, &no_abort, p.err, kErrDrain, kTimeoutNs);
         }
     } else if (warp < kEpiWarp0) {
         // ------------------------------------------------------------------ converters
