@@ -154,8 +154,8 @@ def dist_setup():
 
         # NCCL's communicator set-up lines (rank counts) go to stdout before the JSON line,
         # which is printed last, after the communicators are destroyed
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        os.environ["NCCL_DEBUG"] = "INFO"
+        os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
@@ -807,10 +807,14 @@ def pyxis_arm(args, ws, rank, local):
 
     config1 = run_config1(local, capture, replay_ms, rank == 0 and ws == 1 and not args.no_cpu_baseline)
 
-    lm_vp = row_split = comm = None
+    lm_vp = row_split = comm = comm_info = None
     if ws > 1:
         from pyxis_b200.dist import Comm
         comm = Comm(rank, ws, local)
+        nr, rk = C.c_int(), C.c_int()
+        _native.check(_native.lib().pyxis_cuda_comm_info(comm.handle, C.byref(nr), C.byref(rk)))
+        comm_info = {"nranks": nr.value, "ranks_agree": max_over_ranks(0.0 if nr.value == ws else 1.0, ws) == 0.0,
+                     "nccl_debug": os.environ.get("NCCL_DEBUG")}
         full = {name: w for (name, qt, N, K, bs, w) in weights}
         row_split = run_row_split(ws, rank, local, args.steps, capture, replay_ms, full)
         lm_vp = run_vocab_parallel_head(comm, ws, rank, local, args.steps, full["lm_head"])
@@ -885,6 +889,7 @@ def pyxis_arm(args, ws, rank, local):
                 "batch_decode": batch,
                 "lm_head_vocab_parallel": lm_vp,
                 "row_split": row_split,
+                "comm": comm_info,
                 "parity": None if ws == 1 else {
                     "row_split": row_split["parity"], "vocab_parallel": lm_vp["parity"],
                     "batch_decode_vocab_parallel": None if batch is None else batch.get("vocab_parallel_parity")},

@@ -213,11 +213,12 @@ class OModel(C.Structure):
                 ("final_norm", _vp), ("lm_head", OWeights)]
 
 
-def _model(cfg, bf16, qtype: str):
+def _model(cfg, bf16, qtype: str, head_norm=None):
     """The oracle_model of a config whose tensors ``bf16(name)`` returns (np.uint16 bits; names
     ``layers.{l}.{q,k,v,o,gate,up,down}`` and ``embed``), quantised by the reference's policy
     (src/model.rs:520-530: int8 one scale per row, int4 one per 32), tied lm_head, RMSNorm
-    weights 1, QK-norm when cfg.qk_norm.  Returns (model, arrays to keep alive)."""
+    weights 1, QK-norm when cfg.qk_norm with weights ``head_norm`` (default 1).  Returns (model,
+    arrays to keep alive)."""
     keep = []
 
     def q(bits, in_features):
@@ -239,7 +240,8 @@ def _model(cfg, bf16, qtype: str):
         for k in ws:
             ws[k][l] = q(bf16(f"layers.{l}.{k}"), ins[k])
     ones = np.ones(cfg.hidden, np.float32)
-    hones = np.ones(cfg.head_dim, np.float32)
+    hones = (np.ones(cfg.head_dim, np.float32) if head_norm is None
+             else np.ascontiguousarray(np.asarray(head_norm, np.float32).reshape(cfg.head_dim)))
     norm_arr = (_vp * nl)(*([ones.ctypes.data] * nl))
     hn_arr = (_vp * nl)(*([hones.ctypes.data if cfg.qk_norm else None] * nl))
     emb_bits = bf16("embed")
@@ -254,11 +256,11 @@ def _model(cfg, bf16, qtype: str):
     return m, keep
 
 
-def greedy_decode(cfg, bf16, qtype: str, prompt, n_new: int, nthreads: int = 0, timing=None):
+def greedy_decode(cfg, bf16, qtype: str, prompt, n_new: int, nthreads: int = 0, timing=None, head_norm=None):
     """Greedy tokens (Model::generate with argmax sampling, src/model.rs:245-285) of the model
     ``_model`` builds.  A list passed as ``timing`` receives the seconds of the generation alone
     (the len(prompt) + n_new - 1 forward passes, without the packing)."""
-    m, keep = _model(cfg, bf16, qtype)
+    m, keep = _model(cfg, bf16, qtype, head_norm)
     pr = np.ascontiguousarray(np.asarray(prompt, np.int32))
     out = np.empty(n_new, np.int32)
     t0 = time.perf_counter()
@@ -270,10 +272,10 @@ def greedy_decode(cfg, bf16, qtype: str, prompt, n_new: int, nthreads: int = 0, 
     return out
 
 
-def prefill_hidden(cfg, bf16, qtype: str, prompt, nthreads: int = 0) -> np.ndarray:
+def prefill_hidden(cfg, bf16, qtype: str, prompt, nthreads: int = 0, head_norm=None) -> np.ndarray:
     """The final-norm hidden state [hidden] of the prompt's last position: what the first greedy
     token's lm_head product reads."""
-    m, keep = _model(cfg, bf16, qtype)
+    m, keep = _model(cfg, bf16, qtype, head_norm)
     pr = np.ascontiguousarray(np.asarray(prompt, np.int32))
     out = np.empty(cfg.hidden, np.float32)
     if lib().oracle_prefill_hidden(C.addressof(m), pr.ctypes.data, pr.size, out.ctypes.data, nthreads):

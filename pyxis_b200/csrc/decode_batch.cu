@@ -4,7 +4,8 @@
 // Model::generate (src/model.rs:245-285) with temperature 0, run for n_seq prompts of the same
 // length side by side.  Prefill processes whole prompts: the projections of all their positions
 // are tensor-core GEMMs (pyxis_cuda_matmul_dev's M >= 16 path), attention is the causal
-// prefill kernel below, and the K/V rows go straight into each sequence's cache.  Every
+// tensor-core prefill attention of attn_tc.cu, and the K/V rows go straight into each sequence's
+// cache.  Every
 // generated token is then one batched step -- the projections are GEMMs over the n_seq rows,
 // attention is the fused decode kernel of decode.cu over a (split, kv head, sequence) grid --
 // captured once into a CUDA graph and replayed.  The arithmetic between the projections is the
@@ -19,6 +20,7 @@
 
 #include "../../include/pyxis_decode.h"
 #include "argmax.h"
+#include "attn_tc.h"
 #include "comm.h"
 #include "common.cuh"
 #include "ctx.h"
@@ -103,15 +105,17 @@ __global__ void __launch_bounds__(kRowThreads)
 }
 
 // Prefill row r = (sequence r / P, position pos0 + r % P): per-head QK RMSNorm and RoPE
-// (src/attention.rs:81-93), q to qout[r], k and v to the sequence's cache row (:100).
+// (src/attention.rs:81-93), k and v to the sequence's cache row (:100), q as the prefill
+// attention's operand: each q head row scaled by its power of two and split into fp16 hi/lo, with
+// 2^-e (attn_tc.h).  The largest |k| and |v| of every kv head are folded into tc.kvmax.
 // One CTA per row, one warp per head: warps [0, n_q) the q heads, [n_q, n_q + n_kv) the k heads,
 // warp n_q + n_kv copies v.
 template <int EPL>
 __global__ void qk_rope_rows_kernel(const float *__restrict__ qkv, const float *__restrict__ q_norm,
                                     const float *__restrict__ k_norm, const float *__restrict__ rcos,
                                     const float *__restrict__ rsin, int n_q, int n_kv, float eps, int P, int pos0,
-                                    float *__restrict__ qout, float *__restrict__ kcache, float *__restrict__ vcache,
-                                    long long cache_stride) {
+                                    float *__restrict__ kcache, float *__restrict__ vcache, long long cache_stride,
+                                    AttnTcBuffers tc, int cs) {
     constexpr int HD = 32 * EPL;
     pdl_wait();
     pdl_trigger();
@@ -127,11 +131,47 @@ __global__ void qk_rope_rows_kernel(const float *__restrict__ qkv, const float *
         float v[EPL];
         load_head<EPL>(row + (is_q ? 0 : q_dim) + (size_t)hh * HD + lane * EPL, v);
         norm_rope<EPL>(v, is_q ? q_norm : k_norm, rcos, rsin, pos, eps, lane);
-        float *dst = is_q ? qout + (size_t)r * q_dim + (size_t)hh * HD : kc + (size_t)hh * HD;
+        float m = 0.f;
 #pragma unroll
-        for (int t = 0; t < EPL; ++t) dst[lane * EPL + t] = v[t];
+        for (int t = 0; t < EPL; ++t) m = fmaxf(m, fabsf(v[t]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (is_q) {
+            const int Pp = attn_tc_padded(P);
+            const int e = attn_scale_exp(m);
+            const float sc = attn_pow2(e);
+            const size_t qrow = ((size_t)seq * n_q + hh) * Pp + pos;
+            __half *hi = tc.q + qrow * HD + lane * EPL;
+            __half *lo = hi + (size_t)cs * n_q * Pp * HD;
+#pragma unroll
+            for (int t = 0; t < EPL; t += 2) {
+                const float x0 = v[t] * sc, x1 = v[t + 1] * sc;
+                const __half2 h = __floats2half2_rn(x0, x1);
+                const float2 f = __half22float2(h);
+                *reinterpret_cast<__half2 *>(hi + t) = h;
+                *reinterpret_cast<__half2 *>(lo + t) = __floats2half2_rn(x0 - f.x, x1 - f.y);
+            }
+            if (lane == 0) tc.qinv[qrow] = attn_pow2(-e);
+        } else {
+            float *dst = kc + (size_t)hh * HD;
+#pragma unroll
+            for (int t = 0; t < EPL; ++t) dst[lane * EPL + t] = v[t];
+            if (lane == 0) atomicMax(&tc.kvmax[((size_t)seq * n_kv + hh) * 2], __float_as_uint(m));
+        }
     } else if (warp == n_q + n_kv) {
-        for (int i = lane; i < kv_dim; i += 32) vc[i] = row[q_dim + kv_dim + i];
+        for (int h = 0; h < n_kv; ++h) {
+            float m = 0.f;
+#pragma unroll
+            for (int t = 0; t < EPL; ++t) {
+                const int i = h * HD + t * 32 + lane;
+                const float x = row[q_dim + kv_dim + i];
+                vc[i] = x;
+                m = fmaxf(m, fabsf(x));
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            if (lane == 0) atomicMax(&tc.kvmax[((size_t)seq * n_kv + h) * 2 + 1], __float_as_uint(m));
+        }
     }
 }
 
@@ -160,151 +200,6 @@ __global__ void advance_rows_kernel(const int *__restrict__ tokens, int n_seq, i
     }
 }
 
-// ---------------------------------------------------------------- causal prefill attention --
-// src/attention.rs:107-135 for every position of a prompt at once: query position i of head qh
-// attends the keys 0..i of kv head qh / G, scores (q . k) / sqrt(hd), softmax, sum of p v.
-// CTA = 64 queries x one head x one sequence, 256 threads as 16 x 16: thread (ty, tx) scores
-// queries ty*4..ty*4+3 against keys tx*2, tx*2+1 of each 32-key tile and accumulates output
-// dims tx*DPT.. of the same queries.  Q and K tiles sit transposed in shared memory ([d][query],
-// [d][key]), so each step over d reads one float4 of queries (shared by the 16 tx threads) and
-// one float2 of keys; softmax is online per query row (max and sum over the row's 16 threads by
-// shuffles).  fp32 throughout; the query tiles with the most keys start first.
-constexpr int kPfThreads = 256, kPfBQ = 64, kPfBK = 32;
-
-template <int HD>
-constexpr size_t prefill_smem_floats() {
-    return (size_t)HD * (kPfBQ + 4) + (size_t)HD * (kPfBK + 4) + (size_t)kPfBK * HD + (size_t)kPfBK * (kPfBQ + 4);
-}
-
-template <int HD>
-__global__ void __launch_bounds__(kPfThreads, 2)
-    attention_prefill_kernel(const float *__restrict__ q, int n_q, int n_kv, int P, const float *__restrict__ kcache,
-                             const float *__restrict__ vcache, long long cache_stride, float *__restrict__ out) {
-    constexpr int BQ = kPfBQ, BK = kPfBK, LDQ = BQ + 4, LDK = BK + 4, DPT = HD / 16, D4 = HD / 4;
-    extern __shared__ float4 pf_smem[];
-    float *Qt = reinterpret_cast<float *>(pf_smem);  // [HD][LDQ]
-    float *Kt = Qt + HD * LDQ;                        // [HD][LDK]
-    float *Vs = Kt + HD * LDK;                        // [BK][HD]
-    float *Pt = Vs + BK * HD;                         // [BK][LDQ]: p of (key, query)
-    const int qt = gridDim.x - 1 - blockIdx.x;
-    const int qh = blockIdx.y, seq = blockIdx.z;
-    const int kvh = qh / (n_q / n_kv);
-    const int q_dim = n_q * HD, kv_dim = n_kv * HD;
-    const int q0 = qt * BQ;
-    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-    pdl_wait();
-    pdl_trigger();
-    const float *qb = q + (size_t)seq * P * q_dim + (size_t)qh * HD;
-    const float *kb = kcache + seq * cache_stride + (size_t)kvh * HD;
-    const float *vb = vcache + seq * cache_stride + (size_t)kvh * HD;
-    for (int idx = tid; idx < BQ * D4; idx += kPfThreads) {  // consecutive threads: consecutive queries
-        const int qi = idx % BQ, d4 = idx / BQ;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (q0 + qi < P) v = *reinterpret_cast<const float4 *>(qb + (size_t)(q0 + qi) * q_dim + d4 * 4);
-        Qt[(d4 * 4 + 0) * LDQ + qi] = v.x;
-        Qt[(d4 * 4 + 1) * LDQ + qi] = v.y;
-        Qt[(d4 * 4 + 2) * LDQ + qi] = v.z;
-        Qt[(d4 * 4 + 3) * LDQ + qi] = v.w;
-    }
-    float m[4], l[4], acc[4][DPT];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        m[i] = -INFINITY;
-        l[i] = 0.f;
-#pragma unroll
-        for (int c = 0; c < DPT; ++c) acc[i][c] = 0.f;
-    }
-    const float scale = sqrtf((float)HD);
-    const int kend = min(P, q0 + BQ);  // keys [0, kend) reach some query of the tile
-    for (int k0 = 0; k0 < kend; k0 += BK) {
-        __syncthreads();  // the previous tile's reads are done
-        for (int idx = tid; idx < BK * D4; idx += kPfThreads) {  // K transposed: consecutive keys
-            const int kj = idx % BK, d4 = idx / BK;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (k0 + kj < P) v = *reinterpret_cast<const float4 *>(kb + (size_t)(k0 + kj) * kv_dim + d4 * 4);
-            Kt[(d4 * 4 + 0) * LDK + kj] = v.x;
-            Kt[(d4 * 4 + 1) * LDK + kj] = v.y;
-            Kt[(d4 * 4 + 2) * LDK + kj] = v.z;
-            Kt[(d4 * 4 + 3) * LDK + kj] = v.w;
-        }
-        for (int idx = tid; idx < BK * D4; idx += kPfThreads) {  // V row-major: consecutive dims
-            const int kj = idx / D4, d4 = idx % D4;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (k0 + kj < P) v = *reinterpret_cast<const float4 *>(vb + (size_t)(k0 + kj) * kv_dim + d4 * 4);
-            *reinterpret_cast<float4 *>(Vs + kj * HD + d4 * 4) = v;
-        }
-        __syncthreads();
-        float s[4][2];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) s[i][0] = s[i][1] = 0.f;
-#pragma unroll 8
-        for (int d = 0; d < HD; ++d) {
-            const float4 qv = *reinterpret_cast<const float4 *>(Qt + d * LDQ + ty * 4);
-            const float2 kv = *reinterpret_cast<const float2 *>(Kt + d * LDK + tx * 2);
-            const float qa[4] = {qv.x, qv.y, qv.z, qv.w};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                s[i][0] = __fmaf_rn(qa[i], kv.x, s[i][0]);
-                s[i][1] = __fmaf_rn(qa[i], kv.y, s[i][1]);
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int qi = q0 + ty * 4 + i;
-            float p[2];
-            float mt = -INFINITY;
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const int kj = k0 + tx * 2 + j;
-                s[i][j] = (kj <= qi && kj < P) ? __fdiv_rn(s[i][j], scale) : -INFINITY;
-                mt = fmaxf(mt, s[i][j]);
-            }
-#pragma unroll
-            for (int o = 8; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
-            const float mn = fmaxf(m[i], mt);  // finite: key 0 is in the first tile of every row
-            const float c = expf(__fsub_rn(m[i], mn));
-            p[0] = expf(__fsub_rn(s[i][0], mn));
-            p[1] = expf(__fsub_rn(s[i][1], mn));
-            float rs = __fadd_rn(p[0], p[1]);
-#pragma unroll
-            for (int o = 8; o > 0; o >>= 1) rs = __fadd_rn(rs, __shfl_xor_sync(0xffffffffu, rs, o));
-            l[i] = __fadd_rn(__fmul_rn(l[i], c), rs);
-#pragma unroll
-            for (int cc = 0; cc < DPT; ++cc) acc[i][cc] = __fmul_rn(acc[i][cc], c);
-            m[i] = mn;
-            Pt[(tx * 2 + 0) * LDQ + ty * 4 + i] = p[0];
-            Pt[(tx * 2 + 1) * LDQ + ty * 4 + i] = p[1];
-        }
-        __syncthreads();
-#pragma unroll 4
-        for (int k = 0; k < BK; ++k) {
-            const float4 pv = *reinterpret_cast<const float4 *>(Pt + k * LDQ + ty * 4);
-            const float pa[4] = {pv.x, pv.y, pv.z, pv.w};
-            float vv[DPT];
-#pragma unroll
-            for (int c4 = 0; c4 < DPT / 4; ++c4) {
-                const float4 t = *reinterpret_cast<const float4 *>(Vs + k * HD + tx * DPT + c4 * 4);
-                vv[c4 * 4 + 0] = t.x, vv[c4 * 4 + 1] = t.y, vv[c4 * 4 + 2] = t.z, vv[c4 * 4 + 3] = t.w;
-            }
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int cc = 0; cc < DPT; ++cc) acc[i][cc] = __fmaf_rn(pa[i], vv[cc], acc[i][cc]);
-        }
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int qi = q0 + ty * 4 + i;
-        if (qi >= P) continue;
-        float *o = out + ((size_t)seq * P + qi) * q_dim + (size_t)qh * HD + tx * DPT;
-#pragma unroll
-        for (int c4 = 0; c4 < DPT / 4; ++c4)
-            *reinterpret_cast<float4 *>(o + c4 * 4) =
-                make_float4(__fdiv_rn(acc[i][c4 * 4 + 0], l[i]), __fdiv_rn(acc[i][c4 * 4 + 1], l[i]),
-                            __fdiv_rn(acc[i][c4 * 4 + 2], l[i]), __fdiv_rn(acc[i][c4 * 4 + 3], l[i]));
-    }
-}
-
 }  // namespace
 
 // ------------------------------------------------------------------------------ host side --
@@ -315,7 +210,7 @@ struct BatchState {
     int splits = 1;                          // decode attention key splits
     float *kc = nullptr, *vc = nullptr;      // [n_seq][n_layers][max_seq][kv_dim]
     // prefill rows (chunk * n_prompt)
-    float *px = nullptr, *ph = nullptr, *pqkv = nullptr, *pq = nullptr, *pattn = nullptr, *ptmp = nullptr,
+    float *px = nullptr, *ph = nullptr, *pqkv = nullptr, *pattn = nullptr, *ptmp = nullptr,
           *pgu = nullptr, *pact = nullptr;
     // decode rows (n_seq)
     float *dx = nullptr, *dh = nullptr, *dqkv = nullptr, *dattn = nullptr, *dtmp = nullptr, *dgu = nullptr,
@@ -325,6 +220,8 @@ struct BatchState {
     int vp_ranks = 0;
     float *part = nullptr;
     unsigned *tickets = nullptr;
+    // tensor-core prefill attention operands of one chunk (attn_tc.h); kvmax per layer
+    AttnTcBuffers tc{};
     int *d_prompt = nullptr, *d_tokens = nullptr, *d_out = nullptr, *d_pos = nullptr, *d_step = nullptr;
     void *ws = nullptr;
     size_t ws_bytes = 0;
@@ -413,7 +310,6 @@ int ensure_state(pyxis_cuda_model *m, int n_seq, int n_prompt, int n_new) {
     A(&b->px, rows * H);
     A(&b->ph, rows * H);
     A(&b->pqkv, rows * qkv_rows);
-    A(&b->pq, rows * qd);
     A(&b->pattn, rows * qd);
     A(&b->ptmp, rows * H);
     A(&b->pgu, rows * 2 * ffn);
@@ -430,6 +326,16 @@ int ensure_state(pyxis_cuda_model *m, int n_seq, int n_prompt, int n_new) {
         b->vp_ranks = vp->nranks;
     } else {
         A(&b->dlogits, (size_t)n_seq * c.vocab);
+    }
+    {
+        const size_t Pp = attn_tc_padded(n_prompt), hd = c.head_dim, cs = b->chunk;
+        A(&b->tc.q, 2 * cs * c.n_q_heads * Pp * hd);
+        A(&b->tc.qinv, cs * c.n_q_heads * Pp);
+        A(&b->tc.k, 2 * cs * c.n_kv_heads * Pp * hd);
+        A(&b->tc.vt, 2 * cs * c.n_kv_heads * hd * Pp);
+        A(&b->tc.kvmax, (size_t)c.n_layers * cs * c.n_kv_heads * 2);
+        if (e == cudaSuccess) e = cudaMemset(b->tc.q, 0, 2 * cs * c.n_q_heads * Pp * hd * sizeof(__half));
+        if (e == cudaSuccess) e = cudaMemset(b->tc.qinv, 0, cs * c.n_q_heads * Pp * sizeof(float));
     }
     A(&b->part, (size_t)n_seq * c.n_kv_heads * b->splits * G * (c.head_dim + 2));
     A(&b->tickets, (size_t)n_seq * c.n_kv_heads);
@@ -503,6 +409,8 @@ int enqueue_prefill(pyxis_cuda_model *m, int n_seq, int P, cudaStream_t st) {
     for (int s0 = 0; s0 < n_seq; s0 += b->chunk) {
         const int cs = std::min(b->chunk, n_seq - s0);
         const int M = cs * P;
+        PX_TRY(cudaMemsetAsync(b->tc.kvmax, 0, (size_t)c.n_layers * b->chunk * c.n_kv_heads * 2 * sizeof(unsigned),
+                                   st));
         PX_TRY(launch_kernel(embed_rows_kernel, dim3((H + 255) / 256, M), dim3(256), 0, st, (const uint16_t *)m->emb,
                              (const int *)(b->d_prompt + (size_t)s0 * P), c.vocab, H, b->px));
         for (int l = 0; l < c.n_layers; ++l) {
@@ -514,22 +422,16 @@ int enqueue_prefill(pyxis_cuda_model *m, int n_seq, int P, cudaStream_t st) {
                                  1, 0));
             int rc = run_matmul(ctx, L.wqkv, b->ph, M, H, qkv_rows, H, b->pqkv, qkv_rows, b->ws, b->ws_bytes, st);
             if (rc) return rc;
+            AttnTcBuffers t = b->tc;
+            t.kvmax += (size_t)l * b->chunk * c.n_kv_heads * 2;
             auto rope = c.head_dim == 128 ? qk_rope_rows_kernel<4> : qk_rope_rows_kernel<2>;
             PX_TRY(launch_kernel(rope, dim3(M), dim3((c.n_q_heads + c.n_kv_heads + 1) * 32), 0, st,
                                  (const float *)b->pqkv, (const float *)L.q_norm, (const float *)L.k_norm,
                                  (const float *)m->rope_cos, (const float *)m->rope_sin, c.n_q_heads, c.n_kv_heads,
-                                 c.rms_eps, P, 0, b->pq, kc, vc, (long long)b->cache_stride));
-            const dim3 agrid((P + kPfBQ - 1) / kPfBQ, c.n_q_heads, cs);
-            if (c.head_dim == 128)
-                PX_TRY(launch_kernel(attention_prefill_kernel<128>, agrid, dim3(kPfThreads),
-                                     prefill_smem_floats<128>() * sizeof(float), st, (const float *)b->pq, c.n_q_heads,
-                                     c.n_kv_heads, P, (const float *)kc, (const float *)vc, (long long)b->cache_stride,
-                                     b->pattn));
-            else
-                PX_TRY(launch_kernel(attention_prefill_kernel<64>, agrid, dim3(kPfThreads),
-                                     prefill_smem_floats<64>() * sizeof(float), st, (const float *)b->pq, c.n_q_heads,
-                                     c.n_kv_heads, P, (const float *)kc, (const float *)vc, (long long)b->cache_stride,
-                                     b->pattn));
+                                 c.rms_eps, P, 0, kc, vc, (long long)b->cache_stride, t, cs));
+            PX_TRY(launch_attn_prep_kv(kc, vc, (long long)b->cache_stride, cs, P, c.n_kv_heads, c.head_dim, t, st));
+            PX_TRY(launch_attention_prefill_tc(cs, P, c.n_q_heads, c.n_kv_heads, c.head_dim, t, b->pattn, ctx->d_err,
+                                               st));
             rc = run_matmul(ctx, L.wo, b->pattn, M, qd, H, qd, b->ptmp, H, b->ws, b->ws_bytes, st);
             if (rc) return rc;
             PX_TRY(launch_kernel(add_rmsnorm_rows_kernel, dim3(M), dim3(kRowThreads), 0, st, b->px,
@@ -686,10 +588,6 @@ extern "C" int pyxis_cuda_model_generate_batch(pyxis_cuda_model *m, const int32_
     if (rc) return rc;
     BatchState *b = m->batch;
     cudaStream_t st = m->ctx->stream;
-    PX_TRY(cudaFuncSetAttribute(attention_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)(prefill_smem_floats<128>() * sizeof(float))));
-    PX_TRY(cudaFuncSetAttribute(attention_prefill_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)(prefill_smem_floats<64>() * sizeof(float))));
     // prompts (row stride n_prompt capacity == n_prompt here: the prefill reads rows of n_prompt)
     PX_TRY(cudaMemcpyAsync(b->d_prompt, prompts, n_seq * n_prompt * sizeof(int32_t), cudaMemcpyHostToDevice, st));
     const int zero = 0, last = (int)n_prompt - 1;
@@ -751,10 +649,6 @@ extern "C" int pyxis_cuda_model_prefill_hidden(pyxis_cuda_model *m, const int32_
     if (rc) return rc;
     BatchState *b = m->batch;
     cudaStream_t st = m->ctx->stream;
-    PX_TRY(cudaFuncSetAttribute(attention_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)(prefill_smem_floats<128>() * sizeof(float))));
-    PX_TRY(cudaFuncSetAttribute(attention_prefill_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)(prefill_smem_floats<64>() * sizeof(float))));
     PX_TRY(cudaMemcpyAsync(b->d_prompt, prompts, n_seq * n_prompt * sizeof(int32_t), cudaMemcpyHostToDevice, st));
     const int zero = 0, last = (int)n_prompt - 1;
     PX_TRY(cudaMemcpyAsync(b->d_step, &zero, sizeof(int), cudaMemcpyHostToDevice, st));

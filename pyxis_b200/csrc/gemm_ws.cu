@@ -23,10 +23,12 @@
 //     is finished by the CTA that completes its last part: it adds the parts' partial sums in part
 //     order (reruns are bit-identical) and writes y.
 //
-// Warp roles (320 threads): 0 TMA producer (codes + x_hi / x_lo tiles into a ring), 1 TMEM owner
-// and MMA issuer, 2-5 converters (one weight row per thread), 6-9 epilogue (one row per thread,
-// the warp's TMEM lane quarter).  Every mbarrier wait is bounded; a wait that runs out records a
-// code in the context's device flag and the CTA winds down (drains its copies and MMAs, frees TMEM).
+// Warp roles: 0 TMA producer of the codes (a deep ring of their own, refilled as soon as the
+// converters have read a stage), 1 TMA producer of the x_hi / x_lo tiles (a shorter ring, freed by
+// the MMAs), 2-3 TMEM owner and MMA issuers, 4-7 converters (one weight row per thread), then the
+// epilogue warps (one row per thread, the warp's TMEM lane quarter).  Every mbarrier wait is
+// bounded; a wait that runs out records a code in the context's device flag and the CTA winds down
+// (drains its copies and MMAs, frees TMEM).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
@@ -45,10 +47,12 @@ constexpr int WM = 128;       // weight rows per tile: MMA M, TMEM lanes
 constexpr int WSK = 128;      // K per stage
 constexpr int WG = 32;        // K per scale group (group-scale mode)
 constexpr int kGroupsPerStage = WSK / WG;
-// Warp roles: 0 TMA producer; 1 and 2 MMA issuers (even and odd stages: a tcgen05.mma costs its
-// issuing thread about 70 cycles at any N <= 128, and two issuers overlap that, measured 39-48
-// cycles per MMA); 3-6 converters; then the epilogue warps.  Warp 1 also owns TMEM.
-constexpr int kProdWarp = 0, kMmaWarp = 1, kNumIssuers = 2, kConvWarp0 = 3, kNumConv = 4, kEpiWarp0 = 7;
+// Warp roles: 0 TMA producer of the codes; 1 TMA producer of x; 2 and 3 MMA issuers (even and
+// odd stages: a tcgen05.mma costs its issuing thread about 70 cycles at any N <= 128, and two
+// issuers overlap that, measured 39-48 cycles per MMA); 4-7 converters; then the epilogue warps.
+// Warp 2 also owns TMEM.
+constexpr int kProdWarp = 0, kXWarp = 1, kMmaWarp = 2, kNumIssuers = 2, kConvWarp0 = 4, kNumConv = 4,
+              kEpiWarp0 = 8;
 constexpr int kMaxTokens = 64;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 constexpr uint32_t kABlock = WM * 128;      // one column block (64 of K) of the fp16 weight tile
@@ -111,7 +115,7 @@ struct WsRoles {
     static constexpr int CW = 16;
     static constexpr int EW = NBT / CW;
     static constexpr int kEpiWarps = 4 * EW;
-    static constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;  // 352, 480 or 736
+    static constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;  // 384, 512 or 768
     // A tcgen05.mma costs about the same at any N up to 256, so the MMA count per stage sets the
     // pace.  Up to 32 token columns x_hi and x_lo sit side by side in N (NSTACK): one N = 2 NBT MMA
     // per K-step of 16 multiplies the codes with both, into columns [0, NBT) and [NBT, 2 NBT) of the
@@ -127,22 +131,33 @@ struct WsRoles {
     static_assert(2 * kSetCols <= 512, "two sets of accumulators fit in TMEM");
 };
 
-template <int NBT>
+// Shared memory: NA converted fp16 weight tiles, NX x tiles, and as many stages of codes as fit
+// (the weight stream is what sets the time: with HBM latency of a few microseconds under load an
+// SM needs tens of KB of codes in flight to draw its share of the bandwidth).
+template <int NBT, bool INT4>
 struct WsSmem {
-    static constexpr int NR = NBT <= 32 ? 4 : 3;  // stages of codes + x tiles
-    static constexpr int NA = NBT <= 32 ? 3 : 2;  // converted weight tiles
+    static constexpr int NA = NBT <= 32 ? 3 : 2;                // converted weight tiles
+    static constexpr int NX = NBT == 16 ? 4 : (NBT == 32 ? 3 : 2);  // x tiles
     static constexpr uint32_t kBBlock = NBT * 128;             // one column block of an x tile
-    static constexpr uint32_t kRawMax = WM * 128;              // codes of a stage (int8: 16 KB)
-    // codes, then per 64-K column block c: x_hi rows, x_lo rows (one 2 NBT-row operand for NSTACK)
-    static constexpr uint32_t kStage = kRawMax + 4 * kBBlock;
+    // per 64-K column block c: x_hi rows, x_lo rows (one 2 NBT-row operand for NSTACK)
+    static constexpr uint32_t kXStage = 4 * kBBlock;
+    static constexpr uint32_t kRaw = INT4 ? WM * 64 : WM * 128;  // codes of a stage
+    static constexpr uint32_t kBudget = 232448 - 1024 - 512;      // alignment slack, barriers
+    static constexpr int NRAW_FIT = (int)((kBudget - NA * kABytes - NX * kXStage) / kRaw);
+    static constexpr int NRAW = NRAW_FIT > 16 ? 16 : NRAW_FIT;
     static constexpr uint32_t a = 0;
-    static constexpr uint32_t r = a + NA * kABytes;
-    static constexpr uint32_t bar = r + NR * kStage;
-    static constexpr uint32_t num_bars = 3 * NR + 2 * NA + 4 + 2;
+    static constexpr uint32_t x = a + NA * kABytes;
+    static constexpr uint32_t r = x + NX * kXStage;
+    static constexpr uint32_t bar = r + NRAW * kRaw;
+    static constexpr uint32_t num_bars = 2 * NRAW + 2 * NX + 2 * NA + 4 + 2;
     static constexpr uint32_t misc = bar + num_bars * 8;
     static constexpr uint32_t bytes = misc + 64 + 1024;  // + alignment slack
+    static_assert(NRAW >= 4, "a few stages of codes in flight");
+    static_assert(num_bars * 8 + 64 <= 512, "barriers fit their reserve");
 };
-static_assert(WsSmem<16>::bytes <= 232448 && WsSmem<32>::bytes <= 232448 && WsSmem<64>::bytes <= 232448,
+static_assert(WsSmem<16, true>::bytes <= 232448 && WsSmem<32, true>::bytes <= 232448 &&
+                  WsSmem<64, true>::bytes <= 232448 && WsSmem<16, false>::bytes <= 232448 &&
+                  WsSmem<32, false>::bytes <= 232448 && WsSmem<64, false>::bytes <= 232448,
               "227 KB of shared memory per CTA");
 
 // CW token columns of this warp's 32 TMEM lanes, without waiting (valid after tmem_wait_regs).
@@ -183,28 +198,32 @@ template <int NBT, bool INT4, bool GROUPED>
 __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
     gemm_ws_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_xhi,
                    const __grid_constant__ CUtensorMap tm_xlo, const WsParams p) {
-    using L = WsSmem<NBT>;
+    using L = WsSmem<NBT, INT4>;
     using R = WsRoles<NBT>;
-    constexpr int NR = L::NR, NA = L::NA;
-    constexpr uint32_t kRaw = INT4 ? WM * 64 : WM * 128;
-    constexpr uint32_t kXTx = 4 * L::kBBlock;
+    constexpr int NRAW = L::NRAW, NX = L::NX, NA = L::NA;
+    constexpr uint32_t kRaw = L::kRaw;
+    constexpr uint32_t kXTx = L::kXStage;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::bar);
-    // code / x stages: fullw (the codes landed), fullx (the x tiles landed), rawfree (both consumed)
-    uint64_t *full = bars, *rawfree = bars + NR, *fullx = bars + 2 * NR;
-    uint64_t *conv = bars + 3 * NR, *aempty = conv + NA;   // converted weight tiles
-    uint64_t *accfull = aempty + NA, *accempty = accfull + 2, *drain = accempty + 2;  // per accumulator set
+    // codes: rfull (landed) / rempty (read by the converters); x tiles: xfull / xempty (read by the
+    // MMAs); converted weight tiles: conv / aempty; accumulator sets: accfull / accempty
+    uint64_t *rfull = bars, *rempty = bars + NRAW, *xfull = bars + 2 * NRAW, *xempty = xfull + NX;
+    uint64_t *conv = xempty + NX, *aempty = conv + NA;
+    uint64_t *accfull = aempty + NA, *accempty = accfull + 2, *drain = accempty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::misc);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::misc + 4);
     volatile int *last_flag = reinterpret_cast<volatile int *>(smem + L::misc + 8);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < NR; ++s) {
-            tc::mbar_init(&full[s], 1);
-            tc::mbar_init(&fullx[s], 1);
-            tc::mbar_init(&rawfree[s], kNumConv + 1);  // the converters' reads of the codes + the MMAs' reads of x
+        for (int s = 0; s < NRAW; ++s) {
+            tc::mbar_init(&rfull[s], 1);
+            tc::mbar_init(&rempty[s], kNumConv);
+        }
+        for (int x = 0; x < NX; ++x) {
+            tc::mbar_init(&xfull[x], 1);
+            tc::mbar_init(&xempty[x], 1);
         }
         for (int a = 0; a < NA; ++a) {
             tc::mbar_init(&conv[a], kNumConv);
@@ -227,65 +246,65 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == kProdWarp) {
-        // ------------------------------------------------------------------ TMA producer
+        // ------------------------------------------------------------------ codes producer
+        // The codes do not depend on the previous kernel: they stream from the start, as far
+        // ahead as the ring allows, while the previous kernel may still be finishing.
         if (lane == 0) {
             tc::prefetch_tmap(&tm_w);
-            tc::prefetch_tmap(&tm_xhi);
-            tc::prefetch_tmap(&tm_xlo);
-            // the codes do not depend on the previous kernel: the first NR stages' codes go out (and
-            // are converted) before griddepcontrol.wait, their x tiles after it
-            int xg = 0;  // stages whose x tiles are issued
-            auto issue_x = [&](int slot, int k) {
-                uint8_t *b0 = smem + L::r + slot * L::kStage + L::kRawMax;  // [hi 0 | lo 0 | hi 1 | lo 1]
-                tc::mbar_arrive_expect_tx(&fullx[slot], kXTx);
-                tc::tma_load_2d(b0, &tm_xhi, k, 0, &fullx[slot]);
-                tc::tma_load_2d(b0 + L::kBBlock, &tm_xlo, k, 0, &fullx[slot]);
-                tc::tma_load_2d(b0 + 2 * L::kBBlock, &tm_xhi, k + 64, 0, &fullx[slot]);
-                tc::tma_load_2d(b0 + 3 * L::kBBlock, &tm_xlo, k + 64, 0, &fullx[slot]);
-                ++xg;
-            };
-            int g = 0, s = 0, ph = 0, pend_n = 0;
-            int pend_k[NR];
-            bool ok = true, waited = false;
+            int g = 0;
+            bool ok = true;
             for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
                 int tile, part, s0, s1;
                 unit_range(p, u, tile, part, s0, s1);
                 for (int sk = s0; sk < s1; ++sk, ++g) {
-                    if (g >= NR && !tc::mbar_wait_bounded(&rawfree[s], (uint32_t)((ph - 1) & 1), abort_flag, p.err,
+                    const int s = g % NRAW;
+                    if (g >= NRAW && !tc::mbar_wait_bounded(&rempty[s], (uint32_t)((g / NRAW - 1) & 1), abort_flag,
+                                                            p.err, kErrProd, kTimeoutNs)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::mbar_arrive_expect_tx(&rfull[s], kRaw);
+                    tc::tma_load_2d(smem + L::r + s * kRaw, &tm_w, sk * (INT4 ? 64 : 128), tile * WM, &rfull[s]);
+                }
+            }
+            if (*abort_flag) {  // let the copies already issued land before the CTA exits
+                volatile int no_abort = 0;
+                for (int j = g > NRAW ? g - NRAW : 0; j < g; ++j)
+                    tc::mbar_wait_bounded(&rfull[j % NRAW], (j / NRAW) & 1, &no_abort, p.err, kErrDrain, 100000000ull);
+            }
+        }
+    } else if (warp == kXWarp) {
+        // ------------------------------------------------------------------ x producer
+        if (lane == 0) {
+            tc::prefetch_tmap(&tm_xhi);
+            tc::prefetch_tmap(&tm_xlo);
+            pdl_wait();  // x_hi / x_lo are written by the split kernel just before this one
+            pdl_trigger();
+            int g = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+                int tile, part, s0, s1;
+                unit_range(p, u, tile, part, s0, s1);
+                for (int sk = s0; sk < s1; ++sk, ++g) {
+                    const int x = g % NX;
+                    if (g >= NX && !tc::mbar_wait_bounded(&xempty[x], (uint32_t)((g / NX - 1) & 1), abort_flag, p.err,
                                                           kErrProd, kTimeoutNs)) {
                         ok = false;
                         break;
                     }
-                    tc::mbar_arrive_expect_tx(&full[s], kRaw);
-                    tc::tma_load_2d(smem + L::r + s * L::kStage, &tm_w, sk * (INT4 ? 64 : 128), tile * WM, &full[s]);
-                    if (!waited) {
-                        pend_k[pend_n++] = sk * WSK;  // stage g == slot g here (g < NR)
-                        if (pend_n == NR) {
-                            pdl_wait();
-                            waited = true;
-                            for (int i = 0; i < pend_n; ++i) issue_x(i, pend_k[i]);
-                        }
-                    } else {
-                        issue_x(s, sk * WSK);
-                    }
-                    if (++s == NR) {
-                        s = 0;
-                        ++ph;
-                    }
+                    uint8_t *b0 = smem + L::x + x * L::kXStage;  // [hi 0 | lo 0 | hi 1 | lo 1]
+                    const int k = sk * WSK;
+                    tc::mbar_arrive_expect_tx(&xfull[x], kXTx);
+                    tc::tma_load_2d(b0, &tm_xhi, k, 0, &xfull[x]);
+                    tc::tma_load_2d(b0 + L::kBBlock, &tm_xlo, k, 0, &xfull[x]);
+                    tc::tma_load_2d(b0 + 2 * L::kBBlock, &tm_xhi, k + 64, 0, &xfull[x]);
+                    tc::tma_load_2d(b0 + 3 * L::kBBlock, &tm_xlo, k + 64, 0, &xfull[x]);
                 }
             }
-            if (!waited) {
-                pdl_wait();
-                if (ok)
-                    for (int i = 0; i < pend_n; ++i) issue_x(i, pend_k[i]);
-            }
-            pdl_trigger();
-            if (*abort_flag) {  // let the copies already issued land before the CTA exits
+            if (*abort_flag) {
                 volatile int no_abort = 0;
-                for (int j = g > NR ? g - NR : 0; j < g; ++j)
-                    tc::mbar_wait_bounded(&full[j % NR], (j / NR) & 1, &no_abort, p.err, kErrDrain, 100000000ull);
-                for (int j = xg > NR ? xg - NR : 0; j < xg; ++j)
-                    tc::mbar_wait_bounded(&fullx[j % NR], (j / NR) & 1, &no_abort, p.err, kErrDrain, 100000000ull);
+                for (int j = g > NX ? g - NX : 0; j < g; ++j)
+                    tc::mbar_wait_bounded(&xfull[j % NX], (j / NX) & 1, &no_abort, p.err, kErrDrain, 100000000ull);
             }
         }
     } else if (warp < kMmaWarp + kNumIssuers) {
@@ -296,7 +315,7 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
         if (lane == 0) {
             constexpr uint32_t idesc = tc::idesc_f16_f32(WM, R::NSTACK ? 2 * NBT : NBT);
             const uint64_t a_d = tc::desc_sw128(tc::smem_u32(smem + L::a));
-            const uint64_t b_d = tc::desc_sw128(tc::smem_u32(smem + L::r + L::kRawMax));
+            const uint64_t b_d = tc::desc_sw128(tc::smem_u32(smem + L::x));
             int st = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
@@ -305,15 +324,15 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
                 for (int sk = s0; sk < s1; ++sk, ++st) {
                     if ((st & 1) != issuer) continue;
                     const int set = issuer, use = st >> 1;
-                    const int s = st % NR, sph = st / NR, a = st % NA, aph = st / NA;
+                    const int x = st % NX, xph = st / NX, a = st % NA, aph = st / NA;
                     ok = tc::mbar_wait_bounded(&conv[a], (uint32_t)(aph & 1), abort_flag, p.err, kErrMma, kTimeoutNs) &&
-                         tc::mbar_wait_bounded(&fullx[s], (uint32_t)(sph & 1), abort_flag, p.err, kErrMma, kTimeoutNs) &&
+                         tc::mbar_wait_bounded(&xfull[x], (uint32_t)(xph & 1), abort_flag, p.err, kErrMma, kTimeoutNs) &&
                          (use == 0 || tc::mbar_wait_bounded(&accempty[set], (uint32_t)((use - 1) & 1), abort_flag,
                                                             p.err, kErrMma, kTimeoutNs));
                     if (!ok) break;
                     tc::tc_fence_after();
                     const uint64_t abase = a_d + (uint64_t)(a * (kABytes >> 4));
-                    const uint64_t bbase = b_d + (uint64_t)(s * (L::kStage >> 4));
+                    const uint64_t bbase = b_d + (uint64_t)(x * (L::kXStage >> 4));
                     const uint32_t dset = tmem_base + (uint32_t)(set * R::kSetCols);
                     // K-step ks of group gi covers K [32 gi + 16 ks, +16) of the stage; the issue order
                     // runs over the groups innermost, so consecutive MMAs use different accumulators
@@ -333,7 +352,7 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
                                 tc::mma_f16(d, ad, bd, idesc, (uint32_t)(ks | hl));
                             }
                     tc::mma_commit(&accfull[set]);
-                    tc::mma_commit(&rawfree[s]);
+                    tc::mma_commit(&xempty[x]);
                     tc::mma_commit(&aempty[a]);
                 }
             }
@@ -345,15 +364,16 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
     } else if (warp < kEpiWarp0) {
         // ------------------------------------------------------------------ converters
         const int r = threadIdx.x - kConvWarp0 * 32;  // weight row of the tile
-        int s = 0, sph = 0, a = 0, aph = 0, g = 0;
+        int g = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
             int tile, part, s0, s1;
             unit_range(p, u, tile, part, s0, s1);
             for (int sk = s0; sk < s1; ++sk, ++g) {
+                const int s = g % NRAW, sph = g / NRAW, a = g % NA, aph = g / NA;
                 int w_ok = 1;
                 if (lane == 0) {
-                    w_ok = tc::mbar_wait_bounded(&full[s], (uint32_t)(sph & 1), abort_flag, p.err, kErrConv, kTimeoutNs);
+                    w_ok = tc::mbar_wait_bounded(&rfull[s], (uint32_t)(sph & 1), abort_flag, p.err, kErrConv, kTimeoutNs);
                     if (w_ok && g >= NA)
                         w_ok = tc::mbar_wait_bounded(&aempty[a], (uint32_t)((aph - 1) & 1), abort_flag, p.err, kErrConv,
                                                      kTimeoutNs);
@@ -363,15 +383,18 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
                     ok = false;
                     break;
                 }
-                const uint8_t *raw = smem + L::r + s * L::kStage;
+                const uint8_t *raw = smem + L::r + s * kRaw;
                 uint8_t *ab = smem + L::a + a * kABytes;
                 if constexpr (INT4) {
                     // 64-byte rows, 64-byte TMA swizzle: chunk c at ((c ^ ((r >> 1) & 3)) << 4); chunk c
                     // holds K [32c, 32c + 32): one scale group
+                    uint4 w4[4];
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+                        w4[c] = *reinterpret_cast<const uint4 *>(raw + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
-                        const uint4 w = *reinterpret_cast<const uint4 *>(raw + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
-                        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+                        const uint32_t ws[4] = {w4[c].x, w4[c].y, w4[c].z, w4[c].w};
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {  // word i: K [32c + 8i, 32c + 8i + 8)
                             uint32_t h[4];
@@ -383,14 +406,17 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
                     }
                 } else {
                     // 128-byte rows, 128-byte TMA swizzle: chunk c (16 of K) at ((c ^ (r & 7)) << 4)
+                    uint4 w8[8];
+#pragma unroll
+                    for (int c = 0; c < 8; ++c)
+                        w8[c] = *reinterpret_cast<const uint4 *>(raw + r * 128 + ((c ^ (r & 7)) << 4));
 #pragma unroll
                     for (int c = 0; c < 8; ++c) {
-                        const uint4 w = *reinterpret_cast<const uint4 *>(raw + r * 128 + ((c ^ (r & 7)) << 4));
                         uint32_t h[8];
-                        i8x4_to_h(w.x, h[0], h[1]);
-                        i8x4_to_h(w.y, h[2], h[3]);
-                        i8x4_to_h(w.z, h[4], h[5]);
-                        i8x4_to_h(w.w, h[6], h[7]);
+                        i8x4_to_h(w8[c].x, h[0], h[1]);
+                        i8x4_to_h(w8[c].y, h[2], h[3]);
+                        i8x4_to_h(w8[c].z, h[4], h[5]);
+                        i8x4_to_h(w8[c].w, h[6], h[7]);
                         const int k = 16 * c;
                         uint8_t *blk = ab + (k >> 6) * kABlock;
                         *reinterpret_cast<uint4 *>(blk + sw128_off(r, (k & 63) >> 3)) = make_uint4(h[0], h[1], h[2], h[3]);
@@ -402,15 +428,7 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
                 __syncwarp();
                 if (lane == 0) {
                     tc::mbar_arrive(&conv[a]);
-                    tc::mbar_arrive(&rawfree[s]);
-                }
-                if (++s == NR) {
-                    s = 0;
-                    ++sph;
-                }
-                if (++a == NA) {
-                    a = 0;
-                    ++aph;
+                    tc::mbar_arrive(&rempty[s]);
                 }
             }
         }
@@ -644,10 +662,11 @@ cudaError_t run_ws(const CUtensorMap &tw, const CUtensorMap &th, const CUtensorM
     auto kern = gemm_ws_kernel<NBT, INT4, GROUPED>;
     static std::atomic<uint64_t> attr_done{0};
     const cudaError_t e = once_per_device(attr_done, [&] {
-        return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)WsSmem<NBT>::bytes);
+        return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)WsSmem<NBT, INT4>::bytes);
     });
     if (e != cudaSuccess) return e;
-    return launch_kernel(kern, dim3(grid), dim3(WsRoles<NBT>::kThreads), WsSmem<NBT>::bytes, st, tw, th, tl, p);
+    return launch_kernel(kern, dim3(grid), dim3(WsRoles<NBT>::kThreads), WsSmem<NBT, INT4>::bytes, st, tw, th, tl, p);
 }
 
 template <bool INT4, bool GROUPED>

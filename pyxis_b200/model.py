@@ -61,9 +61,12 @@ class SyntheticModel:
     """Seeded bf16 tensors of one model: ``bf16(name)`` -> np.uint16 bits, generated on demand
     (include/pyxis_synth.h), so the oracle and the device see the same values."""
 
-    def __init__(self, cfg: ModelConfig, seed: int = 0x5EED):
+    def __init__(self, cfg: ModelConfig, seed: int = 0x5EED, head_norm_value: float = 1.0):
+        """``head_norm_value``: the QK-RMSNorm weight (1 like the other norms; larger values
+        sharpen the attention, as trained QK-norm weights do)."""
         self.cfg = cfg
         self.seed = seed
+        self.head_norm_value = head_norm_value
 
     def shape(self, name: str) -> tuple[int, int]:
         c = self.cfg
@@ -81,7 +84,7 @@ class SyntheticModel:
         return np.ones(self.cfg.hidden, np.float32)
 
     def head_norm(self):
-        return np.ones(self.cfg.head_dim, np.float32) if self.cfg.qk_norm else None
+        return np.full(self.cfg.head_dim, self.head_norm_value, np.float32) if self.cfg.qk_norm else None
 
 
 def _quantize(bits: np.ndarray, qtype: str, in_features: int, device: int):

@@ -62,8 +62,9 @@ GQA_2048 = ModelConfig(hidden=256, n_layers=1, n_q_heads=16, n_kv_heads=8, head_
 
 
 def test_prefill_of_2048_positions_matches_oracle():
-    """The batched prefill at the config-5 prompt length: 2048 positions, i.e. 32 query tiles of
-    64 and 64 key tiles of 32 in the causal prefill attention, with the GQA 16 / 8 x 128 heads.
+    """The batched prefill at the config-5 prompt length: 2048 positions, i.e. 16 query tiles of
+    128 with up to 16 key tiles of 128 in the tensor-core causal attention (several raises of the
+    running maximum per row), with the GQA 16 / 8 x 128 heads.
     Sequence 0's final-norm hidden state (the first token's lm_head input) is held to the matmul
     bar against the oracle's prefill -- rel(y, r) = max_i |y_i - r_i| / max(|r_i|, 1e-3 max|r|)
     <= 1e-3 -- and sequence 1's greedy tokens must equal the oracle's."""
@@ -79,6 +80,29 @@ def test_prefill_of_2048_positions_matches_oracle():
     assert err <= 1e-3, err
     want = oracle.greedy_decode(GQA_2048, m.bf16, "int4", list(prompts[1]), 4)
     assert np.array_equal(toks[1], want), (toks[1], want)
+
+
+@pytest.mark.parametrize("hn", [3.0])
+def test_prefill_with_sharp_attention_matches_oracle(hn):
+    """QK-norm weights of 3 (scores 9x those of unit weights): peaked softmax rows whose running
+    maximum is raised at different key tiles for different rows of one warp -- the prefill
+    attention's per-row rescaling -- over 640 positions (5 query and key tiles of 128), against
+    the oracle: the final-norm hidden state of every sequence at the bar of the test above, and
+    the greedy tokens."""
+    cfg = GQA_2048
+    m = SyntheticModel(cfg, seed=43, head_norm_value=hn)
+    hn_w = m.head_norm()
+    dec = Decoder(m, qtype="int8", max_seq=640 + 4)
+    prompts = synth_tokens(0x640, 2 * 640, cfg.vocab).reshape(2, 640)
+    hid = dec.prefill_hidden(prompts)
+    toks, _ = dec.generate_batch(prompts, 3)
+    dec.close()
+    for sq in range(2):
+        r = oracle.prefill_hidden(cfg, m.bf16, "int8", list(prompts[sq]), head_norm=hn_w).astype(np.float64)
+        err = float((np.abs(hid[sq].astype(np.float64) - r) / np.maximum(np.abs(r), 1e-3 * np.abs(r).max())).max())
+        assert err <= 1e-3, (sq, err)
+        want = oracle.greedy_decode(cfg, m.bf16, "int8", list(prompts[sq]), 3, head_norm=hn_w)
+        assert np.array_equal(toks[sq], want), (sq, toks[sq], want)
 
 
 def test_batch_rejects_bad_arguments():
