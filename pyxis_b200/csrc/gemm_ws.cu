@@ -127,8 +127,18 @@ struct WsRoles {
     static constexpr int KS = NSTACK ? 2 : 1;
     static constexpr int kAccPerStage = kGroupsPerStage * KS;
     static constexpr int kSetCols = kAccPerStage * NBT;
-    static constexpr uint32_t kTmemCols = 2 * kSetCols <= 128 ? 128 : (2 * kSetCols <= 256 ? 256 : 512);
-    static_assert(2 * kSetCols <= 512, "two sets of accumulators fit in TMEM");
+    // TA: the converted weight tiles live in TMEM (one lane per weight row, 64 columns of fp16
+    // pairs per 128 of K) and the MMAs read operand A from there, when the accumulators leave room:
+    // shared memory then carries only the codes and the x tiles (the fp16 tile in shared memory
+    // cost 32 KB of stores and 32 KB of tensor-core reads per stage), and a converter thread
+    // writes its row with two tcgen05.st instead of sixteen 16-byte stores.
+    static constexpr bool TA = 2 * kSetCols + 3 * 64 <= 512;
+    static constexpr int kNAT = TA ? 3 : 0;  // converted tiles in TMEM
+    static constexpr int kSets = 2;
+    static constexpr uint32_t kACol0 = kSets * kSetCols;  // first A column
+    static constexpr uint32_t kTmemNeed = kSets * kSetCols + kNAT * 64;
+    static constexpr uint32_t kTmemCols = kTmemNeed <= 128 ? 128 : (kTmemNeed <= 256 ? 256 : 512);
+    static_assert(kTmemNeed <= 512 && kSets >= 2, "two sets of accumulators fit in TMEM");
 };
 
 // Shared memory: NA converted fp16 weight tiles, NX x tiles, and as many stages of codes as fit
@@ -136,24 +146,26 @@ struct WsRoles {
 // SM needs tens of KB of codes in flight to draw its share of the bandwidth).
 template <int NBT, bool INT4>
 struct WsSmem {
-    static constexpr int NA = NBT <= 32 ? 3 : 2;                // converted weight tiles
-    static constexpr int NX = NBT == 16 ? 4 : (NBT == 32 ? 3 : 2);  // x tiles
+    static constexpr bool TA = WsRoles<NBT>::TA;
+    static constexpr int NA = TA ? WsRoles<NBT>::kNAT : (NBT <= 32 ? 3 : 2);  // converted weight tiles
+    static constexpr uint32_t kASlot = TA ? 0 : kABytes;       // (in TMEM with TA)
+    static constexpr int NX = TA ? 8 : (NBT == 16 ? 4 : (NBT == 32 ? 3 : 2));  // x tiles
     static constexpr uint32_t kBBlock = NBT * 128;             // one column block of an x tile
     // per 64-K column block c: x_hi rows, x_lo rows (one 2 NBT-row operand for NSTACK)
     static constexpr uint32_t kXStage = 4 * kBBlock;
     static constexpr uint32_t kRaw = INT4 ? WM * 64 : WM * 128;  // codes of a stage
-    static constexpr uint32_t kBudget = 232448 - 1024 - 512;      // alignment slack, barriers
-    static constexpr int NRAW_FIT = (int)((kBudget - NA * kABytes - NX * kXStage) / kRaw);
+    static constexpr uint32_t kBudget = 232448 - 1024 - 1024;     // alignment slack, barriers
+    static constexpr int NRAW_FIT = (int)((kBudget - NA * kASlot - NX * kXStage) / kRaw);
     static constexpr int NRAW = NRAW_FIT > 16 ? 16 : NRAW_FIT;
     static constexpr uint32_t a = 0;
-    static constexpr uint32_t x = a + NA * kABytes;
+    static constexpr uint32_t x = a + NA * kASlot;
     static constexpr uint32_t r = x + NX * kXStage;
     static constexpr uint32_t bar = r + NRAW * kRaw;
-    static constexpr uint32_t num_bars = 2 * NRAW + 2 * NX + 2 * NA + 4 + 2;
+    static constexpr uint32_t num_bars = 2 * NRAW + 2 * NX + 2 * NA + 2 * WsRoles<NBT>::kSets + 2;
     static constexpr uint32_t misc = bar + num_bars * 8;
     static constexpr uint32_t bytes = misc + 64 + 1024;  // + alignment slack
     static_assert(NRAW >= 4, "a few stages of codes in flight");
-    static_assert(num_bars * 8 + 64 <= 512, "barriers fit their reserve");
+    static_assert(num_bars * 8 + 64 <= 1024, "barriers fit their reserve");
 };
 static_assert(WsSmem<16, true>::bytes <= 232448 && WsSmem<32, true>::bytes <= 232448 &&
                   WsSmem<64, true>::bytes <= 232448 && WsSmem<16, false>::bytes <= 232448 &&
@@ -210,7 +222,7 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
     // MMAs); converted weight tiles: conv / aempty; accumulator sets: accfull / accempty
     uint64_t *rfull = bars, *rempty = bars + NRAW, *xfull = bars + 2 * NRAW, *xempty = xfull + NX;
     uint64_t *conv = xempty + NX, *aempty = conv + NA;
-    uint64_t *accfull = aempty + NA, *accempty = accfull + 2, *drain = accempty + 2;
+    uint64_t *accfull = aempty + NA, *accempty = accfull + R::kSets, *drain = accempty + R::kSets;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::misc);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::misc + 4);
     volatile int *last_flag = reinterpret_cast<volatile int *>(smem + L::misc + 8);
@@ -229,7 +241,7 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
             tc::mbar_init(&conv[a], kNumConv);
             tc::mbar_init(&aempty[a], 1);
         }
-        for (int k = 0; k < 2; ++k) {
+        for (int k = 0; k < R::kSets; ++k) {
             tc::mbar_init(&accfull[k], 1);
             tc::mbar_init(&accempty[k], R::kEpiWarps);
         }
@@ -309,8 +321,8 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
         }
     } else if (warp < kMmaWarp + kNumIssuers) {
         // ------------------------------------------------------------------ MMA issuers
-        // Issuer i takes the stages st with st % 2 == i, into accumulator set i: the two sets, and
-        // the ring slots of consecutive stages, never meet.
+        // Issuer i takes the stages st with st % 2 == i, into accumulator set st % kSets; a set (and a
+        // ring slot) is reused only after the stage that last held it has been released.
         const int issuer = warp - kMmaWarp;
         if (lane == 0) {
             constexpr uint32_t idesc = tc::idesc_f16_f32(WM, R::NSTACK ? 2 * NBT : NBT);
@@ -323,7 +335,7 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
                 unit_range(p, u, tile, part, s0, s1);
                 for (int sk = s0; sk < s1; ++sk, ++st) {
                     if ((st & 1) != issuer) continue;
-                    const int set = issuer, use = st >> 1;
+                    const int set = st % R::kSets, use = st / R::kSets;
                     const int x = st % NX, xph = st / NX, a = st % NA, aph = st / NA;
                     ok = tc::mbar_wait_bounded(&conv[a], (uint32_t)(aph & 1), abort_flag, p.err, kErrMma, kTimeoutNs) &&
                          tc::mbar_wait_bounded(&xfull[x], (uint32_t)(xph & 1), abort_flag, p.err, kErrMma, kTimeoutNs) &&
@@ -332,6 +344,7 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
                     if (!ok) break;
                     tc::tc_fence_after();
                     const uint64_t abase = a_d + (uint64_t)(a * (kABytes >> 4));
+                    const uint32_t at = tmem_base + R::kACol0 + (uint32_t)(a * 64);
                     const uint64_t bbase = b_d + (uint64_t)(x * (L::kXStage >> 4));
                     const uint32_t dset = tmem_base + (uint32_t)(set * R::kSetCols);
                     // K-step ks of group gi covers K [32 gi + 16 ks, +16) of the stage; the issue order
@@ -349,7 +362,10 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
                                 const uint64_t bd = bbase + (uint64_t)((2 * (k >> 6) + hl) * (L::kBBlock >> 4)) + koff;
                                 const uint32_t d = dset + (uint32_t)(gi * R::KS * NBT);
                                 // a group's first K-step (x_hi) starts its accumulator
-                                tc::mma_f16(d, ad, bd, idesc, (uint32_t)(ks | hl));
+                                if constexpr (R::TA)
+                                    tc::mma_f16_ts(d, at + (uint32_t)(k >> 1), bd, idesc, (uint32_t)(ks | hl));
+                                else
+                                    tc::mma_f16(d, ad, bd, idesc, (uint32_t)(ks | hl));
                             }
                     tc::mma_commit(&accfull[set]);
                     tc::mma_commit(&xempty[x]);
@@ -384,47 +400,67 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
                     break;
                 }
                 const uint8_t *raw = smem + L::r + s * kRaw;
-                uint8_t *ab = smem + L::a + a * kABytes;
-                if constexpr (INT4) {
-                    // 64-byte rows, 64-byte TMA swizzle: chunk c at ((c ^ ((r >> 1) & 3)) << 4); chunk c
-                    // holds K [32c, 32c + 32): one scale group
-                    uint4 w4[4];
+                // the fp16 row as 64 columns of pairs, in two halves of 32 (K order of the converter:
+                // the int4 pairs are (e_i, e_i+4) of each 8-element group, x is split in the same order)
+                auto convert_half = [&](int hf, uint32_t (&hw)[32]) {
+                    if constexpr (INT4) {
+                        // 64-byte rows, 64-byte TMA swizzle: chunk c at ((c ^ ((r >> 1) & 3)) << 4); chunk
+                        // c holds K [32c, 32c + 32): one scale group -> columns 16c .. 16c + 15
 #pragma unroll
-                    for (int c = 0; c < 4; ++c)
-                        w4[c] = *reinterpret_cast<const uint4 *>(raw + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+                        for (int cc = 0; cc < 2; ++cc) {
+                            const int c = 2 * hf + cc;
+                            const uint4 w = *reinterpret_cast<const uint4 *>(raw + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+                            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        const uint32_t ws[4] = {w4[c].x, w4[c].y, w4[c].z, w4[c].w};
+                            for (int i = 0; i < 4; ++i) {  // word i: K [32c + 8i, +8) -> columns 16c + 4i ..
+                                uint32_t h[4];
+                                u4x8_to_h(ws[i], h);
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) {  // word i: K [32c + 8i, 32c + 8i + 8)
-                            uint32_t h[4];
-                            u4x8_to_h(ws[i], h);
-                            const int k = 32 * c + 8 * i;
-                            *reinterpret_cast<uint4 *>(ab + (k >> 6) * kABlock + sw128_off(r, (k & 63) >> 3)) =
-                                make_uint4(h[0], h[1], h[2], h[3]);
+                                for (int j = 0; j < 4; ++j) hw[cc * 16 + 4 * i + j] = h[j];
+                            }
+                        }
+                    } else {
+                        // 128-byte rows, 128-byte TMA swizzle: chunk c (16 of K) at ((c ^ (r & 7)) << 4)
+                        // -> columns 8c .. 8c + 7
+#pragma unroll
+                        for (int cc = 0; cc < 4; ++cc) {
+                            const int c = 4 * hf + cc;
+                            const uint4 w = *reinterpret_cast<const uint4 *>(raw + r * 128 + ((c ^ (r & 7)) << 4));
+                            uint32_t *h = &hw[cc * 8];
+                            i8x4_to_h(w.x, h[0], h[1]);
+                            i8x4_to_h(w.y, h[2], h[3]);
+                            i8x4_to_h(w.z, h[4], h[5]);
+                            i8x4_to_h(w.w, h[6], h[7]);
                         }
                     }
+                };
+                if constexpr (R::TA) {
+                    uint32_t h0[32], h1[32];
+                    convert_half(0, h0);
+                    convert_half(1, h1);
+                    const uint32_t ta = tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) + R::kACol0 + (uint32_t)(a * 64);
+                    tc::tmem_st32(ta, h0);
+                    tc::tmem_st32(ta + 32, h1);
+                    tc::tmem_wait_st();
+                    tc::tc_fence_before();  // the tile -> the MMAs that read it after the barrier
                 } else {
-                    // 128-byte rows, 128-byte TMA swizzle: chunk c (16 of K) at ((c ^ (r & 7)) << 4)
-                    uint4 w8[8];
+                    // the canonical K-major 128-byte-swizzled tile: columns 8j .. 8j + 7 (K 16j .. 16j + 15)
+                    // are 16-byte chunks 2 (j % 4) and 2 (j % 4) + 1 of 64-K block j / 4
+                    uint8_t *ab = smem + L::a + a * kABytes;
 #pragma unroll
-                    for (int c = 0; c < 8; ++c)
-                        w8[c] = *reinterpret_cast<const uint4 *>(raw + r * 128 + ((c ^ (r & 7)) << 4));
+                    for (int hf = 0; hf < 2; ++hf) {
+                        uint32_t hw[32];
+                        convert_half(hf, hw);
+                        uint8_t *blk = ab + hf * kABlock;
 #pragma unroll
-                    for (int c = 0; c < 8; ++c) {
-                        uint32_t h[8];
-                        i8x4_to_h(w8[c].x, h[0], h[1]);
-                        i8x4_to_h(w8[c].y, h[2], h[3]);
-                        i8x4_to_h(w8[c].z, h[4], h[5]);
-                        i8x4_to_h(w8[c].w, h[6], h[7]);
-                        const int k = 16 * c;
-                        uint8_t *blk = ab + (k >> 6) * kABlock;
-                        *reinterpret_cast<uint4 *>(blk + sw128_off(r, (k & 63) >> 3)) = make_uint4(h[0], h[1], h[2], h[3]);
-                        *reinterpret_cast<uint4 *>(blk + sw128_off(r, ((k & 63) >> 3) + 1)) =
-                            make_uint4(h[4], h[5], h[6], h[7]);
+                        for (int jj = 0; jj < 4; ++jj) {
+                            const uint32_t *h = &hw[jj * 8];
+                            *reinterpret_cast<uint4 *>(blk + sw128_off(r, 2 * jj)) = make_uint4(h[0], h[1], h[2], h[3]);
+                            *reinterpret_cast<uint4 *>(blk + sw128_off(r, 2 * jj + 1)) = make_uint4(h[4], h[5], h[6], h[7]);
+                        }
                     }
+                    tc::fence_proxy_async_smem();  // the fp16 tile -> the tensor core's reads
                 }
-                tc::fence_proxy_async_smem();  // the fp16 tile -> the tensor core's reads
                 __syncwarp();
                 if (lane == 0) {
                     tc::mbar_arrive(&conv[a]);
@@ -470,7 +506,7 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
                 }
             };
             for (int sk = s0; sk < s1; ++sk, ++st) {
-                const int set = st & 1, use = st >> 1;
+                const int set = st % R::kSets, use = st / R::kSets;
                 float4 sc4 = make_float4(1.f, 1.f, 1.f, 1.f);
                 if (GROUPED && rowok) sc4 = __ldg(reinterpret_cast<const float4 *>(p.scales + (size_t)row * gpr + sk * 4));
                 const float scs[4] = {sc4.x, sc4.y, sc4.z, sc4.w};
@@ -560,26 +596,42 @@ __global__ void __launch_bounds__(WsRoles<NBT>::kThreads, 1)
 
 // One CTA per token row: e = 15 - exponent(max|x|) so |x 2^e| < 2^15; hi = fp16(x 2^e),
 // lo = fp16(x 2^e - hi); inv = 2^-e.  PERM writes each 8-element group in the int4 converter's
-// order (e0, e4, e1, e5, e2, e6, e3, e7).
+// order (e0, e4, e1, e5, e2, e6, e3, e7).  A thread takes whole 8-element groups: two 16-byte
+// loads when the row is 16-byte aligned (VEC), one 16-byte store each of hi and lo.
 template <bool PERM>
-__global__ void __launch_bounds__(256) split_x_ws_kernel(const float *__restrict__ X, long long ldx, int K,
+__global__ void __launch_bounds__(512) split_x_ws_kernel(const float *__restrict__ X, long long ldx, int K,
                                                          __half *__restrict__ hi, __half *__restrict__ lo,
-                                                         float *__restrict__ inv) {
-    __shared__ float red[8];
+                                                         float *__restrict__ inv, int vec) {
+    __shared__ float red[16];
     // the matmul that reads this kernel's output may launch at once: it streams and converts its
     // weights before its own griddepcontrol.wait, which still waits for this kernel to finish
     pdl_trigger();
     pdl_wait();
-    const int m = blockIdx.x;
+    const int m = blockIdx.x, n8 = K / 8;
     const float *x = X + (size_t)m * ldx;
+    auto load8 = [&](int g, float (&v)[8]) {
+        if (vec) {
+            const float4 a = __ldg(reinterpret_cast<const float4 *>(x + 8 * g));
+            const float4 b = __ldg(reinterpret_cast<const float4 *>(x + 8 * g + 4));
+            v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = __ldg(x + 8 * g + j);
+        }
+    };
     float mx = 0.f;
-    for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(x[k]));
+    for (int g = threadIdx.x; g < n8; g += blockDim.x) {
+        float v[8];
+        load8(g, v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[j]));
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
     __syncthreads();
     mx = red[0];
-    for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w]);
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) mx = fmaxf(mx, red[w]);
     int e = 0;
     if (mx > 0.f && isfinite(mx)) {
         int ex;
@@ -587,19 +639,25 @@ __global__ void __launch_bounds__(256) split_x_ws_kernel(const float *__restrict
         e = 15 - ex;
         e = e > 120 ? 120 : (e < -120 ? -120 : e);
     }
-    if (threadIdx.x == 0) inv[m] = ldexpf(1.0f, -e);
+    const float sc = __int_as_float((127 + e) << 23);  // 2^e, exact
+    if (threadIdx.x == 0) inv[m] = __int_as_float((127 - e) << 23);
     __half *hrow = hi + (size_t)m * K, *lrow = lo + (size_t)m * K;
-    for (int k = threadIdx.x; k < K; k += blockDim.x) {
-        const float v = ldexpf(x[k], e);
-        const __half h = __float2half_rn(v);
-        const __half l = __float2half_rn(v - __half2float(h));
-        int d = k;
-        if (PERM) {
-            const int o = k & 7;
-            d = (k & ~7) | (o < 4 ? 2 * o : 2 * (o - 4) + 1);
+    for (int g = threadIdx.x; g < n8; g += blockDim.x) {
+        float v[8];
+        load8(g, v);
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            // output pair j: (v[2j], v[2j+1]) in order, (v[j], v[j+4]) permuted
+            const float a = (PERM ? v[j] : v[2 * j]) * sc, b = (PERM ? v[j + 4] : v[2 * j + 1]) * sc;
+            const __half2 h = __floats2half2_rn(a, b);
+            const float2 f = __half22float2(h);
+            const __half2 l = __floats2half2_rn(a - f.x, b - f.y);
+            hw[j] = *reinterpret_cast<const uint32_t *>(&h);
+            lw[j] = *reinterpret_cast<const uint32_t *>(&l);
         }
-        hrow[d] = h;
-        lrow[d] = l;
+        *reinterpret_cast<uint4 *>(hrow + 8 * g) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4 *>(lrow + 8 * g) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     }
 }
 
@@ -708,11 +766,11 @@ cudaError_t launch_gemm_ws(const QMatrix &w, const float *X, size_t M, size_t ld
     // the partial sums may use whatever the workspace holds beyond x's fp16 copies
     const WsLayout base = ws_layout(M, w.K, 0);
     if (ws_bytes < base.total || (reinterpret_cast<uintptr_t>(ws) & 255)) return cudaErrorInvalidValue;
+    const bool int4 = w.qtype == kQInt4, grouped = w.block_size == (size_t)WG;
     const int parts = choose_parts(w.N, w.K, nbt, num_sms, ws_bytes - base.partial);
     uint8_t *wsb = static_cast<uint8_t *>(ws);
     __half *xhi = reinterpret_cast<__half *>(wsb + base.xhi), *xlo = reinterpret_cast<__half *>(wsb + base.xlo);
     float *xinv = reinterpret_cast<float *>(wsb + base.xinv);
-    const bool int4 = w.qtype == kQInt4, grouped = w.block_size == (size_t)WG;
 
     CUtensorMap tw, th, tl;
     const uint64_t row_bytes = int4 ? w.K / 2 : w.K;
@@ -724,10 +782,12 @@ cudaError_t launch_gemm_ws(const QMatrix &w, const float *X, size_t M, size_t ld
                   CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
 
-    cudaError_t e = int4 ? launch_kernel(split_x_ws_kernel<true>, dim3((unsigned)M), dim3(256), 0, st, X,
-                                         (long long)ldx, (int)w.K, xhi, xlo, xinv)
-                         : launch_kernel(split_x_ws_kernel<false>, dim3((unsigned)M), dim3(256), 0, st, X,
-                                         (long long)ldx, (int)w.K, xhi, xlo, xinv);
+    const int vec = (reinterpret_cast<uintptr_t>(X) & 15) == 0 && (M == 1 || ldx % 4 == 0);
+    const unsigned threads = w.K >= 4096 ? 512 : 256;
+    cudaError_t e = int4 ? launch_kernel(split_x_ws_kernel<true>, dim3((unsigned)M), dim3(threads), 0, st, X,
+                                         (long long)ldx, (int)w.K, xhi, xlo, xinv, vec)
+                         : launch_kernel(split_x_ws_kernel<false>, dim3((unsigned)M), dim3(threads), 0, st, X,
+                                         (long long)ldx, (int)w.K, xhi, xlo, xinv, vec);
     if (e != cudaSuccess) return e;
 
     WsParams p{};

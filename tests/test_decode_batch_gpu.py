@@ -87,8 +87,12 @@ def test_prefill_with_sharp_attention_matches_oracle(hn):
     """QK-norm weights of 3 (scores 9x those of unit weights): peaked softmax rows whose running
     maximum is raised at different key tiles for different rows of one warp -- the prefill
     attention's per-row rescaling -- over 640 positions (5 query and key tiles of 128), against
-    the oracle: the final-norm hidden state of every sequence at the bar of the test above, and
-    the greedy tokens."""
+    the oracle: the greedy tokens, and the final-norm hidden state of every sequence within
+    max_i |y_i - r_i| <= 1e-5 max|r|.  With scores this large the reference's own f32 softmax is
+    the larger error term (about 5e-6 of max |out| against float64, where the tensor-core
+    attention measures 2e-6), so the element-wise 1e-3 bar of the test above would measure the
+    reference's rounding at the hidden state's near-zero elements; the max-norm bar is twice the
+    reference's own error."""
     cfg = GQA_2048
     m = SyntheticModel(cfg, seed=43, head_norm_value=hn)
     hn_w = m.head_norm()
@@ -99,8 +103,10 @@ def test_prefill_with_sharp_attention_matches_oracle(hn):
     dec.close()
     for sq in range(2):
         r = oracle.prefill_hidden(cfg, m.bf16, "int8", list(prompts[sq]), head_norm=hn_w).astype(np.float64)
-        err = float((np.abs(hid[sq].astype(np.float64) - r) / np.maximum(np.abs(r), 1e-3 * np.abs(r).max())).max())
-        assert err <= 1e-3, (sq, err)
+        d = np.abs(hid[sq].astype(np.float64) - r)
+        err_max = float(d.max() / np.abs(r).max())
+        err_elem = float((d / np.maximum(np.abs(r), 1e-3 * np.abs(r).max())).max())
+        assert err_max <= 1e-5, (sq, err_max, err_elem)
         want = oracle.greedy_decode(cfg, m.bf16, "int8", list(prompts[sq]), 3, head_norm=hn_w)
         assert np.array_equal(toks[sq], want), (sq, toks[sq], want)
 
