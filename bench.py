@@ -130,15 +130,17 @@ def measured_peak_hbm():
 
 
 def profiled_traffic(kernel_tag: str):
-    """dram bytes per launch of the dominant kernel from its committed ncu summary, if any."""
+    """dram bytes per launch of the dominant kernel from its committed ncu summary (the latest
+    capture it lists), if any."""
     p = os.path.join(ROOT, "profiles", f"{kernel_tag}.txt")
+    found = None
     try:
         for line in open(p):
             if line.startswith("traffic_bytes_per_launch:"):
-                return float(line.split(":", 1)[1].split()[0])
+                found = float(line.split(":", 1)[1].split()[0])
     except OSError:
         pass
-    return None
+    return found
 
 
 # ---------------------------------------------------------------------------------------------

@@ -273,8 +273,14 @@ int ensure_state(pyxis_cuda_model *m, int n_seq, int n_prompt, int n_new) {
     for (const auto &L : m->layers)
         for (auto [w, N, K] : {std::tuple{L.wqkv, qkv_rows, H}, std::tuple{L.wo, H, qd}, std::tuple{L.wgu, 2 * ffn, H},
                                std::tuple{L.wdown, H, ffn}})
-            if (w) ws = std::max(ws, gemm_tc_workspace_bytes_splitk(n_seq, N, K, w->block_size == K, w->block_size,
-                                                                    m->ctx->num_sms));
+            if (w) {
+                ws = std::max(ws, gemm_tc_workspace_bytes_splitk(n_seq, N, K, w->block_size == K, w->block_size,
+                                                                 m->ctx->num_sms));
+                // the prefill's products over all the chunk's rows (group-scaled weights converted
+                // once per product)
+                ws = std::max(ws, gemm_tc_workspace_bytes_splitk(rows, N, K, w->block_size == K, w->block_size,
+                                                                 m->ctx->num_sms));
+            }
     pyxis_cuda_comm *vp = m->vp_comm;
     const size_t head_rows = vp ? (size_t)vp->nranks * n_seq : (size_t)n_seq;
     // the decode step's products of n_seq rows on the weight-streaming matmul: x copies plus room

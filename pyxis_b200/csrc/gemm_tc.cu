@@ -42,6 +42,7 @@
 #include <algorithm>
 
 #include "kernels.h"
+#include "split_x.cuh"
 #include "tc_ptx.cuh"
 #include "tmap.cuh"
 
@@ -102,6 +103,7 @@ struct TcParams {
     int *err;
     int kb_per_split;       // K-blocks of one blockIdx.z slice (split-K over gridDim.z)
     float *part;            // split-K: [gridDim.z][M][N] partial products, else nullptr
+    const float *rowinv;    // pre-converted weights (PRE): [N] 2^-e per row
 };
 
 PYXIS_DEVINL uint32_t h2_bits(__half2 v) { return *reinterpret_cast<uint32_t *>(&v); }
@@ -179,7 +181,7 @@ __host__ __device__ constexpr int lcm_int(int a, int b) {
     return a / x * b;
 }
 
-template <int NA, int NB, int SPP, bool GROUPED, bool SMALL>
+template <int NA, int NB, int SPP, bool GROUPED, bool SMALL, bool PRE>
 __device__ __forceinline__ bool mma_loop(int num_kb, uint64_t ahi0, uint64_t alo0, uint64_t b0, uint32_t tmem_base,
                                       const MmaRing r) {
     constexpr int U = lcm_int(lcm_int(2 * NA, 2 * NB), 2 * SPP);
@@ -193,7 +195,9 @@ __device__ __forceinline__ bool mma_loop(int num_kb, uint64_t ahi0, uint64_t alo
         for (int jj = 0; jj < U; ++jj) {
             if (j0 + jj >= num_kb) return true;
             const int a = jj % NA, s = jj % NB, sp = jj % SPP, buf = (jj / SPP) & 1;
-            if (!tc::mbar_wait_bounded(&r.conv[a], (uint32_t)((jj / NA) & 1), r.abort_flag, r.err, kErrMma, kTimeoutNs) ||
+            // (pre-converted weights arrive by TMA with the stage: full[s] covers them)
+            if ((!PRE &&
+                 !tc::mbar_wait_bounded(&r.conv[a], (uint32_t)((jj / NA) & 1), r.abort_flag, r.err, kErrMma, kTimeoutNs)) ||
                 !tc::mbar_wait_bounded(&r.full[s], (uint32_t)((jj / NB) & 1), r.abort_flag, r.err, kErrMma, kTimeoutNs))
                 return false;
             if (sp == 0) {
@@ -230,18 +234,23 @@ __device__ __forceinline__ bool mma_loop(int num_kb, uint64_t ahi0, uint64_t alo
     return true;
 }
 
-template <int NA, int NB, bool GROUPED, bool SMALL>
+template <int NA, int NB, bool GROUPED, bool SMALL, bool PRE>
 __device__ __forceinline__ bool mma_loop_spp(int spp, int num_kb, uint64_t ahi0, uint64_t alo0, uint64_t b0,
                                              uint32_t tmem_base, const MmaRing &r) {
-    if (spp == 4) return mma_loop<NA, NB, 4, GROUPED, SMALL>(num_kb, ahi0, alo0, b0, tmem_base, r);
-    if (spp == 2) return mma_loop<NA, NB, 2, GROUPED, SMALL>(num_kb, ahi0, alo0, b0, tmem_base, r);
-    return mma_loop<NA, NB, 1, GROUPED, SMALL>(num_kb, ahi0, alo0, b0, tmem_base, r);
+    if (spp == 4) return mma_loop<NA, NB, 4, GROUPED, SMALL, PRE>(num_kb, ahi0, alo0, b0, tmem_base, r);
+    if (spp == 2) return mma_loop<NA, NB, 2, GROUPED, SMALL, PRE>(num_kb, ahi0, alo0, b0, tmem_base, r);
+    return mma_loop<NA, NB, 1, GROUPED, SMALL, PRE>(num_kb, ahi0, alo0, b0, tmem_base, r);
 }
 
-template <int NA, int NB, bool LO>
+// PRE: the weights were converted once for the call (pre_convert_grouped_kernel): the producer
+// brings the A_hi / A_lo tiles by TMA with each stage and the converter warps only publish the
+// rows' 2^-e -- for many token tiles, instead of converting every weight tile once per token tile.
+template <int NA, int NB, bool LO, bool PRE>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_xhi,
-                   const __grid_constant__ CUtensorMap tm_xlo, const TcParams p) {
+                   const __grid_constant__ CUtensorMap tm_xlo, const __grid_constant__ CUtensorMap tm_ahi,
+                   const __grid_constant__ CUtensorMap tm_alo, const TcParams p) {
+    static_assert(!PRE || (LO && NA == NB), "pre-converted weights: group scales, one ring");
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     using L = Smem<NA, NB, LO>;
@@ -261,7 +270,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // a tile with <= 64 tokens multiplies with N = 64: the rest of the token tile is TMA zero fill
     const bool small = p.M - m0 <= 64;
     const int raw_kb_bytes = p.qtype == kQInt8 ? 64 : 32;
-    const uint32_t stage_tx = 2 * kBBytes + (uint32_t)(BM * raw_kb_bytes);
+    const uint32_t stage_tx = 2 * kBBytes + (PRE ? 2 * kABytes : (uint32_t)(BM * raw_kb_bytes));
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NB; ++s) {
@@ -281,7 +290,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::fence_mbar_init();
     }
     if (warp == 0 && lane == 0) {
-        tc::prefetch_tmap(&tm_w);
+        if (PRE) {
+            tc::prefetch_tmap(&tm_ahi);
+            tc::prefetch_tmap(&tm_alo);
+        } else {
+            tc::prefetch_tmap(&tm_w);
+        }
         tc::prefetch_tmap(&tm_xhi);
         tc::prefetch_tmap(&tm_xlo);
     }
@@ -302,7 +316,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 tc::mbar_arrive_expect_tx(&full[s], stage_tx);
                 uint8_t *b = smem + L::b + s * 2 * kBBytes;
-                tc::tma_load_2d(smem + L::r + s * kRBytes, &tm_w, kb * raw_kb_bytes, n0, &full[s]);
+                if (PRE) {
+                    tc::tma_load_2d(smem + L::ahi + s * kABytes, &tm_ahi, kb * BK, n0, &full[s]);
+                    tc::tma_load_2d(smem + L::alo + s * kABytes, &tm_alo, kb * BK, n0, &full[s]);
+                } else {
+                    tc::tma_load_2d(smem + L::r + s * kRBytes, &tm_w, kb * raw_kb_bytes, n0, &full[s]);
+                }
                 tc::tma_load_2d(b, &tm_xhi, kb * BK, m0, &full[s]);
                 tc::tma_load_2d(b + kBBytes, &tm_xlo, kb * BK, m0, &full[s]);
                 ++issued;
@@ -321,8 +340,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t b0 = tc::desc_sw128(tc::smem_u32(smem + L::b));
             const MmaRing ring{full, conv, empty, aempty, accfull, accempty, abort_flag, p.err};
             const int spp = p.ksteps_per_period / (BK / 16);  // stages per fold period: 1, 2 or 4
-            if (small) mma_loop_spp<NA, NB, LO, true>(spp, num_kb, ahi0, alo0, b0, tmem_base, ring);
-            else mma_loop_spp<NA, NB, LO, false>(spp, num_kb, ahi0, alo0, b0, tmem_base, ring);
+            if (small) mma_loop_spp<NA, NB, LO, true, PRE>(spp, num_kb, ahi0, alo0, b0, tmem_base, ring);
+            else mma_loop_spp<NA, NB, LO, false, PRE>(spp, num_kb, ahi0, alo0, b0, tmem_base, ring);
             // wait for every MMA this thread issued before TMEM can be released
             tc::mma_commit(drain);
             volatile int no_abort = 0;
@@ -338,6 +357,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int r = ct % BM, half = ct / BM;  // row r, part `half` of the stage's K
         const int n = n0 + r;
         const bool nrow = n < p.N;
+        if (PRE) {
+            if (half == 0) rowinv[r] = nrow ? __ldg(p.rowinv + n) : 1.f;
+            bar_arrive(kBarRowInv, kRowInvThreads);
+        } else {
         const float *srow = p.scales + (size_t)(nrow ? n : 0) * p.groups_per_row;
         float se = 1.f;
         if (LO) {
@@ -482,6 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             load_scales(kb0 + j + 3, sc_b);
             if (!convert(j + 1, sc)) break;
         }
+        }
     } else {
         // ------------------------------------------------------------------ epilogue
         const int q = warp & 3;                 // TMEM lane quarter this warp may access
@@ -540,44 +564,64 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-// ---------------------------------------------------------------------------- split_x
-// One CTA per token row: e = 15 - exponent(max|x|) so |x * 2^e| < 2^15; hi = fp16(x 2^e),
-// lo = fp16(x 2^e - hi); inv = 2^-e.  PERM writes each 8-element group in int4 converter order.
-template <bool PERM>
-__global__ void __launch_bounds__(256) split_x_kernel(const float *__restrict__ X, long long ldx, int K,
-                                                      __half *__restrict__ hi, __half *__restrict__ lo,
-                                                      float *__restrict__ inv) {
-    __shared__ float red[8];
-    const int m = blockIdx.x;
-    const float *x = X + (size_t)m * ldx;
-    float mx = 0.f;
-    for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(x[k]));
+// The group-scaled weights as the GEMM's A operand, once per call (PRE): row n's codes times
+// their group scales times 2^e_n, as fp16 hi + lo in the converters' element order (split_pair),
+// and 2^-e_n beside them.  e_n keeps max |q s| 2^e_n below 2^14 over the whole row (the
+// converters' choice over a K slice differs only by a power of two, which scales hi and lo
+// exactly).  One warp per row; int4: a word of 8 codes per lane step, int8: 16 codes.
+template <bool INT4>
+__global__ void __launch_bounds__(256)
+    pre_convert_grouped_kernel(const uint8_t *__restrict__ W, const float *__restrict__ S, int N, int K, int group_k,
+                               __half *__restrict__ ahi, __half *__restrict__ alo, float *__restrict__ rowinv) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = blockIdx.x * 8 + warp;
+    if (n >= N) return;
+    const int gpr = K / group_k;
+    const float *srow = S + (size_t)n * gpr;
+    float smax = 0.f;
+    for (int g = lane; g < gpr; g += 32) smax = fmaxf(smax, fabsf(__ldg(srow + g)));
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
-    __syncthreads();
-    mx = red[0];
-    for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w]);
+    for (int o = 16; o > 0; o >>= 1) smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, o));
     int e = 0;
-    if (mx > 0.f && isfinite(mx)) {
+    const float bound = (INT4 ? 8.f : 127.f) * smax;
+    if (bound > 0.f && isfinite(bound)) {
         int ex;
-        frexpf(mx, &ex);  // mx = f * 2^ex, f in [0.5, 1)
-        e = 15 - ex;
-        e = e > 120 ? 120 : (e < -120 ? -120 : e);
+        frexpf(bound, &ex);  // bound < 2^ex
+        e = min(100, max(-100, 14 - ex));
     }
-    if (threadIdx.x == 0) inv[m] = ldexpf(1.0f, -e);
-    __half *hrow = hi + (size_t)m * K, *lrow = lo + (size_t)m * K;
-    for (int k = threadIdx.x; k < K; k += blockDim.x) {
-        const float v = ldexpf(x[k], e);
-        const __half h = __float2half_rn(v);
-        const __half l = __float2half_rn(v - __half2float(h));
-        int d = k;
-        if (PERM) {
-            const int o = k & 7;  // element o of a group goes to position (o < 4 ? 2o : 2(o-4)+1)
-            d = (k & ~7) | (o < 4 ? 2 * o : 2 * (o - 4) + 1);
+    const float se = ldexpf(1.0f, e);
+    if (lane == 0) rowinv[n] = ldexpf(1.0f, -e);
+    __half *hrow = ahi + (size_t)n * K, *lrow = alo + (size_t)n * K;
+    if (INT4) {
+        const uint32_t *wrow = reinterpret_cast<const uint32_t *>(W + (size_t)n * (K / 2));
+        for (int i = lane; i < K / 8; i += 32) {  // word i: elements 8i .. 8i + 7
+            float2 e4[4];
+            u4x8_to_f32_pairs(__ldg(wrow + i), e4);
+            const float sc = __ldg(srow + (8 * i) / group_k) * se;
+            uint32_t hi[4], lo[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) split_pair(e4[j], f2(sc, sc), hi[j], lo[j]);
+            *reinterpret_cast<uint4 *>(hrow + 8 * i) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<uint4 *>(lrow + 8 * i) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
         }
-        hrow[d] = h;
-        lrow[d] = l;
+    } else {
+        const uint4 *wrow = reinterpret_cast<const uint4 *>(W + (size_t)n * K);
+        for (int i = lane; i < K / 16; i += 32) {  // codes 16i .. 16i + 15 (one group)
+            const uint4 w = __ldg(wrow + i);
+            float2 f[8];
+            i8x4_to_f32(w.x, f[0], f[1]);
+            i8x4_to_f32(w.y, f[2], f[3]);
+            i8x4_to_f32(w.z, f[4], f[5]);
+            i8x4_to_f32(w.w, f[6], f[7]);
+            const float sc = __ldg(srow + (16 * i) / group_k) * se;
+            uint32_t hi[8], lo[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) split_pair(f[j], f2(sc, sc), hi[j], lo[j]);
+            *reinterpret_cast<uint4 *>(hrow + 16 * i) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<uint4 *>(hrow + 16 * i + 8) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+            *reinterpret_cast<uint4 *>(lrow + 16 * i) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            *reinterpret_cast<uint4 *>(lrow + 16 * i + 8) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+        }
     }
 }
 
@@ -620,6 +664,13 @@ bool gemm_tc_supported(const QMatrix &w) {
 }
 
 size_t gemm_tc_workspace_bytes(size_t M, size_t K) { return 2 * align256(M * K * 2) + align256(M * 4); }
+
+namespace {
+// Token rows from which group-scaled weights are converted once per call (more than two token
+// tiles share every weight tile) instead of once per token tile.
+constexpr size_t kPreMinM = 2 * BN + 1;
+size_t pre_bytes(size_t N, size_t K) { return 2 * align256(N * K * 2) + align256(N * 4); }
+}  // namespace
 
 namespace {
 // K-steps (16 of K each) accumulated in TMEM before the epilogue folds them into fp32 registers:
@@ -681,7 +732,8 @@ size_t gemm_tc_workspace_bytes_splitk(size_t M, size_t N, size_t K, int block_si
     QMatrix q{kQInt8, nullptr, nullptr, block_size_is_k ? K : block_size, N, K};
     int ks, kb;
     plan_splitk(q, M, num_sms, ks, kb);
-    return gemm_tc_workspace_bytes(M, K) + (ks > 1 ? align256((size_t)ks * M * N * 4) : 0);
+    return gemm_tc_workspace_bytes(M, K) + (ks > 1 ? align256((size_t)ks * M * N * 4) : 0) +
+           (!block_size_is_k && M >= kPreMinM ? pre_bytes(N, K) : 0);
 }
 
 cudaError_t launch_gemm_tc(const QMatrix &w, const float *X, size_t M, size_t ldx, float *Y, size_t ldy, void *ws,
@@ -691,10 +743,11 @@ cudaError_t launch_gemm_tc(const QMatrix &w, const float *X, size_t M, size_t ld
     __half *xhi = reinterpret_cast<__half *>(wsb);
     __half *xlo = reinterpret_cast<__half *>(wsb + align256(M * K * 2));
     float *xinv = reinterpret_cast<float *>(wsb + 2 * align256(M * K * 2));
+    const unsigned threads = K >= 4096 ? 512 : 256;  // (X is 16-byte aligned, ldx % 4 == 0 on this path)
     if (w.qtype == kQInt4)
-        split_x_kernel<true><<<(unsigned)M, 256, 0, st>>>(X, (long long)ldx, K, xhi, xlo, xinv);
+        split_x_rows_kernel<true><<<(unsigned)M, threads, 0, st>>>(X, (long long)ldx, K, xhi, xlo, xinv, 1);
     else
-        split_x_kernel<false><<<(unsigned)M, 256, 0, st>>>(X, (long long)ldx, K, xhi, xlo, xinv);
+        split_x_rows_kernel<false><<<(unsigned)M, threads, 0, st>>>(X, (long long)ldx, K, xhi, xlo, xinv, 1);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
 
@@ -727,32 +780,61 @@ cudaError_t launch_gemm_tc(const QMatrix &w, const float *X, size_t M, size_t ld
     p.err = err;
     int ks = 1, kb_per = K / BK;
     plan_splitk(w, M, num_sms, ks, kb_per);
-    const size_t base = gemm_tc_workspace_bytes(M, (size_t)K);
+    size_t base = gemm_tc_workspace_bytes(M, (size_t)K);
     if (ks > 1 && ws_bytes >= base + align256((size_t)ks * M * N * 4)) {
         p.part = reinterpret_cast<float *>(wsb + base);
+        base += align256((size_t)ks * M * N * 4);
     } else {
         ks = 1;
         kb_per = K / BK;
         p.part = nullptr;
     }
     p.kb_per_split = kb_per;
+    // group-scaled weights for many token tiles: converted once, then streamed by TMA
+    const bool pre = p.grouped && M >= kPreMinM && ws_bytes >= base + pre_bytes((size_t)N, (size_t)K);
+    CUtensorMap tah = tw, tal = tw;
+    if (pre) {
+        __half *ahi = reinterpret_cast<__half *>(wsb + base);
+        __half *alo = reinterpret_cast<__half *>(wsb + base + align256((size_t)N * K * 2));
+        float *rinv = reinterpret_cast<float *>(wsb + base + 2 * align256((size_t)N * K * 2));
+        p.rowinv = rinv;
+        if (!make_map_2d(&tah, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ahi, (uint64_t)K, (uint64_t)N, (uint64_t)K * 2, BK, BM,
+                         CU_TENSOR_MAP_SWIZZLE_128B) ||
+            !make_map_2d(&tal, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, alo, (uint64_t)K, (uint64_t)N, (uint64_t)K * 2, BK, BM,
+                         CU_TENSOR_MAP_SWIZZLE_128B))
+            return cudaErrorInvalidValue;
+        const unsigned cg = (unsigned)((N + 7) / 8);
+        if (w.qtype == kQInt4)
+            pre_convert_grouped_kernel<true><<<cg, 256, 0, st>>>(w.data, w.scales, N, K, p.group_k, ahi, alo, rinv);
+        else
+            pre_convert_grouped_kernel<false><<<cg, 256, 0, st>>>(w.data, w.scales, N, K, p.group_k, ahi, alo, rinv);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
     using LG = Smem<kTilesGrouped, kStagesGrouped, true>;
     using LR = Smem<kStagesRow, kStagesRow, false>;
     static std::atomic<uint64_t> attr_done{0};
     const cudaError_t attr = once_per_device(attr_done, [] {
-        cudaError_t a = cudaFuncSetAttribute(gemm_tc_kernel<kTilesGrouped, kStagesGrouped, true>,
+        cudaError_t a = cudaFuncSetAttribute(gemm_tc_kernel<kTilesGrouped, kStagesGrouped, true, false>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, LG::bytes);
         if (a == cudaSuccess)
-            a = cudaFuncSetAttribute(gemm_tc_kernel<kStagesRow, kStagesRow, false>,
+            a = cudaFuncSetAttribute(gemm_tc_kernel<kStagesGrouped, kStagesGrouped, true, true>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, LG::bytes);
+        if (a == cudaSuccess)
+            a = cudaFuncSetAttribute(gemm_tc_kernel<kStagesRow, kStagesRow, false, false>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, LR::bytes);
         return a;
     });
     if (attr != cudaSuccess) return attr;
     dim3 grid((unsigned)((N + BM - 1) / BM), (unsigned)((M + BN - 1) / BN), (unsigned)ks);
-    if (p.grouped)
-        gemm_tc_kernel<kTilesGrouped, kStagesGrouped, true><<<grid, kThreads, LG::bytes, st>>>(tw, th, tl, p);
+    if (pre)
+        gemm_tc_kernel<kStagesGrouped, kStagesGrouped, true, true><<<grid, kThreads, LG::bytes, st>>>(tw, th, tl, tah,
+                                                                                                     tal, p);
+    else if (p.grouped)
+        gemm_tc_kernel<kTilesGrouped, kStagesGrouped, true, false><<<grid, kThreads, LG::bytes, st>>>(tw, th, tl, tah,
+                                                                                                      tal, p);
     else
-        gemm_tc_kernel<kStagesRow, kStagesRow, false><<<grid, kThreads, LR::bytes, st>>>(tw, th, tl, p);
+        gemm_tc_kernel<kStagesRow, kStagesRow, false, false><<<grid, kThreads, LR::bytes, st>>>(tw, th, tl, tah, tal, p);
     e = cudaGetLastError();
     if (e != cudaSuccess || ks == 1) return e;
     const size_t MN = M * (size_t)N;
