@@ -90,7 +90,7 @@ def main():
     _native.check(_native.lib().pyxis_cuda_head_greedy_dev(comm.handle, wsh.handle, small_v, lo, hi - lo, small_v,
                                                            C.c_void_p(X.data_ptr()), 3, small_v,
                                                            C.c_void_p(tok.data_ptr()),
-                                                           C.c_void_p(torch.cuda.current_stream().cuda_stream)))
+                                                           C.c_void_p(px._stream_handle(None, local))))
     got = list(tok.cpu().numpy())
     want = [oracle.argmax(vals[m]) for m in range(3)]
     if got != want:
