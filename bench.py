@@ -277,10 +277,11 @@ PREFILL_M = 512
 
 def run_vocab_parallel_head(comm, ws, rank, local, steps, lm_full):
     """Greedy next token through the int8 lm_head split by vocabulary rows over the ranks: each
-    rank's GEMV over V/ws rows, device argmax keys, one NCCL all-gather of 8 bytes per row and
-    rank, the pick on the device (pyxis_cuda_head_greedy_dev).  Device time per token (CUDA
-    events around back-to-back calls, max over ranks), at batch 1 and 8; every rank's tokens are
-    checked against the single-GPU matmul + argmax of the full head on the same rank."""
+    rank's GEMV over V/ws rows, device argmax keys, the keys exchanged (8 bytes per row and rank,
+    over peer memory, or an NCCL all-gather where the GPUs cannot map each other), the pick on the
+    device (pyxis_cuda_head_greedy_dev).  Device time per token (CUDA events around replays of a
+    CUDA graph of 20 calls, as the decode step runs it; max over ranks), at batch 1 and 8; every
+    rank's tokens are checked against the single-GPU matmul + argmax of the full head."""
     import torch
 
     import pyxis_b200 as px
@@ -300,23 +301,37 @@ def run_vocab_parallel_head(comm, ws, rank, local, steps, lm_full):
         want = px.argmax_dev(px.matmul_dev(h, lm_full, V, H))[0]
         same = bool(torch.equal(tok, want))
         parity = parity and same
-        for _ in range(3):
-            head.greedy(h, tokens=tok)
+        reps = 20
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                head.greedy(h, tokens=tok, stream=s)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s, capture_error_mode="thread_local"):
+            for _ in range(reps):
+                head.greedy(h, tokens=tok, stream=s)
+        torch.cuda.synchronize()
+        g.replay()
         torch.cuda.synchronize()
         barrier(ws)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(steps):
-            head.greedy(h, tokens=tok)
+            g.replay()
         e1.record()
         torch.cuda.synchronize()
-        us = max_over_ranks(e0.elapsed_time(e1) * 1e3 / steps, ws)
+        us = max_over_ranks(e0.elapsed_time(e1) * 1e3 / (steps * reps), ws)
+        del g
+        same = same and bool(torch.equal(tok, want))  # after the replays too
+        parity = parity and same
         shard_bytes = gemv_bytes("int8", head.mm.hi - head.mm.lo, H, H, B)
         out["batches"].append({"B": B, "us_per_token": us, "tokens_match_single_gpu": same,
                                "shard_gbs": shard_bytes / us / 1e3, "shard_frac_of_peak": shard_bytes / us / 1e3 / peak,
                                "first_tokens": [int(t) for t in tok[:4].cpu()]})
     out["parity"] = bool(max_over_ranks(0.0 if parity else 1.0, ws) == 0.0)
-    out["note"] = ("device time per call: shard GEMV + argmax keys + NCCL all-gather + device pick; "
+    out["note"] = ("device time per call: shard GEMV + argmax keys + key exchange + device pick; "
                    "shard_frac_of_peak = the shard's algorithmic bytes / time / one GPU's HBM peak")
     return out
 

@@ -3,9 +3,17 @@
 // The lm_head of src/output_head.rs:21-44 split by vocabulary rows: every rank multiplies the
 // same hidden rows with its shard of the head (pyxis_cuda_matmul_dev's kernels), reduces each
 // row's logits to one 64-bit key (argmax.cu: order-preserving value bits, then the inverted
-// global index, so the largest key is the first maximum), the ranks all-gather the keys (8 bytes
-// per row and rank over NVLink), and a small kernel takes the largest key of each row.  Nothing
-// goes through the host; the whole sequence can be captured in a CUDA graph.
+// global index, so the largest key is the first maximum), the ranks exchange the keys (8 bytes
+// per row and rank over NVLink), and each takes the largest key of each row.  Nothing goes through
+// the host; the whole sequence can be captured in a CUDA graph.
+//
+// The exchange is one small kernel over peer memory when the ranks' GPUs can map each other's
+// memory (CUDA IPC, one process per GPU): every rank stores its keys straight into each peer's
+// receive buffer, publishes an epoch flag there with a system-scope release, waits (bounded) for
+// every peer's flag in its own buffer and picks the tokens -- no collective launch, which on these
+// 8-bytes-per-row messages cost more than the stores.  Keys go to one of two buffers by epoch
+// parity: a rank cannot begin call e + 2 before every peer has published call e + 1, i.e. finished
+// reading call e.  Otherwise (IPC unavailable) an NCCL all-gather and a pick kernel do the same.
 //
 // NCCL is loaded with dlopen on first use: libnccl.so.2 resolves to the copy a process already
 // has (PyTorch's, for instance), else the system one.
@@ -20,6 +28,7 @@
 #include "comm.h"
 #include "common.cuh"
 #include "kernels.h"
+#include "tc_ptx.cuh"
 
 namespace pyxis {
 namespace {
@@ -76,6 +85,148 @@ struct DevGuard {
     }
 };
 
+constexpr int kXMaxRows = kArgmaxMaxRows;   // rows per exchange
+constexpr int kXMaxRanks = 8;
+constexpr uint64_t kXTimeoutNs = 2000000000ull;
+constexpr int kErrExchange = 0x701;
+// Layout of a rank's receive buffer: keys [2][kXMaxRanks][kXMaxRows] u64, flags [kXMaxRanks] u32
+// (the epoch each rank last published here), this rank's own epoch counter (u32).
+constexpr size_t kXKeyBytes = 2ull * kXMaxRanks * kXMaxRows * sizeof(uint64_t);
+constexpr size_t kXBytes = kXKeyBytes + 64 + 64;
+
+PYXIS_DEVINL void st_release_sys(unsigned *p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+PYXIS_DEVINL unsigned ld_acquire_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// One CTA: mine [M] keys -> every rank's buffer (slot of this call's epoch parity, row block of
+// this rank), flags, a bounded wait for all ranks' flags here, then tokens[r] for rows
+// [row0, row0 + nrows).  A wait that runs out records kErrExchange and leaves the tokens unwritten.
+__global__ void __launch_bounds__(256)
+    exchange_pick_kernel(const uint64_t *__restrict__ mine, int M, int rank, int nranks, void *const *xtable,
+                         int row0, int nrows, int32_t *__restrict__ tokens, int *err) {
+    __shared__ unsigned s_epoch;
+    __shared__ int s_ok;
+    pdl_wait();
+    pdl_trigger();
+    uint8_t *local = static_cast<uint8_t *>(xtable[rank]);
+    unsigned *epoch_ctr = reinterpret_cast<unsigned *>(local + kXKeyBytes + 64);
+    if (threadIdx.x == 0) {
+        s_epoch = *epoch_ctr + 1;  // every rank makes the same calls: the epochs agree
+        *epoch_ctr = s_epoch;
+        s_ok = 1;
+    }
+    __syncthreads();
+    const unsigned e = s_epoch;
+    const int slot = e & 1;
+    for (int p = 0; p < nranks; ++p) {
+        uint64_t *dst = reinterpret_cast<uint64_t *>(static_cast<uint8_t *>(xtable[p])) +
+                        ((size_t)slot * kXMaxRanks + rank) * kXMaxRows;
+        for (int r = threadIdx.x; r < M; r += blockDim.x) dst[r] = mine[r];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();  // the keys above before the flags, for every peer
+        for (int p = 0; p < nranks; ++p)
+            st_release_sys(reinterpret_cast<unsigned *>(static_cast<uint8_t *>(xtable[p]) + kXKeyBytes) + rank, e);
+        const unsigned *flags = reinterpret_cast<const unsigned *>(local + kXKeyBytes);
+        const uint64_t t0 = tc::globaltimer_ns();
+        for (int q = 0; q < nranks && s_ok; ++q) {
+            while ((int)(ld_acquire_sys(flags + q) - e) < 0) {
+                if (tc::globaltimer_ns() - t0 > kXTimeoutNs) {
+                    atomicCAS(err, 0, kErrExchange);
+                    s_ok = 0;
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    const uint64_t *keys = reinterpret_cast<const uint64_t *>(local) + (size_t)slot * kXMaxRanks * kXMaxRows;
+    for (int r = threadIdx.x; r < nrows; r += blockDim.x) {
+        uint64_t m = 0;
+        for (int q = 0; q < nranks; ++q) {
+            const uint64_t k = __ldcv(keys + (size_t)q * kXMaxRows + row0 + r);
+            m = k > m ? k : m;
+        }
+        tokens[r] = m == 0 ? 0 : (int32_t)(0xFFFFFFFFu - (uint32_t)(m & 0xFFFFFFFFu));
+    }
+}
+
+// Maps every rank's receive buffer into every other rank (collective: all ranks call it in
+// comm_init, and every rank makes the same NCCL calls whatever its own verdict, so none is left
+// waiting).  Leaves c->p2p false, and frees what it made, unless every rank can map every other.
+void setup_p2p(pyxis_cuda_comm *c) {
+    if (c->nranks < 2 || c->nranks > kXMaxRanks) return;
+    const NcclApi &api = nccl();
+    cudaStream_t st = c->ctx->stream;
+    const size_t R = (size_t)c->nranks;
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    uint8_t *scratch = nullptr;  // [R] verdicts (int), then [R] IPC handles of 64 bytes
+    if (cudaMalloc(&scratch, 16 * R + 64 * R) != cudaSuccess) {
+        cudaGetLastError();
+        return;
+    }
+    int *dv = reinterpret_cast<int *>(scratch);
+    uint8_t *hbuf = scratch + 16 * R;
+    cudaIpcMemHandle_t mine{};
+    int ok = cudaMalloc(&c->xbuf, kXBytes) == cudaSuccess && cudaMemset(c->xbuf, 0, kXBytes) == cudaSuccess &&
+             cudaIpcGetMemHandle(&mine, c->xbuf) == cudaSuccess;
+    cudaGetLastError();
+    auto exchange_verdict = [&](int mine_ok) -> bool {
+        int v = mine_ok, all[kXMaxRanks] = {0};
+        bool good = cudaMemcpy(dv + c->rank, &v, sizeof(int), cudaMemcpyHostToDevice) == cudaSuccess;
+        good = api.all_gather(dv + c->rank, dv, 1, ncclInt32, c->nccl, st) == ncclSuccess && good;
+        good = cudaStreamSynchronize(st) == cudaSuccess && good;
+        good = good && cudaMemcpy(all, dv, sizeof(int) * R, cudaMemcpyDeviceToHost) == cudaSuccess;
+        for (size_t q = 0; q < R; ++q) good = good && all[q] != 0;
+        return good;
+    };
+    cudaMemcpy(hbuf + 64 * (size_t)c->rank, &mine, 64, cudaMemcpyHostToDevice);
+    const bool sent = api.all_gather(hbuf + 64 * (size_t)c->rank, hbuf, 64, ncclUint8, c->nccl, st) == ncclSuccess;
+    ok = exchange_verdict(ok && sent);
+    void *bases[kXMaxRanks] = {nullptr};
+    if (ok) {
+        cudaIpcMemHandle_t h[kXMaxRanks];
+        ok = cudaMemcpy(h, hbuf, 64 * R, cudaMemcpyDeviceToHost) == cudaSuccess;
+        for (int q = 0; q < c->nranks && ok; ++q) {
+            if (q == c->rank) {
+                bases[q] = c->xbuf;
+                continue;
+            }
+            ok = cudaIpcOpenMemHandle(&c->peer_base[q], h[q], cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+            bases[q] = c->peer_base[q];
+        }
+        ok = ok && cudaMalloc(&c->xtable, sizeof(void *) * R) == cudaSuccess &&
+             cudaMemcpy(c->xtable, bases, sizeof(void *) * R, cudaMemcpyHostToDevice) == cudaSuccess;
+        cudaGetLastError();
+    }
+    // the ranks must agree on the path
+    ok = exchange_verdict(ok);
+    cudaFree(scratch);
+    cudaGetLastError();
+    if (ok) {
+        c->p2p = true;
+        return;
+    }
+    for (int q = 0; q < kXMaxRanks; ++q)
+        if (c->peer_base[q]) {
+            cudaIpcCloseMemHandle(c->peer_base[q]);
+            c->peer_base[q] = nullptr;
+        }
+    cudaFree(c->xtable);
+    cudaFree(c->xbuf);
+    c->xtable = nullptr;
+    c->xbuf = nullptr;
+    cudaGetLastError();
+}
+
 }  // namespace
 
 int comm_allgather(pyxis_cuda_comm *c, const void *send, void *recv, size_t count, bool u64, cudaStream_t st) {
@@ -123,6 +274,12 @@ int head_greedy_enqueue(pyxis_cuda_comm *c, const pyxis_cuda_weights *shard, siz
     cudaError_t e = launch_argmax_keys(c->logits, M, shard_rows, shard_rows, (int64_t)vocab_lo, mine, ctx->amax,
                                        ctx->num_sms, st);
     if (e != cudaSuccess) return fail(PYXIS_ECUDA, cudaGetErrorString(e));
+    if (c->p2p && M <= (size_t)kXMaxRows) {
+        e = launch_kernel(exchange_pick_kernel, dim3(1), dim3(256), 0, st, (const uint64_t *)mine, (int)M, c->rank,
+                          c->nranks, (void *const *)c->xtable, row0, nrows, tokens, ctx->d_err);
+        if (e != cudaSuccess) return fail(PYXIS_ECUDA, cudaGetErrorString(e));
+        return PYXIS_OK;
+    }
     rc = comm_allgather(c, mine, all, M, true, st);
     if (rc) return rc;
     e = launch_pick_keys(all, c->nranks, (int)M, row0, nrows, tokens, st);
@@ -168,6 +325,7 @@ int pyxis_cuda_comm_init(pyxis_cuda_ctx *ctx, const uint8_t id[PYXIS_COMM_ID_BYT
         delete c;
         return nccl_fail(api, r, "ncclCommInitRank");
     }
+    setup_p2p(c);
     *out = c;
     return PYXIS_OK;
 }
@@ -183,6 +341,10 @@ int pyxis_cuda_comm_free(pyxis_cuda_comm *c) {
     if (!c) return PYXIS_OK;
     DevGuard g(c->ctx->device);
     cudaStreamSynchronize(c->ctx->stream);
+    for (int q = 0; q < 8; ++q)
+        if (c->peer_base[q]) cudaIpcCloseMemHandle(c->peer_base[q]);
+    cudaFree(c->xtable);
+    cudaFree(c->xbuf);
     if (c->nccl) nccl().comm_destroy(c->nccl);
     cudaFree(c->logits);
     cudaFree(c->keys);

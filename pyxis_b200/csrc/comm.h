@@ -20,6 +20,12 @@ struct pyxis_cuda_comm {
     size_t logits_cap = 0;
     uint64_t *keys = nullptr;
     size_t keys_cap = 0;
+    // peer-memory exchange of the head's keys (comm.cu): this rank's receive buffer (mapped into
+    // every peer by CUDA IPC), the peers' mappings, and a device table of the nranks buffers
+    bool p2p = false;
+    void *xbuf = nullptr;                 // local: keys [2 epochs][nranks][kXMaxRows], flags, epoch
+    void *peer_base[8] = {nullptr};       // IPC mappings of the peers' xbuf (nullptr for self)
+    void **xtable = nullptr;              // device [nranks] pointers to every rank's xbuf
 };
 
 namespace pyxis {
