@@ -175,15 +175,23 @@ __global__ void qk_rope_rows_kernel(const float *__restrict__ qkv, const float *
     }
 }
 
-// act[r] = SiLU(gu[r][0:ffn]) * gu[r][ffn:2 ffn] (src/ffn.rs:39-41,52-54); grid (ceil(ffn/256), rows).
+// act[r] = SiLU(gu[r][0:ffn]) * gu[r][ffn:2 ffn] (src/ffn.rs:39-41,52-54); grid (ceil(ffn/1024), rows):
+// four consecutive elements per thread (16-byte loads and store) when ffn % 4 == 0.
 __global__ void silu_rows_kernel(const float *__restrict__ gu, int ffn, float *__restrict__ act) {
     pdl_wait();
     pdl_trigger();
-    const int r = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
+    const int r = blockIdx.y, i = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
     if (i >= ffn) return;
     const float *row = gu + (size_t)r * 2 * ffn;
-    const float g = row[i];
-    act[(size_t)r * ffn + i] = __fmul_rn(silu_f(g), row[ffn + i]);
+    float *out = act + (size_t)r * ffn;
+    if ((ffn & 3) == 0) {
+        const float4 g = __ldg(reinterpret_cast<const float4 *>(row + i));
+        const float4 u = __ldg(reinterpret_cast<const float4 *>(row + ffn + i));
+        *reinterpret_cast<float4 *>(out + i) = make_float4(__fmul_rn(silu_f(g.x), u.x), __fmul_rn(silu_f(g.y), u.y),
+                                                           __fmul_rn(silu_f(g.z), u.z), __fmul_rn(silu_f(g.w), u.w));
+    } else {
+        for (int j = i; j < i + 4 && j < ffn; ++j) out[j] = __fmul_rn(silu_f(row[j]), row[ffn + j]);
+    }
 }
 
 // out[b][step] = tokens[b] for every sequence, then step += 1 and pos += 1 (one CTA).
@@ -444,7 +452,7 @@ int enqueue_prefill(pyxis_cuda_model *m, int n_seq, int P, cudaStream_t st) {
                                  (const float *)b->ptmp, (const float *)L.post_norm, b->ph, H, c.rms_eps, 1, 0));
             rc = run_matmul(ctx, L.wgu, b->ph, M, H, 2 * (size_t)ffn, H, b->pgu, 2 * (size_t)ffn, b->ws, b->ws_bytes, st);
             if (rc) return rc;
-            PX_TRY(launch_kernel(silu_rows_kernel, dim3((ffn + 255) / 256, M), dim3(256), 0, st, (const float *)b->pgu,
+            PX_TRY(launch_kernel(silu_rows_kernel, dim3((ffn + 1023) / 1024, M), dim3(256), 0, st, (const float *)b->pgu,
                                  ffn, b->pact));
             rc = run_matmul(ctx, L.wdown, b->pact, M, ffn, H, ffn, b->ptmp, H, b->ws, b->ws_bytes, st);
             if (rc) return rc;
@@ -489,7 +497,7 @@ int enqueue_step(pyxis_cuda_model *m, int n_seq, cudaStream_t st) {
                              (const float *)b->dtmp, (const float *)L.post_norm, b->dh, H, c.rms_eps, 1, 0));
         rc = run_matmul(ctx, L.wgu, b->dh, n_seq, H, 2 * (size_t)ffn, H, b->dgu, 2 * (size_t)ffn, b->ws, b->ws_bytes, st);
         if (rc) return rc;
-        PX_TRY(launch_kernel(silu_rows_kernel, dim3((ffn + 255) / 256, n_seq), dim3(256), 0, st, (const float *)b->dgu,
+        PX_TRY(launch_kernel(silu_rows_kernel, dim3((ffn + 1023) / 1024, n_seq), dim3(256), 0, st, (const float *)b->dgu,
                              ffn, b->dact));
         rc = run_matmul(ctx, L.wdown, b->dact, n_seq, ffn, H, ffn, b->dtmp, H, b->ws, b->ws_bytes, st);
         if (rc) return rc;
