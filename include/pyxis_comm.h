@@ -5,9 +5,11 @@
  * The reference runs on one device; its lm_head (src/output_head.rs:21-44: logits = matmul of
  * the final hidden state with the [vocab, hidden] head, then argmax) is the path's only step
  * whose work splits across GPUs with an exchange.  Split by vocabulary rows, each rank computes
- * the logits of its rows and their argmax; one all-gather of a 64-bit key per (row, rank) and a
+ * the logits of its rows and their argmax; an exchange of a 64-bit key per (row, rank) and a
  * device-side maximum give every rank the token the single-device argmax picks (the first
- * maximum under strict >, a NaN at index 0 winning as it does in the reference's scan).
+ * maximum under strict >, a NaN at index 0 winning as it does in the reference's scan).  The
+ * exchange is one kernel over peer memory when the ranks' GPUs can map each other's memory
+ * (CUDA IPC, set up by pyxis_cuda_comm_init), else an NCCL all-gather.
  *
  * Row-sharded matmuls and data-parallel sequences need no library support: a rank quantises its
  * own row block with pyxis_cuda_quantize (the block's bytes and scales are exactly that slice of
