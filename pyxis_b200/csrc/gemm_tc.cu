@@ -43,6 +43,7 @@
 
 #include "kernels.h"
 #include "split_x.cuh"
+#include "fp16_codes.cuh"
 #include "tc_ptx.cuh"
 #include "tmap.cuh"
 
@@ -106,24 +107,8 @@ struct TcParams {
     const float *rowinv;    // pre-converted weights (PRE): [N] 2^-e per row
 };
 
-PYXIS_DEVINL uint32_t h2_bits(__half2 v) { return *reinterpret_cast<uint32_t *>(&v); }
-PYXIS_DEVINL __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
 
-// int8 codes (signed bytes) -> exact fp16 pairs: byte b -> fp16(1024 + (b ^ 0x80)) - 1152.
-PYXIS_DEVINL void i8x4_to_h(uint32_t w, uint32_t &h01, uint32_t &h23) {
-    const uint32_t u = w ^ 0x80808080u;
-    const __half2 bias = bits_h2(0x64806480u);  // (1152, 1152)
-    h01 = h2_bits(__hsub2(bits_h2(__byte_perm(u, 0x64646464u, 0x5140u)), bias));
-    h23 = h2_bits(__hsub2(bits_h2(__byte_perm(u, 0x64646464u, 0x5342u)), bias));
-}
 
-// int4 codes (q + 8 in nibbles, element 2j low / 2j+1 high nibble of byte j) -> exact fp16 pairs
-// in the order (e0,e4) (e1,e5) (e2,e6) (e3,e7); split_x applies the same order to X.
-PYXIS_DEVINL void u4x8_to_h(uint32_t w, uint32_t (&h)[4]) {
-    const __half2 bias = bits_h2(0x64086408u);  // (1032, 1032)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) h[i] = h2_bits(__hsub2(bits_h2(((w >> (4 * i)) & 0x000F000Fu) | 0x64006400u), bias));
-}
 
 // A pair of codes q (exact floats) times the scale s (f32, rounded once) as fp16 hi + lo pairs:
 // 22 significant bits.  hi is w rounded to 11 bits by Veltkamp's split (c = w (2^13 + 1),

@@ -38,6 +38,7 @@
 
 #include "kernels.h"
 #include "split_x.cuh"
+#include "fp16_codes.cuh"
 #include "tc_ptx.cuh"
 #include "tmap.cuh"
 
@@ -74,26 +75,8 @@ struct WsParams {
     int *err;
 };
 
-PYXIS_DEVINL uint32_t h2_bits(__half2 v) { return *reinterpret_cast<uint32_t *>(&v); }
-PYXIS_DEVINL __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
 
-// Eight int4 codes (q + 8 in nibbles; element 2j low, 2j+1 high nibble of byte j) -> exact fp16
-// pairs (e0,e4) (e1,e5) (e2,e6) (e3,e7): nibbles i and i+4 of the word land in the two halves of
-// (w >> 4i) & 0x000F000F; OR-ing in 1024's exponent makes them 1024 + (q + 8), then - 1032.  x is
-// split in the same element order (split_x_rows_kernel<true>).
-PYXIS_DEVINL void u4x8_to_h(uint32_t w, uint32_t (&h)[4]) {
-    const __half2 bias = bits_h2(0x64086408u);  // (1032, 1032)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) h[i] = h2_bits(__hsub2(bits_h2(((w >> (4 * i)) & 0x000F000Fu) | 0x64006400u), bias));
-}
 
-// Four int8 codes -> exact fp16 pairs (e0,e1) (e2,e3): byte b -> fp16(1024 + (b ^ 0x80)) - 1152.
-PYXIS_DEVINL void i8x4_to_h(uint32_t w, uint32_t &h01, uint32_t &h23) {
-    const uint32_t u = w ^ 0x80808080u;
-    const __half2 bias = bits_h2(0x64806480u);  // (1152, 1152)
-    h01 = h2_bits(__hsub2(bits_h2(__byte_perm(u, 0x64646464u, 0x5140u)), bias));
-    h23 = h2_bits(__hsub2(bits_h2(__byte_perm(u, 0x64646464u, 0x5342u)), bias));
-}
 
 // Byte offset of 16-byte chunk c of row r in a 128-byte-swizzled K-major block (8-row 1024 B atoms).
 PYXIS_DEVINL uint32_t sw128_off(int r, int c) { return (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4); }

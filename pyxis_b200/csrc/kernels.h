@@ -39,6 +39,13 @@ bool gemv_batch_supported(const QMatrix &w, size_t B, int num_sms);
 cudaError_t launch_gemv_batch(const QMatrix &w, const float *X, size_t B, size_t ldx, float *Y, size_t ldy,
                               int *err, int num_sms, cudaStream_t st);
 
+// 1-8 input rows with the codes fed from registers to mma.sync m16n8k16 (gemv_mma.cu): int4 / int8
+// with a scale per group of 32 or per row, K % 256 (int4) or K % 128 (int8) == 0, X 16-byte
+// aligned, ldx % 4 == 0.
+bool gemv_mma_supported(const QMatrix &w, size_t B, int num_sms);
+cudaError_t launch_gemv_mma(const QMatrix &w, const float *X, size_t B, size_t ldx, float *Y, size_t ldy, int *err,
+                            int num_sms, cudaStream_t st);
+
 // Batch-1 products whose x is computed inside the GEMV from the previous step's outputs:
 // kProAddNorm: x' = x + delta (delta may be NULL; CTA 0 stores x' to xout, which must not alias
 // x), then RMSNorm with weight w; kProSiluMul: SiLU(x[0:K]) * x[K:2K].  All pointers 16-byte

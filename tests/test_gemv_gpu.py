@@ -144,9 +144,12 @@ def test_int8_row_scale_tensor_core_gemv(N, K, B):
     """int8 with one scale per row at batch 1-8.  From 16384 output rows (the lm_head and its
     vocab shards on up to 8 GPUs) it runs
     tcgen05 kind::i8 with x as int8 digits and stream-K (tiles shared by two CTAs added with exact
-    int32 atomics); below that the CUDA-core batch kernel, which finishes first at those sizes."""
+    int32 atomics); below that the mma.sync GEMV from 8 MB of codes (4 MB at 4-8 rows) and the
+    CUDA-core batch kernel under it, whichever finishes first at the size."""
     w, od, os_ = make("int8", N, K, K, seed=N + K + B)
-    assert px.matmul_kernel_name(w, B, N, K) == ("gemv_tc_i8_kernel" if N >= 16384 else "gemv_batch_kernel")
+    mma = N * K >= (8 << 20) or (N * K >= (4 << 20) and B >= 4)
+    assert px.matmul_kernel_name(w, B, N, K) == (
+        "gemv_tc_i8_kernel" if N >= 16384 else "gemv_mma_kernel" if mma else "gemv_batch_kernel")
     X = px.synth_normal_f32(B * 31 + 7, B * K, 1.0).reshape(B, K)
     X[0, :5] = [0.0, -0.0, 1e-30, -3e4, 2.5]
     for rep in range(2):  # the split-K scratch must be left clean for the next launch
@@ -169,8 +172,9 @@ def test_int8_row_scale_tensor_core_gemv(N, K, B):
     ("int4", 300, 4096, 4096, 8),  # int4 with one scale per row
 ])
 def test_batch_kernel(qt, N, K, bs, B):
-    """The CUDA-core batch kernel (x staged by TMA, split-K over warps, fixed-order combine): every
-    batch-1 product, and the batches of 2-8 rows the weight-streaming matmul does not take."""
+    """The CUDA-core batch kernel (x staged by TMA, split-K over warps, fixed-order combine): the
+    products of 1-8 rows that the mma.sync GEMV does not take (matrices under 4 MB, K not a
+    multiple of its weight boxes, scale blocks other than 32 or the whole row)."""
     w, od, os_ = make(qt, N, K, bs, seed=N + 3 * K + bs + B)
     assert px.matmul_kernel_name(w, B, N, K) == "gemv_batch_kernel"
     X = px.synth_normal_f32(B * 13 + 1, B * K, 1.0).reshape(B, K)
@@ -180,6 +184,34 @@ def test_batch_kernel(qt, N, K, bs, B):
     check_matmul(Y1, ref, exact_matmul(qt, od, os_, bs, N, K, X))
     Y2 = px.matmul_batch(X, w, N, K)
     assert np.array_equal(Y1, Y2)  # the combine order is fixed: bit-identical reruns
+    px._native.check(px._native.lib().pyxis_cuda_check_device_error(w.ctx.handle))
+
+
+@pytest.mark.parametrize("qt,N,K,bs,B", [
+    ("int4", 6144, 2048, 32, 4), ("int4", 6144, 2048, 32, 5), ("int4", 6144, 2048, 32, 8),
+    ("int4", 4100, 2048, 32, 8),    # last row tile partly outside the matrix
+    ("int4", 2048, 6144, 32, 8),    # down_proj: 8 K parts of 3 boxes
+    ("int4", 700, 12288, 32, 7),    # 8 parts of 6 boxes (the most shared memory)
+    ("int4", 32768, 256, 32, 4),    # one box: a single K part, no cluster
+    ("int4", 2100, 4096, 4096, 8),  # int4 with one scale per row
+    ("int8", 6144, 2048, 2048, 1),  # int8 per row at batch 1
+    ("int8", 4100, 2048, 2048, 3),  # int8 per row, partial tile
+    ("int8", 4100, 2048, 32, 6),    # GGUF Q8_0 layout
+    ("int4", 40000, 2048, 32, 8),   # many row tiles
+])
+def test_mma_kernel(qt, N, K, bs, B):
+    """The mma.sync GEMV (codes from registers into m16n8k16 with x as fp16 hi / lo, K parts added
+    in rank order through the cluster's shared memory) against the oracle and the exact sum, with
+    zeros, a tiny and an outlying x; reruns are bit-identical."""
+    w, od, os_ = make(qt, N, K, bs, seed=N + 5 * K + bs + B)
+    assert px.matmul_kernel_name(w, B, N, K) == "gemv_mma_kernel"
+    X = px.synth_normal_f32(B * 17 + 3, B * K, 1.0).reshape(B, K)
+    X[0, :4] = [0.0, -0.0, 1e-30, -3e4]
+    ref = ref_matmul(qt, od, os_, bs, X, N, K)
+    Y1 = px.matmul_batch(X, w, N, K)
+    check_matmul(Y1, ref, exact_matmul(qt, od, os_, bs, N, K, X))
+    Y2 = px.matmul_batch(X, w, N, K)
+    assert np.array_equal(Y1, Y2)
     px._native.check(px._native.lib().pyxis_cuda_check_device_error(w.ctx.handle))
 
 
