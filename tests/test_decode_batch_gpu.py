@@ -55,6 +55,25 @@ def test_qwen3_shape_batch_matches_single_sequence_decoder():
     dec.close()
 
 
+def test_qwen3_shape_batch_of_6_on_the_mma_gemv():
+    """Six sequences: the decode steps' 6-row products of the large int4 matrices (qkv, gate|up,
+    down, lm_head) take the mma.sync GEMV, the o projection the CUDA-core batch kernel; every
+    sequence's greedy tokens equal the single-sequence decoder's (batch-1 GEMVs)."""
+    import pyxis_b200 as px
+    m = SyntheticModel(QWEN3_1_7B, seed=0x5EE6)
+    dec = Decoder(m, qtype="int4", max_seq=48)
+    H, F, V = QWEN3_1_7B.hidden, QWEN3_1_7B.ffn, QWEN3_1_7B.vocab
+    probe = px.Weights.quantize_int4(px.synth_normal_bf16(1, 2 * F * H, 0.02), 32)  # the gate|up shape
+    assert px.matmul_kernel_name(probe, 6, 2 * F, H) == "gemv_mma_kernel"
+    del probe
+    prompts = synth_tokens(0xB6, 6 * 24, V).reshape(6, 24)
+    toks, _ = dec.generate_batch(prompts, 5)
+    for s in range(6):
+        one, _ = dec.generate(prompts[s], 5)
+        assert np.array_equal(toks[s], one), (s, toks[s], one)
+    dec.close()
+
+
 # GQA 16 / 8 x 128 like Qwen3-1.7B, narrow elsewhere so that the oracle's prefill of 2048
 # positions takes seconds
 GQA_2048 = ModelConfig(hidden=256, n_layers=1, n_q_heads=16, n_kv_heads=8, head_dim=128, ffn=512, vocab=2048,
