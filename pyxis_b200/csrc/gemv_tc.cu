@@ -17,11 +17,11 @@
 // CTA (persistent, one per SM): warp 0 = TMA producer into an S-stage ring (16 KB stages),
 // warp 1 = TMEM owner + MMA issuer (M=128, N=16|32, K=32 per instruction, 8 accumulators per
 // tile segment so that consecutive stages do not wait on each other, double-buffered in TMEM
-// across segments), warps 2-5 = epilogue (tcgen05.ld, one TMEM lane = one weight row).
-// x itself arrives by one bulk copy into the last ring stages, issued before the first weight
-// copy (or, under programmatic dependent launch, right after the predecessor finishes), so it
-// does not queue behind the weight stream; warps 1-5 turn it into the digit operand and hand the
-// stages back to the producer.  A tile whose stages span several CTAs has its partial int32
+// across segments), warps 2-5 = epilogue (tcgen05.ld, one TMEM lane = one weight row), warps
+// 6-11 helpers.  x itself arrives by one bulk copy into the last ring stages, issued before the
+// first weight copy (or, under programmatic dependent launch, right after the predecessor
+// finishes), so it does not queue behind the weight stream; warps 1-11 turn it into the digit
+// operand and hand the stages back to the producer.  A tile whose stages span several CTAs has its partial int32
 // sums added exactly with atomics into a scratch slot, and the CTA that finishes the tile last
 // converts it and zeroes the scratch for the next launch.  The schedule is stream-K: every CTA
 // gets the same number of (tile, K-block) stages, and works on its (possibly shared) first and
@@ -41,7 +41,12 @@ namespace {
 constexpr int TM = 128;    // weight rows per tile
 constexpr int TKB = 128;   // K bytes (= int8 codes) per stage
 constexpr int kMaxTok = 8;
-constexpr int kThreads = 192;
+// warp 0 the TMA producer, warp 1 the MMA issuer, warps 2-5 the epilogue, 6-11 helpers: warps 1-11
+// build x's digit operand (with one warp per SM sub-partition the build's dependent chains ran
+// at ~1.2 us per pass; more warps hide their latency)
+constexpr int kEpiWarps = 4, kHelperWarps = 6;
+constexpr int kBuildWarps = 1 + kEpiWarps + kHelperWarps;
+constexpr int kThreads = 32 * (1 + kBuildWarps);
 constexpr uint32_t kStageBytes = TM * TKB;
 constexpr uint32_t kSmemTotal = 222 * 1024;
 constexpr int kMaxStages = 12;
@@ -145,8 +150,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *tfull = bars + 2 * kMaxStages, *tempty = tfull + 2, *drain = tempty + 2;
     uint64_t *xfull = drain + 1, *xfree = drain + 2;
     double *xscale = reinterpret_cast<double *>(drain + 3);          // [kMaxTok]
-    float *red = reinterpret_cast<float *>(xscale + kMaxTok);        // [kMaxTok][5]
-    int *xexp = reinterpret_cast<int *>(red + kMaxTok * 5);          // [kMaxTok]
+    float *red = reinterpret_cast<float *>(xscale + kMaxTok);        // [kMaxTok][kBuildWarps]
+    int *xexp = reinterpret_cast<int *>(red + kMaxTok * kBuildWarps);  // [kMaxTok]
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(xexp + kMaxTok);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
     volatile int *last_flag = abort_flag + 1;
@@ -246,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // -------------------------------------------------------------------- digit operand
-        const int bt = threadIdx.x - 32, nbt = kThreads - 32;  // warps 1-5
+        const int bt = threadIdx.x - 32, nbt = kThreads - 32;  // warps 1-11
         const int bwarp = warp - 1;
         pdl_trigger();  // x reaches shared memory through the producer, after its griddepcontrol.wait
         const Sched sc{p.total_stages, (int)gridDim.x, p.num_kb};
@@ -289,14 +294,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     float mb = m[b];
 #pragma unroll
                     for (int o = 16; o > 0; o >>= 1) mb = max_nan(mb, __shfl_xor_sync(0xffffffffu, mb, o));
-                    if (lane == 0) red[b * 5 + bwarp] = mb;
+                    if (lane == 0) red[b * kBuildWarps + bwarp] = mb;
                 }
             }
         }
         named_bar(1, nbt);
         if (bt < p.B) {
-            float m = red[bt * 5];
-            for (int w = 1; w < 5; ++w) m = max_nan(m, red[bt * 5 + w]);
+            float m = red[bt * kBuildWarps];
+            for (int w = 1; w < kBuildWarps; ++w) m = max_nan(m, red[bt * kBuildWarps + w]);
             int E = 0;
             if (m > 0.f && isfinite(m)) frexpf(m, &E);  // m < 2^E
             xexp[bt] = E;
@@ -405,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 volatile int no_abort = 0;
                 tc::mbar_wait_bounded(drain, 0, &no_abort, p.err, kErrDrain, kTimeoutNs);
             }
-        } else {
+        } else if (warp < 2 + kEpiWarps) {
             // ---------------------------------------------------------------- epilogue
             // All four warps run the same item sequence and the same named barriers; a warp
             // whose wait ran out skips the work but keeps the barrier sequence.
