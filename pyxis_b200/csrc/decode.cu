@@ -242,30 +242,56 @@ __global__ void __launch_bounds__(kAttnThreads)
 #pragma unroll
                 for (int g = 0; g < G; ++g)
                     if (g < G) dot[u][g] = __fadd_rn(dot[u][g], __shfl_xor_sync(0xffffffffu, dot[u][g], o));
+        // The round's PF x G scores, their exponentials and the G rescale factors are scalars that
+        // every lane needs: lane u G + g computes the division and the exponential of (key u,
+        // head g), lane PF G + g the factor of head g, and shuffles hand them to every lane (the
+        // same operations on the same values as a per-lane computation, a tenth of the issue).
+        constexpr int NP = PF * G;
+        float dsel = 0.f;
+#pragma unroll
+        for (int u = 0; u < PF; ++u)
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+                if (lane == u * G + g) dsel = dot[u][g];
+        const int pu = lane / G;
+        const float sc_l = lane < NP && jb + pu * NW < j1 ? __fdiv_rn(dsel, scale) : -INFINITY;
+        float sc[PF][G], mn[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float mt = -INFINITY;
+#pragma unroll
+            for (int u = 0; u < PF; ++u) {
+                sc[u][g] = __shfl_sync(0xffffffffu, sc_l, u * G + g);
+                mt = fmaxf(mt, sc[u][g]);
+            }
+            mn[g] = fmaxf(m[g], mt);  // finite: the round has >= 1 key
+        }
+        float ex_arg = 0.f;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+#pragma unroll
+            for (int u = 0; u < PF; ++u)
+                if (lane == u * G + g) ex_arg = __fsub_rn(sc[u][g], mn[g]);
+            if (lane == NP + g) ex_arg = __fsub_rn(m[g], mn[g]);  // -inf on the first round: c = 0
+        }
+        const float ex_l = expf(ex_arg);
 #pragma unroll
         for (int g = 0; g < G; ++g) {
             if (g >= G) break;
-            float sc[PF], mt = -INFINITY;
-#pragma unroll
-            for (int u = 0; u < PF; ++u) {
-                sc[u] = jb + u * NW < j1 ? __fdiv_rn(dot[u][g], scale) : -INFINITY;
-                mt = fmaxf(mt, sc[u]);
-            }
-            const float mn = fmaxf(m[g], mt);           // finite: the round has >= 1 key
-            const float c = expf(__fsub_rn(m[g], mn));  // 0 on the first round (m = -inf)
+            const float c = __shfl_sync(0xffffffffu, ex_l, NP + g);
             float ps = 0.f;
 #pragma unroll
             for (int t = 0; t < EPL; ++t) acc[g][t] = __fmul_rn(acc[g][t], c);
 #pragma unroll
             for (int u = 0; u < PF; ++u) {
+                const float pj = __shfl_sync(0xffffffffu, ex_l, u * G + g);
                 if (jb + u * NW >= j1) break;  // past the split's end: those rows were never loaded
-                const float pj = expf(__fsub_rn(sc[u], mn));
                 ps = __fadd_rn(ps, pj);
 #pragma unroll
                 for (int t = 0; t < EPL; ++t) acc[g][t] = __fadd_rn(acc[g][t], __fmul_rn(pj, vr[u][t]));
             }
             l[g] = __fadd_rn(__fmul_rn(l[g], c), ps);
-            m[g] = mn;
+            m[g] = mn[g];
         }
     }
     cp_async_wait<0>();  // only empty groups can be left: nothing in flight past this point
