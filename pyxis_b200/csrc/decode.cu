@@ -235,56 +235,100 @@ __global__ void __launch_bounds__(kAttnThreads)
                 for (int t = 0; t < EPL; ++t) dot[u][g] = __fadd_rn(dot[u][g], __fmul_rn(qr[g][t], kr[u][t]));
             }
         }
+        // The round's PF x G dot products, each reduced over the 32 lanes.  With NP = PF G a power
+        // of two, a reduce-scatter (levels xor 16, 8, ... keeping half the values each, then full
+        // levels) leaves pair p on the lanes pair_lane(p) + [0, 32 / NP): the same additions in the
+        // same tree as a per-value butterfly, with log2-many fewer shuffles.  The division and the
+        // exponential of each (key, head) pair, and each head's rescale factor, are then computed
+        // once (on the pair's first lane, the factor of head g on pair g's second) and shuffled to
+        // every lane: a tenth of the issue, the same operations on the same values.
+        constexpr int NP = PF * G;
+        constexpr bool RS = (NP & (NP - 1)) == 0 && NP >= 2 && NP <= 16;
+        constexpr int LPP = RS ? 32 / NP : 1;  // lanes holding one pair after the reduction
+        auto pair_lane = [](int pp) {
+            if constexpr (RS) {
+                int L = 0;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
+                for (int j = 0, o = 16, w = NP / 2; w >= 1; ++j, o >>= 1, w >>= 1)
+                    if (pp & w) L |= o;
+                return L;
+            } else {
+                return pp;
+            }
+        };
+        float dsel = 0.f;
+        int pl = lane;  // the pair whose scalars this lane computes
+        if constexpr (RS) {
+            float v[NP];
+#pragma unroll
+            for (int u = 0; u < PF; ++u)
+#pragma unroll
+                for (int g = 0; g < G; ++g) v[u * G + g] = dot[u][g];
+            pl = 0;
+#pragma unroll
+            for (int o = 16, n = NP; n > 1; o >>= 1, n >>= 1) {
+                const bool upper = (lane & o) != 0;
+                if (upper) pl += n / 2;
+#pragma unroll
+                for (int i = 0; i < n / 2; ++i) {
+                    const float send = upper ? v[i] : v[i + n / 2];
+                    const float keep = upper ? v[i + n / 2] : v[i];
+                    v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
+                }
+            }
+#pragma unroll
+            for (int o = 16 / NP; o > 0; o >>= 1) v[0] = __fadd_rn(v[0], __shfl_xor_sync(0xffffffffu, v[0], o));
+            dsel = v[0];
+        } else {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                for (int u = 0; u < PF; ++u)
+#pragma unroll
+                    for (int g = 0; g < G; ++g)
+                        dot[u][g] = __fadd_rn(dot[u][g], __shfl_xor_sync(0xffffffffu, dot[u][g], o));
 #pragma unroll
             for (int u = 0; u < PF; ++u)
 #pragma unroll
                 for (int g = 0; g < G; ++g)
-                    if (g < G) dot[u][g] = __fadd_rn(dot[u][g], __shfl_xor_sync(0xffffffffu, dot[u][g], o));
-        // The round's PF x G scores, their exponentials and the G rescale factors are scalars that
-        // every lane needs: lane u G + g computes the division and the exponential of (key u,
-        // head g), lane PF G + g the factor of head g, and shuffles hand them to every lane (the
-        // same operations on the same values as a per-lane computation, a tenth of the issue).
-        constexpr int NP = PF * G;
-        float dsel = 0.f;
-#pragma unroll
-        for (int u = 0; u < PF; ++u)
-#pragma unroll
-            for (int g = 0; g < G; ++g)
-                if (lane == u * G + g) dsel = dot[u][g];
-        const int pu = lane / G;
-        const float sc_l = lane < NP && jb + pu * NW < j1 ? __fdiv_rn(dsel, scale) : -INFINITY;
+                    if (lane == u * G + g) dsel = dot[u][g];
+        }
+        const int pu = pl / G;
+        const float sc_l = pl < NP && jb + pu * NW < j1 ? __fdiv_rn(dsel, scale) : -INFINITY;
         float sc[PF][G], mn[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) {
             float mt = -INFINITY;
 #pragma unroll
             for (int u = 0; u < PF; ++u) {
-                sc[u][g] = __shfl_sync(0xffffffffu, sc_l, u * G + g);
+                sc[u][g] = __shfl_sync(0xffffffffu, sc_l, pair_lane(u * G + g));
                 mt = fmaxf(mt, sc[u][g]);
             }
             mn[g] = fmaxf(m[g], mt);  // finite: the round has >= 1 key
         }
+        // exponential arguments: pair pl on its first lane, head g's factor on pair g's second lane
+        // (RS) or on lane NP + g
+        const int sub = RS ? (lane & (LPP - 1)) : 0;
+        const int cg = RS ? (sub == 1 ? pl : -1) : lane - NP;
         float ex_arg = 0.f;
 #pragma unroll
         for (int g = 0; g < G; ++g) {
 #pragma unroll
             for (int u = 0; u < PF; ++u)
-                if (lane == u * G + g) ex_arg = __fsub_rn(sc[u][g], mn[g]);
-            if (lane == NP + g) ex_arg = __fsub_rn(m[g], mn[g]);  // -inf on the first round: c = 0
+                if (sub == 0 && pl == u * G + g) ex_arg = __fsub_rn(sc[u][g], mn[g]);
+            if (cg == g) ex_arg = __fsub_rn(m[g], mn[g]);  // -inf on the first round: c = 0
         }
         const float ex_l = expf(ex_arg);
 #pragma unroll
         for (int g = 0; g < G; ++g) {
             if (g >= G) break;
-            const float c = __shfl_sync(0xffffffffu, ex_l, NP + g);
+            const float c = __shfl_sync(0xffffffffu, ex_l, RS ? pair_lane(g) + 1 : NP + g);
             float ps = 0.f;
 #pragma unroll
             for (int t = 0; t < EPL; ++t) acc[g][t] = __fmul_rn(acc[g][t], c);
 #pragma unroll
             for (int u = 0; u < PF; ++u) {
-                const float pj = __shfl_sync(0xffffffffu, ex_l, u * G + g);
+                const float pj = __shfl_sync(0xffffffffu, ex_l, pair_lane(u * G + g));
                 if (jb + u * NW >= j1) break;  // past the split's end: those rows were never loaded
                 ps = __fadd_rn(ps, pj);
 #pragma unroll
