@@ -232,7 +232,7 @@ __global__ void __launch_bounds__(kAttnThreads)
             for (int g = 0; g < G; ++g) {
                 dot[u][g] = 0.f;
 #pragma unroll
-                for (int t = 0; t < EPL; ++t) dot[u][g] = __fadd_rn(dot[u][g], __fmul_rn(qr[g][t], kr[u][t]));
+                for (int t = 0; t < EPL; ++t) dot[u][g] = __fmaf_rn(qr[g][t], kr[u][t], dot[u][g]);  // a sum reduced in parallel: fused
             }
         }
         // The round's PF x G dot products, each reduced over the 32 lanes.  With NP = PF G a power
@@ -332,7 +332,7 @@ __global__ void __launch_bounds__(kAttnThreads)
                 if (jb + u * NW >= j1) break;  // past the split's end: those rows were never loaded
                 ps = __fadd_rn(ps, pj);
 #pragma unroll
-                for (int t = 0; t < EPL; ++t) acc[g][t] = __fadd_rn(acc[g][t], __fmul_rn(pj, vr[u][t]));
+                for (int t = 0; t < EPL; ++t) acc[g][t] = __fmaf_rn(pj, vr[u][t], acc[g][t]);
             }
             l[g] = __fadd_rn(__fmul_rn(l[g], c), ps);
             m[g] = mn[g];
