@@ -46,6 +46,7 @@ constexpr int kMaxTok = 8;
 // at ~1.2 us per pass; more warps hide their latency)
 constexpr int kEpiWarps = 4, kHelperWarps = 6;
 constexpr int kBuildWarps = 1 + kEpiWarps + kHelperWarps;
+constexpr int kXWarp = 2 + kEpiWarps;  // the helper that issues x's copy under programmatic launch
 constexpr int kThreads = 32 * (1 + kBuildWarps);
 constexpr uint32_t kStageBytes = TM * TKB;
 constexpr uint32_t kSmemTotal = 222 * 1024;
@@ -139,6 +140,16 @@ struct Sched {
     }
 };
 
+// x [B][K] f32 into shared memory by bulk copies completing on xfull.
+PYXIS_DEVINL void issue_x_copy(const Params &p, const float *xs, uint64_t *xfull) {
+    const uint32_t row = (uint32_t)p.K * 4u;
+    tc::mbar_arrive_expect_tx(xfull, row * (uint32_t)p.B);
+    uint8_t *dst = const_cast<uint8_t *>(reinterpret_cast<const uint8_t *>(xs));
+    if (p.ldx == p.K) tc::bulk_load(dst, p.x, row * (uint32_t)p.B, xfull);
+    else
+        for (int b = 0; b < p.B; ++b) tc::bulk_load(dst + (size_t)b * row, p.x + (size_t)b * p.ldx, row, xfull);
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     gemv_tc_i8_kernel(const __grid_constant__ CUtensorMap tm_w, const Params p) {
     extern __shared__ uint8_t smem_raw[];
@@ -186,18 +197,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             tc::prefetch_tmap(&tm_w);
             // x first, ahead of the weight stream in the memory queues -- unless it comes from a
-            // kernel still running (PDL): then the weights go first and x after griddepcontrol.wait
-            bool x_issued = false;
-            auto issue_x = [&]() {
-                const uint32_t row = (uint32_t)p.K * 4u;
-                tc::mbar_arrive_expect_tx(xfull, row * (uint32_t)p.B);
-                uint8_t *dst = const_cast<uint8_t *>(reinterpret_cast<const uint8_t *>(xs));
-                if (p.ldx == p.K) tc::bulk_load(dst, p.x, row * (uint32_t)p.B, xfull);
-                else
-                    for (int b = 0; b < p.B; ++b) tc::bulk_load(dst + (size_t)b * row, p.x + (size_t)b * p.ldx, row, xfull);
-                x_issued = true;
-            };
-            if (!p.pdl) issue_x();
+            // kernel still running (PDL): then a helper warp issues it as soon as
+            // griddepcontrol.wait returns, while this thread keeps the weight stages coming
+            if (!p.pdl) issue_x_copy(p, xs, xfull);
             int g = 0;
             const Sched sc{p.total_stages, (int)gridDim.x, p.num_kb};
             const long long sb = sc.begin(blockIdx.x), se = sc.begin(blockIdx.x + 1);
@@ -212,10 +214,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int tile = (int)(s0 / p.num_kb), kb = (int)(s0 - (long long)tile * p.num_kb);
                 for (long long st = s0; st < s1; ++st, ++g) {
                     if (g == x_gate) {  // the stages x borrowed: wait until the digits are built
-                        if (!x_issued) {
-                            pdl_wait();
-                            issue_x();
-                        }
                         if (!tc::mbar_wait_bounded(xfree, 0, abort_flag, p.err, kErrProd, kTimeoutNs)) {
                             ok = false;
                             break;
@@ -238,13 +236,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
-            if (!x_issued && ok) {  // fewer stages than the x_gate: x still has to come
-                pdl_wait();
-                issue_x();
-            }
-            if (*abort_flag) {  // let the copies already issued land
+            if (*abort_flag) {  // let the copies already issued land (x: see the helper below)
                 volatile int no_abort = 0;
-                if (x_issued) tc::mbar_wait_bounded(xfull, 0, &no_abort, p.err, kErrDrain, 100000000ull);
+                if (!p.pdl) tc::mbar_wait_bounded(xfull, 0, &no_abort, p.err, kErrDrain, 100000000ull);
                 for (int j = g > p.stages ? g - p.stages : 0; j < g; ++j)
                     tc::mbar_wait_bounded(&full[j % p.stages], (j / p.stages) & 1, &no_abort, p.err, kErrDrain, 100000000ull);
             }
@@ -253,7 +247,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         // -------------------------------------------------------------------- digit operand
         const int bt = threadIdx.x - 32, nbt = kThreads - 32;  // warps 1-11
         const int bwarp = warp - 1;
-        pdl_trigger();  // x reaches shared memory through the producer, after its griddepcontrol.wait
+        if (p.pdl && warp == kXWarp && lane == 0) {
+            pdl_wait();  // x comes from the previous kernel
+            issue_x_copy(p, xs, xfull);
+        }
+        pdl_trigger();
         const Sched sc{p.total_stages, (int)gridDim.x, p.num_kb};
         const long long my_sb = sc.begin(blockIdx.x), my_se = sc.begin(blockIdx.x + 1);
         // K-blocks this CTA multiplies: a contiguous run (mod num_kb) unless it spans a whole tile
@@ -267,9 +265,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kq = p.K / 4;  // float4 quads per token
         const int kq_shift = (kq & (kq - 1)) == 0 ? __ffs(kq) - 1 : -1;  // token of a quad index by shift
         const float4 *xs4 = reinterpret_cast<const float4 *>(xs);
+        {
+            // operand rows 4B..NB-1 (no token) are zero; written while x is still on its way
+            const uint4 z = make_uint4(0, 0, 0, 0);
+            const int pad_rows = p.NB - 4 * p.B;
+            const int per_kb = pad_rows * (TKB / 16);
+            for (int i = bt; i < p.num_kb * per_kb; i += nbt) {
+                const int kb = i / per_kb, j = i - kb * per_kb, r = 4 * p.B + j / (TKB / 16);
+                if (!needed(kb)) continue;
+                uint8_t *row = xd + (size_t)kb * (p.NB * TKB) + (r >> 3) * 1024 + (r & 7) * 128;
+                reinterpret_cast<uint4 *>(row)[j % (TKB / 16)] = z;  // all-zero row: no swizzle needed
+            }
+        }
         const bool x_ok = tc::mbar_wait_bounded(xfull, 0, abort_flag, p.err, kErrMma, kTimeoutNs);
-        // x arrived after the producer's griddepcontrol.wait, so this returns at once; it keeps the
-        // epilogue's writes (y, the shared scratch) formally ordered after the previous kernel
+        // x was issued after griddepcontrol.wait (by the producer or the helper warp), so this
+        // returns at once; it keeps the epilogue's writes (y, the shared scratch) formally ordered
+        // after the previous kernel
         pdl_wait();
         if (x_ok) {
             // max |x| of every token in one pass
@@ -306,18 +317,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (m > 0.f && isfinite(m)) frexpf(m, &E);  // m < 2^E
             xexp[bt] = E;
             xscale[bt] = isfinite(m) ? ldexp(1.0, E - 27) : __longlong_as_double(0x7ff8000000000000ll);
-        }
-        {
-            // operand rows 4B..NB-1 (no token) are zero
-            const uint4 z = make_uint4(0, 0, 0, 0);
-            const int pad_rows = p.NB - 4 * p.B;
-            const int per_kb = pad_rows * (TKB / 16);
-            for (int i = bt; i < p.num_kb * per_kb; i += nbt) {
-                const int kb = i / per_kb, j = i - kb * per_kb, r = 4 * p.B + j / (TKB / 16);
-                if (!needed(kb)) continue;
-                uint8_t *row = xd + (size_t)kb * (p.NB * TKB) + (r >> 3) * 1024 + (r & 7) * 128;
-                reinterpret_cast<uint4 *>(row)[j % (TKB / 16)] = z;  // all-zero row: no swizzle needed
-            }
         }
         named_bar(1, nbt);
         // digits: t = rint(x 2^(27-E)) as 4 balanced base-128 digits, 8 quads per thread per round
@@ -495,6 +494,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
+    }
+    if (p.pdl && warp == kXWarp && lane == 0 && *abort_flag) {  // x's copy must land before the CTA leaves
+        volatile int no_abort = 0;
+        tc::mbar_wait_bounded(xfull, 0, &no_abort, p.err, kErrDrain, 100000000ull);
     }
     __syncwarp();
     tc::tc_fence_before();
