@@ -702,8 +702,10 @@ extern "C" int pyxis_cuda_model_create(pyxis_cuda_ctx *ctx, const pyxis_model_co
     m->q_dim = c.n_q_heads * c.head_dim;
     m->kv_dim = c.n_kv_heads * c.head_dim;
     m->layers.resize(c.n_layers);
-    // attention key splits: enough (kv head, split) CTAs to cover the SMs, >= 16 keys per split
-    m->attn_splits = std::max(1, std::min({ctx->num_sms / c.n_kv_heads, (c.max_seq + 15) / 16, 64}));
+    // attention key splits: up to one (kv head, split) CTA per SM, each split of >= 256 keys at the
+    // longest context (at short contexts the splits' fixed work -- q/k norm and RoPE in every CTA,
+    // the combine through a ticket -- outweighs their keys)
+    m->attn_splits = std::max(1, std::min({ctx->num_sms / c.n_kv_heads, (c.max_seq + 255) / 256, 64}));
     const size_t H = c.hidden, half = c.head_dim / 2;
     cudaError_t e = cudaSuccess;
     auto A = [&](auto **p, size_t n) {
