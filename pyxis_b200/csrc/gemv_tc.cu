@@ -18,10 +18,12 @@
 // warp 1 = TMEM owner + MMA issuer (M=128, N=16|32, K=32 per instruction, 8 accumulators per
 // tile segment so that consecutive stages do not wait on each other, double-buffered in TMEM
 // across segments), warps 2-5 = epilogue (tcgen05.ld, one TMEM lane = one weight row), warps
-// 6-11 helpers.  x itself arrives by one bulk copy into the last ring stages, issued before the
-// first weight copy (or, under programmatic dependent launch, right after the predecessor
-// finishes), so it does not queue behind the weight stream; warps 1-11 turn it into the digit
-// operand and hand the stages back to the producer.  A tile whose stages span several CTAs has its partial int32
+// 6-11 helpers.  x itself arrives by one TMA box straight into the digit operand's shared memory
+// (each 512-byte block of 128 values of one token is where that block's four digit rows go),
+// issued before the first weight copy (or, under programmatic dependent launch, by a helper warp
+// right after the predecessor finishes), so the whole ring streams weights from the start; warps
+// 2-11 convert the blocks in place in the order the MMAs take the K-blocks, and the MMA issuer
+// waits for each K-block's digits only.  A tile whose stages span several CTAs has its partial int32
 // sums added exactly with atomics into a scratch slot, and the CTA that finishes the tile last
 // converts it and zeroes the scratch for the next launch.  The schedule is stream-K: every CTA
 // gets the same number of (tile, K-block) stages, and works on its (possibly shared) first and
@@ -41,13 +43,14 @@ namespace {
 constexpr int TM = 128;    // weight rows per tile
 constexpr int TKB = 128;   // K bytes (= int8 codes) per stage
 constexpr int kMaxTok = 8;
-// warp 0 the TMA producer, warp 1 the MMA issuer, warps 2-5 the epilogue, 6-11 helpers: warps 1-11
+// warp 0 the TMA producer, warp 1 the MMA issuer, warps 2-5 the epilogue, 6-11 helpers: warps 2-11
 // build x's digit operand (with one warp per SM sub-partition the build's dependent chains ran
 // at ~1.2 us per pass; more warps hide their latency)
 constexpr int kEpiWarps = 4, kHelperWarps = 6;
-constexpr int kBuildWarps = 1 + kEpiWarps + kHelperWarps;
+constexpr int kBuildWarp0 = 2, kBuildWarps = kEpiWarps + kHelperWarps;
 constexpr int kXWarp = 2 + kEpiWarps;  // the helper that issues x's copy under programmatic launch
-constexpr int kThreads = 32 * (1 + kBuildWarps);
+constexpr int kThreads = 32 * (kBuildWarp0 + kBuildWarps);
+constexpr int kMaxKb = 48;  // K-blocks of the digit operand (it is at most 96 KB)
 constexpr uint32_t kStageBytes = TM * TKB;
 constexpr uint32_t kSmemTotal = 222 * 1024;
 constexpr int kMaxStages = 12;
@@ -68,7 +71,6 @@ struct Params {
     int N, K, B, NB;
     int num_kb, num_tiles, stages;
     uint32_t tmem_cols;
-    int x_stages;  // ring stages that hold x [B][K] f32 until the digits are built
     int pdl;       // launched with programmatic stream serialization
     long long total_stages;  // num_tiles * num_kb, split evenly over the grid (stream-K)
     uint32_t xd_bytes;
@@ -140,18 +142,17 @@ struct Sched {
     }
 };
 
-// x [B][K] f32 into shared memory by bulk copies completing on xfull.
-PYXIS_DEVINL void issue_x_copy(const Params &p, const float *xs, uint64_t *xfull) {
-    const uint32_t row = (uint32_t)p.K * 4u;
-    tc::mbar_arrive_expect_tx(xfull, row * (uint32_t)p.B);
-    uint8_t *dst = const_cast<uint8_t *>(reinterpret_cast<const uint8_t *>(xs));
-    if (p.ldx == p.K) tc::bulk_load(dst, p.x, row * (uint32_t)p.B, xfull);
-    else
-        for (int b = 0; b < p.B; ++b) tc::bulk_load(dst + (size_t)b * row, p.x + (size_t)b * p.ldx, row, xfull);
+// x [B][K] f32 by one TMA box into the digit operand's own space, block (K-block kb, token b) of
+// 128 values at byte (kb NB / 4 + b) 512 -- exactly the four digit rows it becomes -- with the
+// token slots past B zero-filled.
+PYXIS_DEVINL void issue_x_copy(const CUtensorMap *tm_x, uint8_t *xd, uint32_t bytes, uint64_t *xfull) {
+    tc::mbar_arrive_expect_tx(xfull, bytes);
+    tc::tma_load_3d(xd, tm_x, 0, 0, 0, xfull);
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    gemv_tc_i8_kernel(const __grid_constant__ CUtensorMap tm_w, const Params p) {
+    gemv_tc_i8_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+                      const Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *xd = smem;                    // digit operand: [kb][NB rows][128 B], 128-byte swizzle
@@ -159,8 +160,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *bars = reinterpret_cast<uint64_t *>(ring + (size_t)p.stages * kStageBytes);
     uint64_t *full = bars, *empty = bars + kMaxStages;
     uint64_t *tfull = bars + 2 * kMaxStages, *tempty = tfull + 2, *drain = tempty + 2;
-    uint64_t *xfull = drain + 1, *xfree = drain + 2;
-    double *xscale = reinterpret_cast<double *>(drain + 3);          // [kMaxTok]
+    uint64_t *xfull = drain + 1, *xready = drain + 2;                // xready: [kMaxKb]
+    double *xscale = reinterpret_cast<double *>(xready + kMaxKb);    // [kMaxTok]
     float *red = reinterpret_cast<float *>(xscale + kMaxTok);        // [kMaxTok][kBuildWarps]
     int *xexp = reinterpret_cast<int *>(red + kMaxTok * kBuildWarps);  // [kMaxTok]
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(xexp + kMaxTok);
@@ -179,7 +180,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc::mbar_init(drain, 1);
         tc::mbar_init(xfull, 1);
-        tc::mbar_init(xfree, 1);
+        for (int kb = 0; kb < p.num_kb; ++kb) tc::mbar_init(&xready[kb], p.B);  // one arrival per token block
         *abort_flag = 0;
         tc::fence_mbar_init();
     }
@@ -188,21 +189,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    // x [B][K] f32 borrows the last x_stages ring stages until the digit operand is built
-    const int x_gate = p.stages - p.x_stages;
-    const float *xs = reinterpret_cast<const float *>(ring + (size_t)x_gate * kStageBytes);
+    const Sched sc{p.total_stages, (int)gridDim.x, p.num_kb};
+    const long long my_sb = sc.begin(blockIdx.x), my_se = sc.begin(blockIdx.x + 1);
 
     if (warp == 0) {
         // -------------------------------------------------------------------- TMA producer
         if (lane == 0) {
             tc::prefetch_tmap(&tm_w);
+            tc::prefetch_tmap(&tm_x);
             // x first, ahead of the weight stream in the memory queues -- unless it comes from a
             // kernel still running (PDL): then a helper warp issues it as soon as
             // griddepcontrol.wait returns, while this thread keeps the weight stages coming
-            if (!p.pdl) issue_x_copy(p, xs, xfull);
+            if (!p.pdl) issue_x_copy(&tm_x, xd, p.xd_bytes, xfull);
             int g = 0;
-            const Sched sc{p.total_stages, (int)gridDim.x, p.num_kb};
-            const long long sb = sc.begin(blockIdx.x), se = sc.begin(blockIdx.x + 1);
+            const long long sb = my_sb, se = my_se;
             const int nseg = sc.num_segments(sb, se);
             bool ok = true;
             // ring slot s of stage g and its round ph = g / stages, tile and K-block of the stage:
@@ -213,12 +213,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 sc.segment(sb, se, i, s0, s1);
                 int tile = (int)(s0 / p.num_kb), kb = (int)(s0 - (long long)tile * p.num_kb);
                 for (long long st = s0; st < s1; ++st, ++g) {
-                    if (g == x_gate) {  // the stages x borrowed: wait until the digits are built
-                        if (!tc::mbar_wait_bounded(xfree, 0, abort_flag, p.err, kErrProd, kTimeoutNs)) {
-                            ok = false;
-                            break;
-                        }
-                    }
                     if (g >= p.stages && !tc::mbar_wait_bounded(&empty[s], (uint32_t)((ph - 1) & 1), abort_flag, p.err,
                                                                 kErrProd, kTimeoutNs)) {
                         ok = false;
@@ -243,56 +237,85 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc::mbar_wait_bounded(&full[j % p.stages], (j / p.stages) & 1, &no_abort, p.err, kErrDrain, 100000000ull);
             }
         }
+    } else if (warp == 1) {
+        // -------------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = idesc_i8(TM, p.NB);
+            // descriptors advance by constant offsets (start address in 16-byte units), the ring
+            // slot and its phase by increments: no per-stage division or descriptor rebuild
+            const uint64_t ring_d = tc::desc_sw128(tc::smem_u32(ring)), xd_d = tc::desc_sw128(tc::smem_u32(xd));
+            const uint32_t stage_step = kStageBytes >> 4, kb_step = (uint32_t)(p.NB * TKB) >> 4;
+            int li = 0, s = 0, ph = 0;
+            bool ok = true;
+            const int nseg = sc.num_segments(my_sb, my_se);
+            for (; li < nseg && ok; ++li) {
+                long long s0, s1;
+                sc.segment(my_sb, my_se, li, s0, s1);
+                const int kb0 = (int)(s0 % p.num_kb), nk = (int)(s1 - s0);
+                const int buf = li & 1;
+                if (li >= 2) {
+                    ok = tc::mbar_wait_bounded(&tempty[buf], ((li >> 1) - 1) & 1, abort_flag, p.err, kErrMma, kTimeoutNs);
+                    if (!ok) break;
+                }
+                tc::tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(buf * kAccPerBuf * p.NB);
+                for (int kb = kb0; kb < kb0 + nk; ++kb) {
+                    // the K-block's digits (converted in place by the builders) and the stage's codes
+                    ok = tc::mbar_wait_bounded(&xready[kb], 0, abort_flag, p.err, kErrMma, kTimeoutNs) &&
+                         tc::mbar_wait_bounded(&full[s], (uint32_t)(ph & 1), abort_flag, p.err, kErrMma, kTimeoutNs);
+                    if (!ok) break;
+                    tc::tc_fence_after();
+                    const uint64_t a0 = ring_d + (uint64_t)(s * stage_step);
+                    const uint64_t b0 = xd_d + (uint64_t)(kb * kb_step);
+                    const uint32_t dset = d + (uint32_t)(((kb - kb0) & 1) * kAccPerStage * p.NB);
+#pragma unroll
+                    for (int q = 0; q < kAccPerStage; ++q)
+                        mma_i8(dset + (uint32_t)(q * p.NB), a0 + (uint64_t)(2 * q), b0 + (uint64_t)(2 * q), idesc,
+                               kb - kb0 >= 2 ? 1u : 0u);
+                    tc::mma_commit(&empty[s]);
+                    if (++s == p.stages) {
+                        s = 0;
+                        ++ph;
+                    }
+                }
+                if (ok) tc::mma_commit(&tfull[buf]);
+            }
+            tc::mma_commit(drain);
+            volatile int no_abort = 0;
+            tc::mbar_wait_bounded(drain, 0, &no_abort, p.err, kErrDrain, kTimeoutNs);
+        }
     } else {
         // -------------------------------------------------------------------- digit operand
-        const int bt = threadIdx.x - 32, nbt = kThreads - 32;  // warps 1-11
-        const int bwarp = warp - 1;
+        const int bt = threadIdx.x - 32 * kBuildWarp0, nbt = 32 * kBuildWarps;  // warps 2-11
+        const int bwarp = warp - kBuildWarp0;
         if (p.pdl && warp == kXWarp && lane == 0) {
             pdl_wait();  // x comes from the previous kernel
-            issue_x_copy(p, xs, xfull);
+            issue_x_copy(&tm_x, xd, p.xd_bytes, xfull);
         }
         pdl_trigger();
-        const Sched sc{p.total_stages, (int)gridDim.x, p.num_kb};
-        const long long my_sb = sc.begin(blockIdx.x), my_se = sc.begin(blockIdx.x + 1);
-        // K-blocks this CTA multiplies: a contiguous run (mod num_kb) unless it spans a whole tile
+        // K-blocks this CTA multiplies: a contiguous run (mod num_kb) from need_lo unless it spans
+        // a whole tile; the MMAs take them in that order
         const int need_lo = (int)(my_sb % p.num_kb);
-        const long long need_n = my_se - my_sb;
-        auto needed = [&](int kb) {  // kb, need_lo in [0, num_kb): a wrap-around offset without a modulo
-            int d = kb - need_lo;
-            if (d < 0) d += p.num_kb;
-            return need_n >= p.num_kb || d < need_n;
-        };
-        const int kq = p.K / 4;  // float4 quads per token
-        const int kq_shift = (kq & (kq - 1)) == 0 ? __ffs(kq) - 1 : -1;  // token of a quad index by shift
-        const float4 *xs4 = reinterpret_cast<const float4 *>(xs);
-        {
-            // operand rows 4B..NB-1 (no token) are zero; written while x is still on its way
-            const uint4 z = make_uint4(0, 0, 0, 0);
-            const int pad_rows = p.NB - 4 * p.B;
-            const int per_kb = pad_rows * (TKB / 16);
-            for (int i = bt; i < p.num_kb * per_kb; i += nbt) {
-                const int kb = i / per_kb, j = i - kb * per_kb, r = 4 * p.B + j / (TKB / 16);
-                if (!needed(kb)) continue;
-                uint8_t *row = xd + (size_t)kb * (p.NB * TKB) + (r >> 3) * 1024 + (r & 7) * 128;
-                reinterpret_cast<uint4 *>(row)[j % (TKB / 16)] = z;  // all-zero row: no swizzle needed
-            }
-        }
+        const int n_need = my_se - my_sb >= p.num_kb ? p.num_kb : (int)(my_se - my_sb);
+        const int nbq = p.NB / 4;  // token slots per K-block
+        const float4 *xd4 = reinterpret_cast<const float4 *>(xd);
         const bool x_ok = tc::mbar_wait_bounded(xfull, 0, abort_flag, p.err, kErrMma, kTimeoutNs);
         // x was issued after griddepcontrol.wait (by the producer or the helper warp), so this
         // returns at once; it keeps the epilogue's writes (y, the shared scratch) formally ordered
         // after the previous kernel
         pdl_wait();
         if (x_ok) {
-            // max |x| of every token in one pass
+            // max |x| of every token over all of K, the same in every CTA
             float m[kMaxTok];
 #pragma unroll
             for (int b = 0; b < kMaxTok; ++b) m[b] = 0.f;
 #pragma unroll 2
-            for (int k4 = bt; k4 < kq; k4 += nbt) {
+            for (int i = bt; i < p.num_kb * 32; i += nbt) {  // (K-block, quad of the block)
+                const int kb = i >> 5, q = i & 31;
                 float4 v[kMaxTok];
 #pragma unroll
                 for (int b = 0; b < kMaxTok; ++b)
-                    if (b < p.B) v[b] = xs4[(size_t)b * kq + k4];
+                    if (b < p.B) v[b] = xd4[(size_t)(kb * nbq + b) * 32 + q];
 #pragma unroll
                 for (int b = 0; b < kMaxTok; ++b)
                     if (b < p.B)
@@ -319,30 +342,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             xscale[bt] = isfinite(m) ? ldexp(1.0, E - 27) : __longlong_as_double(0x7ff8000000000000ll);
         }
         named_bar(1, nbt);
-        // digits: t = rint(x 2^(27-E)) as 4 balanced base-128 digits, 8 quads per thread per round
-        const int total = x_ok ? p.B * kq : 0;
-        for (int base = bt; base < total; base += 8 * nbt) {
-            float4 xv[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int idx = base + u * nbt;
-                if (idx < total) xv[u] = xs4[idx];
-            }
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int idx = base + u * nbt;
-                if (idx >= total) break;
-                const int b = kq_shift >= 0 ? idx >> kq_shift : idx / kq, k = (idx - b * kq) * 4;
-                if (!needed(k / TKB)) continue;
+        // digits: t = rint(x 2^(27-E)) as 4 balanced base-128 digits.  A warp converts one (K-block,
+        // token) block at a time in place -- its 128 f32 values are read into the lanes, then the
+        // block's 512 bytes become the token's four 128-byte-swizzled digit rows -- in the order the
+        // MMAs take the K-blocks, and each K-block's digits are handed to the MMA warp as soon as
+        // its B blocks are done.  The token slots past B arrived as zeros, i.e. zero digits.
+        if (x_ok) {
+            for (int blk = bwarp; blk < n_need * p.B; blk += kBuildWarps) {
+                const int o = blk / p.B, b = blk - o * p.B;
+                const int kb = need_lo + o < p.num_kb ? need_lo + o : need_lo + o - p.num_kb;
+                uint8_t *kbase = xd + (size_t)kb * (p.NB * TKB);
+                const float4 xv = xd4[(size_t)(kb * nbq + b) * 32 + lane];  // elements 4 lane .. 4 lane + 3
+                __syncwarp();  // the whole block is in registers before any digit overwrites it
                 // x 2^(27-E) exactly, as two power-of-two products (27 - E lies in [-101, 175])
                 const int sh = 27 - xexp[b];
                 const int sa = sh < 127 ? sh : 127;
                 const float f1 = pow2f(sa), f2 = pow2f(sh - sa);
-                const float xs4[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
+                const float xe[4] = {xv.x, xv.y, xv.z, xv.w};
                 uint32_t word[4] = {0, 0, 0, 0};
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const float v = (xs4[e] * f1) * f2;
+                    const float v = (xe[e] * f1) * f2;
                     const int t = isfinite(v) ? __float2int_rn(v) : 0;
                     const uint32_t ub = (uint32_t)(t + kDigitBias);
                     word[0] |= (ub >> 21) << (8 * e);
@@ -350,66 +370,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                     word[2] |= ((ub >> 7) & 127u) << (8 * e);
                     word[3] |= (ub & 127u) << (8 * e);
                 }
-                const int kb = k / TKB, kk = k % TKB, c = kk >> 4;
+                const int c = lane >> 2;  // 16-byte chunk of the 128-byte row holding K 4 lane .. 4 lane + 3
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const int r = 4 * b + i;
-                    uint8_t *row = xd + (size_t)kb * (p.NB * TKB) + (r >> 3) * 1024 + (r & 7) * 128;
-                    *reinterpret_cast<uint32_t *>(row + ((c ^ (r & 7)) << 4) + (kk & 15)) =
+                    uint8_t *row = kbase + (r >> 3) * 1024 + (r & 7) * 128;
+                    *reinterpret_cast<uint32_t *>(row + ((c ^ (r & 7)) << 4) + 4 * (lane & 3)) =
                         __vsub4(word[i], 0x40404040u);  // digit + 64 -> digit, per byte
                 }
+                tc::fence_proxy_async_smem();  // digit writes -> the MMAs' reads
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&xready[kb]);
             }
         }
-        tc::fence_proxy_async_smem();  // digit writes -> MMA reads; x reads -> the producer's reuse
-        named_bar(1, nbt);
-        if (bt == 0) tc::mbar_arrive(xfree);  // the stages that held x go back to the weights
 
-        if (warp == 1) {
-            // ---------------------------------------------------------------- MMA issuer
-            if (lane == 0) {
-                const uint32_t idesc = idesc_i8(TM, p.NB);
-                // descriptors advance by constant offsets (start address in 16-byte units), the ring
-                // slot and its phase by increments: no per-stage division or descriptor rebuild
-                const uint64_t ring_d = tc::desc_sw128(tc::smem_u32(ring)), xd_d = tc::desc_sw128(tc::smem_u32(xd));
-                const uint32_t stage_step = kStageBytes >> 4, kb_step = (uint32_t)(p.NB * TKB) >> 4;
-                int li = 0, s = 0, ph = 0;
-                bool ok = true;
-                const int nseg = sc.num_segments(my_sb, my_se);
-                for (; li < nseg && ok; ++li) {
-                    long long s0, s1;
-                    sc.segment(my_sb, my_se, li, s0, s1);
-                    const int kb0 = (int)(s0 % p.num_kb), nk = (int)(s1 - s0);
-                    const int buf = li & 1;
-                    if (li >= 2) {
-                        ok = tc::mbar_wait_bounded(&tempty[buf], ((li >> 1) - 1) & 1, abort_flag, p.err, kErrMma, kTimeoutNs);
-                        if (!ok) break;
-                    }
-                    tc::tc_fence_after();
-                    const uint32_t d = tmem_base + (uint32_t)(buf * kAccPerBuf * p.NB);
-                    for (int kb = kb0; kb < kb0 + nk; ++kb) {
-                        ok = tc::mbar_wait_bounded(&full[s], (uint32_t)(ph & 1), abort_flag, p.err, kErrMma, kTimeoutNs);
-                        if (!ok) break;
-                        tc::tc_fence_after();
-                        const uint64_t a0 = ring_d + (uint64_t)(s * stage_step);
-                        const uint64_t b0 = xd_d + (uint64_t)(kb * kb_step);
-                        const uint32_t dset = d + (uint32_t)(((kb - kb0) & 1) * kAccPerStage * p.NB);
-#pragma unroll
-                        for (int q = 0; q < kAccPerStage; ++q)
-                            mma_i8(dset + (uint32_t)(q * p.NB), a0 + (uint64_t)(2 * q), b0 + (uint64_t)(2 * q), idesc,
-                                   kb - kb0 >= 2 ? 1u : 0u);
-                        tc::mma_commit(&empty[s]);
-                        if (++s == p.stages) {
-                            s = 0;
-                            ++ph;
-                        }
-                    }
-                    if (ok) tc::mma_commit(&tfull[buf]);
-                }
-                tc::mma_commit(drain);
-                volatile int no_abort = 0;
-                tc::mbar_wait_bounded(drain, 0, &no_abort, p.err, kErrDrain, kTimeoutNs);
-            }
-        } else if (warp < 2 + kEpiWarps) {
+        if (warp < 2 + kEpiWarps) {
             // ---------------------------------------------------------------- epilogue
             // All four warps run the same item sequence and the same named barriers; a warp
             // whose wait ran out skips the work but keeps the barrier sequence.
@@ -512,7 +487,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() { return tensor_map_encoder(); }
 
 struct Plan {
     bool ok = false;
-    int NB = 16, stages = 0, x_stages = 0;
+    int NB = 16, stages = 0;
     uint32_t xd_bytes = 0;
 };
 
@@ -524,10 +499,10 @@ Plan plan_for(const QMatrix &w, size_t B, int num_sms) {
     pl.NB = 4 * (int)B <= 16 ? 16 : 32;
     pl.xd_bytes = (uint32_t)(w.K * pl.NB);
     if (pl.xd_bytes > 96 * 1024) return pl;
-    const uint32_t avail = kSmemTotal - 1024 - 1024 - pl.xd_bytes;  // alignment slack, barriers
+    if (w.K / TKB > (size_t)kMaxKb) return pl;
+    const uint32_t avail = kSmemTotal - 1024 - 2048 - pl.xd_bytes;  // alignment slack, barriers and scalars
     pl.stages = std::min<int>(kMaxStages, (int)(avail / kStageBytes));
-    pl.x_stages = (int)((B * w.K * sizeof(float) + kStageBytes - 1) / kStageBytes);
-    if (pl.stages < 2 || pl.x_stages >= pl.stages) return pl;
+    if (pl.stages < 2) return pl;
     pl.ok = true;
     return pl;
 }
@@ -563,6 +538,19 @@ cudaError_t launch_gemv_tc(const QMatrix &w, const float *X, size_t B, size_t ld
            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return cudaErrorInvalidValue;
+    // x as (128 values of a K-block, token, K-block) with strides (4 B, ldx * 4, 512 B): one box of
+    // (128, NB / 4, K / 128) lands as [K-block][token slot][128] f32, token slots past B zero
+    CUtensorMap tx;
+    {
+        cuuint64_t xdims[3] = {(cuuint64_t)TKB, (cuuint64_t)B, (cuuint64_t)(w.K / TKB)};
+        cuuint64_t xstrides[2] = {(cuuint64_t)(B > 1 ? ldx : w.K) * sizeof(float), (cuuint64_t)TKB * sizeof(float)};
+        cuuint32_t xbox[3] = {(cuuint32_t)TKB, (cuuint32_t)(pl.NB / 4), (cuuint32_t)(w.K / TKB)};
+        cuuint32_t xes[3] = {1, 1, 1};
+        if (fn(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(X), xdims, xstrides, xbox, xes,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
     Params p{};
     p.N = (int)w.N;
     p.K = (int)w.K;
@@ -573,7 +561,6 @@ cudaError_t launch_gemv_tc(const QMatrix &w, const float *X, size_t B, size_t ld
     p.total_stages = total;
     p.stages = pl.stages;
     p.tmem_cols = (uint32_t)(2 * kAccPerBuf * pl.NB);  // 256 or 512
-    p.x_stages = pl.x_stages;
     p.pdl = pdl_enabled() ? 1 : 0;
     p.xd_bytes = pl.xd_bytes;
     p.x = X;
@@ -592,7 +579,7 @@ cudaError_t launch_gemv_tc(const QMatrix &w, const float *X, size_t B, size_t ld
         return cudaFuncSetAttribute(gemv_tc_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTotal);
     });
     if (attr != cudaSuccess) return attr;
-    return launch_kernel(gemv_tc_i8_kernel, dim3(grid), dim3(kThreads), kSmemTotal, st, tm, p);
+    return launch_kernel(gemv_tc_i8_kernel, dim3(grid), dim3(kThreads), kSmemTotal, st, tm, tx, p);
 }
 
 }  // namespace pyxis
