@@ -137,7 +137,11 @@ int pyxis_cuda_matmul(pyxis_cuda_ctx *ctx, const float *input, const pyxis_cuda_
 
 /* Batched form with host buffers: M independent rows, input [M, in_features] -> out
  * [M, out_features] (the reference's prefill calls matmul once per position,
- * src/attention.rs:74-79). */
+ * src/attention.rs:74-79).  When `out` is page-locked memory this device can address
+ * (cudaHostAlloc / cudaMallocHost, or cudaHostRegister'ed and mapped) and the product runs on a
+ * GEMV kernel (every M <= 8, and larger M that the tensor-core products do not take), the kernel
+ * stores the results into it directly instead of through a device buffer and a copy; the values
+ * are the same either way.  Pageable `out` takes the copy. */
 int pyxis_cuda_matmul_batch(pyxis_cuda_ctx *ctx, const float *input, size_t M,
                             const pyxis_cuda_weights *w, size_t out_features, size_t in_features,
                             float *out);

@@ -542,6 +542,18 @@ const char *pyxis_cuda_matmul_kernel(pyxis_cuda_ctx *ctx, const pyxis_cuda_weigh
     return gemv_kernel_name(q, b, ctx->num_sms);
 }
 
+// The device address of page-locked host memory that the current device can store to
+// (cudaHostAlloc / cudaMallocHost under unified addressing, or cudaHostRegister'ed memory mapped
+// for this device); NULL for pageable memory and device memory.
+static void *mapped_host(const void *p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        (void)cudaGetLastError();  // not a pointer CUDA knows: take the copy path
+        return nullptr;
+    }
+    return a.type == cudaMemoryTypeHost ? a.devicePointer : nullptr;
+}
+
 int pyxis_cuda_matmul_batch(pyxis_cuda_ctx *ctx, const float *input, size_t M, const pyxis_cuda_weights *w,
                             size_t out_features, size_t in_features, float *out) {
     int rc = check_matmul(ctx, w, out_features, in_features);
@@ -552,13 +564,23 @@ int pyxis_cuda_matmul_batch(pyxis_cuda_ctx *ctx, const float *input, size_t M, c
     std::lock_guard<std::mutex> lock(ctx->host_mu);
     rc = grow(&ctx->dx, &ctx->dx_cap, M * in_features);
     if (rc) return rc;
-    rc = grow(&ctx->dy, &ctx->dy_cap, M * out_features);
-    if (rc) return rc;
+    // The GEMV kernels store each output element once, with plain stores from whole warps: into a
+    // page-locked output they write across PCIe while the kernel runs, instead of in a copy after
+    // it (the lm_head at 8 rows: 4.9 MB of results that took a 97 us copy behind a 71 us kernel).
+    // The tensor-core products (workspace partial sums, their own epilogues) keep the copy.
+    const QMatrix q = qmatrix(w, out_features, in_features);
+    float *direct = (use_gemm_ws(q, M) || use_gemm_tc(q, M, ctx->dx, in_features))
+                        ? nullptr : static_cast<float *>(mapped_host(out));
+    if (!direct) {
+        rc = grow(&ctx->dy, &ctx->dy_cap, M * out_features);
+        if (rc) return rc;
+    }
     PYXIS_CUDA_TRY(cudaMemcpyAsync(ctx->dx, input, M * in_features * sizeof(float), cudaMemcpyHostToDevice, ctx->stream), "copy input");
-    rc = pyxis_cuda_matmul_dev(ctx, w, ctx->dx, M, in_features, out_features, in_features, ctx->dy,
+    rc = pyxis_cuda_matmul_dev(ctx, w, ctx->dx, M, in_features, out_features, in_features, direct ? direct : ctx->dy,
                                out_features, nullptr, 0, nullptr);
     if (rc) return rc;
-    PYXIS_CUDA_TRY(cudaMemcpyAsync(out, ctx->dy, M * out_features * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream), "copy output");
+    if (!direct)
+        PYXIS_CUDA_TRY(cudaMemcpyAsync(out, ctx->dy, M * out_features * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream), "copy output");
     PYXIS_CUDA_TRY(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
     return PYXIS_OK;
 }

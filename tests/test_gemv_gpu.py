@@ -244,3 +244,50 @@ def test_host_calls_from_several_threads():
     for th in threads:
         th.join()
     assert not bad, bad
+
+
+@pytest.mark.parametrize("qt,N,K,bs,B", [
+    ("int4", 2048, 2048, 32, 1),      # batch GEMV
+    ("int4", 1024, 2048, 32, 8),      # batch GEMV, 8 rows
+    ("int4", 6144, 2048, 32, 8),      # mma GEMV
+    ("int8", 33000, 2048, 2048, 1),   # tensor-core GEMV
+    ("int8", 33000, 2048, 2048, 8),
+    ("int4", 5, 7, 3, 3),             # generic GEMV
+    ("int4", 2048, 2048, 32, 16),     # weight-streaming matmul: keeps the copy
+    ("int8", 512, 1024, 1024, 80),    # prefill GEMM: keeps the copy
+])
+def test_host_call_into_page_locked_output(qt, N, K, bs, B):
+    """pyxis_cuda_matmul_batch with a page-locked output: the GEMV kernels store into it
+    directly (torch pinned memory, cudaHostRegister'ed numpy memory, and an output that starts
+    4 bytes past an allocation's start), the tensor-core products copy into it; each gives the
+    pageable-output result bit for bit, and that result matches the oracle."""
+    import ctypes as C
+    import torch
+    w, od, os_ = make(qt, N, K, bs, seed=N + 3 * K + B)
+    X = px.synth_normal_f32(900 + B, B * K, 1.0).reshape(B, K)
+    X[0, :2] = [-3e4, -0.0]
+    Y0 = px.matmul_batch(X, w, N, K)
+    check_matmul(Y0, ref_matmul(qt, od, os_, bs, X, N, K), exact_matmul(qt, od, os_, bs, N, K, X))
+    L = px._native.lib()
+    xp = torch.from_numpy(X).pin_memory()
+
+    def run(out_ptr):
+        px._native.check(L.pyxis_cuda_matmul_batch(w.ctx.handle, C.c_void_p(xp.data_ptr()), B, w.handle, N, K,
+                                                   C.c_void_p(out_ptr)))
+
+    pinned = torch.full((B * N + 1,), float("nan"), dtype=torch.float32).pin_memory()
+    for off in (0, 1):
+        pinned.fill_(float("nan"))
+        run(pinned.data_ptr() + 4 * off)
+        got = pinned[off:off + B * N].numpy().reshape(B, N)
+        assert np.array_equal(got.view(np.uint32), Y0.view(np.uint32)), off
+        assert np.isnan(pinned[1 - off if off else B * N].item())  # nothing stored past the output
+    reg = np.full((B, N), np.nan, dtype=np.float32)
+    cr = torch.cuda.cudart()
+    assert int(cr.cudaHostRegister(reg.ctypes.data, reg.nbytes, 0)) == 0
+    try:
+        run(reg.ctypes.data)
+    finally:
+        assert int(cr.cudaHostUnregister(reg.ctypes.data)) == 0
+    assert np.array_equal(reg.view(np.uint32), Y0.view(np.uint32))
+    px._native.check(L.pyxis_cuda_check_device_error(w.ctx.handle))
