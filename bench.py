@@ -375,8 +375,9 @@ def run_row_split(ws, rank, local, steps, capture, replay_ms, full):
     job_bytes = sum(gemv_bytes(qt, hi - lo, K, bs, B) for B in BATCHES for (_, qt, N, K, bs, _) in shards
                     for (lo, hi) in (shard_range(N, r, ws) for r in range(ws)))
     peak, peak_kind = measured_peak_hbm()
-    # parity: all-gathered shards == the full matrix on this rank: bit for bit, or (where the
-    # weight-streaming matmul splits K by the row count) within the matmul bar
+    # parity: all-gathered shards == the full matrix on this rank: bit for bit, or (where the shard
+    # and the full matrix take different kernels by size, or the kernel -- the mma GEMV, the
+    # weight-streaming matmul -- splits K by the row count) within the matmul bar
     # max_i |y_i - r_i| / max(|r_i|, 1e-3 max|r|) <= 1e-3
     parity = True
     mismatch, bitwise, max_rel = [], [], 0.0

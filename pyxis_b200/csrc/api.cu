@@ -191,6 +191,17 @@ bool use_gemv_tc(const pyxis_cuda_ctx *ctx, const QMatrix &q, size_t b, const fl
 }
 }  // namespace
 
+bool pyxis::head_gemv_keys(pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, const float *X, size_t M, size_t ldx,
+                           size_t N, size_t K, float *Y, size_t ldy, int64_t index_base, uint64_t *keys,
+                           cudaStream_t st, cudaError_t *err) {
+    const QMatrix q = qmatrix(w, N, K);
+    if (M == 0 || M > 8 || !use_gemv_tc(ctx, q, M, X, ldx)) return false;
+    PdlScope pdl;
+    *err = launch_gemv_tc(q, X, M, ldx, Y, ldy, ctx->tcg_scratch, ctx->tcg_scratch_bytes, ctx->d_err, ctx->num_sms,
+                          st, keys, (long long)index_base);
+    return true;
+}
+
 int pyxis::run_matmul(pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, const float *X, size_t M, size_t ldx,
                       size_t out_features, size_t in_features, float *Y, size_t ldy, void *workspace,
                       size_t workspace_bytes, cudaStream_t st) {

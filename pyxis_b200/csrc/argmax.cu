@@ -20,23 +20,6 @@
 
 namespace pyxis {
 
-PYXIS_DEVINL uint64_t argmax_key(float v, uint32_t idx) {
-    if (isnan(v)) return 0;  // below every number, including -inf
-    if (v == 0.0f) v = 0.0f; // -0.0 ties with +0.0
-    uint32_t u = __float_as_uint(v);
-    uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-    return ((uint64_t)ord << 32) | (uint64_t)(0xFFFFFFFFu - idx);
-}
-
-PYXIS_DEVINL uint64_t warp_max_u64(uint64_t k) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        uint64_t other = __shfl_xor_sync(0xffffffffu, k, o);
-        k = other > k ? other : k;
-    }
-    return k;
-}
-
 // Reduce a CTA's 64-bit keys; result valid in thread 0.
 PYXIS_DEVINL uint64_t cta_max_u64(uint64_t k, uint64_t *red) {
     k = warp_max_u64(k);
@@ -128,26 +111,30 @@ cudaError_t launch_argmax_keys(const float *values, size_t M, size_t n, size_t l
                          (int32_t *)nullptr, (float *)nullptr, keys, s);
 }
 
-// tokens[r] = the index in the largest of the nranks keys of row row0 + r (keys_all [nranks][rows]).
-__global__ void pick_keys_kernel(const uint64_t *__restrict__ keys_all, int nranks, int rows, int row0, int nrows,
-                                 int32_t *__restrict__ tokens) {
+// tokens[r] = the index in the largest of the nranks keys of row row0 + r (keys_all [nranks][rows]);
+// one CTA, which then zeroes keys_all and zero_keys for the next call.
+__global__ void pick_keys_kernel(uint64_t *__restrict__ keys_all, int nranks, int rows, int row0, int nrows,
+                                 int32_t *__restrict__ tokens, uint64_t *__restrict__ zero_keys, int zero_n) {
     pdl_wait();
     pdl_trigger();
-    const int r = blockIdx.x * blockDim.x + threadIdx.x;
-    if (r >= nrows) return;
-    uint64_t m = 0;
-    for (int w = 0; w < nranks; ++w) {
-        const uint64_t k = keys_all[(size_t)w * rows + row0 + r];
-        m = k > m ? k : m;
+    for (int r = threadIdx.x; r < nrows; r += blockDim.x) {
+        uint64_t m = 0;
+        for (int w = 0; w < nranks; ++w) {
+            const uint64_t k = keys_all[(size_t)w * rows + row0 + r];
+            m = k > m ? k : m;
+        }
+        tokens[r] = m == 0 ? 0 : (int32_t)(0xFFFFFFFFu - (uint32_t)(m & 0xFFFFFFFFu));
     }
-    tokens[r] = m == 0 ? 0 : (int32_t)(0xFFFFFFFFu - (uint32_t)(m & 0xFFFFFFFFu));
+    __syncthreads();
+    for (int i = threadIdx.x; i < nranks * rows; i += blockDim.x) keys_all[i] = 0;
+    for (int i = threadIdx.x; i < zero_n; i += blockDim.x) zero_keys[i] = 0;
 }
 
-cudaError_t launch_pick_keys(const uint64_t *keys_all, int nranks, int rows, int row0, int nrows, int32_t *tokens,
-                             cudaStream_t st) {
-    if (nrows <= 0) return cudaSuccess;
-    return launch_kernel(pick_keys_kernel, dim3((nrows + 127) / 128), dim3(128), 0, st, keys_all, nranks, rows, row0,
-                         nrows, tokens);
+cudaError_t launch_pick_keys(uint64_t *keys_all, int nranks, int rows, int row0, int nrows, int32_t *tokens,
+                             uint64_t *zero_keys, int zero_n, cudaStream_t st) {
+    if (nrows <= 0 && zero_n <= 0) return cudaSuccess;
+    return launch_kernel(pick_keys_kernel, dim3(1), dim3(256), 0, st, keys_all, nranks, rows, row0, nrows, tokens,
+                         zero_keys, zero_n);
 }
 
 }  // namespace pyxis

@@ -39,8 +39,36 @@ cudaError_t launch_argmax_keys(const float *values, size_t M, size_t n, size_t l
                                uint64_t *keys, const ArgmaxScratch &s, int num_sms, cudaStream_t st);
 
 // tokens[r] for r < nrows: the index in the largest key of row row0 + r over keys_all
-// [nranks][rows] (0 when every key is 0).
-cudaError_t launch_pick_keys(const uint64_t *keys_all, int nranks, int rows, int row0, int nrows, int32_t *tokens,
-                             cudaStream_t st);
+// [nranks][rows] (0 when every key is 0).  Then zeroes keys_all and zero_keys[0, zero_n) (the
+// local keys, which the tensor-core GEMV's epilogue max-reduces into: they must be 0 before it).
+cudaError_t launch_pick_keys(uint64_t *keys_all, int nranks, int rows, int row0, int nrows, int32_t *tokens,
+                             uint64_t *zero_keys, int zero_n, cudaStream_t st);
+
+#ifdef __CUDACC__
+// One element's key: order-preserving float bits << 32 | (0xFFFFFFFF - idx).  A NaN is 0, below
+// every number (the reference's `>` never picks one), and -0.0 ties with +0.0.
+__device__ __forceinline__ uint64_t argmax_key(float v, uint32_t idx) {
+    if (isnan(v)) return 0;
+    if (v == 0.0f) v = 0.0f;
+    const uint32_t u = __float_as_uint(v);
+    const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((uint64_t)ord << 32) | (uint64_t)(0xFFFFFFFFu - idx);
+}
+
+// The key of a logit at global vocabulary index g, as the shards' keys are compared: a NaN at
+// index 0 wins over everything (nothing is `>` values[0] then), other NaNs lose to everything.
+__device__ __forceinline__ uint64_t argmax_key_global(float v, long long g) {
+    return (g == 0 && isnan(v)) ? ~0ull : argmax_key(v, (uint32_t)g);
+}
+
+__device__ __forceinline__ uint64_t warp_max_u64(uint64_t k) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const uint64_t other = __shfl_xor_sync(0xffffffffu, k, o);
+        k = other > k ? other : k;
+    }
+    return k;
+}
+#endif
 
 }  // namespace pyxis

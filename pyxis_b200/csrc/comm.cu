@@ -104,10 +104,11 @@ PYXIS_DEVINL unsigned ld_acquire_sys(const unsigned *p) {
 }
 
 // One CTA: mine [M] keys -> every rank's buffer (slot of this call's epoch parity, row block of
-// this rank), flags, a bounded wait for all ranks' flags here, then tokens[r] for rows
-// [row0, row0 + nrows).  A wait that runs out records kErrExchange and leaves the tokens unwritten.
+// this rank), then mine zeroed for the next call, flags, a bounded wait for all ranks' flags here,
+// then tokens[r] for rows [row0, row0 + nrows).  A wait that runs out records kErrExchange and
+// leaves the tokens unwritten.
 __global__ void __launch_bounds__(256)
-    exchange_pick_kernel(const uint64_t *__restrict__ mine, int M, int rank, int nranks, void *const *xtable,
+    exchange_pick_kernel(uint64_t *__restrict__ mine, int M, int rank, int nranks, void *const *xtable,
                          int row0, int nrows, int32_t *__restrict__ tokens, int *err) {
     __shared__ unsigned s_epoch;
     __shared__ int s_ok;
@@ -129,6 +130,8 @@ __global__ void __launch_bounds__(256)
         for (int r = threadIdx.x; r < M; r += blockDim.x) dst[r] = mine[r];
     }
     __syncthreads();
+    // the tensor-core GEMV's epilogue max-reduces the next call's keys into mine
+    for (int r = threadIdx.x; r < M; r += blockDim.x) mine[r] = 0;
     if (threadIdx.x == 0) {
         __threadfence_system();  // the keys above before the flags, for every peer
         for (int p = 0; p < nranks; ++p)
@@ -257,6 +260,11 @@ int head_reserve(pyxis_cuda_comm *c, size_t M, size_t shard_rows) {
             cudaGetLastError();
             return fail(PYXIS_ENOMEM, "head: cudaMalloc(keys) failed");
         }
+        // zero: the fused head GEMV max-reduces into it (and every call leaves it zero again)
+        if (cudaMemset(c->keys, 0, nk * sizeof(uint64_t)) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(PYXIS_ECUDA, "head: cudaMemset(keys) failed");
+        }
         c->keys_cap = nk;
     }
     return PYXIS_OK;
@@ -268,21 +276,27 @@ int head_greedy_enqueue(pyxis_cuda_comm *c, const pyxis_cuda_weights *shard, siz
     if (M * shard_rows > c->logits_cap || M * (size_t)(c->nranks + 1) > c->keys_cap)
         return fail(PYXIS_EINVAL, "head: buffers not reserved for this many rows");
     pyxis_cuda_ctx *ctx = c->ctx;
-    int rc = run_matmul(ctx, shard, X, M, ldx, shard_rows, hidden, c->logits, shard_rows, ws, ws_bytes, st);
-    if (rc) return rc;
     uint64_t *mine = c->keys, *all = c->keys + M;
-    cudaError_t e = launch_argmax_keys(c->logits, M, shard_rows, shard_rows, (int64_t)vocab_lo, mine, ctx->amax,
-                                       ctx->num_sms, st);
+    // int8 shards on the tensor-core GEMV write the keys from its epilogue (into mine, which the
+    // consumers below leave zero); other shards take the GEMV, then the argmax scan over the logits
+    cudaError_t e = cudaSuccess;
+    if (!head_gemv_keys(ctx, shard, X, M, ldx, shard_rows, hidden, c->logits, shard_rows, (int64_t)vocab_lo, mine,
+                        st, &e)) {
+        int rc = run_matmul(ctx, shard, X, M, ldx, shard_rows, hidden, c->logits, shard_rows, ws, ws_bytes, st);
+        if (rc) return rc;
+        e = launch_argmax_keys(c->logits, M, shard_rows, shard_rows, (int64_t)vocab_lo, mine, ctx->amax, ctx->num_sms,
+                               st);
+    }
     if (e != cudaSuccess) return fail(PYXIS_ECUDA, cudaGetErrorString(e));
     if (c->p2p && M <= (size_t)kXMaxRows) {
-        e = launch_kernel(exchange_pick_kernel, dim3(1), dim3(256), 0, st, (const uint64_t *)mine, (int)M, c->rank,
-                          c->nranks, (void *const *)c->xtable, row0, nrows, tokens, ctx->d_err);
+        e = launch_kernel(exchange_pick_kernel, dim3(1), dim3(256), 0, st, mine, (int)M, c->rank, c->nranks,
+                          (void *const *)c->xtable, row0, nrows, tokens, ctx->d_err);
         if (e != cudaSuccess) return fail(PYXIS_ECUDA, cudaGetErrorString(e));
         return PYXIS_OK;
     }
-    rc = comm_allgather(c, mine, all, M, true, st);
+    int rc = comm_allgather(c, mine, all, M, true, st);
     if (rc) return rc;
-    e = launch_pick_keys(all, c->nranks, (int)M, row0, nrows, tokens, st);
+    e = launch_pick_keys(all, c->nranks, (int)M, row0, nrows, tokens, mine, (int)M, st);
     if (e != cudaSuccess) return fail(PYXIS_ECUDA, cudaGetErrorString(e));
     return PYXIS_OK;
 }

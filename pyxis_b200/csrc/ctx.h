@@ -51,4 +51,12 @@ namespace pyxis {
 // records the message like every entry point.
 int run_matmul(pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, const float *X, size_t M, size_t ldx,
                size_t N, size_t K, float *Y, size_t ldy, void *workspace, size_t workspace_bytes, cudaStream_t st);
+// The greedy head's vocab shard on the tensor-core GEMV with each row's argmax key folded into its
+// epilogue: keys[m] (0 on entry) becomes the key of row m's first maximum, global index
+// index_base + n, as launch_argmax_keys would write it.  Returns false and launches nothing when
+// the product does not take that kernel (more than 8 rows, a matrix the CUDA-core GEMVs take);
+// otherwise *err is the launch's status.
+bool head_gemv_keys(pyxis_cuda_ctx *ctx, const pyxis_cuda_weights *w, const float *X, size_t M, size_t ldx, size_t N,
+                    size_t K, float *Y, size_t ldy, int64_t index_base, uint64_t *keys, cudaStream_t st,
+                    cudaError_t *err);
 }  // namespace pyxis

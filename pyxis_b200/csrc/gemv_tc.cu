@@ -33,6 +33,7 @@
 
 #include <algorithm>
 
+#include "argmax.h"
 #include "kernels.h"
 #include "tc_ptx.cuh"
 #include "tmap.cuh"
@@ -82,6 +83,10 @@ struct Params {
     int *accum;         // [grid][NB][128] int32 partial tiles, zero between launches
     unsigned *tickets;  // [grid], zero between launches
     int *err;
+    // A vocab shard of the greedy head: keys[b] = the max over this launch's logits of row b of
+    // argmax_key_global(y, key_base + n) (0 on entry); null otherwise.
+    unsigned long long *keys;
+    long long key_base;
 };
 
 // int8 instruction descriptor: s32 accumulate, signed A and B, both K-major.
@@ -390,6 +395,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             // whose wait ran out skips the work but keeps the barrier sequence.
             const int qd = warp & 3;  // TMEM lane quarter of this warp
             const int nseg = sc.num_segments(my_sb, my_se);
+            uint64_t kmax[kMaxTok];  // the greedy head's keys of the logits this thread wrote
+#pragma unroll
+            for (int b = 0; b < kMaxTok; ++b) kmax[b] = 0;
             for (int li = 0; li < nseg; ++li) {
                 long long s0, s1;
                 sc.segment(my_sb, my_se, li, s0, s1);
@@ -431,7 +439,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const double sr = (double)__ldg(p.scales + row);
 #pragma unroll
                         for (int b = 0; b < kMaxTok; ++b)
-                            if (b < p.B) p.y[(size_t)b * p.ldy + row] = combine(&D[4 * b], xscale[b], sr);
+                            if (b < p.B) {
+                                const float v = combine(&D[4 * b], xscale[b], sr);
+                                p.y[(size_t)b * p.ldy + row] = v;
+                                if (p.keys) {
+                                    const uint64_t k = argmax_key_global(v, p.key_base + row);
+                                    kmax[b] = k > kmax[b] ? k : kmax[b];
+                                }
+                            }
                     }
                 } else {
                     // column j of the slot is 128 contiguous ints: a warp's 32 rows share one line
@@ -461,12 +476,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const double sr = (double)__ldg(p.scales + row);
 #pragma unroll
                             for (int b = 0; b < kMaxTok; ++b)
-                                if (b < p.B) p.y[(size_t)b * p.ldy + row] = combine(&S[4 * b], xscale[b], sr);
+                                if (b < p.B) {
+                                    const float v = combine(&S[4 * b], xscale[b], sr);
+                                    p.y[(size_t)b * p.ldy + row] = v;
+                                    if (p.keys) {
+                                        const uint64_t k = argmax_key_global(v, p.key_base + row);
+                                        kmax[b] = k > kmax[b] ? k : kmax[b];
+                                    }
+                                }
                         }
                     }
                     named_bar(2, 128);
                     if (last && warp == 2 && lane == 0) p.tickets[first] = 0;
                 }
+            }
+            if (p.keys) {
+                // one atomic per warp and input row; max is associative, so the order of the
+                // CTAs' atomics does not matter
+#pragma unroll
+                for (int b = 0; b < kMaxTok; ++b)
+                    if (b < p.B) {
+                        const uint64_t k = warp_max_u64(kmax[b]);
+                        if (lane == 0 && k) atomicMax(p.keys + b, (unsigned long long)k);
+                    }
             }
         }
     }
@@ -516,7 +548,8 @@ size_t gemv_tc_scratch_bytes(int max_grid) {
 bool gemv_tc_supported(const QMatrix &w, size_t B, int num_sms) { return plan_for(w, B, num_sms).ok; }
 
 cudaError_t launch_gemv_tc(const QMatrix &w, const float *X, size_t B, size_t ldx, float *Y, size_t ldy,
-                           void *scratch, size_t scratch_bytes, int *err, int num_sms, cudaStream_t st) {
+                           void *scratch, size_t scratch_bytes, int *err, int num_sms, cudaStream_t st,
+                           uint64_t *keys, long long key_base) {
     const Plan pl = plan_for(w, B, num_sms);
     if (!pl.ok) return cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(X) & 15) || (B > 1 && ldx % 4)) return cudaErrorInvalidValue;
@@ -574,6 +607,8 @@ cudaError_t launch_gemv_tc(const QMatrix &w, const float *X, size_t B, size_t ld
         p.tickets = reinterpret_cast<unsigned *>(sb + (size_t)grid * TM * 32 * sizeof(int));
     }
     p.err = err;
+    p.keys = reinterpret_cast<unsigned long long *>(keys);
+    p.key_base = key_base;
     static std::atomic<uint64_t> attr_done{0};
     const cudaError_t attr = once_per_device(attr_done, [] {
         return cudaFuncSetAttribute(gemv_tc_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTotal);

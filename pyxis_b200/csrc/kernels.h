@@ -81,8 +81,12 @@ cudaError_t launch_gemm_tc(const QMatrix &w, const float *X, size_t M, size_t ld
 // max_grid); it must be zero before the first launch and the kernel leaves it zero.
 bool gemv_tc_supported(const QMatrix &w, size_t B, int num_sms);
 size_t gemv_tc_scratch_bytes(int max_grid);
+// With `keys` (the greedy head's vocab shard): the epilogue also max-reduces, per input row b,
+// the argmax key of every logit at global index key_base + n into keys[b] (atomicMax; keys[0, B)
+// must be 0 before the launch), the key launch_argmax_keys would write for the row.
 cudaError_t launch_gemv_tc(const QMatrix &w, const float *X, size_t B, size_t ldx, float *Y, size_t ldy,
-                           void *scratch, size_t scratch_bytes, int *err, int num_sms, cudaStream_t st);
+                           void *scratch, size_t scratch_bytes, int *err, int num_sms, cudaStream_t st,
+                           uint64_t *keys = nullptr, long long key_base = 0);
 
 // Weight-streaming matmul for 1..64 tokens on tcgen05 (gemm_ws.cu): int4 or int8 codes with a scale
 // per group of 32, or int8 with one scale per row; K % 128 == 0.  The workspace holds x's fp16

@@ -5,7 +5,8 @@ Only the parts that shard naturally are split; nothing here reduces partial sums
   * row-sharded matmul: rank r owns output rows [r*N/n, (r+1)*N/n) of a matrix.  With one scale
     per row (int8) or per 32 values (int4, in_features a multiple of 32) a row block's packed bytes
     and scales are exactly that slice of the full pack, so each rank quantises only its rows and
-    the outputs concatenate to the single-GPU result (optionally all-gathered, NCCL over NVLink).
+    the outputs concatenate to the single-GPU result -- bit for bit where the shard takes the full
+    matrix's kernel (kernels are chosen by size) -- optionally all-gathered (NCCL over NVLink).
   * vocab-parallel lm_head + greedy argmax (src/output_head.rs:21-44): each rank computes the
     logits of its vocab shard and reduces every row to one 64-bit key on the device
     (order-preserving value bits, then the inverted global index); the ranks all-gather the keys
