@@ -305,10 +305,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int nbq = p.NB / 4;  // token slots per K-block
         const float4 *xd4 = reinterpret_cast<const float4 *>(xd);
         const bool x_ok = tc::mbar_wait_bounded(xfull, 0, abort_flag, p.err, kErrMma, kTimeoutNs);
-        // x was issued after griddepcontrol.wait (by the producer or the helper warp), so this
-        // returns at once; it keeps the epilogue's writes (y, the shared scratch) formally ordered
-        // after the previous kernel
-        pdl_wait();
+        // (x was issued after griddepcontrol.wait, by the producer or the helper warp.  The warps
+        // that write global memory -- the epilogue: y, the shared scratch, the keys -- wait on the
+        // dependency themselves, before their first write.)
         if (x_ok) {
             // max |x| of every token over all of K, the same in every CTA
             float m[kMaxTok];
@@ -327,15 +326,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                         m[b] = max_nan(max_nan(max_nan(max_nan(m[b], fabsf(v[b].x)), fabsf(v[b].y)), fabsf(v[b].z)),
                                        fabsf(v[b].w));
             }
+            // the tokens' butterflies interleaved, step by step: independent shuffles (tokens past B
+            // reduce zeros and are not stored)
 #pragma unroll
-            for (int b = 0; b < kMaxTok; ++b) {
-                if (b < p.B) {  // uniform: every lane takes the same branches
-                    float mb = m[b];
+            for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) mb = max_nan(mb, __shfl_xor_sync(0xffffffffu, mb, o));
-                    if (lane == 0) red[b * kBuildWarps + bwarp] = mb;
-                }
-            }
+                for (int b = 0; b < kMaxTok; ++b) m[b] = max_nan(m[b], __shfl_xor_sync(0xffffffffu, m[b], o));
+            if (lane == 0)
+#pragma unroll
+                for (int b = 0; b < kMaxTok; ++b)
+                    if (b < p.B) red[b * kBuildWarps + bwarp] = m[b];
         }
         named_bar(1, nbt);
         if (bt < p.B) {
@@ -393,6 +393,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             // ---------------------------------------------------------------- epilogue
             // All four warps run the same item sequence and the same named barriers; a warp
             // whose wait ran out skips the work but keeps the barrier sequence.
+            // y, the shared scratch and the keys are written only after the previous kernel is
+            // done with them (it has finished by now: x came after the same wait)
+            pdl_wait();
             const int qd = warp & 3;  // TMEM lane quarter of this warp
             const int nseg = sc.num_segments(my_sb, my_se);
             uint64_t kmax[kMaxTok];  // the greedy head's keys of the logits this thread wrote
