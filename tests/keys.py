@@ -29,3 +29,27 @@ def shard_key(v, lo: int) -> int:
 def pick(keys) -> int:
     m = max(int(k) for k in keys)
     return 0 if m == 0 else 0xFFFFFFFF - (m & 0xFFFFFFFF)
+
+
+def element_key(x, g: int) -> int:
+    """argmax_key_global (pyxis_b200/csrc/argmax.h): the key of one logit at global index g, as
+    the tensor-core GEMV's epilogue builds it for every logit it writes."""
+    x = np.float32(x)
+    if np.isnan(x):
+        return (1 << 64) - 1 if g == 0 else 0
+    return (ordered(x) << 32) | (0xFFFFFFFF - g)
+
+
+def epilogue_key(v, lo: int, rng) -> int:
+    """The fused epilogue's key of a shard: element keys max-reduced in an arbitrary grouping and
+    order (threads, warps, CTAs, then atomicMax into a slot that starts at 0)."""
+    v = np.asarray(v, np.float32)
+    keys = [element_key(x, lo + i) for i, x in enumerate(v)]
+    order = rng.permutation(len(keys))
+    slot = 0
+    for chunk in np.array_split(order, max(1, int(rng.integers(1, 6)))):
+        part = 0
+        for i in chunk:
+            part = max(part, keys[i])
+        slot = max(slot, part)
+    return slot

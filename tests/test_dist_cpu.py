@@ -11,7 +11,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 import oracle
-from keys import pick, shard_key
+from keys import epilogue_key, pick, shard_key
 from pyxis_b200.dist import bits_rows, exchange_comm_id, shard_range
 
 
@@ -42,6 +42,31 @@ def test_key_pick_matches_reference_argmax(world):
             v[:] = np.nan
         keys = [shard_key(v[lo:hi], lo) for lo, hi in (shard_range(n, r, world) for r in range(world)) if hi > lo]
         assert pick(keys) == oracle.argmax(v), (v, keys)
+
+
+@pytest.mark.parametrize("world", [1, 2, 5])
+def test_epilogue_keys_equal_the_scan_keys(world):
+    """The key the tensor-core GEMV's epilogue builds for a shard (every logit's key at its global
+    index, max-reduced in any grouping and order into a zeroed slot) equals the scan's shard key
+    (launch_argmax_keys: the shard's first maximum, then its global index), so the fused head picks
+    the same token: NaN at global index 0, NaNs elsewhere, ties across shards, -0.0 / +0.0."""
+    rng = np.random.default_rng(10 + world)
+    for trial in range(200):
+        n = int(rng.integers(1, 50))
+        v = rng.integers(-2, 3, size=n).astype(np.float32)
+        if trial % 3 == 0:
+            v[rng.integers(0, n)] = -0.0
+        if trial % 4 == 0:
+            v[rng.integers(0, n)] = np.nan
+        if trial % 13 == 0:
+            v[0] = np.nan
+        if trial % 19 == 0:
+            v[:] = np.nan
+        shards = [(lo, hi) for lo, hi in (shard_range(n, r, world) for r in range(world)) if hi > lo]
+        fused = [epilogue_key(v[lo:hi], lo, rng) for lo, hi in shards]
+        scan = [shard_key(v[lo:hi], lo) for lo, hi in shards]
+        assert fused == scan, (v, fused, scan)
+        assert pick(fused) == oracle.argmax(v)
 
 
 @pytest.mark.parametrize("qt,N,K,bs", [("int8", 37, 96, 96), ("int4", 37, 96, 32), ("int4", 10, 2048, 32),
